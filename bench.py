@@ -1,0 +1,360 @@
+"""Benchmark of the quantised MoE expert FFN on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the routed-expert FFN of a
+Qwen3-30B-A3B-shaped MoE layer at batch 1 - 128 experts, top-8 softmax
+routing, gate/up [768 x 2048] Q4_K, down [2048 x 768] Q6_K, x ~ N(0,1) f32
+quantised to Q8_K on the device, router logits ~ N(0,1). All experts of 48
+such layers (18.8 GB) are resident in HBM; one step is one token through the
+48 layers' expert FFNs (48 independent layer-tokens), so each step walks
+1.17 GB of selected expert weights and nothing is reused from the 126 MB L2.
+
+Metric: expert weight bytes per second (24,477,696 algorithmic bytes per
+layer-token), the reference's own matvec unit. `value` runs with inputs
+resident in HBM; `e2e` runs the same steps through the public C ABI call
+(tlmg_expert_ffn_many) with pinned host buffers, host<->device copies inside
+the timed region. The reference arm (--impl reference) times the
+reference's own AVX-512 kernels through its worker pool on the host cores.
+
+Under torchrun each rank runs an independent replica on its own GPU (the
+bs=1 path does not shard: no collective on the data path); value is the sum
+over ranks divided by the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+D, DE, E, K = 2048, 768, 128, 8
+DT_GATE, DT_DOWN = 12, 14                       # Q4_K gate/up, Q6_K down
+BYTES_LAYER_TOKEN = K * (2 * DE * (D // 256 * 144) + D * (DE // 256 * 210))   # 24,477,696
+METRIC = "expert GEMV HBM GB/s, bs=1 MoE expert FFN (Qwen3-30B-A3B layer shape, Q4_K gate/up + Q6_K down)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines: list[str] = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def cpu_reference_run(seconds: float, layers_host: int = 2, threads: int = 0, steps: int | None = None,
+                      warmup: int = 0, step_layers: int = 48):
+    """Time the reference's CPU path on the host cores: its own kernels
+    (tlm_quantize_act / tlm_matvec_rows, AVX-512 tier) orchestrated like
+    run_batch() through its worker pool, all threads, rotating over
+    layers_host x 128 host-resident experts (>> L3). Returns a dict."""
+    import oracle
+    from tierlm_b200 import synth
+    R = oracle.ref()
+    kind = "reference"
+    if R is None:
+        raise RuntimeError("oracle/_ref/libtlmref.so is not built (make -C oracle ref)")
+    R.tlmref_open(threads)
+    nthreads = R.tlmref_threads()
+    rng = np.random.default_rng(1234)
+    layers = [[synth.rand_expert(rng, D, DE, (DT_GATE, DT_GATE, DT_DOWN)) for _ in range(E)]
+              for _ in range(layers_host)]
+    dt = (C.c_int * 3)(DT_GATE, DT_GATE, DT_DOWN)
+    ffn = np.zeros(D, np.float32)
+    inputs = [(rng.standard_normal(D).astype(np.float32), rng.standard_normal(E).astype(np.float32))
+              for _ in range(64)]
+
+    def one(i):
+        x, lg = inputs[i % len(inputs)]
+        ids, w = oracle.route(0, lg, K)     # routing: negligible next to the matvecs
+        experts = layers[i % layers_host]
+        g = (C.c_void_p * K)(*[experts[e][0].ctypes.data + experts[e][1][0] for e in ids])
+        u = (C.c_void_p * K)(*[experts[e][0].ctypes.data + experts[e][1][1] for e in ids])
+        d = (C.c_void_p * K)(*[experts[e][0].ctypes.data + experts[e][1][2] for e in ids])
+        R.tlmref_expert_ffn(D, DE, K, dt, g, u, d, x.ctypes.data, w.ctypes.data, ffn.ctypes.data)
+
+    for i in range(8):
+        one(i)
+    if steps is None:
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            one(n)
+            n += 1
+        el = time.perf_counter() - t0
+        units = n
+        sample = f"{n} layer-tokens over {el:.1f} s, rotating {layers_host} host layers x {E} experts"
+    else:
+        for i in range(warmup * step_layers):
+            one(i)
+        t0 = time.perf_counter()
+        for i in range(steps * step_layers):
+            one(i)
+        el = time.perf_counter() - t0
+        units = steps * step_layers
+        sample = (f"{steps} steps x {step_layers} layer-tokens, rotating {layers_host} host layers x {E} "
+                  f"experts ({layers_host * E * 3.06:.0f} MB > L3)")
+    gbs = units * BYTES_LAYER_TOKEN / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": nthreads, "kind": kind,
+            "tier": R.tlmref_tier().decode(), "cpu": R.tlmref_cpu_model().decode().strip(),
+            "sample": sample, "seconds": el, "units": units}
+
+
+def run_reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    r = cpu_reference_run(0, layers_host=2, steps=args.steps, warmup=args.warmup)
+    ms = r["seconds"] * 1e3 / args.steps
+    line = {"metric": METRIC, "value": r["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8/int32+f32", "data": "synthetic", "impl": "reference",
+            "config": config_dict(args),
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "tier", "cpu")},
+            "e2e": {"value": r["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args) -> dict:
+    return {"workload": "BASELINE config 2: isolated expert FFN (GEMV+SwiGLU+combine), Qwen3-30B-A3B layer "
+                        "shape, bs=1; one step = one token through 48 layers' expert FFNs",
+            "layers": args.layers, "n_experts": E, "top_k": K, "d_model": D, "d_expert": DE, "batch": 1,
+            "weights": "gate/up Q4_K, down Q6_K (random codes, finite random f16 scales)",
+            "inputs": "x ~ N(0,1) f32 -> Q8_K on device; router logits ~ N(0,1), softmax top-8 renorm",
+            "l2": f"inputs larger than L2: {args.layers} layers x {E} experts resident "
+                  f"({args.layers * E * 3.06e-3:.1f} GB) walked once per step",
+            "parallelism": f"replicas x{args.gpus} (bs=1 does not shard)"}
+
+
+# ---------------------------------------------------------------------------
+def build_context(args, dev, seed: int):
+    import torch
+
+    from tierlm_b200 import synth
+    from tierlm_b200.moe import MoeContext
+    ctx = MoeContext(args.layers, D, DE, E, K, router=0, device=dev.index)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    rb_g, rb_d = D // 256 * 144, DE // 256 * 210
+    og, ou, od = 0, DE * rb_g, 2 * DE * rb_g
+    per = 2 * DE * rb_g + D * rb_d
+    for layer in range(args.layers):
+        gu = synth.device_rows(DT_GATE, E * 2 * DE, D, gen, dev).view(E, 2 * DE * rb_g)
+        dn = synth.device_rows(DT_DOWN, E * D, DE, gen, dev).view(E, D * rb_d)
+        buf = torch.cat([gu, dn], dim=1).contiguous()          # [E, per]: gate | up | down
+        for e in range(E):
+            p = buf[e]
+            ctx._lib.tlmg_set_expert(ctx._h, layer, e, (C.c_int32 * 3)(DT_GATE, DT_GATE, DT_DOWN),
+                                     C.c_void_p(p.data_ptr()), per, (C.c_uint64 * 3)(og, ou, od))
+        del gu, dn, buf
+    torch.cuda.synchronize(dev)
+    return ctx
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("TLMG_BENCH_ALLOW_SHORT"), \
+        "use at least 3 warm-up steps"
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    args.gpus = max(args.gpus, world)
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from tierlm_b200 import _lib
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _lib.check(_lib.load().tlmg_init(local))
+
+    ctx = build_context(args, dev, seed=1000 + rank)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream)
+    L = args.layers
+    P = 8                                              # distinct token input sets, rotated
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    xs = torch.randn((P, L, D), generator=g, device=dev)
+    lgs = torch.randn((P, L, E), generator=g, device=dev)
+    out = torch.empty((P, L, D), device=dev)
+
+    def step(s):
+        i = s % P
+        ctx.expert_ffn_many(0, xs[i], lgs[i], out[i])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(fn, n):
+        torch.cuda.synchronize(dev)
+        barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for s in range(n):
+            fn(s)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        ms = t0.elapsed_time(t1)
+        if world > 1:
+            tm = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            ms = float(tm.item())
+        return ms
+
+    # ---- value: inputs resident in HBM
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = ctx.launches
+    ms = timed(step, args.steps)
+    launches = ctx.launches - launches0
+    clk = clocks.stop()
+    bytes_step = L * BYTES_LAYER_TOKEN
+    value = world * args.steps * bytes_step / (ms * 1e-3) / 1e9
+
+    # ---- roofline of the dominant kernel: per-launch CUDA events, second pass
+    kern = ctx.kernel_times(lambda: [step(s) for s in range(args.steps)])
+    peak, peak_src = peaks()
+
+    # ---- e2e: the same steps through the C ABI with pinned host buffers
+    hx = xs.cpu().pin_memory()
+    hl = lgs.cpu().pin_memory()
+    ho = torch.empty((P, L, D)).pin_memory()
+
+    def step_host(s):
+        i = s % P
+        ctx.expert_ffn_many(0, hx[i], hl[i], ho[i])
+
+    for s in range(args.warmup):
+        step_host(s)
+    ms_e2e = timed(step_host, args.steps)
+    e2e = world * args.steps * bytes_step / (ms_e2e * 1e-3) / 1e9
+    h2d = L * (D + E) * 4
+    d2h = L * D * 4
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r = cpu_reference_run(args.cpu_seconds)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "tier", "cpu")}
+        except Exception as ex:   # the baseline is reported, never required
+            cpu = {"value": None, "unit": "GB/s", "cores": None, "kind": "reference", "sample": f"failed: {ex}"}
+
+    if rank == 0:
+        kname, kms, kn, kbytes = kern
+        achieved = kbytes / (kms / kn * 1e-3) / 1e9 if kn else None
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8/int32+f32", "data": "synthetic", "config": config_dict(args),
+            "tokens_per_s": round(world * args.steps / (ms * 1e-3), 2),
+            "layer_tokens_per_s": round(world * args.steps * L / (ms * 1e-3), 1),
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e / args.steps, "api": "tlmg_expert_ffn_many (pinned host buffers)"},
+            "roofline": {"bound": "hbm", "kernel": kname,
+                         "achieved": None if achieved is None else round(achieved, 1),
+                         "peak": peak, "unit": "GB/s",
+                         "frac": None if achieved is None else round(achieved / peak, 4),
+                         "traffic": None, "peak_source": peak_src,
+                         "launches": kn, "avg_us": None if not kn else round(kms / kn * 1e3, 3),
+                         "algorithmic_bytes_per_launch": kbytes,
+                         "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
+            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

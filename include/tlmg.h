@@ -1,0 +1,182 @@
+/* tlmg.h - C ABI of libtlmg, the B200 (sm_100a) tier of tierlm's quantised
+ * MoE decoder step.
+ *
+ * Plain C: pointers, sizes and integer codes only; no CUDA or torch types
+ * in the signatures (a CUDA stream travels as `void *`, NULL = the
+ * library's own stream). All fallible functions return 0 (TLMG_OK) or a
+ * negative code with the same numbering as the reference's TLM_E* codes
+ * (src/lib/tlm_platform.h:26-36), and leave a thread-local message for
+ * tlmg_errmsg(). Numerics follow the reference contract
+ * (src/lib/tlm_quant.h:113-128): exact int32 sums inside a block, then per
+ * block acc = fmaf(d_w*d_a, (float)isum, acc) (and the min term for
+ * Q4_K/Q5_K) in ascending block order; every result below is bit-identical
+ * to the reference scalar kernels given the same inputs.
+ *
+ * Pointer rules. "device" pointers must be CUDA device (or managed)
+ * memory. Entry points marked "host or device" accept either: host
+ * buffers are staged through pinned memory by the library and the call
+ * returns after the result is back on the host. Activation buffers must be
+ * 4-byte aligned (src/lib/tlm_quant.h:105-106); weight rows may start at
+ * any byte offset.
+ */
+#ifndef TLMG_H
+#define TLMG_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    TLMG_OK = 0, TLMG_EIO = -1, TLMG_ENOMEM = -2, TLMG_EINVAL = -3, TLMG_EFORMAT = -4,
+    TLMG_ERANGE = -5, TLMG_ENOTFOUND = -6, TLMG_EUNSUP = -7, TLMG_EBUSY = -8
+};
+
+/* dtype codes = tlm_dtype values (src/lib/tlm_quant.h:31-42). */
+enum {
+    TLMG_DT_F32 = 0, TLMG_DT_F16 = 1, TLMG_DT_BF16 = 2, TLMG_DT_Q8_0 = 8, TLMG_DT_Q4_K = 12,
+    TLMG_DT_Q5_K = 13, TLMG_DT_Q6_K = 14, TLMG_DT_Q8_K = 15, TLMG_DT_MXFP4 = 39
+};
+
+/* ---- library --------------------------------------------------------- */
+/* Thread-local message of the last failure (replaces tlm_errmsg,
+ * src/lib/tlm_platform.h:37). */
+const char *tlmg_errmsg(void);
+/* Tier name, "cuda-sm100a" (mirrors tlm_quant_tier, src/lib/tlm_quant.h:83). */
+const char *tlmg_tier(void);
+/* Select the CUDA device for the calling thread and create the library's
+ * stream on it (idempotent). */
+int tlmg_init(int device);
+/* Wait for all work the library queued on `stream` (NULL = its own). */
+int tlmg_sync(void *stream);
+
+/* ---- formats (src/lib/tlm_quant.h:45-50, :66) ------------------------ */
+int    tlmg_dtype_block(int dt);
+size_t tlmg_dtype_block_bytes(int dt);
+size_t tlmg_row_bytes(int dt, int64_t n);
+size_t tlmg_qact_bytes(int kind, int64_t n);
+int    tlmg_act_kind_for(int weight_dt);
+
+/* ---- kernel level (device pointers, asynchronous on `stream`) -------- */
+/* Activation quantisation, replaces tlm_quantize_act
+ * (src/lib/tlm_quant.h:69, src/lib/tlm_quant.c:458-512). kind = Q8_K,
+ * Q8_0 or F32. x: device f32[n]; dst: device, tlmg_qact_bytes(kind, n). */
+int tlmg_quantize_act(int kind, const float *x, int64_t n, void *dst, void *stream);
+
+/* y[r] = dot(W[r], act) for r in [r0, r1); replaces tlm_matvec_rows
+ * (src/lib/tlm_quant.h:77-79, src/lib/tlm_quant.c:1119-1143). W: device,
+ * row_bytes stride, any byte offset; act: device output of
+ * tlmg_quantize_act (or f32 for float weights); y: device f32 indexed by
+ * absolute row. Bad dtype / width: TLMG_EINVAL and NaN in y[r0..r1). */
+int tlmg_matvec_rows(int dt, const void *W, size_t row_bytes, const void *act, float *y,
+                     int64_t n, int64_t r0, int64_t r1, void *stream);
+
+/* Per-block exact integer partials of rows [0, nrows) (integer formats):
+ * isum/msum: device int32[nrows * n/block]. These are the int32 sums the
+ * reference's scalar dots form before their fmaf chain
+ * (dot_kq_affine_ref / dot_q6_k_ref / dot_q8_0_ref / dot_q8_k_ref /
+ * dot_mxfp4_ref, src/lib/tlm_quant.c:778-902); msum is 0 except for
+ * Q4_K/Q5_K. For parity checks of the integer stage. */
+int tlmg_block_partials(int dt, const void *W, size_t row_bytes, const void *act, int64_t n,
+                        int64_t nrows, int32_t *isum, int32_t *msum, void *stream);
+
+/* Router top-k over device logits[E] (route/topk, src/lib/tlm_model.c:
+ * 776-839): router 0 = softmax, top-k, renormalise; 1 = softmax, top-k;
+ * 2 = sigmoid + bias selection, renormalise. mask (u8[E], 1 = pruned)
+ * and bias (f32[E]) may be NULL. ids/w: device int32[k], f32[k]. */
+int tlmg_route(int router, const float *logits, const uint8_t *mask, const float *bias, int E,
+               int k, float routed_scale, int32_t *ids, float *w, void *stream);
+
+/* ---- host-buffer adapters with the tier-table signature -------------- */
+/* Same contract as tlm_qmv_fn (src/lib/tlm_quant.h:160-163): W, act, y are
+ * HOST pointers; the call copies in, runs, copies out and returns. For the
+ * reference's bit-exact tier self-test harness (selftest_tier,
+ * src/lib/tlm_quant.c:1014-1056). Errors leave NaN in y. */
+void tlmg_qmv_host(int dt, const void *W, size_t row_bytes, const void *act, float *y, int64_t n,
+                   int64_t nrows);
+/* Same contract as tlm_qdot_fn (src/lib/tlm_quant.h:158): one HOST row. */
+float tlmg_qdot_host(int dt, const void *wrow, const void *act, int64_t n);
+
+/* ---- layer level: the MoE expert FFN with HBM-resident expert slots --- */
+typedef struct tlmg_ctx tlmg_ctx;
+
+/* Geometry of the MoE block (subset of tlm_model_geom,
+ * src/lib/tlm_packet.h:84-95). */
+typedef struct {
+    int32_t n_layers, d_model, d_expert, d_shared, n_experts, top_k;
+    int32_t router;          /* 0, 1, 2 as in tlm_model_geom.router */
+    float   routed_scale, norm_eps;
+} tlmg_geom;
+
+/* Create a context on `device` (replaces the MoE half of tlm_model_open,
+ * src/lib/tlm_model.h:36). Expert slots are allocated lazily per layer. */
+int  tlmg_open(const tlmg_geom *g, int device, tlmg_ctx **out);
+void tlmg_close(tlmg_ctx *ctx);
+
+/* Upload one routed expert into its HBM slot: the packet payload bytes
+ * (host or device pointer) with gate/up/down at item_off[0..2] (tlm_packet_hdr,
+ * src/lib/tlm_packet.h:40-55; expert_mats, src/lib/tlm_model.c:880-896).
+ * dt[3] are the dtypes of gate, up, down (the reference packet has one
+ * dtype for all three; pass it three times). Synchronous. */
+int tlmg_set_expert(tlmg_ctx *ctx, int layer, int expert, const int32_t dt[3],
+                    const void *payload, size_t payload_len, const uint64_t item_off[3]);
+
+/* Resident per-layer tensors of the MoE block (DENSE packet,
+ * src/lib/tlm_model.c:940-1055): ffn_norm f32[D]; router [E x D] of
+ * router_dt (tlmc keeps it f32); router_bias f32[E] or NULL; mask u8[E]
+ * or NULL. HOST pointers, copied. */
+int tlmg_set_layer(tlmg_ctx *ctx, int layer, const float *ffn_norm, int router_dt,
+                   const void *router_w, size_t router_row_bytes, const float *router_bias,
+                   const uint8_t *mask);
+
+/* Shared expert of a layer: gate/up [ds x D], down [D x ds] with dtypes
+ * dt[3], plus the optional sigmoid gate vector f32[D]. HOST pointers. */
+int tlmg_set_shared(tlmg_ctx *ctx, int layer, const int32_t dt[3], const void *gate,
+                    const void *up, const void *down, const float *gate_inp);
+
+/* Routed-expert FFN of one token (run_batch + rank-ordered combine,
+ * src/lib/tlm_model.c:900-938, :1029-1036): x = normalised input f32[D],
+ * logits f32[E]; ffn f32[D] receives sum_r w[r] * down_r(SiLU(gate_r x) *
+ * up_r x). ids/w (top_k, may be NULL) receive the routing. Pointers: host
+ * or device (all of one kind). */
+int tlmg_expert_ffn(tlmg_ctx *ctx, int layer, const float *x, const float *logits, float *ffn,
+                    int32_t *ids, float *w);
+
+/* The same for n_tok independent (x, logits) pairs, pair t using layer
+ * (layer0 + t) % n_layers: x f32[n_tok][D], logits f32[n_tok][E], ffn
+ * f32[n_tok][D]. One host->device copy in, one device->host copy out when
+ * the pointers are host memory. */
+int tlmg_expert_ffn_many(tlmg_ctx *ctx, int layer0, int n_tok, const float *x,
+                         const float *logits, float *ffn);
+
+/* The whole moe() block for one token (src/lib/tlm_model.c:940-1055):
+ * RMSNorm, router matvec, route, experts, shared expert, h += ffn.
+ * h: f32[D] in/out; ids/w may be NULL. Host or device pointers. */
+int tlmg_moe_layer(tlmg_ctx *ctx, int layer, float *h, int32_t *ids, float *w);
+
+/* Run the context's work on `stream` (a cudaStream_t passed as void *) from
+ * now on; NULL returns to the context's own stream. Lets a caller order the
+ * MoE block with its other work and time it with events on that stream. */
+int tlmg_set_stream(tlmg_ctx *ctx, void *stream);
+
+/* Per-launch timing of the expert-FFN kernels with CUDA events recorded on
+ * the launch stream around each launch (off by default; on = 1 clears the
+ * totals). Kernel classes: 0 = gate/up + SwiGLU (or the fused expert-FFN
+ * kernel), 1 = down + combine, 2 = router top-k. */
+int tlmg_profile(tlmg_ctx *ctx, int on);
+/* Totals since profiling was switched on (synchronises the stream): device
+ * milliseconds, launches, and the algorithmic weight bytes one launch of
+ * that class reads (from the layer's expert dtypes). */
+int tlmg_profile_read(tlmg_ctx *ctx, int kclass, double *ms, int64_t *launches,
+                      int64_t *bytes_per_launch);
+
+/* Kernel launches issued by the library since the context was opened
+ * (counted on the host at each launch). */
+int64_t tlmg_launch_count(const tlmg_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,103 @@
+"""ctypes binding of libtlmg.so (the C ABI declared in include/tlmg.h).
+
+The library is the product: there is no CPU fallback. load() raises when
+the shared object is missing or cannot be loaded, and every wrapper in this
+package goes through it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libtlmg.so"
+
+# error codes (include/tlmg.h; same numbering as the reference's TLM_E*)
+TLMG_OK, TLMG_EIO, TLMG_ENOMEM, TLMG_EINVAL, TLMG_EFORMAT = 0, -1, -2, -3, -4
+TLMG_ERANGE, TLMG_ENOTFOUND, TLMG_EUNSUP, TLMG_EBUSY = -5, -6, -7, -8
+
+# dtype codes (= tlm_dtype)
+F32, F16, BF16, Q8_0, Q4_K, Q5_K, Q6_K, Q8_K, MXFP4 = 0, 1, 2, 8, 12, 13, 14, 15, 39
+DTYPE_NAMES = {F32: "f32", F16: "f16", BF16: "bf16", Q8_0: "q8_0", Q4_K: "q4_k", Q5_K: "q5_k",
+               Q6_K: "q6_k", Q8_K: "q8_k", MXFP4: "mxfp4"}
+
+
+class TlmError(RuntimeError):
+    """A negative return code from libtlmg, with its thread-local message."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libtlmg error {code}: {msg}")
+        self.code = code
+
+
+class Geom(C.Structure):
+    _fields_ = [("n_layers", C.c_int32), ("d_model", C.c_int32), ("d_expert", C.c_int32),
+                ("d_shared", C.c_int32), ("n_experts", C.c_int32), ("top_k", C.c_int32),
+                ("router", C.c_int32), ("routed_scale", C.c_float), ("norm_eps", C.c_float)]
+
+
+_lib = None
+
+_P, _I, _I64, _SZ, _F = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
+_SIGS = {
+    "tlmg_errmsg": (C.c_char_p, []),
+    "tlmg_tier": (C.c_char_p, []),
+    "tlmg_init": (_I, [_I]),
+    "tlmg_sync": (_I, [_P]),
+    "tlmg_dtype_block": (_I, [_I]),
+    "tlmg_dtype_block_bytes": (_SZ, [_I]),
+    "tlmg_row_bytes": (_SZ, [_I, _I64]),
+    "tlmg_qact_bytes": (_SZ, [_I, _I64]),
+    "tlmg_act_kind_for": (_I, [_I]),
+    "tlmg_quantize_act": (_I, [_I, _P, _I64, _P, _P]),
+    "tlmg_matvec_rows": (_I, [_I, _P, _SZ, _P, _P, _I64, _I64, _I64, _P]),
+    "tlmg_block_partials": (_I, [_I, _P, _SZ, _P, _I64, _I64, _P, _P, _P]),
+    "tlmg_route": (_I, [_I, _P, _P, _P, _I, _I, _F, _P, _P, _P]),
+    "tlmg_qmv_host": (None, [_I, _P, _SZ, _P, _P, _I64, _I64]),
+    "tlmg_qdot_host": (_F, [_I, _P, _P, _I64]),
+    "tlmg_open": (_I, [C.POINTER(Geom), _I, C.POINTER(_P)]),
+    "tlmg_close": (None, [_P]),
+    "tlmg_set_expert": (_I, [_P, _I, _I, _P, _P, _SZ, _P]),
+    "tlmg_set_layer": (_I, [_P, _I, _P, _I, _P, _SZ, _P, _P]),
+    "tlmg_set_shared": (_I, [_P, _I, _P, _P, _P, _P, _P]),
+    "tlmg_expert_ffn": (_I, [_P, _I, _P, _P, _P, _P, _P]),
+    "tlmg_expert_ffn_many": (_I, [_P, _I, _I, _P, _P, _P]),
+    "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
+    "tlmg_set_stream": (_I, [_P, _P]),
+    "tlmg_profile": (_I, [_P, _I]),
+    "tlmg_profile_read": (_I, [_P, _I, C.POINTER(C.c_double), C.POINTER(_I64), C.POINTER(_I64)]),
+    "tlmg_launch_count": (_I64, [_P]),
+}
+
+
+def load() -> C.CDLL:
+    """Load libtlmg.so (building it first when a toolchain is present)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists() and os.environ.get("TLMG_NO_BUILD") != "1":
+        from . import build as _build
+        _build.build()
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m tierlm_b200.build`")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def declared_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def errmsg() -> str:
+    return (load().tlmg_errmsg() or b"").decode(errors="replace")
+
+
+def check(rc: int) -> int:
+    if rc < 0:
+        raise TlmError(rc, errmsg())
+    return rc

@@ -1,0 +1,32 @@
+// tlmg_internal.h - host-side helpers shared by the library's .cu files.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/tlmg.h"
+
+namespace tlmg {
+
+// printf-style; stores the thread-local message and returns `code`.
+int set_error(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+// CUDA error -> TLMG_EIO with a message naming the failing step.
+int cuda_fail(cudaError_t e, const char *what);
+
+// The calling thread's library stream on the current device (created by
+// tlmg_init); `user` overrides it when non-NULL.
+cudaStream_t pick_stream(void *user);
+
+// Kernel launches issued through the library (host-side counter).
+void count_launch(int n = 1);
+int64_t launches_total();
+
+// Launchers of the kernel-level ops (also used by the layer code).
+int launch_quant_act(int kind, const float *x, int64_t n, void *dst, cudaStream_t st);
+int launch_matvec(int dt, const void *W, size_t rb, const void *act, float *y, int64_t n, int64_t r0,
+                  int64_t r1, cudaStream_t st);
+int launch_route(int router, const float *logits, const uint8_t *mask, const float *bias, int E, int k,
+                 float routed_scale, int32_t *ids, float *w, cudaStream_t st);
+
+bool is_device_ptr(const void *p);
+
+}  // namespace tlmg

@@ -1,0 +1,535 @@
+// tlmg_kernels.cu - kernel-level ops of the sm_100a tier: activation
+// quantisation, the generic row-matvec (drop-in for tlm_matvec_rows), exact
+// per-block partials, the router top-k, error handling and the host-buffer
+// adapters with the reference's tier-table signatures.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+#include <vector>
+
+#include "tlmg_dev.cuh"
+#include "tlmg_internal.h"
+
+namespace tlmg {
+
+// ---------------------------------------------------------------------------
+// errors (reference convention: src/lib/tlm_platform.h:23-41)
+static thread_local char t_errmsg[512];
+
+int set_error(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_errmsg, sizeof t_errmsg, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return set_error(TLMG_EIO, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+static std::atomic<int64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+int64_t launches_total() { return g_launches.load(std::memory_order_relaxed); }
+
+static thread_local cudaStream_t t_stream = nullptr;
+static thread_local int t_stream_dev = -1;
+
+cudaStream_t pick_stream(void *user) {
+    if (user) return (cudaStream_t)user;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!t_stream || t_stream_dev != dev) {
+        cudaStreamCreateWithFlags(&t_stream, cudaStreamNonBlocking);
+        t_stream_dev = dev;
+    }
+    return t_stream;
+}
+
+bool is_device_ptr(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// ---------------------------------------------------------------------------
+// activation quantisation: one warp per block
+__global__ void k_quant_q8k(const float *__restrict__ x, int64_t n, uint8_t *__restrict__ dst) {
+    int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (b * 256 >= n) return;
+    int64_t rem = n - b * 256;
+    warp_quant_q8k(x + b * 256, rem >= 256 ? 256 : (int)rem, dst + 292 * b, lane);
+}
+
+__global__ void k_quant_q80(const float *__restrict__ x, int64_t n, uint8_t *__restrict__ dst) {
+    int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int lane = threadIdx.x & 31;
+    if (b * 32 >= n) return;
+    int64_t rem = n - b * 32;
+    warp_quant_q80(x + b * 32, rem >= 32 ? 32 : (int)rem, dst + 36 * b, lane);
+}
+
+int launch_quant_act(int kind, const float *x, int64_t n, void *dst, cudaStream_t st) {
+    if (n <= 0) return TLMG_OK;
+    if (kind == DT_F32) {
+        cudaError_t e = cudaMemcpyAsync(dst, x, (size_t)n * 4, cudaMemcpyDeviceToDevice, st);
+        return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "quantize_act copy");
+    }
+    if (kind != DT_Q8_K && kind != DT_Q8_0)
+        return set_error(TLMG_EINVAL, "quantize_act: unsupported activation kind %d", kind);
+    int64_t nb = kind == DT_Q8_K ? (n + 255) / 256 : (n + 31) / 32;
+    const int wpb = 8;
+    unsigned grid = (unsigned)((nb + wpb - 1) / wpb);
+    if (kind == DT_Q8_K) k_quant_q8k<<<grid, 32 * wpb, 0, st>>>(x, n, (uint8_t *)dst);
+    else k_quant_q80<<<grid, 32 * wpb, 0, st>>>(x, n, (uint8_t *)dst);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "quantize_act launch");
+}
+
+// ---------------------------------------------------------------------------
+// generic row matvec. One warp per row; the 8-lane groups of the warp take
+// four blocks per pass, reduce each block's exact integer partials, and the
+// group leader stores (isum, msum, dA, dM) in shared memory; lane 0 then runs
+// the reference's serial fmaf chain over the blocks in ascending order.
+constexpr int MV_WARPS = 8;
+constexpr int MV_CHUNK = FCHUNK;
+
+template <int A>
+__global__ void __launch_bounds__(MV_WARPS * 32)
+k_matvec_q(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act,
+           float *__restrict__ y, int64_t n, int64_t r0, int64_t r1) {
+    __shared__ BlockPart part[MV_WARPS][MV_CHUNK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
+    const int qk = dt_block(dt), bb = dt_block_bytes(dt), abb = act_block_bytes(act_kind_for(dt));
+    const int nb = (int)(n / qk);
+    for (int64_t row = r0 + (int64_t)blockIdx.x * MV_WARPS + warp; row < r1;
+         row += (int64_t)gridDim.x * MV_WARPS) {
+        const uint8_t *wr = W + (size_t)row * rb;
+        float acc = 0.0f;
+        for (int c0 = 0; c0 < nb; c0 += MV_CHUNK) {
+            int nc = min(MV_CHUNK, nb - c0);
+            for (int p0 = 0; p0 < nc; p0 += 4) {
+                int p = p0 + g;
+                bool valid = p < nc;
+                int is = 0, ms = 0;
+                const uint8_t *blk = wr + (size_t)(c0 + p) * bb;
+                const uint8_t *ab = act + (size_t)(c0 + p) * abb;
+                if (valid) block_part<WLoad<A>>(dt, blk, ab, j, is, ms);
+                group8_sum(is, ms);
+                if (valid && j == 0) {
+                    float dA, dM;
+                    block_scales<WLoad<A>>(dt, blk, ab, dA, dM);
+                    part[warp][p] = BlockPart{ is, ms, dA, dM };
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                for (int p = 0; p < nc; p++) {
+                    BlockPart q = part[warp][p];
+                    acc = chain_step(dt, acc, q.dA, q.dM, q.is, q.ms);
+                }
+            __syncwarp();
+        }
+        if (lane == 0) y[row] = acc;
+    }
+}
+
+// Float weights: element i into lane i mod 32 with fmaf, then the fixed
+// tree (reference tlm_quant.c:724-770).
+template <int A>
+__global__ void __launch_bounds__(MV_WARPS * 32)
+k_matvec_f(int dt, const uint8_t *__restrict__ W, size_t rb, const float *__restrict__ x,
+           float *__restrict__ y, int64_t n, int64_t r0, int64_t r1) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t row = r0 + (int64_t)blockIdx.x * MV_WARPS + warp; row < r1;
+         row += (int64_t)gridDim.x * MV_WARPS) {
+        const uint8_t *wr = W + (size_t)row * rb;
+        float acc = 0.0f;
+        for (int64_t i = lane; i < n; i += 32) {
+            float w;
+            if (dt == DT_F32) w = __uint_as_float(WLoad<A>::u32(wr + 4 * i));
+            else if (dt == DT_F16) w = f16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
+            else w = bf16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
+            acc = __fmaf_rn(w, __ldg(x + i), acc);
+        }
+        acc = tree32(acc);
+        if (lane == 0) y[row] = acc;
+    }
+}
+
+static int align_of(uintptr_t a) {
+    if ((a & 15u) == 0) return 16;
+    if ((a & 3u) == 0) return 4;
+    if ((a & 1u) == 0) return 2;
+    return 1;
+}
+
+static unsigned mv_grid(int64_t rows) {
+    int64_t g = (rows + MV_WARPS - 1) / MV_WARPS;
+    if (g > 148 * 16) g = 148 * 16;
+    return (unsigned)(g < 1 ? 1 : g);
+}
+
+__global__ void k_fill_nan(float *y, int64_t r0, int64_t r1) {
+    int64_t r = r0 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < r1) y[r] = __uint_as_float(0x7FC00000u);
+}
+
+int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, int64_t n, int64_t r0,
+                  int64_t r1, cudaStream_t st) {
+    int qk = dt_block(dt);
+    if (qk == 0 || n < 0 || n % qk) {
+        if (r1 > r0) {
+            k_fill_nan<<<(unsigned)((r1 - r0 + 255) / 256), 256, 0, st>>>(y, r0, r1);
+            count_launch();
+        }
+        return set_error(TLMG_EINVAL, "matvec_rows: bad dtype %d or n=%lld", dt, (long long)n);
+    }
+    if (r1 <= r0) return TLMG_OK;
+    const uint8_t *W = (const uint8_t *)Wv;
+    int A = align_of((uintptr_t)W | (uintptr_t)rb | (uintptr_t)(qk > 1 ? dt_block_bytes(dt) : 16));
+    unsigned grid = mv_grid(r1 - r0);
+    const unsigned thr = MV_WARPS * 32;
+    if (qk == 1) {
+        const float *x = (const float *)act;
+        switch (A) {
+        case 16: case 4: k_matvec_f<4><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1); break;
+        case 2: k_matvec_f<2><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1); break;
+        default: k_matvec_f<1><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1); break;
+        }
+    } else {
+        const uint8_t *a = (const uint8_t *)act;
+        switch (A) {
+        case 16: k_matvec_q<16><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
+        case 4: k_matvec_q<4><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
+        case 2: k_matvec_q<2><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
+        default: k_matvec_q<1><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
+        }
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "matvec_rows launch");
+}
+
+// ---------------------------------------------------------------------------
+// exact per-block integer partials of rows [0, nrows)
+template <int A>
+__global__ void __launch_bounds__(MV_WARPS * 32)
+k_partials(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act, int64_t n,
+           int64_t nrows, int32_t *__restrict__ isum, int32_t *__restrict__ msum) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
+    const int qk = dt_block(dt), bb = dt_block_bytes(dt), abb = act_block_bytes(act_kind_for(dt));
+    const int nb = (int)(n / qk);
+    for (int64_t row = (int64_t)blockIdx.x * MV_WARPS + warp; row < nrows; row += (int64_t)gridDim.x * MV_WARPS) {
+        const uint8_t *wr = W + (size_t)row * rb;
+        for (int p0 = 0; p0 < nb; p0 += 4) {
+            int p = p0 + g;
+            bool valid = p < nb;
+            int is = 0, ms = 0;
+            if (valid) block_part<WLoad<A>>(dt, wr + (size_t)p * bb, act + (size_t)p * abb, j, is, ms);
+            group8_sum(is, ms);
+            if (valid && j == 0) {
+                isum[row * nb + p] = is;
+                msum[row * nb + p] = ms;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// router top-k (reference tlm_model.c:776-839), one warp. Entry e lives in
+// lane e % 32, slot e / 32.
+constexpr int RT_PER = 16;   // E <= 512
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+    // larger value wins; equal values -> lower index; bi < 0 = nothing yet
+    return bi < 0 || v > bv || (v == bv && i < bi);
+}
+
+// Top-k of v[] over entries not masked, not NaN, not used; fallback = lowest
+// unmasked unused index, else 0 (reference topk, tlm_model.c:776-795).
+__device__ void warp_topk(const float (&v)[RT_PER], const bool (&off)[RT_PER], int E, int k, int lane,
+                          int32_t *ids_sm) {
+    bool used[RT_PER];
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) used[s] = false;
+    for (int r = 0; r < k; r++) {
+        float bv = 0.0f;
+        int bi = -1;
+        int fb = -1;   // lowest unmasked unused index of this lane
+#pragma unroll
+        for (int s = 0; s < RT_PER; s++) {
+            int e = lane + 32 * s;
+            if (e >= E || off[s] || used[s]) continue;
+            if (fb < 0) fb = e;
+            if (v[s] != v[s]) continue;
+            if (better(v[s], e, bv, bi)) { bv = v[s]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+            int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+            int of = __shfl_xor_sync(0xFFFFFFFFu, fb, o);
+            if (oi >= 0 && better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+            if (of >= 0 && (fb < 0 || of < fb)) fb = of;
+        }
+        int pick = bi >= 0 ? bi : (fb >= 0 ? fb : 0);
+        if ((pick & 31) == lane && pick < E) used[pick >> 5] = true;
+        if (lane == 0) ids_sm[r] = pick;
+    }
+}
+
+__global__ void k_route(int router, const float *__restrict__ logits, const uint8_t *__restrict__ mask,
+                        const float *__restrict__ bias, int E, int k, float routed_scale, int32_t *ids,
+                        float *w) {
+    __shared__ float p_sm[RT_PER * 32];
+    __shared__ int32_t ids_sm[64];
+    const int lane = threadIdx.x;
+    float p[RT_PER], v[RT_PER];
+    bool off[RT_PER];
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        off[s] = e < E ? (mask && mask[e]) : true;
+        p[s] = 0.0f;
+        v[s] = 0.0f;
+    }
+    if (router == 2) {
+#pragma unroll
+        for (int s = 0; s < RT_PER; s++) {
+            int e = lane + 32 * s;
+            if (e >= E) continue;
+            p[s] = sigmoid_f(logits[e]);
+            v[s] = __fadd_rn(p[s], bias ? bias[e] : 0.0f);
+            p_sm[e] = p[s];
+        }
+        warp_topk(v, off, E, k, lane, ids_sm);
+        __syncwarp();
+        if (lane == 0) {
+            double s = 0.0;
+            for (int r = 0; r < k; r++) s = __dadd_rn(s, (double)p_sm[ids_sm[r]]);
+            float inv = __double2float_rn(__ddiv_rn(1.0, __dadd_rn(s, 1e-20)));
+            for (int r = 0; r < k; r++) {
+                ids[r] = ids_sm[r];
+                w[r] = __fmul_rn(__fmul_rn(p_sm[ids_sm[r]], inv), routed_scale);
+            }
+        }
+        return;
+    }
+    // softmax over routable entries
+    float mx = -__uint_as_float(0x7F800000u);
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        if (e < E && !off[s]) {
+            float l = logits[e];
+            if (l > mx) mx = l;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    const bool none = mx == -__uint_as_float(0x7F800000u);
+    double part = 0.0;
+    uint32_t min_bits = 0x7F800000u;   // smallest nonzero p seen
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        if (e >= E) continue;
+        float l = logits[e];
+        p[s] = (off[s] || !(l == l) || none) ? 0.0f : cr_expf(__fsub_rn(l, mx));
+        p_sm[e] = p[s];
+        part = __dadd_rn(part, (double)p[s]);
+        if (p[s] != 0.0f) min_bits = min(min_bits, __float_as_uint(p[s]));
+    }
+    // The reference sums in double, sequentially in index order. When every
+    // nonzero term is >= 2^(floor(log2 E) - 29) all partial sums are exact
+    // in double, so any order gives the same sum; otherwise lane 0 redoes it
+    // sequentially.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        part = __dadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, o));
+        min_bits = min(min_bits, __shfl_xor_sync(0xFFFFFFFFu, min_bits, o));
+    }
+    int lg = 31 - __clz(E);
+    bool exact = min_bits == 0x7F800000u || __uint_as_float(min_bits) >= ldexpf(1.0f, lg - 29);
+    __syncwarp();
+    double sum = part;
+    if (!exact) {
+        if (lane == 0) {
+            double s = 0.0;
+            for (int e = 0; e < E; e++) s = __dadd_rn(s, (double)p_sm[e]);
+            part = s;
+        }
+        sum = __shfl_sync(0xFFFFFFFFu, part, 0);
+    }
+    float inv = sum > 0.0 ? __double2float_rn(__ddiv_rn(1.0, sum)) : 0.0f;
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        if (e < E) {
+            p[s] = __fmul_rn(p[s], inv);
+            p_sm[e] = p[s];
+        }
+    }
+    warp_topk(p, off, E, k, lane, ids_sm);
+    __syncwarp();
+    if (lane == 0) {
+        float wr[64];
+        for (int r = 0; r < k; r++) wr[r] = p_sm[ids_sm[r]];
+        if (router == 0) {
+            double t = 0.0;
+            for (int r = 0; r < k; r++) t = __dadd_rn(t, (double)wr[r]);
+            if (t > 0.0) {
+                float it = __double2float_rn(__ddiv_rn(1.0, t));
+                for (int r = 0; r < k; r++) wr[r] = __fmul_rn(wr[r], it);
+            }
+        }
+        if (routed_scale != 1.0f)
+            for (int r = 0; r < k; r++) wr[r] = __fmul_rn(wr[r], routed_scale);
+        for (int r = 0; r < k; r++) {
+            ids[r] = ids_sm[r];
+            w[r] = wr[r];
+        }
+    }
+}
+
+int launch_route(int router, const float *logits, const uint8_t *mask, const float *bias, int E, int k,
+                 float routed_scale, int32_t *ids, float *w, cudaStream_t st) {
+    if (E <= 0 || E > RT_PER * 32 || k <= 0 || k > E || k > 64 || router < 0 || router > 2)
+        return set_error(TLMG_EINVAL, "route: unsupported E=%d k=%d router=%d (E <= %d, k <= 64)", E, k,
+                         router, RT_PER * 32);
+    k_route<<<1, 32, 0, st>>>(router, logits, mask, bias, E, k, routed_scale, ids, w);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "route launch");
+}
+
+}  // namespace tlmg
+
+using namespace tlmg;
+
+// ---------------------------------------------------------------------------
+// C ABI (kernel level)
+extern "C" {
+
+const char *tlmg_errmsg(void) { return t_errmsg; }
+const char *tlmg_tier(void) { return "cuda-sm100a"; }
+
+int tlmg_init(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return set_error(TLMG_EUNSUP, "no CUDA device (%s)", cudaGetErrorString(e));
+    if (device < 0 || device >= n) return set_error(TLMG_EINVAL, "device %d out of range (have %d)", device, n);
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    cudaDeviceProp prop;
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major != 10) return set_error(TLMG_EUNSUP, "device %d is sm_%d%d; this library is built for sm_100a",
+                                           device, prop.major, prop.minor);
+    pick_stream(nullptr);
+    return TLMG_OK;
+}
+
+int tlmg_sync(void *stream) {
+    cudaError_t e = cudaStreamSynchronize(pick_stream(stream));
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "stream synchronize");
+}
+
+int tlmg_dtype_block(int dt) { return dt_block(dt); }
+size_t tlmg_dtype_block_bytes(int dt) { return (size_t)dt_block_bytes(dt); }
+size_t tlmg_row_bytes(int dt, int64_t n) {
+    int qk = dt_block(dt);
+    if (!qk || n < 0 || n % qk) return 0;
+    return (size_t)(n / qk) * (size_t)dt_block_bytes(dt);
+}
+size_t tlmg_qact_bytes(int kind, int64_t n) {
+    if (n < 0) return 0;
+    if (kind == DT_Q8_K) return (size_t)((n + 255) / 256) * 292u;
+    if (kind == DT_Q8_0) return (size_t)((n + 31) / 32) * 36u;
+    if (kind == DT_F32) return (size_t)n * 4u;
+    return 0;
+}
+int tlmg_act_kind_for(int wdt) { return act_kind_for(wdt); }
+
+int tlmg_quantize_act(int kind, const float *x, int64_t n, void *dst, void *stream) {
+    return launch_quant_act(kind, x, n, dst, pick_stream(stream));
+}
+
+int tlmg_matvec_rows(int dt, const void *W, size_t row_bytes, const void *act, float *y, int64_t n, int64_t r0,
+                     int64_t r1, void *stream) {
+    return launch_matvec(dt, W, row_bytes, act, y, n, r0, r1, pick_stream(stream));
+}
+
+int tlmg_block_partials(int dt, const void *W, size_t row_bytes, const void *act, int64_t n, int64_t nrows,
+                        int32_t *isum, int32_t *msum, void *stream) {
+    int qk = dt_block(dt);
+    if (qk <= 1 || n < 0 || n % qk) return set_error(TLMG_EINVAL, "block_partials: bad dtype %d or n=%lld", dt, (long long)n);
+    if (nrows <= 0) return TLMG_OK;
+    cudaStream_t st = pick_stream(stream);
+    const uint8_t *Wb = (const uint8_t *)W;
+    const uint8_t *a = (const uint8_t *)act;
+    int A = align_of((uintptr_t)Wb | (uintptr_t)row_bytes | (uintptr_t)dt_block_bytes(dt));
+    unsigned grid = mv_grid(nrows);
+    const unsigned thr = MV_WARPS * 32;
+    switch (A) {
+    case 16: k_partials<16><<<grid, thr, 0, st>>>(dt, Wb, row_bytes, a, n, nrows, isum, msum); break;
+    case 4: k_partials<4><<<grid, thr, 0, st>>>(dt, Wb, row_bytes, a, n, nrows, isum, msum); break;
+    case 2: k_partials<2><<<grid, thr, 0, st>>>(dt, Wb, row_bytes, a, n, nrows, isum, msum); break;
+    default: k_partials<1><<<grid, thr, 0, st>>>(dt, Wb, row_bytes, a, n, nrows, isum, msum); break;
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "block_partials launch");
+}
+
+int tlmg_route(int router, const float *logits, const uint8_t *mask, const float *bias, int E, int k,
+               float routed_scale, int32_t *ids, float *w, void *stream) {
+    return launch_route(router, logits, mask, bias, E, k, routed_scale, ids, w, pick_stream(stream));
+}
+
+// Host-buffer adapters for the reference's tier table (tlm_qmv_fn /
+// tlm_qdot_fn). Synchronous; NaN on any failure.
+void tlmg_qmv_host(int dt, const void *W, size_t row_bytes, const void *act, float *y, int64_t n, int64_t nrows) {
+    if (nrows <= 0) return;
+    auto fail = [&](int code, const char *what) {
+        set_error(code, "qmv_host: %s", what);
+        for (int64_t r = 0; r < nrows; r++) y[r] = NAN;
+    };
+    int qk = dt_block(dt);
+    if (!qk || n < 0 || n % qk) return fail(TLMG_EINVAL, "bad dtype or width");
+    size_t wbytes = (size_t)(nrows - 1) * row_bytes + tlmg_row_bytes(dt, n);
+    size_t abytes = qk == 1 ? (size_t)n * 4 : tlmg_qact_bytes(act_kind_for(dt), n);
+    size_t woff = (uintptr_t)W & 15u;   // keep the caller's byte alignment
+    cudaStream_t st = pick_stream(nullptr);
+    uint8_t *dW = nullptr, *dA = nullptr;
+    float *dy = nullptr;
+    if (cudaMalloc(&dW, wbytes + woff + 16) != cudaSuccess || cudaMalloc(&dA, abytes + 16) != cudaSuccess ||
+        cudaMalloc(&dy, (size_t)nrows * 4) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFree(dW); cudaFree(dA); cudaFree(dy);
+        return fail(TLMG_ENOMEM, "device allocation failed");
+    }
+    bool ok = cudaMemcpyAsync(dW + woff, W, wbytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+              cudaMemcpyAsync(dA, act, abytes, cudaMemcpyHostToDevice, st) == cudaSuccess;
+    if (ok) ok = launch_matvec(dt, dW + woff, row_bytes, dA, dy, n, 0, nrows, st) == TLMG_OK;
+    if (ok) ok = cudaMemcpyAsync(y, dy, (size_t)nrows * 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    if (ok) ok = cudaStreamSynchronize(st) == cudaSuccess;
+    cudaFree(dW); cudaFree(dA); cudaFree(dy);
+    if (!ok) fail(TLMG_EIO, "device copy or launch failed");
+}
+
+float tlmg_qdot_host(int dt, const void *wrow, const void *act, int64_t n) {
+    float y = NAN;
+    tlmg_qmv_host(dt, wrow, tlmg_row_bytes(dt, n), act, &y, n, 1);
+    return y;
+}
+
+}  // extern "C"

@@ -1,0 +1,846 @@
+// tlmg_moe.cu - layer level of the sm_100a tier: HBM-resident expert slots,
+// the routed-expert FFN (gate/up + SwiGLU, re-quantisation, down + the
+// rank-ordered weighted combine) and the whole moe() block.
+//
+// Reference: moe() / run_batch() / expert_mats(), src/lib/tlm_model.c:880-1055.
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "tlmg_dev.cuh"
+#include "tlmg_fused.cuh"
+#include "tlmg_internal.h"
+
+namespace tlmg {
+
+// Bump allocator for expert slots: large cudaMalloc chunks, 256-byte
+// aligned sub-allocations, freed together with the context.
+struct Arena {
+    std::vector<void *> chunks;
+    uint8_t *cur = nullptr;
+    size_t left = 0;
+    static constexpr size_t kChunk = size_t(256) << 20;
+    void *get(size_t bytes) {
+        bytes = (bytes + 255) & ~size_t(255);
+        if (bytes > left) {
+            size_t sz = bytes > kChunk ? bytes : kChunk;
+            void *p = nullptr;
+            if (cudaMalloc(&p, sz) != cudaSuccess) {
+                cudaGetLastError();
+                return nullptr;
+            }
+            chunks.push_back(p);
+            cur = (uint8_t *)p;
+            left = sz;
+        }
+        void *r = cur;
+        cur += bytes;
+        left -= bytes;
+        return r;
+    }
+    void release() {
+        for (void *p : chunks) cudaFree(p);
+        chunks.clear();
+        cur = nullptr;
+        left = 0;
+    }
+};
+
+struct Layer {
+    Slot *d_slots = nullptr;       // [E] on the device
+    std::vector<Slot> h_slots;     // host mirror
+    bool slots_dirty = false;
+    float *ffn_norm = nullptr;
+    int router_dt = -1;
+    void *router_w = nullptr;
+    size_t router_rb = 0;
+    float *router_bias = nullptr;
+    uint8_t *mask = nullptr;
+    bool has_shared = false;
+    int sh_dt[3] = { 0, 0, 0 };
+    void *sh_w[3] = { nullptr, nullptr, nullptr };
+    float *sh_gate_inp = nullptr;
+};
+
+}  // namespace tlmg
+
+using namespace tlmg;
+
+struct tlmg_ctx {
+    tlmg_geom g;
+    int device = 0;
+    cudaStream_t st = nullptr;       // where work is queued (own_st or the caller's)
+    cudaStream_t own_st = nullptr;
+    std::vector<Layer> L;
+    Arena arena;
+    std::vector<void *> owned;     // other device allocations
+    // device scratch for one token
+    float *x = nullptr, *logits = nullptr, *ffn = nullptr, *h = nullptr, *hbuf = nullptr;
+    uint8_t *xq8k = nullptr, *xq80 = nullptr, *hq = nullptr;
+    int32_t *ids = nullptr;
+    float *w = nullptr;
+    size_t hq_stride = 0;
+    float *sg = nullptr, *sh = nullptr, *s_out = nullptr, *sgate = nullptr;
+    uint8_t *shq = nullptr;
+    // many-token scratch
+    float *mx = nullptr, *mlog = nullptr, *mffn = nullptr;
+    int m_cap = 0;
+    // pinned staging
+    uint8_t *pin = nullptr;
+    size_t pin_cap = 0;
+    int64_t launch0 = 0;
+    FusedScratch fused;
+    // per-launch event timing (tlmg_profile)
+    bool prof = false;
+    std::vector<cudaEvent_t> ev_pool;
+    struct Mark { int cls; cudaEvent_t a, b; };
+    std::vector<Mark> marks;
+    int64_t prof_bytes[3] = { 0, 0, 0 };
+};
+
+namespace tlmg {
+
+static void *dalloc(tlmg_ctx *c, size_t bytes) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes ? bytes : 16) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    c->owned.push_back(p);
+    return p;
+}
+
+static int ensure_pin(tlmg_ctx *c, size_t bytes) {
+    if (bytes <= c->pin_cap) return TLMG_OK;
+    if (c->pin) cudaFreeHost(c->pin);
+    c->pin = nullptr;
+    c->pin_cap = 0;
+    if (cudaMallocHost(&c->pin, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(TLMG_ENOMEM, "pinned staging of %zu bytes failed", bytes);
+    }
+    c->pin_cap = bytes;
+    return TLMG_OK;
+}
+
+static int check_layer(tlmg_ctx *c, int layer) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    if (layer < 0 || layer >= c->g.n_layers)
+        return set_error(TLMG_ERANGE, "layer %d out of range [0, %d)", layer, c->g.n_layers);
+    return TLMG_OK;
+}
+
+static int sync_slots(tlmg_ctx *c, Layer &Ly) {
+    if (!Ly.slots_dirty) return TLMG_OK;
+    cudaError_t e = cudaMemcpy(Ly.d_slots, Ly.h_slots.data(), sizeof(Slot) * Ly.h_slots.size(),
+                               cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "slot table upload");
+    Ly.slots_dirty = false;
+    return TLMG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// kernels
+
+// Dot of one weight row with an activation, by one warp, result in lane 0.
+template <class LD>
+__device__ __forceinline__ float warp_row_dot_t(int dt, const uint8_t *wr, const uint8_t *act, int nb,
+                                                BlockPart *part, int lane) {
+    const int g = lane >> 3, j = lane & 7, bb = dt_block_bytes(dt), abb = act_block_bytes(act_kind_for(dt));
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < nb; c0 += FCHUNK) {
+        int nc = min(FCHUNK, nb - c0);
+        for (int p0 = 0; p0 < nc; p0 += 4) {
+            int p = p0 + g;
+            bool valid = p < nc;
+            int is = 0, ms = 0;
+            const uint8_t *blk = wr + (size_t)(c0 + p) * bb;
+            const uint8_t *ab = act + (size_t)(c0 + p) * abb;
+            if (valid) block_part<LD>(dt, blk, ab, j, is, ms);
+            group8_sum(is, ms);
+            if (valid && j == 0) {
+                float dA, dM;
+                block_scales<LD>(dt, blk, ab, dA, dM);
+                part[p] = BlockPart{ is, ms, dA, dM };
+            }
+        }
+        __syncwarp();
+        if (lane == 0)
+            for (int p = 0; p < nc; p++) acc = chain_step(dt, acc, part[p].dA, part[p].dM, part[p].is, part[p].ms);
+        __syncwarp();
+    }
+    return acc;
+}
+
+// Slot matrices start 256-byte aligned, so a block's alignment follows from
+// its dtype's block size.
+__device__ __forceinline__ float warp_row_dot(int dt, const uint8_t *wr, const uint8_t *act, int nb,
+                                              BlockPart *part, int lane) {
+    switch (dt) {
+    case DT_Q4_K: case DT_Q5_K: return warp_row_dot_t<WLoad<16>>(dt, wr, act, nb, part, lane);
+    case DT_Q8_K: return warp_row_dot_t<WLoad<4>>(dt, wr, act, nb, part, lane);
+    case DT_Q6_K: case DT_Q8_0: return warp_row_dot_t<WLoad<2>>(dt, wr, act, nb, part, lane);
+    default: return warp_row_dot_t<WLoad<1>>(dt, wr, act, nb, part, lane);
+    }
+}
+
+constexpr int FFN_WARPS = 8;
+
+// gate/up rows of the k selected experts + SwiGLU: one warp per (rank, row).
+__global__ void __launch_bounds__(FFN_WARPS * 32)
+k_ffn_gateup(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, int k, int D, int de,
+             const uint8_t *__restrict__ xq8k, const uint8_t *__restrict__ xq80, float *__restrict__ hbuf) {
+    __shared__ BlockPart part[FFN_WARPS][FCHUNK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t p = (int64_t)blockIdx.x * FFN_WARPS + warp; p < (int64_t)k * de; p += (int64_t)gridDim.x * FFN_WARPS) {
+        int r = (int)(p / de), j = (int)(p % de);
+        Slot s = slots[ids[r]];
+        float gu[2];
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            int dt = s.dt[m];
+            const uint8_t *act = act_kind_for(dt) == DT_Q8_0 ? xq80 : xq8k;
+            size_t rb = (size_t)(D / dt_block(dt)) * dt_block_bytes(dt);
+            gu[m] = warp_row_dot(dt, s.m[m] + (size_t)j * rb, act, D / dt_block(dt), part[warp], lane);
+        }
+        if (lane == 0) hbuf[p] = __fmul_rn(silu_f(gu[0]), gu[1]);
+    }
+}
+
+// Re-quantise SwiGLU rows per rank with the activation kind of that
+// expert's down matrix: one warp per activation block.
+__global__ void k_quant_h(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, int k, int de,
+                          const float *__restrict__ hbuf, uint8_t *__restrict__ hq, size_t hq_stride) {
+    const int lane = threadIdx.x & 31;
+    int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    int nb8k = (de + 255) / 256, nb80 = (de + 31) / 32;
+    int per = nb80 > nb8k ? nb80 : nb8k;
+    int r = (int)(wid / per), b = (int)(wid % per);
+    if (r >= k) return;
+    int kind = act_kind_for(slots[ids[r]].dt[2]);
+    const float *h = hbuf + (size_t)r * de;
+    uint8_t *dst = hq + hq_stride * r;
+    if (kind == DT_Q8_K) {
+        if (b < nb8k) warp_quant_q8k(h + 256 * b, min(256, de - 256 * b), dst + 292 * b, lane);
+    } else {
+        if (b < nb80) warp_quant_q80(h + 32 * b, min(32, de - 32 * b), dst + 36 * b, lane);
+    }
+}
+
+// down rows of all k experts + rank-ordered combine: one warp per output
+// row i. ffn[i] = sum_r w[r]*eo_r[i] (product rounded, then added; ascending
+// r). With s_out: ffn[i] += sgate * s_out[i]. With h: h[i] += ffn[i].
+__global__ void __launch_bounds__(FFN_WARPS * 32)
+k_ffn_down(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, const float *__restrict__ w, int k,
+           int D, int de, const uint8_t *__restrict__ hq, size_t hq_stride, const float *__restrict__ s_out,
+           const float *__restrict__ sgate, float *__restrict__ ffn, float *__restrict__ h) {
+    __shared__ BlockPart part[FFN_WARPS][FCHUNK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = blockIdx.x * FFN_WARPS + warp; i < D; i += gridDim.x * FFN_WARPS) {
+        float acc = 0.0f;
+        for (int r = 0; r < k; r++) {
+            Slot s = slots[ids[r]];
+            int dt = s.dt[2];
+            size_t rb = (size_t)(de / dt_block(dt)) * dt_block_bytes(dt);
+            float eo = warp_row_dot(dt, s.m[2] + (size_t)i * rb, hq + hq_stride * r, de / dt_block(dt), part[warp], lane);
+            acc = __fadd_rn(acc, __fmul_rn(w[r], eo));
+        }
+        if (lane == 0) {
+            if (s_out) acc = __fadd_rn(acc, __fmul_rn(*sgate, s_out[i]));
+            ffn[i] = acc;
+            if (h) h[i] = __fadd_rn(h[i], acc);
+        }
+    }
+}
+
+// RMSNorm (reference tlm_model.c:164-169): the sum of squares is a double
+// sum in index order. A fixed tree gives the same float after the division
+// unless the value lies within the two sums' combined error bound of a float
+// rounding boundary; then thread 0 redoes the sequential sum.
+__global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ wn, int n, float eps,
+                          float *__restrict__ out) {
+    __shared__ double red[32];
+    __shared__ float r_sh;
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __dadd_rn(s, __dmul_rn((double)x[i], (double)x[i]));
+    for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int q = 0; q < (int)(blockDim.x >> 5); q++) t = __dadd_rn(t, red[q]);
+        double bound = __dmul_rn(t, __dmul_rn(2.0 * (double)n + 8.0, 0x1p-53));
+        float flo = __double2float_rn(__ddiv_rn(__dsub_rn(t, bound), (double)n));
+        float fhi = __double2float_rn(__ddiv_rn(__dadd_rn(t, bound), (double)n));
+        float f;
+        if (flo == fhi) {
+            f = flo;
+        } else {
+            double q = 0.0;
+            for (int i = 0; i < n; i++) q = __dadd_rn(q, __dmul_rn((double)x[i], (double)x[i]));
+            f = __double2float_rn(__ddiv_rn(q, (double)n));
+        }
+        r_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, eps)));
+    }
+    __syncthreads();
+    float r = r_sh;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], r), wn[i]);
+}
+
+// silu(g)*u over a shared-expert row pair buffer [g | u].
+__global__ void k_swiglu(const float *__restrict__ gu, int n, float *__restrict__ h) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = __fmul_rn(silu_f(gu[i]), gu[n + i]);
+}
+
+// sgate = sigmoid(sum_i g[i]*x[i]) as a sequential float sum (reference
+// tlm_model.c:1039-1044).
+__global__ void k_shared_gate(const float *__restrict__ g, const float *__restrict__ x, int n, float *out) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    float d = 0.0f;
+    for (int i = 0; i < n; i++) d = __fadd_rn(d, __fmul_rn(g[i], x[i]));
+    *out = sigmoid_f(d);
+}
+
+static int launched(const char *what) {
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, what);
+}
+
+static cudaEvent_t prof_event(tlmg_ctx *c) {
+    cudaEvent_t e = nullptr;
+    if (!c->ev_pool.empty()) {
+        e = c->ev_pool.back();
+        c->ev_pool.pop_back();
+    } else if (cudaEventCreate(&e) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return e;
+}
+
+// Bracket one launch of kernel class `cls`: call with begin = true before
+// the launch and false after it.
+static void prof_mark(tlmg_ctx *c, int cls, bool begin) {
+    if (!c->prof) return;
+    if (begin) {
+        cudaEvent_t a = prof_event(c);
+        if (!a) return;
+        cudaEventRecord(a, c->st);
+        c->marks.push_back({ cls, a, nullptr });
+    } else if (!c->marks.empty() && c->marks.back().b == nullptr && c->marks.back().cls == cls) {
+        cudaEvent_t b = prof_event(c);
+        if (!b) return;
+        cudaEventRecord(b, c->st);
+        c->marks.back().b = b;
+    }
+}
+
+// Algorithmic weight bytes of one launch per class, from slot 0's dtypes.
+static void prof_bytes(tlmg_ctx *c, const Layer &Ly) {
+    if (!c->prof || Ly.h_slots.empty()) return;
+    const Slot &s = Ly.h_slots[0];
+    const int64_t D = c->g.d_model, de = c->g.d_expert, k = c->g.top_k;
+    int64_t gu = k * de * (int64_t)(tlmg_row_bytes(s.dt[0], D) + tlmg_row_bytes(s.dt[1], D));
+    int64_t dn = k * D * (int64_t)tlmg_row_bytes(s.dt[2], de);
+    bool fused = c->fused.enabled;
+    c->prof_bytes[0] = fused ? gu + dn : gu;
+    c->prof_bytes[1] = dn;
+    c->prof_bytes[2] = 4 * (int64_t)c->g.n_experts;
+}
+
+// x (device f32[D], normalised) -> the activation kinds the layer needs.
+static int quant_inputs(tlmg_ctx *c, const float *x) {
+    int rc = launch_quant_act(DT_Q8_K, x, c->g.d_model, c->xq8k, c->st);
+    if (rc == TLMG_OK && c->g.d_model % 32 == 0) rc = launch_quant_act(DT_Q8_0, x, c->g.d_model, c->xq80, c->st);
+    return rc;
+}
+
+// Routed experts for one token on the device: logits -> ids/w -> ffn (and
+// h += ffn when h != NULL). Inputs already quantised in xq8k / xq80.
+static int run_experts(tlmg_ctx *c, Layer &Ly, const float *logits, float *ffn, float *h, const float *s_out,
+                       const float *sgate, const float *x) {
+    const tlmg_geom &g = c->g;
+    prof_bytes(c, Ly);
+    prof_mark(c, 2, true);
+    int rc = launch_route(g.router, logits, Ly.mask, Ly.router_bias, g.n_experts, g.top_k, g.routed_scale, c->ids,
+                          c->w, c->st);
+    prof_mark(c, 2, false);
+    if (rc) return rc;
+    if (use_fused(c->fused, g, x != nullptr)) {
+        prof_mark(c, 0, true);
+        rc = launch_fused_ffn(c->fused, g, Ly.d_slots, c->ids, c->w, x, ffn, h, s_out, sgate, c->st);
+        prof_mark(c, 0, false);
+        return rc;
+    }
+    int k = g.top_k, D = g.d_model, de = g.d_expert;
+    unsigned grid = (unsigned)std::min<int64_t>(((int64_t)k * de + FFN_WARPS - 1) / FFN_WARPS, 148 * 8);
+    prof_mark(c, 0, true);
+    k_ffn_gateup<<<grid, FFN_WARPS * 32, 0, c->st>>>(Ly.d_slots, c->ids, k, D, de, c->xq8k, c->xq80, c->hbuf);
+    prof_mark(c, 0, false);
+    if ((rc = launched("ffn gate/up"))) return rc;
+    int per = std::max((de + 255) / 256, (de + 31) / 32);
+    int64_t nw = (int64_t)k * per;
+    k_quant_h<<<(unsigned)((nw + 7) / 8), 256, 0, c->st>>>(Ly.d_slots, c->ids, k, de, c->hbuf, c->hq, c->hq_stride);
+    if ((rc = launched("ffn requant"))) return rc;
+    prof_mark(c, 1, true);
+    k_ffn_down<<<(unsigned)std::min(148 * 8, (D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, c->st>>>(
+        Ly.d_slots, c->ids, c->w, k, D, de, c->hq, c->hq_stride, s_out, sgate, ffn, h);
+    prof_mark(c, 1, false);
+    return launched("ffn down");
+}
+
+static bool layer_ready(tlmg_ctx *c, Layer &Ly) {
+    for (const Slot &s : Ly.h_slots)
+        if (!s.ok) return false;
+    return !Ly.h_slots.empty();
+}
+
+// Device-pointer core of tlmg_expert_ffn.
+static int expert_ffn_dev(tlmg_ctx *c, int layer, const float *x, const float *logits, float *ffn) {
+    Layer &Ly = c->L[layer];
+    int rc = sync_slots(c, Ly);
+    if (rc) return rc;
+    if (!layer_ready(c, Ly)) return set_error(TLMG_ENOTFOUND, "layer %d: not every expert slot is loaded", layer);
+    if ((rc = quant_inputs(c, x))) return rc;
+    return run_experts(c, Ly, logits, ffn, nullptr, nullptr, nullptr, x);
+}
+
+enum PtrKind { PK_DEVICE, PK_PINNED, PK_PAGEABLE };
+static PtrKind ptr_kind(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return PK_PAGEABLE;
+    }
+    if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) return PK_DEVICE;
+    if (a.type == cudaMemoryTypeHost) return PK_PINNED;
+    return PK_PAGEABLE;
+}
+
+// host -> device copy of `bytes` from src into dst (device), through the
+// pinned staging area at `stage_off` when src is pageable.
+static int h2d(tlmg_ctx *c, void *dst, const void *src, size_t bytes, PtrKind k, size_t stage_off) {
+    const void *from = src;
+    if (k == PK_PAGEABLE) {
+        memcpy(c->pin + stage_off, src, bytes);
+        from = c->pin + stage_off;
+    }
+    cudaError_t e = cudaMemcpyAsync(dst, from, bytes, cudaMemcpyHostToDevice, c->st);
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "host to device copy");
+}
+
+static int d2h(tlmg_ctx *c, void *dst, const void *src, size_t bytes, PtrKind k, size_t stage_off) {
+    void *to = k == PK_PAGEABLE ? (void *)(c->pin + stage_off) : dst;
+    cudaError_t e = cudaMemcpyAsync(to, src, bytes, cudaMemcpyDeviceToHost, c->st);
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "device to host copy");
+}
+
+static int finish_d2h(tlmg_ctx *c, void *dst, size_t bytes, PtrKind k, size_t stage_off) {
+    if (k == PK_PAGEABLE) memcpy(dst, c->pin + stage_off, bytes);
+    return TLMG_OK;
+}
+
+static int stream_sync(tlmg_ctx *c) {
+    cudaError_t e = cudaStreamSynchronize(c->st);
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "stream synchronize");
+}
+
+
+
+}  // namespace tlmg
+
+// ---------------------------------------------------------------------------
+// C ABI (layer level)
+extern "C" {
+
+int tlmg_open(const tlmg_geom *g, int device, tlmg_ctx **out) {
+    if (!g || !out) return set_error(TLMG_EINVAL, "tlmg_open: NULL argument");
+    *out = nullptr;
+    if (g->n_layers <= 0 || g->d_model <= 0 || g->n_experts < 0 || g->top_k < 0 || g->d_expert < 0 ||
+        g->d_shared < 0 || (g->n_experts > 0 && (g->top_k == 0 || g->top_k > g->n_experts || g->top_k > 64)) ||
+        g->n_experts > 512 || g->router < 0 || g->router > 2)
+        return set_error(TLMG_EINVAL, "tlmg_open: bad geometry (layers %d, D %d, E %d, k %d, de %d, router %d)",
+                         g->n_layers, g->d_model, g->n_experts, g->top_k, g->d_expert, g->router);
+    if (g->d_model % 256 || g->d_expert % 256 || g->d_shared % 256)
+        return set_error(TLMG_EINVAL, "tlmg_open: d_model, d_expert, d_shared must be multiples of 256");
+    int rc = tlmg_init(device);
+    if (rc) return rc;
+    tlmg_ctx *c = new tlmg_ctx();
+    c->g = *g;
+    c->device = device;
+    if (cudaStreamCreateWithFlags(&c->own_st, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return set_error(TLMG_EIO, "stream creation failed");
+    }
+    c->st = c->own_st;
+    int D = g->d_model, de = g->d_expert > 0 ? g->d_expert : 256, E = g->n_experts > 0 ? g->n_experts : 1;
+    int k = g->top_k > 0 ? g->top_k : 1, ds = g->d_shared > 0 ? g->d_shared : 256;
+    c->hq_stride = (std::max(tlmg_qact_bytes(DT_Q8_K, de), tlmg_qact_bytes(DT_Q8_0, de)) + 255) & ~size_t(255);
+    size_t xq = std::max(tlmg_qact_bytes(DT_Q8_K, D), tlmg_qact_bytes(DT_Q8_0, D)) + 256;
+    bool ok = (c->x = (float *)dalloc(c, 4 * (size_t)D)) && (c->logits = (float *)dalloc(c, 4 * (size_t)E)) &&
+              (c->ffn = (float *)dalloc(c, 4 * (size_t)D)) && (c->h = (float *)dalloc(c, 4 * (size_t)D)) &&
+              (c->hbuf = (float *)dalloc(c, 4 * (size_t)k * de)) && (c->xq8k = (uint8_t *)dalloc(c, xq)) &&
+              (c->xq80 = (uint8_t *)dalloc(c, xq)) && (c->hq = (uint8_t *)dalloc(c, c->hq_stride * k)) &&
+              (c->ids = (int32_t *)dalloc(c, 4 * 64)) && (c->w = (float *)dalloc(c, 4 * 64)) &&
+              (c->sg = (float *)dalloc(c, 8 * (size_t)ds)) && (c->sh = (float *)dalloc(c, 4 * (size_t)ds)) &&
+              (c->s_out = (float *)dalloc(c, 4 * (size_t)D)) && (c->sgate = (float *)dalloc(c, 16)) &&
+              (c->shq = (uint8_t *)dalloc(c, std::max(tlmg_qact_bytes(DT_Q8_K, ds), tlmg_qact_bytes(DT_Q8_0, ds)) + 256));
+    if (ok) ok = ensure_pin(c, 4 * (size_t)(2 * D + E + 2 * 64) + 1024) == TLMG_OK;
+    if (ok) ok = fused_init(c->fused, *g) == TLMG_OK;
+    if (!ok) {
+        tlmg_close(c);
+        return set_error(TLMG_ENOMEM, "tlmg_open: device scratch allocation failed");
+    }
+    c->L.resize(g->n_layers);
+    for (Layer &Ly : c->L) {
+        Ly.h_slots.assign(E, Slot{ { nullptr, nullptr, nullptr }, { 0, 0, 0 }, 0 });
+        Ly.d_slots = (Slot *)dalloc(c, sizeof(Slot) * E);
+        if (!Ly.d_slots) {
+            tlmg_close(c);
+            return set_error(TLMG_ENOMEM, "tlmg_open: slot table allocation failed");
+        }
+        Ly.slots_dirty = true;
+    }
+    c->launch0 = launches_total();
+    *out = c;
+    return TLMG_OK;
+}
+
+void tlmg_close(tlmg_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->st) cudaStreamSynchronize(c->st);
+    if (c->own_st) cudaStreamSynchronize(c->own_st);
+    fused_release(c->fused);
+    c->arena.release();
+    for (void *p : c->owned) cudaFree(p);
+    if (c->pin) cudaFreeHost(c->pin);
+    if (c->own_st) cudaStreamDestroy(c->own_st);
+    for (auto &m : c->marks) {
+        cudaEventDestroy(m.a);
+        if (m.b) cudaEventDestroy(m.b);
+    }
+    for (cudaEvent_t e : c->ev_pool) cudaEventDestroy(e);
+    delete c;
+}
+
+int tlmg_profile(tlmg_ctx *c, int on) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    cudaSetDevice(c->device);
+    if (on) {
+        cudaStreamSynchronize(c->st);
+        for (auto &m : c->marks) {
+            c->ev_pool.push_back(m.a);
+            if (m.b) c->ev_pool.push_back(m.b);
+        }
+        c->marks.clear();
+    }
+    c->prof = on != 0;
+    return TLMG_OK;
+}
+
+int tlmg_profile_read(tlmg_ctx *c, int cls, double *ms, int64_t *launches, int64_t *bytes_per_launch) {
+    if (!c || cls < 0 || cls > 2) return set_error(TLMG_EINVAL, "profile_read: bad arguments");
+    cudaSetDevice(c->device);
+    cudaError_t e = cudaStreamSynchronize(c->st);
+    if (e != cudaSuccess) return cuda_fail(e, "profile_read synchronize");
+    double tot = 0.0;
+    int64_t n = 0;
+    for (auto &m : c->marks) {
+        if (m.cls != cls || !m.b) continue;
+        float t = 0.0f;
+        if (cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess) {
+            tot += t;
+            n++;
+        }
+    }
+    if (ms) *ms = tot;
+    if (launches) *launches = n;
+    if (bytes_per_launch) *bytes_per_launch = c->prof_bytes[cls];
+    return TLMG_OK;
+}
+
+int tlmg_set_stream(tlmg_ctx *c, void *stream) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    cudaSetDevice(c->device);
+    cudaStream_t next = stream ? (cudaStream_t)stream : c->own_st;
+    if (next != c->st) {
+        // order: work already queued on the old stream happens before new work
+        cudaEvent_t ev;
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return set_error(TLMG_EIO, "event");
+        cudaEventRecord(ev, c->st);
+        cudaStreamWaitEvent(next, ev, 0);
+        cudaEventDestroy(ev);
+        c->st = next;
+    }
+    return TLMG_OK;
+}
+
+int64_t tlmg_launch_count(const tlmg_ctx *c) { return c ? launches_total() - c->launch0 : 0; }
+
+int tlmg_set_expert(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], const void *payload,
+                    size_t payload_len, const uint64_t item_off[3]) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    if (expert < 0 || expert >= c->g.n_experts)
+        return set_error(TLMG_ERANGE, "expert %d out of range [0, %d)", expert, c->g.n_experts);
+    if (!dt || !payload || !item_off) return set_error(TLMG_EINVAL, "set_expert: NULL argument");
+    const int D = c->g.d_model, de = c->g.d_expert;
+    size_t bytes[3];
+    for (int m = 0; m < 3; m++) {
+        int q = dt_block(dt[m]);
+        if (q <= 1 || (m < 2 ? D : de) % q)
+            return set_error(TLMG_EUNSUP, "set_expert %d:%d: matrix %d dtype %d is not a block-quantised type", layer,
+                             expert, m, dt[m]);
+        bytes[m] = m < 2 ? (size_t)de * tlmg_row_bytes(dt[m], D) : (size_t)D * tlmg_row_bytes(dt[m], de);
+        if (item_off[m] > payload_len || bytes[m] > payload_len - item_off[m])
+            return set_error(TLMG_EFORMAT, "set_expert %d:%d: matrix %d [%llu, +%zu) exceeds payload %zu", layer,
+                             expert, m, (unsigned long long)item_off[m], bytes[m], payload_len);
+    }
+    Layer &Ly = c->L[layer];
+    Slot &s = Ly.h_slots[expert];
+    size_t pad[3];
+    for (int m = 0; m < 3; m++) pad[m] = (bytes[m] + 16 + 255) & ~size_t(255);
+    uint8_t *base = nullptr;
+    bool reuse = s.ok && s.dt[0] == dt[0] && s.dt[1] == dt[1] && s.dt[2] == dt[2];
+    if (reuse) {
+        base = (uint8_t *)s.m[0];
+    } else {
+        base = (uint8_t *)c->arena.get(pad[0] + pad[1] + pad[2]);
+        if (!base) return set_error(TLMG_ENOMEM, "set_expert %d:%d: HBM slot allocation failed", layer, expert);
+    }
+    const uint8_t *src = (const uint8_t *)payload;
+    size_t off = 0;
+    for (int m = 0; m < 3; m++) {
+        cudaError_t e = cudaMemcpy(base + off, src + item_off[m], bytes[m], cudaMemcpyDefault);
+        if (e != cudaSuccess) return cuda_fail(e, "expert upload");
+        s.m[m] = base + off;
+        s.dt[m] = dt[m];
+        off += pad[m];
+    }
+    s.ok = 1;
+    Ly.slots_dirty = true;
+    return TLMG_OK;
+}
+
+int tlmg_set_layer(tlmg_ctx *c, int layer, const float *ffn_norm, int router_dt, const void *router_w,
+                   size_t router_rb, const float *router_bias, const uint8_t *mask) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    Layer &Ly = c->L[layer];
+    const int D = c->g.d_model, E = c->g.n_experts;
+    auto up = [&](void **dst, const void *src, size_t bytes) -> bool {
+        if (!src) return true;
+        if (!*dst && !(*dst = dalloc(c, bytes + 16))) return false;
+        return cudaMemcpy(*dst, src, bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+    };
+    if (ffn_norm && !up((void **)&Ly.ffn_norm, ffn_norm, 4 * (size_t)D)) return set_error(TLMG_EIO, "set_layer: norm upload");
+    if (router_w) {
+        int q = dt_block(router_dt);
+        if (!q || D % q || router_rb < tlmg_row_bytes(router_dt, D))
+            return set_error(TLMG_EINVAL, "set_layer: bad router dtype %d / row bytes %zu", router_dt, router_rb);
+        if (Ly.router_w && (Ly.router_dt != router_dt || Ly.router_rb != router_rb)) Ly.router_w = nullptr;
+        if (!up(&Ly.router_w, router_w, router_rb * (size_t)E)) return set_error(TLMG_EIO, "set_layer: router upload");
+        Ly.router_dt = router_dt;
+        Ly.router_rb = router_rb;
+    }
+    if (router_bias && !up((void **)&Ly.router_bias, router_bias, 4 * (size_t)E))
+        return set_error(TLMG_EIO, "set_layer: bias upload");
+    if (mask && !up((void **)&Ly.mask, mask, (size_t)E)) return set_error(TLMG_EIO, "set_layer: mask upload");
+    return TLMG_OK;
+}
+
+int tlmg_set_shared(tlmg_ctx *c, int layer, const int32_t dt[3], const void *gate, const void *up_w,
+                    const void *down, const float *gate_inp) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    cudaSetDevice(c->device);
+    const int D = c->g.d_model, ds = c->g.d_shared;
+    if (ds <= 0) return set_error(TLMG_EINVAL, "set_shared: geometry has d_shared = 0");
+    Layer &Ly = c->L[layer];
+    const void *src[3] = { gate, up_w, down };
+    for (int m = 0; m < 3; m++) {
+        int q = dt_block(dt[m]);
+        if (!q || (m < 2 ? D : ds) % q) return set_error(TLMG_EUNSUP, "set_shared: bad dtype %d", dt[m]);
+        size_t bytes = m < 2 ? (size_t)ds * tlmg_row_bytes(dt[m], D) : (size_t)D * tlmg_row_bytes(dt[m], ds);
+        void *p = dalloc(c, bytes + 256);
+        if (!p || cudaMemcpy(p, src[m], bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(TLMG_EIO, "set_shared: upload failed");
+        Ly.sh_w[m] = p;
+        Ly.sh_dt[m] = dt[m];
+    }
+    if (gate_inp) {
+        void *p = dalloc(c, 4 * (size_t)D);
+        if (!p || cudaMemcpy(p, gate_inp, 4 * (size_t)D, cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(TLMG_EIO, "set_shared: gate upload failed");
+        Ly.sh_gate_inp = (float *)p;
+    } else {
+        Ly.sh_gate_inp = nullptr;
+    }
+    Ly.has_shared = true;
+    return TLMG_OK;
+}
+
+int tlmg_expert_ffn(tlmg_ctx *c, int layer, const float *x, const float *logits, float *ffn, int32_t *ids,
+                    float *w) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!x || !logits || !ffn) return set_error(TLMG_EINVAL, "expert_ffn: NULL argument");
+    if (c->g.n_experts <= 0) return set_error(TLMG_EINVAL, "expert_ffn: geometry has no routed experts");
+    cudaSetDevice(c->device);
+    const int D = c->g.d_model, E = c->g.n_experts, k = c->g.top_k;
+    PtrKind kx = ptr_kind(x);
+    if (kx == PK_DEVICE) {
+        if ((rc = expert_ffn_dev(c, layer, x, logits, ffn))) return rc;
+        if (ids && cudaMemcpyAsync(ids, c->ids, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st) != cudaSuccess)
+            return set_error(TLMG_EIO, "ids copy");
+        if (w && cudaMemcpyAsync(w, c->w, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st) != cudaSuccess)
+            return set_error(TLMG_EIO, "w copy");
+        return TLMG_OK;
+    }
+    // host buffers: copies in and out are part of the call
+    PtrKind kl = ptr_kind(logits), kf = ptr_kind(ffn);
+    size_t o_x = 0, o_l = 4 * (size_t)D, o_f = o_l + 4 * (size_t)E, o_i = o_f + 4 * (size_t)D, o_w = o_i + 256;
+    if ((rc = h2d(c, c->x, x, 4 * (size_t)D, kx, o_x))) return rc;
+    if ((rc = h2d(c, c->logits, logits, 4 * (size_t)E, kl, o_l))) return rc;
+    if ((rc = expert_ffn_dev(c, layer, c->x, c->logits, c->ffn))) return rc;
+    if ((rc = d2h(c, ffn, c->ffn, 4 * (size_t)D, kf, o_f))) return rc;
+    if (ids && (rc = d2h(c, c->pin + o_i, c->ids, 4 * (size_t)k, PK_PINNED, 0))) return rc;
+    if (w && (rc = d2h(c, c->pin + o_w, c->w, 4 * (size_t)k, PK_PINNED, 0))) return rc;
+    if ((rc = stream_sync(c))) return rc;
+    finish_d2h(c, ffn, 4 * (size_t)D, kf, o_f);
+    if (ids) memcpy(ids, c->pin + o_i, 4 * (size_t)k);
+    if (w) memcpy(w, c->pin + o_w, 4 * (size_t)k);
+    return TLMG_OK;
+}
+
+int tlmg_expert_ffn_many(tlmg_ctx *c, int layer0, int n_tok, const float *x, const float *logits, float *ffn) {
+    int rc = check_layer(c, layer0);
+    if (rc) return rc;
+    if (n_tok <= 0) return TLMG_OK;
+    if (!x || !logits || !ffn) return set_error(TLMG_EINVAL, "expert_ffn_many: NULL argument");
+    cudaSetDevice(c->device);
+    const int D = c->g.d_model, E = c->g.n_experts, NL = c->g.n_layers;
+    PtrKind kx = ptr_kind(x);
+    const float *dx = x, *dl = logits;
+    float *df = ffn;
+    PtrKind kl = PK_DEVICE, kf = PK_DEVICE;
+    if (kx != PK_DEVICE) {
+        if (n_tok > c->m_cap) {
+            void *a = dalloc(c, 4 * (size_t)n_tok * D), *b = dalloc(c, 4 * (size_t)n_tok * E),
+                 *f = dalloc(c, 4 * (size_t)n_tok * D);
+            if (!a || !b || !f) return set_error(TLMG_ENOMEM, "expert_ffn_many: scratch allocation");
+            c->mx = (float *)a;
+            c->mlog = (float *)b;
+            c->mffn = (float *)f;
+            c->m_cap = n_tok;
+        }
+        kl = ptr_kind(logits);
+        kf = ptr_kind(ffn);
+        size_t need = 4 * (size_t)n_tok * (2 * D + E) + 64;
+        if ((kx == PK_PAGEABLE || kl == PK_PAGEABLE || kf == PK_PAGEABLE) && (rc = ensure_pin(c, need))) return rc;
+        if ((rc = h2d(c, c->mx, x, 4 * (size_t)n_tok * D, kx, 0))) return rc;
+        if ((rc = h2d(c, c->mlog, logits, 4 * (size_t)n_tok * E, kl, 4 * (size_t)n_tok * D))) return rc;
+        dx = c->mx;
+        dl = c->mlog;
+        df = c->mffn;
+    }
+    for (int t = 0; t < n_tok; t++) {
+        int layer = (layer0 + t) % NL;
+        if ((rc = expert_ffn_dev(c, layer, dx + (size_t)t * D, dl + (size_t)t * E, df + (size_t)t * D))) return rc;
+    }
+    if (kx != PK_DEVICE) {
+        size_t off = 4 * (size_t)n_tok * (D + E);
+        if ((rc = d2h(c, ffn, c->mffn, 4 * (size_t)n_tok * D, kf, off))) return rc;
+        if ((rc = stream_sync(c))) return rc;
+        finish_d2h(c, ffn, 4 * (size_t)n_tok * D, kf, off);
+    }
+    return TLMG_OK;
+}
+
+int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!h) return set_error(TLMG_EINVAL, "moe_layer: NULL h");
+    cudaSetDevice(c->device);
+    Layer &Ly = c->L[layer];
+    const tlmg_geom &g = c->g;
+    const int D = g.d_model, E = g.n_experts, k = g.top_k;
+    if (!Ly.ffn_norm) return set_error(TLMG_ENOTFOUND, "moe_layer: layer %d has no ffn_norm", layer);
+    if (E > 0 && !Ly.router_w) return set_error(TLMG_ENOTFOUND, "moe_layer: layer %d has no router", layer);
+    PtrKind kh = ptr_kind(h);
+    float *dh = h;
+    if (kh != PK_DEVICE) {
+        if ((rc = h2d(c, c->h, h, 4 * (size_t)D, kh, 0))) return rc;
+        dh = c->h;
+    }
+    // xb = rmsnorm(h); activations of xb
+    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, Ly.ffn_norm, D, g.norm_eps, c->x);
+    if ((rc = launched("rmsnorm"))) return rc;
+    if ((rc = quant_inputs(c, c->x))) return rc;
+    const float *s_out = nullptr, *sgate = nullptr;
+    if (Ly.has_shared && g.d_shared > 0) {
+        const int ds = g.d_shared;
+        for (int m = 0; m < 2; m++) {
+            int dt = Ly.sh_dt[m];
+            const void *act = act_kind_for(dt) == DT_Q8_0 ? (const void *)c->xq80 : (const void *)c->xq8k;
+            if ((rc = launch_matvec(dt, Ly.sh_w[m], tlmg_row_bytes(dt, D), act, c->sg + (size_t)m * ds, D, 0, ds, c->st)))
+                return rc;
+        }
+        k_swiglu<<<(ds + 255) / 256, 256, 0, c->st>>>(c->sg, ds, c->sh);
+        if ((rc = launched("shared swiglu"))) return rc;
+        int kd = act_kind_for(Ly.sh_dt[2]);
+        if ((rc = launch_quant_act(kd, c->sh, ds, c->shq, c->st))) return rc;
+        if ((rc = launch_matvec(Ly.sh_dt[2], Ly.sh_w[2], tlmg_row_bytes(Ly.sh_dt[2], ds), c->shq, c->s_out, ds, 0, D,
+                                c->st)))
+            return rc;
+        float one = 1.0f;
+        if (Ly.sh_gate_inp) {
+            k_shared_gate<<<1, 32, 0, c->st>>>(Ly.sh_gate_inp, c->x, D, c->sgate);
+            if ((rc = launched("shared gate"))) return rc;
+        } else if (cudaMemcpyAsync(c->sgate, &one, 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) {
+            return set_error(TLMG_EIO, "shared gate copy");
+        }
+        s_out = c->s_out;
+        sgate = c->sgate;
+        if ((rc = stream_sync(c))) return rc;   // `one` lives on this stack frame
+    }
+    if (E > 0) {
+        if ((rc = sync_slots(c, Ly))) return rc;
+        if (!layer_ready(c, Ly)) return set_error(TLMG_ENOTFOUND, "layer %d: not every expert slot is loaded", layer);
+        int kr = act_kind_for(Ly.router_dt);
+        const void *ract = kr == DT_F32 ? (const void *)c->x : kr == DT_Q8_0 ? (const void *)c->xq80 : (const void *)c->xq8k;
+        if ((rc = launch_matvec(Ly.router_dt, Ly.router_w, Ly.router_rb, ract, c->logits, D, 0, E, c->st))) return rc;
+        if ((rc = run_experts(c, Ly, c->logits, c->ffn, dh, s_out, sgate, c->x))) return rc;
+    } else if (s_out) {
+        // no routed experts: ffn = sgate * s_out, h += ffn
+        k_ffn_down<<<(unsigned)((D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, c->st>>>(
+            Ly.d_slots, c->ids, c->w, 0, D, g.d_expert, c->hq, c->hq_stride, s_out, sgate, c->ffn, dh);
+        if ((rc = launched("shared combine"))) return rc;
+    }
+    if (kh != PK_DEVICE) {
+        if ((rc = d2h(c, h, dh, 4 * (size_t)D, kh, 0))) return rc;
+    }
+    const size_t o_ids = 4 * (size_t)D + 256, o_w = o_ids + 256;   // inside the staging area (>= 4D + 1024)
+    if (ids && E > 0) {
+        if (is_device_ptr(ids)) cudaMemcpyAsync(ids, c->ids, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st);
+        else cudaMemcpyAsync(c->pin + o_ids, c->ids, 4 * (size_t)k, cudaMemcpyDeviceToHost, c->st);
+    }
+    if (w && E > 0) {
+        if (is_device_ptr(w)) cudaMemcpyAsync(w, c->w, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st);
+        else cudaMemcpyAsync(c->pin + o_w, c->w, 4 * (size_t)k, cudaMemcpyDeviceToHost, c->st);
+    }
+    if (kh != PK_DEVICE || (ids && !is_device_ptr(ids)) || (w && !is_device_ptr(w))) {
+        if ((rc = stream_sync(c))) return rc;
+        if (kh != PK_DEVICE) finish_d2h(c, h, 4 * (size_t)D, kh, 0);
+        if (ids && E > 0 && !is_device_ptr(ids)) memcpy(ids, c->pin + o_ids, 4 * (size_t)k);
+        if (w && E > 0 && !is_device_ptr(w)) memcpy(w, c->pin + o_w, 4 * (size_t)k);
+    }
+    return TLMG_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,111 @@
+"""Layer-level interface: HBM-resident expert slots and the MoE block.
+
+MoeContext wraps a tlmg_ctx (include/tlmg.h). It mirrors the MoE half of
+the reference's tlm_model (src/lib/tlm_model.h): experts are uploaded once
+from packet payload bytes (set_expert), and expert_ffn / moe_layer replace
+run_batch() + combine and moe() (src/lib/tlm_model.c:900-1055).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+
+from ._lib import Geom, check, load
+
+
+def _ptr(a) -> int | None:
+    if a is None:
+        return None
+    if isinstance(a, torch.Tensor):
+        if not a.is_contiguous():
+            raise ValueError("tensor must be contiguous")
+        return a.data_ptr()
+    if isinstance(a, np.ndarray):
+        if not a.flags["C_CONTIGUOUS"]:
+            raise ValueError("array must be C-contiguous")
+        return a.ctypes.data
+    raise TypeError(f"unsupported buffer type {type(a)!r}")
+
+
+class MoeContext:
+    def __init__(self, n_layers: int, d_model: int, d_expert: int, n_experts: int, top_k: int,
+                 router: int = 0, routed_scale: float = 1.0, norm_eps: float = 1e-6, d_shared: int = 0,
+                 device: int = 0):
+        self.geom = Geom(n_layers, d_model, d_expert, d_shared, n_experts, top_k, router, routed_scale, norm_eps)
+        self._lib = load()
+        h = C.c_void_p()
+        check(self._lib.tlmg_open(C.byref(self.geom), device, C.byref(h)))
+        self._h = h
+        self.device = device
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and self._h.value:
+            self._lib.tlmg_close(self._h)
+            self._h = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream=None) -> None:
+        """Queue work on a torch.cuda.Stream (None: the context's own stream)."""
+        ptr = None if stream is None else stream.cuda_stream
+        check(self._lib.tlmg_set_stream(self._h, ptr))
+
+    KERNEL_CLASSES = ("expert_ffn_gateup_or_fused", "expert_ffn_down", "route")
+
+    def kernel_times(self, fn) -> tuple[str, float, int, int]:
+        """Run fn() with per-launch event timing; return the dominant kernel
+        class as (name, total ms, launches, algorithmic bytes per launch)."""
+        check(self._lib.tlmg_profile(self._h, 1))
+        try:
+            fn()
+            best = None
+            for cls, name in enumerate(self.KERNEL_CLASSES):
+                ms, n, b = C.c_double(), C.c_int64(), C.c_int64()
+                check(self._lib.tlmg_profile_read(self._h, cls, C.byref(ms), C.byref(n), C.byref(b)))
+                if best is None or ms.value > best[1]:
+                    best = (name, ms.value, n.value, b.value)
+            return best
+        finally:
+            check(self._lib.tlmg_profile(self._h, 0))
+
+    @property
+    def launches(self) -> int:
+        return int(self._lib.tlmg_launch_count(self._h))
+
+    def set_expert(self, layer: int, expert: int, dts, payload: np.ndarray, item_off) -> None:
+        dt = (C.c_int32 * 3)(*dts)
+        off = (C.c_uint64 * 3)(*item_off)
+        payload = np.ascontiguousarray(payload, dtype=np.uint8)
+        check(self._lib.tlmg_set_expert(self._h, layer, expert, dt, payload.ctypes.data, payload.nbytes, off))
+
+    def set_layer(self, layer: int, ffn_norm=None, router_dt: int = 0, router_w=None, router_row_bytes: int = 0,
+                  router_bias=None, mask=None) -> None:
+        check(self._lib.tlmg_set_layer(self._h, layer, _ptr(ffn_norm), router_dt, _ptr(router_w), router_row_bytes,
+                                       _ptr(router_bias), _ptr(mask)))
+
+    def set_shared(self, layer: int, dts, gate, up, down, gate_inp=None) -> None:
+        dt = (C.c_int32 * 3)(*dts)
+        check(self._lib.tlmg_set_shared(self._h, layer, dt, _ptr(gate), _ptr(up), _ptr(down), _ptr(gate_inp)))
+
+    def expert_ffn(self, layer: int, x, logits, ffn, ids=None, w=None) -> None:
+        """Routed-expert FFN of one token; host (numpy / pinned) or CUDA buffers."""
+        check(self._lib.tlmg_expert_ffn(self._h, layer, _ptr(x), _ptr(logits), _ptr(ffn), _ptr(ids), _ptr(w)))
+
+    def expert_ffn_many(self, layer0: int, x, logits, ffn) -> None:
+        n_tok = (x.shape[0] if hasattr(x, "shape") and len(x.shape) == 2 else 1)
+        check(self._lib.tlmg_expert_ffn_many(self._h, layer0, n_tok, _ptr(x), _ptr(logits), _ptr(ffn)))
+
+    def moe_layer(self, layer: int, h, ids=None, w=None) -> None:
+        check(self._lib.tlmg_moe_layer(self._h, layer, _ptr(h), _ptr(ids), _ptr(w)))
