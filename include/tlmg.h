@@ -2,8 +2,9 @@
  * MoE decoder step.
  *
  * Plain C: pointers, sizes and integer codes only; no CUDA or torch types
- * in the signatures (a CUDA stream travels as `void *`, NULL = the
- * library's own stream). All fallible functions return 0 (TLMG_OK) or a
+ * in the signatures (a CUDA stream travels as `void *`; NULL = the
+ * library's own non-blocking stream, so pass cudaStreamLegacy (0x1) to
+ * order work with the legacy default stream). All fallible functions return 0 (TLMG_OK) or a
  * negative code with the same numbering as the reference's TLM_E* codes
  * (src/lib/tlm_platform.h:26-36), and leave a thread-local message for
  * tlmg_errmsg(). Numerics follow the reference contract

@@ -434,4 +434,155 @@ __device__ __forceinline__ float tree32(float v) {
     return v;
 }
 
+// ---------------------------------------------------------------------------
+// router top-k (reference tlm_model.c:776-839), one warp. Entry e lives in
+// lane e % 32, slot e / 32.
+constexpr int RT_PER = 16;   // E <= 512
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+    // larger value wins; equal values -> lower index; bi < 0 = nothing yet
+    return bi < 0 || v > bv || (v == bv && i < bi);
+}
+
+// Top-k of v[] over entries not masked, not NaN, not used; fallback = lowest
+// unmasked unused index, else 0 (reference topk, tlm_model.c:776-795).
+__device__ __forceinline__ void warp_topk(const float (&v)[RT_PER], const bool (&off)[RT_PER], int E, int k, int lane,
+                          int32_t *ids_sm) {
+    bool used[RT_PER];
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) used[s] = false;
+    for (int r = 0; r < k; r++) {
+        float bv = 0.0f;
+        int bi = -1;
+        int fb = -1;   // lowest unmasked unused index of this lane
+#pragma unroll
+        for (int s = 0; s < RT_PER; s++) {
+            int e = lane + 32 * s;
+            if (e >= E || off[s] || used[s]) continue;
+            if (fb < 0) fb = e;
+            if (v[s] != v[s]) continue;
+            if (better(v[s], e, bv, bi)) { bv = v[s]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+            int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+            int of = __shfl_xor_sync(0xFFFFFFFFu, fb, o);
+            if (oi >= 0 && better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+            if (of >= 0 && (fb < 0 || of < fb)) fb = of;
+        }
+        int pick = bi >= 0 ? bi : (fb >= 0 ? fb : 0);
+        if ((pick & 31) == lane && pick < E) used[pick >> 5] = true;
+        if (lane == 0) ids_sm[r] = pick;
+    }
+}
+
+// Router of one token by one full warp (lane = 0..31). p_sm: scratch of
+// RT_PER*32 floats; ids_sm / w_sm: outputs (k entries), valid after the
+// call in all lanes of the warp (the call ends with __syncwarp).
+static __device__ __noinline__ void warp_route(int router, const float *__restrict__ logits, const uint8_t *__restrict__ mask,
+                           const float *__restrict__ bias, int E, int k, float routed_scale, float *p_sm,
+                           int32_t *ids_sm, float *w_sm, int lane) {
+    float p[RT_PER], v[RT_PER];
+    bool off[RT_PER];
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        off[s] = e < E ? (mask && mask[e]) : true;
+        p[s] = 0.0f;
+        v[s] = 0.0f;
+    }
+    if (router == 2) {
+#pragma unroll
+        for (int s = 0; s < RT_PER; s++) {
+            int e = lane + 32 * s;
+            if (e >= E) continue;
+            p[s] = sigmoid_f(logits[e]);
+            v[s] = __fadd_rn(p[s], bias ? bias[e] : 0.0f);
+            p_sm[e] = p[s];
+        }
+        warp_topk(v, off, E, k, lane, ids_sm);
+        __syncwarp();
+        if (lane == 0) {
+            double s = 0.0;
+            for (int r = 0; r < k; r++) s = __dadd_rn(s, (double)p_sm[ids_sm[r]]);
+            float inv = __double2float_rn(__ddiv_rn(1.0, __dadd_rn(s, 1e-20)));
+            for (int r = 0; r < k; r++) w_sm[r] = __fmul_rn(__fmul_rn(p_sm[ids_sm[r]], inv), routed_scale);
+        }
+        __syncwarp();
+        return;
+    }
+    // softmax over routable entries
+    float mx = -__uint_as_float(0x7F800000u);
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        if (e < E && !off[s]) {
+            float l = logits[e];
+            if (l > mx) mx = l;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    const bool none = mx == -__uint_as_float(0x7F800000u);
+    double part = 0.0;
+    uint32_t min_bits = 0x7F800000u;   // smallest nonzero p seen
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        if (e >= E) continue;
+        float l = logits[e];
+        p[s] = (off[s] || !(l == l) || none) ? 0.0f : cr_expf(__fsub_rn(l, mx));
+        p_sm[e] = p[s];
+        part = __dadd_rn(part, (double)p[s]);
+        if (p[s] != 0.0f) min_bits = min(min_bits, __float_as_uint(p[s]));
+    }
+    // The reference sums in double, sequentially in index order. When every
+    // nonzero term is >= 2^(floor(log2 E) - 29) all partial sums are exact
+    // in double, so any order gives the same sum; otherwise lane 0 redoes it
+    // sequentially.
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        part = __dadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, o));
+        min_bits = min(min_bits, __shfl_xor_sync(0xFFFFFFFFu, min_bits, o));
+    }
+    int lg = 31 - __clz(E);
+    bool exact = min_bits == 0x7F800000u || __uint_as_float(min_bits) >= ldexpf(1.0f, lg - 29);
+    __syncwarp();
+    double sum = part;
+    if (!exact) {
+        if (lane == 0) {
+            double s = 0.0;
+            for (int e = 0; e < E; e++) s = __dadd_rn(s, (double)p_sm[e]);
+            part = s;
+        }
+        sum = __shfl_sync(0xFFFFFFFFu, part, 0);
+    }
+    float inv = sum > 0.0 ? __double2float_rn(__ddiv_rn(1.0, sum)) : 0.0f;
+#pragma unroll
+    for (int s = 0; s < RT_PER; s++) {
+        int e = lane + 32 * s;
+        if (e < E) {
+            p[s] = __fmul_rn(p[s], inv);
+            p_sm[e] = p[s];
+        }
+    }
+    warp_topk(p, off, E, k, lane, ids_sm);
+    __syncwarp();
+    if (lane == 0) {
+        for (int r = 0; r < k; r++) w_sm[r] = p_sm[ids_sm[r]];
+        if (router == 0) {
+            double t = 0.0;
+            for (int r = 0; r < k; r++) t = __dadd_rn(t, (double)w_sm[r]);
+            if (t > 0.0) {
+                float it = __double2float_rn(__ddiv_rn(1.0, t));
+                for (int r = 0; r < k; r++) w_sm[r] = __fmul_rn(w_sm[r], it);
+            }
+        }
+        if (routed_scale != 1.0f)
+            for (int r = 0; r < k; r++) w_sm[r] = __fmul_rn(w_sm[r], routed_scale);
+    }
+    __syncwarp();
+}
+
 }  // namespace tlmg

@@ -59,7 +59,8 @@ class MoeContext:
 
     def set_stream(self, stream=None) -> None:
         """Queue work on a torch.cuda.Stream (None: the context's own stream)."""
-        ptr = None if stream is None else stream.cuda_stream
+        from .quant import stream_handle
+        ptr = None if stream is None else stream_handle(stream)
         check(self._lib.tlmg_set_stream(self._h, ptr))
 
     KERNEL_CLASSES = ("expert_ffn_gateup_or_fused", "expert_ffn_down", "route")

@@ -17,8 +17,19 @@ from ._lib import (BF16, DTYPE_NAMES, F16, F32, MXFP4, Q4_K, Q5_K, Q6_K, Q8_0, Q
                    TlmError, check, load)
 
 
+CUDA_STREAM_LEGACY = 1   # cudaStreamLegacy: the legacy default stream handle
+
+
+def stream_handle(stream=None) -> int:
+    """cudaStream_t of a torch stream for the C ABI. torch's default stream
+    has handle 0, which the ABI reads as "the library's own stream", so it
+    is passed as cudaStreamLegacy instead."""
+    s = (stream or torch.cuda.current_stream()).cuda_stream
+    return s if s else CUDA_STREAM_LEGACY
+
+
 def _stream_ptr() -> int:
-    return torch.cuda.current_stream().cuda_stream
+    return stream_handle()
 
 
 def tier() -> str:
