@@ -162,6 +162,24 @@ int tlmg_moe_layer(tlmg_ctx *ctx, int layer, float *h, int32_t *ids, float *w);
  * MoE block with its other work and time it with events on that stream. */
 int tlmg_set_stream(tlmg_ctx *ctx, void *stream);
 
+/* Choose the expert-FFN kernels: on = 1 (default) the persistent
+ * single-launch kernel wherever it can serve the layer, on = 0 the
+ * multi-kernel path (router, gate/up, re-quantise, down launches). Both
+ * give identical bits. TLMG_EUNSUP when on = 1 and the device cannot run
+ * the persistent kernel (the multi-kernel path stays in use). */
+int tlmg_set_fused(tlmg_ctx *ctx, int on);
+/* Wait for the context's queued work and report a failure the kernels
+ * raised since the last check (a bounded wait that expired: TLMG_EIO). */
+int tlmg_check(tlmg_ctx *ctx);
+
+/* Phase trace of the persistent kernel (the reference's per-step stats,
+ * src/lib/tlm_model.h:263-266, at kernel granularity): with on = 1 every
+ * launch stamps %globaltimer at its phase boundaries per CTA (start, routed,
+ * planned, gate/up done, grid barrier passed, h quantised, end). Copies up
+ * to `cap` stamps of the last launch ([CTA][8] u64 ns) to `out` (host) and
+ * returns how many; on = 0 stops tracing. */
+int tlmg_trace(tlmg_ctx *ctx, int on, uint64_t *out, int cap);
+
 /* Per-launch timing of the expert-FFN kernels with CUDA events recorded on
  * the launch stream around each launch (off by default; on = 1 clears the
  * totals). Kernel classes: 0 = gate/up + SwiGLU (or the fused expert-FFN

@@ -150,9 +150,11 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a.astype(np.float64) - b) / max(np.linalg.norm(b.astype(np.float64)), 1e-30))
 
 
-def test_expert_ffn_golden(dev, orc):
+@pytest.mark.parametrize("fused", [True, False])
+def test_expert_ffn_golden(dev, orc, fused):
     """The routed-expert FFN (incl. the Qwen3-30B-A3B layer shape) against
-    the reference's output and, bit for bit, against the oracle."""
+    the reference's output and, bit for bit, against the oracle - through
+    the persistent kernel and through the multi-kernel path."""
     from tests.golden.make_golden import ffn_case
     for c in cases("expert_ffn.npz"):
         seed, D, de, E, k, router = (int(c[x]) for x in ("seed", "D", "de", "E", "k", "router"))
@@ -160,6 +162,7 @@ def test_expert_ffn_golden(dev, orc):
         experts, x, logits, digest = ffn_case(seed, D, de, E, k, dts)
         assert digest == str(c["digest"])
         ctx = build_ctx(experts, D, de, E, k, router)
+        ctx.set_fused(fused)
         ffn = np.zeros(D, np.float32)
         ids = np.zeros(k, np.int32)
         w = np.zeros(k, np.float32)
@@ -292,3 +295,38 @@ def test_qmv_host_adapter(dev, orc):
         assert same_bits(np.float32(d), ref[3])
     ptr = C.c_void_p
     assert ptr is not None
+
+
+@pytest.mark.parametrize("dts", [(12, 12, 14), (13, 13, 15), (8, 8, 8), (14, 14, 14), (12, 12, 12)])
+def test_fused_matches_multikernel(dev, orc, dts):
+    """The persistent kernel and the multi-kernel path give identical bits on
+    the config-2 layer shape (D 2048, de 768, k 8) over many consecutive
+    launches (the grid barrier is reused every launch), and both equal the
+    oracle."""
+    from tierlm_b200 import synth
+    rng = np.random.default_rng(sum(dts))
+    D, de, E, k = 2048, 768, 24, 8
+    experts = [synth.rand_expert(rng, D, de, dts) for _ in range(E)]
+    ctx = build_ctx(experts, D, de, E, k, 0)
+    T = 24
+    x = rng.standard_normal((T, D)).astype(np.float32)
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    lg[5] = 0.0                                   # all-tie routing row
+    outs = {}
+    for fused in (True, False):
+        ctx.set_fused(fused)
+        xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
+        od = torch.zeros((T, D), device=dev)
+        ctx.expert_ffn_many(0, xd, ld, od)
+        ctx.check()
+        outs[fused] = od.cpu().numpy()
+    assert same_bits(outs[True], outs[False]).all()
+    orc.set_expf_mode(1)
+    try:
+        geom = dict(d_model=D, d_expert=de, n_experts=E, top_k=k, router=0)
+        for t in (0, 5, T - 1):
+            ref, _, _ = orc.expert_ffn(geom, experts, x[t], lg[t])
+            assert same_bits(outs[True][t], ref).all(), t
+    finally:
+        orc.set_expf_mode(0)
+    ctx.close()

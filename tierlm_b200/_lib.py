@@ -64,6 +64,9 @@ _SIGS = {
     "tlmg_expert_ffn_many": (_I, [_P, _I, _I, _P, _P, _P]),
     "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
     "tlmg_set_stream": (_I, [_P, _P]),
+    "tlmg_set_fused": (_I, [_P, _I]),
+    "tlmg_check": (_I, [_P]),
+    "tlmg_trace": (_I, [_P, _I, _P, _I]),
     "tlmg_profile": (_I, [_P, _I]),
     "tlmg_profile_read": (_I, [_P, _I, C.POINTER(C.c_double), C.POINTER(_I64), C.POINTER(_I64)]),
     "tlmg_launch_count": (_I64, [_P]),

@@ -356,14 +356,20 @@ __device__ __forceinline__ void part_q80(const uint8_t *blk, const uint8_t *act,
     ms = 0;
 }
 
-__constant__ static const int8_t k_e2m1x2[16] = { 0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12 };
+// Doubled E2M1 value of a 4-bit code (reference k_e2m1_x2, tlm_quant.c:515):
+// magnitudes 0 1 2 3 4 6 8 12 for codes 0..7, bit 3 is the sign.
+__device__ __forceinline__ int e2m1x2(uint32_t c) {
+    int m = (int)(c & 7u);
+    int v = m < 4 ? m : (m < 6 ? 2 * m - 4 : 4 * m - 16);
+    return (c & 8u) ? -v : v;
+}
 
 template <class L>
 __device__ __forceinline__ void part_mxfp4(const uint8_t *blk, const uint8_t *act, int j, int &is, int &ms) {
     uint32_t b0 = L::u8(blk + 1 + 2 * j), b1 = L::u8(blk + 2 + 2 * j);
     const int8_t *x = reinterpret_cast<const int8_t *>(act + 4);
-    is = (int)k_e2m1x2[b0 & 15] * x[2 * j] + (int)k_e2m1x2[b1 & 15] * x[2 * j + 1] +
-         (int)k_e2m1x2[b0 >> 4] * x[2 * j + 16] + (int)k_e2m1x2[b1 >> 4] * x[2 * j + 17];
+    is = e2m1x2(b0 & 15u) * x[2 * j] + e2m1x2(b1 & 15u) * x[2 * j + 1] + e2m1x2(b0 >> 4) * x[2 * j + 16] +
+         e2m1x2(b1 >> 4) * x[2 * j + 17];
     ms = 0;
 }
 
@@ -448,9 +454,7 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 // unmasked unused index, else 0 (reference topk, tlm_model.c:776-795).
 __device__ __forceinline__ void warp_topk(const float (&v)[RT_PER], const bool (&off)[RT_PER], int E, int k, int lane,
                           int32_t *ids_sm) {
-    bool used[RT_PER];
-#pragma unroll
-    for (int s = 0; s < RT_PER; s++) used[s] = false;
+    uint32_t used = 0u;   // bit s: slot s of this lane is taken (registers, no local array)
     for (int r = 0; r < k; r++) {
         float bv = 0.0f;
         int bi = -1;
@@ -458,7 +462,7 @@ __device__ __forceinline__ void warp_topk(const float (&v)[RT_PER], const bool (
 #pragma unroll
         for (int s = 0; s < RT_PER; s++) {
             int e = lane + 32 * s;
-            if (e >= E || off[s] || used[s]) continue;
+            if (e >= E || off[s] || ((used >> s) & 1u)) continue;
             if (fb < 0) fb = e;
             if (v[s] != v[s]) continue;
             if (better(v[s], e, bv, bi)) { bv = v[s]; bi = e; }
@@ -472,7 +476,7 @@ __device__ __forceinline__ void warp_topk(const float (&v)[RT_PER], const bool (
             if (of >= 0 && (fb < 0 || of < fb)) fb = of;
         }
         int pick = bi >= 0 ? bi : (fb >= 0 ? fb : 0);
-        if ((pick & 31) == lane && pick < E) used[pick >> 5] = true;
+        if ((pick & 31) == lane && pick < E) used |= 1u << (pick >> 5);
         if (lane == 0) ids_sm[r] = pick;
     }
 }
@@ -480,7 +484,7 @@ __device__ __forceinline__ void warp_topk(const float (&v)[RT_PER], const bool (
 // Router of one token by one full warp (lane = 0..31). p_sm: scratch of
 // RT_PER*32 floats; ids_sm / w_sm: outputs (k entries), valid after the
 // call in all lanes of the warp (the call ends with __syncwarp).
-static __device__ __noinline__ void warp_route(int router, const float *__restrict__ logits, const uint8_t *__restrict__ mask,
+static __device__ __forceinline__ void warp_route(int router, const float *__restrict__ logits, const uint8_t *__restrict__ mask,
                            const float *__restrict__ bias, int E, int k, float routed_scale, float *p_sm,
                            int32_t *ids_sm, float *w_sm, int lane) {
     float p[RT_PER], v[RT_PER];

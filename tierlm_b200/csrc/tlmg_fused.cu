@@ -42,8 +42,8 @@ constexpr int MAXCH = 128;              // chunks per CTA
 constexpr int MAXPIECE = 16;            // pieces per chunk (phase B: one per rank)
 constexpr int MAXK = 16;
 constexpr int SLOT_BYTES = 24576;
-constexpr uint32_t WAIT_LIMIT = 1u << 22;   // try_wait rounds (each may suspend ~us)
-constexpr uint32_t SPIN_LIMIT = 1u << 24;   // grid-barrier polls
+constexpr uint64_t WAIT_NS = 200000000ull;       // 0.2 s: an mbarrier wait gives up
+constexpr uint64_t BARRIER_NS = 500000000ull;    // 0.5 s: the grid barrier gives up
 
 struct ChunkDesc {
     uint8_t phase, rank, npiece, pad;
@@ -78,11 +78,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait for the phase with `parity` to complete.
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Wait for the phase with `parity` to complete, for at most WAIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (;;) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (now_ns() - t0 > WAIT_NS) return false;
+    }
+}
+// Record error bits for the host (mapped pinned word) and make them sticky
+// for later launches (device word bar[2]) until the host resets them.
+__device__ __forceinline__ void raise_error(uint32_t *err, uint32_t *bar, uint32_t bits) {
+    volatile uint32_t *e = err;
+    *e = *e | bits;
+    atomicOr(&bar[2], bits);
 }
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
     asm volatile(
@@ -209,7 +225,10 @@ __device__ int plan_phase_a(const FusedArgs &a, const Slot *sl, ChunkDesc *desc,
         const Slot &s = sl[r];
         int rbg = rb_of(s.dt[0], a.D), rbu = rb_of(s.dt[1], a.D);
         int cap = (SLOT_BYTES - 96) / (rbg + rbu);
-        int nr = (int)min<int64_t>(min<int64_t>(cap, p1 - p), a.de - j);
+        int64_t nr64 = p1 - p;
+        if (nr64 > cap) nr64 = cap;
+        if (nr64 > a.de - j) nr64 = a.de - j;
+        int nr = (int)nr64;
         uint32_t off = 0, tx = 0;
         for (int m = 0; m < 2; m++) {
             uintptr_t src = (uintptr_t)(s.m[m] + (size_t)j * (m ? rbu : rbg));
@@ -221,6 +240,7 @@ __device__ int plan_phase_a(const FusedArgs &a, const Slot *sl, ChunkDesc *desc,
         desc[n] = ChunkDesc{ 0, (uint8_t)r, 2, 0, (uint16_t)nr, 0, (uint32_t)j, tx };
         n++;
         p += nr;
+        if (p < p1 && n == MAXCH) return -1;   // plan does not fit: refuse rather than drop rows
     }
     return n - first;
 }
@@ -229,7 +249,7 @@ __device__ int plan_phase_b(const FusedArgs &a, const Slot *sl, ChunkDesc *desc,
     const int i0 = (int)((int64_t)a.D * blockIdx.x / gridDim.x), i1 = (int)((int64_t)a.D * (blockIdx.x + 1) / gridDim.x);
     int sum = 0;
     for (int r = 0; r < a.k; r++) sum += rb_of(sl[r].dt[2], a.de);
-    int cap = (SLOT_BYTES - 32 * a.k) / sum;
+    int cap = (SLOT_BYTES - 48 * a.k) / sum;   // each piece may add 45 bytes of alignment
     int n = first;
     for (int i = i0; i < i1 && n < MAXCH;) {
         int nr = min(cap, i1 - i);
@@ -245,6 +265,7 @@ __device__ int plan_phase_b(const FusedArgs &a, const Slot *sl, ChunkDesc *desc,
         desc[n] = ChunkDesc{ 1, 0, (uint8_t)a.k, 0, (uint16_t)nr, 0, (uint32_t)i, tx };
         n++;
         i += nr;
+        if (i < i1 && n == MAXCH) return -1;
     }
     return n - first;
 }
@@ -284,6 +305,8 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t hs = hq_stride(a.de);
+    uint64_t *tr = a.trace ? a.trace + (size_t)blockIdx.x * FUSED_TRACE_POINTS : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = now_ns();
 
     // ---- prologue
     if (threadIdx.x == 0) {
@@ -293,10 +316,12 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         misc[2] = 0;
+        misc[3] = ld_acquire(&bar[2]) != 0;   // an earlier launch failed: do nothing until reset
     }
     if (warp == 0) {
         warp_route(a.router, a.logits, a.mask, a.bias, a.E, a.k, a.routed_scale, p_sm, ids, wr, lane);
         if (lane < a.k) sl[lane] = a.slots[ids[lane]];
+        if (tr && lane == 0) tr[1] = now_ns();
     } else if (warp <= NCW) {
         // x -> Q8_K and/or Q8_0 blocks, one warp per block
         const int nb8k = (a.x_kinds & 1u) ? a.D / 256 : 0, nb80 = (a.x_kinds & 2u) ? a.D / 32 : 0;
@@ -306,15 +331,26 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
         }
     }
     __syncthreads();
+    if (misc[3]) {
+        if (threadIdx.x == 0) raise_error(err, bar, FUSED_ERR_BARRIER);
+        return;
+    }
     if (threadIdx.x == 32) misc[0] = plan_phase_a(a, sl, desc, poff, 0);
     __syncthreads();
-    if (threadIdx.x == 32) misc[1] = plan_phase_b(a, sl, desc, poff, misc[0]);
+    if (threadIdx.x == 32) misc[1] = misc[0] < 0 ? 0 : plan_phase_b(a, sl, desc, poff, misc[0]);
     if (blockIdx.x == 0 && threadIdx.x < a.k) {
         a.ids_out[threadIdx.x] = ids[threadIdx.x];
         a.w_out[threadIdx.x] = wr[threadIdx.x];
     }
     __syncthreads();
+    if (misc[0] < 0 || misc[1] < 0) {
+        // the plan did not fit in MAXCH chunks: nothing was issued; every CTA
+        // takes this path before the grid barrier, so none waits there
+        if (threadIdx.x == 0) raise_error(err, bar, FUSED_ERR_PLAN);
+        return;
+    }
     const int nA = misc[0], nCh = misc[0] + misc[1];
+    if (tr && threadIdx.x == 0) tr[2] = now_ns();
 
     if (warp == NCW) {
         // ---- producer
@@ -322,7 +358,7 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
             for (int c = 0; c < nCh; c++) {
                 int s = c % nslot, u = c / nslot;
                 if (u > 0 && !mbar_wait(&empty[s], (uint32_t)(u - 1) & 1u)) {
-                    atomicOr(err, FUSED_ERR_COPY);
+                    raise_error(err, bar, FUSED_ERR_COPY);
                     break;
                 }
                 issue_chunk(a, sl, desc[c], stage + (size_t)s * SLOT_BYTES, &full[s]);
@@ -333,12 +369,13 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
 
     // ---- phase A: gate/up + SwiGLU
     BlockPart *part = parts + warp * FCHUNK;
-    bool abort = false;
+    bool abort = false;      // skip the arithmetic (results of this launch are invalid)
+    bool dead = false;       // a copy wait expired: stop waiting on copies
     for (int c = 0; c < nA; c++) {
         int s = c % nslot;
-        if (!mbar_wait(&full[s], (uint32_t)(c / nslot) & 1u)) {
-            abort = true;
-            if (lane == 0) atomicOr(err, FUSED_ERR_COPY);
+        if (!dead && !mbar_wait(&full[s], (uint32_t)(c / nslot) & 1u)) {
+            dead = abort = true;
+            if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
         }
         const ChunkDesc d = desc[c];
         const uint8_t *base = stage + (size_t)s * SLOT_BYTES;
@@ -361,6 +398,7 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
 
     // ---- grid barrier: every CTA's hbuf rows are written
     consumer_sync();
+    if (tr && threadIdx.x == 0) tr[3] = now_ns();
     if (threadIdx.x == 0) {
         uint32_t gen = ld_acquire(&bar[1]);
         __threadfence();
@@ -370,20 +408,21 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
             __threadfence();
             st_release(&bar[1], gen + 1u);
         } else {
-            uint32_t i = 0;
+            const uint64_t t0 = now_ns();
             while (ld_acquire(&bar[1]) == gen) {
-                if (++i > SPIN_LIMIT) {
-                    atomicOr(err, FUSED_ERR_BARRIER);
+                if (now_ns() - t0 > BARRIER_NS) {
+                    raise_error(err, bar, FUSED_ERR_BARRIER);
                     misc[2] = 1;
                     break;
                 }
-                __nanosleep(64);
+                __nanosleep(32);
             }
         }
         __threadfence();
     }
     consumer_sync();
     abort = abort || misc[2] != 0;
+    if (tr && threadIdx.x == 0) tr[4] = now_ns();
 
     // ---- re-quantise h for all k experts (each CTA holds the full set)
     if (!abort) {
@@ -397,13 +436,14 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
         }
     }
     consumer_sync();
+    if (tr && threadIdx.x == 0) tr[5] = now_ns();
 
     // ---- phase B: down rows of all k experts + rank-ordered combine
     for (int c = nA; c < nCh; c++) {
         int s = c % nslot;
-        if (!mbar_wait(&full[s], (uint32_t)(c / nslot) & 1u)) {
-            abort = true;
-            if (lane == 0) atomicOr(err, FUSED_ERR_COPY);
+        if (!dead && !mbar_wait(&full[s], (uint32_t)(c / nslot) & 1u)) {
+            dead = abort = true;
+            if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
         }
         const ChunkDesc d = desc[c];
         const uint8_t *base = stage + (size_t)s * SLOT_BYTES;
@@ -426,6 +466,10 @@ k_fused_ffn(const FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict_
             }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (tr) {
+        consumer_sync();
+        if (threadIdx.x == 0) tr[6] = now_ns();
     }
 }
 
@@ -492,13 +536,13 @@ bool fused_supports(const FusedScratch &f, const tlmg_geom &g, const int *gu, in
         max_dn = std::max(max_dn, g.d_expert / dt_block(dn[i]) * dt_block_bytes(dn[i]));
     }
     if (2 * max_gu + 96 > SLOT_BYTES) return false;
-    if (g.top_k * (max_dn + 32) > SLOT_BYTES) return false;
+    if (g.top_k * (max_dn + 48) > SLOT_BYTES) return false;
     // chunk budget: phase A chunks + expert splits, phase B chunks
     const int G = f.nsm;
     int64_t pairs = ((int64_t)g.top_k * g.d_expert + G - 1) / G;
     int64_t ca = pairs / std::max(1, (SLOT_BYTES - 96) / (2 * max_gu)) + g.top_k + 2;
     int64_t rows = (g.d_model + G - 1) / G;
-    int64_t cb = rows / std::max(1, (SLOT_BYTES - 32 * g.top_k) / (g.top_k * max_dn)) + 2;
+    int64_t cb = rows / std::max(1, (SLOT_BYTES - 48 * g.top_k) / (g.top_k * max_dn)) + 2;
     return ca + cb <= MAXCH;
 }
 
@@ -521,7 +565,12 @@ int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
 uint32_t fused_take_error(FusedScratch &f) {
     if (!f.err_host) return 0;
     uint32_t e = *(volatile uint32_t *)f.err_host;
-    if (e) *(volatile uint32_t *)f.err_host = 0;
+    if (e) {
+        // the stream is idle (the caller synchronised): clear the sticky
+        // device word and the barrier state for the next launch
+        *(volatile uint32_t *)f.err_host = 0;
+        cudaMemset(f.bar, 0, 64);
+    }
     return e;
 }
 

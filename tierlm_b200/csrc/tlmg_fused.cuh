@@ -49,7 +49,12 @@ struct FusedArgs {
     int D, de, E, k, router;
     float routed_scale;
     uint32_t x_kinds;              // bit 0: Q8_K input needed, bit 1: Q8_0 input needed
+    uint64_t *trace;               // NULL, or [gridDim][FUSED_TRACE_POINTS] %globaltimer stamps
 };
+
+// Phase boundaries stamped per CTA when tracing: start, routed, planned,
+// phase A done, grid barrier passed, h quantised, end.
+constexpr int FUSED_TRACE_POINTS = 8;
 
 int fused_init(FusedScratch &f, const tlmg_geom &g);
 void fused_release(FusedScratch &f);

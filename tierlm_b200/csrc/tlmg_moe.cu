@@ -56,6 +56,8 @@ struct Layer {
     size_t router_rb = 0;
     float *router_bias = nullptr;
     uint8_t *mask = nullptr;
+    bool fused_ok = false;         // the persistent kernel can serve this layer
+    uint32_t x_kinds = 0;          // input activation kinds gate/up need (bit 0 Q8_K, bit 1 Q8_0)
     bool has_shared = false;
     int sh_dt[3] = { 0, 0, 0 };
     void *sh_w[3] = { nullptr, nullptr, nullptr };
@@ -90,6 +92,8 @@ struct tlmg_ctx {
     size_t pin_cap = 0;
     int64_t launch0 = 0;
     FusedScratch fused;
+    bool fused_on = true;
+    uint64_t *trace = nullptr;     // device [nsm][FUSED_TRACE_POINTS] when tracing
     // per-launch event timing (tlmg_profile)
     bool prof = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -136,6 +140,21 @@ static int sync_slots(tlmg_ctx *c, Layer &Ly) {
                                cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "slot table upload");
     Ly.slots_dirty = false;
+    // which kernels can serve the layer: the distinct dtypes of its experts
+    int gu[8], dn[8], ngu = 0, ndn = 0;
+    bool all = true;
+    Ly.x_kinds = 0;
+    for (const Slot &sl : Ly.h_slots) {
+        if (!sl.ok) { all = false; continue; }
+        for (int m = 0; m < 3; m++) {
+            int *arr = m < 2 ? gu : dn, &n = m < 2 ? ngu : ndn;
+            bool seen = false;
+            for (int i = 0; i < n; i++) seen |= arr[i] == sl.dt[m];
+            if (!seen && n < 8) arr[n++] = sl.dt[m];
+            if (m < 2) Ly.x_kinds |= act_kind_for(sl.dt[m]) == DT_Q8_0 ? 2u : 1u;
+        }
+    }
+    Ly.fused_ok = all && fused_supports(c->fused, c->g, gu, ngu, dn, ndn);
     return TLMG_OK;
 }
 
@@ -344,7 +363,7 @@ static void prof_bytes(tlmg_ctx *c, const Layer &Ly) {
     const int64_t D = c->g.d_model, de = c->g.d_expert, k = c->g.top_k;
     int64_t gu = k * de * (int64_t)(tlmg_row_bytes(s.dt[0], D) + tlmg_row_bytes(s.dt[1], D));
     int64_t dn = k * D * (int64_t)tlmg_row_bytes(s.dt[2], de);
-    bool fused = c->fused.enabled;
+    bool fused = c->fused_on && Ly.fused_ok;
     c->prof_bytes[0] = fused ? gu + dn : gu;
     c->prof_bytes[1] = dn;
     c->prof_bytes[2] = 4 * (int64_t)c->g.n_experts;
@@ -363,17 +382,39 @@ static int run_experts(tlmg_ctx *c, Layer &Ly, const float *logits, float *ffn, 
                        const float *sgate, const float *x) {
     const tlmg_geom &g = c->g;
     prof_bytes(c, Ly);
+    if (c->fused_on && Ly.fused_ok && x) {
+        FusedArgs a;
+        a.slots = Ly.d_slots;
+        a.logits = logits;
+        a.mask = Ly.mask;
+        a.bias = Ly.router_bias;
+        a.x = x;
+        a.hbuf = c->hbuf;
+        a.ffn = ffn;
+        a.h = h;
+        a.s_out = s_out;
+        a.sgate = sgate;
+        a.ids_out = c->ids;
+        a.w_out = c->w;
+        a.D = g.d_model;
+        a.de = g.d_expert;
+        a.E = g.n_experts;
+        a.k = g.top_k;
+        a.router = g.router;
+        a.routed_scale = g.routed_scale;
+        a.x_kinds = Ly.x_kinds;
+        a.trace = c->trace;
+        prof_mark(c, 0, true);
+        int rc = launch_fused_ffn(c->fused, a, c->st);
+        prof_mark(c, 0, false);
+        return rc;
+    }
     prof_mark(c, 2, true);
     int rc = launch_route(g.router, logits, Ly.mask, Ly.router_bias, g.n_experts, g.top_k, g.routed_scale, c->ids,
                           c->w, c->st);
     prof_mark(c, 2, false);
     if (rc) return rc;
-    if (use_fused(c->fused, g, x != nullptr)) {
-        prof_mark(c, 0, true);
-        rc = launch_fused_ffn(c->fused, g, Ly.d_slots, c->ids, c->w, x, ffn, h, s_out, sgate, c->st);
-        prof_mark(c, 0, false);
-        return rc;
-    }
+    (void)x;
     int k = g.top_k, D = g.d_model, de = g.d_expert;
     unsigned grid = (unsigned)std::min<int64_t>(((int64_t)k * de + FFN_WARPS - 1) / FFN_WARPS, 148 * 8);
     prof_mark(c, 0, true);
@@ -403,7 +444,7 @@ static int expert_ffn_dev(tlmg_ctx *c, int layer, const float *x, const float *l
     int rc = sync_slots(c, Ly);
     if (rc) return rc;
     if (!layer_ready(c, Ly)) return set_error(TLMG_ENOTFOUND, "layer %d: not every expert slot is loaded", layer);
-    if ((rc = quant_inputs(c, x))) return rc;
+    if (!(c->fused_on && Ly.fused_ok) && (rc = quant_inputs(c, x))) return rc;
     return run_experts(c, Ly, logits, ffn, nullptr, nullptr, nullptr, x);
 }
 
@@ -444,7 +485,13 @@ static int finish_d2h(tlmg_ctx *c, void *dst, size_t bytes, PtrKind k, size_t st
 
 static int stream_sync(tlmg_ctx *c) {
     cudaError_t e = cudaStreamSynchronize(c->st);
-    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "stream synchronize");
+    if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    uint32_t fe = fused_take_error(c->fused);
+    if (fe)
+        return set_error(TLMG_EIO, "expert FFN kernel gave up waiting (%s%s%s); results of this call are invalid",
+                         fe & FUSED_ERR_BARRIER ? "grid barrier " : "", fe & FUSED_ERR_COPY ? "weight copies " : "",
+                         fe & FUSED_ERR_PLAN ? "work plan" : "");
+    return TLMG_OK;
 }
 
 
@@ -560,6 +607,37 @@ int tlmg_profile_read(tlmg_ctx *c, int cls, double *ms, int64_t *launches, int64
     if (launches) *launches = n;
     if (bytes_per_launch) *bytes_per_launch = c->prof_bytes[cls];
     return TLMG_OK;
+}
+
+int tlmg_set_fused(tlmg_ctx *c, int on) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    c->fused_on = on != 0;
+    return c->fused.enabled ? TLMG_OK : (on ? set_error(TLMG_EUNSUP, "persistent kernel unavailable on this device") : TLMG_OK);
+}
+
+int tlmg_trace(tlmg_ctx *c, int on, uint64_t *out, int cap) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    cudaSetDevice(c->device);
+    const int n = c->fused.nsm * FUSED_TRACE_POINTS;
+    if (on && !c->trace) {
+        if (!(c->trace = (uint64_t *)dalloc(c, 8 * (size_t)n))) return set_error(TLMG_ENOMEM, "trace buffer");
+        cudaMemset(c->trace, 0, 8 * (size_t)n);
+    }
+    int rc = stream_sync(c);
+    if (rc) return rc;
+    int got = 0;
+    if (out && c->trace && cap > 0) {
+        got = cap < n ? cap : n;
+        cudaMemcpy(out, c->trace, 8 * (size_t)got, cudaMemcpyDeviceToHost);
+    }
+    if (!on) c->trace = nullptr;   // the buffer stays owned by the context
+    return got;
+}
+
+int tlmg_check(tlmg_ctx *c) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    cudaSetDevice(c->device);
+    return stream_sync(c);
 }
 
 int tlmg_set_stream(tlmg_ctx *c, void *stream) {

@@ -57,6 +57,21 @@ class MoeContext:
         except Exception:
             pass
 
+    def set_fused(self, on: bool) -> None:
+        """Persistent single-launch kernel (True, default) or the multi-kernel path."""
+        check(self._lib.tlmg_set_fused(self._h, 1 if on else 0))
+
+    def check(self) -> None:
+        """Wait for queued work; raise if a kernel reported an expired wait."""
+        check(self._lib.tlmg_check(self._h))
+
+    def trace(self, on: bool = True):
+        """Switch the persistent kernel's phase trace on / off; returns the
+        last launch's stamps as int64 [CTAs, 8] (ns) or None."""
+        buf = np.zeros(4096 * 8, np.uint64)
+        n = check(self._lib.tlmg_trace(self._h, 1 if on else 0, buf.ctypes.data, buf.size))
+        return buf[:n].reshape(-1, 8).astype(np.int64) if n else None
+
     def set_stream(self, stream=None) -> None:
         """Queue work on a torch.cuda.Stream (None: the context's own stream)."""
         from .quant import stream_handle
