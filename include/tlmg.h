@@ -191,6 +191,35 @@ int tlmg_profile(tlmg_ctx *ctx, int on);
 int tlmg_profile_read(tlmg_ctx *ctx, int kclass, double *ms, int64_t *launches,
                       int64_t *bytes_per_launch);
 
+/* ---- allocation-free expert FFN --------------------------------------- */
+/* One routed expert given by device pointers to its gate [de x D], up
+ * [de x D] and down [D x de] matrices and their dtypes. */
+typedef struct {
+    const void *m[3];
+    int32_t     dt[3];
+    int32_t     pad;
+} tlmg_expert_slot;
+
+/* No counterpart in the reference: this is an addition of this library.
+ * The routed-expert FFN of one token, like tlmg_expert_ffn, for callers
+ * that cannot allocate device memory on their decode path (a runtime that
+ * sizes every buffer once at start-up and then runs a latency-bound token
+ * loop, where cudaMalloc/cudaFree may block or synchronise the device).
+ * No context, no allocation: experts (HOST array of E entries, device
+ * pointers inside) and x f32[D], logits f32[E], ffn f32[D], ids int32[k],
+ * w f32[k] (DEVICE pointers; ids/w may be NULL) are the caller's; the only
+ * scratch is a fixed 1 MiB array in device memory that every GPU loading
+ * the library holds until the process exits. Sizes needing more scratch
+ * (about k*de*4 + k*(de+34) + 2.3*D + 40*E bytes) return TLMG_ERANGE.
+ * The first call on each device looks up the array's device address (with
+ * that device current): make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU (different
+ * streams or threads without ordering) race and give wrong results. Same
+ * bits as tlmg_expert_ffn for the same experts and inputs. */
+int tlmg_expert_ffn_noalloc(const tlmg_expert_slot *experts, int E, int D, int de, int k, int router,
+                            float routed_scale, const float *x, const float *logits, float *ffn,
+                            int32_t *ids, float *w, void *stream);
+
 /* Kernel launches issued by the library since the context was opened
  * (counted on the host at each launch). */
 int64_t tlmg_launch_count(const tlmg_ctx *ctx);

@@ -30,6 +30,11 @@ class TlmError(RuntimeError):
         self.code = code
 
 
+class ExpertSlot(C.Structure):
+    """tlmg_expert_slot: device pointers of one expert's gate, up, down."""
+    _fields_ = [("m", C.c_void_p * 3), ("dt", C.c_int32 * 3), ("pad", C.c_int32)]
+
+
 class Geom(C.Structure):
     _fields_ = [("n_layers", C.c_int32), ("d_model", C.c_int32), ("d_expert", C.c_int32),
                 ("d_shared", C.c_int32), ("n_experts", C.c_int32), ("top_k", C.c_int32),
@@ -70,6 +75,7 @@ _SIGS = {
     "tlmg_profile": (_I, [_P, _I]),
     "tlmg_profile_read": (_I, [_P, _I, C.POINTER(C.c_double), C.POINTER(_I64), C.POINTER(_I64)]),
     "tlmg_launch_count": (_I64, [_P]),
+    "tlmg_expert_ffn_noalloc": (_I, [_P, _I, _I, _I, _I, _I, _F, _P, _P, _P, _P, _P, _P]),
 }
 
 

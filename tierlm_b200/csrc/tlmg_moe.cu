@@ -5,6 +5,7 @@
 // Reference: moe() / run_batch() / expert_mats(), src/lib/tlm_model.c:880-1055.
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "tlmg_dev.cuh"
@@ -922,3 +923,107 @@ int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free expert FFN.
+//
+// For callers that must not allocate device memory on their decode path: a
+// host runtime that sizes every buffer once at start-up (as the reference
+// sizes its slot arena and scratch in tlm_model_open) and then runs a
+// latency-bound per-token loop, where cudaMalloc / cudaFree could block on
+// the allocator or synchronise the device behind other streams' work. This
+// entry point takes the caller's device buffers and uses, as its only
+// scratch, the fixed array below, which lives in every GPU that loads the
+// library until the process exits.
+namespace tlmg {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(1) << 20;   // 1 MiB per device
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mu;
+static uint8_t *g_noalloc_addr[64];   // device address of the array, per device ordinal
+
+// Set-up, once per device with that device current: the array's name is
+// only a host-side stand-in, so its device address must be looked up.
+static int noalloc_scratch(uint8_t **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "expert_ffn_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= 64) return set_error(TLMG_EUNSUP, "expert_ffn_noalloc: device ordinal %d >= 64", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "expert_ffn_noalloc: cudaGetSymbolAddress");
+        g_noalloc_addr[dev] = (uint8_t *)p;
+    }
+    *out = g_noalloc_addr[dev];
+    return TLMG_OK;
+}
+
+}  // namespace tlmg
+
+extern "C" int tlmg_expert_ffn_noalloc(const tlmg_expert_slot *experts, int E, int D, int de, int k, int router,
+                                       float routed_scale, const float *x, const float *logits, float *ffn,
+                                       int32_t *ids, float *w, void *stream) {
+    if (!experts || !x || !logits || !ffn) return set_error(TLMG_EINVAL, "expert_ffn_noalloc: NULL argument");
+    if (E <= 0 || E > RT_PER * 32 || k <= 0 || k > E || k > 64 || router < 0 || router > 2)
+        return set_error(TLMG_EINVAL, "expert_ffn_noalloc: E=%d k=%d router=%d unsupported", E, k, router);
+    if (D <= 0 || de <= 0 || D % 256 || de % 256)
+        return set_error(TLMG_EINVAL, "expert_ffn_noalloc: D=%d de=%d must be positive multiples of 256", D, de);
+    for (int e = 0; e < E; e++)
+        for (int m = 0; m < 3; m++) {
+            int q = dt_block(experts[e].dt[m]);
+            if (q <= 1 || !experts[e].m[m])
+                return set_error(TLMG_EINVAL, "expert_ffn_noalloc: expert %d matrix %d: dtype %d / pointer", e, m,
+                                 experts[e].dt[m]);
+        }
+    // scratch layout: slot table | x as Q8_K | x as Q8_0 | ids | w | SwiGLU rows | re-quantised rows
+    const size_t hq_stride = (std::max(tlmg_qact_bytes(DT_Q8_K, de), tlmg_qact_bytes(DT_Q8_0, de)) + 255) & ~size_t(255);
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t o_slots = 0, o_xk = up(o_slots + sizeof(Slot) * (size_t)E);
+    const size_t o_x0 = up(o_xk + tlmg_qact_bytes(DT_Q8_K, D)), o_ids = up(o_x0 + tlmg_qact_bytes(DT_Q8_0, D));
+    const size_t o_w = up(o_ids + 4 * 64), o_h = up(o_w + 4 * 64), o_hq = up(o_h + 4 * (size_t)k * de);
+    const size_t need = o_hq + hq_stride * (size_t)k;
+    if (need > NOALLOC_SCRATCH_BYTES)
+        return set_error(TLMG_ERANGE, "expert_ffn_noalloc: needs %zu bytes of scratch, the fixed array has %zu", need,
+                         NOALLOC_SCRATCH_BYTES);
+    uint8_t *sc = nullptr;
+    int rc = noalloc_scratch(&sc);
+    if (rc) return rc;
+    cudaStream_t st = pick_stream(stream);
+    Slot slots[RT_PER * 32];
+    for (int e = 0; e < E; e++) {
+        for (int m = 0; m < 3; m++) {
+            slots[e].m[m] = (const uint8_t *)experts[e].m[m];
+            slots[e].dt[m] = experts[e].dt[m];
+        }
+        slots[e].ok = 1;
+    }
+    Slot *d_slots = (Slot *)(sc + o_slots);
+    uint8_t *xk = sc + o_xk, *x0 = sc + o_x0, *hq = sc + o_hq;
+    int32_t *d_ids = (int32_t *)(sc + o_ids);
+    float *d_w = (float *)(sc + o_w), *hbuf = (float *)(sc + o_h);
+    // the slot table is copied from this stack frame; a copy from pageable
+    // memory has consumed its source when cudaMemcpyAsync returns
+    cudaError_t e = cudaMemcpyAsync(d_slots, slots, sizeof(Slot) * (size_t)E, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_fail(e, "expert_ffn_noalloc: slot table copy");
+    if ((rc = launch_quant_act(DT_Q8_K, x, D, xk, st))) return rc;
+    if ((rc = launch_quant_act(DT_Q8_0, x, D, x0, st))) return rc;
+    if ((rc = launch_route(router, logits, nullptr, nullptr, E, k, routed_scale, d_ids, d_w, st))) return rc;
+    unsigned grid = (unsigned)std::min<int64_t>(((int64_t)k * de + FFN_WARPS - 1) / FFN_WARPS, 148 * 8);
+    k_ffn_gateup<<<grid, FFN_WARPS * 32, 0, st>>>(d_slots, d_ids, k, D, de, xk, x0, hbuf);
+    if ((rc = launched("noalloc gate/up"))) return rc;
+    int per = std::max((de + 255) / 256, (de + 31) / 32);
+    int64_t nw = (int64_t)k * per;
+    k_quant_h<<<(unsigned)((nw + 7) / 8), 256, 0, st>>>(d_slots, d_ids, k, de, hbuf, hq, hq_stride);
+    if ((rc = launched("noalloc requant"))) return rc;
+    k_ffn_down<<<(unsigned)std::min(148 * 8, (D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, st>>>(
+        d_slots, d_ids, d_w, k, D, de, hq, hq_stride, nullptr, nullptr, ffn, nullptr);
+    if ((rc = launched("noalloc down"))) return rc;
+    if (ids && (e = cudaMemcpyAsync(ids, d_ids, 4 * (size_t)k, cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+        return cuda_fail(e, "expert_ffn_noalloc: ids copy");
+    if (w && (e = cudaMemcpyAsync(w, d_w, 4 * (size_t)k, cudaMemcpyDeviceToDevice, st)) != cudaSuccess)
+        return cuda_fail(e, "expert_ffn_noalloc: w copy");
+    return TLMG_OK;
+}
