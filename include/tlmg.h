@@ -174,10 +174,12 @@ int tlmg_check(tlmg_ctx *ctx);
 
 /* Phase trace of the persistent kernel (the reference's per-step stats,
  * src/lib/tlm_model.h:263-266, at kernel granularity): with on = 1 every
- * launch stamps %globaltimer at its phase boundaries per CTA (start, routed,
- * planned, gate/up done, grid barrier passed, h quantised, end). Copies up
- * to `cap` stamps of the last launch ([CTA][8] u64 ns) to `out` (host) and
- * returns how many; on = 0 stops tracing. */
+ * launch records per CTA 16 u64 values: %globaltimer ns at start, routed,
+ * gate/up done, fenced, arrived, barrier passed, h quantised, end, then the
+ * consumer warps' summed ns waiting for / computing gate/up chunks and
+ * waiting for / computing down chunks. Copies up to `cap` values of the
+ * last launch ([CTA][16]) to `out` (host) and returns how many; on = 0 stops
+ * tracing. */
 int tlmg_trace(tlmg_ctx *ctx, int on, uint64_t *out, int cap);
 
 /* Per-launch timing of the expert-FFN kernels with CUDA events recorded on
@@ -186,8 +188,9 @@ int tlmg_trace(tlmg_ctx *ctx, int on, uint64_t *out, int cap);
  * kernel), 1 = down + combine, 2 = router top-k. */
 int tlmg_profile(tlmg_ctx *ctx, int on);
 /* Totals since profiling was switched on (synchronises the stream): device
- * milliseconds, launches, and the algorithmic weight bytes one launch of
- * that class reads (from the layer's expert dtypes). */
+ * milliseconds, launches, and the average algorithmic weight bytes one
+ * launch of that class reads (from the layers' expert dtypes and the tokens
+ * each launch served). */
 int tlmg_profile_read(tlmg_ctx *ctx, int kclass, double *ms, int64_t *launches,
                       int64_t *bytes_per_launch);
 

@@ -230,7 +230,9 @@ def test_moe_layer_vs_oracle(dev, orc, variant):
 
 
 def test_expert_ffn_many_matches_single(dev):
-    """The batched host-buffer call equals per-token calls, layer by layer."""
+    """The batched host-buffer call equals per-token calls, layer by layer
+    (token t uses layer (layer0 + t) % n_layers), through the persistent
+    multi-token launch and through the per-token multi-kernel path."""
     from tierlm_b200 import synth
     rng = np.random.default_rng(21)
     D, de, E, k, NL = 512, 256, 16, 4, 3
@@ -240,11 +242,16 @@ def test_expert_ffn_many_matches_single(dev):
     x = rng.standard_normal((T, D)).astype(np.float32)
     lg = rng.standard_normal((T, E)).astype(np.float32)
     out = np.zeros((T, D), np.float32)
+    n0 = ctx.launches
     ctx.expert_ffn_many(1, x, lg, out)
-    for t in range(T):
-        one = np.zeros(D, np.float32)
-        ctx.expert_ffn((1 + t) % NL, x[t], lg[t], one)
-        assert same_bits(one, out[t]).all(), t
+    assert ctx.launches - n0 == 1
+    for fused in (True, False):
+        ctx.set_fused(fused)
+        for t in range(T):
+            one = np.zeros(D, np.float32)
+            ctx.expert_ffn((1 + t) % NL, x[t], lg[t], one)
+            assert same_bits(one, out[t]).all(), (fused, t)
+    ctx.set_fused(True)
     pinned_x = torch.from_numpy(x).pin_memory()
     pinned_l = torch.from_numpy(lg).pin_memory()
     pinned_o = torch.zeros((T, D)).pin_memory()
@@ -297,36 +304,55 @@ def test_qmv_host_adapter(dev, orc):
     assert ptr is not None
 
 
-@pytest.mark.parametrize("dts", [(12, 12, 14), (13, 13, 15), (8, 8, 8), (14, 14, 14), (12, 12, 12)])
-def test_fused_matches_multikernel(dev, orc, dts):
-    """The persistent kernel and the multi-kernel path give identical bits on
-    the config-2 layer shape (D 2048, de 768, k 8) over many consecutive
-    launches (the grid barrier is reused every launch), and both equal the
-    oracle."""
+FUSED_SHAPES = [
+    # (D, de, E, k, dtypes, fused kernel expected)
+    (2048, 768, 24, 8, (12, 12, 14), True),    # config-2 layer shape
+    (2048, 768, 24, 8, (13, 13, 13), True),
+    (2048, 768, 24, 8, (14, 14, 14), True),
+    (512, 256, 32, 4, (14, 14, 14), True),     # config-1 shape: fewer units than lanes
+    (4096, 1536, 12, 8, (12, 12, 12), True),   # 235B-A22B shape: two units per lane
+    (1024, 512, 160, 6, (12, 12, 13), True),   # E > 136: one thread per router entry
+    (2048, 768, 24, 8, (13, 13, 15), False),   # Q8_K down: multi-kernel path
+    (1024, 512, 16, 4, (8, 8, 8), False),      # Q8_0 experts: multi-kernel path
+]
+
+
+@pytest.mark.parametrize("shape", FUSED_SHAPES, ids=lambda s: f"D{s[0]}-de{s[1]}-E{s[2]}-k{s[3]}-{s[4]}")
+def test_fused_matches_multikernel(dev, orc, shape):
+    """The persistent kernel and the multi-kernel path give identical bits
+    over many consecutive tokens (the grid barrier, the stage ring and the
+    double-buffered routing are reused token after token), both equal the
+    oracle, and the persistent kernel really runs as one launch for the
+    whole token batch where it applies."""
     from tierlm_b200 import synth
-    rng = np.random.default_rng(sum(dts))
-    D, de, E, k = 2048, 768, 24, 8
+    D, de, E, k, dts, fused_expected = shape
+    rng = np.random.default_rng(D + de + E + k + sum(dts))
     experts = [synth.rand_expert(rng, D, de, dts) for _ in range(E)]
     ctx = build_ctx(experts, D, de, E, k, 0)
-    T = 24
+    T = 12
     x = rng.standard_normal((T, D)).astype(np.float32)
     lg = rng.standard_normal((T, E)).astype(np.float32)
     lg[5] = 0.0                                   # all-tie routing row
-    outs = {}
+    outs, launches = {}, {}
     for fused in (True, False):
         ctx.set_fused(fused)
         xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
         od = torch.zeros((T, D), device=dev)
+        n0 = ctx.launches
         ctx.expert_ffn_many(0, xd, ld, od)
         ctx.check()
+        launches[fused] = ctx.launches - n0
         outs[fused] = od.cpu().numpy()
+    # the persistent kernel serves all T tokens in one launch
+    assert (launches[True] == 1) == fused_expected, launches
     assert same_bits(outs[True], outs[False]).all()
     orc.set_expf_mode(1)
     try:
         geom = dict(d_model=D, d_expert=de, n_experts=E, top_k=k, router=0)
         for t in (0, 5, T - 1):
             ref, _, _ = orc.expert_ffn(geom, experts, x[t], lg[t])
-            assert same_bits(outs[True][t], ref).all(), t
+            bad = np.flatnonzero(~same_bits(outs[True][t], ref))
+            assert bad.size == 0, (t, bad[:4], outs[True][t][bad[:4]], ref[bad[:4]])
     finally:
         orc.set_expf_mode(0)
     ctx.close()

@@ -28,6 +28,11 @@ NVCC_FLAGS = [
 ]
 
 
+# The persistent kernel runs 17 warps per SM (96 registers a thread); its
+# per-step device functions are compiled separately under the same cap.
+FILE_FLAGS = {"tlmg_fused.cu": ["-maxrregcount=96"]}
+
+
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
         if cand and Path(cand).exists():
@@ -59,7 +64,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
     objs = []
     for src in sources():
         obj = objdir / (src.stem + ".o")
-        cmd = [cc, *NVCC_FLAGS, "-I", str(INCLUDE), "-dc", str(src), "-o", str(obj)]
+        cmd = [cc, *NVCC_FLAGS, *FILE_FLAGS.get(src.name, []), "-I", str(INCLUDE), "-dc", str(src), "-o", str(obj)]
         if ptxas_v:
             cmd[1:1] = ["-Xptxas", "-v"]
         if verbose:

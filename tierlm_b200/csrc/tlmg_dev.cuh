@@ -442,149 +442,188 @@ __device__ __forceinline__ float tree32(float v) {
 
 // ---------------------------------------------------------------------------
 // router top-k (reference tlm_model.c:776-839), one warp. Entry e lives in
-// lane e % 32, slot e / 32.
-constexpr int RT_PER = 16;   // E <= 512
+// lane e % 32, slot e / 32. The warp keeps the probabilities and the
+// selection keys in shared memory (RT_SCRATCH words), not in registers, so
+// a producer warp that routes stays small.
+constexpr int RT_PER = 16;                  // E <= 512
+constexpr int RT_SCRATCH = 2 * RT_PER * 32; // 32-bit words of router scratch
 
-__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
-    // larger value wins; equal values -> lower index; bi < 0 = nothing yet
-    return bi < 0 || v > bv || (v == bv && i < bi);
+// Order-preserving map of a non-NaN float to u32 (-0 and +0 map alike, as
+// they compare equal); 0 is below every key and marks "not a candidate".
+__device__ __forceinline__ uint32_t fkey(float v) {
+    uint32_t b = __float_as_uint(__fadd_rn(v, 0.0f));
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// Top-k of v[] over entries not masked, not NaN, not used; fallback = lowest
-// unmasked unused index, else 0 (reference topk, tlm_model.c:776-795).
-__device__ __forceinline__ void warp_topk(const float (&v)[RT_PER], const bool (&off)[RT_PER], int E, int k, int lane,
-                          int32_t *ids_sm) {
-    uint32_t used = 0u;   // bit s: slot s of this lane is taken (registers, no local array)
+// Top-k by key among entries with a nonzero key (unmasked, not NaN); ties ->
+// lowest index; when no candidate is left, the lowest entry of `avail`
+// (unmasked, unused), else 0 (reference topk, tlm_model.c:776-795). Each
+// round is one warp max-reduction of the lanes' best keys and one
+// min-reduction of the indices holding it; only the lane that owned the
+// pick rescans its slots. Lane r returns ids[r] in id0 and ids[r + 32] in id1.
+__device__ __forceinline__ void warp_topk(uint32_t *key_sm, uint32_t avail, int E, int k, int lane, int &id0,
+                                          int &id1) {
+    const int nper = (E + 31) >> 5;
+    uint32_t bk = 0u, bi = 0xFFFFFFFFu;
+    for (int s = 0; s < nper; s++) {
+        const int e = lane + 32 * s;
+        if (e < E) {
+            const uint32_t key = key_sm[e];
+            if (key > bk) { bk = key; bi = (uint32_t)e; }
+        }
+    }
+    id0 = id1 = 0;
     for (int r = 0; r < k; r++) {
-        float bv = 0.0f;
-        int bi = -1;
-        int fb = -1;   // lowest unmasked unused index of this lane
-#pragma unroll
-        for (int s = 0; s < RT_PER; s++) {
-            int e = lane + 32 * s;
-            if (e >= E || off[s] || ((used >> s) & 1u)) continue;
-            if (fb < 0) fb = e;
-            if (v[s] != v[s]) continue;
-            if (better(v[s], e, bv, bi)) { bv = v[s]; bi = e; }
+        const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, bk);
+        uint32_t pick;
+        if (m != 0u) {
+            pick = __reduce_min_sync(0xFFFFFFFFu, bk == m ? bi : 0xFFFFFFFFu);
+        } else {
+            const uint32_t fb = avail ? (uint32_t)(lane + 32 * (__ffs(avail) - 1)) : 0xFFFFFFFFu;
+            pick = __reduce_min_sync(0xFFFFFFFFu, fb);
+            if (pick == 0xFFFFFFFFu) pick = 0u;
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-            int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-            int of = __shfl_xor_sync(0xFFFFFFFFu, fb, o);
-            if (oi >= 0 && better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-            if (of >= 0 && (fb < 0 || of < fb)) fb = of;
+        if (lane == r) id0 = (int)pick;
+        if (lane + 32 == r) id1 = (int)pick;
+        if ((int)(pick & 31u) == lane && (int)pick < E) {
+            avail &= ~(1u << (pick >> 5));
+            key_sm[pick] = 0u;
+            bk = 0u;
+            bi = 0xFFFFFFFFu;
+            for (int s = 0; s < nper; s++) {
+                const int e = lane + 32 * s;
+                if (e < E) {
+                    const uint32_t key = key_sm[e];
+                    if (key > bk) { bk = key; bi = (uint32_t)e; }
+                }
+            }
         }
-        int pick = bi >= 0 ? bi : (fb >= 0 ? fb : 0);
-        if ((pick & 31) == lane && pick < E) used |= 1u << (pick >> 5);
-        if (lane == 0) ids_sm[r] = pick;
     }
 }
 
-// Router of one token by one full warp (lane = 0..31). p_sm: scratch of
-// RT_PER*32 floats; ids_sm / w_sm: outputs (k entries), valid after the
-// call in all lanes of the warp (the call ends with __syncwarp).
-static __device__ __forceinline__ void warp_route(int router, const float *__restrict__ logits, const uint8_t *__restrict__ mask,
-                           const float *__restrict__ bias, int E, int k, float routed_scale, float *p_sm,
-                           int32_t *ids_sm, float *w_sm, int lane) {
-    float p[RT_PER], v[RT_PER];
-    bool off[RT_PER];
-#pragma unroll
-    for (int s = 0; s < RT_PER; s++) {
-        int e = lane + 32 * s;
-        off[s] = e < E ? (mask && mask[e]) : true;
-        p[s] = 0.0f;
-        v[s] = 0.0f;
+// Weight of rank r held by lane r % 32 (w0 for r < 32, w1 above).
+__device__ __forceinline__ float rank_w(float w0, float w1, int r) {
+    return __shfl_sync(0xFFFFFFFFu, r < 32 ? w0 : w1, r & 31);
+}
+
+// Router of one token by one full warp (lane = 0..31). scratch: RT_SCRATCH
+// words of shared memory; ids_sm / w_sm: outputs (k entries), valid in all
+// lanes after the call (it ends with __syncwarp). k <= 64.
+static __device__ __forceinline__ void warp_route(int router, const float *__restrict__ logits,
+                                                  const uint8_t *__restrict__ mask, const float *__restrict__ bias,
+                                                  int E, int k, float routed_scale, uint32_t *scratch,
+                                                  int32_t *ids_sm, float *w_sm, int lane) {
+    float *p_sm = reinterpret_cast<float *>(scratch);
+    uint32_t *key_sm = scratch + RT_PER * 32;
+    const int nper = (E + 31) >> 5;
+    uint32_t avail = 0u;   // bit s: entry lane + 32 s is unmasked
+    for (int s = 0; s < nper; s++) {
+        const int e = lane + 32 * s;
+        if (e < E && !(mask && mask[e])) avail |= 1u << s;
     }
     if (router == 2) {
-#pragma unroll
-        for (int s = 0; s < RT_PER; s++) {
-            int e = lane + 32 * s;
+        for (int s = 0; s < nper; s++) {
+            const int e = lane + 32 * s;
             if (e >= E) continue;
-            p[s] = sigmoid_f(logits[e]);
-            v[s] = __fadd_rn(p[s], bias ? bias[e] : 0.0f);
-            p_sm[e] = p[s];
+            const float p = sigmoid_f(logits[e]);
+            const float v = __fadd_rn(p, bias ? bias[e] : 0.0f);
+            p_sm[e] = p;
+            key_sm[e] = (((avail >> s) & 1u) && v == v) ? fkey(v) : 0u;
         }
-        warp_topk(v, off, E, k, lane, ids_sm);
         __syncwarp();
-        if (lane == 0) {
-            double s = 0.0;
-            for (int r = 0; r < k; r++) s = __dadd_rn(s, (double)p_sm[ids_sm[r]]);
-            float inv = __double2float_rn(__ddiv_rn(1.0, __dadd_rn(s, 1e-20)));
-            for (int r = 0; r < k; r++) w_sm[r] = __fmul_rn(__fmul_rn(p_sm[ids_sm[r]], inv), routed_scale);
+        int id0, id1;
+        warp_topk(key_sm, avail, E, k, lane, id0, id1);
+        __syncwarp();
+        const float p0 = lane < k ? p_sm[id0] : 0.0f, p1 = lane + 32 < k ? p_sm[id1] : 0.0f;
+        double sum = 0.0;
+        for (int r = 0; r < k; r++) sum = __dadd_rn(sum, (double)rank_w(p0, p1, r));
+        const float inv = __double2float_rn(__ddiv_rn(1.0, __dadd_rn(sum, 1e-20)));
+        if (lane < k) {
+            ids_sm[lane] = id0;
+            w_sm[lane] = __fmul_rn(__fmul_rn(p0, inv), routed_scale);
+        }
+        if (lane + 32 < k) {
+            ids_sm[lane + 32] = id1;
+            w_sm[lane + 32] = __fmul_rn(__fmul_rn(p1, inv), routed_scale);
         }
         __syncwarp();
         return;
     }
-    // softmax over routable entries
-    float mx = -__uint_as_float(0x7F800000u);
-#pragma unroll
-    for (int s = 0; s < RT_PER; s++) {
-        int e = lane + 32 * s;
-        if (e < E && !off[s]) {
-            float l = logits[e];
-            if (l > mx) mx = l;
+    // softmax over the routable entries
+    float mxl = -__uint_as_float(0x7F800000u);
+    for (int s = 0; s < nper; s++) {
+        const int e = lane + 32 * s;
+        if ((avail >> s) & 1u) {
+            const float l = logits[e];
+            if (l > mxl) mxl = l;
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    const uint32_t mk = __reduce_max_sync(0xFFFFFFFFu, fkey(mxl));
+    const float mx = __uint_as_float((mk & 0x80000000u) ? (mk & 0x7FFFFFFFu) : ~mk);
     const bool none = mx == -__uint_as_float(0x7F800000u);
     double part = 0.0;
     uint32_t min_bits = 0x7F800000u;   // smallest nonzero p seen
-#pragma unroll
-    for (int s = 0; s < RT_PER; s++) {
-        int e = lane + 32 * s;
+    for (int s = 0; s < nper; s++) {
+        const int e = lane + 32 * s;
         if (e >= E) continue;
-        float l = logits[e];
-        p[s] = (off[s] || !(l == l) || none) ? 0.0f : cr_expf(__fsub_rn(l, mx));
-        p_sm[e] = p[s];
-        part = __dadd_rn(part, (double)p[s]);
-        if (p[s] != 0.0f) min_bits = min(min_bits, __float_as_uint(p[s]));
+        const float l = logits[e];
+        const float p = (!((avail >> s) & 1u) || !(l == l) || none) ? 0.0f : cr_expf(__fsub_rn(l, mx));
+        p_sm[e] = p;
+        part = __dadd_rn(part, (double)p);
+        if (p != 0.0f) min_bits = min(min_bits, __float_as_uint(p));
     }
     // The reference sums in double, sequentially in index order. When every
     // nonzero term is >= 2^(floor(log2 E) - 29) all partial sums are exact
     // in double, so any order gives the same sum; otherwise lane 0 redoes it
     // sequentially.
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        part = __dadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, o));
-        min_bits = min(min_bits, __shfl_xor_sync(0xFFFFFFFFu, min_bits, o));
-    }
-    int lg = 31 - __clz(E);
-    bool exact = min_bits == 0x7F800000u || __uint_as_float(min_bits) >= ldexpf(1.0f, lg - 29);
+    for (int o = 16; o > 0; o >>= 1) part = __dadd_rn(part, __shfl_xor_sync(0xFFFFFFFFu, part, o));
+    min_bits = __reduce_min_sync(0xFFFFFFFFu, min_bits);
+    const int lg = 31 - __clz(E);
+    const bool exact = min_bits == 0x7F800000u || __uint_as_float(min_bits) >= ldexpf(1.0f, lg - 29);
     __syncwarp();
     double sum = part;
     if (!exact) {
         if (lane == 0) {
-            double s = 0.0;
-            for (int e = 0; e < E; e++) s = __dadd_rn(s, (double)p_sm[e]);
-            part = s;
+            double q = 0.0;
+            for (int e = 0; e < E; e++) q = __dadd_rn(q, (double)p_sm[e]);
+            part = q;
         }
         sum = __shfl_sync(0xFFFFFFFFu, part, 0);
     }
-    float inv = sum > 0.0 ? __double2float_rn(__ddiv_rn(1.0, sum)) : 0.0f;
-#pragma unroll
-    for (int s = 0; s < RT_PER; s++) {
-        int e = lane + 32 * s;
-        if (e < E) {
-            p[s] = __fmul_rn(p[s], inv);
-            p_sm[e] = p[s];
+    const float inv = sum > 0.0 ? __double2float_rn(__ddiv_rn(1.0, sum)) : 0.0f;
+    for (int s = 0; s < nper; s++) {
+        const int e = lane + 32 * s;
+        if (e >= E) continue;
+        const float p = __fmul_rn(p_sm[e], inv);
+        p_sm[e] = p;
+        key_sm[e] = ((avail >> s) & 1u) ? fkey(p) : 0u;   // p is never NaN here
+    }
+    __syncwarp();
+    int id0, id1;
+    warp_topk(key_sm, avail, E, k, lane, id0, id1);
+    __syncwarp();
+    float w0 = lane < k ? p_sm[id0] : 0.0f, w1 = lane + 32 < k ? p_sm[id1] : 0.0f;
+    if (router == 0) {
+        double t = 0.0;
+        for (int r = 0; r < k; r++) t = __dadd_rn(t, (double)rank_w(w0, w1, r));
+        if (t > 0.0) {
+            const float it = __double2float_rn(__ddiv_rn(1.0, t));
+            w0 = __fmul_rn(w0, it);
+            w1 = __fmul_rn(w1, it);
         }
     }
-    warp_topk(p, off, E, k, lane, ids_sm);
-    __syncwarp();
-    if (lane == 0) {
-        for (int r = 0; r < k; r++) w_sm[r] = p_sm[ids_sm[r]];
-        if (router == 0) {
-            double t = 0.0;
-            for (int r = 0; r < k; r++) t = __dadd_rn(t, (double)w_sm[r]);
-            if (t > 0.0) {
-                float it = __double2float_rn(__ddiv_rn(1.0, t));
-                for (int r = 0; r < k; r++) w_sm[r] = __fmul_rn(w_sm[r], it);
-            }
-        }
-        if (routed_scale != 1.0f)
-            for (int r = 0; r < k; r++) w_sm[r] = __fmul_rn(w_sm[r], routed_scale);
+    if (routed_scale != 1.0f) {
+        w0 = __fmul_rn(w0, routed_scale);
+        w1 = __fmul_rn(w1, routed_scale);
+    }
+    if (lane < k) {
+        ids_sm[lane] = id0;
+        w_sm[lane] = w0;
+    }
+    if (lane + 32 < k) {
+        ids_sm[lane + 32] = id1;
+        w_sm[lane + 32] = w1;
     }
     __syncwarp();
 }

@@ -5,6 +5,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <map>
 
 #include "../../include/tlmg.h"
 
@@ -18,53 +19,90 @@ struct Slot {
     int32_t ok;
 };
 
+// One chunk of a CTA's work: rows of the selected experts' matrices that one
+// shared-memory stage holds. Phase A: `nrows` (gate, up) row pairs of rank
+// `rank` starting at row `row0`, two copies (gate, up). Phase B: `nrows`
+// output rows starting at `row0`, one copy per rank from its down matrix,
+// rank r's copy at stage offset r * dst[0]. Offsets are relative to each
+// matrix's base, which is 256-byte aligned, so one plan serves every choice
+// of experts of the same dtypes.
+struct ChunkDesc {
+    uint8_t phase, rank;
+    uint16_t nrows;
+    uint32_t row0;
+    uint32_t tx;          // bytes the chunk's copies deliver
+    uint32_t lo[2];       // first copied byte (16-aligned) inside the matrix
+    uint32_t size[2];     // copy sizes (multiples of 16)
+    uint16_t dst[2];      // stage offset of each copy (phase B: stride between ranks)
+    uint16_t roff[2];     // offset of row0's first byte inside its copy
+    uint32_t pad;
+};
+
+// Host-built work plan for one dtype signature: per CTA, the number of
+// phase A / phase B chunks and the chunks themselves.
+constexpr int FUSED_MAXCH = 48;
+struct FusedPlanKey {
+    int dt_gu, dt_dn;
+    bool operator<(const FusedPlanKey &o) const { return dt_gu != o.dt_gu ? dt_gu < o.dt_gu : dt_dn < o.dt_dn; }
+};
+
 // Per-context state of the persistent kernel.
 struct FusedScratch {
     bool enabled = false;          // usable on this device / geometry
-    uint32_t *bar = nullptr;       // device: [0] arrivals, [1] generation
+    uint32_t *bar = nullptr;       // device: [2] sticky error, [4..11] four 64-bit barrier arrival words
     uint32_t *err_host = nullptr;  // mapped pinned word: error bits set by the kernel
     uint32_t *err_dev = nullptr;   // its device alias
     int nsm = 0;                   // CTAs = SMs (one persistent CTA per SM)
-    int slot_bytes = 0, nslot = 0; // shared-memory stage ring
+    int nslot = 0;                 // shared-memory stage ring depth
+    uint64_t rounds = 0;           // grid-barrier rounds (tokens) launched since the barrier word was reset
     size_t smem = 0;               // dynamic shared memory per CTA
+    size_t smem_limit = 0;
+    std::map<FusedPlanKey, void *> plans;   // device: int2 counts[nsm] | ChunkDesc [nsm][FUSED_MAXCH]
 };
 
 // Error bits the kernel reports through err_host.
 enum : uint32_t { FUSED_ERR_BARRIER = 1u, FUSED_ERR_COPY = 2u, FUSED_ERR_PLAN = 4u };
 
-// Everything one launch needs.
+// Everything one launch needs. The launch processes n_tok independent
+// tokens; token t uses layer (layer0 + t) % n_layers, input x + t*D, router
+// logits + t*E and writes ffn + t*D (and ids_out / w_out + t*k when given).
 struct FusedArgs {
-    const Slot *slots;             // [E] for the layer
-    const float *logits;           // [E]
-    const uint8_t *mask;           // [E] or NULL
-    const float *bias;             // [E] or NULL
-    const float *x;                // [D] normalised input
-    float *hbuf;                   // [k * de] SwiGLU rows (cross-CTA exchange)
-    float *ffn;                    // [D] out
-    float *h;                      // [D] in/out (h += ffn) or NULL
-    const float *s_out;            // [D] shared-expert output or NULL
-    const float *sgate;            // shared-expert gate (device scalar) or NULL
-    int32_t *ids_out;              // [k]
-    float *w_out;                  // [k]
+    const void *plan;              // FusedScratch::plans entry for the layers' dtypes
+    const Slot *slots_all;         // [n_layers][E] slot tables, contiguous
+    const uint8_t *mask_all;       // [n_layers][E] (1 = pruned) or NULL
+    const float *bias_all;         // [n_layers][E] router bias or NULL
+    int layer0, n_layers, n_tok;
+    const float *x;                // [n_tok][D] normalised inputs
+    const float *logits;           // [n_tok][E]
+    float *ffn;                    // [n_tok][D] out
+    float *h;                      // n_tok == 1 only: [D] in/out (h += ffn) or NULL
+    const float *s_out;            // n_tok == 1 only: [D] shared-expert output or NULL
+    const float *sgate;            // n_tok == 1 only: shared-expert gate (device scalar) or NULL
+    int32_t *ids_out;              // [n_tok][k] or NULL
+    float *w_out;                  // [n_tok][k] or NULL
+    float *hbuf;                   // [4][k * de] SwiGLU rows (cross-CTA exchange, by token % 4)
     int D, de, E, k, router;
     float routed_scale;
-    uint32_t x_kinds;              // bit 0: Q8_K input needed, bit 1: Q8_0 input needed
-    uint64_t *trace;               // NULL, or [gridDim][FUSED_TRACE_POINTS] %globaltimer stamps
+    int dt_gu, dt_dn;              // dtype of every gate/up and every down matrix of the layers
+    uint64_t *trace;               // NULL, or [gridDim][FUSED_TRACE_POINTS]
+    uint64_t bar_base;             // set by launch_fused_ffn: grid-barrier rounds before this launch
 };
 
-// Phase boundaries stamped per CTA when tracing: start, routed, planned,
-// phase A done, grid barrier passed, h quantised, end.
-constexpr int FUSED_TRACE_POINTS = 8;
+// Per CTA when tracing: %globaltimer at [0] start, and for the launch's
+// first token [1] routed, [2] gate/up done and arrived, [5] barrier passed,
+// [6] h quantised, [7] combined; [8..11] summed over the consumer warps and
+// all tokens: ns waiting for gate/up chunks, ns computing gate/up, ns
+// waiting for down chunks, ns computing down; [12] end of the launch.
+constexpr int FUSED_TRACE_POINTS = 16;
 
 int fused_init(FusedScratch &f, const tlmg_geom &g);
 void fused_release(FusedScratch &f);
-// Can the kernel serve a layer whose experts use these dtypes? `dts`: the
-// distinct gate/up/down dtypes present (any order), n of them.
-bool fused_supports(const FusedScratch &f, const tlmg_geom &g, const int *gate_up_dts, int n_gu,
-                    const int *down_dts, int n_dn);
+// The work plan for a layer whose gate/up matrices are all dt_gu and down
+// matrices all dt_dn, or NULL when the kernel cannot serve it.
+const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dt_gu, int dt_dn);
 int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st);
-// Error bits raised since the last call (clears them). Call after the
-// stream has been synchronised.
+// Error bits raised since the last call (clears them and resets the
+// barrier state). Call after the stream has been synchronised.
 uint32_t fused_take_error(FusedScratch &f);
 
 }  // namespace tlmg

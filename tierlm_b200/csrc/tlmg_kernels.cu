@@ -247,10 +247,10 @@ k_partials(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__re
 // ---------------------------------------------------------------------------
 __global__ void k_route(int router, const float *__restrict__ logits, const uint8_t *__restrict__ mask,
                         const float *__restrict__ bias, int E, int k, float routed_scale, int32_t *ids, float *w) {
-    __shared__ float p_sm[RT_PER * 32];
+    __shared__ uint32_t scratch[RT_SCRATCH];
     __shared__ int32_t ids_sm[64];
     __shared__ float w_sm[64];
-    warp_route(router, logits, mask, bias, E, k, routed_scale, p_sm, ids_sm, w_sm, threadIdx.x & 31);
+    warp_route(router, logits, mask, bias, E, k, routed_scale, scratch, ids_sm, w_sm, threadIdx.x & 31);
     if (threadIdx.x < k) {
         ids[threadIdx.x] = ids_sm[threadIdx.x];
         w[threadIdx.x] = w_sm[threadIdx.x];

@@ -57,8 +57,8 @@ struct Layer {
     size_t router_rb = 0;
     float *router_bias = nullptr;
     uint8_t *mask = nullptr;
-    bool fused_ok = false;         // the persistent kernel can serve this layer
-    uint32_t x_kinds = 0;          // input activation kinds gate/up need (bit 0 Q8_K, bit 1 Q8_0)
+    const void *fused_plan = nullptr;   // the persistent kernel's plan when it can serve this layer
+    int dt_gu = -1, dt_dn = -1;         // uniform gate/up and down dtypes of the layer (or -1)
     bool has_shared = false;
     int sh_dt[3] = { 0, 0, 0 };
     void *sh_w[3] = { nullptr, nullptr, nullptr };
@@ -95,10 +95,13 @@ struct tlmg_ctx {
     FusedScratch fused;
     bool fused_on = true;
     uint64_t *trace = nullptr;     // device [nsm][FUSED_TRACE_POINTS] when tracing
+    Slot *slots_all = nullptr;     // device [n_layers][E]: every layer's slot table, contiguous
+    uint8_t *mask_all = nullptr;   // device [n_layers][E] (zero-filled) once any layer has a mask
+    float *bias_all = nullptr;     // device [n_layers][E] (zero-filled) once any layer has a router bias
     // per-launch event timing (tlmg_profile)
     bool prof = false;
     std::vector<cudaEvent_t> ev_pool;
-    struct Mark { int cls; cudaEvent_t a, b; };
+    struct Mark { int cls; cudaEvent_t a, b; int64_t bytes; };
     std::vector<Mark> marks;
     int64_t prof_bytes[3] = { 0, 0, 0 };
 };
@@ -141,21 +144,18 @@ static int sync_slots(tlmg_ctx *c, Layer &Ly) {
                                cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "slot table upload");
     Ly.slots_dirty = false;
-    // which kernels can serve the layer: the distinct dtypes of its experts
-    int gu[8], dn[8], ngu = 0, ndn = 0;
-    bool all = true;
-    Ly.x_kinds = 0;
+    // the persistent kernel serves layers whose experts all share one
+    // gate/up dtype and one down dtype
+    int dgu = -1, ddn = -1;
+    bool uniform = true;
     for (const Slot &sl : Ly.h_slots) {
-        if (!sl.ok) { all = false; continue; }
-        for (int m = 0; m < 3; m++) {
-            int *arr = m < 2 ? gu : dn, &n = m < 2 ? ngu : ndn;
-            bool seen = false;
-            for (int i = 0; i < n; i++) seen |= arr[i] == sl.dt[m];
-            if (!seen && n < 8) arr[n++] = sl.dt[m];
-            if (m < 2) Ly.x_kinds |= act_kind_for(sl.dt[m]) == DT_Q8_0 ? 2u : 1u;
-        }
+        if (!sl.ok) { uniform = false; break; }
+        if (dgu < 0) { dgu = sl.dt[0]; ddn = sl.dt[2]; }
+        if (sl.dt[0] != dgu || sl.dt[1] != dgu || sl.dt[2] != ddn) uniform = false;
     }
-    Ly.fused_ok = all && fused_supports(c->fused, c->g, gu, ngu, dn, ndn);
+    Ly.dt_gu = uniform ? dgu : -1;
+    Ly.dt_dn = uniform ? ddn : -1;
+    Ly.fused_plan = uniform ? fused_plan(c->fused, c->g, dgu, ddn) : nullptr;
     return TLMG_OK;
 }
 
@@ -328,6 +328,12 @@ static int launched(const char *what) {
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, what);
 }
 
+// The persistent kernel runs when enabled, when it has a plan for the
+// layer's dtypes and when x is 16-byte aligned (it reads x as float4).
+static bool use_fused_path(const tlmg_ctx *c, const Layer &Ly, const float *x) {
+    return c->fused_on && Ly.fused_plan && x && ((uintptr_t)x & 15u) == 0;
+}
+
 static cudaEvent_t prof_event(tlmg_ctx *c) {
     cudaEvent_t e = nullptr;
     if (!c->ev_pool.empty()) {
@@ -340,15 +346,15 @@ static cudaEvent_t prof_event(tlmg_ctx *c) {
     return e;
 }
 
-// Bracket one launch of kernel class `cls`: call with begin = true before
-// the launch and false after it.
-static void prof_mark(tlmg_ctx *c, int cls, bool begin) {
+// Bracket one launch of kernel class `cls` that serves n_tok tokens: call
+// with begin = true before the launch and false after it.
+static void prof_mark(tlmg_ctx *c, int cls, bool begin, int n_tok = 1) {
     if (!c->prof) return;
     if (begin) {
         cudaEvent_t a = prof_event(c);
         if (!a) return;
         cudaEventRecord(a, c->st);
-        c->marks.push_back({ cls, a, nullptr });
+        c->marks.push_back({ cls, a, nullptr, c->prof_bytes[cls] * n_tok });
     } else if (!c->marks.empty() && c->marks.back().b == nullptr && c->marks.back().cls == cls) {
         cudaEvent_t b = prof_event(c);
         if (!b) return;
@@ -364,7 +370,7 @@ static void prof_bytes(tlmg_ctx *c, const Layer &Ly) {
     const int64_t D = c->g.d_model, de = c->g.d_expert, k = c->g.top_k;
     int64_t gu = k * de * (int64_t)(tlmg_row_bytes(s.dt[0], D) + tlmg_row_bytes(s.dt[1], D));
     int64_t dn = k * D * (int64_t)tlmg_row_bytes(s.dt[2], de);
-    bool fused = c->fused_on && Ly.fused_ok;
+    bool fused = c->fused_on && Ly.fused_plan;
     c->prof_bytes[0] = fused ? gu + dn : gu;
     c->prof_bytes[1] = dn;
     c->prof_bytes[2] = 4 * (int64_t)c->g.n_experts;
@@ -377,34 +383,47 @@ static int quant_inputs(tlmg_ctx *c, const float *x) {
     return rc;
 }
 
+// Arguments of a persistent-kernel launch of n_tok tokens from `layer`.
+static FusedArgs fused_args(tlmg_ctx *c, const Layer &Ly, int layer, int n_tok) {
+    const tlmg_geom &g = c->g;
+    FusedArgs a{};
+    a.plan = Ly.fused_plan;
+    a.slots_all = c->slots_all;
+    a.mask_all = c->mask_all;
+    a.bias_all = c->bias_all;
+    a.layer0 = layer;
+    a.n_layers = g.n_layers;
+    a.n_tok = n_tok;
+    a.hbuf = c->hbuf;
+    a.D = g.d_model;
+    a.de = g.d_expert;
+    a.E = g.n_experts;
+    a.k = g.top_k;
+    a.router = g.router;
+    a.routed_scale = g.routed_scale;
+    a.dt_gu = Ly.dt_gu;
+    a.dt_dn = Ly.dt_dn;
+    a.trace = c->trace;
+    return a;
+}
+
 // Routed experts for one token on the device: logits -> ids/w -> ffn (and
 // h += ffn when h != NULL). Inputs already quantised in xq8k / xq80.
-static int run_experts(tlmg_ctx *c, Layer &Ly, const float *logits, float *ffn, float *h, const float *s_out,
+static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, float *h, const float *s_out,
                        const float *sgate, const float *x) {
     const tlmg_geom &g = c->g;
+    Layer &Ly = c->L[layer];
     prof_bytes(c, Ly);
-    if (c->fused_on && Ly.fused_ok && x) {
-        FusedArgs a;
-        a.slots = Ly.d_slots;
-        a.logits = logits;
-        a.mask = Ly.mask;
-        a.bias = Ly.router_bias;
+    if (use_fused_path(c, Ly, x)) {
+        FusedArgs a = fused_args(c, Ly, layer, 1);
         a.x = x;
-        a.hbuf = c->hbuf;
+        a.logits = logits;
         a.ffn = ffn;
         a.h = h;
         a.s_out = s_out;
         a.sgate = sgate;
         a.ids_out = c->ids;
         a.w_out = c->w;
-        a.D = g.d_model;
-        a.de = g.d_expert;
-        a.E = g.n_experts;
-        a.k = g.top_k;
-        a.router = g.router;
-        a.routed_scale = g.routed_scale;
-        a.x_kinds = Ly.x_kinds;
-        a.trace = c->trace;
         prof_mark(c, 0, true);
         int rc = launch_fused_ffn(c->fused, a, c->st);
         prof_mark(c, 0, false);
@@ -445,8 +464,8 @@ static int expert_ffn_dev(tlmg_ctx *c, int layer, const float *x, const float *l
     int rc = sync_slots(c, Ly);
     if (rc) return rc;
     if (!layer_ready(c, Ly)) return set_error(TLMG_ENOTFOUND, "layer %d: not every expert slot is loaded", layer);
-    if (!(c->fused_on && Ly.fused_ok) && (rc = quant_inputs(c, x))) return rc;
-    return run_experts(c, Ly, logits, ffn, nullptr, nullptr, nullptr, x);
+    if (!use_fused_path(c, Ly, x) && (rc = quant_inputs(c, x))) return rc;
+    return run_experts(c, layer, logits, ffn, nullptr, nullptr, nullptr, x);
 }
 
 enum PtrKind { PK_DEVICE, PK_PINNED, PK_PAGEABLE };
@@ -529,7 +548,7 @@ int tlmg_open(const tlmg_geom *g, int device, tlmg_ctx **out) {
     size_t xq = std::max(tlmg_qact_bytes(DT_Q8_K, D), tlmg_qact_bytes(DT_Q8_0, D)) + 256;
     bool ok = (c->x = (float *)dalloc(c, 4 * (size_t)D)) && (c->logits = (float *)dalloc(c, 4 * (size_t)E)) &&
               (c->ffn = (float *)dalloc(c, 4 * (size_t)D)) && (c->h = (float *)dalloc(c, 4 * (size_t)D)) &&
-              (c->hbuf = (float *)dalloc(c, 4 * (size_t)k * de)) && (c->xq8k = (uint8_t *)dalloc(c, xq)) &&
+              (c->hbuf = (float *)dalloc(c, 4 * 4 * (size_t)k * de)) && (c->xq8k = (uint8_t *)dalloc(c, xq)) &&
               (c->xq80 = (uint8_t *)dalloc(c, xq)) && (c->hq = (uint8_t *)dalloc(c, c->hq_stride * k)) &&
               (c->ids = (int32_t *)dalloc(c, 4 * 64)) && (c->w = (float *)dalloc(c, 4 * 64)) &&
               (c->sg = (float *)dalloc(c, 8 * (size_t)ds)) && (c->sh = (float *)dalloc(c, 4 * (size_t)ds)) &&
@@ -542,13 +561,15 @@ int tlmg_open(const tlmg_geom *g, int device, tlmg_ctx **out) {
         return set_error(TLMG_ENOMEM, "tlmg_open: device scratch allocation failed");
     }
     c->L.resize(g->n_layers);
-    for (Layer &Ly : c->L) {
+    c->slots_all = (Slot *)dalloc(c, sizeof(Slot) * (size_t)E * g->n_layers);
+    if (!c->slots_all) {
+        tlmg_close(c);
+        return set_error(TLMG_ENOMEM, "tlmg_open: slot table allocation failed");
+    }
+    for (int l = 0; l < g->n_layers; l++) {
+        Layer &Ly = c->L[l];
         Ly.h_slots.assign(E, Slot{ { nullptr, nullptr, nullptr }, { 0, 0, 0 }, 0 });
-        Ly.d_slots = (Slot *)dalloc(c, sizeof(Slot) * E);
-        if (!Ly.d_slots) {
-            tlmg_close(c);
-            return set_error(TLMG_ENOMEM, "tlmg_open: slot table allocation failed");
-        }
+        Ly.d_slots = c->slots_all + (size_t)l * E;
         Ly.slots_dirty = true;
     }
     c->launch0 = launches_total();
@@ -595,18 +616,19 @@ int tlmg_profile_read(tlmg_ctx *c, int cls, double *ms, int64_t *launches, int64
     cudaError_t e = cudaStreamSynchronize(c->st);
     if (e != cudaSuccess) return cuda_fail(e, "profile_read synchronize");
     double tot = 0.0;
-    int64_t n = 0;
+    int64_t n = 0, bytes = 0;
     for (auto &m : c->marks) {
         if (m.cls != cls || !m.b) continue;
         float t = 0.0f;
         if (cudaEventElapsedTime(&t, m.a, m.b) == cudaSuccess) {
             tot += t;
             n++;
+            bytes += m.bytes;
         }
     }
     if (ms) *ms = tot;
     if (launches) *launches = n;
-    if (bytes_per_launch) *bytes_per_launch = c->prof_bytes[cls];
+    if (bytes_per_launch) *bytes_per_launch = n ? bytes / n : 0;
     return TLMG_OK;
 }
 
@@ -727,9 +749,28 @@ int tlmg_set_layer(tlmg_ctx *c, int layer, const float *ffn_norm, int router_dt,
         Ly.router_dt = router_dt;
         Ly.router_rb = router_rb;
     }
-    if (router_bias && !up((void **)&Ly.router_bias, router_bias, 4 * (size_t)E))
-        return set_error(TLMG_EIO, "set_layer: bias upload");
-    if (mask && !up((void **)&Ly.mask, mask, (size_t)E)) return set_error(TLMG_EIO, "set_layer: mask upload");
+    // router bias and expert mask live in [n_layers][E] arrays, zero-filled
+    // for layers that have none (bias 0 and mask 0 leave routing unchanged),
+    // so one launch can serve tokens of different layers
+    const int NL = c->g.n_layers;
+    if (router_bias) {
+        if (!c->bias_all) {
+            if (!(c->bias_all = (float *)dalloc(c, 4 * (size_t)E * NL))) return set_error(TLMG_ENOMEM, "bias table");
+            cudaMemset(c->bias_all, 0, 4 * (size_t)E * NL);
+            for (int l = 0; l < NL; l++) c->L[l].router_bias = c->bias_all + (size_t)l * E;
+        }
+        if (cudaMemcpy(Ly.router_bias, router_bias, 4 * (size_t)E, cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(TLMG_EIO, "set_layer: bias upload");
+    }
+    if (mask) {
+        if (!c->mask_all) {
+            if (!(c->mask_all = (uint8_t *)dalloc(c, (size_t)E * NL))) return set_error(TLMG_ENOMEM, "mask table");
+            cudaMemset(c->mask_all, 0, (size_t)E * NL);
+            for (int l = 0; l < NL; l++) c->L[l].mask = c->mask_all + (size_t)l * E;
+        }
+        if (cudaMemcpy(Ly.mask, mask, (size_t)E, cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(TLMG_EIO, "set_layer: mask upload");
+    }
     return TLMG_OK;
 }
 
@@ -828,9 +869,35 @@ int tlmg_expert_ffn_many(tlmg_ctx *c, int layer0, int n_tok, const float *x, con
         dl = c->mlog;
         df = c->mffn;
     }
-    for (int t = 0; t < n_tok; t++) {
-        int layer = (layer0 + t) % NL;
-        if ((rc = expert_ffn_dev(c, layer, dx + (size_t)t * D, dl + (size_t)t * E, df + (size_t)t * D))) return rc;
+    // one persistent launch for all tokens when every layer involved has the
+    // same kernel plan; otherwise one call per token
+    bool one = c->fused_on && ((uintptr_t)dx & 15u) == 0;
+    const void *plan = nullptr;
+    for (int t = 0; t < n_tok && one; t++) {
+        Layer &Ly = c->L[(layer0 + t) % NL];
+        if ((rc = sync_slots(c, Ly))) return rc;
+        if (!layer_ready(c, Ly)) return set_error(TLMG_ENOTFOUND, "layer %d: not every expert slot is loaded",
+                                                  (layer0 + t) % NL);
+        if (!Ly.fused_plan || (plan && Ly.fused_plan != plan)) one = false;
+        plan = Ly.fused_plan;
+    }
+    if (one && n_tok > 1) {
+        Layer &L0 = c->L[layer0];
+        prof_bytes(c, L0);
+        FusedArgs a = fused_args(c, L0, layer0, n_tok);
+        a.x = dx;
+        a.logits = dl;
+        a.ffn = df;
+        prof_mark(c, 0, true, n_tok);
+        rc = launch_fused_ffn(c->fused, a, c->st);
+        prof_mark(c, 0, false);
+        if (rc) return rc;
+    } else {
+        for (int t = 0; t < n_tok; t++) {
+            int layer = (layer0 + t) % NL;
+            if ((rc = expert_ffn_dev(c, layer, dx + (size_t)t * D, dl + (size_t)t * E, df + (size_t)t * D)))
+                return rc;
+        }
     }
     if (kx != PK_DEVICE) {
         size_t off = 4 * (size_t)n_tok * (D + E);
@@ -894,7 +961,7 @@ int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
         int kr = act_kind_for(Ly.router_dt);
         const void *ract = kr == DT_F32 ? (const void *)c->x : kr == DT_Q8_0 ? (const void *)c->xq80 : (const void *)c->xq8k;
         if ((rc = launch_matvec(Ly.router_dt, Ly.router_w, Ly.router_rb, ract, c->logits, D, 0, E, c->st))) return rc;
-        if ((rc = run_experts(c, Ly, c->logits, c->ffn, dh, s_out, sgate, c->x))) return rc;
+        if ((rc = run_experts(c, layer, c->logits, c->ffn, dh, s_out, sgate, c->x))) return rc;
     } else if (s_out) {
         // no routed experts: ffn = sgate * s_out, h += ffn
         k_ffn_down<<<(unsigned)((D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, c->st>>>(
