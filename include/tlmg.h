@@ -174,12 +174,24 @@ int tlmg_check(tlmg_ctx *ctx);
 
 /* Phase trace of the persistent kernel (the reference's per-step stats,
  * src/lib/tlm_model.h:263-266, at kernel granularity): with on = 1 every
- * launch records per CTA 16 u64 values: %globaltimer ns at start, routed,
- * gate/up done, fenced, arrived, barrier passed, h quantised, end, then the
- * consumer warps' summed ns waiting for / computing gate/up chunks and
- * waiting for / computing down chunks. Copies up to `cap` values of the
- * last launch ([CTA][16]) to `out` (host) and returns how many; on = 0 stops
- * tracing. */
+ * launch records per CTA TLMG_TRACE_POINTS u64 values, %globaltimer ns
+ * unless noted, for the launch's token n_tok / 2:
+ *   [0] launch start            [1] token routed
+ *   [2] gate/up phase entered   [3] x arrived     [4] x quantised
+ *   [5] first gate/up chunk in  [6] last gate/up chunk in
+ *   [7] gate/up rows done       [8] barrier arrival
+ *   [9] down phase entered      [10] barrier passed [11] h quantised
+ *   [12] first down chunk in    [13] last down chunk in
+ *   [14] down rows done         [15] combined
+ *   [16..19] consumer warps' summed ns over all tokens: waiting for gate/up
+ *            chunks, in the gate/up chunk loop, waiting for down chunks, in
+ *            the down chunk loop
+ *   [20] launch end
+ *   [21] x copy issued  [22] / [23] first / last gate/up chunk issued
+ *   [24] / [25] first / last down chunk issued
+ * Copies up to `cap` values of the last launch ([CTA][TLMG_TRACE_POINTS]) to
+ * `out` (host) and returns how many; on = 0 stops tracing. */
+#define TLMG_TRACE_POINTS 32
 int tlmg_trace(tlmg_ctx *ctx, int on, uint64_t *out, int cap);
 
 /* Per-launch timing of the expert-FFN kernels with CUDA events recorded on

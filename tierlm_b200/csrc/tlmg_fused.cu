@@ -42,8 +42,8 @@
 
 namespace tlmg {
 
-constexpr int NCW = 16;                 // consumer warps
-constexpr int NTHREADS = 32 * (NCW + 1);
+constexpr int NCW = 16;                 // consumer warps; warp NCW streams, warp NCW + 1 routes
+constexpr int NTHREADS = 32 * (NCW + 2);
 constexpr int MAXCH = FUSED_MAXCH;
 constexpr int MAXK = 16;
 constexpr int SLOT_BYTES = 24576;
@@ -144,151 +144,179 @@ __device__ __forceinline__ float h2f(uint32_t bits) {
 }
 
 // ---------------------------------------------------------------------------
-// One "unit" = 64 elements of one 256-element block (quarter q = 0..3).
-// The activation of a unit, in registers.
-struct UAct {
-    uint32_t c[16];   // 64 int8 codes in the order the weight dtype consumes them
-    int bs[4];        // the activation group sums the unit's min / offset terms need
-    float d;          // activation block scale
-};
-
 // Q8_K activation blocks in shared memory, bank-swizzled: the 16-byte
 // piece p (codes 16p .. 16p+15) of block beta of an NB-block vector lives at
 // codes + (p * NB + beta) * 16, so lanes that read the same piece of
-// consecutive blocks hit consecutive banks. bsums[16] and d per block
-// separately.
+// consecutive blocks hit consecutive banks. bsums[16] (32 bytes, 16-aligned)
+// and d per block separately.
 __device__ __forceinline__ const uint8_t *swz(const uint8_t *codes, int NB, int beta, int p) {
     return codes + ((size_t)p * NB + beta) * 16;
 }
-// The activation of unit (block beta, quarter q) in the order the weight
-// dtype consumes it. Q4_K / Q5_K quarter q: elements 64q .. 64q+63
-// (sub-blocks 2q, 2q+1). Q6_K quarter q = (h = q/2, lq = q%2): elements
-// 128h + 32m + 16lq + 0..15, m = 0..3 (groups 8h + 2m + lq), matching the
-// ql/qh layout (reference tlm_quant.c:406-411).
-template <int DT>
-__device__ __forceinline__ void load_uact(const uint8_t *codes, int NB, int beta, const int16_t *bs, float d, int q,
-                                          UAct &a) {
-    if constexpr (DT == DT_Q6_K) {
-        const int h = q >> 1, lq = q & 1;
-#pragma unroll
-        for (int m = 0; m < 4; m++) {
-            uint4 v = lds128(swz(codes, NB, beta, 8 * h + 2 * m + lq));
-            a.c[4 * m + 0] = v.x; a.c[4 * m + 1] = v.y; a.c[4 * m + 2] = v.z; a.c[4 * m + 3] = v.w;
-            a.bs[m] = bs[8 * h + 2 * m + lq];
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            uint4 v = lds128(swz(codes, NB, beta, 4 * q + i));
-            a.c[4 * i + 0] = v.x; a.c[4 * i + 1] = v.y; a.c[4 * i + 2] = v.z; a.c[4 * i + 3] = v.w;
-        }
-        a.bs[0] = (int)bs[4 * q] + (int)bs[4 * q + 1];
-        a.bs[1] = (int)bs[4 * q + 2] + (int)bs[4 * q + 3];
-        a.bs[2] = a.bs[3] = 0;
-    }
-    a.d = d;
+struct XBlk {
+    const uint8_t *codes;
+    int NB, beta;
+    const int16_t *bs;
+    float d;
+};
+__device__ __forceinline__ uint4 xpiece(const XBlk &x, int p) { return lds128(swz(x.codes, x.NB, x.beta, p)); }
+__device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+// unsigned bytes of a times signed bytes of b, plus c
+__device__ __forceinline__ int dp4us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
+// the sum of the two signed 16-bit halves of w
+__device__ __forceinline__ int hsum16(uint32_t w) { return __dp2a_lo((int)w, 0x0101, 0); }
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int i) { return (w >> (8 * i)) & 0xFFu; }
 
-// Exact int32 partials of one unit of a weight block in shared memory, and
-// the block's float factors (used from the lane that owns quarter 0).
-template <int DT>
-__device__ __forceinline__ void unit_dot(const uint8_t *blk, int q, const UAct &a, int &is, int &ms, float &dA,
-                                         float &dM) {
-    if constexpr (DT == DT_Q4_K || DT == DT_Q5_K) {
-        const uint4 hd = lds128(blk);
-        uint32_t qw[8], hw[8];
-        const int qoff = DT == DT_Q4_K ? 16 : 48;
-        uint4 v0 = lds128(blk + qoff + 32 * q), v1 = lds128(blk + qoff + 16 + 32 * q);
-        qw[0] = v0.x; qw[1] = v0.y; qw[2] = v0.z; qw[3] = v0.w;
-        qw[4] = v1.x; qw[5] = v1.y; qw[6] = v1.z; qw[7] = v1.w;
-        if constexpr (DT == DT_Q5_K) {
-            uint4 h0 = lds128(blk + 16), h1 = lds128(blk + 32);
-            hw[0] = h0.x; hw[1] = h0.y; hw[2] = h0.z; hw[3] = h0.w;
-            hw[4] = h1.x; hw[5] = h1.y; hw[6] = h1.z; hw[7] = h1.w;
-        }
-        int lo = 0, hi = 0;
-#pragma unroll
-        for (int w = 0; w < 8; w++) {
-            uint32_t l4 = qw[w] & 0x0F0F0F0Fu, h4 = (qw[w] >> 4) & 0x0F0F0F0Fu;
-            if constexpr (DT == DT_Q5_K) {
-                l4 |= ((hw[w] >> (2 * q)) & 0x01010101u) << 4;
-                h4 |= ((hw[w] >> (2 * q + 1)) & 0x01010101u) << 4;
-            }
-            lo = dp4(l4, a.c[w], lo);
-            hi = dp4(h4, a.c[8 + w], hi);
-        }
-        int sc0, mn0, sc1, mn1;
-        kq_scale_min(hd.y, hd.z, hd.w, 2 * q, sc0, mn0);
-        kq_scale_min(hd.y, hd.z, hd.w, 2 * q + 1, sc1, mn1);
-        is = sc0 * lo + sc1 * hi;
-        ms = mn0 * a.bs[0] + mn1 * a.bs[1];
-        dA = __fmul_rn(h2f(hd.x & 0xFFFFu), a.d);
-        dM = __fmul_rn(h2f(hd.x >> 16), a.d);
-    } else {   // Q6_K: 2-byte aligned blocks
-        const int h = q >> 1, lq = q & 1;
-        const uint4 A = lds128_a2(blk + 64 * h + 16 * lq), B = lds128_a2(blk + 64 * h + 32 + 16 * lq);
-        const uint4 Cq = lds128_a2(blk + 128 + 32 * h + 16 * lq);
-        const uint32_t aw[4] = { A.x, A.y, A.z, A.w }, bw[4] = { B.x, B.y, B.z, B.w },
-                       cw[4] = { Cq.x, Cq.y, Cq.z, Cq.w };
-        int g0 = 0, g1 = 0, g2 = 0, g3 = 0;
-#pragma unroll
-        for (int w = 0; w < 4; w++) {
-            uint32_t u0 = (aw[w] & 0x0F0F0F0Fu) | ((cw[w] & 0x03030303u) << 4);
-            uint32_t u1 = (bw[w] & 0x0F0F0F0Fu) | (((cw[w] >> 2) & 0x03030303u) << 4);
-            uint32_t u2 = ((aw[w] >> 4) & 0x0F0F0F0Fu) | (((cw[w] >> 4) & 0x03030303u) << 4);
-            uint32_t u3 = ((bw[w] >> 4) & 0x0F0F0F0Fu) | (((cw[w] >> 6) & 0x03030303u) << 4);
-            g0 = dp4(u0, a.c[w], g0);
-            g1 = dp4(u1, a.c[4 + w], g1);
-            g2 = dp4(u2, a.c[8 + w], g2);
-            g3 = dp4(u3, a.c[12 + w], g3);
-        }
-        const uint32_t s0 = lds32_a2(blk + 192 + 8 * h), s1 = lds32_a2(blk + 196 + 8 * h);
-        // group 8h + 2m + lq: scale byte 2m + lq of the half's 8 scales
-        is = sbyte(s0, lq) * (g0 - 32 * a.bs[0]) + sbyte(s0, 2 + lq) * (g1 - 32 * a.bs[1]) +
-             sbyte(s1, lq) * (g2 - 32 * a.bs[2]) + sbyte(s1, 2 + lq) * (g3 - 32 * a.bs[3]);
-        ms = 0;
-        dA = __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(blk + 208)), a.d);
-        dM = 0.0f;
-    }
-}
-
-// Exact int32 partials of a whole block (four quarters) of a weight block in
-// shared memory against activation block beta, and its float factors.
+// Exact int32 partials (is = sum_j scale_j * dot_j, ms = sum_j min_j * bsum_j)
+// and the float factors (dA = d_w * d_a, dM = dmin_w * d_a) of NM weight
+// blocks of one K-quant dtype against one activation block (the reference's
+// per-block integer sums, tlm_quant.c:253-296 for Q4_K / Q5_K, :392-420 for
+// Q6_K). Each activation piece is loaded once for all NM weight blocks.
 struct BlockSum {
     int is, ms;
     float dA, dM;
 };
-template <int DT>
-__device__ __forceinline__ void block_dot(const uint8_t *blk, const uint8_t *codes, int NB, int beta,
-                                          const int16_t *bs, float d, BlockSum &o) {
-    o.is = o.ms = 0;
+
+// Q4_K (144 B: d, dmin, scales[12], qs[128]) / Q5_K (176 B: + qh[32] before
+// qs). Blocks are 16-byte aligned in the stage. Sub-block j's 6-bit scale /
+// min are bytes of sc03 / mn03 (j < 4) and sc47 / mn47 (j >= 4) (reference
+// tlm_quant.c:253-261). Quarter q holds sub-blocks 2q (low nibbles) and
+// 2q+1 (high nibbles) of qs[32q ..].
+template <int DT, int NM>
+__device__ __forceinline__ void kblock_dot_k45(const uint8_t *const (&w)[NM], const XBlk &x, BlockSum (&o)[NM]) {
+    constexpr int QOFF = DT == DT_Q4_K ? 16 : 48;
+    uint32_t sc03[NM], sc47[NM];
+    {
+        const uint4 b0 = lds128(reinterpret_cast<const uint8_t *>(x.bs)),
+                    b1 = lds128(reinterpret_cast<const uint8_t *>(x.bs) + 16);
+        const int bs0 = hsum16(b0.x), bs1 = hsum16(b0.y), bs2 = hsum16(b0.z), bs3 = hsum16(b0.w);
+        const int bs4 = hsum16(b1.x), bs5 = hsum16(b1.y), bs6 = hsum16(b1.z), bs7 = hsum16(b1.w);
 #pragma unroll
+        for (int m = 0; m < NM; m++) {
+            const uint4 h = lds128(w[m]);
+            sc03[m] = h.y & 0x3F3F3F3Fu;
+            sc47[m] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+            const uint32_t mn03 = h.z & 0x3F3F3F3Fu;
+            const uint32_t mn47 = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+            o[m].dA = __fmul_rn(h2f(h.x & 0xFFFFu), x.d);
+            o[m].dM = __fmul_rn(h2f(h.x >> 16), x.d);
+            o[m].is = 0;
+            o[m].ms = (int)byte_of(mn03, 0) * bs0 + (int)byte_of(mn03, 1) * bs1 + (int)byte_of(mn03, 2) * bs2 +
+                      (int)byte_of(mn03, 3) * bs3 + (int)byte_of(mn47, 0) * bs4 + (int)byte_of(mn47, 1) * bs5 +
+                      (int)byte_of(mn47, 2) * bs6 + (int)byte_of(mn47, 3) * bs7;
+        }
+    }
+#pragma unroll 1
     for (int q = 0; q < 4; q++) {
-        UAct xa;
-        load_uact<DT>(codes, NB, beta, bs, d, q, xa);
-        int is, ms;
-        unit_dot<DT>(blk, q, xa, is, ms, o.dA, o.dM);
-        o.is += is;
-        o.ms += ms;
+        const uint4 xl0 = xpiece(x, 4 * q), xl1 = xpiece(x, 4 * q + 1);       // sub-block 2q
+        const uint4 xh0 = xpiece(x, 4 * q + 2), xh1 = xpiece(x, 4 * q + 3);   // sub-block 2q+1
+#pragma unroll
+        for (int m = 0; m < NM; m++) {
+            const uint4 v0 = lds128(w[m] + QOFF + 32 * q), v1 = lds128(w[m] + QOFF + 32 * q + 16);
+            uint4 g0 = make_uint4(0u, 0u, 0u, 0u), g1 = g0;
+            if constexpr (DT == DT_Q5_K) {
+                g0 = lds128(w[m] + 16);
+                g1 = lds128(w[m] + 32);
+            }
+            int lo = 0, hi = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t qw = wsel(i < 4 ? v0 : v1, i & 3);
+                const uint32_t xlw = wsel(i < 4 ? xl0 : xl1, i & 3), xhw = wsel(i < 4 ? xh0 : xh1, i & 3);
+                if constexpr (DT == DT_Q4_K) {
+                    lo = dp4(qw & 0x0F0F0F0Fu, xlw, lo);
+                    hi = dp4us(qw & 0xF0F0F0F0u, xhw, hi);   // 16 x the high-nibble dot
+                } else {
+                    const uint32_t hw = wsel(i < 4 ? g0 : g1, i & 3);
+                    const uint32_t l5 = (qw & 0x0F0F0F0Fu) | (((hw >> (2 * q)) & 0x01010101u) << 4);
+                    const uint32_t h5 = ((qw >> 4) & 0x0F0F0F0Fu) | (((hw >> (2 * q + 1)) & 0x01010101u) << 4);
+                    lo = dp4(l5, xlw, lo);
+                    hi = dp4(h5, xhw, hi);
+                }
+            }
+            if constexpr (DT == DT_Q4_K) hi >>= 4;   // exact: the sum is a multiple of 16
+            const uint32_t sw = q < 2 ? sc03[m] : sc47[m];
+            o[m].is += (int)((sw >> (16 * (q & 1))) & 0xFFu) * lo + (int)((sw >> (16 * (q & 1) + 8)) & 0xFFu) * hi;
+        }
     }
 }
-// The same for two weight blocks (gate and up) against one activation block.
-template <int DT>
-__device__ __forceinline__ void block_dot2(const uint8_t *g, const uint8_t *u, const uint8_t *codes, int NB, int beta,
-                                           const int16_t *bs, float d, BlockSum &og, BlockSum &ou) {
-    og.is = og.ms = ou.is = ou.ms = 0;
+
+// Q6_K (210 B: ql[128], qh[64], int8 scales[16], f16 d) at a 2-byte aligned
+// stage address: the block's words are read 4-byte aligned and realigned
+// with funnel shifts. Half h, element l + 32m (l = 0..31, m = 0..3):
+// q = ((ql[64h + l + 32(m&1)] >> 4(m>>1)) & 15) | (((qh[32h + l] >> 2m) & 3) << 4),
+// minus 32 (applied through the group's activation sum), in group
+// 8h + 2m + l/16 with scale scales[8h + 2m + l/16] (reference
+// tlm_quant.c:392-420).
+template <int NM>
+__device__ __forceinline__ void kblock_dot_q6(const uint8_t *const (&w)[NM], const XBlk &x, BlockSum (&o)[NM]) {
+    int bsg[16];
+    {
+        const uint4 b0 = lds128(reinterpret_cast<const uint8_t *>(x.bs)),
+                    b1 = lds128(reinterpret_cast<const uint8_t *>(x.bs) + 16);
+        const uint32_t bw[8] = { b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w };
 #pragma unroll
-    for (int q = 0; q < 4; q++) {
-        UAct xa;
-        load_uact<DT>(codes, NB, beta, bs, d, q, xa);
-        int is, ms;
-        unit_dot<DT>(g, q, xa, is, ms, og.dA, og.dM);
-        og.is += is;
-        og.ms += ms;
-        unit_dot<DT>(u, q, xa, is, ms, ou.dA, ou.dM);
-        ou.is += is;
-        ou.ms += ms;
+        for (int i = 0; i < 8; i++) {
+            bsg[2 * i] = (int)(int16_t)(bw[i] & 0xFFFFu);
+            bsg[2 * i + 1] = (int)(int16_t)(bw[i] >> 16);
+        }
     }
+#pragma unroll
+    for (int m = 0; m < NM; m++) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(w[m]);
+        const uint32_t *wp = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(a & 3u) * 8u;   // 0 or 16
+        int is = 0;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            int dot[8];   // group 8h + 2mm + p at index 2mm + p
+#pragma unroll
+            for (int i = 0; i < 8; i++) dot[i] = 0;
+#pragma unroll
+            for (int p = 0; p < 2; p++) {   // l = 16p .. 16p+15
+                uint4 xv[4];
+#pragma unroll
+                for (int mm = 0; mm < 4; mm++) xv[mm] = xpiece(x, 8 * h + 2 * mm + p);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int lw = 4 * p + i;
+                    const int ja = 16 * h + lw, jb = 16 * h + 8 + lw, jc = 32 + 8 * h + lw;
+                    const uint32_t A = __funnelshift_r(wp[ja], wp[ja + 1], sh);
+                    const uint32_t B = __funnelshift_r(wp[jb], wp[jb + 1], sh);
+                    const uint32_t Cq = __funnelshift_r(wp[jc], wp[jc + 1], sh);
+                    const uint32_t u0 = (A & 0x0F0F0F0Fu) | ((Cq << 4) & 0x30303030u);
+                    const uint32_t u1 = (B & 0x0F0F0F0Fu) | ((Cq << 2) & 0x30303030u);
+                    const uint32_t u2 = ((A >> 4) & 0x0F0F0F0Fu) | (Cq & 0x30303030u);
+                    const uint32_t u3 = ((B >> 4) & 0x0F0F0F0Fu) | ((Cq >> 2) & 0x30303030u);
+                    dot[0 + p] = dp4(u0, wsel(xv[0], i), dot[0 + p]);
+                    dot[2 + p] = dp4(u1, wsel(xv[1], i), dot[2 + p]);
+                    dot[4 + p] = dp4(u2, wsel(xv[2], i), dot[4 + p]);
+                    dot[6 + p] = dp4(u3, wsel(xv[3], i), dot[6 + p]);
+                }
+            }
+            // scales 8h .. 8h+7 (bytes 192 + 8h ..)
+            const uint32_t s0 = __funnelshift_r(wp[48 + 2 * h], wp[49 + 2 * h], sh);
+            const uint32_t s1 = __funnelshift_r(wp[49 + 2 * h], wp[50 + 2 * h], sh);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int sc = (int)(int8_t)byte_of(i < 4 ? s0 : s1, i & 3);
+                is += sc * (dot[i] - 32 * bsg[8 * h + i]);
+            }
+        }
+        o[m].is = is;
+        o[m].ms = 0;
+        o[m].dA = __fmul_rn(h2f(__funnelshift_r(wp[52], wp[53], sh) & 0xFFFFu), x.d);
+        o[m].dM = 0.0f;
+    }
+}
+
+template <int DT, int NM>
+__device__ __forceinline__ void kblock_dot(const uint8_t *const (&w)[NM], const XBlk &x, BlockSum (&o)[NM]) {
+    if constexpr (DT == DT_Q6_K) kblock_dot_q6<NM>(w, x, o);
+    else kblock_dot_k45<DT, NM>(w, x, o);
 }
 
 // One block's step of the reference's fmaf chain.
@@ -331,34 +359,63 @@ __device__ __forceinline__ void warp_quant_swz(const float4 &a, const float4 &b,
 }
 
 // ---------------------------------------------------------------------------
-// shared-memory layout
-constexpr int NBUF = 4;   // routing / h buffers, by token % NBUF
-struct SmemLayout {
-    uint32_t stage, full, empty, xfull, xempty, idsfree, xs, xc, xd, xbs, hc, hd, hbs, p, ids, w, desc, sl, misc, total;
-};
+// Quantised activation vectors (the x of a token, the h of a token): nb
+// Q8_K blocks as codes[256 nb] (swizzled), bsums[16 nb], d[nb], each part
+// 16-byte aligned. The layout is the same in global and in shared memory,
+// so one bulk copy moves a vector.
 __host__ __device__ inline uint32_t up16(uint32_t v) { return (v + 15u) & ~15u; }
+__host__ __device__ inline uint32_t qv_bsums(int nb) { return 256u * (uint32_t)nb; }
+__host__ __device__ inline uint32_t qv_d(int nb) { return qv_bsums(nb) + 32u * (uint32_t)nb; }
+__host__ __device__ inline uint32_t qv_bytes(int nb) { return qv_d(nb) + up16(4u * (uint32_t)nb); }
+struct QVec {
+    uint8_t *codes;
+    int16_t *bs;
+    float *d;
+    int nb;
+};
+__device__ __forceinline__ QVec qvec(uint8_t *base, int nb) {
+    return QVec{ base, reinterpret_cast<int16_t *>(base + qv_bsums(nb)), reinterpret_cast<float *>(base + qv_d(nb)),
+                 nb };
+}
+// A full warp quantises block b of a vector (this lane's 8 inputs, elements
+// 8*lane ..) into q.
+__device__ __forceinline__ void quant_block(const float4 &v0, const float4 &v1, const QVec &q, int b, int lane) {
+    warp_quant_swz(v0, v1, q.codes, q.nb, b, q.bs + 16 * b, q.d + b, lane);
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory layout
+constexpr int NBUF = 4;   // routing buffers, by token % NBUF
+struct SmemLayout {
+    uint32_t stage, full, empty, seq, done, xs, xfull, xfree, xseq, hs, hfull, hfree, hseq, routed, idsfree, ids, w, sl,
+        rscr, cnt, desc, ipre, misc, total;
+};
 __host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nslot) {
     SmemLayout L;
     uint32_t o = 0;
-    const uint32_t nbx = (uint32_t)(D / 256), nbh = (uint32_t)(k * (de / 256));
+    const int nbx = D / 256, nbh = k * (de / 256);
     L.stage = o; o += (uint32_t)nslot * SLOT_BYTES;
     L.full = o; o += 8u * nslot;
     L.empty = o; o += 8u * nslot;
-    L.xfull = o; o += 8u;
-    L.xempty = o; o += 8u;
+    L.seq = o; o += 4u * nslot;
+    L.done = o = (o + 7u) & ~7u; o += 4u * nslot;
+    L.xfull = o = (o + 7u) & ~7u; o += 16u;
+    L.xfree = o; o += 16u;
+    L.hfull = o; o += 16u;
+    L.hfree = o; o += 16u;
+    L.routed = o; o += 8u * NBUF;
     L.idsfree = o; o += 8u * NBUF;
-    L.xs = o = up16(o); o += 4u * (uint32_t)D;
-    L.xc = o = up16(o); o += 256u * nbx;
-    L.xd = o; o += 4u * nbx;
-    L.xbs = o = up16(o); o += 32u * nbx;
-    L.hc = o = up16(o); o += 256u * nbh;
-    L.hd = o; o += 4u * nbh;
-    L.hbs = o = up16(o); o += 32u * nbh;
-    L.p = o = up16(o); o += 4u * (uint32_t)RT_SCRATCH;
+    L.xseq = o; o += 8u;
+    L.hseq = o; o += 8u;
+    L.xs = o = up16(o); o += 2u * qv_bytes(nbx);
+    L.hs = o = up16(o); o += 2u * qv_bytes(nbh);
+    L.rscr = o = up16(o); o += 4u * (uint32_t)RT_SCRATCH;
     L.ids = o; o += 4u * 64 * NBUF;
     L.w = o; o += 4u * 64 * NBUF;
+    L.sl = o = up16(o); o += (uint32_t)sizeof(Slot) * MAXK * NBUF;
+    L.cnt = o = up16(o); o += 4u * 2 * NBUF;
     L.desc = o = up16(o); o += (uint32_t)sizeof(ChunkDesc) * MAXCH;
-    L.sl = o = up16(o); o += (uint32_t)sizeof(Slot) * MAXK * 2;
+    L.ipre = o; o += 4u * (MAXCH + 2);
     L.misc = o = up16(o); o += 64;
     L.total = o;
     return L;
@@ -366,8 +423,7 @@ __host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nslo
 
 // The launch's schedule, shared by the producer and the consumers: step j
 // of 2 * n_tok is phase A (gate/up) or phase B (down + combine) of a token,
-// in the order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1). Phase A of
-// the next token runs while the grid barrier of the current one settles.
+// in the order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1).
 __device__ __forceinline__ void step_of(int j, int n, int &tok, bool &isA) {
     if (j == 0) { tok = 0; isA = true; }
     else if ((j & 1) && ((j + 1) >> 1) < n) { tok = (j + 1) >> 1; isA = true; }
@@ -377,361 +433,322 @@ __device__ __forceinline__ void step_of(int j, int n, int &tok, bool &isA) {
 
 // Grid barriers: token number gt (counted since the host last reset the
 // words; a launch's token t is gt = bar_base + t) uses the 64-bit arrival
-// word gt % NBUF at bar + 4, which every CTA increments once per token, so
-// barrier gt is complete at (gt / NBUF + 1) * gridDim.x arrivals. A CTA
-// arrives for token gt + 1 before it waits for gt (phase A of the next
-// token runs first), but it cannot arrive for gt + NBUF before every CTA
-// has passed barrier gt + 2 and so arrived for gt: one word per token in
-// flight keeps the counts exact.
+// word gt % NBUF at bar + 4, which every CTA increments once per token when
+// its gate/up rows of the token are written, so barrier gt is complete at
+// (gt / NBUF + 1) * gridDim.x arrivals. A CTA arrives for token gt + NBUF
+// only after its router released the routing buffer of token gt, i.e.
+// after its down phase of token gt, which follows barrier gt: one word per
+// token in flight keeps the counts exact. The word at bar + 12 counts the
+// CTAs that quantised their share of the launch's inputs.
 __device__ __forceinline__ unsigned long long *barrier_word(uint32_t *bar, uint64_t gt) {
     return reinterpret_cast<unsigned long long *>(bar + 4) + (gt % NBUF);
 }
+__device__ __forceinline__ unsigned long long *xbar_word(uint32_t *bar) {
+    return reinterpret_cast<unsigned long long *>(bar + 12);
+}
+// Wait until *w >= target, for at most BARRIER_NS.
+__device__ __forceinline__ bool grid_wait(const unsigned long long *w, uint64_t target) {
+    if (ld_acquire64(w) >= target) return true;
+    const uint64_t t0 = now_ns();
+    while (ld_acquire64(w) < target)
+        if (now_ns() - t0 > BARRIER_NS) return false;
+    return true;
+}
+// Wait until the shared word *p equals v (the producer publishes which
+// chunk / token a buffer holds before its mbarrier phase can complete), for
+// at most WAIT_NS.
+__device__ __forceinline__ bool seq_wait(const uint32_t *p, uint32_t v) {
+    const volatile uint32_t *q = p;
+    if (*q == v) return true;
+    const uint64_t t0 = now_ns();
+    while (*q != v)
+        if (now_ns() - t0 > WAIT_NS) return false;
+    return true;
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
-// Consumer state carried from step to step.
-enum : uint32_t { ST_ABORT = 1u, ST_DEAD = 2u };   // results invalid / stop waiting on copies
+// Consumer state carried from item to item.
+enum : uint32_t { ST_ABORT = 1u, ST_DEAD = 2u };   // results invalid / stop waiting
 
+// The token whose phase boundaries the trace stamps: one in the middle of
+// the launch (steady state).
+__device__ __forceinline__ int trace_tok(const FusedArgs &a) { return a.n_tok / 2; }
 __device__ __forceinline__ uint64_t *trace_row(const FusedArgs &a) {
     return a.trace ? a.trace + (size_t)blockIdx.x * FUSED_TRACE_POINTS : nullptr;
 }
 
-// Phase A of token `tok`: x -> Q8_K, then gate/up + SwiGLU over this CTA's
-// (rank, row) pairs (chunks cc0 .. cc0 + nA - 1 of the ring), h rows to
-// hbuf[tok % NBUF], and this CTA's arrival at the token's grid barrier.
-// Work item = four consecutive (gate, up) row pairs of a chunk; items go
-// round-robin to the warps. Lane (g, lb) = (lane / 8, lane % 8) owns row
-// pair g of the item and blocks lb, lb + 8, ... of both rows (exact int32
-// block partials over the four quarters); lane 8g runs the gate chain and
-// lane 8g + 1 the up chain over the blocks in ascending order, gathering
-// the partials by shuffles. NB8 = blocks per lane (D <= 2048: 1, <= 4096: 2).
-template <int DGU, int NB8>
-__device__ __forceinline__ uint32_t consumer_a(const FusedArgs &a, uint8_t *smem, int nslot, int tok, uint32_t cc0,
-                                               int nA, uint32_t *bar, uint32_t *err, uint32_t st) {
-    const int D = a.D, de = a.de, k = a.k;
-    const SmemLayout L = smem_layout(D, de, k, nslot);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.full);
-    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.empty);
-    uint8_t *xc = smem + L.xc;
-    float *xd = reinterpret_cast<float *>(smem + L.xd);
-    int16_t *xbs = reinterpret_cast<int16_t *>(smem + L.xbs);
-    const ChunkDesc *desc = reinterpret_cast<const ChunkDesc *>(smem + L.desc);
-    uint64_t *tr = trace_row(a);
-    const bool tr0 = tr && tok == 0;
-    const int nbx = D / 256, rbg = nbx * dt_block_bytes(DGU);
-    float *hb = a.hbuf + (size_t)(tok % NBUF) * k * de;
-
-    // x of this token (bulk-copied by the producer) -> Q8_K codes
-    if (!(st & ST_DEAD) && !mbar_wait(reinterpret_cast<uint64_t *>(smem + L.xfull), (uint32_t)tok & 1u)) {
-        st |= ST_DEAD | ST_ABORT;
-        if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
-    }
-    if (warp < nbx) {
-        const float4 *x4 = reinterpret_cast<const float4 *>(smem + L.xs) + 64 * warp + 2 * lane;
-        warp_quant_swz(x4[0], x4[1], xc, nbx, warp, xbs + 16 * warp, xd + warp, lane);
-    }
-    consumer_sync();
-    if (t == 0) mbar_arrive(reinterpret_cast<uint64_t *>(smem + L.xempty));
-
-    const int g = lane >> 3, lb = lane & 7;
-    uint32_t tw = 0, t_in = tr ? (uint32_t)now_ns() : 0u;   // trace: ns waiting for chunks
-    int base = 0;   // first item of chunk c
-    for (int c = 0; c < nA; c++) {
-        const uint32_t cc = cc0 + (uint32_t)c, s = cc % (uint32_t)nslot;
-        const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
-        if (!(st & ST_DEAD) && !mbar_wait(&full[s], (cc / (uint32_t)nslot) & 1u)) {
-            st |= ST_DEAD | ST_ABORT;
-            if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
+// ---------------------------------------------------------------------------
+// One phase-A work item: eight (gate, up) row pairs. Lane (p, j) =
+// (lane / 4, lane % 4) owns row pair p (gate row at grow, up row at urow,
+// valid or not) and blocks j, j + 4, ... of both rows: it computes their
+// exact partials (even row pairs their low block first, odd ones their high
+// block, so that the 8 lanes of a quarter warp read 8 different banks), then
+// the gate and up fmaf chains run over the blocks in ascending order, the
+// lane holding block b applying it and passing the accumulators on by
+// shuffle. Returns silu(gate) * up on every lane of the row pair.
+template <int DGU, int BPL>
+__device__ __forceinline__ float a_item(const uint8_t *grow, const uint8_t *urow, bool valid, const QVec &x, int nbx,
+                                        int lane) {
+    const int j = lane & 3, odd = (lane >> 2) & 1;
+    // rg/ru[ii]: the ii-th block the lane computes; vg/vu[i]: block j + 4i
+    BlockSum rg[BPL], ru[BPL], vg[BPL], vu[BPL];
+#pragma unroll
+    for (int ii = 0; ii < BPL; ii++) {
+        const int i = (BPL == 2 && odd) ? 1 - ii : ii;
+        const int b = j + 4 * i;
+        rg[ii] = BlockSum{ 0, 0, 0.f, 0.f };
+        ru[ii] = rg[ii];
+        if (valid && b < nbx) {
+            const uint8_t *wb[2] = { grow + b * dt_block_bytes(DGU), urow + b * dt_block_bytes(DGU) };
+            BlockSum o2[2];
+            kblock_dot<DGU, 2>(wb, XBlk{ x.codes, nbx, b, x.bs + 16 * b, x.d[b] }, o2);
+            rg[ii] = o2[0];
+            ru[ii] = o2[1];
         }
-        if (tr) tw += (uint32_t)now_ns() - tw0;
-        const ChunkDesc d = desc[c];
-        const int nit = (d.nrows + 3) >> 2;
-        const uint8_t *stg = smem + L.stage + (size_t)s * SLOT_BYTES;
-        if (!(st & ST_ABORT))
-            for (int it = base + (warp - base % NCW + NCW) % NCW; it < base + nit; it += NCW) {
-                const int row = 4 * (it - base) + g;
-                const bool valid = row < d.nrows;
-                const uint8_t *grow = stg + d.dst[0] + d.roff[0] + (size_t)row * rbg;
-                const uint8_t *urow = stg + d.dst[1] + d.roff[1] + (size_t)row * rbg;
-                BlockSum vg[NB8], vu[NB8];
+    }
 #pragma unroll
-                for (int i = 0; i < NB8; i++) {
-                    const int b = lb + 8 * i;
-                    vg[i] = BlockSum{ 0, 0, 0.f, 0.f };
-                    vu[i] = vg[i];
-                    if (valid && b < nbx)
-                        block_dot2<DGU>(grow + b * dt_block_bytes(DGU), urow + b * dt_block_bytes(DGU), xc, nbx, b,
-                                        xbs + 16 * b, xd[b], vg[i], vu[i]);
-                }
-                float ag = 0.0f, au = 0.0f;
+    for (int i = 0; i < BPL; i++) {
+        const bool sw = BPL == 2 && odd;
+        vg[i] = sw ? rg[BPL - 1 - i] : rg[i];
+        vu[i] = sw ? ru[BPL - 1 - i] : ru[i];
+    }
+    float ag = 0.0f, au = 0.0f;
+    const int base = lane & ~3;
 #pragma unroll
-                for (int i = 0; i < NB8; i++)
+    for (int i = 0; i < BPL; i++)
 #pragma unroll
-                    for (int j = 0; j < 8; j++)
-                        if (8 * i + j < nbx) {
-                            ag = chain_from<DGU>(ag, vg[i], (lane & ~7) | j);
-                            au = chain_from<DGU>(au, vu[i], (lane & ~7) | j);
-                        }
-                if (lb == 0 && valid) hb[(size_t)d.rank * de + d.row0 + row] = __fmul_rn(silu_f(ag), au);
+        for (int h = 0; h < 4; h++) {
+            if (h + 4 * i >= nbx) break;
+            if (j == h) {
+                ag = chain<DGU>(ag, vg[i].dA, vg[i].is, vg[i].dM, vg[i].ms);
+                au = chain<DGU>(au, vu[i].dA, vu[i].is, vu[i].dM, vu[i].ms);
             }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        base += nit;
-    }
-    if (tr && lane == 0) {
-        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[8]), (unsigned long long)tw);
-        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[9]), (unsigned long long)((uint32_t)now_ns() - t_in));
-    }
-    // arrive at the token's grid barrier once every warp's h rows are written
-    consumer_sync();
-    if (t == 0) {
-        if (tr0) tr[2] = now_ns();
-        __threadfence();
-        atomicAdd(barrier_word(bar, a.bar_base + (uint64_t)tok), 1ull);
-    }
-    return st;
+            ag = __shfl_sync(0xFFFFFFFFu, ag, base | h);
+            au = __shfl_sync(0xFFFFFFFFu, au, base | h);
+        }
+    return __fmul_rn(silu_f(ag), au);
 }
 
-// Phase B of token `tok`: wait for the token's grid barrier, re-quantise h
-// (k x de, swizzled) into shared memory, then down rows + the rank-ordered
-// combine over chunks cc0 .. cc0 + nB - 1. Work item = one output row of a
-// chunk; items go round-robin to the warps. Lane u (+32) owns unit
-// u = r * nbd + b (expert rank r, block b): the exact block partials over
-// the four quarters; lane r runs expert r's chain over its blocks in
-// ascending order, and lane 0 combines ffn = sum_r w[r] * eo_r in
-// ascending rank. NS = unit slots per lane (k * nbd <= 32 * NS).
-template <int DDN, int NS>
-__device__ __forceinline__ uint32_t consumer_b(const FusedArgs &a, uint8_t *smem, int nslot, int tok, uint32_t cc0,
-                                               int nA, int nB, uint32_t *bar, uint32_t *err, uint32_t st) {
-    const int D = a.D, de = a.de, k = a.k;
-    const SmemLayout L = smem_layout(D, de, k, nslot);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.full);
-    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.empty);
-    uint8_t *hc = smem + L.hc;
-    float *hd = reinterpret_cast<float *>(smem + L.hd);
-    int16_t *hbs = reinterpret_cast<int16_t *>(smem + L.hbs);
-    const ChunkDesc *desc = reinterpret_cast<const ChunkDesc *>(smem + L.desc) + nA;
-    int *misc = reinterpret_cast<int *>(smem + L.misc);
-    uint64_t *tr = trace_row(a);
-    const bool tr0 = tr && tok == 0;
-    const int nbd = de / 256, rbd = nbd * dt_block_bytes(DDN), nbh = k * nbd;
-    const float *hb = a.hbuf + (size_t)(tok % NBUF) * k * de;
-
-    // grid barrier of this token: every CTA has written its h rows
-    if (t == 0) {
-        const uint64_t gt = a.bar_base + (uint64_t)tok;
-        const unsigned long long *arrivals = barrier_word(bar, gt);
-        const uint64_t target = (gt / NBUF + 1u) * gridDim.x;
-        if (ld_acquire64(arrivals) < target) {
-            const uint64_t t0 = now_ns();
-            while (ld_acquire64(arrivals) < target) {
-                if (now_ns() - t0 > BARRIER_NS) {
-                    raise_error(err, bar, FUSED_ERR_BARRIER);
-                    misc[2] = 1;
-                    break;
-                }
-            }
-        }
-        __threadfence();
-        if (tr0) tr[5] = now_ns();
-    }
-    consumer_sync();
-    if (misc[2]) st |= ST_ABORT;
-
-    // re-quantise h for all k experts (each CTA holds the full set); two
-    // blocks per warp have their loads in flight together
-    if (!(st & ST_ABORT)) {
-        for (int b0 = warp; b0 < nbh; b0 += 2 * NCW) {
-            float4 hv[2][2];
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int beta = b0 + j * NCW;
-                if (beta < nbh) {
-                    const float4 *h4 = reinterpret_cast<const float4 *>(hb + (size_t)(beta / nbd) * de +
-                                                                        (size_t)(beta % nbd) * 256 + 8 * lane);
-                    hv[j][0] = __ldcg(h4);
-                    hv[j][1] = __ldcg(h4 + 1);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                const int beta = b0 + j * NCW;
-                if (beta < nbh) warp_quant_swz(hv[j][0], hv[j][1], hc, nbh, beta, hbs + 16 * beta, hd + beta, lane);
-            }
+// One phase-B work item: 32 / k output rows. Lane (g, r) = (lane / k,
+// lane % k) owns row g of the item (rank r's copy of it at row_r0 + r * rs,
+// valid or not) and runs expert r's fmaf chain over its nbd blocks in
+// ascending order; then ffn = sum_r w[r] * eo_r in ascending rank. Returns
+// ffn on the lanes (g, 0) (all lanes take part).
+template <int DDN>
+__device__ __forceinline__ float b_item(const uint8_t *row_r0, uint32_t rs, bool valid, const QVec &h, int nbd, int k,
+                                        const float *wr, int lane) {
+    const int g = lane / k, r = lane - g * k;
+    float eo = 0.0f;
+    if (valid) {
+        const uint8_t *row = row_r0 + (size_t)r * rs;
+        for (int b = 0; b < nbd; b++) {
+            const int beta = r * nbd + b;
+            const uint8_t *wb[1] = { row + b * dt_block_bytes(DDN) };
+            BlockSum o1[1];
+            kblock_dot<DDN, 1>(wb, XBlk{ h.codes, h.nb, beta, h.bs + 16 * beta, h.d[beta] }, o1);
+            eo = chain<DDN>(eo, o1[0].dA, o1[0].is, o1[0].dM, o1[0].ms);
         }
     }
-    consumer_sync();
-    if (tr0 && t == 0) tr[6] = now_ns();
-
-    const float *wr = reinterpret_cast<const float *>(smem + L.w) + 64 * (tok % NBUF);
-    uint32_t tw = 0, t_in = tr ? (uint32_t)now_ns() : 0u;
-    int base = 0;
-    for (int c = 0; c < nB; c++) {
-        const uint32_t cc = cc0 + (uint32_t)c, s = cc % (uint32_t)nslot;
-        const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
-        if (!(st & ST_DEAD) && !mbar_wait(&full[s], (cc / (uint32_t)nslot) & 1u)) {
-            st |= ST_DEAD | ST_ABORT;
-            if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
-        }
-        if (tr) tw += (uint32_t)now_ns() - tw0;
-        const ChunkDesc d = desc[c];
-        const int nit = d.nrows;
-        const uint8_t *stg = smem + L.stage + (size_t)s * SLOT_BYTES;
-        if (!(st & ST_ABORT))
-            for (int it = base + (warp - base % NCW + NCW) % NCW; it < base + nit; it += NCW) {
-                const int row = it - base;
-                BlockSum v[NS];
-#pragma unroll
-                for (int i = 0; i < NS; i++) {
-                    const int u = lane + 32 * i;
-                    v[i] = BlockSum{ 0, 0, 0.f, 0.f };
-                    if (u < nbh) {
-                        const int r = u / nbd, b = u - r * nbd;
-                        block_dot<DDN>(stg + (size_t)r * d.dst[0] + d.roff[0] + (size_t)row * rbd +
-                                           b * dt_block_bytes(DDN),
-                                       hc, nbh, u, hbs + 16 * u, hd[u], v[i]);
-                    }
-                }
-                // expert lane's chain over its blocks (unit lane * nbd + b)
-                float eo = 0.0f;
-                for (int b = 0; b < nbd; b++) {
-                    const int su = (lane < k ? lane : 0) * nbd + b;
-                    if constexpr (NS == 1) {
-                        eo = chain_from<DDN>(eo, v[0], su & 31);
-                    } else {
-                        const float e0 = chain_from<DDN>(eo, v[0], su & 31);
-                        const float e1 = chain_from<DDN>(eo, v[1], su & 31);
-                        eo = (su >> 5) ? e1 : e0;
-                    }
-                }
-                float f = 0.0f;
-                for (int r = 0; r < k; r++) f = __fadd_rn(f, __fmul_rn(wr[r], __shfl_sync(0xFFFFFFFFu, eo, r)));
-                if (lane == 0) {
-                    const int i = (int)d.row0 + row;
-                    if (a.s_out) f = __fadd_rn(f, __fmul_rn(*a.sgate, a.s_out[i]));
-                    a.ffn[(size_t)tok * D + i] = f;
-                    if (a.h) a.h[i] = __fadd_rn(a.h[i], f);
-                }
-            }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        base += nit;
-    }
-    if (tr && lane == 0) {
-        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[10]), (unsigned long long)tw);
-        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[11]), (unsigned long long)((uint32_t)now_ns() - t_in));
-    }
-    consumer_sync();   // the token's routing is no longer read
-    if (t == 0) {
-        mbar_arrive(reinterpret_cast<uint64_t *>(smem + L.idsfree) + (tok % NBUF));
-        if (tr0) tr[7] = now_ns();
-    }
-    return st;
+    const int src0 = g * k < 32 ? g * k : 0;
+    float f = 0.0f;
+    for (int q = 0; q < k; q++) f = __fadd_rn(f, __fmul_rn(wr[q], __shfl_sync(0xFFFFFFFFu, eo, (src0 + q) & 31)));
+    return f;
 }
 
 // ---------------------------------------------------------------------------
-// W: blocks per lane in phase A (D / 256 <= 8 W) and unit slots per lane in
-// phase B (k * de / 256 <= 32 W).
+// The persistent kernel. One CTA per SM: warps 0..NCW-1 consume work items,
+// warp NCW streams (lane 0: x and weight chunks; lane 1: the quantised h of
+// each token once its grid barrier completes), warp NCW + 1 routes.
+//
+//   launch start  every CTA quantises its share of the launch's inputs x
+//                 (n_tok x D / 256 blocks) into a.xq; one grid-wide count.
+//   router        routes token t into buffer t % NBUF once the consumers
+//                 are done with token t - NBUF.
+//   stream        per step of the schedule: the token's quantised x (phase
+//                 A) and the step's chunks of weight rows, in a ring of
+//                 stages; each stage's sequence word names the chunk it is
+//                 armed for.
+//   work items    warp w takes items w, w + NCW, ... of the launch's item
+//                 sequence (the steps' items in schedule order) and waits
+//                 only for what its item reads: the chunk, the token's x or
+//                 h. A stage is released when its chunk's last item is done.
+//   token A done  the warp that finishes a token's last gate/up item of the
+//                 CTA adds the CTA's rows to the counts of the h blocks they
+//                 belong to; the CTA completing a block quantises it into
+//                 a.hq; then the CTA arrives at the token's grid barrier.
+//   token B done  the warp that finishes the token's last down item frees
+//                 the token's h and routing buffers.
+//
+// Every wait is bounded; on expiry the kernel raises an error bit the host
+// reads and stops waiting (results of the launch are invalid).
 template <int DGU, int DDN, int W>
 __global__ void __launch_bounds__(NTHREADS, 1)
 k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict__ err, int nslot) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const SmemLayout L = smem_layout(a.D, a.de, a.k, nslot);
+    const int D = a.D, de = a.de, k = a.k, E = a.E, n = a.n_tok;
+    const int nbx = D / 256, nbd = de / 256, nbh = k * nbd;
+    const SmemLayout L = smem_layout(D, de, k, nslot);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.full);
     uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.empty);
+    uint32_t *seq = reinterpret_cast<uint32_t *>(smem + L.seq);
+    uint32_t *done = reinterpret_cast<uint32_t *>(smem + L.done);
+    uint64_t *xfull = reinterpret_cast<uint64_t *>(smem + L.xfull);
+    uint64_t *xfree = reinterpret_cast<uint64_t *>(smem + L.xfree);
+    uint64_t *hfull = reinterpret_cast<uint64_t *>(smem + L.hfull);
+    uint64_t *hfree = reinterpret_cast<uint64_t *>(smem + L.hfree);
+    uint64_t *routed = reinterpret_cast<uint64_t *>(smem + L.routed);
+    uint64_t *idsfree = reinterpret_cast<uint64_t *>(smem + L.idsfree);
+    uint32_t *xseq = reinterpret_cast<uint32_t *>(smem + L.xseq);   // [2]: token in xs[i]
+    uint32_t *hseq = reinterpret_cast<uint32_t *>(smem + L.hseq);   // [2]: token in hs[i]
+    uint32_t *cnt = reinterpret_cast<uint32_t *>(smem + L.cnt);     // [NBUF] A items done, [NBUF] B items done
     ChunkDesc *desc = reinterpret_cast<ChunkDesc *>(smem + L.desc);
-    int *misc = reinterpret_cast<int *>(smem + L.misc);   // [2] barrier abort, [3] sticky error seen
+    int *ipre = reinterpret_cast<int *>(smem + L.ipre);   // [0..nA] A item prefix, [nA+1..nA+nB+1] B item prefix
+    Slot *slb = reinterpret_cast<Slot *>(smem + L.sl);     // [NBUF][MAXK] selected experts
+    int *misc = reinterpret_cast<int *>(smem + L.misc);    // [0] IA, [1] IB, [3] sticky error seen
+    const uint32_t qvx = qv_bytes(nbx), qvh = qv_bytes(nbh);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
     uint64_t *tr = trace_row(a);
     if (tr && t == 0) {
+        for (int i = 1; i < FUSED_TRACE_POINTS; i++) tr[i] = 0;
         tr[0] = now_ns();
-        tr[8] = tr[9] = tr[10] = tr[11] = 0;
     }
 
-    // ---- prologue: the plan (same for every token; nA phase A chunks, then
-    // nB phase B chunks) and the barriers
+    // ---- prologue: the plan (same for every token: nA gate/up chunks, then
+    // nB down chunks), the barriers, the item prefix tables
     const int2 *plan_n = reinterpret_cast<const int2 *>(a.plan);
     const ChunkDesc *plan_d = reinterpret_cast<const ChunkDesc *>(plan_n + gridDim.x) + (size_t)blockIdx.x * MAXCH;
-    const int2 cnt = plan_n[blockIdx.x];
-    const int nA = cnt.x, nB = cnt.y;
+    const int2 cnt_pl = plan_n[blockIdx.x];
+    const int nA = cnt_pl.x, nB = cnt_pl.y;
     const bool plan_ok = nA >= 0 && nB >= 0 && nA + nB <= MAXCH;
     constexpr int DW = (int)(sizeof(ChunkDesc) / 8);
     if (plan_ok && t < (nA + nB) * DW) reinterpret_cast<uint2 *>(desc)[t] = reinterpret_cast<const uint2 *>(plan_d)[t];
+    if (t < nslot) {
+        seq[t] = 0xFFFFFFFFu;
+        done[t] = 0u;
+    }
+    if (t < 2 * NBUF) cnt[t] = 0u;
+    if (t < 2) {
+        xseq[t] = 0xFFFFFFFFu;
+        hseq[t] = 0xFFFFFFFFu;
+    }
     if (t == 0) {
         for (int s = 0; s < nslot; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], NCW);
+            mbar_init(&empty[s], 1);
         }
-        mbar_init(reinterpret_cast<uint64_t *>(smem + L.xfull), 1);
-        mbar_init(reinterpret_cast<uint64_t *>(smem + L.xempty), 1);
-        for (int b = 0; b < NBUF; b++) mbar_init(reinterpret_cast<uint64_t *>(smem + L.idsfree) + b, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&xfull[i], 1);
+            mbar_init(&xfree[i], 1);
+            mbar_init(&hfull[i], 1);
+            mbar_init(&hfree[i], 1);
+        }
+        for (int b = 0; b < NBUF; b++) {
+            mbar_init(&routed[b], 1);
+            mbar_init(&idsfree[b], 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        misc[2] = 0;
         misc[3] = ld_acquire(&bar[2]) != 0;   // an earlier launch failed: do nothing until reset
+    }
+    __syncthreads();
+    if (t == 0 && plan_ok) {
+        const int rpi = 32 / k;
+        int s = 0;
+        for (int c = 0; c < nA; c++) { ipre[c] = s; s += (desc[c].nrows + 7) >> 3; }
+        ipre[nA] = s;
+        misc[0] = s;
+        s = 0;
+        for (int c = 0; c < nB; c++) { ipre[nA + 1 + c] = s; s += (desc[nA + c].nrows + rpi - 1) / rpi; }
+        ipre[nA + 1 + nB] = s;
+        misc[1] = s;
     }
     __syncthreads();
     if (misc[3] || !plan_ok) {
         if (t == 0) raise_error(err, bar, misc[3] ? FUSED_ERR_BARRIER : FUSED_ERR_PLAN);
         return;   // every CTA sees the same sticky word / plan before any barrier
     }
-    const int n = a.n_tok, E = a.E, k = a.k;
+    const int IA = misc[0], IB = misc[1];
+
+    if (warp == NCW + 1) {
+        // ---- router
+        uint32_t *rscratch = reinterpret_cast<uint32_t *>(smem + L.rscr);
+        for (int tok = 0; tok < n; tok++) {
+            const int b = tok % NBUF;
+            if (tok >= NBUF && !mbar_wait(&idsfree[b], (uint32_t)(tok / NBUF - 1) & 1u)) {
+                if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
+                break;   // the others time out on what is missing
+            }
+            const int layer = (a.layer0 + tok) % a.n_layers;
+            int32_t *ids = reinterpret_cast<int32_t *>(smem + L.ids) + 64 * b;
+            float *wr = reinterpret_cast<float *>(smem + L.w) + 64 * b;
+            warp_route(a.router, a.logits + (size_t)tok * E, a.mask_all ? a.mask_all + (size_t)layer * E : nullptr,
+                       a.bias_all ? a.bias_all + (size_t)layer * E : nullptr, E, k, a.routed_scale, rscratch, ids, wr,
+                       lane);
+            if (blockIdx.x == 0 && lane < k) {
+                if (a.ids_out) a.ids_out[(size_t)tok * k + lane] = ids[lane];
+                if (a.w_out) a.w_out[(size_t)tok * k + lane] = wr[lane];
+            }
+            if (lane < k) slb[MAXK * b + lane] = a.slots_all[(size_t)layer * E + ids[lane]];
+            __syncwarp();
+            if (lane == 0) {
+                if (tr && tok == trace_tok(a)) tr[1] = now_ns();
+                mbar_arrive(&routed[b]);
+            }
+        }
+        return;
+    }
+
+    // ---- launch start: quantise this CTA's share of the inputs x (the
+    // consumer warps), then count the CTA in
+    if (warp < NCW) {
+        for (int q = blockIdx.x * NCW + warp; q < n * nbx; q += gridDim.x * NCW) {
+            const int tok = q / nbx, b = q - tok * nbx;
+            const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)tok * D + 256 * b) + 2 * lane;
+            quant_block(__ldg(x4), __ldg(x4 + 1), qvec(a.xq + (size_t)tok * qvx, nbx), b, lane);
+        }
+        consumer_sync();
+        if (t == 0) {
+            __threadfence();
+            atomicAdd(xbar_word(bar), 1ull);
+        }
+    }
 
     if (warp == NCW) {
-        // ---- producer: route each token when its phase A comes up, then
-        // stream x and the chunks of each step in the consumers' order
-        uint32_t *rscratch = reinterpret_cast<uint32_t *>(smem + L.p);
-        uint8_t *xs = smem + L.xs;
-        uint64_t *xfull = reinterpret_cast<uint64_t *>(smem + L.xfull);
-        uint64_t *xempty = reinterpret_cast<uint64_t *>(smem + L.xempty);
-        uint64_t *idsfree = reinterpret_cast<uint64_t *>(smem + L.idsfree);
-        Slot *sl2 = reinterpret_cast<Slot *>(smem + L.sl);   // [2][MAXK] by token parity
-        uint32_t cc = 0;
-        int failed = 0;
-        for (int j = 0; j < 2 * n && !failed; j++) {
-            int tok;
-            bool isA;
-            step_of(j, n, tok, isA);
-            const int b = tok % NBUF;
-            Slot *sl = sl2 + MAXK * (tok & 1);
-            if (isA) {
-                if (tok >= NBUF && !mbar_wait(&idsfree[b], (uint32_t)(tok / NBUF - 1) & 1u)) failed = 1;
-                if (!failed) {
-                    const int layer = (a.layer0 + tok) % a.n_layers;
-                    int32_t *ids = reinterpret_cast<int32_t *>(smem + L.ids) + 64 * b;
-                    float *wr = reinterpret_cast<float *>(smem + L.w) + 64 * b;
-                    warp_route(a.router, a.logits + (size_t)tok * E,
-                               a.mask_all ? a.mask_all + (size_t)layer * E : nullptr,
-                               a.bias_all ? a.bias_all + (size_t)layer * E : nullptr, E, k, a.routed_scale, rscratch,
-                               ids, wr, lane);
-                    if (tr && tok == 0 && lane == 0) tr[1] = now_ns();
-                    if (blockIdx.x == 0 && lane < k) {
-                        if (a.ids_out) a.ids_out[(size_t)tok * k + lane] = ids[lane];
-                        if (a.w_out) a.w_out[(size_t)tok * k + lane] = wr[lane];
-                    }
-                    if (lane < k) sl[lane] = a.slots_all[(size_t)layer * E + ids[lane]];
-                    __syncwarp();
-                }
-            }
-            if (lane == 0 && !failed) {
+        if (lane == 0) {
+            // ---- stream: x of each token and the chunks of each step
+            bool failed = !grid_wait(xbar_word(bar), a.xbar_target);
+            fence_proxy_async();   // the quantised x was written by other CTAs' generic stores
+            uint32_t cc = 0;
+            for (int j = 0; j < 2 * n && !failed; j++) {
+                int tok;
+                bool isA;
+                step_of(j, n, tok, isA);
+                const int b = tok % NBUF, xb = tok & 1;
+                const Slot *sl = slb + MAXK * b;
                 if (isA) {
-                    if (tok >= 1 && !mbar_wait(xempty, (uint32_t)(tok - 1) & 1u)) failed = 1;
-                    if (!failed) {
-                        mbar_expect_tx(xfull, 4u * (uint32_t)a.D);
-                        bulk_g2s(xs, a.x + (size_t)tok * a.D, 4u * (uint32_t)a.D, xfull);
+                    if (!mbar_wait(&routed[b], (uint32_t)(tok / NBUF) & 1u) ||
+                        (tok >= 2 && !mbar_wait(&xfree[xb], (uint32_t)((tok >> 1) - 1) & 1u))) {
+                        failed = true;
+                        break;
                     }
+                    mbar_expect_tx(&xfull[xb], qvx);
+                    bulk_g2s(smem + L.xs + xb * qvx, a.xq + (size_t)tok * qvx, qvx, &xfull[xb]);
+                    *reinterpret_cast<volatile uint32_t *>(&xseq[xb]) = (uint32_t)tok;
+                    if (tr && tok == trace_tok(a)) tr[21] = now_ns();
                 }
                 const int n_c = isA ? nA : nB;
                 const ChunkDesc *dd = isA ? desc : desc + nA;
-                for (int c = 0; c < n_c && !failed; c++, cc++) {
+                for (int c = 0; c < n_c; c++, cc++) {
                     const uint32_t s = cc % (uint32_t)nslot, u = cc / (uint32_t)nslot;
                     if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1u)) {
-                        failed = 1;
+                        failed = true;
                         break;
                     }
                     const ChunkDesc &d = dd[c];
                     uint8_t *stg = smem + L.stage + (size_t)s * SLOT_BYTES;
                     mbar_expect_tx(&full[s], d.tx);
+                    if (tr && tok == trace_tok(a) && (c == 0 || c == n_c - 1))
+                        tr[(isA ? 22 : 24) + (c == 0 ? 0 : 1)] = now_ns();
                     if (isA) {
                         bulk_g2s(stg + d.dst[0], sl[d.rank].m[0] + d.lo[0], d.size[0], &full[s]);
                         bulk_g2s(stg + d.dst[1], sl[d.rank].m[1] + d.lo[1], d.size[1], &full[s]);
@@ -739,26 +756,160 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                         for (int r = 0; r < k; r++)
                             bulk_g2s(stg + (size_t)r * d.dst[0], sl[r].m[2] + d.lo[0], d.size[0], &full[s]);
                     }
+                    *reinterpret_cast<volatile uint32_t *>(&seq[s]) = cc;
                 }
-                if (failed) raise_error(err, bar, FUSED_ERR_COPY);
             }
-            failed = __shfl_sync(0xFFFFFFFFu, failed, 0);   // consumers time out on what is missing
+            if (failed) raise_error(err, bar, FUSED_ERR_COPY);   // the consumers time out on what is missing
+        } else if (lane == 1) {
+            // ---- h fetch: the quantised h of each token once its barrier completes
+            for (int tok = 0; tok < n; tok++) {
+                const int hb = tok & 1;
+                const uint64_t gt = a.bar_base + (uint64_t)tok;
+                if ((tok >= 2 && !mbar_wait(&hfree[hb], (uint32_t)((tok >> 1) - 1) & 1u)) ||
+                    !grid_wait(barrier_word(bar, gt), (gt / NBUF + 1u) * gridDim.x)) {
+                    raise_error(err, bar, FUSED_ERR_BARRIER);
+                    break;
+                }
+                fence_proxy_async();   // h was quantised by other CTAs' generic stores
+                mbar_expect_tx(&hfull[hb], qvh);
+                bulk_g2s(smem + L.hs + hb * qvh, a.hq + (size_t)tok * qvh, qvh, &hfull[hb]);
+                *reinterpret_cast<volatile uint32_t *>(&hseq[hb]) = (uint32_t)tok;
+                if (tr && tok == trace_tok(a)) tr[10] = now_ns();
+            }
         }
         return;
     }
 
-    // ---- consumers: the same schedule, A0, then (A(t+1), B(t)) pairs, then
-    // B(n-1)
-    uint32_t st = consumer_a<DGU, W>(a, smem, nslot, 0, 0u, nA, bar, err, 0u);
-    uint32_t cc = (uint32_t)nA;
-    for (int tok = 0; tok + 1 < n; tok++) {
-        st = consumer_a<DGU, W>(a, smem, nslot, tok + 1, cc, nA, bar, err, st);
-        cc += (uint32_t)nA;
-        st = consumer_b<DDN, W>(a, smem, nslot, tok, cc, nA, nB, bar, err, st);
-        cc += (uint32_t)nB;
+    // ---- consumers: work items
+    const int64_t P = (int64_t)k * de;
+    const int p0 = (int)(P * blockIdx.x / gridDim.x), p1 = (int)(P * (blockIdx.x + 1) / gridDim.x);
+    const int rbg = nbx * dt_block_bytes(DGU), rbd = nbd * dt_block_bytes(DDN), rpi = 32 / k;
+    uint32_t st = 0;
+    int j = 0, jbase = 0, tok = 0;
+    uint32_t cbase = 0;
+    bool isA = true;
+    uint32_t tw = 0;   // trace: ns this warp waited for its items' inputs
+    for (int it = warp;; it += NCW) {
+        // the step holding item it
+        while (j < 2 * n && it >= jbase + (isA ? IA : IB)) {
+            jbase += isA ? IA : IB;
+            cbase += (uint32_t)(isA ? nA : nB);
+            if (++j < 2 * n) step_of(j, n, tok, isA);
+        }
+        if (j >= 2 * n) break;
+        const int li = it - jbase;
+        const int *pre = isA ? ipre : ipre + nA + 1;
+        const int nc = isA ? nA : nB;
+        int c = 0;
+        while (c + 1 < nc && li >= pre[c + 1]) c++;
+        const int ii = li - pre[c];
+        const uint32_t cc = cbase + (uint32_t)c, s = cc % (uint32_t)nslot;
+        const ChunkDesc d = desc[(isA ? 0 : nA) + c];
+        const bool tr0 = tr && tok == trace_tok(a) && t == 0;
+        if (tr0) tr[isA ? 2 : 9] = now_ns();
+
+        // inputs: the chunk, then the token's x / h
+        const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
+        const int vb = tok & 1;
+        uint8_t *vbuf = smem + (isA ? L.xs + vb * qvx : L.hs + vb * qvh);
+        if (!(st & ST_DEAD)) {
+            const bool ok = seq_wait(&seq[s], cc) && mbar_wait(&full[s], (cc / (uint32_t)nslot) & 1u) &&
+                            seq_wait(isA ? &xseq[vb] : &hseq[vb], (uint32_t)tok) &&
+                            mbar_wait(isA ? &xfull[vb] : &hfull[vb], (uint32_t)(tok >> 1) & 1u);
+            if (!ok) {
+                st |= ST_DEAD | ST_ABORT;
+                if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
+            }
+        }
+        if (tr) tw += (uint32_t)now_ns() - tw0;
+        if (tr0) tr[isA ? 3 : 11] = now_ns();
+        const uint8_t *stg = smem + L.stage + (size_t)s * SLOT_BYTES;
+
+        if (isA) {
+            const int row = 8 * ii + (lane >> 2);
+            const bool valid = row < d.nrows;
+            if (!(st & ST_ABORT)) {
+                const float hv = a_item<DGU, 2 * W>(stg + d.dst[0] + d.roff[0] + (size_t)row * rbg,
+                                                    stg + d.dst[1] + d.roff[1] + (size_t)row * rbg, valid,
+                                                    qvec(vbuf, nbx), nbx, lane);
+                if ((lane & 3) == 0 && valid)
+                    a.hbuf[(size_t)tok * P + (size_t)d.rank * de + d.row0 + row] = hv;
+            }
+            __threadfence();   // this item's h rows, before the counts below
+        } else {
+            const int gq = lane / k, row = rpi * ii + gq;
+            const bool valid = gq < rpi && row < d.nrows;
+            if (!(st & ST_ABORT)) {
+                const float *wr = reinterpret_cast<const float *>(smem + L.w) + 64 * (tok % NBUF);
+                float f = b_item<DDN>(stg + d.roff[0] + (size_t)row * rbd, d.dst[0], valid, qvec(vbuf, nbh), nbd, k,
+                                      wr, lane);
+                if (valid && lane == gq * k) {
+                    const int i = (int)d.row0 + row;
+                    if (a.s_out) f = __fadd_rn(f, __fmul_rn(*a.sgate, a.s_out[i]));
+                    a.ffn[(size_t)tok * D + i] = f;
+                    if (a.h) a.h[i] = __fadd_rn(a.h[i], f);
+                }
+            }
+        }
+        __syncwarp();
+
+        // release the stage when its chunk's last item is done
+        int last = 0;
+        if (lane == 0) {
+            const int nit = pre[c + 1] - pre[c];
+            if ((int)atomicAdd(&done[s], 1u) + 1 == nit) {
+                done[s] = 0u;
+                mbar_arrive(&empty[s]);
+            }
+            last = (int)atomicAdd(&cnt[(isA ? 0 : NBUF) + tok % NBUF], 1u) + 1 == (isA ? IA : IB);
+        }
+        last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        if (!last) continue;
+
+        if (isA) {
+            // ---- the CTA's last gate/up item of the token
+            if (lane == 0) {
+                cnt[tok % NBUF] = 0u;
+                mbar_arrive(&xfree[vb]);
+            }
+            // h blocks the CTA's rows [p0, p1) belong to: the CTA completing
+            // a block quantises it
+            for (int beta = p0 >> 8; beta <= (p1 - 1) >> 8 && p1 > p0; beta++) {
+                const int lo = p0 > 256 * beta ? p0 : 256 * beta, hi = p1 < 256 * beta + 256 ? p1 : 256 * beta + 256;
+                int complete = 0;
+                if (lane == 0) {
+                    uint32_t *hc = a.hcnt + (size_t)tok * nbh + beta;
+                    complete = (int)atomicAdd(hc, (uint32_t)(hi - lo)) + (hi - lo) == 256;
+                    if (complete) *hc = 0u;   // ready for the next launch
+                }
+                complete = __shfl_sync(0xFFFFFFFFu, complete, 0);
+                if (complete) {
+                    __threadfence();
+                    if (!(st & ST_ABORT)) {
+                        const float4 *h4 =
+                            reinterpret_cast<const float4 *>(a.hbuf + (size_t)tok * P + 256 * beta) + 2 * lane;
+                        quant_block(__ldcg(h4), __ldcg(h4 + 1), qvec(a.hq + (size_t)tok * qvh, nbh), beta, lane);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence();
+                atomicAdd(barrier_word(bar, a.bar_base + (uint64_t)tok), 1ull);
+                if (tr && tok == trace_tok(a)) tr[8] = now_ns();
+            }
+        } else {
+            // ---- the CTA's last down item of the token
+            if (lane == 0) {
+                cnt[NBUF + tok % NBUF] = 0u;
+                mbar_arrive(&hfree[vb]);
+                mbar_arrive(&idsfree[tok % NBUF]);
+                if (tr && tok == trace_tok(a)) tr[15] = now_ns();
+            }
+        }
     }
-    consumer_b<DDN, W>(a, smem, nslot, n - 1, cc, nA, nB, bar, err, st);
-    if (tr && t == 0) tr[12] = now_ns();
+    if (tr && lane == 0) atomicAdd(reinterpret_cast<unsigned long long *>(&tr[16]), (unsigned long long)tw);
+    if (tr && t == 0) tr[20] = now_ns();
 }
 
 // ---------------------------------------------------------------------------
@@ -790,7 +941,7 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return cuda_fail(cudaGetLastError(), "device properties");
     if (!prop.cooperativeLaunch) return TLMG_OK;
-    if (g.n_experts <= 0 || g.n_experts > NTHREADS || g.n_experts > RT_PER * 32 || g.top_k > MAXK) return TLMG_OK;
+    if (g.n_experts <= 0 || g.n_experts > RT_PER * 32 || g.top_k > MAXK) return TLMG_OK;
     if (g.d_model % 256 || g.d_expert % 256 || g.d_model > 4096) return TLMG_OK;
     f.smem_limit = prop.sharedMemPerBlockOptin;
     int nslot = 0;
@@ -803,9 +954,13 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     f.nslot = nslot;
     f.smem = smem_layout(g.d_model, g.d_expert, g.top_k, nslot).total;
     f.nsm = prop.multiProcessorCount;
+    f.D = g.d_model;
+    f.de = g.d_expert;
+    f.k = g.top_k;
     if (cudaMalloc(&f.bar, 64) != cudaSuccess) return set_error(TLMG_ENOMEM, "fused barrier allocation");
     cudaMemset(f.bar, 0, 64);
     f.rounds = 0;
+    f.launches = 0;
     if (cudaHostAlloc(&f.err_host, 64, cudaHostAllocMapped) != cudaSuccess)
         return set_error(TLMG_ENOMEM, "fused error word allocation");
     *f.err_host = 0;
@@ -814,7 +969,41 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     return TLMG_OK;
 }
 
+static void free_tokens(FusedScratch &f) {
+    if (f.xq) cudaFree(f.xq);
+    if (f.hbuf) cudaFree(f.hbuf);
+    if (f.hq) cudaFree(f.hq);
+    if (f.hcnt) cudaFree(f.hcnt);
+    f.xq = nullptr;
+    f.hbuf = nullptr;
+    f.hq = nullptr;
+    f.hcnt = nullptr;
+    f.tok_cap = 0;
+}
+
+// Per-token scratch for launches of up to n_tok tokens (grows; the device
+// is idle when it does, as cudaFree synchronises).
+static int reserve_tokens(FusedScratch &f, int n_tok) {
+    if (n_tok <= f.tok_cap) return TLMG_OK;
+    free_tokens(f);
+    const int cap = n_tok < 64 ? 64 : n_tok;
+    const int nbx = f.D / 256, nbh = f.k * (f.de / 256);
+    const size_t P = (size_t)f.k * f.de;
+    if (cudaMalloc(&f.xq, (size_t)cap * qv_bytes(nbx)) != cudaSuccess ||
+        cudaMalloc(&f.hbuf, (size_t)cap * P * 4) != cudaSuccess ||
+        cudaMalloc(&f.hq, (size_t)cap * qv_bytes(nbh)) != cudaSuccess ||
+        cudaMalloc(&f.hcnt, (size_t)cap * nbh * 4) != cudaSuccess) {
+        cudaGetLastError();
+        free_tokens(f);
+        return set_error(TLMG_ENOMEM, "fused per-token scratch for %d tokens", n_tok);
+    }
+    cudaMemset(f.hcnt, 0, (size_t)cap * nbh * 4);
+    f.tok_cap = cap;
+    return TLMG_OK;
+}
+
 void fused_release(FusedScratch &f) {
+    free_tokens(f);
     if (f.bar) cudaFree(f.bar);
     if (f.err_host) cudaFreeHost(f.err_host);
     for (auto &kv : f.plans) cudaFree(kv.second);
@@ -840,8 +1029,8 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
         ChunkDesc *out = &descs[(size_t)c * MAXCH];
         int n = 0;
         const int64_t P = (int64_t)k * de, p0 = P * c / G, p1 = P * (c + 1) / G;
-        // phase A chunks hold whole work items (4 row pairs) where a stage can
-        const int fitA = (SLOT_BYTES - 96) / (2 * rbg), capA = fitA >= 4 ? fitA & ~3 : fitA;
+        // phase A chunks hold whole work items (8 row pairs) where a stage can
+        const int fitA = (SLOT_BYTES - 96) / (2 * rbg), capA = fitA >= 8 ? fitA & ~7 : fitA;
         for (int64_t p = p0; p < p1;) {
             if (n == MAXCH) return nullptr;
             const int r = (int)(p / de), j = (int)(p % de);
@@ -868,7 +1057,9 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
         }
         const int nA = n;
         const int i0 = (int)((int64_t)D * c / G), i1 = (int)((int64_t)D * (c + 1) / G);
-        const int capB = (SLOT_BYTES - 48 * k) / (k * rbd);
+        // phase B chunks hold whole work items (32 / k rows) where a stage can
+        const int fitB = (SLOT_BYTES - 48 * k) / (k * rbd), rpi = 32 / k;
+        const int capB = fitB >= rpi ? fitB - fitB % rpi : fitB;
         for (int i = i0; i < i1;) {
             if (n == MAXCH) return nullptr;
             const int nr = std::min(capB, i1 - i);
@@ -925,12 +1116,20 @@ int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    int rc = reserve_tokens(f, a.n_tok);
+    if (rc) return rc;
     FusedArgs la = a;
+    la.xq = f.xq;
+    la.hbuf = f.hbuf;
+    la.hq = f.hq;
+    la.hcnt = f.hcnt;
     la.bar_base = f.rounds;
+    la.xbar_target = (f.launches + 1) * (uint64_t)f.nsm;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kf, la, f.bar, f.err_dev, f.nslot);
     count_launch();
     if (e != cudaSuccess) return cuda_fail(e, "fused expert FFN launch");
     f.rounds += (uint64_t)a.n_tok;   // every CTA arrives once per token
+    f.launches++;                    // and once per launch after quantising its inputs
     return TLMG_OK;
 }
 
@@ -942,7 +1141,9 @@ uint32_t fused_take_error(FusedScratch &f) {
         // device word and the barrier state for the next launch
         *(volatile uint32_t *)f.err_host = 0;
         cudaMemset(f.bar, 0, 64);
+        if (f.hcnt) cudaMemset(f.hcnt, 0, (size_t)f.tok_cap * f.k * (f.de / 256) * 4);
         f.rounds = 0;
+        f.launches = 0;
     }
     return e;
 }

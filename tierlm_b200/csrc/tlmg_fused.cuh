@@ -54,7 +54,15 @@ struct FusedScratch {
     uint32_t *err_dev = nullptr;   // its device alias
     int nsm = 0;                   // CTAs = SMs (one persistent CTA per SM)
     int nslot = 0;                 // shared-memory stage ring depth
-    uint64_t rounds = 0;           // grid-barrier rounds (tokens) launched since the barrier word was reset
+    uint64_t rounds = 0;           // grid-barrier rounds (tokens) launched since the barrier words were reset
+    uint64_t launches = 0;         // launches since the barrier words were reset
+    // per-token global scratch of a launch, for up to tok_cap tokens
+    int tok_cap = 0;
+    uint8_t *xq = nullptr;         // [tok_cap][quantised x]
+    float *hbuf = nullptr;         // [tok_cap][k * de] SwiGLU rows
+    uint8_t *hq = nullptr;         // [tok_cap][quantised h]
+    uint32_t *hcnt = nullptr;      // [tok_cap][k * de / 256] rows written per h block (zero between launches)
+    int D = 0, de = 0, k = 0;
     size_t smem = 0;               // dynamic shared memory per CTA
     size_t smem_limit = 0;
     std::map<FusedPlanKey, void *> plans;   // device: int2 counts[nsm] | ChunkDesc [nsm][FUSED_MAXCH]
@@ -80,20 +88,21 @@ struct FusedArgs {
     const float *sgate;            // n_tok == 1 only: shared-expert gate (device scalar) or NULL
     int32_t *ids_out;              // [n_tok][k] or NULL
     float *w_out;                  // [n_tok][k] or NULL
-    float *hbuf;                   // [4][k * de] SwiGLU rows (cross-CTA exchange, by token % 4)
+    // filled by launch_fused_ffn from the FusedScratch:
+    uint8_t *xq;                   // [n_tok] quantised inputs
+    float *hbuf;                   // [n_tok][k * de] SwiGLU rows (cross-CTA exchange)
+    uint8_t *hq;                   // [n_tok] quantised h
+    uint32_t *hcnt;                // [n_tok][k * de / 256] h block row counts
     int D, de, E, k, router;
     float routed_scale;
     int dt_gu, dt_dn;              // dtype of every gate/up and every down matrix of the layers
     uint64_t *trace;               // NULL, or [gridDim][FUSED_TRACE_POINTS]
-    uint64_t bar_base;             // set by launch_fused_ffn: grid-barrier rounds before this launch
+    uint64_t bar_base;             // grid-barrier rounds before this launch
+    uint64_t xbar_target;          // input-quantisation count that completes this launch's
 };
 
-// Per CTA when tracing: %globaltimer at [0] start, and for the launch's
-// first token [1] routed, [2] gate/up done and arrived, [5] barrier passed,
-// [6] h quantised, [7] combined; [8..11] summed over the consumer warps and
-// all tokens: ns waiting for gate/up chunks, ns computing gate/up, ns
-// waiting for down chunks, ns computing down; [12] end of the launch.
-constexpr int FUSED_TRACE_POINTS = 16;
+// Per CTA when tracing: the stamps listed at tlmg_trace (include/tlmg.h).
+constexpr int FUSED_TRACE_POINTS = TLMG_TRACE_POINTS;
 
 int fused_init(FusedScratch &f, const tlmg_geom &g);
 void fused_release(FusedScratch &f);

@@ -394,7 +394,6 @@ static FusedArgs fused_args(tlmg_ctx *c, const Layer &Ly, int layer, int n_tok) 
     a.layer0 = layer;
     a.n_layers = g.n_layers;
     a.n_tok = n_tok;
-    a.hbuf = c->hbuf;
     a.D = g.d_model;
     a.de = g.d_expert;
     a.E = g.n_experts;

@@ -67,10 +67,13 @@ class MoeContext:
 
     def trace(self, on: bool = True):
         """Switch the persistent kernel's phase trace on / off; returns the
-        last launch's stamps as int64 [CTAs, 16] (ns) or None."""
-        buf = np.zeros(4096 * 16, np.uint64)
+        last launch's stamps as int64 [CTAs, TRACE_POINTS] (ns) or None; the
+        points are listed at tlmg_trace in include/tlmg.h."""
+        buf = np.zeros(4096 * self.TRACE_POINTS, np.uint64)
         n = check(self._lib.tlmg_trace(self._h, 1 if on else 0, buf.ctypes.data, buf.size))
-        return buf[:n].reshape(-1, 16).astype(np.int64) if n else None
+        return buf[:n].reshape(-1, self.TRACE_POINTS).astype(np.int64) if n else None
+
+    TRACE_POINTS = 32
 
     def set_stream(self, stream=None) -> None:
         """Queue work on a torch.cuda.Stream (None: the context's own stream)."""
