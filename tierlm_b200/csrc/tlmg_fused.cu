@@ -43,10 +43,12 @@
 namespace tlmg {
 
 constexpr int NCW = 16;                 // consumer warps; warp NCW streams, warp NCW + 1 routes
+constexpr int NAW = 10;                 // consumer warps [0, NAW) take gate/up items, the others down items
 constexpr int NTHREADS = 32 * (NCW + 2);
 constexpr int MAXCH = FUSED_MAXCH;
 constexpr int MAXK = 16;
-constexpr int SLOT_BYTES = 24576;
+constexpr int SLOT_A = 50176;   // gate/up stage: the gate rows and the up rows of a chunk, half each
+constexpr int SLOT_B = 24576;   // down stage: the rows of one expert
 constexpr uint64_t WAIT_NS = 200000000ull;       // 0.2 s: an mbarrier wait gives up
 constexpr uint64_t BARRIER_NS = 500000000ull;    // 0.5 s: the grid barrier gives up
 
@@ -359,10 +361,10 @@ __device__ __forceinline__ void warp_quant_swz(const float4 &a, const float4 &b,
 }
 
 // ---------------------------------------------------------------------------
-// Quantised activation vectors (the x of a token, the h of a token): nb
-// Q8_K blocks as codes[256 nb] (swizzled), bsums[16 nb], d[nb], each part
-// 16-byte aligned. The layout is the same in global and in shared memory,
-// so one bulk copy moves a vector.
+// Quantised activation vectors (the x of a token, the h of one expert of a
+// token): nb Q8_K blocks as codes[256 nb] (swizzled), bsums[16 nb], d[nb],
+// each part 16-byte aligned. The layout is the same in global and in shared
+// memory, so one bulk copy moves a vector.
 __host__ __device__ inline uint32_t up16(uint32_t v) { return (v + 15u) & ~15u; }
 __host__ __device__ inline uint32_t qv_bsums(int nb) { return 256u * (uint32_t)nb; }
 __host__ __device__ inline uint32_t qv_d(int nb) { return qv_bsums(nb) + 32u * (uint32_t)nb; }
@@ -384,21 +386,35 @@ __device__ __forceinline__ void quant_block(const float4 &v0, const float4 &v1, 
 }
 
 // ---------------------------------------------------------------------------
-// shared-memory layout
-constexpr int NBUF = 4;   // routing buffers, by token % NBUF
+// Work split of one token over the CTAs. Phase A (gate/up): (rank, row)
+// pairs p = r * de + j, CTA c owns [P c / G, P (c+1) / G), P = k * de.
+// Phase B (down): (rank, output row) pairs q = r * D + i, CTA c owns
+// [Q c / G, Q (c+1) / G), Q = k * D. Either range is contiguous in the
+// weight matrices of at most two experts (for G >= 64), so a CTA streams it
+// in a few large bulk copies (copies of ~24 KB reach the HBM peak; small
+// scattered ones do not).
+__host__ __device__ inline int range_lo(int64_t n, int c, int G) { return (int)(n * c / G); }
+// Pairs one CTA owns at most, for grids of >= 64 CTAs.
+__host__ __device__ inline int range_max(int64_t n) { return (int)((n + 63) / 64 + 1); }
+
+// ---------------------------------------------------------------------------
+// shared-memory layout: nsA gate/up stages of SLOT_A bytes, nsB down stages
+// of SLOT_B bytes, then the small state
+constexpr int NBUF = 4;   // routing / staging buffers, by token % NBUF
 struct SmemLayout {
-    uint32_t stage, full, empty, seq, done, xs, xfull, xfree, xseq, hs, hfull, hfree, hseq, routed, idsfree, ids, w, sl,
-        rscr, cnt, desc, ipre, misc, total;
+    uint32_t stageA, stageB, full, empty, seq, done, xs, xfull, xfree, xseq, hs, hfull, hfree, hseq, routed, idsfree,
+        ids, w, sl, rscr, cnt, hrow, erow, desc, ipre, misc, total;
 };
-__host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nslot) {
+__host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nsA, int nsB) {
     SmemLayout L;
     uint32_t o = 0;
-    const int nbx = D / 256, nbh = k * (de / 256);
-    L.stage = o; o += (uint32_t)nslot * SLOT_BYTES;
-    L.full = o; o += 8u * nslot;
-    L.empty = o; o += 8u * nslot;
-    L.seq = o; o += 4u * nslot;
-    L.done = o = (o + 7u) & ~7u; o += 4u * nslot;
+    const int nbx = D / 256, nbd = de / 256, ns = nsA + nsB;
+    L.stageA = o; o += (uint32_t)nsA * SLOT_A;
+    L.stageB = o; o += (uint32_t)nsB * SLOT_B;
+    L.full = o; o += 8u * ns;
+    L.empty = o; o += 8u * ns;
+    L.seq = o; o += 4u * ns;
+    L.done = o = (o + 7u) & ~7u; o += 4u * ns;
     L.xfull = o = (o + 7u) & ~7u; o += 16u;
     L.xfree = o; o += 16u;
     L.hfull = o; o += 16u;
@@ -408,27 +424,19 @@ __host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nslo
     L.xseq = o; o += 8u;
     L.hseq = o; o += 8u;
     L.xs = o = up16(o); o += 2u * qv_bytes(nbx);
-    L.hs = o = up16(o); o += 2u * qv_bytes(nbh);
+    L.hs = o = up16(o); o += 2u * 2u * qv_bytes(nbd);   // [2][two experts]
     L.rscr = o = up16(o); o += 4u * (uint32_t)RT_SCRATCH;
     L.ids = o; o += 4u * 64 * NBUF;
     L.w = o; o += 4u * 64 * NBUF;
     L.sl = o = up16(o); o += (uint32_t)sizeof(Slot) * MAXK * NBUF;
-    L.cnt = o = up16(o); o += 4u * 2 * NBUF;
+    L.cnt = o = up16(o); o += 4u * (2 * NBUF + 2);
+    L.hrow = o = up16(o); o += 4u * (uint32_t)NBUF * (uint32_t)range_max((int64_t)k * de);
+    L.erow = o = up16(o); o += 4u * (uint32_t)NBUF * (uint32_t)range_max((int64_t)k * D);
     L.desc = o = up16(o); o += (uint32_t)sizeof(ChunkDesc) * MAXCH;
     L.ipre = o; o += 4u * (MAXCH + 2);
     L.misc = o = up16(o); o += 64;
     L.total = o;
     return L;
-}
-
-// The launch's schedule, shared by the producer and the consumers: step j
-// of 2 * n_tok is phase A (gate/up) or phase B (down + combine) of a token,
-// in the order A0, A1, B0, A2, B1, ..., A(n-1), B(n-2), B(n-1).
-__device__ __forceinline__ void step_of(int j, int n, int &tok, bool &isA) {
-    if (j == 0) { tok = 0; isA = true; }
-    else if ((j & 1) && ((j + 1) >> 1) < n) { tok = (j + 1) >> 1; isA = true; }
-    else if (j & 1) { tok = n - 1; isA = false; }
-    else { tok = (j >> 1) - 1; isA = false; }
 }
 
 // Grid barriers: token number gt (counted since the host last reset the
@@ -446,12 +454,15 @@ __device__ __forceinline__ unsigned long long *barrier_word(uint32_t *bar, uint6
 __device__ __forceinline__ unsigned long long *xbar_word(uint32_t *bar) {
     return reinterpret_cast<unsigned long long *>(bar + 12);
 }
-// Wait until *w >= target, for at most BARRIER_NS.
+// Wait until *w >= target, for at most BARRIER_NS; polls with a short sleep
+// so that a waiting lane takes few issue slots from the warps computing.
 __device__ __forceinline__ bool grid_wait(const unsigned long long *w, uint64_t target) {
     if (ld_acquire64(w) >= target) return true;
     const uint64_t t0 = now_ns();
-    while (ld_acquire64(w) < target)
+    while (ld_acquire64(w) < target) {
         if (now_ns() - t0 > BARRIER_NS) return false;
+        __nanosleep(128);
+    }
     return true;
 }
 // Wait until the shared word *p equals v (the producer publishes which
@@ -461,8 +472,10 @@ __device__ __forceinline__ bool seq_wait(const uint32_t *p, uint32_t v) {
     const volatile uint32_t *q = p;
     if (*q == v) return true;
     const uint64_t t0 = now_ns();
-    while (*q != v)
+    while (*q != v) {
         if (now_ns() - t0 > WAIT_NS) return false;
+        __nanosleep(64);
+    }
     return true;
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
@@ -478,47 +491,39 @@ __device__ __forceinline__ uint64_t *trace_row(const FusedArgs &a) {
 }
 
 // ---------------------------------------------------------------------------
-// One phase-A work item: eight (gate, up) row pairs. Lane (p, j) =
-// (lane / 4, lane % 4) owns row pair p (gate row at grow, up row at urow,
-// valid or not) and blocks j, j + 4, ... of both rows: it computes their
-// exact partials (even row pairs their low block first, odd ones their high
-// block, so that the 8 lanes of a quarter warp read 8 different banks), then
-// the gate and up fmaf chains run over the blocks in ascending order, the
-// lane holding block b applying it and passing the accumulators on by
-// shuffle. Returns silu(gate) * up on every lane of the row pair.
+// One phase-A work item: four (gate, up) row pairs. Lane (p, j) =
+// (lane / 8, lane % 8) owns row pair p (gate row at grow, up row at urow,
+// valid or not) and blocks j, j + 8, ... of both rows: it computes their
+// exact partials (the 8 lanes of a quarter warp read 8 consecutive blocks
+// of one row: 8 different banks). Then the gate and up fmaf chains run over
+// the blocks in ascending order: the lane holding block b applies it and
+// the accumulators are passed on by shuffle. Returns silu(gate) * up on
+// every lane of the row pair.
 template <int DGU, int BPL>
 __device__ __forceinline__ float a_item(const uint8_t *grow, const uint8_t *urow, bool valid, const QVec &x, int nbx,
                                         int lane) {
-    const int j = lane & 3, odd = (lane >> 2) & 1;
-    // rg/ru[ii]: the ii-th block the lane computes; vg/vu[i]: block j + 4i
-    BlockSum rg[BPL], ru[BPL], vg[BPL], vu[BPL];
+    const int j = lane & 7;
+    BlockSum vg[BPL], vu[BPL];
 #pragma unroll
-    for (int ii = 0; ii < BPL; ii++) {
-        const int i = (BPL == 2 && odd) ? 1 - ii : ii;
-        const int b = j + 4 * i;
-        rg[ii] = BlockSum{ 0, 0, 0.f, 0.f };
-        ru[ii] = rg[ii];
+    for (int i = 0; i < BPL; i++) {
+        const int b = j + 8 * i;
+        vg[i] = BlockSum{ 0, 0, 0.f, 0.f };
+        vu[i] = vg[i];
         if (valid && b < nbx) {
             const uint8_t *wb[2] = { grow + b * dt_block_bytes(DGU), urow + b * dt_block_bytes(DGU) };
             BlockSum o2[2];
             kblock_dot<DGU, 2>(wb, XBlk{ x.codes, nbx, b, x.bs + 16 * b, x.d[b] }, o2);
-            rg[ii] = o2[0];
-            ru[ii] = o2[1];
+            vg[i] = o2[0];
+            vu[i] = o2[1];
         }
     }
-#pragma unroll
-    for (int i = 0; i < BPL; i++) {
-        const bool sw = BPL == 2 && odd;
-        vg[i] = sw ? rg[BPL - 1 - i] : rg[i];
-        vu[i] = sw ? ru[BPL - 1 - i] : ru[i];
-    }
     float ag = 0.0f, au = 0.0f;
-    const int base = lane & ~3;
+    const int base = lane & ~7;
 #pragma unroll
     for (int i = 0; i < BPL; i++)
 #pragma unroll
-        for (int h = 0; h < 4; h++) {
-            if (h + 4 * i >= nbx) break;
+        for (int h = 0; h < 8; h++) {
+            if (h + 8 * i >= nbx) break;
             if (j == h) {
                 ag = chain<DGU>(ag, vg[i].dA, vg[i].is, vg[i].dM, vg[i].ms);
                 au = chain<DGU>(au, vu[i].dA, vu[i].is, vu[i].dM, vu[i].ms);
@@ -529,65 +534,69 @@ __device__ __forceinline__ float a_item(const uint8_t *grow, const uint8_t *urow
     return __fmul_rn(silu_f(ag), au);
 }
 
-// One phase-B work item: 32 / k output rows. Lane (g, r) = (lane / k,
-// lane % k) owns row g of the item (rank r's copy of it at row_r0 + r * rs,
-// valid or not) and runs expert r's fmaf chain over its nbd blocks in
-// ascending order; then ffn = sum_r w[r] * eo_r in ascending rank. Returns
-// ffn on the lanes (g, 0) (all lanes take part).
+// One phase-B work item: 32 / nbd rows of one expert's down matrix. Lane
+// (g, b) = (lane / nbd, lane % nbd) owns block b of row g (at row0, valid
+// or not) and computes its exact partials against the expert's h; the
+// row's fmaf chain runs over the blocks in ascending order, the lane
+// holding block b applying it and passing the accumulator on by shuffle.
+// Returns the row's expert output eo on every lane of the row.
 template <int DDN>
-__device__ __forceinline__ float b_item(const uint8_t *row_r0, uint32_t rs, bool valid, const QVec &h, int nbd, int k,
-                                        const float *wr, int lane) {
-    const int g = lane / k, r = lane - g * k;
-    float eo = 0.0f;
+__device__ __forceinline__ float b_item(const uint8_t *row, bool valid, const QVec &h, int nbd, int lane) {
+    const int g = lane / nbd, b = lane - g * nbd;
+    BlockSum v = BlockSum{ 0, 0, 0.f, 0.f };
     if (valid) {
-        const uint8_t *row = row_r0 + (size_t)r * rs;
-        for (int b = 0; b < nbd; b++) {
-            const int beta = r * nbd + b;
-            const uint8_t *wb[1] = { row + b * dt_block_bytes(DDN) };
-            BlockSum o1[1];
-            kblock_dot<DDN, 1>(wb, XBlk{ h.codes, h.nb, beta, h.bs + 16 * beta, h.d[beta] }, o1);
-            eo = chain<DDN>(eo, o1[0].dA, o1[0].is, o1[0].dM, o1[0].ms);
-        }
+        const uint8_t *wb[1] = { row + b * dt_block_bytes(DDN) };
+        BlockSum o1[1];
+        kblock_dot<DDN, 1>(wb, XBlk{ h.codes, nbd, b, h.bs + 16 * b, h.d[b] }, o1);
+        v = o1[0];
     }
-    const int src0 = g * k < 32 ? g * k : 0;
-    float f = 0.0f;
-    for (int q = 0; q < k; q++) f = __fadd_rn(f, __fmul_rn(wr[q], __shfl_sync(0xFFFFFFFFu, eo, (src0 + q) & 31)));
-    return f;
+    float eo = 0.0f;
+    const int gb = g * nbd < 32 - nbd + 1 ? g * nbd : 0;
+    for (int hh = 0; hh < nbd; hh++) {
+        if (b == hh) eo = chain<DDN>(eo, v.dA, v.is, v.dM, v.ms);
+        eo = __shfl_sync(0xFFFFFFFFu, eo, gb + hh);
+    }
+    return eo;
 }
 
 // ---------------------------------------------------------------------------
 // The persistent kernel. One CTA per SM: warps 0..NCW-1 consume work items,
-// warp NCW streams (lane 0: x and weight chunks; lane 1: the quantised h of
-// each token once its grid barrier completes), warp NCW + 1 routes.
+// warp NCW streams (lane 0: the tokens' x and gate/up chunks; lane 1: each
+// token's quantised h and down chunks once its grid barrier completes),
+// warp NCW + 1 routes.
 //
 //   launch start  every CTA quantises its share of the launch's inputs x
 //                 (n_tok x D / 256 blocks) into a.xq; one grid-wide count.
-//   router        routes token t into buffer t % NBUF once the consumers
-//                 are done with token t - NBUF.
-//   stream        per step of the schedule: the token's quantised x (phase
-//                 A) and the step's chunks of weight rows, in a ring of
-//                 stages; each stage's sequence word names the chunk it is
-//                 armed for.
-//   work items    warp w takes items w, w + NCW, ... of the launch's item
-//                 sequence (the steps' items in schedule order) and waits
-//                 only for what its item reads: the chunk, the token's x or
-//                 h. A stage is released when its chunk's last item is done.
-//   token A done  the warp that finishes a token's last gate/up item of the
-//                 CTA adds the CTA's rows to the counts of the h blocks they
-//                 belong to; the CTA completing a block quantises it into
-//                 a.hq; then the CTA arrives at the token's grid barrier.
-//   token B done  the warp that finishes the token's last down item frees
-//                 the token's h and routing buffers.
+//   router        routes token t into buffer t % NBUF once the CTA is done
+//                 with token t - NBUF.
+//   work items    gate/up warps [0, NAW) and down warps [NAW, NCW) take the
+//                 next item of their kind (shared counters, token order) and
+//                 wait only for what the item reads: its chunk (the
+//                 stage's sequence word names the chunk it is armed for)
+//                 and the token's x or h. A stage is released when its
+//                 chunk's last item is done. Items stage their results
+//                 (h rows, expert outputs) in shared memory.
+//   token A done  the warp finishing the CTA's last gate/up item of a token
+//                 writes the CTA's h rows, adds them to the counts of the h
+//                 blocks they belong to (the CTA completing a block
+//                 quantises it into a.hq) and arrives at the token's grid
+//                 barrier.
+//   token B done  the warp finishing the CTA's last down item writes the
+//                 CTA's expert outputs, adds them to the counts of the
+//                 64-row groups they belong to (the CTA completing a group
+//                 runs its rank-ordered combine) and frees the token's h
+//                 and routing buffers.
 //
 // Every wait is bounded; on expiry the kernel raises an error bit the host
 // reads and stops waiting (results of the launch are invalid).
 template <int DGU, int DDN, int W>
 __global__ void __launch_bounds__(NTHREADS, 1)
-k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict__ err, int nslot) {
+k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uint32_t *__restrict__ err, int nsA,
+            int nsB) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int D = a.D, de = a.de, k = a.k, E = a.E, n = a.n_tok;
     const int nbx = D / 256, nbd = de / 256, nbh = k * nbd;
-    const SmemLayout L = smem_layout(D, de, k, nslot);
+    const SmemLayout L = smem_layout(D, de, k, nsA, nsB);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.full);
     uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.empty);
     uint32_t *seq = reinterpret_cast<uint32_t *>(smem + L.seq);
@@ -600,12 +609,17 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     uint64_t *idsfree = reinterpret_cast<uint64_t *>(smem + L.idsfree);
     uint32_t *xseq = reinterpret_cast<uint32_t *>(smem + L.xseq);   // [2]: token in xs[i]
     uint32_t *hseq = reinterpret_cast<uint32_t *>(smem + L.hseq);   // [2]: token in hs[i]
-    uint32_t *cnt = reinterpret_cast<uint32_t *>(smem + L.cnt);     // [NBUF] A items done, [NBUF] B items done
+    // [NBUF] A items done and [NBUF] B items done by token, then the next A / B item to take
+    uint32_t *cnt = reinterpret_cast<uint32_t *>(smem + L.cnt);
     ChunkDesc *desc = reinterpret_cast<ChunkDesc *>(smem + L.desc);
     int *ipre = reinterpret_cast<int *>(smem + L.ipre);   // [0..nA] A item prefix, [nA+1..nA+nB+1] B item prefix
     Slot *slb = reinterpret_cast<Slot *>(smem + L.sl);     // [NBUF][MAXK] selected experts
     int *misc = reinterpret_cast<int *>(smem + L.misc);    // [0] IA, [1] IB, [3] sticky error seen
-    const uint32_t qvx = qv_bytes(nbx), qvh = qv_bytes(nbh);
+    const uint32_t qvx = qv_bytes(nbx), qvd = qv_bytes(nbd);
+    const int64_t P = (int64_t)k * de, Q = (int64_t)k * D;
+    const int p0 = range_lo(P, blockIdx.x, gridDim.x), p1 = range_lo(P, blockIdx.x + 1, gridDim.x);
+    const int q0 = range_lo(Q, blockIdx.x, gridDim.x), q1 = range_lo(Q, blockIdx.x + 1, gridDim.x);
+    const int rq0 = q0 / D;   // first expert rank of the CTA's down rows
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
     uint64_t *tr = trace_row(a);
@@ -623,17 +637,18 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     const bool plan_ok = nA >= 0 && nB >= 0 && nA + nB <= MAXCH;
     constexpr int DW = (int)(sizeof(ChunkDesc) / 8);
     if (plan_ok && t < (nA + nB) * DW) reinterpret_cast<uint2 *>(desc)[t] = reinterpret_cast<const uint2 *>(plan_d)[t];
-    if (t < nslot) {
+    const int ns = nsA + nsB;
+    if (t < ns) {
         seq[t] = 0xFFFFFFFFu;
         done[t] = 0u;
     }
-    if (t < 2 * NBUF) cnt[t] = 0u;
+    if (t < 2 * NBUF + 2) cnt[t] = 0u;
     if (t < 2) {
         xseq[t] = 0xFFFFFFFFu;
         hseq[t] = 0xFFFFFFFFu;
     }
     if (t == 0) {
-        for (int s = 0; s < nslot; s++) {
+        for (int s = 0; s < ns; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -652,13 +667,13 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     }
     __syncthreads();
     if (t == 0 && plan_ok) {
-        const int rpi = 32 / k;
+        const int rb = 32 / nbd;
         int s = 0;
-        for (int c = 0; c < nA; c++) { ipre[c] = s; s += (desc[c].nrows + 7) >> 3; }
+        for (int c = 0; c < nA; c++) { ipre[c] = s; s += (desc[c].nrows + 3) >> 2; }
         ipre[nA] = s;
         misc[0] = s;
         s = 0;
-        for (int c = 0; c < nB; c++) { ipre[nA + 1 + c] = s; s += (desc[nA + c].nrows + rpi - 1) / rpi; }
+        for (int c = 0; c < nB; c++) { ipre[nA + 1 + c] = s; s += (desc[nA + c].nrows + rb - 1) / rb; }
         ipre[nA + 1 + nB] = s;
         misc[1] = s;
     }
@@ -714,106 +729,106 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     }
 
     if (warp == NCW) {
-        if (lane == 0) {
-            // ---- stream: x of each token and the chunks of each step
-            bool failed = !grid_wait(xbar_word(bar), a.xbar_target);
-            fence_proxy_async();   // the quantised x was written by other CTAs' generic stores
-            uint32_t cc = 0;
-            for (int j = 0; j < 2 * n && !failed; j++) {
-                int tok;
-                bool isA;
-                step_of(j, n, tok, isA);
-                const int b = tok % NBUF, xb = tok & 1;
+        if (lane == 0 || lane == 1) {
+            // ---- stream, in token order. Lane 0: each token's x and gate/up
+            // chunks once it is routed. Lane 1: once the token's grid barrier
+            // completes, the quantised h of the CTA's down experts and the
+            // down chunks (down chunks would otherwise hold stages while the
+            // barrier settles).
+            const bool isA = lane == 0;
+            bool failed = isA && !grid_wait(xbar_word(bar), a.xbar_target);
+            if (isA) fence_proxy_async();   // the quantised x was written by other CTAs' generic stores
+            const int nc = isA ? nA : nB, nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA;
+            const ChunkDesc *dd = isA ? desc : desc + nA;
+            const int ne = (q1 - 1) / D - rq0 + 1;   // down experts of the CTA (1 or 2)
+            for (int tok = 0; tok < n && !failed; tok++) {
+                const int b = tok % NBUF, vb = tok & 1;
                 const Slot *sl = slb + MAXK * b;
+                if (!mbar_wait(&routed[b], (uint32_t)(tok / NBUF) & 1u)) {
+                    failed = true;
+                    break;
+                }
                 if (isA) {
-                    if (!mbar_wait(&routed[b], (uint32_t)(tok / NBUF) & 1u) ||
-                        (tok >= 2 && !mbar_wait(&xfree[xb], (uint32_t)((tok >> 1) - 1) & 1u))) {
+                    if (tok >= 2 && !mbar_wait(&xfree[vb], (uint32_t)((tok >> 1) - 1) & 1u)) {
                         failed = true;
                         break;
                     }
-                    mbar_expect_tx(&xfull[xb], qvx);
-                    bulk_g2s(smem + L.xs + xb * qvx, a.xq + (size_t)tok * qvx, qvx, &xfull[xb]);
-                    *reinterpret_cast<volatile uint32_t *>(&xseq[xb]) = (uint32_t)tok;
+                    mbar_expect_tx(&xfull[vb], qvx);
+                    bulk_g2s(smem + L.xs + vb * qvx, a.xq + (size_t)tok * qvx, qvx, &xfull[vb]);
+                    *reinterpret_cast<volatile uint32_t *>(&xseq[vb]) = (uint32_t)tok;
                     if (tr && tok == trace_tok(a)) tr[21] = now_ns();
+                } else {
+                    const uint64_t gt = a.bar_base + (uint64_t)tok;
+                    if ((tok >= 2 && !mbar_wait(&hfree[vb], (uint32_t)((tok >> 1) - 1) & 1u)) ||
+                        !grid_wait(barrier_word(bar, gt), (gt / NBUF + 1u) * gridDim.x)) {
+                        failed = true;
+                        break;
+                    }
+                    fence_proxy_async();   // h was quantised by other CTAs' generic stores
+                    mbar_expect_tx(&hfull[vb], ne * qvd);
+                    bulk_g2s(smem + L.hs + vb * 2 * qvd, a.hq + ((size_t)tok * k + rq0) * qvd, ne * qvd, &hfull[vb]);
+                    *reinterpret_cast<volatile uint32_t *>(&hseq[vb]) = (uint32_t)tok;
+                    if (tr && tok == trace_tok(a)) tr[10] = now_ns();
                 }
-                const int n_c = isA ? nA : nB;
-                const ChunkDesc *dd = isA ? desc : desc + nA;
-                for (int c = 0; c < n_c; c++, cc++) {
-                    const uint32_t s = cc % (uint32_t)nslot, u = cc / (uint32_t)nslot;
+                for (int c = 0; c < nc; c++) {
+                    const uint32_t cc = (uint32_t)(tok * nc + c), u = cc / (uint32_t)nsr;
+                    const int s = s0 + (int)(cc % (uint32_t)nsr);
                     if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1u)) {
                         failed = true;
                         break;
                     }
                     const ChunkDesc &d = dd[c];
-                    uint8_t *stg = smem + L.stage + (size_t)s * SLOT_BYTES;
+                    uint8_t *stg = smem + (isA ? L.stageA + (size_t)s * SLOT_A : L.stageB + (size_t)(s - nsA) * SLOT_B);
                     mbar_expect_tx(&full[s], d.tx);
-                    if (tr && tok == trace_tok(a) && (c == 0 || c == n_c - 1))
+                    if (tr && tok == trace_tok(a) && (c == 0 || c == nc - 1))
                         tr[(isA ? 22 : 24) + (c == 0 ? 0 : 1)] = now_ns();
                     if (isA) {
                         bulk_g2s(stg + d.dst[0], sl[d.rank].m[0] + d.lo[0], d.size[0], &full[s]);
                         bulk_g2s(stg + d.dst[1], sl[d.rank].m[1] + d.lo[1], d.size[1], &full[s]);
                     } else {
-                        for (int r = 0; r < k; r++)
-                            bulk_g2s(stg + (size_t)r * d.dst[0], sl[r].m[2] + d.lo[0], d.size[0], &full[s]);
+                        bulk_g2s(stg, sl[d.rank].m[2] + d.lo[0], d.size[0], &full[s]);
                     }
                     *reinterpret_cast<volatile uint32_t *>(&seq[s]) = cc;
                 }
             }
-            if (failed) raise_error(err, bar, FUSED_ERR_COPY);   // the consumers time out on what is missing
-        } else if (lane == 1) {
-            // ---- h fetch: the quantised h of each token once its barrier completes
-            for (int tok = 0; tok < n; tok++) {
-                const int hb = tok & 1;
-                const uint64_t gt = a.bar_base + (uint64_t)tok;
-                if ((tok >= 2 && !mbar_wait(&hfree[hb], (uint32_t)((tok >> 1) - 1) & 1u)) ||
-                    !grid_wait(barrier_word(bar, gt), (gt / NBUF + 1u) * gridDim.x)) {
-                    raise_error(err, bar, FUSED_ERR_BARRIER);
-                    break;
-                }
-                fence_proxy_async();   // h was quantised by other CTAs' generic stores
-                mbar_expect_tx(&hfull[hb], qvh);
-                bulk_g2s(smem + L.hs + hb * qvh, a.hq + (size_t)tok * qvh, qvh, &hfull[hb]);
-                *reinterpret_cast<volatile uint32_t *>(&hseq[hb]) = (uint32_t)tok;
-                if (tr && tok == trace_tok(a)) tr[10] = now_ns();
-            }
+            if (failed) raise_error(err, bar, isA ? FUSED_ERR_COPY : FUSED_ERR_BARRIER);
         }
         return;
     }
 
-    // ---- consumers: work items
-    const int64_t P = (int64_t)k * de;
-    const int p0 = (int)(P * blockIdx.x / gridDim.x), p1 = (int)(P * (blockIdx.x + 1) / gridDim.x);
-    const int rbg = nbx * dt_block_bytes(DGU), rbd = nbd * dt_block_bytes(DDN), rpi = 32 / k;
+    // ---- consumers: warps [0, NAW) take gate/up items, the others down
+    // items, each the next one of its kind (shared counters), in token
+    // order; an item waits only for what it reads
+    const bool isA = warp < NAW;
+    const int rbg = nbx * dt_block_bytes(DGU), rbd = nbd * dt_block_bytes(DDN), rb = 32 / nbd;
+    const int I = isA ? IA : IB, nc = isA ? nA : nB, nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA;
+    const int *pre = isA ? ipre : ipre + nA + 1;
+    float *hrow = reinterpret_cast<float *>(smem + L.hrow);   // [NBUF][range_max(P)] the CTA's h rows by token
+    float *erow = reinterpret_cast<float *>(smem + L.erow);   // [NBUF][range_max(Q)] the CTA's expert outputs
+    const int hrow_n = range_max(P), erow_n = range_max(Q);
     uint32_t st = 0;
-    int j = 0, jbase = 0, tok = 0;
-    uint32_t cbase = 0;
-    bool isA = true;
-    uint32_t tw = 0;   // trace: ns this warp waited for its items' inputs
-    for (int it = warp;; it += NCW) {
-        // the step holding item it
-        while (j < 2 * n && it >= jbase + (isA ? IA : IB)) {
-            jbase += isA ? IA : IB;
-            cbase += (uint32_t)(isA ? nA : nB);
-            if (++j < 2 * n) step_of(j, n, tok, isA);
-        }
-        if (j >= 2 * n) break;
-        const int li = it - jbase;
-        const int *pre = isA ? ipre : ipre + nA + 1;
-        const int nc = isA ? nA : nB;
+    uint32_t tw = 0, tc = 0, td = 0;   // trace: ns this warp waited for inputs / in items / in token duties
+    for (;;) {
+        int item = 0;
+        if (lane == 0) item = (int)atomicAdd(&cnt[2 * NBUF + (isA ? 0 : 1)], 1u);
+        item = __shfl_sync(0xFFFFFFFFu, item, 0);
+        if (item >= n * I) break;
+        const int tok = item / I, li = item - tok * I;
         int c = 0;
         while (c + 1 < nc && li >= pre[c + 1]) c++;
         const int ii = li - pre[c];
-        const uint32_t cc = cbase + (uint32_t)c, s = cc % (uint32_t)nslot;
+        const uint32_t cc = (uint32_t)(tok * nc + c);
+        const int s = s0 + (int)(cc % (uint32_t)nsr);
         const ChunkDesc d = desc[(isA ? 0 : nA) + c];
-        const bool tr0 = tr && tok == trace_tok(a) && t == 0;
+        const bool tr0 = tr && tok == trace_tok(a) && li == 0 && lane == 0;
         if (tr0) tr[isA ? 2 : 9] = now_ns();
 
         // inputs: the chunk, then the token's x / h
         const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
         const int vb = tok & 1;
-        uint8_t *vbuf = smem + (isA ? L.xs + vb * qvx : L.hs + vb * qvh);
+        uint8_t *vbuf = smem + (isA ? L.xs + vb * qvx : L.hs + vb * 2 * qvd);
         if (!(st & ST_DEAD)) {
-            const bool ok = seq_wait(&seq[s], cc) && mbar_wait(&full[s], (cc / (uint32_t)nslot) & 1u) &&
+            const bool ok = seq_wait(&seq[s], cc) && mbar_wait(&full[s], (cc / (uint32_t)nsr) & 1u) &&
                             seq_wait(isA ? &xseq[vb] : &hseq[vb], (uint32_t)tok) &&
                             mbar_wait(isA ? &xfull[vb] : &hfull[vb], (uint32_t)(tok >> 1) & 1u);
             if (!ok) {
@@ -821,37 +836,34 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                 if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
             }
         }
-        if (tr) tw += (uint32_t)now_ns() - tw0;
+        const uint32_t tc0 = tr ? (uint32_t)now_ns() : 0u;
+        if (tr) tw += tc0 - tw0;
         if (tr0) tr[isA ? 3 : 11] = now_ns();
-        const uint8_t *stg = smem + L.stage + (size_t)s * SLOT_BYTES;
 
         if (isA) {
-            const int row = 8 * ii + (lane >> 2);
+            const uint8_t *stg = smem + L.stageA + (size_t)s * SLOT_A;
+            const int row = 4 * ii + (lane >> 3);
             const bool valid = row < d.nrows;
             if (!(st & ST_ABORT)) {
-                const float hv = a_item<DGU, 2 * W>(stg + d.dst[0] + d.roff[0] + (size_t)row * rbg,
-                                                    stg + d.dst[1] + d.roff[1] + (size_t)row * rbg, valid,
-                                                    qvec(vbuf, nbx), nbx, lane);
-                if ((lane & 3) == 0 && valid)
-                    a.hbuf[(size_t)tok * P + (size_t)d.rank * de + d.row0 + row] = hv;
+                const float hv = a_item<DGU, W>(stg + d.dst[0] + d.roff[0] + (size_t)row * rbg,
+                                                stg + d.dst[1] + d.roff[1] + (size_t)row * rbg, valid,
+                                                qvec(vbuf, nbx), nbx, lane);
+                if ((lane & 7) == 0 && valid)
+                    hrow[(tok % NBUF) * hrow_n + (int)(d.rank * de + d.row0 + row - p0)] = hv;
             }
-            __threadfence();   // this item's h rows, before the counts below
         } else {
-            const int gq = lane / k, row = rpi * ii + gq;
-            const bool valid = gq < rpi && row < d.nrows;
+            const uint8_t *stg = smem + L.stageB + (size_t)(s - nsA) * SLOT_B;
+            const int g = lane / nbd, row = rb * ii + g;
+            const bool valid = g < rb && row < d.nrows;
             if (!(st & ST_ABORT)) {
-                const float *wr = reinterpret_cast<const float *>(smem + L.w) + 64 * (tok % NBUF);
-                float f = b_item<DDN>(stg + d.roff[0] + (size_t)row * rbd, d.dst[0], valid, qvec(vbuf, nbh), nbd, k,
-                                      wr, lane);
-                if (valid && lane == gq * k) {
-                    const int i = (int)d.row0 + row;
-                    if (a.s_out) f = __fadd_rn(f, __fmul_rn(*a.sgate, a.s_out[i]));
-                    a.ffn[(size_t)tok * D + i] = f;
-                    if (a.h) a.h[i] = __fadd_rn(a.h[i], f);
-                }
+                const float eo = b_item<DDN>(stg + d.roff[0] + (size_t)row * rbd, valid,
+                                             qvec(vbuf + (d.rank - rq0) * qvd, nbd), nbd, lane);
+                if (valid && lane == g * nbd)
+                    erow[(tok % NBUF) * erow_n + (int)((int64_t)d.rank * D + d.row0 + row - q0)] = eo;
             }
         }
         __syncwarp();
+        if (tr) tc += (uint32_t)now_ns() - tc0;
 
         // release the stage when its chunk's last item is done
         int last = 0;
@@ -861,19 +873,25 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                 done[s] = 0u;
                 mbar_arrive(&empty[s]);
             }
-            last = (int)atomicAdd(&cnt[(isA ? 0 : NBUF) + tok % NBUF], 1u) + 1 == (isA ? IA : IB);
+            __threadfence_block();   // this item's staged results, before the count
+            last = (int)atomicAdd(&cnt[(isA ? 0 : NBUF) + tok % NBUF], 1u) + 1 == I;
         }
         last = __shfl_sync(0xFFFFFFFFu, last, 0);
         if (!last) continue;
 
+        const uint32_t td0 = tr ? (uint32_t)now_ns() : 0u;
+        __threadfence_block();
         if (isA) {
-            // ---- the CTA's last gate/up item of the token
+            // ---- the CTA's last gate/up item of the token: its h rows out
+            // (one fence), then the h block counts; the CTA completing a block
+            // quantises it (into expert r's vector of the token's h)
             if (lane == 0) {
                 cnt[tok % NBUF] = 0u;
                 mbar_arrive(&xfree[vb]);
             }
-            // h blocks the CTA's rows [p0, p1) belong to: the CTA completing
-            // a block quantises it
+            for (int i = lane; i < p1 - p0; i += 32) a.hbuf[(size_t)tok * P + p0 + i] = hrow[(tok % NBUF) * hrow_n + i];
+            __syncwarp();
+            __threadfence();
             for (int beta = p0 >> 8; beta <= (p1 - 1) >> 8 && p1 > p0; beta++) {
                 const int lo = p0 > 256 * beta ? p0 : 256 * beta, hi = p1 < 256 * beta + 256 ? p1 : 256 * beta + 256;
                 int complete = 0;
@@ -886,9 +904,11 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                 if (complete) {
                     __threadfence();
                     if (!(st & ST_ABORT)) {
+                        const int r = beta / nbd, bb = beta - r * nbd;
                         const float4 *h4 =
                             reinterpret_cast<const float4 *>(a.hbuf + (size_t)tok * P + 256 * beta) + 2 * lane;
-                        quant_block(__ldcg(h4), __ldcg(h4 + 1), qvec(a.hq + (size_t)tok * qvh, nbh), beta, lane);
+                        quant_block(__ldcg(h4), __ldcg(h4 + 1), qvec(a.hq + ((size_t)tok * k + r) * qvd, nbd), bb,
+                                    lane);
                     }
                 }
             }
@@ -899,7 +919,40 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                 if (tr && tok == trace_tok(a)) tr[8] = now_ns();
             }
         } else {
-            // ---- the CTA's last down item of the token
+            // ---- the CTA's last down item of the token: its expert outputs
+            // out (one fence), then the counts of the 64-row output groups;
+            // the CTA completing a group combines its rows
+            for (int i = lane; i < q1 - q0; i += 32) a.eo[(size_t)tok * Q + q0 + i] = erow[(tok % NBUF) * erow_n + i];
+            __syncwarp();
+            __threadfence();
+            const float *wr = reinterpret_cast<const float *>(smem + L.w) + 64 * (tok % NBUF);
+            for (int r = rq0; r <= (q1 - 1) / D; r++) {
+                const int ia = (q0 > r * D ? q0 - r * D : 0), ib = (q1 < (r + 1) * D ? q1 - r * D : D);
+                for (int grp = ia >> 6; grp <= (ib - 1) >> 6; grp++) {
+                    const int ga = ia > 64 * grp ? ia : 64 * grp, gz = ib < 64 * grp + 64 ? ib : 64 * grp + 64;
+                    int complete = 0;
+                    if (lane == 0) {
+                        uint32_t *gc = a.ocnt + (size_t)tok * (D / 64) + grp;
+                        complete = (int)atomicAdd(gc, (uint32_t)(gz - ga)) + (gz - ga) == 64 * k;
+                        if (complete) *gc = 0u;   // ready for the next launch
+                    }
+                    complete = __shfl_sync(0xFFFFFFFFu, complete, 0);
+                    if (complete) {
+                        __threadfence();
+                        if (!(st & ST_ABORT))
+                            for (int i = 64 * grp + lane; i < 64 * grp + 64; i += 32) {
+                                float f = 0.0f;
+                                for (int q = 0; q < k; q++)
+                                    f = __fadd_rn(f, __fmul_rn(wr[q], __ldcg(a.eo + (size_t)tok * Q +
+                                                                          (size_t)q * D + i)));
+                                if (a.s_out) f = __fadd_rn(f, __fmul_rn(*a.sgate, a.s_out[i]));
+                                a.ffn[(size_t)tok * D + i] = f;
+                                if (a.h) a.h[i] = __fadd_rn(a.h[i], f);
+                            }
+                    }
+                }
+            }
+            __syncwarp();
             if (lane == 0) {
                 cnt[NBUF + tok % NBUF] = 0u;
                 mbar_arrive(&hfree[vb]);
@@ -907,14 +960,19 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                 if (tr && tok == trace_tok(a)) tr[15] = now_ns();
             }
         }
+        if (tr) td += (uint32_t)now_ns() - td0;
     }
-    if (tr && lane == 0) atomicAdd(reinterpret_cast<unsigned long long *>(&tr[16]), (unsigned long long)tw);
+    if (tr && lane == 0) {
+        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 16 : 18]), (unsigned long long)tw);
+        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 17 : 19]), (unsigned long long)tc);
+        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 26 : 27]), (unsigned long long)td);
+    }
     if (tr && t == 0) tr[20] = now_ns();
 }
 
 // ---------------------------------------------------------------------------
 // host side
-using KernelFn = void (*)(const FusedArgs, uint32_t *, uint32_t *, int);
+using KernelFn = void (*)(const FusedArgs, uint32_t *, uint32_t *, int, int);
 
 // W = 1 when D <= 2048 and k * de / 256 <= 32, else 2 (D <= 4096, k * de / 256 <= 64).
 static int pick_width(int D, int de, int k) {
@@ -944,15 +1002,17 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     if (g.n_experts <= 0 || g.n_experts > RT_PER * 32 || g.top_k > MAXK) return TLMG_OK;
     if (g.d_model % 256 || g.d_expert % 256 || g.d_model > 4096) return TLMG_OK;
     f.smem_limit = prop.sharedMemPerBlockOptin;
-    int nslot = 0;
-    for (int ns = 8; ns >= 2; ns--)
-        if (smem_layout(g.d_model, g.d_expert, g.top_k, ns).total + 1024 <= f.smem_limit) {
-            nslot = ns;
+    // stage counts: two gate/up stages, as many down stages as fit (>= 2)
+    int nsB = 0;
+    for (int nb = 4; nb >= 2; nb--)
+        if (smem_layout(g.d_model, g.d_expert, g.top_k, 2, nb).total + 1024 <= f.smem_limit) {
+            nsB = nb;
             break;
         }
-    if (!nslot) return TLMG_OK;
-    f.nslot = nslot;
-    f.smem = smem_layout(g.d_model, g.d_expert, g.top_k, nslot).total;
+    if (!nsB) return TLMG_OK;
+    f.nsA = 2;
+    f.nsB = nsB;
+    f.smem = smem_layout(g.d_model, g.d_expert, g.top_k, 2, nsB).total;
     f.nsm = prop.multiProcessorCount;
     f.D = g.d_model;
     f.de = g.d_expert;
@@ -970,14 +1030,14 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
 }
 
 static void free_tokens(FusedScratch &f) {
-    if (f.xq) cudaFree(f.xq);
-    if (f.hbuf) cudaFree(f.hbuf);
-    if (f.hq) cudaFree(f.hq);
-    if (f.hcnt) cudaFree(f.hcnt);
+    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.hq, (void *)f.hcnt, (void *)f.eo, (void *)f.ocnt })
+        if (p) cudaFree(p);
     f.xq = nullptr;
     f.hbuf = nullptr;
     f.hq = nullptr;
     f.hcnt = nullptr;
+    f.eo = nullptr;
+    f.ocnt = nullptr;
     f.tok_cap = 0;
 }
 
@@ -987,17 +1047,20 @@ static int reserve_tokens(FusedScratch &f, int n_tok) {
     if (n_tok <= f.tok_cap) return TLMG_OK;
     free_tokens(f);
     const int cap = n_tok < 64 ? 64 : n_tok;
-    const int nbx = f.D / 256, nbh = f.k * (f.de / 256);
-    const size_t P = (size_t)f.k * f.de;
+    const int nbx = f.D / 256, nbd = f.de / 256, nbh = f.k * nbd;
+    const size_t P = (size_t)f.k * f.de, Q = (size_t)f.k * f.D;
     if (cudaMalloc(&f.xq, (size_t)cap * qv_bytes(nbx)) != cudaSuccess ||
         cudaMalloc(&f.hbuf, (size_t)cap * P * 4) != cudaSuccess ||
-        cudaMalloc(&f.hq, (size_t)cap * qv_bytes(nbh)) != cudaSuccess ||
-        cudaMalloc(&f.hcnt, (size_t)cap * nbh * 4) != cudaSuccess) {
+        cudaMalloc(&f.hq, (size_t)cap * f.k * qv_bytes(nbd)) != cudaSuccess ||
+        cudaMalloc(&f.hcnt, (size_t)cap * nbh * 4) != cudaSuccess ||
+        cudaMalloc(&f.eo, (size_t)cap * Q * 4) != cudaSuccess ||
+        cudaMalloc(&f.ocnt, (size_t)cap * (f.D / 64) * 4) != cudaSuccess) {
         cudaGetLastError();
         free_tokens(f);
         return set_error(TLMG_ENOMEM, "fused per-token scratch for %d tokens", n_tok);
     }
     cudaMemset(f.hcnt, 0, (size_t)cap * nbh * 4);
+    cudaMemset(f.ocnt, 0, (size_t)cap * (f.D / 64) * 4);
     f.tok_cap = cap;
     return TLMG_OK;
 }
@@ -1010,9 +1073,11 @@ void fused_release(FusedScratch &f) {
     f = FusedScratch{};
 }
 
-// Split of the layer-token's work over the CTAs, in chunks that fit one
-// stage: phase A = (rank, row) pairs [P*c/G, P*(c+1)/G), phase B = output
-// rows [D*c/G, D*(c+1)/G).
+// Split of the layer-token's work over the CTAs (range_lo): phase A
+// (rank, row) pairs, phase B (rank, output row) pairs, each cut per expert
+// into balanced chunks of contiguous rows that fit one stage: a gate/up
+// chunk is one copy of gate rows and one of the same up rows, a down chunk
+// one copy of down rows.
 const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
     if (!f.enabled || !pick_kernel(dgu, ddn, g.d_model, g.d_expert, g.top_k)) return nullptr;
     const FusedPlanKey key{ dgu, ddn };
@@ -1020,65 +1085,50 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
     if (it != f.plans.end()) return it->second;
     const int D = g.d_model, de = g.d_expert, k = g.top_k, G = f.nsm;
     const int rbg = D / 256 * dt_block_bytes(dgu), rbd = de / 256 * dt_block_bytes(ddn);
-    if (2 * rbg + 96 > SLOT_BYTES || k * (rbd + 48) > SLOT_BYTES) return nullptr;
-    if (k > 32) return nullptr;   // phase B: lane r runs expert r's chain
+    const int capA = (SLOT_A / 2 - 15) / rbg, capB = (SLOT_B - 15) / rbd;
+    if (capA < 1 || capB < 1) return nullptr;
+    if (de / 256 > 32) return nullptr;   // phase B: a row's blocks fit one warp
+    if (G < 64) return nullptr;          // per-CTA ranges sized for >= 64 CTAs
     if (g.n_experts > RT_PER * 32 || k > MAXK) return nullptr;
     std::vector<int2> counts(G);
     std::vector<ChunkDesc> descs((size_t)G * MAXCH);
+    const int64_t P = (int64_t)k * de, Q = (int64_t)k * D;
     for (int c = 0; c < G; c++) {
         ChunkDesc *out = &descs[(size_t)c * MAXCH];
         int n = 0;
-        const int64_t P = (int64_t)k * de, p0 = P * c / G, p1 = P * (c + 1) / G;
-        // phase A chunks hold whole work items (8 row pairs) where a stage can
-        const int fitA = (SLOT_BYTES - 96) / (2 * rbg), capA = fitA >= 8 ? fitA & ~7 : fitA;
-        for (int64_t p = p0; p < p1;) {
-            if (n == MAXCH) return nullptr;
-            const int r = (int)(p / de), j = (int)(p % de);
-            const int nr = (int)std::min<int64_t>(std::min<int64_t>(capA, p1 - p), de - j);
-            ChunkDesc d{};
-            d.phase = 0;
-            d.rank = (uint8_t)r;
-            d.nrows = (uint16_t)nr;
-            d.row0 = (uint32_t)j;
-            uint32_t off = 0;
-            for (int m = 0; m < 2; m++) {
-                const uint64_t start = (uint64_t)j * rbg, lo = start & ~15ull;
-                const uint64_t hi = (start + (uint64_t)nr * rbg + 15) & ~15ull;
-                d.lo[m] = (uint32_t)lo;
-                d.size[m] = (uint32_t)(hi - lo);
-                d.dst[m] = (uint16_t)off;
-                d.roff[m] = (uint16_t)(start - lo);
-                off = up16(off + d.size[m]);
+        for (int ph = 0; ph < 2; ph++) {
+            const int64_t N = ph == 0 ? P : Q, len = ph == 0 ? de : D;
+            const int64_t lo = range_lo(N, c, G), hi = range_lo(N, c + 1, G);
+            const int cap = ph == 0 ? capA : capB, rbytes = ph == 0 ? rbg : rbd;
+            for (int64_t p = lo; p < hi;) {
+                const int r = (int)(p / len), j0 = (int)(p % len);
+                const int seg = (int)std::min<int64_t>(hi - p, len - j0);   // rows of expert r
+                const int nch = (seg + cap - 1) / cap, per = (seg + nch - 1) / nch;
+                for (int j = j0; j < j0 + seg; j += per) {
+                    if (n == MAXCH) return nullptr;
+                    const int nr = std::min(per, j0 + seg - j);
+                    ChunkDesc d{};
+                    d.phase = (uint8_t)ph;
+                    d.rank = (uint8_t)r;
+                    d.nrows = (uint16_t)nr;
+                    d.row0 = (uint32_t)j;
+                    const uint64_t start = (uint64_t)j * rbytes, a0 = start & ~15ull;
+                    const uint64_t a1 = (start + (uint64_t)nr * rbytes + 15) & ~15ull;
+                    for (int m = 0; m < (ph == 0 ? 2 : 1); m++) {
+                        d.lo[m] = (uint32_t)a0;
+                        d.size[m] = (uint32_t)(a1 - a0);
+                        d.dst[m] = (uint16_t)(m * (SLOT_A / 2));
+                        d.roff[m] = (uint16_t)(start - a0);
+                    }
+                    if (d.size[0] > (uint32_t)(ph == 0 ? SLOT_A / 2 : SLOT_B)) return nullptr;
+                    d.tx = ph == 0 ? 2 * d.size[0] : d.size[0];
+                    out[n++] = d;
+                }
+                p += seg;
             }
-            if (off > (uint32_t)SLOT_BYTES) return nullptr;
-            d.tx = d.size[0] + d.size[1];
-            out[n++] = d;
-            p += nr;
+            if (ph == 0) counts[c].x = n;
         }
-        const int nA = n;
-        const int i0 = (int)((int64_t)D * c / G), i1 = (int)((int64_t)D * (c + 1) / G);
-        // phase B chunks hold whole work items (32 / k rows) where a stage can
-        const int fitB = (SLOT_BYTES - 48 * k) / (k * rbd), rpi = 32 / k;
-        const int capB = fitB >= rpi ? fitB - fitB % rpi : fitB;
-        for (int i = i0; i < i1;) {
-            if (n == MAXCH) return nullptr;
-            const int nr = std::min(capB, i1 - i);
-            ChunkDesc d{};
-            d.phase = 1;
-            d.nrows = (uint16_t)nr;
-            d.row0 = (uint32_t)i;
-            const uint64_t start = (uint64_t)i * rbd, lo = start & ~15ull;
-            const uint64_t hi = (start + (uint64_t)nr * rbd + 15) & ~15ull;
-            d.lo[0] = (uint32_t)lo;
-            d.size[0] = (uint32_t)(hi - lo);
-            d.dst[0] = (uint16_t)up16(d.size[0]);
-            d.roff[0] = (uint16_t)(start - lo);
-            if ((uint32_t)k * d.dst[0] > (uint32_t)SLOT_BYTES) return nullptr;
-            d.tx = (uint32_t)k * d.size[0];
-            out[n++] = d;
-            i += nr;
-        }
-        counts[c] = make_int2(nA, n - nA);
+        counts[c].y = n - counts[c].x;
     }
     KernelFn kf = pick_kernel(dgu, ddn, D, de, k);
     if (cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)f.smem) != cudaSuccess) {
@@ -1123,9 +1173,11 @@ int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
     la.hbuf = f.hbuf;
     la.hq = f.hq;
     la.hcnt = f.hcnt;
+    la.eo = f.eo;
+    la.ocnt = f.ocnt;
     la.bar_base = f.rounds;
     la.xbar_target = (f.launches + 1) * (uint64_t)f.nsm;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kf, la, f.bar, f.err_dev, f.nslot);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kf, la, f.bar, f.err_dev, f.nsA, f.nsB);
     count_launch();
     if (e != cudaSuccess) return cuda_fail(e, "fused expert FFN launch");
     f.rounds += (uint64_t)a.n_tok;   // every CTA arrives once per token
@@ -1142,6 +1194,7 @@ uint32_t fused_take_error(FusedScratch &f) {
         *(volatile uint32_t *)f.err_host = 0;
         cudaMemset(f.bar, 0, 64);
         if (f.hcnt) cudaMemset(f.hcnt, 0, (size_t)f.tok_cap * f.k * (f.de / 256) * 4);
+        if (f.ocnt) cudaMemset(f.ocnt, 0, (size_t)f.tok_cap * (f.D / 64) * 4);
         f.rounds = 0;
         f.launches = 0;
     }

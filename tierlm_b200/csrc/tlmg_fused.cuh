@@ -19,13 +19,12 @@ struct Slot {
     int32_t ok;
 };
 
-// One chunk of a CTA's work: rows of the selected experts' matrices that one
-// shared-memory stage holds. Phase A: `nrows` (gate, up) row pairs of rank
-// `rank` starting at row `row0`, two copies (gate, up). Phase B: `nrows`
-// output rows starting at `row0`, one copy per rank from its down matrix,
-// rank r's copy at stage offset r * dst[0]. Offsets are relative to each
-// matrix's base, which is 256-byte aligned, so one plan serves every choice
-// of experts of the same dtypes.
+// One chunk of a CTA's work: contiguous rows of one selected expert's
+// matrices that one shared-memory stage holds. Phase A: `nrows` (gate, up)
+// row pairs of rank `rank` starting at row `row0`, two copies (gate at
+// dst[0], up at dst[1]). Phase B: `nrows` rows of rank `rank`'s down matrix
+// starting at row `row0`, one copy. Offsets are relative to each matrix's
+// base, so one plan serves every choice of experts of the same dtypes.
 struct ChunkDesc {
     uint8_t phase, rank;
     uint16_t nrows;
@@ -53,7 +52,7 @@ struct FusedScratch {
     uint32_t *err_host = nullptr;  // mapped pinned word: error bits set by the kernel
     uint32_t *err_dev = nullptr;   // its device alias
     int nsm = 0;                   // CTAs = SMs (one persistent CTA per SM)
-    int nslot = 0;                 // shared-memory stage ring depth
+    int nsA = 0, nsB = 0;          // gate/up and down stages in shared memory
     uint64_t rounds = 0;           // grid-barrier rounds (tokens) launched since the barrier words were reset
     uint64_t launches = 0;         // launches since the barrier words were reset
     // per-token global scratch of a launch, for up to tok_cap tokens
@@ -62,6 +61,8 @@ struct FusedScratch {
     float *hbuf = nullptr;         // [tok_cap][k * de] SwiGLU rows
     uint8_t *hq = nullptr;         // [tok_cap][quantised h]
     uint32_t *hcnt = nullptr;      // [tok_cap][k * de / 256] rows written per h block (zero between launches)
+    float *eo = nullptr;           // [tok_cap][k * D] expert outputs
+    uint32_t *ocnt = nullptr;      // [tok_cap][D / 64] expert outputs written per 64-row group (zero between launches)
     int D = 0, de = 0, k = 0;
     size_t smem = 0;               // dynamic shared memory per CTA
     size_t smem_limit = 0;
@@ -91,8 +92,10 @@ struct FusedArgs {
     // filled by launch_fused_ffn from the FusedScratch:
     uint8_t *xq;                   // [n_tok] quantised inputs
     float *hbuf;                   // [n_tok][k * de] SwiGLU rows (cross-CTA exchange)
-    uint8_t *hq;                   // [n_tok] quantised h
+    uint8_t *hq;                   // [n_tok][k] quantised h per expert
     uint32_t *hcnt;                // [n_tok][k * de / 256] h block row counts
+    float *eo;                     // [n_tok][k * D] expert outputs (cross-CTA combine)
+    uint32_t *ocnt;                // [n_tok][D / 64] output group counts
     int D, de, E, k, router;
     float routed_scale;
     int dt_gu, dt_dn;              // dtype of every gate/up and every down matrix of the layers
