@@ -189,6 +189,9 @@ int tlmg_check(tlmg_ctx *ctx);
  *   [20] launch end
  *   [21] x copy issued  [22] / [23] first / last gate/up chunk issued
  *   [24] / [25] first / last down chunk issued
+ *   [26] / [27] gate/up / down warps' summed ns in token duties
+ *   [28] x copy issued, [29] barrier arrival, [30] h fetch issued and
+ *        [31] down done for token n_tok / 2 + 1
  * Copies up to `cap` values of the last launch ([CTA][TLMG_TRACE_POINTS]) to
  * `out` (host) and returns how many; on = 0 stops tracing. */
 #define TLMG_TRACE_POINTS 32

@@ -42,9 +42,9 @@
 
 namespace tlmg {
 
-constexpr int NCW = 16;                 // consumer warps; warp NCW streams, warp NCW + 1 routes
-constexpr int NAW = 10;                 // consumer warps [0, NAW) take gate/up items, the others down items
-constexpr int NTHREADS = 32 * (NCW + 2);
+constexpr int NCW = 16;                 // consumer warps; warp NCW streams, NCW + 1 routes, NCW + 2 / NCW + 3 do duties
+constexpr int NAW = 8;                  // consumer warps [0, NAW) process gate/up chunks, the others down chunks
+constexpr int NTHREADS = 32 * (NCW + 4);   // + stream, router and two duty warps
 constexpr int MAXCH = FUSED_MAXCH;
 constexpr int MAXK = 16;
 constexpr int SLOT_A = 50176;   // gate/up stage: the gate rows and the up rows of a chunk, half each
@@ -315,6 +315,103 @@ __device__ __forceinline__ void kblock_dot_q6(const uint8_t *const (&w)[NM], con
     }
 }
 
+// The exact partials of half `half` (elements 128 half .. 128 half + 127)
+// of one weight block of dtype DT against activation block x: the block's
+// is / ms are the sums of its two halves' (integer addition is exact), its
+// dA / dM are the same for both halves.
+template <int DT>
+__device__ __forceinline__ void kblock_half(const uint8_t *w, const XBlk &x, int half, BlockSum &o) {
+    const uint4 bv = lds128(reinterpret_cast<const uint8_t *>(x.bs) + 16 * half);   // bsums 8 half .. 8 half + 7
+    const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
+    if constexpr (DT == DT_Q6_K) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(w);
+        const uint32_t *wp = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(a & 3u) * 8u;   // 0 or 16
+        const int h = half;
+        int dot[8];   // group 8h + 2mm + p at index 2mm + p
+#pragma unroll
+        for (int i = 0; i < 8; i++) dot[i] = 0;
+#pragma unroll
+        for (int p = 0; p < 2; p++) {
+            uint4 xv[4];
+#pragma unroll
+            for (int mm = 0; mm < 4; mm++) xv[mm] = xpiece(x, 8 * h + 2 * mm + p);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int lw = 4 * p + i;
+                const int ja = 16 * h + lw, jb = 16 * h + 8 + lw, jc = 32 + 8 * h + lw;
+                const uint32_t A = __funnelshift_r(wp[ja], wp[ja + 1], sh);
+                const uint32_t B = __funnelshift_r(wp[jb], wp[jb + 1], sh);
+                const uint32_t Cq = __funnelshift_r(wp[jc], wp[jc + 1], sh);
+                const uint32_t u0 = (A & 0x0F0F0F0Fu) | ((Cq << 4) & 0x30303030u);
+                const uint32_t u1 = (B & 0x0F0F0F0Fu) | ((Cq << 2) & 0x30303030u);
+                const uint32_t u2 = ((A >> 4) & 0x0F0F0F0Fu) | (Cq & 0x30303030u);
+                const uint32_t u3 = ((B >> 4) & 0x0F0F0F0Fu) | ((Cq >> 2) & 0x30303030u);
+                dot[0 + p] = dp4(u0, wsel(xv[0], i), dot[0 + p]);
+                dot[2 + p] = dp4(u1, wsel(xv[1], i), dot[2 + p]);
+                dot[4 + p] = dp4(u2, wsel(xv[2], i), dot[4 + p]);
+                dot[6 + p] = dp4(u3, wsel(xv[3], i), dot[6 + p]);
+            }
+        }
+        const uint32_t s0 = __funnelshift_r(wp[48 + 2 * h], wp[49 + 2 * h], sh);
+        const uint32_t s1 = __funnelshift_r(wp[49 + 2 * h], wp[50 + 2 * h], sh);
+        int is = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int sc = (int)(int8_t)byte_of(i < 4 ? s0 : s1, i & 3);
+            const int bs = (int)(int16_t)((bw[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
+            is += sc * (dot[i] - 32 * bs);
+        }
+        o.is = is;
+        o.ms = 0;
+        o.dA = __fmul_rn(h2f(__funnelshift_r(wp[52], wp[53], sh) & 0xFFFFu), x.d);
+        o.dM = 0.0f;
+    } else {
+        constexpr int QOFF = DT == DT_Q4_K ? 16 : 48;
+        const uint4 hd = lds128(w);
+        const uint32_t sc03 = hd.y & 0x3F3F3F3Fu, mn03 = hd.z & 0x3F3F3F3Fu;
+        const uint32_t sc47 = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+        const uint32_t mn47 = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+        const uint32_t sw = half ? sc47 : sc03, mw = half ? mn47 : mn03;   // sub-blocks 4 half .. 4 half + 3
+        o.dA = __fmul_rn(h2f(hd.x & 0xFFFFu), x.d);
+        o.dM = __fmul_rn(h2f(hd.x >> 16), x.d);
+        o.ms = (int)byte_of(mw, 0) * hsum16(bw[0]) + (int)byte_of(mw, 1) * hsum16(bw[1]) +
+               (int)byte_of(mw, 2) * hsum16(bw[2]) + (int)byte_of(mw, 3) * hsum16(bw[3]);
+        uint4 g0 = make_uint4(0u, 0u, 0u, 0u), g1 = g0;
+        if constexpr (DT == DT_Q5_K) {
+            g0 = lds128(w + 16);
+            g1 = lds128(w + 32);
+        }
+        int is = 0;
+#pragma unroll
+        for (int qq = 0; qq < 2; qq++) {
+            const int q = 2 * half + qq;
+            const uint4 xl0 = xpiece(x, 4 * q), xl1 = xpiece(x, 4 * q + 1);
+            const uint4 xh0 = xpiece(x, 4 * q + 2), xh1 = xpiece(x, 4 * q + 3);
+            const uint4 v0 = lds128(w + QOFF + 32 * q), v1 = lds128(w + QOFF + 32 * q + 16);
+            int lo = 0, hi = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t qw = wsel(i < 4 ? v0 : v1, i & 3);
+                const uint32_t xlw = wsel(i < 4 ? xl0 : xl1, i & 3), xhw = wsel(i < 4 ? xh0 : xh1, i & 3);
+                if constexpr (DT == DT_Q4_K) {
+                    lo = dp4(qw & 0x0F0F0F0Fu, xlw, lo);
+                    hi = dp4us(qw & 0xF0F0F0F0u, xhw, hi);
+                } else {
+                    const uint32_t hw = wsel(i < 4 ? g0 : g1, i & 3);
+                    const uint32_t l5 = (qw & 0x0F0F0F0Fu) | (((hw >> (2 * q)) & 0x01010101u) << 4);
+                    const uint32_t h5 = ((qw >> 4) & 0x0F0F0F0Fu) | (((hw >> (2 * q + 1)) & 0x01010101u) << 4);
+                    lo = dp4(l5, xlw, lo);
+                    hi = dp4(h5, xhw, hi);
+                }
+            }
+            if constexpr (DT == DT_Q4_K) hi >>= 4;
+            is += (int)byte_of(sw, 2 * qq) * lo + (int)byte_of(sw, 2 * qq + 1) * hi;
+        }
+        o.is = is;
+    }
+}
+
 template <int DT, int NM>
 __device__ __forceinline__ void kblock_dot(const uint8_t *const (&w)[NM], const XBlk &x, BlockSum (&o)[NM]) {
     if constexpr (DT == DT_Q6_K) kblock_dot_q6<NM>(w, x, o);
@@ -396,15 +493,30 @@ __device__ __forceinline__ void quant_block(const float4 &v0, const float4 &v1, 
 __host__ __device__ inline int range_lo(int64_t n, int c, int G) { return (int)(n * c / G); }
 // Pairs one CTA owns at most, for grids of >= 64 CTAs.
 __host__ __device__ inline int range_max(int64_t n) { return (int)((n + 63) / 64 + 1); }
+// Phase B split: expert rank r gets the CTAs [G r / k, G (r+1) / k) (G >= k),
+// which split its D rows evenly; returns the first (rank, row) pair
+// r * D + i of CTA c (c = G: k * D). Every CTA reads rows of one expert.
+__host__ __device__ inline int qrange_lo(int c, int G, int k, int D) {
+    if (c >= G) return k * D;
+    int r = 0;
+    while (r + 1 < k && (int)((int64_t)G * (r + 1) / k) <= c) r++;
+    const int c0 = (int)((int64_t)G * r / k), c1 = (int)((int64_t)G * (r + 1) / k);
+    return r * D + (int)((int64_t)D * (c - c0) / (c1 - c0));
+}
 
 // ---------------------------------------------------------------------------
 // shared-memory layout: nsA gate/up stages of SLOT_A bytes, nsB down stages
 // of SLOT_B bytes, then the small state
-constexpr int NBUF = 4;   // routing / staging buffers, by token % NBUF
+constexpr int NBUF = 8;   // routing / staging buffers, by token % NBUF (tokens in flight)
+constexpr int NX = 3;     // quantised-x buffers, by token % NX
 struct SmemLayout {
-    uint32_t stageA, stageB, full, empty, seq, done, xs, xfull, xfree, xseq, hs, hfull, hfree, hseq, routed, idsfree,
-        ids, w, sl, rscr, cnt, hrow, erow, desc, ipre, misc, total;
+    uint32_t stageA, stageB, full, empty, seq, xs, xfull, xfree, xseq, hraw, hs, hfull, hfree, hseq, routed, idsfree,
+        adone, bdone, ids, w, sl, rscr, partA, partB, desc, misc, total;
 };
+// Rows one gate/up stage (one down stage) holds at most, for rows of nb
+// blocks of the smallest K-quant block (144 bytes).
+__host__ __device__ inline int capA_rows(int nbx) { return (SLOT_A / 2 - 15) / (nbx * 144); }
+__host__ __device__ inline int capB_rows(int nbd) { return (SLOT_B - 15) / (nbd * 144); }
 __host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nsA, int nsB) {
     SmemLayout L;
     uint32_t o = 0;
@@ -414,26 +526,28 @@ __host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nsA,
     L.full = o; o += 8u * ns;
     L.empty = o; o += 8u * ns;
     L.seq = o; o += 4u * ns;
-    L.done = o = (o + 7u) & ~7u; o += 4u * ns;
-    L.xfull = o = (o + 7u) & ~7u; o += 16u;
-    L.xfree = o; o += 16u;
+    L.xfull = o = (o + 7u) & ~7u; o += 8u * NX;
+    L.xfree = o; o += 8u * NX;
     L.hfull = o; o += 16u;
     L.hfree = o; o += 16u;
     L.routed = o; o += 8u * NBUF;
     L.idsfree = o; o += 8u * NBUF;
-    L.xseq = o; o += 8u;
+    L.adone = o; o += 8u * NBUF;
+    L.bdone = o; o += 8u * NBUF;
+    L.xseq = o; o += 4u * NX;
     L.hseq = o; o += 8u;
-    L.xs = o = up16(o); o += 2u * qv_bytes(nbx);
-    L.hs = o = up16(o); o += 2u * 2u * qv_bytes(nbd);   // [2][two experts]
+    L.xs = o = up16(o); o += (uint32_t)NX * qv_bytes(nbx);
+    L.hraw = o = up16(o); o += 2u * 4u * (uint32_t)de;        // [two experts][de] h rows of the down experts
+    L.hs = o = up16(o); o += 2u * qv_bytes(nbd);              // [two experts] the same, quantised
     L.rscr = o = up16(o); o += 4u * (uint32_t)RT_SCRATCH;
-    L.ids = o; o += 4u * 64 * NBUF;
-    L.w = o; o += 4u * 64 * NBUF;
+    L.ids = o; o += 4u * MAXK * NBUF;
+    L.w = o; o += 4u * MAXK * NBUF;
     L.sl = o = up16(o); o += (uint32_t)sizeof(Slot) * MAXK * NBUF;
-    L.cnt = o = up16(o); o += 4u * (2 * NBUF + 2);
-    L.hrow = o = up16(o); o += 4u * (uint32_t)NBUF * (uint32_t)range_max((int64_t)k * de);
-    L.erow = o = up16(o); o += 4u * (uint32_t)NBUF * (uint32_t)range_max((int64_t)k * D);
+    // partial sums of a chunk's units, double-buffered: gate/up [2][2 rows][nbx + 1] (block units),
+    // down [2][rows][2 nbd + 1] (half-block units)
+    L.partA = o = up16(o); o += 16u * 2u * 2u * (uint32_t)capA_rows(nbx) * (uint32_t)(nbx + 1);
+    L.partB = o = up16(o); o += 16u * 2u * (uint32_t)capB_rows(nbd) * (uint32_t)(2 * nbd + 1);
     L.desc = o = up16(o); o += (uint32_t)sizeof(ChunkDesc) * MAXCH;
-    L.ipre = o; o += 4u * (MAXCH + 2);
     L.misc = o = up16(o); o += 64;
     L.total = o;
     return L;
@@ -441,19 +555,20 @@ __host__ __device__ inline SmemLayout smem_layout(int D, int de, int k, int nsA,
 
 // Grid barriers: token number gt (counted since the host last reset the
 // words; a launch's token t is gt = bar_base + t) uses the 64-bit arrival
-// word gt % NBUF at bar + 4, which every CTA increments once per token when
+// word gt % NBUF at bar + 8, which every CTA increments once per token when
 // its gate/up rows of the token are written, so barrier gt is complete at
 // (gt / NBUF + 1) * gridDim.x arrivals. A CTA arrives for token gt + NBUF
 // only after its router released the routing buffer of token gt, i.e.
 // after its down phase of token gt, which follows barrier gt: one word per
-// token in flight keeps the counts exact. The word at bar + 12 counts the
+// token in flight keeps the counts exact. The word at bar + 4 counts the
 // CTAs that quantised their share of the launch's inputs.
 __device__ __forceinline__ unsigned long long *barrier_word(uint32_t *bar, uint64_t gt) {
-    return reinterpret_cast<unsigned long long *>(bar + 4) + (gt % NBUF);
+    return reinterpret_cast<unsigned long long *>(bar + 8) + (gt % NBUF);
 }
 __device__ __forceinline__ unsigned long long *xbar_word(uint32_t *bar) {
-    return reinterpret_cast<unsigned long long *>(bar + 12);
+    return reinterpret_cast<unsigned long long *>(bar + 4);
 }
+constexpr int BAR_BYTES = 32 + 8 * NBUF;   // [2] sticky error, xbar word, barrier words
 // Wait until *w >= target, for at most BARRIER_NS; polls with a short sleep
 // so that a waiting lane takes few issue slots from the warps computing.
 __device__ __forceinline__ bool grid_wait(const unsigned long long *w, uint64_t target) {
@@ -491,74 +606,6 @@ __device__ __forceinline__ uint64_t *trace_row(const FusedArgs &a) {
 }
 
 // ---------------------------------------------------------------------------
-// One phase-A work item: four (gate, up) row pairs. Lane (p, j) =
-// (lane / 8, lane % 8) owns row pair p (gate row at grow, up row at urow,
-// valid or not) and blocks j, j + 8, ... of both rows: it computes their
-// exact partials (the 8 lanes of a quarter warp read 8 consecutive blocks
-// of one row: 8 different banks). Then the gate and up fmaf chains run over
-// the blocks in ascending order: the lane holding block b applies it and
-// the accumulators are passed on by shuffle. Returns silu(gate) * up on
-// every lane of the row pair.
-template <int DGU, int BPL>
-__device__ __forceinline__ float a_item(const uint8_t *grow, const uint8_t *urow, bool valid, const QVec &x, int nbx,
-                                        int lane) {
-    const int j = lane & 7;
-    BlockSum vg[BPL], vu[BPL];
-#pragma unroll
-    for (int i = 0; i < BPL; i++) {
-        const int b = j + 8 * i;
-        vg[i] = BlockSum{ 0, 0, 0.f, 0.f };
-        vu[i] = vg[i];
-        if (valid && b < nbx) {
-            const uint8_t *wb[2] = { grow + b * dt_block_bytes(DGU), urow + b * dt_block_bytes(DGU) };
-            BlockSum o2[2];
-            kblock_dot<DGU, 2>(wb, XBlk{ x.codes, nbx, b, x.bs + 16 * b, x.d[b] }, o2);
-            vg[i] = o2[0];
-            vu[i] = o2[1];
-        }
-    }
-    float ag = 0.0f, au = 0.0f;
-    const int base = lane & ~7;
-#pragma unroll
-    for (int i = 0; i < BPL; i++)
-#pragma unroll
-        for (int h = 0; h < 8; h++) {
-            if (h + 8 * i >= nbx) break;
-            if (j == h) {
-                ag = chain<DGU>(ag, vg[i].dA, vg[i].is, vg[i].dM, vg[i].ms);
-                au = chain<DGU>(au, vu[i].dA, vu[i].is, vu[i].dM, vu[i].ms);
-            }
-            ag = __shfl_sync(0xFFFFFFFFu, ag, base | h);
-            au = __shfl_sync(0xFFFFFFFFu, au, base | h);
-        }
-    return __fmul_rn(silu_f(ag), au);
-}
-
-// One phase-B work item: 32 / nbd rows of one expert's down matrix. Lane
-// (g, b) = (lane / nbd, lane % nbd) owns block b of row g (at row0, valid
-// or not) and computes its exact partials against the expert's h; the
-// row's fmaf chain runs over the blocks in ascending order, the lane
-// holding block b applying it and passing the accumulator on by shuffle.
-// Returns the row's expert output eo on every lane of the row.
-template <int DDN>
-__device__ __forceinline__ float b_item(const uint8_t *row, bool valid, const QVec &h, int nbd, int lane) {
-    const int g = lane / nbd, b = lane - g * nbd;
-    BlockSum v = BlockSum{ 0, 0, 0.f, 0.f };
-    if (valid) {
-        const uint8_t *wb[1] = { row + b * dt_block_bytes(DDN) };
-        BlockSum o1[1];
-        kblock_dot<DDN, 1>(wb, XBlk{ h.codes, nbd, b, h.bs + 16 * b, h.d[b] }, o1);
-        v = o1[0];
-    }
-    float eo = 0.0f;
-    const int gb = g * nbd < 32 - nbd + 1 ? g * nbd : 0;
-    for (int hh = 0; hh < nbd; hh++) {
-        if (b == hh) eo = chain<DDN>(eo, v.dA, v.is, v.dM, v.ms);
-        eo = __shfl_sync(0xFFFFFFFFu, eo, gb + hh);
-    }
-    return eo;
-}
-
 // ---------------------------------------------------------------------------
 // The persistent kernel. One CTA per SM: warps 0..NCW-1 consume work items,
 // warp NCW streams (lane 0: the tokens' x and gate/up chunks; lane 1: each
@@ -569,23 +616,21 @@ __device__ __forceinline__ float b_item(const uint8_t *row, bool valid, const QV
 //                 (n_tok x D / 256 blocks) into a.xq; one grid-wide count.
 //   router        routes token t into buffer t % NBUF once the CTA is done
 //                 with token t - NBUF.
-//   work items    gate/up warps [0, NAW) and down warps [NAW, NCW) take the
-//                 next item of their kind (shared counters, token order) and
-//                 wait only for what the item reads: its chunk (the
-//                 stage's sequence word names the chunk it is armed for)
-//                 and the token's x or h. A stage is released when its
-//                 chunk's last item is done. Items stage their results
-//                 (h rows, expert outputs) in shared memory.
-//   token A done  the warp finishing the CTA's last gate/up item of a token
-//                 writes the CTA's h rows, adds them to the counts of the h
-//                 blocks they belong to (the CTA completing a block
-//                 quantises it into a.hq) and arrives at the token's grid
-//                 barrier.
-//   token B done  the warp finishing the CTA's last down item writes the
-//                 CTA's expert outputs, adds them to the counts of the
-//                 64-row groups they belong to (the CTA completing a group
-//                 runs its rank-ordered combine) and frees the token's h
-//                 and routing buffers.
+//   chunks        gate/up warps [0, NAW) and down warps [NAW, NCW) process
+//                 their kind of chunk in token order (the stage's sequence
+//                 word names the chunk it is armed for): one (row, block)
+//                 unit per thread into shared partials, a group barrier
+//                 that releases the stage, then one thread per row runs the
+//                 row's chains and stages the result (h row, expert output)
+//                 in shared memory.
+//   token A done  warp 0 writes the CTA's h rows of the token, adds them to
+//                 the counts of the h blocks they belong to (the CTA
+//                 completing a block quantises it into a.hq) and arrives at
+//                 the token's grid barrier.
+//   token B done  warp NAW writes the CTA's expert outputs, adds them to
+//                 the counts of the 64-row groups they belong to (the CTA
+//                 completing a group runs its rank-ordered combine) and
+//                 frees the token's routing buffer.
 //
 // Every wait is bounded; on expiry the kernel raises an error bit the host
 // reads and stops waiting (results of the launch are invalid).
@@ -595,30 +640,28 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
             int nsB) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int D = a.D, de = a.de, k = a.k, E = a.E, n = a.n_tok;
-    const int nbx = D / 256, nbd = de / 256, nbh = k * nbd;
+    const int nbx = D / 256, nbd = de / 256;
     const SmemLayout L = smem_layout(D, de, k, nsA, nsB);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.full);
     uint64_t *empty = reinterpret_cast<uint64_t *>(smem + L.empty);
     uint32_t *seq = reinterpret_cast<uint32_t *>(smem + L.seq);
-    uint32_t *done = reinterpret_cast<uint32_t *>(smem + L.done);
     uint64_t *xfull = reinterpret_cast<uint64_t *>(smem + L.xfull);
     uint64_t *xfree = reinterpret_cast<uint64_t *>(smem + L.xfree);
     uint64_t *hfull = reinterpret_cast<uint64_t *>(smem + L.hfull);
     uint64_t *hfree = reinterpret_cast<uint64_t *>(smem + L.hfree);
     uint64_t *routed = reinterpret_cast<uint64_t *>(smem + L.routed);
     uint64_t *idsfree = reinterpret_cast<uint64_t *>(smem + L.idsfree);
-    uint32_t *xseq = reinterpret_cast<uint32_t *>(smem + L.xseq);   // [2]: token in xs[i]
-    uint32_t *hseq = reinterpret_cast<uint32_t *>(smem + L.hseq);   // [2]: token in hs[i]
-    // [NBUF] A items done and [NBUF] B items done by token, then the next A / B item to take
-    uint32_t *cnt = reinterpret_cast<uint32_t *>(smem + L.cnt);
+    uint64_t *adone = reinterpret_cast<uint64_t *>(smem + L.adone);   // [NBUF] the CTA's gate/up results of a token staged
+    uint64_t *bdone = reinterpret_cast<uint64_t *>(smem + L.bdone);   // [NBUF] the CTA's down results of a token staged
+    uint32_t *xseq = reinterpret_cast<uint32_t *>(smem + L.xseq);   // [NX]: token in xs[i]
+    uint32_t *hseq = reinterpret_cast<uint32_t *>(smem + L.hseq);   // [2]: token in hraw[i]
     ChunkDesc *desc = reinterpret_cast<ChunkDesc *>(smem + L.desc);
-    int *ipre = reinterpret_cast<int *>(smem + L.ipre);   // [0..nA] A item prefix, [nA+1..nA+nB+1] B item prefix
     Slot *slb = reinterpret_cast<Slot *>(smem + L.sl);     // [NBUF][MAXK] selected experts
-    int *misc = reinterpret_cast<int *>(smem + L.misc);    // [0] IA, [1] IB, [3] sticky error seen
+    int *misc = reinterpret_cast<int *>(smem + L.misc);    // [3] sticky error seen
     const uint32_t qvx = qv_bytes(nbx), qvd = qv_bytes(nbd);
     const int64_t P = (int64_t)k * de, Q = (int64_t)k * D;
     const int p0 = range_lo(P, blockIdx.x, gridDim.x), p1 = range_lo(P, blockIdx.x + 1, gridDim.x);
-    const int q0 = range_lo(Q, blockIdx.x, gridDim.x), q1 = range_lo(Q, blockIdx.x + 1, gridDim.x);
+    const int q0 = qrange_lo(blockIdx.x, gridDim.x, k, D), q1 = qrange_lo(blockIdx.x + 1, gridDim.x, k, D);
     const int rq0 = q0 / D;   // first expert rank of the CTA's down rows
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
@@ -629,7 +672,7 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     }
 
     // ---- prologue: the plan (same for every token: nA gate/up chunks, then
-    // nB down chunks), the barriers, the item prefix tables
+    // nB down chunks) and the barriers
     const int2 *plan_n = reinterpret_cast<const int2 *>(a.plan);
     const ChunkDesc *plan_d = reinterpret_cast<const ChunkDesc *>(plan_n + gridDim.x) + (size_t)blockIdx.x * MAXCH;
     const int2 cnt_pl = plan_n[blockIdx.x];
@@ -638,51 +681,36 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     constexpr int DW = (int)(sizeof(ChunkDesc) / 8);
     if (plan_ok && t < (nA + nB) * DW) reinterpret_cast<uint2 *>(desc)[t] = reinterpret_cast<const uint2 *>(plan_d)[t];
     const int ns = nsA + nsB;
-    if (t < ns) {
-        seq[t] = 0xFFFFFFFFu;
-        done[t] = 0u;
-    }
-    if (t < 2 * NBUF + 2) cnt[t] = 0u;
-    if (t < 2) {
-        xseq[t] = 0xFFFFFFFFu;
-        hseq[t] = 0xFFFFFFFFu;
-    }
+    if (t < ns) seq[t] = 0xFFFFFFFFu;
+    if (t < NX) xseq[t] = 0xFFFFFFFFu;
+    if (t < 2) hseq[t] = 0xFFFFFFFFu;
     if (t == 0) {
         for (int s = 0; s < ns; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < NX; i++) {
             mbar_init(&xfull[i], 1);
             mbar_init(&xfree[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
             mbar_init(&hfull[i], 1);
             mbar_init(&hfree[i], 1);
         }
         for (int b = 0; b < NBUF; b++) {
             mbar_init(&routed[b], 1);
             mbar_init(&idsfree[b], 1);
+            mbar_init(&adone[b], 1);
+            mbar_init(&bdone[b], 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         misc[3] = ld_acquire(&bar[2]) != 0;   // an earlier launch failed: do nothing until reset
-    }
-    __syncthreads();
-    if (t == 0 && plan_ok) {
-        const int rb = 32 / nbd;
-        int s = 0;
-        for (int c = 0; c < nA; c++) { ipre[c] = s; s += (desc[c].nrows + 3) >> 2; }
-        ipre[nA] = s;
-        misc[0] = s;
-        s = 0;
-        for (int c = 0; c < nB; c++) { ipre[nA + 1 + c] = s; s += (desc[nA + c].nrows + rb - 1) / rb; }
-        ipre[nA + 1 + nB] = s;
-        misc[1] = s;
     }
     __syncthreads();
     if (misc[3] || !plan_ok) {
         if (t == 0) raise_error(err, bar, misc[3] ? FUSED_ERR_BARRIER : FUSED_ERR_PLAN);
         return;   // every CTA sees the same sticky word / plan before any barrier
     }
-    const int IA = misc[0], IB = misc[1];
 
     if (warp == NCW + 1) {
         // ---- router
@@ -694,8 +722,8 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                 break;   // the others time out on what is missing
             }
             const int layer = (a.layer0 + tok) % a.n_layers;
-            int32_t *ids = reinterpret_cast<int32_t *>(smem + L.ids) + 64 * b;
-            float *wr = reinterpret_cast<float *>(smem + L.w) + 64 * b;
+            int32_t *ids = reinterpret_cast<int32_t *>(smem + L.ids) + MAXK * b;
+            float *wr = reinterpret_cast<float *>(smem + L.w) + MAXK * b;
             warp_route(a.router, a.logits + (size_t)tok * E, a.mask_all ? a.mask_all + (size_t)layer * E : nullptr,
                        a.bias_all ? a.bias_all + (size_t)layer * E : nullptr, E, k, a.routed_scale, rscratch, ids, wr,
                        lane);
@@ -742,33 +770,37 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
             const ChunkDesc *dd = isA ? desc : desc + nA;
             const int ne = (q1 - 1) / D - rq0 + 1;   // down experts of the CTA (1 or 2)
             for (int tok = 0; tok < n && !failed; tok++) {
-                const int b = tok % NBUF, vb = tok & 1;
+                const int b = tok % NBUF;
                 const Slot *sl = slb + MAXK * b;
                 if (!mbar_wait(&routed[b], (uint32_t)(tok / NBUF) & 1u)) {
                     failed = true;
                     break;
                 }
                 if (isA) {
-                    if (tok >= 2 && !mbar_wait(&xfree[vb], (uint32_t)((tok >> 1) - 1) & 1u)) {
+                    const int xb = tok % NX;
+                    if (tok >= NX && !mbar_wait(&xfree[xb], (uint32_t)(tok / NX - 1) & 1u)) {
                         failed = true;
                         break;
                     }
-                    mbar_expect_tx(&xfull[vb], qvx);
-                    bulk_g2s(smem + L.xs + vb * qvx, a.xq + (size_t)tok * qvx, qvx, &xfull[vb]);
-                    *reinterpret_cast<volatile uint32_t *>(&xseq[vb]) = (uint32_t)tok;
+                    mbar_expect_tx(&xfull[xb], qvx);
+                    bulk_g2s(smem + L.xs + xb * qvx, a.xq + (size_t)tok * qvx, qvx, &xfull[xb]);
+                    *reinterpret_cast<volatile uint32_t *>(&xseq[xb]) = (uint32_t)tok;
                     if (tr && tok == trace_tok(a)) tr[21] = now_ns();
+                    if (tr && tok == trace_tok(a) + 1) tr[28] = now_ns();
                 } else {
                     const uint64_t gt = a.bar_base + (uint64_t)tok;
-                    if ((tok >= 2 && !mbar_wait(&hfree[vb], (uint32_t)((tok >> 1) - 1) & 1u)) ||
+                    if ((tok >= 1 && !mbar_wait(&hfree[0], (uint32_t)(tok - 1) & 1u)) ||
                         !grid_wait(barrier_word(bar, gt), (gt / NBUF + 1u) * gridDim.x)) {
                         failed = true;
                         break;
                     }
-                    fence_proxy_async();   // h was quantised by other CTAs' generic stores
-                    mbar_expect_tx(&hfull[vb], ne * qvd);
-                    bulk_g2s(smem + L.hs + vb * 2 * qvd, a.hq + ((size_t)tok * k + rq0) * qvd, ne * qvd, &hfull[vb]);
-                    *reinterpret_cast<volatile uint32_t *>(&hseq[vb]) = (uint32_t)tok;
+                    fence_proxy_async();   // the h rows were written by other CTAs' generic stores
+                    const uint32_t hb = (uint32_t)(ne * de) * 4u;   // h rows of the CTA's down experts
+                    mbar_expect_tx(&hfull[0], hb);
+                    bulk_g2s(smem + L.hraw, a.hbuf + (size_t)tok * P + (size_t)rq0 * de, hb, &hfull[0]);
+                    *reinterpret_cast<volatile uint32_t *>(&hseq[0]) = (uint32_t)tok;
                     if (tr && tok == trace_tok(a)) tr[10] = now_ns();
+                    if (tr && tok == trace_tok(a) + 1) tr[30] = now_ns();
                 }
                 for (int c = 0; c < nc; c++) {
                     const uint32_t cc = (uint32_t)(tok * nc + c), u = cc / (uint32_t)nsr;
@@ -796,179 +828,235 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
         return;
     }
 
-    // ---- consumers: warps [0, NAW) take gate/up items, the others down
-    // items, each the next one of its kind (shared counters), in token
-    // order; an item waits only for what it reads
-    const bool isA = warp < NAW;
-    const int rbg = nbx * dt_block_bytes(DGU), rbd = nbd * dt_block_bytes(DDN), rb = 32 / nbd;
-    const int I = isA ? IA : IB, nc = isA ? nA : nB, nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA;
-    const int *pre = isA ? ipre : ipre + nA + 1;
-    float *hrow = reinterpret_cast<float *>(smem + L.hrow);   // [NBUF][range_max(P)] the CTA's h rows by token
-    float *erow = reinterpret_cast<float *>(smem + L.erow);   // [NBUF][range_max(Q)] the CTA's expert outputs
-    const int hrow_n = range_max(P), erow_n = range_max(Q);
-    uint32_t st = 0;
-    uint32_t tw = 0, tc = 0, td = 0;   // trace: ns this warp waited for inputs / in items / in token duties
-    for (;;) {
-        int item = 0;
-        if (lane == 0) item = (int)atomicAdd(&cnt[2 * NBUF + (isA ? 0 : 1)], 1u);
-        item = __shfl_sync(0xFFFFFFFFu, item, 0);
-        if (item >= n * I) break;
-        const int tok = item / I, li = item - tok * I;
-        int c = 0;
-        while (c + 1 < nc && li >= pre[c + 1]) c++;
-        const int ii = li - pre[c];
-        const uint32_t cc = (uint32_t)(tok * nc + c);
-        const int s = s0 + (int)(cc % (uint32_t)nsr);
-        const ChunkDesc d = desc[(isA ? 0 : nA) + c];
-        const bool tr0 = tr && tok == trace_tok(a) && li == 0 && lane == 0;
-        if (tr0) tr[isA ? 2 : 9] = now_ns();
-
-        // inputs: the chunk, then the token's x / h
-        const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
-        const int vb = tok & 1;
-        uint8_t *vbuf = smem + (isA ? L.xs + vb * qvx : L.hs + vb * 2 * qvd);
-        if (!(st & ST_DEAD)) {
-            const bool ok = seq_wait(&seq[s], cc) && mbar_wait(&full[s], (cc / (uint32_t)nsr) & 1u) &&
-                            seq_wait(isA ? &xseq[vb] : &hseq[vb], (uint32_t)tok) &&
-                            mbar_wait(isA ? &xfull[vb] : &hfull[vb], (uint32_t)(tok >> 1) & 1u);
-            if (!ok) {
-                st |= ST_DEAD | ST_ABORT;
-                if (lane == 0) raise_error(err, bar, FUSED_ERR_COPY);
+    if (warp == NCW + 2) {
+        // ---- gate/up duties, token by token: once the gate/up group has
+        // written all the CTA's h rows of the token (group barrier, then the
+        // adone arrival), one gpu-scope fence makes them visible and the CTA
+        // arrives at the token's grid barrier
+        uint32_t td = 0;
+        for (int tok = 0; tok < n; tok++) {
+            if (!mbar_wait(&adone[tok % NBUF], (uint32_t)(tok / NBUF) & 1u)) {
+                if (lane == 0) raise_error(err, bar, FUSED_ERR_BARRIER);
+                break;
             }
-        }
-        const uint32_t tc0 = tr ? (uint32_t)now_ns() : 0u;
-        if (tr) tw += tc0 - tw0;
-        if (tr0) tr[isA ? 3 : 11] = now_ns();
-
-        if (isA) {
-            const uint8_t *stg = smem + L.stageA + (size_t)s * SLOT_A;
-            const int row = 4 * ii + (lane >> 3);
-            const bool valid = row < d.nrows;
-            if (!(st & ST_ABORT)) {
-                const float hv = a_item<DGU, W>(stg + d.dst[0] + d.roff[0] + (size_t)row * rbg,
-                                                stg + d.dst[1] + d.roff[1] + (size_t)row * rbg, valid,
-                                                qvec(vbuf, nbx), nbx, lane);
-                if ((lane & 7) == 0 && valid)
-                    hrow[(tok % NBUF) * hrow_n + (int)(d.rank * de + d.row0 + row - p0)] = hv;
-            }
-        } else {
-            const uint8_t *stg = smem + L.stageB + (size_t)(s - nsA) * SLOT_B;
-            const int g = lane / nbd, row = rb * ii + g;
-            const bool valid = g < rb && row < d.nrows;
-            if (!(st & ST_ABORT)) {
-                const float eo = b_item<DDN>(stg + d.roff[0] + (size_t)row * rbd, valid,
-                                             qvec(vbuf + (d.rank - rq0) * qvd, nbd), nbd, lane);
-                if (valid && lane == g * nbd)
-                    erow[(tok % NBUF) * erow_n + (int)((int64_t)d.rank * D + d.row0 + row - q0)] = eo;
-            }
-        }
-        __syncwarp();
-        if (tr) tc += (uint32_t)now_ns() - tc0;
-
-        // release the stage when its chunk's last item is done
-        int last = 0;
-        if (lane == 0) {
-            const int nit = pre[c + 1] - pre[c];
-            if ((int)atomicAdd(&done[s], 1u) + 1 == nit) {
-                done[s] = 0u;
-                mbar_arrive(&empty[s]);
-            }
-            __threadfence_block();   // this item's staged results, before the count
-            last = (int)atomicAdd(&cnt[(isA ? 0 : NBUF) + tok % NBUF], 1u) + 1 == I;
-        }
-        last = __shfl_sync(0xFFFFFFFFu, last, 0);
-        if (!last) continue;
-
-        const uint32_t td0 = tr ? (uint32_t)now_ns() : 0u;
-        __threadfence_block();
-        if (isA) {
-            // ---- the CTA's last gate/up item of the token: its h rows out
-            // (one fence), then the h block counts; the CTA completing a block
-            // quantises it (into expert r's vector of the token's h)
-            if (lane == 0) {
-                cnt[tok % NBUF] = 0u;
-                mbar_arrive(&xfree[vb]);
-            }
-            for (int i = lane; i < p1 - p0; i += 32) a.hbuf[(size_t)tok * P + p0 + i] = hrow[(tok % NBUF) * hrow_n + i];
-            __syncwarp();
-            __threadfence();
-            for (int beta = p0 >> 8; beta <= (p1 - 1) >> 8 && p1 > p0; beta++) {
-                const int lo = p0 > 256 * beta ? p0 : 256 * beta, hi = p1 < 256 * beta + 256 ? p1 : 256 * beta + 256;
-                int complete = 0;
-                if (lane == 0) {
-                    uint32_t *hc = a.hcnt + (size_t)tok * nbh + beta;
-                    complete = (int)atomicAdd(hc, (uint32_t)(hi - lo)) + (hi - lo) == 256;
-                    if (complete) *hc = 0u;   // ready for the next launch
-                }
-                complete = __shfl_sync(0xFFFFFFFFu, complete, 0);
-                if (complete) {
-                    __threadfence();
-                    if (!(st & ST_ABORT)) {
-                        const int r = beta / nbd, bb = beta - r * nbd;
-                        const float4 *h4 =
-                            reinterpret_cast<const float4 *>(a.hbuf + (size_t)tok * P + 256 * beta) + 2 * lane;
-                        quant_block(__ldcg(h4), __ldcg(h4 + 1), qvec(a.hq + ((size_t)tok * k + r) * qvd, nbd), bb,
-                                    lane);
-                    }
-                }
-            }
-            __syncwarp();
+            const uint32_t td0 = tr ? (uint32_t)now_ns() : 0u;
             if (lane == 0) {
                 __threadfence();
                 atomicAdd(barrier_word(bar, a.bar_base + (uint64_t)tok), 1ull);
                 if (tr && tok == trace_tok(a)) tr[8] = now_ns();
+                if (tr && tok == trace_tok(a) + 1) tr[29] = now_ns();
             }
-        } else {
-            // ---- the CTA's last down item of the token: its expert outputs
-            // out (one fence), then the counts of the 64-row output groups;
-            // the CTA completing a group combines its rows
-            for (int i = lane; i < q1 - q0; i += 32) a.eo[(size_t)tok * Q + q0 + i] = erow[(tok % NBUF) * erow_n + i];
-            __syncwarp();
+            if (tr) td += (uint32_t)now_ns() - td0;
+        }
+        if (tr && lane == 0) atomicAdd(reinterpret_cast<unsigned long long *>(&tr[26]), (unsigned long long)td);
+        return;
+    }
+    if (warp == NCW + 3) {
+        // ---- down duties, token by token: once the down group has written
+        // all the CTA's expert outputs of the token, one gpu-scope fence; the
+        // counts of the 64-row output groups go out together (one lane per
+        // group); the token's combine weights are copied and its routing
+        // buffer freed; then the CTA completing a group combines its rows in
+        // ascending rank
+        uint32_t td = 0;
+        // the CTA's output groups: rows [ia, ib) of expert rq0 (one expert)
+        const int ia = q0 - rq0 * D, ib = q1 - rq0 * D;
+        const int g0 = ia >> 6, ng = ((ib - 1) >> 6) - g0 + 1;   // <= 32 groups
+        for (int tok = 0; tok < n; tok++) {
+            if (!mbar_wait(&bdone[tok % NBUF], (uint32_t)(tok / NBUF) & 1u)) {
+                if (lane == 0) raise_error(err, bar, FUSED_ERR_BARRIER);
+                break;
+            }
+            const uint32_t td0 = tr ? (uint32_t)now_ns() : 0u;
             __threadfence();
-            const float *wr = reinterpret_cast<const float *>(smem + L.w) + 64 * (tok % NBUF);
-            for (int r = rq0; r <= (q1 - 1) / D; r++) {
-                const int ia = (q0 > r * D ? q0 - r * D : 0), ib = (q1 < (r + 1) * D ? q1 - r * D : D);
-                for (int grp = ia >> 6; grp <= (ib - 1) >> 6; grp++) {
-                    const int ga = ia > 64 * grp ? ia : 64 * grp, gz = ib < 64 * grp + 64 ? ib : 64 * grp + 64;
-                    int complete = 0;
-                    if (lane == 0) {
-                        uint32_t *gc = a.ocnt + (size_t)tok * (D / 64) + grp;
-                        complete = (int)atomicAdd(gc, (uint32_t)(gz - ga)) + (gz - ga) == 64 * k;
-                        if (complete) *gc = 0u;   // ready for the next launch
+            uint32_t complete = 0;
+            if (lane < ng) {
+                const int grp = g0 + lane;
+                const int ga = ia > 64 * grp ? ia : 64 * grp, gz = ib < 64 * grp + 64 ? ib : 64 * grp + 64;
+                uint32_t *gc = a.ocnt + (size_t)tok * (D / 64) + grp;
+                const bool c = (int)atomicAdd(gc, (uint32_t)(gz - ga)) + (gz - ga) == 64 * k;
+                if (c) *gc = 0u;   // ready for the next launch
+                complete = c;
+            }
+            complete = __ballot_sync(0xFFFFFFFFu, complete != 0);
+            const float *wr = reinterpret_cast<const float *>(smem + L.w) + MAXK * (tok % NBUF);
+            float wk[MAXK];
+#pragma unroll
+            for (int q = 0; q < MAXK; q++) wk[q] = q < k ? wr[q] : 0.0f;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&idsfree[tok % NBUF]);
+            if (complete) __threadfence();
+            while (complete) {
+                const int grp = g0 + __ffs(complete) - 1;
+                complete &= complete - 1;
+                // rows 64 grp + lane and + 32: every expert output loaded first
+                // (independent L2 reads in flight together), then the
+                // rank-ordered sums
+                float e0[MAXK], e1[MAXK];
+                const float *eb = a.eo + (size_t)tok * Q + 64 * grp + lane;
+#pragma unroll
+                for (int q = 0; q < MAXK; q++) {
+                    e0[q] = q < k ? __ldcg(eb + (size_t)q * D) : 0.0f;
+                    e1[q] = q < k ? __ldcg(eb + (size_t)q * D + 32) : 0.0f;
+                }
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const int i = 64 * grp + lane + 32 * hh;
+                    float f = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < MAXK; q++)
+                        if (q < k) f = __fadd_rn(f, __fmul_rn(wk[q], hh ? e1[q] : e0[q]));
+                    if (a.s_out) f = __fadd_rn(f, __fmul_rn(*a.sgate, a.s_out[i]));
+                    a.ffn[(size_t)tok * D + i] = f;
+                    if (a.h) a.h[i] = __fadd_rn(a.h[i], f);
+                }
+            }
+            if (lane == 0) {
+                if (tr && tok == trace_tok(a)) tr[15] = now_ns();
+                if (tr && tok == trace_tok(a) + 1) tr[31] = now_ns();
+            }
+            if (tr) td += (uint32_t)now_ns() - td0;
+        }
+        if (tr && lane == 0) atomicAdd(reinterpret_cast<unsigned long long *>(&tr[27]), (unsigned long long)td);
+        return;
+    }
+
+    // ---- consumers: warps [0, NAW) process the gate/up chunks, the others
+    // the down chunks, each group chunk by chunk in token order. All
+    // threads of the group split the chunk's (row, block) units, one unit
+    // each, and write the units' exact partials to shared memory; after a
+    // group barrier the stage is released and one thread per row runs the
+    // row's fmaf chain(s) over the blocks in ascending order (the next
+    // chunk's units go to the other partials buffer meanwhile). A stage is
+    // thus held for one unit's work, not for a row's.
+    const bool isA = warp < NAW;
+    const int gth = isA ? NAW * 32 : (NCW - NAW) * 32, gt = isA ? t : t - NAW * 32;
+    const int rbg = nbx * dt_block_bytes(DGU), rbd = nbd * dt_block_bytes(DDN);
+    const int nc = isA ? nA : nB, nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA;
+    const int nbu = isA ? nbx : 2 * nbd;         // units per row: blocks (gate/up), half blocks (down)
+    const int pstr = nbu + 1;                    // partials row stride (padded: conflict-free chain reads)
+    const int pcap = isA ? capA_rows(nbx) : capB_rows(nbd);
+    BlockSum *part = reinterpret_cast<BlockSum *>(smem + (isA ? L.partA : L.partB));   // [2][(A: 2) pcap][pstr]
+    const int pbuf = (isA ? 2 : 1) * pcap * pstr;
+    auto gsync = [&]() {
+        if (isA) asm volatile("bar.sync 2, %0;" ::"n"(NAW * 32) : "memory");
+        else asm volatile("bar.sync 3, %0;" ::"n"((NCW - NAW) * 32) : "memory");
+    };
+    uint32_t st = 0;
+    uint32_t tw = 0, tc = 0;   // trace (lane 0 of each warp): ns waiting for inputs / in units and chains
+    int pb = 0;
+    for (int tok = 0; tok < n; tok++) {
+        const int xb = tok % NX;
+        uint8_t *vbuf = smem + (isA ? L.xs + xb * qvx : L.hs);
+        const bool trt = tr && tok == trace_tok(a) && gt == 0;
+        if (!isA) {
+            // the token's h rows of the CTA's down experts -> Q8_K in shared
+            // memory (one block per warp of the group), then the raw buffer is free
+            const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
+            if (!(st & ST_DEAD) &&
+                !(seq_wait(&hseq[0], (uint32_t)tok) && mbar_wait(&hfull[0], (uint32_t)tok & 1u))) {
+                st |= ST_DEAD | ST_ABORT;
+                raise_error(err, bar, FUSED_ERR_COPY);
+            }
+            if (tr) tw += (uint32_t)now_ns() - tw0;
+            const int ne = (q1 - 1) / D - rq0 + 1;
+            const float *hr = reinterpret_cast<const float *>(smem + L.hraw);
+            for (int qb = warp - NAW; qb < ne * nbd && !(st & ST_ABORT); qb += NCW - NAW) {
+                const int e = qb / nbd, b = qb - e * nbd;
+                const float4 *h4 = reinterpret_cast<const float4 *>(hr + e * de + 256 * b) + 2 * lane;
+                quant_block(h4[0], h4[1], qvec(smem + L.hs + e * qvd, nbd), b, lane);
+            }
+            gsync();
+            if (gt == 0) mbar_arrive(&hfree[0]);
+        }
+        for (int c = 0; c < nc; c++) {
+            const uint32_t cc = (uint32_t)(tok * nc + c);
+            const int s = s0 + (int)(cc % (uint32_t)nsr);
+            const ChunkDesc d = desc[(isA ? 0 : nA) + c];
+            if (trt && c == 0) tr[isA ? 2 : 9] = now_ns();
+
+            // inputs: the chunk, and (first gate/up chunk) the token's x
+            const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
+            if (!(st & ST_DEAD)) {
+                bool ok = seq_wait(&seq[s], cc) && mbar_wait(&full[s], (cc / (uint32_t)nsr) & 1u);
+                if (ok && c == 0 && isA)
+                    ok = seq_wait(&xseq[xb], (uint32_t)tok) && mbar_wait(&xfull[xb], (uint32_t)(tok / NX) & 1u);
+                if (!ok) {
+                    st |= ST_DEAD | ST_ABORT;
+                    raise_error(err, bar, FUSED_ERR_COPY);
+                }
+            }
+            const uint32_t tc0 = tr ? (uint32_t)now_ns() : 0u;
+            if (tr) tw += tc0 - tw0;
+            if (trt && c == 0) tr[isA ? 3 : 11] = now_ns();
+
+            // the chunk's units
+            BlockSum *pp = part + pb * pbuf;
+            const int units = d.nrows * nbu;
+            if (!(st & ST_ABORT)) {
+                if (isA) {
+                    const uint8_t *stg = smem + L.stageA + (size_t)s * SLOT_A;
+                    const QVec x = qvec(vbuf, nbx);
+                    for (int u = gt; u < units; u += gth) {
+                        const int row = u / nbx, b = u - row * nbx;
+                        const uint8_t *wb[2] = { stg + d.dst[0] + d.roff[0] + (size_t)row * rbg + b * dt_block_bytes(DGU),
+                                                 stg + d.dst[1] + d.roff[1] + (size_t)row * rbg + b * dt_block_bytes(DGU) };
+                        BlockSum o2[2];
+                        kblock_dot<DGU, 2>(wb, XBlk{ x.codes, nbx, b, x.bs + 16 * b, x.d[b] }, o2);
+                        pp[row * pstr + b] = o2[0];
+                        pp[(pcap + row) * pstr + b] = o2[1];
                     }
-                    complete = __shfl_sync(0xFFFFFFFFu, complete, 0);
-                    if (complete) {
-                        __threadfence();
-                        if (!(st & ST_ABORT))
-                            for (int i = 64 * grp + lane; i < 64 * grp + 64; i += 32) {
-                                float f = 0.0f;
-                                for (int q = 0; q < k; q++)
-                                    f = __fadd_rn(f, __fmul_rn(wr[q], __ldcg(a.eo + (size_t)tok * Q +
-                                                                          (size_t)q * D + i)));
-                                if (a.s_out) f = __fadd_rn(f, __fmul_rn(*a.sgate, a.s_out[i]));
-                                a.ffn[(size_t)tok * D + i] = f;
-                                if (a.h) a.h[i] = __fadd_rn(a.h[i], f);
-                            }
+                } else {
+                    const uint8_t *stg = smem + L.stageB + (size_t)(s - nsA) * SLOT_B;
+                    const QVec h = qvec(vbuf + (d.rank - rq0) * qvd, nbd);
+                    for (int u = gt; u < units; u += gth) {
+                        const int row = u / nbu, ub = u - row * nbu, b = ub >> 1;
+                        BlockSum o1;
+                        kblock_half<DDN>(stg + d.roff[0] + (size_t)row * rbd + b * dt_block_bytes(DDN),
+                                         XBlk{ h.codes, nbd, b, h.bs + 16 * b, h.d[b] }, ub & 1, o1);
+                        pp[row * pstr + ub] = o1;
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) {
-                cnt[NBUF + tok % NBUF] = 0u;
-                mbar_arrive(&hfree[vb]);
-                mbar_arrive(&idsfree[tok % NBUF]);
-                if (tr && tok == trace_tok(a)) tr[15] = now_ns();
+            gsync();   // the chunk's partials are written; the stage is no longer read
+            if (gt == 0) {
+                mbar_arrive(&empty[s]);
+                if (c == nc - 1 && isA) mbar_arrive(&xfree[xb]);
             }
+
+            // the rows' chains
+            if (!(st & ST_ABORT) && gt < d.nrows) {
+                const int row = gt;
+                if (isA) {
+                    float ag = 0.0f, au = 0.0f;
+                    for (int b = 0; b < nbx; b++) {
+                        const BlockSum eg = pp[row * pstr + b], eu = pp[(pcap + row) * pstr + b];
+                        ag = chain<DGU>(ag, eg.dA, eg.is, eg.dM, eg.ms);
+                        au = chain<DGU>(au, eu.dA, eu.is, eu.dM, eu.ms);
+                    }
+                    a.hbuf[(size_t)tok * P + (size_t)d.rank * de + d.row0 + row] = __fmul_rn(silu_f(ag), au);
+                } else {
+                    float eo = 0.0f;
+                    for (int b = 0; b < nbd; b++) {
+                        const BlockSum e0 = pp[row * pstr + 2 * b], e1 = pp[row * pstr + 2 * b + 1];
+                        eo = chain<DDN>(eo, e0.dA, e0.is + e1.is, e0.dM, e0.ms + e1.ms);
+                    }
+                    a.eo[(size_t)tok * Q + (size_t)d.rank * D + d.row0 + row] = eo;
+                }
+            }
+            if (tr) tc += (uint32_t)now_ns() - tc0;
+            pb ^= 1;
         }
-        if (tr) td += (uint32_t)now_ns() - td0;
+        gsync();   // the token's staged rows are complete: hand them to the duty warp
+        if (gt == 0) mbar_arrive(isA ? &adone[tok % NBUF] : &bdone[tok % NBUF]);
     }
     if (tr && lane == 0) {
         atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 16 : 18]), (unsigned long long)tw);
         atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 17 : 19]), (unsigned long long)tc);
-        atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 26 : 27]), (unsigned long long)td);
     }
     if (tr && t == 0) tr[20] = now_ns();
 }
+
 
 // ---------------------------------------------------------------------------
 // host side
@@ -1004,7 +1092,7 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     f.smem_limit = prop.sharedMemPerBlockOptin;
     // stage counts: two gate/up stages, as many down stages as fit (>= 2)
     int nsB = 0;
-    for (int nb = 4; nb >= 2; nb--)
+    for (int nb = 3; nb >= 2; nb--)
         if (smem_layout(g.d_model, g.d_expert, g.top_k, 2, nb).total + 1024 <= f.smem_limit) {
             nsB = nb;
             break;
@@ -1017,8 +1105,8 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     f.D = g.d_model;
     f.de = g.d_expert;
     f.k = g.top_k;
-    if (cudaMalloc(&f.bar, 64) != cudaSuccess) return set_error(TLMG_ENOMEM, "fused barrier allocation");
-    cudaMemset(f.bar, 0, 64);
+    if (cudaMalloc(&f.bar, BAR_BYTES) != cudaSuccess) return set_error(TLMG_ENOMEM, "fused barrier allocation");
+    cudaMemset(f.bar, 0, BAR_BYTES);
     f.rounds = 0;
     f.launches = 0;
     if (cudaHostAlloc(&f.err_host, 64, cudaHostAllocMapped) != cudaSuccess)
@@ -1030,12 +1118,10 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
 }
 
 static void free_tokens(FusedScratch &f) {
-    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.hq, (void *)f.hcnt, (void *)f.eo, (void *)f.ocnt })
+    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.eo, (void *)f.ocnt })
         if (p) cudaFree(p);
     f.xq = nullptr;
     f.hbuf = nullptr;
-    f.hq = nullptr;
-    f.hcnt = nullptr;
     f.eo = nullptr;
     f.ocnt = nullptr;
     f.tok_cap = 0;
@@ -1047,19 +1133,16 @@ static int reserve_tokens(FusedScratch &f, int n_tok) {
     if (n_tok <= f.tok_cap) return TLMG_OK;
     free_tokens(f);
     const int cap = n_tok < 64 ? 64 : n_tok;
-    const int nbx = f.D / 256, nbd = f.de / 256, nbh = f.k * nbd;
+    const int nbx = f.D / 256;
     const size_t P = (size_t)f.k * f.de, Q = (size_t)f.k * f.D;
     if (cudaMalloc(&f.xq, (size_t)cap * qv_bytes(nbx)) != cudaSuccess ||
         cudaMalloc(&f.hbuf, (size_t)cap * P * 4) != cudaSuccess ||
-        cudaMalloc(&f.hq, (size_t)cap * f.k * qv_bytes(nbd)) != cudaSuccess ||
-        cudaMalloc(&f.hcnt, (size_t)cap * nbh * 4) != cudaSuccess ||
         cudaMalloc(&f.eo, (size_t)cap * Q * 4) != cudaSuccess ||
         cudaMalloc(&f.ocnt, (size_t)cap * (f.D / 64) * 4) != cudaSuccess) {
         cudaGetLastError();
         free_tokens(f);
         return set_error(TLMG_ENOMEM, "fused per-token scratch for %d tokens", n_tok);
     }
-    cudaMemset(f.hcnt, 0, (size_t)cap * nbh * 4);
     cudaMemset(f.ocnt, 0, (size_t)cap * (f.D / 64) * 4);
     f.tok_cap = cap;
     return TLMG_OK;
@@ -1085,7 +1168,7 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
     if (it != f.plans.end()) return it->second;
     const int D = g.d_model, de = g.d_expert, k = g.top_k, G = f.nsm;
     const int rbg = D / 256 * dt_block_bytes(dgu), rbd = de / 256 * dt_block_bytes(ddn);
-    const int capA = (SLOT_A / 2 - 15) / rbg, capB = (SLOT_B - 15) / rbd;
+    const int capA = (SLOT_A / 2 - 15) / rbg, capB = (SLOT_B - 15) / rbd;   // <= capA_rows / capB_rows
     if (capA < 1 || capB < 1) return nullptr;
     if (de / 256 > 32) return nullptr;   // phase B: a row's blocks fit one warp
     if (G < 64) return nullptr;          // per-CTA ranges sized for >= 64 CTAs
@@ -1098,7 +1181,8 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
         int n = 0;
         for (int ph = 0; ph < 2; ph++) {
             const int64_t N = ph == 0 ? P : Q, len = ph == 0 ? de : D;
-            const int64_t lo = range_lo(N, c, G), hi = range_lo(N, c + 1, G);
+            const int64_t lo = ph == 0 ? range_lo(N, c, G) : qrange_lo(c, G, k, D);
+            const int64_t hi = ph == 0 ? range_lo(N, c + 1, G) : qrange_lo(c + 1, G, k, D);
             const int cap = ph == 0 ? capA : capB, rbytes = ph == 0 ? rbg : rbd;
             for (int64_t p = lo; p < hi;) {
                 const int r = (int)(p / len), j0 = (int)(p % len);
@@ -1171,8 +1255,6 @@ int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
     FusedArgs la = a;
     la.xq = f.xq;
     la.hbuf = f.hbuf;
-    la.hq = f.hq;
-    la.hcnt = f.hcnt;
     la.eo = f.eo;
     la.ocnt = f.ocnt;
     la.bar_base = f.rounds;
@@ -1192,8 +1274,7 @@ uint32_t fused_take_error(FusedScratch &f) {
         // the stream is idle (the caller synchronised): clear the sticky
         // device word and the barrier state for the next launch
         *(volatile uint32_t *)f.err_host = 0;
-        cudaMemset(f.bar, 0, 64);
-        if (f.hcnt) cudaMemset(f.hcnt, 0, (size_t)f.tok_cap * f.k * (f.de / 256) * 4);
+        cudaMemset(f.bar, 0, BAR_BYTES);
         if (f.ocnt) cudaMemset(f.ocnt, 0, (size_t)f.tok_cap * (f.D / 64) * 4);
         f.rounds = 0;
         f.launches = 0;

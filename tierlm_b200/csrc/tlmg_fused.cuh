@@ -59,8 +59,6 @@ struct FusedScratch {
     int tok_cap = 0;
     uint8_t *xq = nullptr;         // [tok_cap][quantised x]
     float *hbuf = nullptr;         // [tok_cap][k * de] SwiGLU rows
-    uint8_t *hq = nullptr;         // [tok_cap][quantised h]
-    uint32_t *hcnt = nullptr;      // [tok_cap][k * de / 256] rows written per h block (zero between launches)
     float *eo = nullptr;           // [tok_cap][k * D] expert outputs
     uint32_t *ocnt = nullptr;      // [tok_cap][D / 64] expert outputs written per 64-row group (zero between launches)
     int D = 0, de = 0, k = 0;
@@ -92,8 +90,6 @@ struct FusedArgs {
     // filled by launch_fused_ffn from the FusedScratch:
     uint8_t *xq;                   // [n_tok] quantised inputs
     float *hbuf;                   // [n_tok][k * de] SwiGLU rows (cross-CTA exchange)
-    uint8_t *hq;                   // [n_tok][k] quantised h per expert
-    uint32_t *hcnt;                // [n_tok][k * de / 256] h block row counts
     float *eo;                     // [n_tok][k * D] expert outputs (cross-CTA combine)
     uint32_t *ocnt;                // [n_tok][D / 64] output group counts
     int D, de, E, k, router;
