@@ -44,6 +44,10 @@ DT_GATE, DT_DOWN = 12, 14                       # Q4_K gate/up, Q6_K down
 BYTES_LAYER_TOKEN = K * (2 * DE * (D // 256 * 144) + D * (DE // 256 * 210))   # 24,477,696
 METRIC = "expert GEMV HBM GB/s, bs=1 MoE expert FFN (Qwen3-30B-A3B layer shape, Q4_K gate/up + Q6_K down)"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) per layer-token of the persistent kernel, from one
+# ncu capture of a 4-layer-token launch (profiles/k_fused_ffn_config2.md):
+# 98,111,744 read + 5,188,096 written, over 4 layer-tokens.
+TRAFFIC_LAYER_TOKEN = (98_111_744 + 5_188_096) // 4
 
 
 def peaks() -> tuple[float, str]:
@@ -344,7 +348,10 @@ def main() -> None:
                          "achieved": None if achieved is None else round(achieved, 1),
                          "peak": peak, "unit": "GB/s",
                          "frac": None if achieved is None else round(achieved / peak, 4),
-                         "traffic": None, "peak_source": peak_src,
+                         "traffic": None if not kbytes else int(kbytes // BYTES_LAYER_TOKEN * TRAFFIC_LAYER_TOKEN),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-layer-token "
+                                           "launch, scaled by layer-tokens per launch",
+                         "peak_source": peak_src,
                          "launches": kn, "avg_us": None if not kn else round(kms / kn * 1e3, 3),
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
