@@ -232,6 +232,7 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=64, help="batched-decode section: tokens per layer call (<= 1: off)")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("TLMG_BENCH_ALLOW_SHORT"), \
         "use at least 3 warm-up steps"
@@ -325,6 +326,54 @@ def main() -> None:
     h2d = L * (D + E) * 4
     d2h = L * D * 4
 
+    # ---- batched decode (bs = BATCH tokens through each layer, one call per layer)
+    batch = None
+    if args.batch > 1:
+        B = args.batch
+        bx = torch.randn((2, L, B, D), generator=g, device=dev)
+        bl = torch.randn((2, L, B, E), generator=g, device=dev)
+        bo = torch.empty((2, L, B, D), device=dev)
+        # distinct experts each layer call reads (softmax top-k = the k largest logits)
+        sel = torch.topk(bl, K, dim=-1).indices                               # [2, L, B, K]
+        hit = torch.zeros((2, L, E), dtype=torch.bool, device=dev)
+        hit.scatter_(2, sel.reshape(2, L, B * K), True)
+        uniq = hit.sum(-1).double()                                            # [2, L]
+        bytes_expert = BYTES_LAYER_TOKEN // K
+
+        def bstep(s):
+            i = s % 2
+            for layer in range(L):
+                ctx.expert_ffn_batch(layer, bx[i, layer], bl[i, layer], bo[i, layer])
+
+        for s in range(args.warmup):
+            bstep(s)
+        torch.cuda.synchronize(dev)
+        n0 = ctx.launches
+        bms = timed(bstep, args.steps)
+        blaunch = ctx.launches - n0
+        ubytes = sum(float(uniq[s % 2].sum()) for s in range(args.steps)) * bytes_expert
+        hbx, hbl = bx.cpu().pin_memory(), bl.cpu().pin_memory()
+        hbo = torch.empty((2, L, B, D)).pin_memory()
+
+        def bstep_host(s):
+            i = s % 2
+            for layer in range(L):
+                ctx.expert_ffn_batch(layer, hbx[i, layer], hbl[i, layer], hbo[i, layer])
+
+        for s in range(args.warmup):
+            bstep_host(s)
+        bms_e2e = timed(bstep_host, args.steps)
+        batch = {"batch": B, "metric": f"decode tok/s, bs={B}, expert FFN of {L} layers per token",
+                 "tokens_per_s": round(world * args.steps * B / (bms * 1e-3), 1),
+                 "ms_per_step": bms / args.steps,
+                 "unique_expert_GBps": round(world * ubytes / (bms * 1e-3) / 1e9, 1),
+                 "unique_experts_per_layer": round(float(uniq.mean()), 2),
+                 "gpu_launches": blaunch,
+                 "e2e": {"tokens_per_s": round(world * args.steps * B / (bms_e2e * 1e-3), 1),
+                         "h2d_bytes_per_step": L * B * (D + E) * 4, "d2h_bytes_per_step": L * B * D * 4,
+                         "api": "tlmg_expert_ffn_batch (pinned host buffers)"},
+                 "note": "one call per layer serves all B tokens; each selected expert is read once per call"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -356,6 +405,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
+            "batched_decode": batch,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

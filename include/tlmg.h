@@ -152,6 +152,16 @@ int tlmg_expert_ffn(tlmg_ctx *ctx, int layer, const float *x, const float *logit
 int tlmg_expert_ffn_many(tlmg_ctx *ctx, int layer0, int n_tok, const float *x,
                          const float *logits, float *ffn);
 
+/* Batched decode: n_tok tokens through the SAME layer (the reference's
+ * per-token run_batch, src/lib/tlm_model.c:900-938, applied to every
+ * sequence of a decode batch). Each expert selected by any token is read
+ * from HBM once per call. x f32[n_tok][D], logits f32[n_tok][E], ffn
+ * f32[n_tok][D]; ids i32[n_tok][top_k] and w f32[n_tok][top_k] (may be
+ * NULL) receive the routing. Results are bit-identical to n_tok calls of
+ * tlmg_expert_ffn. Pointers: host or device (all of one kind). */
+int tlmg_expert_ffn_batch(tlmg_ctx *ctx, int layer, int n_tok, const float *x,
+                          const float *logits, float *ffn, int32_t *ids, float *w);
+
 /* The whole moe() block for one token (src/lib/tlm_model.c:940-1055):
  * RMSNorm, router matvec, route, experts, shared expert, h += ffn.
  * h: f32[D] in/out; ids/w may be NULL. Host or device pointers. */

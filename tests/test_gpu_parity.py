@@ -356,3 +356,60 @@ def test_fused_matches_multikernel(dev, orc, shape):
     finally:
         orc.set_expf_mode(0)
     ctx.close()
+
+
+BATCH_SHAPES = [
+    # (D, de, E, k, dtypes, router, n_tok, batched kernels expected)
+    (2048, 768, 32, 8, (12, 12, 14), 0, 64, True),    # config-2 layer shape, bs=64: 16 pairs per expert
+    (2048, 768, 24, 8, (13, 13, 13), 0, 3, True),
+    (512, 256, 16, 4, (14, 14, 14), 0, 5, True),      # nbd = 1: 32 down rows per warp
+    (4096, 1536, 12, 8, (12, 12, 12), 0, 9, True),    # two blocks per lane, nbd = 6 (30 of 32 lanes)
+    (1024, 512, 160, 6, (12, 12, 13), 0, 33, True),   # E > 128
+    (1024, 512, 40, 4, (12, 12, 14), 1, 17, True),    # sigmoid router
+    (1024, 768, 8, 2, (13, 13, 15), 0, 4, False),     # Q8_K down: per-token fallback
+]
+
+
+@pytest.mark.parametrize("shape", BATCH_SHAPES,
+                         ids=lambda s: f"D{s[0]}-de{s[1]}-E{s[2]}-k{s[3]}-{s[4]}-r{s[5]}-n{s[6]}")
+def test_expert_ffn_batch_matches_single(dev, orc, shape):
+    """Batched decode (n tokens through one layer, each selected expert
+    read once) gives the bits of n single-token calls: ffn rows, expert ids
+    and weights; host and device buffers agree; the grouped kernels run as
+    seven launches for the whole batch where they apply; one row equals the
+    oracle."""
+    from tierlm_b200 import synth
+    D, de, E, k, dts, router, T, batched = shape
+    rng = np.random.default_rng(7 * D + de + E + k + T)
+    experts = [synth.rand_expert(rng, D, de, dts) for _ in range(E)]
+    ctx = build_ctx(experts, D, de, E, k, router)
+    x = rng.standard_normal((T, D)).astype(np.float32)
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    lg[T // 2] = 0.0                              # all-tie routing row
+    out = np.zeros((T, D), np.float32)
+    ids = np.zeros((T, k), np.int32)
+    w = np.zeros((T, k), np.float32)
+    ctx.expert_ffn_batch(0, x, lg, out, ids, w)
+    ctx.check()
+    for t in range(T):
+        one, i1, w1 = np.zeros(D, np.float32), np.zeros(k, np.int32), np.zeros(k, np.float32)
+        ctx.expert_ffn(0, x[t], lg[t], one, i1, w1)
+        assert np.array_equal(i1, ids[t]) and same_bits(w1, w[t]).all(), t
+        bad = np.flatnonzero(~same_bits(one, out[t]))
+        assert bad.size == 0, (t, bad[:4], out[t][bad[:4]], one[bad[:4]])
+    xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
+    od = torch.zeros((T, D), device=dev)
+    n0 = ctx.launches
+    ctx.expert_ffn_batch(0, xd, ld, od)
+    ctx.check()
+    assert ((ctx.launches - n0) == 7) == batched, ctx.launches - n0
+    assert same_bits(od.cpu().numpy(), out).all()
+    orc.set_expf_mode(1)
+    try:
+        geom = dict(d_model=D, d_expert=de, n_experts=E, top_k=k, router=router)
+        ref, rid, _ = orc.expert_ffn(geom, experts, x[T - 1], lg[T - 1])
+        assert np.array_equal(rid, ids[T - 1])
+        assert same_bits(out[T - 1], ref).all()
+    finally:
+        orc.set_expf_mode(0)
+    ctx.close()

@@ -67,6 +67,7 @@ _SIGS = {
     "tlmg_set_shared": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "tlmg_expert_ffn": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "tlmg_expert_ffn_many": (_I, [_P, _I, _I, _P, _P, _P]),
+    "tlmg_expert_ffn_batch": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
     "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
     "tlmg_set_stream": (_I, [_P, _P]),
     "tlmg_set_fused": (_I, [_P, _I]),

@@ -1,0 +1,296 @@
+// tlmg_batch.cu - batched expert FFN for n tokens of one MoE layer (batched
+// decode, reference run_batch over several sequences, src/lib/tlm_model.c:
+// 900-938 with the combine of :1029-1036 per token).
+//
+//   k_bquant    inputs x -> swizzled Q8_K vectors (one warp per block)
+//   k_broute    router top-k per token (one warp per token, warp_route)
+//   k_bgroup    (token, rank) pairs grouped by expert: offsets, the active
+//               experts, the pair list (one CTA)
+//   k_bgateup   per active expert and tile of 4 rows: every pair of the
+//               expert, gate/up partials + chains + SwiGLU -> hbuf[pair]
+//               (the expert's rows come from HBM once and from L1 for the
+//               expert's other tokens)
+//   k_bquant    h rows -> Q8_K per pair
+//   k_bdown     per active expert and tile of 32 / nbd rows: every pair,
+//               down partials + chain -> eo[pair]
+//   k_bcombine  ffn[t] = sum_r w[t][r] * eo[t, r] in ascending rank
+//
+// Per pair the arithmetic is the single-token path's (exact int32 block
+// partials, one fmaf per block (two for Q4_K/Q5_K) in block order, SiLU
+// with the correctly rounded expf), so results are bit-identical to
+// tlmg_expert_ffn on each token.
+#include <algorithm>
+
+#include "tlmg_batch.cuh"
+#include "tlmg_dev.cuh"
+#include "tlmg_internal.h"
+#include "tlmg_kq.cuh"
+
+namespace tlmg {
+
+namespace {
+
+constexpr int BMAXK = 16;
+__host__ __device__ inline uint32_t up16b(uint32_t v) { return (v + 15u) & ~15u; }
+__host__ __device__ inline uint32_t qvb(int nb) { return 256u * nb + 32u * nb + up16b(4u * nb); }
+
+// rows x len floats -> rows quantised vectors of len / 256 blocks
+__global__ void k_bquant(const float *__restrict__ in, int rows, int len, uint8_t *__restrict__ out) {
+    const int lane = threadIdx.x & 31, nb = len / 256;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t qb = qvb(nb);
+    for (int q = gw; q < rows * nb; q += nw) {
+        const int r = q / nb, b = q - r * nb;
+        const float4 *v = reinterpret_cast<const float4 *>(in + (size_t)r * len + 256 * b) + 2 * lane;
+        uint8_t *base = out + (size_t)r * qb;
+        warp_quant_swz(__ldg(v), __ldg(v + 1), base, nb, b, reinterpret_cast<int16_t *>(base + 256 * nb) + 16 * b,
+                       reinterpret_cast<float *>(base + 288 * nb) + b, lane);
+    }
+}
+
+// one warp per token
+constexpr int RW = 2;   // warps per CTA
+__global__ void __launch_bounds__(32 * RW) k_broute(BatchArgs a, int32_t *__restrict__ ids, float *__restrict__ w) {
+    __shared__ uint32_t scr[RW][RT_SCRATCH];
+    __shared__ int32_t sid[RW][64];
+    __shared__ float sw[RW][64];
+    const int wi = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * RW + wi;
+    if (t >= a.n) return;
+    warp_route(a.router, a.logits + (size_t)t * a.E, a.mask, a.bias, a.E, a.k, a.routed_scale, scr[wi], sid[wi],
+               sw[wi], lane);
+    if (lane < a.k) {
+        ids[(size_t)t * a.k + lane] = sid[wi][lane];
+        w[(size_t)t * a.k + lane] = sw[wi][lane];
+        if (a.ids_out) a.ids_out[(size_t)t * a.k + lane] = sid[wi][lane];
+        if (a.w_out) a.w_out[(size_t)t * a.k + lane] = sw[wi][lane];
+    }
+}
+
+// grp: [0, E] expert offsets into the pair list, [E + 1, 2E] active experts
+// in ascending id, [2E + 1] their count, [2E + 2, ..) the pairs t * k + r
+// grouped by expert (in no particular order inside an expert: every pair's
+// results are independent of the others)
+__global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids, int np, int E, int32_t *grp) {
+    __shared__ int cnt[RT_PER * 32], off[RT_PER * 32 + 1], fill[RT_PER * 32];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        cnt[e] = 0;
+        fill[e] = 0;
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < np; p += blockDim.x) atomicAdd(&cnt[ids[p]], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0, na = 0;
+        for (int e = 0; e < E; e++) {
+            off[e] = s;
+            s += cnt[e];
+            if (cnt[e]) grp[E + 1 + na++] = e;
+        }
+        off[E] = s;
+        grp[2 * E + 1] = na;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) grp[e] = off[e];
+    for (int p = threadIdx.x; p < np; p += blockDim.x) {
+        const int e = ids[p];
+        grp[2 * E + 2 + off[e] + atomicAdd(&fill[e], 1)] = p;
+    }
+}
+
+// Work item = (active expert, tile of 4 gate/up rows); one warp per item.
+// Lane (p, j) = (lane / 8, lane % 8) owns row p of the tile and blocks
+// j, j + 8, ... of the gate and up rows; for each pair of the expert it
+// computes their exact partials against the pair's token, the chains run in
+// block order (the holder of block b applies it, the accumulators are
+// broadcast to the row's lanes by shuffle) and lane (p, 0) writes
+// silu(gate) * up.
+template <int DGU, int BPL>
+__global__ void __launch_bounds__(256) k_bgateup(const Slot *__restrict__ slots, const int32_t *__restrict__ grp,
+                                                 const uint8_t *__restrict__ xq, int D, int de, int E, int k,
+                                                 float *__restrict__ hbuf) {
+    const int lane = threadIdx.x & 31, p = lane >> 3, j = lane & 7;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+    const int nbx = D / 256, tiles = (de + 3) / 4, na = grp[2 * E + 1];
+    const uint32_t qx = qvb(nbx);
+    const int rb = nbx * dt_block_bytes(DGU);
+    for (int item = gw; item < na * tiles; item += nw) {
+        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+        const int row = 4 * tile + p;
+        const bool valid = row < de;
+        const uint8_t *grow = slots[e].m[0] + (size_t)row * rb, *urow = slots[e].m[1] + (size_t)row * rb;
+        for (int q = grp[e]; q < grp[e + 1]; q++) {
+            const int pair = grp[2 * E + 2 + q], t = pair / k;
+            const uint8_t *xb = xq + (size_t)t * qx;
+            const int16_t *xbs = reinterpret_cast<const int16_t *>(xb + 256 * nbx);
+            const float *xd = reinterpret_cast<const float *>(xb + 288 * nbx);
+            BlockSum vg[BPL], vu[BPL];
+#pragma unroll
+            for (int i = 0; i < BPL; i++) {
+                const int b = j + 8 * i;
+                vg[i] = BlockSum{ 0, 0, 0.f, 0.f };
+                vu[i] = vg[i];
+                if (valid && b < nbx) {
+                    const uint8_t *wb[2] = { grow + b * dt_block_bytes(DGU), urow + b * dt_block_bytes(DGU) };
+                    BlockSum o2[2];
+                    kblock_dot<DGU, 2>(wb, XBlk{ xb, nbx, b, xbs + 16 * b, xd[b] }, o2);
+                    vg[i] = o2[0];
+                    vu[i] = o2[1];
+                }
+            }
+            float ag = 0.0f, au = 0.0f;
+            const int base = lane & ~7;
+#pragma unroll
+            for (int i = 0; i < BPL; i++)
+#pragma unroll
+                for (int h = 0; h < 8; h++) {
+                    if (h + 8 * i >= nbx) break;
+                    if (j == h) {
+                        ag = chain<DGU>(ag, vg[i].dA, vg[i].is, vg[i].dM, vg[i].ms);
+                        au = chain<DGU>(au, vu[i].dA, vu[i].is, vu[i].dM, vu[i].ms);
+                    }
+                    ag = __shfl_sync(0xFFFFFFFFu, ag, base | h);
+                    au = __shfl_sync(0xFFFFFFFFu, au, base | h);
+                }
+            if (j == 0 && valid) hbuf[(size_t)pair * de + row] = __fmul_rn(silu_f(ag), au);
+        }
+    }
+}
+
+// Work item = (active expert, tile of 32 / nbd down rows); one warp per
+// item. Lane (g, b) = (lane / nbd, lane % nbd) owns block b of row g; per
+// pair of the expert: exact partials against the pair's quantised h, then
+// the row's chain in block order, lane (g, 0) writes eo[pair][row].
+template <int DDN>
+__global__ void __launch_bounds__(256) k_bdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp,
+                                               const uint8_t *__restrict__ hq, int D, int de, int E, int k,
+                                               float *__restrict__ eo) {
+    const int lane = threadIdx.x & 31, nbd = de / 256, rpt = 32 / nbd;
+    const int g = lane / nbd, b = lane - g * nbd;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+    const int tiles = (D + rpt - 1) / rpt, na = grp[2 * E + 1];
+    const uint32_t qh = qvb(nbd);
+    const int rb = nbd * dt_block_bytes(DDN);
+    const int gb = g < rpt ? g * nbd : 0;
+    for (int item = gw; item < na * tiles; item += nw) {
+        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+        const int row = rpt * tile + g;
+        const bool valid = g < rpt && row < D;
+        const uint8_t *wrow = slots[e].m[2] + (size_t)row * rb;
+        for (int q = grp[e]; q < grp[e + 1]; q++) {
+            const int pair = grp[2 * E + 2 + q];
+            const uint8_t *hb = hq + (size_t)pair * qh;
+            BlockSum v = BlockSum{ 0, 0, 0.f, 0.f };
+            if (valid) {
+                const uint8_t *wb[1] = { wrow + b * dt_block_bytes(DDN) };
+                BlockSum o1[1];
+                kblock_dot<DDN, 1>(wb,
+                                   XBlk{ hb, nbd, b, reinterpret_cast<const int16_t *>(hb + 256 * nbd) + 16 * b,
+                                         reinterpret_cast<const float *>(hb + 288 * nbd)[b] },
+                                   o1);
+                v = o1[0];
+            }
+            float acc = 0.0f;
+            for (int h = 0; h < nbd; h++) {
+                if (b == h) acc = chain<DDN>(acc, v.dA, v.is, v.dM, v.ms);
+                acc = __shfl_sync(0xFFFFFFFFu, acc, gb + h);
+            }
+            if (b == 0 && valid) eo[(size_t)pair * D + row] = acc;
+        }
+    }
+}
+
+// ffn[t][i] = sum_r w[t][r] * eo[t * k + r][i], ascending r
+__global__ void k_bcombine(const float *__restrict__ eo, const float *__restrict__ w, int n, int D, int k,
+                           float *__restrict__ ffn) {
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n * D; idx += gridDim.x * blockDim.x) {
+        const int t = idx / D, i = idx - t * D;
+        float f = 0.0f;
+        for (int r = 0; r < k; r++) f = __fadd_rn(f, __fmul_rn(w[(size_t)t * k + r], eo[((size_t)t * k + r) * D + i]));
+        ffn[idx] = f;
+    }
+}
+
+}  // namespace
+
+using GateUpFn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, int, float *);
+using DownFn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, int, float *);
+
+static GateUpFn pick_gateup(int dt, int D) {
+    const bool two = D > 2048;
+    switch (dt) {
+    case DT_Q4_K: return two ? k_bgateup<DT_Q4_K, 2> : k_bgateup<DT_Q4_K, 1>;
+    case DT_Q5_K: return two ? k_bgateup<DT_Q5_K, 2> : k_bgateup<DT_Q5_K, 1>;
+    case DT_Q6_K: return two ? k_bgateup<DT_Q6_K, 2> : k_bgateup<DT_Q6_K, 1>;
+    default: return nullptr;
+    }
+}
+static DownFn pick_down(int dt) {
+    switch (dt) {
+    case DT_Q4_K: return k_bdown<DT_Q4_K>;
+    case DT_Q5_K: return k_bdown<DT_Q5_K>;
+    case DT_Q6_K: return k_bdown<DT_Q6_K>;
+    default: return nullptr;
+    }
+}
+
+bool batch_supported(int dt_gu, int dt_dn, int D, int de, int E, int k) {
+    return pick_gateup(dt_gu, D) && pick_down(dt_dn) && D % 256 == 0 && de % 256 == 0 && D <= 4096 &&
+           de / 256 <= 32 && E > 0 && E <= RT_PER * 32 && k > 0 && k <= BMAXK && k <= E;
+}
+
+void batch_release(BatchScratch &s) {
+    for (void *p : { (void *)s.xq, (void *)s.ids, (void *)s.w, (void *)s.grp, (void *)s.hbuf, (void *)s.hq,
+                     (void *)s.eo })
+        if (p) cudaFree(p);
+    s = BatchScratch{};
+}
+
+int batch_reserve(BatchScratch &s, int n, int D, int de, int E, int k) {
+    if (n <= s.cap) return TLMG_OK;
+    batch_release(s);
+    const int cap = n < 16 ? 16 : n;
+    const size_t np = (size_t)cap * k;
+    if (cudaMalloc(&s.xq, (size_t)cap * qvb(D / 256)) != cudaSuccess ||
+        cudaMalloc(&s.ids, 4 * np) != cudaSuccess || cudaMalloc(&s.w, 4 * np) != cudaSuccess ||
+        cudaMalloc(&s.grp, 4 * (2 * (size_t)E + 2 + np)) != cudaSuccess ||
+        cudaMalloc(&s.hbuf, 4 * np * de) != cudaSuccess || cudaMalloc(&s.hq, np * qvb(de / 256)) != cudaSuccess ||
+        cudaMalloc(&s.eo, 4 * np * D) != cudaSuccess) {
+        cudaGetLastError();
+        batch_release(s);
+        return set_error(TLMG_ENOMEM, "batched expert FFN scratch for %d tokens", n);
+    }
+    s.cap = cap;
+    return TLMG_OK;
+}
+
+int launch_batch(BatchScratch &s, const BatchArgs &a, cudaStream_t st) {
+    if (!batch_supported(a.dt_gu, a.dt_dn, a.D, a.de, a.E, a.k))
+        return set_error(TLMG_EUNSUP, "batched expert FFN: dtypes %d/%d or shape unsupported", a.dt_gu, a.dt_dn);
+    if (a.n <= 0) return TLMG_OK;
+    int rc = batch_reserve(s, a.n, a.D, a.de, a.E, a.k);
+    if (rc) return rc;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    const int np = a.n * a.k;
+    auto blocks_for = [&](int64_t warps) { return (unsigned)std::min<int64_t>((warps + 7) / 8, 8 * (int64_t)nsm); };
+    k_bquant<<<blocks_for((int64_t)a.n * (a.D / 256)), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
+    k_broute<<<(a.n + RW - 1) / RW, 32 * RW, 0, st>>>(a, s.ids, s.w);
+    k_bgroup<<<1, 1024, 0, st>>>(s.ids, np, a.E, s.grp);
+    // one warp per (expert, tile): at most min(np, E) experts are active
+    const int64_t na_max = std::min(np, a.E);
+    pick_gateup(a.dt_gu, a.D)<<<blocks_for(na_max * ((a.de + 3) / 4)), 256, 0, st>>>(a.slots, s.grp, s.xq, a.D, a.de,
+                                                                                    a.E, a.k, s.hbuf);
+    k_bquant<<<blocks_for((int64_t)np * (a.de / 256)), 256, 0, st>>>(s.hbuf, np, a.de, s.hq);
+    const int rpt = 32 / (a.de / 256);
+    pick_down(a.dt_dn)<<<blocks_for(na_max * ((a.D + rpt - 1) / rpt)), 256, 0, st>>>(a.slots, s.grp, s.hq, a.D, a.de,
+                                                                                    a.E, a.k, s.eo);
+    k_bcombine<<<(unsigned)std::min<int64_t>(((int64_t)a.n * a.D + 255) / 256, 4 * (int64_t)nsm), 256, 0, st>>>(
+        s.eo, s.w, a.n, a.D, a.k, a.ffn);
+    count_launch(7);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "batched expert FFN launch");
+}
+
+}  // namespace tlmg

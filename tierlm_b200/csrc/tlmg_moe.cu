@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "tlmg_dev.cuh"
+#include "tlmg_batch.cuh"
 #include "tlmg_fused.cuh"
 #include "tlmg_internal.h"
 
@@ -88,11 +89,16 @@ struct tlmg_ctx {
     // many-token scratch
     float *mx = nullptr, *mlog = nullptr, *mffn = nullptr;
     int m_cap = 0;
+    // batched-decode staging on the device (host-pointer calls)
+    float *bx = nullptr, *blog = nullptr, *bffn = nullptr, *bw = nullptr;
+    int32_t *bids = nullptr;
+    int b_cap = 0;
     // pinned staging
     uint8_t *pin = nullptr;
     size_t pin_cap = 0;
     int64_t launch0 = 0;
     FusedScratch fused;
+    BatchScratch batch;            // batched-decode scratch (tlmg_expert_ffn_batch)
     bool fused_on = true;
     uint64_t *trace = nullptr;     // device [nsm][FUSED_TRACE_POINTS] when tracing
     Slot *slots_all = nullptr;     // device [n_layers][E]: every layer's slot table, contiguous
@@ -582,6 +588,7 @@ void tlmg_close(tlmg_ctx *c) {
     if (c->st) cudaStreamSynchronize(c->st);
     if (c->own_st) cudaStreamSynchronize(c->own_st);
     fused_release(c->fused);
+    batch_release(c->batch);
     c->arena.release();
     for (void *p : c->owned) cudaFree(p);
     if (c->pin) cudaFreeHost(c->pin);
@@ -903,6 +910,94 @@ int tlmg_expert_ffn_many(tlmg_ctx *c, int layer0, int n_tok, const float *x, con
         if ((rc = d2h(c, ffn, c->mffn, 4 * (size_t)n_tok * D, kf, off))) return rc;
         if ((rc = stream_sync(c))) return rc;
         finish_d2h(c, ffn, 4 * (size_t)n_tok * D, kf, off);
+    }
+    return TLMG_OK;
+}
+
+int tlmg_expert_ffn_batch(tlmg_ctx *c, int layer, int n_tok, const float *x, const float *logits, float *ffn,
+                          int32_t *ids, float *w) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (n_tok < 0) return set_error(TLMG_EINVAL, "expert_ffn_batch: n_tok %d", n_tok);
+    if (n_tok == 0) return TLMG_OK;
+    if (!x || !logits || !ffn) return set_error(TLMG_EINVAL, "expert_ffn_batch: NULL argument");
+    if (c->g.n_experts <= 0) return set_error(TLMG_EINVAL, "expert_ffn_batch: geometry has no routed experts");
+    cudaSetDevice(c->device);
+    const int D = c->g.d_model, E = c->g.n_experts, k = c->g.top_k;
+    Layer &Ly = c->L[layer];
+    if ((rc = sync_slots(c, Ly))) return rc;
+    if (!layer_ready(c, Ly)) return set_error(TLMG_ENOTFOUND, "layer %d: not every expert slot is loaded", layer);
+    PtrKind kx = ptr_kind(x);
+    const float *dx = x, *dl = logits;
+    float *df = ffn;
+    int32_t *di = ids;
+    float *dw = w;
+    PtrKind kl = PK_DEVICE, kf = PK_DEVICE;
+    const size_t bx = 4 * (size_t)n_tok * D, bl = 4 * (size_t)n_tok * E, bk = 4 * (size_t)n_tok * k;
+    if (kx != PK_DEVICE) {
+        if (n_tok > c->b_cap) {
+            void *a = dalloc(c, bx), *b = dalloc(c, bl), *f = dalloc(c, bx), *i = dalloc(c, bk), *ww = dalloc(c, bk);
+            if (!a || !b || !f || !i || !ww) return set_error(TLMG_ENOMEM, "expert_ffn_batch: scratch allocation");
+            c->bx = (float *)a;
+            c->blog = (float *)b;
+            c->bffn = (float *)f;
+            c->bids = (int32_t *)i;
+            c->bw = (float *)ww;
+            c->b_cap = n_tok;
+        }
+        kl = ptr_kind(logits);
+        kf = ptr_kind(ffn);
+        // staging: x | logits | ffn | ids | w
+        if ((rc = ensure_pin(c, 2 * bx + bl + 2 * bk + 64))) return rc;
+        if ((rc = h2d(c, c->bx, x, bx, kx, 0))) return rc;
+        if ((rc = h2d(c, c->blog, logits, bl, kl, bx))) return rc;
+        dx = c->bx;
+        dl = c->blog;
+        df = c->bffn;
+        di = ids ? c->bids : nullptr;
+        dw = w ? c->bw : nullptr;
+    }
+    if (c->fused_on && Ly.dt_gu >= 0 && Ly.dt_dn >= 0 && ((uintptr_t)dx & 15u) == 0 &&
+        batch_supported(Ly.dt_gu, Ly.dt_dn, D, c->g.d_expert, E, k)) {
+        BatchArgs a{};
+        a.slots = Ly.d_slots;
+        a.mask = Ly.mask;
+        a.bias = Ly.router_bias;
+        a.n = n_tok;
+        a.D = D;
+        a.de = c->g.d_expert;
+        a.E = E;
+        a.k = k;
+        a.router = c->g.router;
+        a.routed_scale = c->g.routed_scale;
+        a.dt_gu = Ly.dt_gu;
+        a.dt_dn = Ly.dt_dn;
+        a.x = dx;
+        a.logits = dl;
+        a.ffn = df;
+        a.ids_out = di;
+        a.w_out = dw;
+        if ((rc = launch_batch(c->batch, a, c->st))) return rc;
+    } else {
+        // dtypes or shapes the batched kernels do not serve: one call per token
+        for (int t = 0; t < n_tok; t++) {
+            if ((rc = expert_ffn_dev(c, layer, dx + (size_t)t * D, dl + (size_t)t * E, df + (size_t)t * D)))
+                return rc;
+            if (di && cudaMemcpyAsync(di + (size_t)t * k, c->ids, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st))
+                return set_error(TLMG_EIO, "ids copy");
+            if (dw && cudaMemcpyAsync(dw + (size_t)t * k, c->w, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st))
+                return set_error(TLMG_EIO, "w copy");
+        }
+    }
+    if (kx != PK_DEVICE) {
+        const size_t o_f = bx + bl, o_i = o_f + bx, o_w = o_i + bk;
+        if ((rc = d2h(c, ffn, c->bffn, bx, kf, o_f))) return rc;
+        if (ids && (rc = d2h(c, c->pin + o_i, c->bids, bk, PK_PINNED, 0))) return rc;
+        if (w && (rc = d2h(c, c->pin + o_w, c->bw, bk, PK_PINNED, 0))) return rc;
+        if ((rc = stream_sync(c))) return rc;
+        finish_d2h(c, ffn, bx, kf, o_f);
+        if (ids) memcpy(ids, c->pin + o_i, bk);
+        if (w) memcpy(w, c->pin + o_w, bk);
     }
     return TLMG_OK;
 }

@@ -126,5 +126,13 @@ class MoeContext:
         n_tok = (x.shape[0] if hasattr(x, "shape") and len(x.shape) == 2 else 1)
         check(self._lib.tlmg_expert_ffn_many(self._h, layer0, n_tok, _ptr(x), _ptr(logits), _ptr(ffn)))
 
+    def expert_ffn_batch(self, layer: int, x, logits, ffn, ids=None, w=None) -> None:
+        """Batched decode: x [n][D] and logits [n][E] of n tokens through one
+        layer; ffn [n][D], ids/w [n][top_k] out. Bit-identical per token to
+        expert_ffn; every selected expert is read once per call."""
+        n_tok = x.shape[0] if hasattr(x, "shape") and len(x.shape) == 2 else 1
+        check(self._lib.tlmg_expert_ffn_batch(self._h, layer, n_tok, _ptr(x), _ptr(logits), _ptr(ffn),
+                                              _ptr(ids), _ptr(w)))
+
     def moe_layer(self, layer: int, h, ids=None, w=None) -> None:
         check(self._lib.tlmg_moe_layer(self._h, layer, _ptr(h), _ptr(ids), _ptr(w)))
