@@ -162,6 +162,42 @@ int tlmg_expert_ffn_many(tlmg_ctx *ctx, int layer0, int n_tok, const float *x,
 int tlmg_expert_ffn_batch(tlmg_ctx *ctx, int layer, int n_tok, const float *x,
                           const float *logits, float *ffn, int32_t *ids, float *w);
 
+/* ---- Expert parallelism over n_ranks GPUs (one process per GPU).
+ * The reference runs every expert in one process; these three calls split
+ * its per-token run_batch + rank-ordered combine (src/lib/tlm_model.c:
+ * 900-938, :1029-1036) at the (token, expert) pair, so a caller can move
+ * the pairs between GPUs with an all-to-all. Expert e of a layer is owned
+ * by GPU floor(e * n_ranks / n_experts). Results are bit-identical to
+ * tlmg_expert_ffn_batch for any n_ranks. All buffers are DEVICE memory,
+ * 16-byte aligned, except counts (host). Layers need uniform K-quant
+ * gate/up and down dtypes (TLMG_EUNSUP otherwise). */
+
+/* Bytes of one dispatch record: int32 expert id, 12 zero bytes, the
+ * token's quantised input. */
+size_t tlmg_ep_record_bytes(const tlmg_ctx *ctx);
+
+/* Home GPU: route n_tok tokens (x f32[n_tok][D], logits f32[n_tok][E]) and
+ * write one record per (token, rank) pair into send (room for n_tok * top_k
+ * records), grouped by owner GPU, ascending pair order inside an owner.
+ * perm i32[n_tok * top_k] receives each pair's record index, w f32[n_tok *
+ * top_k] its routing weight, counts[n_ranks] the records per owner. Waits
+ * for the stream (the counts size the exchange). */
+int tlmg_ep_dispatch(tlmg_ctx *ctx, int layer, int n_tok, const float *x, const float *logits,
+                     int n_ranks, void *send, int32_t *perm, float *w, int64_t *counts);
+
+/* Owner GPU of experts [e_lo, e_hi) (only those need to be loaded): n_rec
+ * received records of `layer` -> eo f32[n_rec][D], one expert output row
+ * per record, in record order. A record naming an expert outside the range
+ * gets a NaN row, and the next tlmg_ep_dispatch or tlmg_check returns
+ * TLMG_EINVAL. */
+int tlmg_ep_experts(tlmg_ctx *ctx, int layer, int e_lo, int e_hi, int64_t n_rec,
+                    const void *recv, float *eo);
+
+/* Home GPU: ffn[t] = sum_r w[t * k + r] * back[perm[t * k + r]] in
+ * ascending r (back = the expert output rows returned in record order). */
+int tlmg_ep_combine(tlmg_ctx *ctx, int n_tok, const float *back, const int32_t *perm,
+                    const float *w, float *ffn);
+
 /* The whole moe() block for one token (src/lib/tlm_model.c:940-1055):
  * RMSNorm, router matvec, route, experts, shared expert, h += ffn.
  * h: f32[D] in/out; ids/w may be NULL. Host or device pointers. */

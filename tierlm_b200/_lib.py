@@ -68,6 +68,10 @@ _SIGS = {
     "tlmg_expert_ffn": (_I, [_P, _I, _P, _P, _P, _P, _P]),
     "tlmg_expert_ffn_many": (_I, [_P, _I, _I, _P, _P, _P]),
     "tlmg_expert_ffn_batch": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
+    "tlmg_ep_record_bytes": (_SZ, [_P]),
+    "tlmg_ep_dispatch": (_I, [_P, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
+    "tlmg_ep_experts": (_I, [_P, _I, _I, _I, _I64, _P, _P]),
+    "tlmg_ep_combine": (_I, [_P, _I, _P, _P, _P, _P]),
     "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
     "tlmg_set_stream": (_I, [_P, _P]),
     "tlmg_set_fused": (_I, [_P, _I]),

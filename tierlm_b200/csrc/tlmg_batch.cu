@@ -71,14 +71,25 @@ __global__ void __launch_bounds__(32 * RW) k_broute(BatchArgs a, int32_t *__rest
 // in ascending id, [2E + 1] their count, [2E + 2, ..) the pairs t * k + r
 // grouped by expert (in no particular order inside an expert: every pair's
 // results are independent of the others)
-__global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids, int np, int E, int32_t *grp) {
+__global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids, int istride, int np, int E,
+                                                  int lo, int hi, int32_t *grp, float *eo, int D, int32_t *bad) {
     __shared__ int cnt[RT_PER * 32], off[RT_PER * 32 + 1], fill[RT_PER * 32];
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         cnt[e] = 0;
         fill[e] = 0;
     }
     __syncthreads();
-    for (int p = threadIdx.x; p < np; p += blockDim.x) atomicAdd(&cnt[ids[p]], 1);
+    for (int p = threadIdx.x; p < np; p += blockDim.x) {
+        const int e = ids[(size_t)p * istride];
+        if (e >= lo && e < hi) {
+            atomicAdd(&cnt[e], 1);
+        } else {
+            // an expert outside [lo, hi): no weights here; the pair's output
+            // row becomes NaN and the host is told
+            atomicAdd(bad, 1);
+            for (int i = 0; i < D; i++) eo[(size_t)p * D + i] = __int_as_float(0x7fc00000);
+        }
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
         int s = 0, na = 0;
@@ -93,8 +104,8 @@ __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids
     __syncthreads();
     for (int e = threadIdx.x; e <= E; e += blockDim.x) grp[e] = off[e];
     for (int p = threadIdx.x; p < np; p += blockDim.x) {
-        const int e = ids[p];
-        grp[2 * E + 2 + off[e] + atomicAdd(&fill[e], 1)] = p;
+        const int e = ids[(size_t)p * istride];
+        if (e >= lo && e < hi) grp[2 * E + 2 + off[e] + atomicAdd(&fill[e], 1)] = p;
     }
 }
 
@@ -107,12 +118,11 @@ __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids
 // silu(gate) * up.
 template <int DGU, int BPL>
 __global__ void __launch_bounds__(256) k_bgateup(const Slot *__restrict__ slots, const int32_t *__restrict__ grp,
-                                                 const uint8_t *__restrict__ xq, int D, int de, int E, int k,
-                                                 float *__restrict__ hbuf) {
+                                                 const uint8_t *__restrict__ xq, size_t xstride, int xdiv, int D,
+                                                 int de, int E, float *__restrict__ hbuf) {
     const int lane = threadIdx.x & 31, p = lane >> 3, j = lane & 7;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
     const int nbx = D / 256, tiles = (de + 3) / 4, na = grp[2 * E + 1];
-    const uint32_t qx = qvb(nbx);
     const int rb = nbx * dt_block_bytes(DGU);
     for (int item = gw; item < na * tiles; item += nw) {
         const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
@@ -120,8 +130,8 @@ __global__ void __launch_bounds__(256) k_bgateup(const Slot *__restrict__ slots,
         const bool valid = row < de;
         const uint8_t *grow = slots[e].m[0] + (size_t)row * rb, *urow = slots[e].m[1] + (size_t)row * rb;
         for (int q = grp[e]; q < grp[e + 1]; q++) {
-            const int pair = grp[2 * E + 2 + q], t = pair / k;
-            const uint8_t *xb = xq + (size_t)t * qx;
+            const int pair = grp[2 * E + 2 + q];
+            const uint8_t *xb = xq + (size_t)(pair / xdiv) * xstride;
             const int16_t *xbs = reinterpret_cast<const int16_t *>(xb + 256 * nbx);
             const float *xd = reinterpret_cast<const float *>(xb + 288 * nbx);
             BlockSum vg[BPL], vu[BPL];
@@ -163,7 +173,7 @@ __global__ void __launch_bounds__(256) k_bgateup(const Slot *__restrict__ slots,
 // the row's chain in block order, lane (g, 0) writes eo[pair][row].
 template <int DDN>
 __global__ void __launch_bounds__(256) k_bdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp,
-                                               const uint8_t *__restrict__ hq, int D, int de, int E, int k,
+                                               const uint8_t *__restrict__ hq, int D, int de, int E,
                                                float *__restrict__ eo) {
     const int lane = threadIdx.x & 31, nbd = de / 256, rpt = 32 / nbd;
     const int g = lane / nbd, b = lane - g * nbd;
@@ -200,21 +210,83 @@ __global__ void __launch_bounds__(256) k_bdown(const Slot *__restrict__ slots, c
     }
 }
 
-// ffn[t][i] = sum_r w[t][r] * eo[t * k + r][i], ascending r
-__global__ void k_bcombine(const float *__restrict__ eo, const float *__restrict__ w, int n, int D, int k,
-                           float *__restrict__ ffn) {
+// ffn[t][i] = sum_r w[t][r] * eo[row(t, r)][i] in ascending r, row(t, r) =
+// perm[t * k + r] when perm is given, else t * k + r
+__global__ void k_bcombine(const float *__restrict__ eo, const int32_t *__restrict__ perm, const float *__restrict__ w,
+                           int n, int D, int k, float *__restrict__ ffn) {
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n * D; idx += gridDim.x * blockDim.x) {
         const int t = idx / D, i = idx - t * D;
         float f = 0.0f;
-        for (int r = 0; r < k; r++) f = __fadd_rn(f, __fmul_rn(w[(size_t)t * k + r], eo[((size_t)t * k + r) * D + i]));
+        for (int r = 0; r < k; r++) {
+            const int row = perm ? perm[t * k + r] : t * k + r;
+            f = __fadd_rn(f, __fmul_rn(w[(size_t)t * k + r], eo[(size_t)row * D + i]));
+        }
         ffn[idx] = f;
+    }
+}
+
+// Expert-parallel dispatch layout. Pair p = t * k + r goes to the GPU owning
+// expert ids[p], owner(e) = floor(e * nr / E); records are grouped by owner,
+// inside an owner in ascending pair order. perm[p] = the pair's record index,
+// cnt[d] = records for owner d.
+__global__ void __launch_bounds__(1024) k_epcount(const int32_t *__restrict__ ids, int np, int E, int nr,
+                                                   int32_t *__restrict__ perm, int32_t *__restrict__ cnt) {
+    __shared__ int tot[EP_MAX_RANKS], base[EP_MAX_RANKS], wsum[32];
+    const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    for (int d = threadIdx.x; d < nr; d += blockDim.x) tot[d] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < np; p += blockDim.x) atomicAdd(&tot[(int)((int64_t)ids[p] * nr / E)], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0;
+        for (int d = 0; d < nr; d++) {
+            base[d] = s;
+            cnt[d] = tot[d];
+            s += tot[d];
+        }
+    }
+    __syncthreads();
+    for (int c0 = 0; c0 < np; c0 += blockDim.x) {
+        const int p = c0 + threadIdx.x;
+        const int me = p < np ? (int)((int64_t)ids[p] * nr / E) : -1;
+        for (int d = 0; d < nr; d++) {
+            const unsigned m = __ballot_sync(0xFFFFFFFFu, me == d);
+            if (lane == 0) wsum[wi] = __popc(m);
+            __syncthreads();
+            if (me == d) {
+                int before = 0;
+                for (int v = 0; v < wi; v++) before += wsum[v];
+                perm[p] = base[d] + before + __popc(m & ((1u << lane) - 1u));
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                int s = 0;
+                for (int v = 0; v < nwarp; v++) s += wsum[v];
+                base[d] += s;
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// One warp per pair: record perm[p] = { int32 expert id, 12 zero bytes,
+// the token's quantised vector (qx bytes) }.
+__global__ void k_eppack(const int32_t *__restrict__ ids, const int32_t *__restrict__ perm, int np, int k,
+                         const uint8_t *__restrict__ xq, uint32_t qx, uint8_t *__restrict__ send, size_t rec) {
+    const int lane = threadIdx.x & 31;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+    for (int p = gw; p < np; p += nw) {
+        uint8_t *dst = send + (size_t)perm[p] * rec;
+        const uint4 *src = reinterpret_cast<const uint4 *>(xq + (size_t)(p / k) * qx);
+        if (lane == 0) *reinterpret_cast<uint4 *>(dst) = make_uint4((uint32_t)ids[p], 0u, 0u, 0u);
+        for (uint32_t i = lane; i < qx / 16; i += 32) reinterpret_cast<uint4 *>(dst + 16)[i] = __ldg(src + i);
     }
 }
 
 }  // namespace
 
-using GateUpFn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, int, float *);
-using DownFn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, int, float *);
+using GateUpFn = void (*)(const Slot *, const int32_t *, const uint8_t *, size_t, int, int, int, int, float *);
+using DownFn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, float *);
 
 static GateUpFn pick_gateup(int dt, int D) {
     const bool two = D > 2048;
@@ -239,29 +311,75 @@ bool batch_supported(int dt_gu, int dt_dn, int D, int de, int E, int k) {
            de / 256 <= 32 && E > 0 && E <= RT_PER * 32 && k > 0 && k <= BMAXK && k <= E;
 }
 
+size_t ep_record_bytes(int D) { return 16 + qvb(D / 256); }
+
 void batch_release(BatchScratch &s) {
     for (void *p : { (void *)s.xq, (void *)s.ids, (void *)s.w, (void *)s.grp, (void *)s.hbuf, (void *)s.hq,
                      (void *)s.eo })
         if (p) cudaFree(p);
+    if (s.cnt) cudaFreeHost(s.cnt);
     s = BatchScratch{};
 }
 
-int batch_reserve(BatchScratch &s, int n, int D, int de, int E, int k) {
-    if (n <= s.cap) return TLMG_OK;
+// Grows the scratch to hold n_tok tokens and n_pairs (token, expert) pairs.
+static int reserve(BatchScratch &s, int n_tok, int64_t n_pairs, int D, int de, int E) {
+    if (n_tok <= s.cap && n_pairs <= s.cap_pairs && E <= s.cap_e) return TLMG_OK;
+    const int cap = std::max({ n_tok, s.cap, 16 });
+    const int64_t np = std::max<int64_t>({ n_pairs, s.cap_pairs, 64 });
+    const int ce = std::max(E, s.cap_e);
     batch_release(s);
-    const int cap = n < 16 ? 16 : n;
-    const size_t np = (size_t)cap * k;
-    if (cudaMalloc(&s.xq, (size_t)cap * qvb(D / 256)) != cudaSuccess ||
-        cudaMalloc(&s.ids, 4 * np) != cudaSuccess || cudaMalloc(&s.w, 4 * np) != cudaSuccess ||
-        cudaMalloc(&s.grp, 4 * (2 * (size_t)E + 2 + np)) != cudaSuccess ||
+    if (cudaMalloc(&s.xq, (size_t)cap * qvb(D / 256)) != cudaSuccess || cudaMalloc(&s.ids, 4 * np) != cudaSuccess ||
+        cudaMalloc(&s.w, 4 * np) != cudaSuccess || cudaMalloc(&s.grp, 4 * (2 * (size_t)ce + 2 + np)) != cudaSuccess ||
         cudaMalloc(&s.hbuf, 4 * np * de) != cudaSuccess || cudaMalloc(&s.hq, np * qvb(de / 256)) != cudaSuccess ||
-        cudaMalloc(&s.eo, 4 * np * D) != cudaSuccess) {
+        cudaMalloc(&s.eo, 4 * np * D) != cudaSuccess || cudaMallocHost(&s.cnt, 4 * (EP_MAX_RANKS + 1)) != cudaSuccess) {
         cudaGetLastError();
         batch_release(s);
-        return set_error(TLMG_ENOMEM, "batched expert FFN scratch for %d tokens", n);
+        return set_error(TLMG_ENOMEM, "batched expert FFN scratch for %d tokens / %lld pairs", n_tok,
+                         (long long)n_pairs);
     }
+    s.cnt[EP_MAX_RANKS] = 0;
     s.cap = cap;
+    s.cap_pairs = np;
+    s.cap_e = ce;
     return TLMG_OK;
+}
+
+int batch_reserve(BatchScratch &s, int n, int D, int de, int E, int k) {
+    return reserve(s, n, (int64_t)n * k, D, de, E);
+}
+
+static int sm_count() {
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    return nsm;
+}
+
+static unsigned warp_blocks(int64_t warps, int nsm) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, 8 * (int64_t)nsm));
+}
+
+// The expert stage shared by batched decode and the expert-parallel owner:
+// np pairs, pair q's expert id at ids[q * istride] and its quantised input at
+// x + (q / xdiv) * xstride -> eo[q] (f32 [D]).
+static void expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, int de, int E, int lo,
+                         int hi, const int32_t *ids, int istride, int64_t np, const uint8_t *x, size_t xstride,
+                         int xdiv, float *eo, cudaStream_t st) {
+    const int nsm = sm_count();
+    k_bgroup<<<1, 1024, 0, st>>>(ids, istride, (int)np, E, lo, hi, s.grp, eo, D, s.cnt + EP_MAX_RANKS);
+    // one warp per (expert, tile): at most min(np, E) experts are active
+    const int64_t na_max = std::min<int64_t>(np, E);
+    pick_gateup(dt_gu, D)<<<warp_blocks(na_max * ((de + 3) / 4), nsm), 256, 0, st>>>(slots, s.grp, x, xstride, xdiv,
+                                                                                    D, de, E, s.hbuf);
+    k_bquant<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, (int)np, de, s.hq);
+    const int rpt = 32 / (de / 256);
+    pick_down(dt_dn)<<<warp_blocks(na_max * ((D + rpt - 1) / rpt), nsm), 256, 0, st>>>(slots, s.grp, s.hq, D, de, E,
+                                                                                      eo);
+    count_launch(4);
+}
+
+static unsigned combine_blocks(int n, int D) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)n * D + 255) / 256, 4 * (int64_t)sm_count()));
 }
 
 int launch_batch(BatchScratch &s, const BatchArgs &a, cudaStream_t st) {
@@ -270,27 +388,76 @@ int launch_batch(BatchScratch &s, const BatchArgs &a, cudaStream_t st) {
     if (a.n <= 0) return TLMG_OK;
     int rc = batch_reserve(s, a.n, a.D, a.de, a.E, a.k);
     if (rc) return rc;
-    int dev = 0, nsm = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    const int np = a.n * a.k;
-    auto blocks_for = [&](int64_t warps) { return (unsigned)std::min<int64_t>((warps + 7) / 8, 8 * (int64_t)nsm); };
-    k_bquant<<<blocks_for((int64_t)a.n * (a.D / 256)), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
+    const int np = a.n * a.k, nsm = sm_count();
+    k_bquant<<<warp_blocks((int64_t)a.n * (a.D / 256), nsm), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
     k_broute<<<(a.n + RW - 1) / RW, 32 * RW, 0, st>>>(a, s.ids, s.w);
-    k_bgroup<<<1, 1024, 0, st>>>(s.ids, np, a.E, s.grp);
-    // one warp per (expert, tile): at most min(np, E) experts are active
-    const int64_t na_max = std::min(np, a.E);
-    pick_gateup(a.dt_gu, a.D)<<<blocks_for(na_max * ((a.de + 3) / 4)), 256, 0, st>>>(a.slots, s.grp, s.xq, a.D, a.de,
-                                                                                    a.E, a.k, s.hbuf);
-    k_bquant<<<blocks_for((int64_t)np * (a.de / 256)), 256, 0, st>>>(s.hbuf, np, a.de, s.hq);
-    const int rpt = 32 / (a.de / 256);
-    pick_down(a.dt_dn)<<<blocks_for(na_max * ((a.D + rpt - 1) / rpt)), 256, 0, st>>>(a.slots, s.grp, s.hq, a.D, a.de,
-                                                                                    a.E, a.k, s.eo);
-    k_bcombine<<<(unsigned)std::min<int64_t>(((int64_t)a.n * a.D + 255) / 256, 4 * (int64_t)nsm), 256, 0, st>>>(
-        s.eo, s.w, a.n, a.D, a.k, a.ffn);
-    count_launch(7);
+    count_launch(2);
+    expert_stage(s, a.slots, a.dt_gu, a.dt_dn, a.D, a.de, a.E, 0, a.E, s.ids, 1, np, s.xq, qvb(a.D / 256), a.k, s.eo,
+                 st);
+    k_bcombine<<<combine_blocks(a.n, a.D), 256, 0, st>>>(s.eo, nullptr, s.w, a.n, a.D, a.k, a.ffn);
+    count_launch(1);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "batched expert FFN launch");
+}
+
+int ep_dispatch(BatchScratch &s, const BatchArgs &a, int nr, uint8_t *send, int32_t *perm, float *w, int64_t *counts,
+                cudaStream_t st) {
+    if (!batch_supported(a.dt_gu, a.dt_dn, a.D, a.de, a.E, a.k))
+        return set_error(TLMG_EUNSUP, "expert-parallel dispatch: dtypes %d/%d or shape unsupported", a.dt_gu, a.dt_dn);
+    if (nr < 1 || nr > EP_MAX_RANKS || nr > a.E)
+        return set_error(TLMG_EINVAL, "expert-parallel dispatch: %d ranks (1..%d, at most E)", nr, EP_MAX_RANKS);
+    if (a.n <= 0) {
+        for (int d = 0; d < nr; d++) counts[d] = 0;
+        return TLMG_OK;
+    }
+    int rc = batch_reserve(s, a.n, a.D, a.de, a.E, a.k);
+    if (rc) return rc;
+    const int np = a.n * a.k, nsm = sm_count();
+    const uint32_t qx = qvb(a.D / 256);
+    BatchArgs r = a;
+    r.w_out = w;
+    k_bquant<<<warp_blocks((int64_t)a.n * (a.D / 256), nsm), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
+    k_broute<<<(a.n + RW - 1) / RW, 32 * RW, 0, st>>>(r, s.ids, s.w);
+    k_epcount<<<1, 1024, 0, st>>>(s.ids, np, a.E, nr, perm, s.cnt);
+    k_eppack<<<warp_blocks(np, nsm), 256, 0, st>>>(s.ids, perm, np, a.k, s.xq, qx, send, ep_record_bytes(a.D));
+    count_launch(4);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);    // the record counts size the exchange
+    if (e != cudaSuccess) return cuda_fail(e, "expert-parallel dispatch");
+    for (int d = 0; d < nr; d++) counts[d] = s.cnt[d];
+    return batch_take_error(s);
+}
+
+int ep_experts(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, int de, int E, int lo, int hi,
+               int64_t n_rec, const uint8_t *recv, float *eo, cudaStream_t st) {
+    if (!batch_supported(dt_gu, dt_dn, D, de, E, 1))
+        return set_error(TLMG_EUNSUP, "expert-parallel experts: dtypes %d/%d or shape unsupported", dt_gu, dt_dn);
+    if (n_rec <= 0) return TLMG_OK;
+    if (n_rec > INT32_MAX / 2) return set_error(TLMG_EINVAL, "expert-parallel experts: %lld records", (long long)n_rec);
+    int rc = reserve(s, 1, n_rec, D, de, E);
+    if (rc) return rc;
+    const size_t rec = ep_record_bytes(D);
+    expert_stage(s, slots, dt_gu, dt_dn, D, de, E, lo, hi, reinterpret_cast<const int32_t *>(recv), (int)(rec / 4),
+                 n_rec, recv + 16, rec, 1, eo, st);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "expert-parallel expert launch");
+}
+
+int batch_take_error(BatchScratch &s) {
+    if (!s.cnt || s.cnt[EP_MAX_RANKS] == 0) return TLMG_OK;
+    const int n = s.cnt[EP_MAX_RANKS];
+    s.cnt[EP_MAX_RANKS] = 0;
+    return set_error(TLMG_EINVAL, "expert parallel: %d received records named experts this GPU does not own "
+                                  "(their output rows are NaN)", n);
+}
+
+int ep_combine(int n, int D, int k, const float *back, const int32_t *perm, const float *w, float *ffn,
+               cudaStream_t st) {
+    if (n <= 0) return TLMG_OK;
+    k_bcombine<<<combine_blocks(n, D), 256, 0, st>>>(back, perm, w, n, D, k, ffn);
+    count_launch(1);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "expert-parallel combine launch");
 }
 
 }  // namespace tlmg

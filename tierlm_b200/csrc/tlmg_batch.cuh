@@ -10,9 +10,13 @@
 
 namespace tlmg {
 
+constexpr int EP_MAX_RANKS = 64;   // expert-parallel GPUs per dispatch
+
 // Device scratch of one batched call, for up to `cap` tokens.
 struct BatchScratch {
-    int cap = 0;
+    int cap = 0;                // tokens
+    int64_t cap_pairs = 0;      // (token, expert) pairs or received records
+    int cap_e = 0;              // experts
     uint8_t *xq = nullptr;      // [cap] quantised inputs (swizzled Q8_K vectors)
     int32_t *ids = nullptr;     // [cap][k]
     float *w = nullptr;         // [cap][k]
@@ -20,6 +24,8 @@ struct BatchScratch {
     float *hbuf = nullptr;      // [cap * k][de] SwiGLU rows per (token, rank) pair
     uint8_t *hq = nullptr;      // [cap * k] quantised h per pair
     float *eo = nullptr;        // [cap * k][D] expert outputs per pair
+    int32_t *cnt = nullptr;     // pinned host [EP_MAX_RANKS + 1]: dispatch record counts, then the count of
+                                // received records naming an expert outside the owner's range
 };
 
 struct BatchArgs {
@@ -42,5 +48,27 @@ int batch_reserve(BatchScratch &s, int n, int D, int de, int E, int k);
 void batch_release(BatchScratch &s);
 // Queues the whole batched call on `st` (no host synchronisation).
 int launch_batch(BatchScratch &s, const BatchArgs &a, cudaStream_t st);
+
+// Expert parallelism over nr GPUs: expert e is owned by GPU floor(e * nr / E).
+// A dispatch record is { int32 expert id, 12 zero bytes, the token's
+// quantised input (swizzled Q8_K vector) }.
+size_t ep_record_bytes(int D);
+// Home GPU: quantise + route a.n tokens, write one record per (token, rank)
+// pair into `send` grouped by owner (ascending pair order inside an owner),
+// perm[t * k + r] = the pair's record index, w[t * k + r] its weight,
+// counts[d] = records for owner d (waits for the stream).
+int ep_dispatch(BatchScratch &s, const BatchArgs &a, int nr, uint8_t *send, int32_t *perm, float *w, int64_t *counts,
+                cudaStream_t st);
+// Owner GPU of experts [lo, hi): n_rec received records -> eo [n_rec][D],
+// one row per record (NaN rows for records outside [lo, hi), counted for
+// batch_take_error).
+int ep_experts(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, int de, int E, int lo, int hi,
+               int64_t n_rec, const uint8_t *recv, float *eo, cudaStream_t st);
+// TLMG_EINVAL (and a reset) once records outside an owner's range were seen;
+// read after the stream has been synchronised.
+int batch_take_error(BatchScratch &s);
+// Home GPU: ffn[t] = sum_r w[t * k + r] * back[perm[t * k + r]] in ascending r.
+int ep_combine(int n, int D, int k, const float *back, const int32_t *perm, const float *w, float *ffn,
+               cudaStream_t st);
 
 }  // namespace tlmg

@@ -150,15 +150,17 @@ static int sync_slots(tlmg_ctx *c, Layer &Ly) {
                                cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "slot table upload");
     Ly.slots_dirty = false;
-    // the persistent kernel serves layers whose experts all share one
-    // gate/up dtype and one down dtype
+    // the persistent and batched kernels serve layers whose (loaded) experts
+    // all share one gate/up dtype and one down dtype; calls that need every
+    // expert check layer_ready() as well
     int dgu = -1, ddn = -1;
     bool uniform = true;
     for (const Slot &sl : Ly.h_slots) {
-        if (!sl.ok) { uniform = false; break; }
+        if (!sl.ok) continue;
         if (dgu < 0) { dgu = sl.dt[0]; ddn = sl.dt[2]; }
         if (sl.dt[0] != dgu || sl.dt[1] != dgu || sl.dt[2] != ddn) uniform = false;
     }
+    uniform = uniform && dgu >= 0;
     Ly.dt_gu = uniform ? dgu : -1;
     Ly.dt_dn = uniform ? ddn : -1;
     Ly.fused_plan = uniform ? fused_plan(c->fused, c->g, dgu, ddn) : nullptr;
@@ -511,6 +513,7 @@ static int finish_d2h(tlmg_ctx *c, void *dst, size_t bytes, PtrKind k, size_t st
 static int stream_sync(tlmg_ctx *c) {
     cudaError_t e = cudaStreamSynchronize(c->st);
     if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    if (int be = batch_take_error(c->batch)) return be;
     uint32_t fe = fused_take_error(c->fused);
     if (fe)
         return set_error(TLMG_EIO, "expert FFN kernel gave up waiting (%s%s%s); results of this call are invalid",
@@ -1000,6 +1003,76 @@ int tlmg_expert_ffn_batch(tlmg_ctx *c, int layer, int n_tok, const float *x, con
         if (w) memcpy(w, c->pin + o_w, bk);
     }
     return TLMG_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism: dispatch / owner experts / combine (device pointers)
+
+static int ep_layer(tlmg_ctx *c, int layer, Layer **out) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (c->g.n_experts <= 0) return set_error(TLMG_EINVAL, "expert parallel: geometry has no routed experts");
+    cudaSetDevice(c->device);
+    Layer &Ly = c->L[layer];
+    if ((rc = sync_slots(c, Ly))) return rc;
+    if (Ly.dt_gu < 0 || Ly.dt_dn < 0 ||
+        !batch_supported(Ly.dt_gu, Ly.dt_dn, c->g.d_model, c->g.d_expert, c->g.n_experts, c->g.top_k))
+        return set_error(TLMG_EUNSUP, "expert parallel: layer %d needs uniform K-quant gate/up and down dtypes", layer);
+    *out = &Ly;
+    return TLMG_OK;
+}
+
+size_t tlmg_ep_record_bytes(const tlmg_ctx *c) { return c ? ep_record_bytes(c->g.d_model) : 0; }
+
+int tlmg_ep_dispatch(tlmg_ctx *c, int layer, int n_tok, const float *x, const float *logits, int n_ranks, void *send,
+                     int32_t *perm, float *w, int64_t *counts) {
+    Layer *Ly = nullptr;
+    int rc = ep_layer(c, layer, &Ly);
+    if (rc) return rc;
+    if (n_tok < 0 || !counts || (n_tok > 0 && (!x || !logits || !send || !perm || !w)))
+        return set_error(TLMG_EINVAL, "ep_dispatch: bad argument");
+    if (n_tok > 0 && (ptr_kind(x) != PK_DEVICE || ptr_kind(send) != PK_DEVICE || ((uintptr_t)x & 15u) ||
+                      ((uintptr_t)send & 15u)))
+        return set_error(TLMG_EINVAL, "ep_dispatch: x and send must be 16-byte aligned device memory");
+    BatchArgs a{};
+    a.slots = Ly->d_slots;
+    a.mask = Ly->mask;
+    a.bias = Ly->router_bias;
+    a.n = n_tok;
+    a.D = c->g.d_model;
+    a.de = c->g.d_expert;
+    a.E = c->g.n_experts;
+    a.k = c->g.top_k;
+    a.router = c->g.router;
+    a.routed_scale = c->g.routed_scale;
+    a.dt_gu = Ly->dt_gu;
+    a.dt_dn = Ly->dt_dn;
+    a.x = x;
+    a.logits = logits;
+    return ep_dispatch(c->batch, a, n_ranks, (uint8_t *)send, perm, w, counts, c->st);
+}
+
+int tlmg_ep_experts(tlmg_ctx *c, int layer, int e_lo, int e_hi, int64_t n_rec, const void *recv, float *eo) {
+    Layer *Ly = nullptr;
+    int rc = ep_layer(c, layer, &Ly);
+    if (rc) return rc;
+    if (n_rec < 0 || (n_rec > 0 && (!recv || !eo)) || e_lo < 0 || e_hi > c->g.n_experts || e_lo > e_hi)
+        return set_error(TLMG_EINVAL, "ep_experts: bad argument");
+    if (n_rec > 0 && (ptr_kind(recv) != PK_DEVICE || ((uintptr_t)recv & 15u)))
+        return set_error(TLMG_EINVAL, "ep_experts: recv must be 16-byte aligned device memory");
+    for (int e = e_lo; e < e_hi; e++)
+        if (!Ly->h_slots[e].ok)
+            return set_error(TLMG_ENOTFOUND, "layer %d: owned expert %d is not loaded", layer, e);
+    return ep_experts(c->batch, Ly->d_slots, Ly->dt_gu, Ly->dt_dn, c->g.d_model, c->g.d_expert, c->g.n_experts, e_lo,
+                      e_hi, n_rec, (const uint8_t *)recv, eo, c->st);
+}
+
+int tlmg_ep_combine(tlmg_ctx *c, int n_tok, const float *back, const int32_t *perm, const float *w, float *ffn) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    if (n_tok < 0 || (n_tok > 0 && (!back || !perm || !w || !ffn)))
+        return set_error(TLMG_EINVAL, "ep_combine: bad argument");
+    cudaSetDevice(c->device);
+    return ep_combine(n_tok, c->g.d_model, c->g.top_k, back, perm, w, ffn, c->st);
 }
 
 int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {

@@ -134,5 +134,28 @@ class MoeContext:
         check(self._lib.tlmg_expert_ffn_batch(self._h, layer, n_tok, _ptr(x), _ptr(logits), _ptr(ffn),
                                               _ptr(ids), _ptr(w)))
 
+    # ---- expert parallelism (device buffers; see tierlm_b200.ep)
+    @property
+    def ep_record_bytes(self) -> int:
+        return int(self._lib.tlmg_ep_record_bytes(self._h))
+
+    def ep_dispatch(self, layer: int, x, logits, n_ranks: int, send, perm, w) -> list[int]:
+        """Route + quantise x [n][D]; pack one record per (token, rank) pair
+        into send grouped by owner GPU; returns the records per owner."""
+        n_tok = x.shape[0]
+        counts = (C.c_int64 * n_ranks)()
+        check(self._lib.tlmg_ep_dispatch(self._h, layer, n_tok, _ptr(x), _ptr(logits), n_ranks, _ptr(send),
+                                         _ptr(perm), _ptr(w), counts))
+        return list(counts)
+
+    def ep_experts(self, layer: int, e_lo: int, e_hi: int, n_rec: int, recv, eo) -> None:
+        """Owner side of experts [e_lo, e_hi): n_rec received records -> eo [n_rec][D]."""
+        check(self._lib.tlmg_ep_experts(self._h, layer, e_lo, e_hi, n_rec, _ptr(recv) if n_rec else None,
+                                        _ptr(eo) if n_rec else None))
+
+    def ep_combine(self, n_tok: int, back, perm, w, ffn) -> None:
+        """Home side: ffn[t] = sum_r w[t, r] * back[perm[t, r]] in ascending r."""
+        check(self._lib.tlmg_ep_combine(self._h, n_tok, _ptr(back), _ptr(perm), _ptr(w), _ptr(ffn)))
+
     def moe_layer(self, layer: int, h, ids=None, w=None) -> None:
         check(self._lib.tlmg_moe_layer(self._h, layer, _ptr(h), _ptr(ids), _ptr(w)))
