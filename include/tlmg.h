@@ -214,6 +214,14 @@ int tlmg_set_stream(tlmg_ctx *ctx, void *stream);
  * give identical bits. TLMG_EUNSUP when on = 1 and the device cannot run
  * the persistent kernel (the multi-kernel path stays in use). */
 int tlmg_set_fused(tlmg_ctx *ctx, int on);
+/* Expert kernels of tlmg_expert_ffn_batch and the expert-parallel owner:
+ * mode 2 (default) the tensor-core kernels (tcgen05.mma kind::i8, one int32
+ * TMEM accumulator per K-quant sub-block), 1 the tiled CUDA-core kernels (a
+ * CTA per 64-row tile of an expert, one thread per row and token), 0 the
+ * warp-per-row-tile kernels; 10 * g + d selects gate/up mode g and down
+ * mode d separately. Each falls back to the next lower mode for dtypes or
+ * shapes it does not serve. Identical bits in every mode. */
+int tlmg_set_batch_kernels(tlmg_ctx *ctx, int mode);
 /* Wait for the context's queued work and report a failure the kernels
  * raised since the last check (a bounded wait that expired: TLMG_EIO). */
 int tlmg_check(tlmg_ctx *ctx);

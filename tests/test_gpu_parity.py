@@ -366,6 +366,7 @@ BATCH_SHAPES = [
     (4096, 1536, 12, 8, (12, 12, 12), 0, 9, True),    # two blocks per lane, nbd = 6 (30 of 32 lanes)
     (1024, 512, 160, 6, (12, 12, 13), 0, 33, True),   # E > 128
     (1024, 512, 40, 4, (12, 12, 14), 1, 17, True),    # sigmoid router
+    (1024, 512, 4, 4, (12, 12, 14), 0, 40, True),     # every expert > 16 tokens: several passes per tile
     (1024, 768, 8, 2, (13, 13, 15), 0, 4, False),     # Q8_K down: per-token fallback
 ]
 
@@ -398,12 +399,14 @@ def test_expert_ffn_batch_matches_single(dev, orc, shape):
         bad = np.flatnonzero(~same_bits(one, out[t]))
         assert bad.size == 0, (t, bad[:4], out[t][bad[:4]], one[bad[:4]])
     xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
-    od = torch.zeros((T, D), device=dev)
-    n0 = ctx.launches
-    ctx.expert_ffn_batch(0, xd, ld, od)
-    ctx.check()
-    assert ((ctx.launches - n0) == 7) == batched, ctx.launches - n0
-    assert same_bits(od.cpu().numpy(), out).all()
+    for tiled in ("warp", "tiled", "mma"):        # every batched kernel variant
+        ctx.set_batch_kernels(tiled)
+        od = torch.zeros((T, D), device=dev)
+        n0 = ctx.launches
+        ctx.expert_ffn_batch(0, xd, ld, od)
+        ctx.check()
+        assert ((ctx.launches - n0) == 7) == batched, ctx.launches - n0
+        assert same_bits(od.cpu().numpy(), out).all(), tiled
     orc.set_expf_mode(1)
     try:
         geom = dict(d_model=D, d_expert=de, n_experts=E, top_k=k, router=router)

@@ -75,6 +75,7 @@ _SIGS = {
     "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
     "tlmg_set_stream": (_I, [_P, _P]),
     "tlmg_set_fused": (_I, [_P, _I]),
+    "tlmg_set_batch_kernels": (_I, [_P, _I]),
     "tlmg_check": (_I, [_P]),
     "tlmg_trace": (_I, [_P, _I, _P, _I]),
     "tlmg_profile": (_I, [_P, _I]),

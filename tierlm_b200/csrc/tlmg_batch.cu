@@ -20,11 +20,14 @@
 // with the correctly rounded expf), so results are bit-identical to
 // tlmg_expert_ffn on each token.
 #include <algorithm>
+#include <utility>
+#include <vector>
 
 #include "tlmg_batch.cuh"
 #include "tlmg_dev.cuh"
 #include "tlmg_internal.h"
 #include "tlmg_kq.cuh"
+#include "tlmg_mma.cuh"
 
 namespace tlmg {
 
@@ -283,6 +286,156 @@ __global__ void k_eppack(const int32_t *__restrict__ ids, const int32_t *__restr
     }
 }
 
+// ---------------------------------------------------------------------------
+// Tiled expert kernels: one CTA works on a tile of TR rows of one expert for
+// all of the expert's tokens (up to TC per pass). Thread (row, tq) owns one
+// weight row and the tokens tq, tq + TQ, ...; it walks the row's blocks in
+// ascending order, so every (row, token) chain stays in one thread (no
+// shuffles) and each weight byte is read from HBM once per pass. Weights are
+// staged with cp.async into shared memory; the tokens' quantised inputs are
+// staged once per pass and read by all rows as broadcasts.
+
+constexpr int TR = 64;              // rows per tile
+constexpr int TQ = 4;               // token lanes per row: 256 threads
+constexpr int TC = 16;              // tokens per pass
+constexpr int TPT = TC / TQ;        // tokens per thread per pass
+constexpr int NSG = 4;              // gate/up block-column stages
+
+template <int DT> constexpr int bbytes() { return DT == DT_Q4_K ? 144 : DT == DT_Q5_K ? 176 : 210; }
+
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// copy n16 16-byte pieces src -> dst with all threads of the CTA
+__device__ __forceinline__ void cp_span(uint8_t *dst, const uint8_t *src, int n16) {
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) cp16(dst + 16 * i, src + 16 * i);
+}
+
+__device__ __forceinline__ XBlk xblk_at(const uint8_t *v, int nb, int b) {
+    return XBlk{ v, nb, b, reinterpret_cast<const int16_t *>(v + 256 * nb) + 16 * b,
+                 reinterpret_cast<const float *>(v + 288 * nb)[b] };
+}
+
+// gate/up of Q4_K / Q5_K (16-byte aligned blocks): block column b of the
+// tile's gate and up rows is staged as [2][TR][BB] (row stride BB = 9 or 11
+// 16-byte units, odd, so the rows' 16-byte loads are free of bank conflicts).
+template <int DGU>
+__global__ void __launch_bounds__(TR * TQ, 2)
+    k_tgateup(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
+              size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ hbuf) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    constexpr int BB = bbytes<DGU>(), CPB = BB / 16;
+    const int nbx = D / 256;
+    const uint32_t qx = qvb(nbx);
+    uint8_t *sw = sm, *sx = sm + NSG * 2 * TR * BB;
+    const int tid = threadIdx.x, row = tid % TR, tq = tid / TR;
+    const int tiles = de / TR, na = grp[2 * E + 1];
+    const size_t rb = (size_t)nbx * BB;
+    const int32_t *pairs = grp + 2 * E + 2;
+    for (int item = blockIdx.x; item < na * tiles; item += gridDim.x) {
+        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+        const uint8_t *wsg = slots[e].m[0] + (size_t)tile * TR * rb, *wsu = slots[e].m[1] + (size_t)tile * TR * rb;
+        auto issue = [&](int b) {
+            if (b < nbx) {
+                uint8_t *st = sw + (b % NSG) * 2 * TR * BB;
+                for (int i = tid; i < 2 * TR * CPB; i += TR * TQ) {
+                    const int m = i / (TR * CPB), r = (i / CPB) % TR, c = i % CPB;
+                    cp16(st + (m * TR + r) * BB + 16 * c, (m ? wsu : wsg) + r * rb + (size_t)b * BB + 16 * c);
+                }
+            }
+            cp_commit();
+        };
+        for (int c0 = grp[e]; c0 < grp[e + 1]; c0 += TC) {
+            const int nt = min(TC, grp[e + 1] - c0);
+            for (int t = 0; t < nt; t++) cp_span(sx + t * qx, x + (size_t)(pairs[c0 + t] / xdiv) * xstride, qx / 16);
+#pragma unroll
+            for (int b = 0; b < NSG - 1; b++) issue(b);
+            float ag[TPT], au[TPT];
+#pragma unroll
+            for (int i = 0; i < TPT; i++) ag[i] = au[i] = 0.0f;
+            for (int b = 0; b < nbx; b++) {
+                cp_wait<NSG - 2>();
+                __syncthreads();
+                issue(b + NSG - 1);
+                const uint8_t *st = sw + (b % NSG) * 2 * TR * BB;
+                const uint8_t *w2[2] = { st + row * BB, st + (TR + row) * BB };
+#pragma unroll
+                for (int i = 0; i < TPT; i++) {
+                    const int t = tq + TQ * i;
+                    if (t < nt) {
+                        BlockSum o[2];
+                        kblock_dot<DGU, 2>(w2, xblk_at(sx + t * qx, nbx, b), o);
+                        ag[i] = chain<DGU>(ag[i], o[0].dA, o[0].is, o[0].dM, o[0].ms);
+                        au[i] = chain<DGU>(au[i], o[1].dA, o[1].is, o[1].dM, o[1].ms);
+                    }
+                }
+            }
+            cp_wait<0>();
+            __syncthreads();   // stages and staged inputs are rewritten next
+#pragma unroll
+            for (int i = 0; i < TPT; i++) {
+                const int t = tq + TQ * i;
+                if (t < nt) hbuf[(size_t)pairs[c0 + t] * de + tile * TR + row] = __fmul_rn(silu_f(ag[i]), au[i]);
+            }
+        }
+    }
+}
+
+// down: the tile's TR rows (all nbd blocks, contiguous in HBM) are staged
+// once per tile; the expert's quantised h rows are staged per pass of TC.
+template <int DDN>
+__global__ void __launch_bounds__(TR * TQ, 2)
+    k_tdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ hq, int D,
+            int de, int E, float *__restrict__ eo) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    constexpr int BB = bbytes<DDN>();
+    const int nbd = de / 256;
+    const uint32_t qh = qvb(nbd);
+    const int rbd = nbd * BB;
+    const int wtile = up16b((uint32_t)(TR * rbd));
+    uint8_t *sw = sm, *sx = sm + wtile;
+    const int tid = threadIdx.x, row = tid % TR, tq = tid / TR;
+    const int tiles = D / TR, na = grp[2 * E + 1];
+    const int32_t *pairs = grp + 2 * E + 2;
+    for (int item = blockIdx.x; item < na * tiles; item += gridDim.x) {
+        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+        cp_span(sw, slots[e].m[2] + (size_t)tile * TR * rbd, TR * rbd / 16);
+        for (int c0 = grp[e]; c0 < grp[e + 1]; c0 += TC) {
+            const int nt = min(TC, grp[e + 1] - c0);
+            for (int t = 0; t < nt; t++) cp_span(sx + t * qh, hq + (size_t)pairs[c0 + t] * qh, qh / 16);
+            cp_commit();
+            cp_wait<0>();
+            __syncthreads();
+            const uint8_t *w1[1] = { sw + row * rbd };
+            float acc[TPT];
+#pragma unroll
+            for (int i = 0; i < TPT; i++) acc[i] = 0.0f;
+            for (int b = 0; b < nbd; b++) {
+                const uint8_t *wb[1] = { w1[0] + b * BB };
+#pragma unroll
+                for (int i = 0; i < TPT; i++) {
+                    const int t = tq + TQ * i;
+                    if (t < nt) {
+                        BlockSum o[1];
+                        kblock_dot<DDN, 1>(wb, xblk_at(sx + t * qh, nbd, b), o);
+                        acc[i] = chain<DDN>(acc[i], o[0].dA, o[0].is, o[0].dM, o[0].ms);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < TPT; i++) {
+                const int t = tq + TQ * i;
+                if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * TR + row] = acc[i];
+            }
+            __syncthreads();   // staged h rows (and, after the last pass, the tile) are rewritten next
+        }
+    }
+}
+
 }  // namespace
 
 using GateUpFn = void (*)(const Slot *, const int32_t *, const uint8_t *, size_t, int, int, int, int, float *);
@@ -314,11 +467,14 @@ bool batch_supported(int dt_gu, int dt_dn, int D, int de, int E, int k) {
 size_t ep_record_bytes(int D) { return 16 + qvb(D / 256); }
 
 void batch_release(BatchScratch &s) {
+    const int kmode = s.kmode, kmode_dn = s.kmode_dn;
     for (void *p : { (void *)s.xq, (void *)s.ids, (void *)s.w, (void *)s.grp, (void *)s.hbuf, (void *)s.hq,
                      (void *)s.eo })
         if (p) cudaFree(p);
     if (s.cnt) cudaFreeHost(s.cnt);
     s = BatchScratch{};
+    s.kmode = kmode;
+    s.kmode_dn = kmode_dn;
 }
 
 // Grows the scratch to hold n_tok tokens and n_pairs (token, expert) pairs.
@@ -331,13 +487,14 @@ static int reserve(BatchScratch &s, int n_tok, int64_t n_pairs, int D, int de, i
     if (cudaMalloc(&s.xq, (size_t)cap * qvb(D / 256)) != cudaSuccess || cudaMalloc(&s.ids, 4 * np) != cudaSuccess ||
         cudaMalloc(&s.w, 4 * np) != cudaSuccess || cudaMalloc(&s.grp, 4 * (2 * (size_t)ce + 2 + np)) != cudaSuccess ||
         cudaMalloc(&s.hbuf, 4 * np * de) != cudaSuccess || cudaMalloc(&s.hq, np * qvb(de / 256)) != cudaSuccess ||
-        cudaMalloc(&s.eo, 4 * np * D) != cudaSuccess || cudaMallocHost(&s.cnt, 4 * (EP_MAX_RANKS + 1)) != cudaSuccess) {
+        cudaMalloc(&s.eo, 4 * np * D) != cudaSuccess || cudaMallocHost(&s.cnt, 4 * (EP_MAX_RANKS + 2)) != cudaSuccess) {
         cudaGetLastError();
         batch_release(s);
         return set_error(TLMG_ENOMEM, "batched expert FFN scratch for %d tokens / %lld pairs", n_tok,
                          (long long)n_pairs);
     }
     s.cnt[EP_MAX_RANKS] = 0;
+    s.cnt[EP_MAX_RANKS + 1] = 0;
     s.cap = cap;
     s.cap_pairs = np;
     s.cap_e = ce;
@@ -362,20 +519,80 @@ static unsigned warp_blocks(int64_t warps, int nsm) {
 // The expert stage shared by batched decode and the expert-parallel owner:
 // np pairs, pair q's expert id at ids[q * istride] and its quantised input at
 // x + (q / xdiv) * xstride -> eo[q] (f32 [D]).
-static void expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, int de, int E, int lo,
+using TGateUpFn = void (*)(const Slot *, const int32_t *, const uint8_t *, size_t, int, int, int, int, float *);
+using TDownFn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, float *);
+
+static TGateUpFn pick_tgateup(int dt) {
+    return dt == DT_Q4_K ? k_tgateup<DT_Q4_K> : dt == DT_Q5_K ? k_tgateup<DT_Q5_K> : nullptr;
+}
+static TDownFn pick_tdown(int dt) {
+    return dt == DT_Q4_K ? k_tdown<DT_Q4_K> : dt == DT_Q5_K ? k_tdown<DT_Q5_K> : dt == DT_Q6_K ? k_tdown<DT_Q6_K>
+                                                                                            : nullptr;
+}
+static size_t tgateup_smem(int dt, int D) {
+    return (size_t)NSG * 2 * TR * dt_block_bytes(dt) + (size_t)TC * qvb(D / 256);
+}
+static size_t tdown_smem(int dt, int de) {
+    return up16b((uint32_t)(TR * (de / 256) * dt_block_bytes(dt))) + (size_t)TC * qvb(de / 256);
+}
+constexpr size_t SMEM_MAX = 227 * 1024;
+
+// Opts a kernel into `bytes` of dynamic shared memory (once per size).
+template <typename F>
+static bool smem_opt_in(F fn, size_t bytes) {
+    static thread_local std::vector<std::pair<const void *, size_t>> done;
+    for (auto &d : done)
+        if (d.first == (const void *)fn && d.second >= bytes) return true;
+    if (cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    done.push_back({ (const void *)fn, bytes });
+    return true;
+}
+
+// The expert stage shared by batched decode and the expert-parallel owner:
+// np pairs, pair q's expert id at ids[q * istride] and its quantised input at
+// x + (q / xdiv) * xstride -> eo[q] (f32 [D]).
+static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, int de, int E, int lo,
                          int hi, const int32_t *ids, int istride, int64_t np, const uint8_t *x, size_t xstride,
                          int xdiv, float *eo, cudaStream_t st) {
     const int nsm = sm_count();
     k_bgroup<<<1, 1024, 0, st>>>(ids, istride, (int)np, E, lo, hi, s.grp, eo, D, s.cnt + EP_MAX_RANKS);
-    // one warp per (expert, tile): at most min(np, E) experts are active
+    // at most min(np, E) experts are active
     const int64_t na_max = std::min<int64_t>(np, E);
-    pick_gateup(dt_gu, D)<<<warp_blocks(na_max * ((de + 3) / 4), nsm), 256, 0, st>>>(slots, s.grp, x, xstride, xdiv,
-                                                                                    D, de, E, s.hbuf);
+    const size_t sgu = tgateup_smem(dt_gu, D), sdn = tdown_smem(dt_dn, de);
+    uint32_t *err = reinterpret_cast<uint32_t *>(s.cnt + EP_MAX_RANKS + 1);
+    TGateUpFn tgu = s.kmode >= 1 ? pick_tgateup(dt_gu) : nullptr;
+    if (s.kmode >= 2 && mma_gateup_supported(dt_gu, D, de)) {
+        int rc = launch_mma_gateup(dt_gu, slots, s.grp, x, xstride, xdiv, D, de, E, na_max * (de / 128), s.hbuf, err, st);
+        if (rc) return rc;
+    } else if (tgu && sgu <= SMEM_MAX && smem_opt_in(tgu, sgu)) {
+        const int64_t items = na_max * (de / TR);
+        tgu<<<(unsigned)std::min<int64_t>(items, 2 * (int64_t)nsm), TR * TQ, sgu, st>>>(slots, s.grp, x, xstride,
+                                                                                         xdiv, D, de, E, s.hbuf);
+    } else {
+        // one warp per (expert, tile of 4 rows)
+        pick_gateup(dt_gu, D)<<<warp_blocks(na_max * ((de + 3) / 4), nsm), 256, 0, st>>>(slots, s.grp, x, xstride,
+                                                                                        xdiv, D, de, E, s.hbuf);
+    }
     k_bquant<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, (int)np, de, s.hq);
-    const int rpt = 32 / (de / 256);
-    pick_down(dt_dn)<<<warp_blocks(na_max * ((D + rpt - 1) / rpt), nsm), 256, 0, st>>>(slots, s.grp, s.hq, D, de, E,
-                                                                                      eo);
+    TDownFn tdn = s.kmode_dn >= 1 ? pick_tdown(dt_dn) : nullptr;
+    if (s.kmode_dn >= 2 && mma_down_supported(dt_dn, D, de)) {
+        int rc = launch_mma_down(dt_dn, slots, s.grp, s.hq, D, de, E, na_max * (D / 128), eo, err, st);
+        if (rc) return rc;
+    } else if (tdn && sdn <= SMEM_MAX && smem_opt_in(tdn, sdn)) {
+        const int64_t items = na_max * (D / TR);
+        tdn<<<(unsigned)std::min<int64_t>(items, 3 * (int64_t)nsm), TR * TQ, sdn, st>>>(slots, s.grp, s.hq, D, de, E,
+                                                                                        eo);
+    } else {
+        const int rpt = 32 / (de / 256);
+        pick_down(dt_dn)<<<warp_blocks(na_max * ((D + rpt - 1) / rpt), nsm), 256, 0, st>>>(slots, s.grp, s.hq, D, de,
+                                                                                          E, eo);
+    }
     count_launch(4);
+    return TLMG_OK;
 }
 
 static unsigned combine_blocks(int n, int D) {
@@ -392,8 +609,9 @@ int launch_batch(BatchScratch &s, const BatchArgs &a, cudaStream_t st) {
     k_bquant<<<warp_blocks((int64_t)a.n * (a.D / 256), nsm), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
     k_broute<<<(a.n + RW - 1) / RW, 32 * RW, 0, st>>>(a, s.ids, s.w);
     count_launch(2);
-    expert_stage(s, a.slots, a.dt_gu, a.dt_dn, a.D, a.de, a.E, 0, a.E, s.ids, 1, np, s.xq, qvb(a.D / 256), a.k, s.eo,
-                 st);
+    if ((rc = expert_stage(s, a.slots, a.dt_gu, a.dt_dn, a.D, a.de, a.E, 0, a.E, s.ids, 1, np, s.xq, qvb(a.D / 256),
+                           a.k, s.eo, st)))
+        return rc;
     k_bcombine<<<combine_blocks(a.n, a.D), 256, 0, st>>>(s.eo, nullptr, s.w, a.n, a.D, a.k, a.ffn);
     count_launch(1);
     cudaError_t e = cudaGetLastError();
@@ -437,14 +655,21 @@ int ep_experts(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, 
     int rc = reserve(s, 1, n_rec, D, de, E);
     if (rc) return rc;
     const size_t rec = ep_record_bytes(D);
-    expert_stage(s, slots, dt_gu, dt_dn, D, de, E, lo, hi, reinterpret_cast<const int32_t *>(recv), (int)(rec / 4),
-                 n_rec, recv + 16, rec, 1, eo, st);
+    if ((rc = expert_stage(s, slots, dt_gu, dt_dn, D, de, E, lo, hi, reinterpret_cast<const int32_t *>(recv),
+                           (int)(rec / 4), n_rec, recv + 16, rec, 1, eo, st)))
+        return rc;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "expert-parallel expert launch");
 }
 
 int batch_take_error(BatchScratch &s) {
-    if (!s.cnt || s.cnt[EP_MAX_RANKS] == 0) return TLMG_OK;
+    if (!s.cnt) return TLMG_OK;
+    if (s.cnt[EP_MAX_RANKS + 1]) {
+        s.cnt[EP_MAX_RANKS + 1] = 0;
+        return set_error(TLMG_EIO, "batched expert kernel gave up waiting for its tensor-core MMAs; results of this "
+                                   "call are invalid");
+    }
+    if (s.cnt[EP_MAX_RANKS] == 0) return TLMG_OK;
     const int n = s.cnt[EP_MAX_RANKS];
     s.cnt[EP_MAX_RANKS] = 0;
     return set_error(TLMG_EINVAL, "expert parallel: %d received records named experts this GPU does not own "

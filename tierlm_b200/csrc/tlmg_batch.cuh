@@ -17,6 +17,9 @@ struct BatchScratch {
     int cap = 0;                // tokens
     int64_t cap_pairs = 0;      // (token, expert) pairs or received records
     int cap_e = 0;              // experts
+    int kmode = 2;              // gate/up kernels: 2 tensor cores, 1 tiled CUDA cores, 0 warp per row tile
+                                // (each falls back to the next lower one where it does not apply)
+    int kmode_dn = 2;           // the same for the down projection
     uint8_t *xq = nullptr;      // [cap] quantised inputs (swizzled Q8_K vectors)
     int32_t *ids = nullptr;     // [cap][k]
     float *w = nullptr;         // [cap][k]
@@ -24,8 +27,9 @@ struct BatchScratch {
     float *hbuf = nullptr;      // [cap * k][de] SwiGLU rows per (token, rank) pair
     uint8_t *hq = nullptr;      // [cap * k] quantised h per pair
     float *eo = nullptr;        // [cap * k][D] expert outputs per pair
-    int32_t *cnt = nullptr;     // pinned host [EP_MAX_RANKS + 1]: dispatch record counts, then the count of
-                                // received records naming an expert outside the owner's range
+    int32_t *cnt = nullptr;     // pinned host [EP_MAX_RANKS + 2]: dispatch record counts, the count of
+                                // received records naming an expert outside the owner's range, and
+                                // the tensor-core kernels' error bits
 };
 
 struct BatchArgs {

@@ -1,0 +1,581 @@
+// tlmg_mma.cu - grouped expert GEMM on tcgen05 (sm_100a), exact.
+//
+// Work item = (active expert, tile of 128 weight rows); one CTA of 128
+// threads, thread r <-> weight row r <-> TMEM lane r. For each pass of up to
+// 16 tokens of the expert and each K-quant block b in ascending order:
+//
+//   1. the tile's raw block column is staged with cp.async (16-byte pieces);
+//   2. thread r unpacks its row into int8 codes in the canonical K-major
+//      no-swizzle UMMA layout (core matrix = 8 rows x 16 bytes) - Q4_K / Q5_K
+//      codes 0..31, Q6_K codes minus 32 - and keeps the block's scales;
+//   3. one thread issues one tcgen05.mma kind::i8 (M = 128, N = 16, K = 32)
+//      per sub-block: A = the sub-block's codes, B = the tokens' Q8_K codes of
+//      the same elements, D = that sub-block's own int32 accumulator in TMEM
+//      (a Q4_K / Q5_K sub-block is 32 elements; a Q6_K group is 16 elements,
+//      its second K half reads a zero chunk of B). Each accumulator is the
+//      exact integer dot of one sub-block;
+//   4. thread r reads its row's accumulators (tcgen05.ld) and forms the
+//      reference's per-block sums is = sum_s scale_s * dot_s (and the min
+//      sum ms from the activation block sums), then the fmaf chain step of
+//      block b for every token (acc = fmaf(d_w d_a, is, acc), Q4_K / Q5_K also
+//      fmaf(-dmin_w d_a, ms, acc)).
+//
+// Integer addition is exact, so is / ms equal the reference's per-block
+// integer sums, and the chain runs in block order: results are bit-identical
+// to the single-token kernels (reference dot_kq_affine_ref / dot_q6_k_ref,
+// src/lib/tlm_quant.c:814-882).
+//
+// Waits on the MMA completion barrier are bounded; on expiry the kernel sets
+// bit 0 of *err, waits (bounded) once more, frees its TMEM and returns.
+#include <algorithm>
+#include <vector>
+
+#include "tlmg_dev.cuh"
+#include "tlmg_internal.h"
+#include "tlmg_kq.cuh"
+#include "tlmg_mma.cuh"
+
+namespace tlmg {
+
+namespace {
+
+constexpr int MR = 128;   // rows per tile = TMEM lanes = MMA M = threads
+constexpr int MT = 16;    // tokens per pass = MMA N
+constexpr int MAXNB = 16; // K blocks per row (K <= 4096)
+
+template <int DT> struct KQ;
+template <> struct KQ<DT_Q4_K> { static constexpr int BB = 144, SUB = 8; };
+template <> struct KQ<DT_Q5_K> { static constexpr int BB = 176, SUB = 8; };
+template <> struct KQ<DT_Q6_K> { static constexpr int BB = 210, SUB = 16; };
+
+__host__ __device__ constexpr uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+__host__ __device__ inline uint32_t qvec_bytes(int nb) { return 288u * nb + align_up(4u * nb, 16u); }
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+__device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// generic-proxy shared writes -> visible to the tensor cores' async proxy
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// UMMA shared-memory descriptor, K-major, no swizzle: start, leading byte
+// offset (between the two 16-byte K halves), stride byte offset (between
+// 8-row core-matrix groups), version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t start, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((start >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor: D s32 (c_format 2), A and B signed 8-bit, both
+// K-major, N = 16, M = 128.
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MT >> 3) << 17) |
+                           ((uint32_t)(MR >> 4) << 24);
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b) {
+    // D = A * B (enable-input-d false: every accumulator starts from zero)
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(IDESC), "r"(z), "r"(z)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(mbar))
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_init(uint64_t *mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(mbar)), "r"(count) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");   // visible to the tensor cores' arrive
+}
+// Waits for phase `parity` of the barrier to complete; false after `limit` polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t *mbar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(saddr(mbar)), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(dst)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// 16 consecutive 32-bit columns of this thread's TMEM lane. The load and its
+// wait are one asm statement: the registers are only valid after
+// tcgen05.wait::ld, and the compiler must not schedule their uses earlier.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+
+constexpr uint32_t WAIT_LIMIT = 1u << 20;   // polls of a completion barrier before giving up
+
+// ---------------------------------------------------------------------------
+// Row unpack: one weight block of this thread's row -> 16 chunks of 16 int8
+// codes (chunk c = elements 16c .. 16c + 15) at A + c * 128 + (row % 8) * 16
+// within the row's 8-row group; the block's scale factors are returned.
+struct RowBlk {
+    uint32_t s[4];   // Q4_K/Q5_K: sc03, sc47, mn03, mn47 (6-bit bytes); Q6_K: int8 scales 0..15
+    float d, dmin;
+};
+
+__device__ __forceinline__ void st16(uint8_t *p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    *reinterpret_cast<uint4 *>(p) = make_uint4(a, b, c, d);
+}
+
+template <int DT>
+__device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A) {
+    RowBlk rb;
+    if constexpr (DT == DT_Q4_K || DT == DT_Q5_K) {
+        constexpr int QOFF = DT == DT_Q4_K ? 16 : 48;
+        const uint4 h = lds128(blk);
+        rb.d = h2f(h.x & 0xFFFFu);
+        rb.dmin = h2f(h.x >> 16);
+        rb.s[0] = h.y & 0x3F3F3F3Fu;
+        rb.s[1] = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+        rb.s[2] = h.z & 0x3F3F3F3Fu;
+        rb.s[3] = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+        uint4 g[2] = { make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u) };
+        if constexpr (DT == DT_Q5_K) {
+            g[0] = lds128(blk + 16);
+            g[1] = lds128(blk + 32);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {   // qs piece j: chunk c = j / 2, bytes 16 (j % 2) ..
+            const int c = j >> 1, hh = j & 1;
+            const uint4 v = lds128(blk + QOFF + 16 * j);
+            uint4 lo = make_uint4(v.x & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, v.z & 0x0F0F0F0Fu, v.w & 0x0F0F0F0Fu);
+            uint4 hi = make_uint4((v.x >> 4) & 0x0F0F0F0Fu, (v.y >> 4) & 0x0F0F0F0Fu, (v.z >> 4) & 0x0F0F0F0Fu,
+                                  (v.w >> 4) & 0x0F0F0F0Fu);
+            if constexpr (DT == DT_Q5_K) {   // 5th bit: qh[l] bit 2c (low) / 2c + 1 (high), l = 16 hh + i
+                const uint4 q = g[hh];
+                lo.x |= ((q.x >> (2 * c)) & 0x01010101u) << 4;
+                lo.y |= ((q.y >> (2 * c)) & 0x01010101u) << 4;
+                lo.z |= ((q.z >> (2 * c)) & 0x01010101u) << 4;
+                lo.w |= ((q.w >> (2 * c)) & 0x01010101u) << 4;
+                hi.x |= ((q.x >> (2 * c + 1)) & 0x01010101u) << 4;
+                hi.y |= ((q.y >> (2 * c + 1)) & 0x01010101u) << 4;
+                hi.z |= ((q.z >> (2 * c + 1)) & 0x01010101u) << 4;
+                hi.w |= ((q.w >> (2 * c + 1)) & 0x01010101u) << 4;
+            }
+            st16(A + (4 * c + hh) * 128, lo.x, lo.y, lo.z, lo.w);       // elements 64c + 16hh ..
+            st16(A + (4 * c + 2 + hh) * 128, hi.x, hi.y, hi.z, hi.w);   // elements 64c + 32 + 16hh ..
+        }
+    } else {
+        // Q6_K at a 2-byte aligned address: 4-byte aligned words + funnel shifts
+        const uintptr_t a = reinterpret_cast<uintptr_t>(blk);
+        const uint32_t *wp = reinterpret_cast<const uint32_t *>(a & ~(uintptr_t)3);
+        const uint32_t sh = (uint32_t)(a & 3u) * 8u;
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+                uint32_t u[4][4];   // [mm][i]: chunk 8h + 2mm + p, word i
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int lw = 4 * p + i;
+                    const int ja = 16 * h + lw, jb = 16 * h + 8 + lw, jc = 32 + 8 * h + lw;
+                    const uint32_t Aw = __funnelshift_r(wp[ja], wp[ja + 1], sh);
+                    const uint32_t Bw = __funnelshift_r(wp[jb], wp[jb + 1], sh);
+                    const uint32_t Cw = __funnelshift_r(wp[jc], wp[jc + 1], sh);
+                    u[0][i] = __vsub4((Aw & 0x0F0F0F0Fu) | ((Cw << 4) & 0x30303030u), 0x20202020u);
+                    u[1][i] = __vsub4((Bw & 0x0F0F0F0Fu) | ((Cw << 2) & 0x30303030u), 0x20202020u);
+                    u[2][i] = __vsub4(((Aw >> 4) & 0x0F0F0F0Fu) | (Cw & 0x30303030u), 0x20202020u);
+                    u[3][i] = __vsub4(((Bw >> 4) & 0x0F0F0F0Fu) | ((Cw >> 2) & 0x30303030u), 0x20202020u);
+                }
+#pragma unroll
+                for (int mm = 0; mm < 4; mm++) st16(A + (8 * h + 2 * mm + p) * 128, u[mm][0], u[mm][1], u[mm][2], u[mm][3]);
+            }
+        rb.s[0] = __funnelshift_r(wp[48], wp[49], sh);
+        rb.s[1] = __funnelshift_r(wp[49], wp[50], sh);
+        rb.s[2] = __funnelshift_r(wp[50], wp[51], sh);
+        rb.s[3] = __funnelshift_r(wp[51], wp[52], sh);
+        rb.d = h2f(__funnelshift_r(wp[52], wp[53], sh) & 0xFFFFu);
+        rb.dmin = 0.0f;
+    }
+    return rb;
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory plan of one CTA (same on host and device).
+struct MPlan {
+    uint32_t raw, raw_bytes;   // raw weight stages
+    uint32_t A;                // unpacked int8 tiles [nmat][16 groups][16 chunks][8 rows][16 B]
+    uint32_t X, xsbo;          // token codes [2 groups][KC + 1 chunks][8 tokens][16 B] (chunk KC zero)
+    uint32_t dx, bs;           // f32 [MT][MAXNB] block scales, int32 [MT][MAXNB][8] sub-block bsums
+    uint32_t bar, total;
+};
+__host__ __device__ inline MPlan mplan(int nmat, uint32_t raw_bytes, int nb) {
+    MPlan p{};
+    p.raw = 0;
+    p.raw_bytes = raw_bytes;
+    p.A = align_up(raw_bytes, 1024u);
+    p.X = p.A + (uint32_t)nmat * MR * 256u;
+    p.xsbo = (uint32_t)(16 * nb + 1) * 128u;
+    p.dx = p.X + 2u * p.xsbo;
+    p.bs = p.dx + (uint32_t)MT * MAXNB * 4u;
+    p.bar = p.bs + (uint32_t)MT * MAXNB * 8u * 4u;
+    p.total = p.bar + 16u;
+    return p;
+}
+
+// Stages the pass's tokens: codes into the canonical B layout (cp.async),
+// block scales and sub-block sums into dx / bs. Zeroes the chunk KC of each
+// token group once per CTA (first == true).
+template <int DT>
+__device__ __forceinline__ void stage_tokens(uint8_t *sm, const MPlan &P, const uint8_t *x, size_t xstride, int xdiv,
+                                             const int32_t *pairs, int nt, int nb, bool first) {
+    const int KC = 16 * nb;
+    uint8_t *X = sm + P.X;
+    if (first)
+        for (int i = threadIdx.x; i < 2 * 8; i += blockDim.x)
+            *reinterpret_cast<uint4 *>(X + (i >> 3) * P.xsbo + KC * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = threadIdx.x; i < nt * KC; i += blockDim.x) {
+        const int t = i / KC, kc = i - t * KC;
+        const uint8_t *v = x + (size_t)(pairs[t] / xdiv) * xstride;
+        // swizzled Q8_K vector: piece p of block b at (p * nb + b) * 16
+        cp16(X + (t >> 3) * P.xsbo + kc * 128 + (t & 7) * 16, v + ((size_t)(kc & 15) * nb + (kc >> 4)) * 16);
+    }
+    float *dx = reinterpret_cast<float *>(sm + P.dx);
+    int *bs = reinterpret_cast<int *>(sm + P.bs);
+    for (int i = threadIdx.x; i < nt * nb; i += blockDim.x) {
+        const int t = i / nb, b = i - t * nb;
+        const uint8_t *v = x + (size_t)(pairs[t] / xdiv) * xstride;
+        dx[t * MAXNB + b] = reinterpret_cast<const float *>(v + 288 * nb)[b];
+        if constexpr (DT != DT_Q6_K) {
+            const int16_t *s16 = reinterpret_cast<const int16_t *>(v + 256 * nb) + 16 * b;
+#pragma unroll
+            for (int s = 0; s < 8; s++) bs[(t * MAXNB + b) * 8 + s] = (int)s16[2 * s] + (int)s16[2 * s + 1];
+        }
+    }
+}
+
+// One block of the tile: (after the caller's barrier) thread 0 issues the
+// sub-block MMAs of nmat matrices, everyone waits for them, and each thread
+// folds its row's accumulators into the per-token chains acc[m][t].
+template <int DT, int NMAT>
+__device__ __forceinline__ bool mma_block(uint8_t *sm, const MPlan &P, uint32_t tmem, uint32_t &phase, int b,
+                                          const RowBlk (&rb)[NMAT], float (&acc)[NMAT][MT], int nt) {
+    constexpr int SUB = KQ<DT>::SUB;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + P.bar);
+    const uint32_t Xs = saddr(sm + P.X), As = saddr(sm + P.A);
+    const int KC = (int)(P.xsbo / 128u) - 1;
+    if (threadIdx.x == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int m = 0; m < NMAT; m++)
+#pragma unroll
+            for (int s = 0; s < SUB; s++) {
+                uint64_t ad, bd;
+                if constexpr (DT == DT_Q6_K) {
+                    // group s = chunk s; B's second K half is the zero chunk KC
+                    const int kc = 16 * b + s;
+                    ad = umma_desc(As + m * MR * 256u + s * 128u, 128u, 2048u);
+                    bd = umma_desc(Xs + kc * 128u, (uint32_t)(KC - kc) * 128u, P.xsbo);
+                } else {
+                    const int kc = 16 * b + 2 * s;
+                    ad = umma_desc(As + m * MR * 256u + 2 * s * 128u, 128u, 2048u);
+                    bd = umma_desc(Xs + kc * 128u, 128u, P.xsbo);
+                }
+                umma_i8(tmem + (uint32_t)((m * SUB + s) * MT), ad, bd);
+            }
+        umma_commit(bar);
+    }
+    const bool ok = mbar_wait(bar, phase, WAIT_LIMIT);
+    phase ^= 1u;
+    tc_fence_after();
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (threadIdx.x >> 5)) << 16);
+    const float *dx = reinterpret_cast<const float *>(sm + P.dx);
+    const int *bs = reinterpret_cast<const int *>(sm + P.bs);
+#pragma unroll
+    for (int m = 0; m < NMAT; m++) {
+        int is[MT];
+#pragma unroll
+        for (int t = 0; t < MT; t++) is[t] = 0;
+#pragma unroll
+        for (int s = 0; s < SUB; s++) {
+            int v[16];
+            tmem_ld16(lane_base + (uint32_t)((m * SUB + s) * MT), v);
+            int sc;
+            if constexpr (DT == DT_Q6_K) sc = (int)(int8_t)byte_of(rb[m].s[s >> 2], s & 3);
+            else sc = (int)byte_of(rb[m].s[s >> 2], s & 3);
+#pragma unroll
+            for (int t = 0; t < MT; t++) is[t] += sc * v[t];
+        }
+#pragma unroll
+        for (int t = 0; t < MT; t++) {
+            if (t < nt) {
+                const float d = dx[t * MAXNB + b];
+                int ms = 0;
+                if constexpr (DT != DT_Q6_K) {
+                    const int *bt = bs + (t * MAXNB + b) * 8;
+#pragma unroll
+                    for (int s = 0; s < 8; s++) ms += (int)byte_of(rb[m].s[2 + (s >> 2)], s & 3) * bt[s];
+                }
+                acc[m][t] = chain<DT>(acc[m][t], __fmul_rn(rb[m].d, d), is[t], __fmul_rn(rb[m].dmin, d), ms);
+            }
+        }
+    }
+    tc_fence_before();
+    return ok;
+}
+
+__device__ __forceinline__ void report(uint32_t *err, bool ok) {
+    if (!ok && threadIdx.x == 0) atomicOr(err, 1u);
+}
+
+// gate/up: K = D, raw stages hold one block column [NS][2][MR][BB] of the
+// tile's gate and up rows; hbuf[pair][row] = SiLU(gate) * up.
+template <int DT, int NS>
+__global__ void __launch_bounds__(MR, 1)
+    k_mgateup(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
+              size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ hbuf, uint32_t *err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    constexpr int BB = KQ<DT>::BB, CPB = BB / 16;
+    static_assert(BB % 16 == 0, "gate/up blocks must be 16-byte multiples");
+    const int nb = D / 256;
+    const MPlan P = mplan(2, (uint32_t)NS * 2 * MR * BB, nb);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
+    const int r = threadIdx.x;
+    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    if (r < 32) tmem_alloc(tmem_slot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    uint32_t phase = 0;
+    bool ok = true;
+    const int tiles = de / MR, na = grp[2 * E + 1];
+    const size_t rb = (size_t)nb * BB;
+    const int32_t *pairs = grp + 2 * E + 2;
+    bool first = true;
+    uint8_t *Arow0 = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16, *Arow1 = Arow0 + MR * 256;
+    for (int item = blockIdx.x; item < na * tiles && ok; item += gridDim.x) {
+        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+        const uint8_t *wg = slots[e].m[0] + (size_t)tile * MR * rb, *wu = slots[e].m[1] + (size_t)tile * MR * rb;
+        auto issue = [&](int b) {
+            if (b < nb) {
+                uint8_t *st = sm + P.raw + (b % NS) * 2 * MR * BB;
+                for (int i = r; i < 2 * MR * CPB; i += MR) {
+                    const int m = i / (MR * CPB), rr = (i / CPB) % MR, c = i % CPB;
+                    cp16(st + (m * MR + rr) * BB + 16 * c, (m ? wu : wg) + rr * rb + (size_t)b * BB + 16 * c);
+                }
+            }
+            cp_commit();
+        };
+        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += MT) {
+            const int nt = min(MT, grp[e + 1] - c0);
+            stage_tokens<DT>(sm, P, x, xstride, xdiv, pairs + c0, nt, nb, first);
+            first = false;
+#pragma unroll
+            for (int b = 0; b < NS - 1; b++) issue(b);
+            float acc[2][MT];
+#pragma unroll
+            for (int t = 0; t < MT; t++) acc[0][t] = acc[1][t] = 0.0f;
+            for (int b = 0; b < nb; b++) {
+                cp_wait<NS - 2>();
+                __syncthreads();   // block b staged; the previous block's unpacked tiles are consumed
+                issue(b + NS - 1);
+                const uint8_t *st = sm + P.raw + (b % NS) * 2 * MR * BB;
+                RowBlk rbk[2];
+                rbk[0] = unpack_row<DT>(st + r * BB, Arow0);
+                rbk[1] = unpack_row<DT>(st + (MR + r) * BB, Arow1);
+                fence_async_smem();
+                __syncthreads();
+                const bool got = mma_block<DT, 2>(sm, P, tmem, phase, b, rbk, acc, nt);
+                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
+                if (!ok) break;
+            }
+            cp_wait<0>();
+            __syncthreads();
+#pragma unroll
+            for (int t = 0; t < MT; t++)
+                if (t < nt) hbuf[(size_t)pairs[c0 + t] * de + tile * MR + r] = __fmul_rn(silu_f(acc[0][t]), acc[1][t]);
+        }
+    }
+    if (!ok) {   // an MMA may still be in flight: one more bounded wait before the TMEM goes
+        mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase ^ 1u, WAIT_LIMIT);   // the phase that expired
+        report(err, false);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (r < 32) tmem_free(tmem, 256);
+}
+
+// down: K = de; the tile's MR rows x all blocks (contiguous in HBM) are
+// staged whole, double-buffered across items; eo[pair][row].
+template <int DT>
+__global__ void __launch_bounds__(MR, 1)
+    k_mdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ hq, int D,
+            int de, int E, float *__restrict__ eo, uint32_t *err) {
+    extern __shared__ __align__(1024) uint8_t sm[];
+    constexpr int BB = KQ<DT>::BB, SUB = KQ<DT>::SUB;
+    constexpr uint32_t NCOL = SUB * MT <= 128 ? 128 : 256;
+    const int nb = de / 256;
+    const uint32_t tile_bytes = (uint32_t)MR * nb * BB;   // a multiple of 16
+    const uint32_t tstride = align_up(tile_bytes, 128u);
+    const MPlan P = mplan(1, 2 * tstride, nb);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
+    const int r = threadIdx.x;
+    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    if (r < 32) tmem_alloc(tmem_slot, NCOL);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    uint32_t phase = 0;
+    bool ok = true;
+    const int tiles = D / MR, na = grp[2 * E + 1], n_items = na * tiles;
+    const size_t rbd = (size_t)nb * BB;
+    const int32_t *pairs = grp + 2 * E + 2;
+    const uint32_t qh = qvec_bytes(nb);
+    uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
+    auto issue_tile = [&](int item, int buf) {
+        if (item < n_items) {
+            const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+            const uint8_t *src = slots[e].m[2] + (size_t)tile * MR * rbd;
+            uint8_t *dst = sm + P.raw + buf * tstride;
+            for (uint32_t i = r; i < tile_bytes / 16; i += MR) cp16(dst + 16 * i, src + 16 * i);
+        }
+        cp_commit();
+    };
+    bool first = true;
+    int buf = 0;
+    issue_tile(blockIdx.x, 0);
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, buf ^= 1) {
+        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
+        const uint8_t *wt = sm + P.raw + buf * tstride + (size_t)r * rbd;
+        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += MT) {
+            const int nt = min(MT, grp[e + 1] - c0);
+            stage_tokens<DT>(sm, P, hq, qh, 1, pairs + c0, nt, nb, first);
+            cp_commit();
+            cp_wait<0>();          // this item's tile and the pass's tokens
+            first = false;
+            __syncthreads();
+            // first pass of an item: prefetch the next item's tile into the
+            // other buffer (its previous item ended at a barrier)
+            if (c0 == grp[e]) issue_tile(item + gridDim.x, buf ^ 1);
+            float acc[1][MT];
+#pragma unroll
+            for (int t = 0; t < MT; t++) acc[0][t] = 0.0f;
+            for (int b = 0; b < nb; b++) {
+                RowBlk rbk[1];   // A is free: every thread waited for the previous block's MMAs
+                rbk[0] = unpack_row<DT>(wt + b * BB, Arow);
+                fence_async_smem();
+                __syncthreads();
+                const bool got = mma_block<DT, 1>(sm, P, tmem, phase, b, rbk, acc, nt);
+                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
+                if (!ok) break;
+            }
+#pragma unroll
+            for (int t = 0; t < MT; t++)
+                if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * MR + r] = acc[0][t];
+            __syncthreads();   // staged tokens and, after the last pass, this buffer are rewritten next
+        }
+    }
+    cp_wait<0>();
+    if (!ok) {
+        mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase ^ 1u, WAIT_LIMIT);   // the phase that expired
+        report(err, false);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (r < 32) tmem_free(tmem, NCOL);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+static int gateup_stages(int D) { return D <= 2048 ? 3 : 2; }
+
+static uint32_t gateup_smem(int dt, int D) {
+    const int BB = dt_block_bytes(dt);
+    return mplan(2, (uint32_t)gateup_stages(D) * 2 * MR * BB, D / 256).total;
+}
+static uint32_t down_smem(int dt, int de) {
+    const uint32_t tile = (uint32_t)MR * (de / 256) * dt_block_bytes(dt);
+    return mplan(1, 2 * align_up(tile, 128u), de / 256).total;
+}
+constexpr uint32_t SMEM_LIMIT = 227 * 1024;
+
+bool mma_gateup_supported(int dt, int D, int de) {
+    return (dt == DT_Q4_K || dt == DT_Q5_K) && D % 256 == 0 && D / 256 <= MAXNB && de % MR == 0 &&
+           gateup_smem(dt, D) <= SMEM_LIMIT;
+}
+bool mma_down_supported(int dt, int D, int de) {
+    return (dt == DT_Q4_K || dt == DT_Q5_K || dt == DT_Q6_K) && de % 256 == 0 && de / 256 <= MAXNB && D % MR == 0 &&
+           down_smem(dt, de) <= SMEM_LIMIT;
+}
+
+template <typename F>
+static int opt_in(F fn, uint32_t bytes) {
+    static thread_local std::vector<std::pair<const void *, uint32_t>> done;
+    for (auto &d : done)
+        if (d.first == (const void *)fn && d.second >= bytes) return TLMG_OK;
+    cudaError_t e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor-core kernel shared memory");
+    done.push_back({ (const void *)fn, bytes });
+    return TLMG_OK;
+}
+
+static int grid_for(int64_t max_items) {
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    return (int)std::max<int64_t>(1, std::min<int64_t>(max_items, nsm));
+}
+
+int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8_t *x, size_t xstride, int xdiv,
+                      int D, int de, int E, int64_t max_items, float *hbuf, uint32_t *err, cudaStream_t st) {
+    if (!mma_gateup_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core gate/up: dtype %d D %d", dt, D);
+    const uint32_t smem = gateup_smem(dt, D);
+    const int grid = grid_for(max_items);
+    const bool three = gateup_stages(D) == 3;
+    auto fn = dt == DT_Q4_K ? (three ? k_mgateup<DT_Q4_K, 3> : k_mgateup<DT_Q4_K, 2>)
+                            : (three ? k_mgateup<DT_Q5_K, 3> : k_mgateup<DT_Q5_K, 2>);
+    int rc = opt_in(fn, smem);
+    if (rc) return rc;
+    fn<<<grid, MR, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, hbuf, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core gate/up launch");
+}
+
+int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t *hq, int D, int de, int E,
+                    int64_t max_items, float *eo, uint32_t *err, cudaStream_t st) {
+    if (!mma_down_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core down: dtype %d de %d", dt, de);
+    const uint32_t smem = down_smem(dt, de);
+    const int grid = grid_for(max_items);
+    auto fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K> : dt == DT_Q5_K ? k_mdown<DT_Q5_K> : k_mdown<DT_Q6_K>;
+    int rc = opt_in(fn, smem);
+    if (rc) return rc;
+    fn<<<grid, MR, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core down launch");
+}
+
+}  // namespace tlmg

@@ -647,6 +647,16 @@ int tlmg_set_fused(tlmg_ctx *c, int on) {
     return c->fused.enabled ? TLMG_OK : (on ? set_error(TLMG_EUNSUP, "persistent kernel unavailable on this device") : TLMG_OK);
 }
 
+int tlmg_set_batch_kernels(tlmg_ctx *c, int mode) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    // 0..2: both projections; 10 * g + d: gate/up mode g, down mode d
+    const int g = mode >= 10 ? mode / 10 : mode, d = mode >= 10 ? mode % 10 : mode;
+    if (mode < 0 || g > 2 || d > 2) return set_error(TLMG_EINVAL, "batch kernel mode %d", mode);
+    c->batch.kmode = g;
+    c->batch.kmode_dn = d;
+    return TLMG_OK;
+}
+
 int tlmg_trace(tlmg_ctx *c, int on, uint64_t *out, int cap) {
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     cudaSetDevice(c->device);

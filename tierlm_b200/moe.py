@@ -61,6 +61,18 @@ class MoeContext:
         """Persistent single-launch kernel (True, default) or the multi-kernel path."""
         check(self._lib.tlmg_set_fused(self._h, 1 if on else 0))
 
+    BATCH_KERNELS = {"warp": 0, "tiled": 1, "mma": 2}
+
+    def set_batch_kernels(self, mode: str, down: str | None = None) -> None:
+        """Batched expert kernels: "mma" (tcgen05 tensor cores, default),
+        "tiled" (CUDA cores, CTA per row tile) or "warp"; `down` picks the
+        down projection's separately. Identical bits."""
+        g = self.BATCH_KERNELS[mode]
+        d = g if down is None else self.BATCH_KERNELS[down]
+        if g == 0 and d != 0:
+            raise ValueError("gate/up 'warp' combines only with down 'warp'")
+        check(self._lib.tlmg_set_batch_kernels(self._h, g if g == d else 10 * g + d))
+
     def check(self) -> None:
         """Wait for queued work; raise if a kernel reported an expired wait."""
         check(self._lib.tlmg_check(self._h))
