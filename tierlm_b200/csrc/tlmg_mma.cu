@@ -117,16 +117,14 @@ __device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
 __device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-// 16 consecutive 32-bit columns of this thread's TMEM lane. The load and its
-// wait are one asm statement: the registers are only valid after
+// 64 consecutive 32-bit columns of this thread's TMEM lane. The load and
+// its wait are one asm statement: the registers are only valid after
 // tcgen05.wait::ld, and the compiler must not schedule their uses earlier.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, int (&v)[64]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
         "tcgen05.wait::ld.sync.aligned;\n"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
         : "r"(taddr)
         : "memory");
 }
@@ -137,6 +135,7 @@ constexpr uint32_t WAIT_LIMIT = 1u << 20;   // polls of a completion barrier bef
 // Row unpack: one weight block of this thread's row -> 16 chunks of 16 int8
 // codes (chunk c = elements 16c .. 16c + 15) at A + c * 128 + (row % 8) * 16
 // within the row's 8-row group; the block's scale factors are returned.
+// half = 0 / 1 unpacks only the first / second half of the sub-blocks.
 struct RowBlk {
     uint32_t s[4];   // Q4_K/Q5_K: sc03, sc47, mn03, mn47 (6-bit bytes); Q6_K: int8 scales 0..15
     float d, dmin;
@@ -147,7 +146,7 @@ __device__ __forceinline__ void st16(uint8_t *p, uint32_t a, uint32_t b, uint32_
 }
 
 template <int DT>
-__device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A) {
+__device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A, int half = -1) {
     RowBlk rb;
     if constexpr (DT == DT_Q4_K || DT == DT_Q5_K) {
         constexpr int QOFF = DT == DT_Q4_K ? 16 : 48;
@@ -165,6 +164,7 @@ __device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A) {
         }
 #pragma unroll
         for (int j = 0; j < 8; j++) {   // qs piece j: chunk c = j / 2, bytes 16 (j % 2) ..
+            if (half >= 0 && (j >> 2) != half) continue;   // half h: sub-blocks 4h .. 4h + 3
             const int c = j >> 1, hh = j & 1;
             const uint4 v = lds128(blk + QOFF + 16 * j);
             uint4 lo = make_uint4(v.x & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, v.z & 0x0F0F0F0Fu, v.w & 0x0F0F0F0Fu);
@@ -193,6 +193,7 @@ __device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A) {
         for (int h = 0; h < 2; h++)
 #pragma unroll
             for (int p = 0; p < 2; p++) {
+                if (half >= 0 && h != half) continue;   // half h: groups 8h .. 8h + 7
                 uint32_t u[4][4];   // [mm][i]: chunk 8h + 2mm + p, word i
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -221,12 +222,14 @@ __device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A) {
 
 // ---------------------------------------------------------------------------
 // Shared-memory plan of one CTA (same on host and device).
+constexpr int NTH = 2 * MR;   // threads: two per weight row (8 warps)
 struct MPlan {
     uint32_t raw, raw_bytes;   // raw weight stages
     uint32_t A;                // unpacked int8 tiles [nmat][16 groups][16 chunks][8 rows][16 B]
     uint32_t X, xsbo;          // token codes [2 groups][KC + 1 chunks][8 tokens][16 B] (chunk KC zero)
     uint32_t dx, bs;           // f32 [MT][MAXNB] block scales, int32 [MT][MAXNB][8] sub-block bsums
-    uint32_t bar, total;
+    uint32_t xch;              // 32-bit [MR][MT]: the second thread of a row hands its results over
+    uint32_t bar, total;       // mbarrier (8 B) + TMEM address (4 B)
 };
 __host__ __device__ inline MPlan mplan(int nmat, uint32_t raw_bytes, int nb) {
     MPlan p{};
@@ -237,7 +240,8 @@ __host__ __device__ inline MPlan mplan(int nmat, uint32_t raw_bytes, int nb) {
     p.xsbo = (uint32_t)(16 * nb + 1) * 128u;
     p.dx = p.X + 2u * p.xsbo;
     p.bs = p.dx + (uint32_t)MT * MAXNB * 4u;
-    p.bar = p.bs + (uint32_t)MT * MAXNB * 8u * 4u;
+    p.xch = p.bs + (uint32_t)MT * MAXNB * 8u * 4u;
+    p.bar = p.xch + (uint32_t)MR * MT * 4u;
     p.total = p.bar + 16u;
     return p;
 }
@@ -273,74 +277,78 @@ __device__ __forceinline__ void stage_tokens(uint8_t *sm, const MPlan &P, const 
     }
 }
 
-// One block of the tile: (after the caller's barrier) thread 0 issues the
-// sub-block MMAs of nmat matrices, everyone waits for them, and each thread
-// folds its row's accumulators into the per-token chains acc[m][t].
+// Thread 0 issues the MMAs of block b for nmat matrices (every sub-block
+// into its own accumulator) and commits them to the barrier.
 template <int DT, int NMAT>
-__device__ __forceinline__ bool mma_block(uint8_t *sm, const MPlan &P, uint32_t tmem, uint32_t &phase, int b,
-                                          const RowBlk (&rb)[NMAT], float (&acc)[NMAT][MT], int nt) {
+__device__ __forceinline__ void issue_block(uint8_t *sm, const MPlan &P, uint32_t tmem, int b) {
     constexpr int SUB = KQ<DT>::SUB;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(sm + P.bar);
     const uint32_t Xs = saddr(sm + P.X), As = saddr(sm + P.A);
     const int KC = (int)(P.xsbo / 128u) - 1;
-    if (threadIdx.x == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int m = 0; m < NMAT; m++)
-#pragma unroll
-            for (int s = 0; s < SUB; s++) {
-                uint64_t ad, bd;
-                if constexpr (DT == DT_Q6_K) {
-                    // group s = chunk s; B's second K half is the zero chunk KC
-                    const int kc = 16 * b + s;
-                    ad = umma_desc(As + m * MR * 256u + s * 128u, 128u, 2048u);
-                    bd = umma_desc(Xs + kc * 128u, (uint32_t)(KC - kc) * 128u, P.xsbo);
-                } else {
-                    const int kc = 16 * b + 2 * s;
-                    ad = umma_desc(As + m * MR * 256u + 2 * s * 128u, 128u, 2048u);
-                    bd = umma_desc(Xs + kc * 128u, 128u, P.xsbo);
-                }
-                umma_i8(tmem + (uint32_t)((m * SUB + s) * MT), ad, bd);
-            }
-        umma_commit(bar);
-    }
-    const bool ok = mbar_wait(bar, phase, WAIT_LIMIT);
-    phase ^= 1u;
     tc_fence_after();
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * (threadIdx.x >> 5)) << 16);
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int s = 0; s < SUB; s++) {
+            uint64_t ad, bd;
+            if constexpr (DT == DT_Q6_K) {
+                // group s = chunk s; B's second K half is the zero chunk KC
+                const int kc = 16 * b + s;
+                ad = umma_desc(As + m * MR * 256u + s * 128u, 128u, 2048u);
+                bd = umma_desc(Xs + kc * 128u, (uint32_t)(KC - kc) * 128u, P.xsbo);
+            } else {
+                const int kc = 16 * b + 2 * s;
+                ad = umma_desc(As + m * MR * 256u + 2 * s * 128u, 128u, 2048u);
+                bd = umma_desc(Xs + kc * 128u, 128u, P.xsbo);
+            }
+            umma_i8(tmem + (uint32_t)((m * SUB + s) * MT), ad, bd);
+        }
+    umma_commit(reinterpret_cast<uint64_t *>(sm + P.bar));
+}
+
+// is[t] += scale_s * dot_s[t] over sub-blocks s0 .. s0 + 4 * n4 - 1 of one
+// matrix whose sub-block s accumulator starts at column col0 + s * MT.
+template <int DT>
+__device__ __forceinline__ void add_scaled(uint32_t lane_base, uint32_t col0, int s0, int n4, const RowBlk &rb,
+                                           int (&is)[MT]) {
+#pragma unroll 1
+    for (int g = 0; g < n4; g++) {
+        int v[64];
+        tmem_ld64(lane_base + col0 + (uint32_t)((s0 + 4 * g) * MT), v);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int s = s0 + 4 * g + j;
+            int sc;
+            if constexpr (DT == DT_Q6_K) sc = (int)(int8_t)byte_of(rb.s[s >> 2], s & 3);
+            else sc = (int)byte_of(rb.s[s >> 2], s & 3);
+#pragma unroll
+            for (int t = 0; t < MT; t++) is[t] += sc * v[16 * j + t];
+        }
+    }
+}
+
+// The block's chain step for every token of the pass: acc[t] =
+// fmaf(d_w d_a, is, acc) (and, Q4_K / Q5_K, fmaf(-dmin_w d_a, ms, acc)).
+template <int DT>
+__device__ __forceinline__ void chain_tokens(const uint8_t *sm, const MPlan &P, int b, const RowBlk &rb,
+                                             const int (&is)[MT], float (&acc)[MT], int nt) {
     const float *dx = reinterpret_cast<const float *>(sm + P.dx);
     const int *bs = reinterpret_cast<const int *>(sm + P.bs);
 #pragma unroll
-    for (int m = 0; m < NMAT; m++) {
-        int is[MT];
-#pragma unroll
-        for (int t = 0; t < MT; t++) is[t] = 0;
-#pragma unroll
-        for (int s = 0; s < SUB; s++) {
-            int v[16];
-            tmem_ld16(lane_base + (uint32_t)((m * SUB + s) * MT), v);
-            int sc;
-            if constexpr (DT == DT_Q6_K) sc = (int)(int8_t)byte_of(rb[m].s[s >> 2], s & 3);
-            else sc = (int)byte_of(rb[m].s[s >> 2], s & 3);
-#pragma unroll
-            for (int t = 0; t < MT; t++) is[t] += sc * v[t];
-        }
-#pragma unroll
-        for (int t = 0; t < MT; t++) {
-            if (t < nt) {
-                const float d = dx[t * MAXNB + b];
-                int ms = 0;
-                if constexpr (DT != DT_Q6_K) {
-                    const int *bt = bs + (t * MAXNB + b) * 8;
-#pragma unroll
-                    for (int s = 0; s < 8; s++) ms += (int)byte_of(rb[m].s[2 + (s >> 2)], s & 3) * bt[s];
-                }
-                acc[m][t] = chain<DT>(acc[m][t], __fmul_rn(rb[m].d, d), is[t], __fmul_rn(rb[m].dmin, d), ms);
+    for (int t = 0; t < MT; t++) {
+        if (t < nt) {
+            const float d = dx[t * MAXNB + b];
+            int ms = 0;
+            if constexpr (DT != DT_Q6_K) {
+                const int4 b0 = *reinterpret_cast<const int4 *>(bs + (t * MAXNB + b) * 8);
+                const int4 b1 = *reinterpret_cast<const int4 *>(bs + (t * MAXNB + b) * 8 + 4);
+                ms = (int)byte_of(rb.s[2], 0) * b0.x + (int)byte_of(rb.s[2], 1) * b0.y +
+                     (int)byte_of(rb.s[2], 2) * b0.z + (int)byte_of(rb.s[2], 3) * b0.w +
+                     (int)byte_of(rb.s[3], 0) * b1.x + (int)byte_of(rb.s[3], 1) * b1.y +
+                     (int)byte_of(rb.s[3], 2) * b1.z + (int)byte_of(rb.s[3], 3) * b1.w;
             }
+            acc[t] = chain<DT>(acc[t], __fmul_rn(rb.d, d), is[t], __fmul_rn(rb.dmin, d), ms);
         }
     }
-    tc_fence_before();
-    return ok;
 }
 
 __device__ __forceinline__ void report(uint32_t *err, bool ok) {
@@ -348,9 +356,10 @@ __device__ __forceinline__ void report(uint32_t *err, bool ok) {
 }
 
 // gate/up: K = D, raw stages hold one block column [NS][2][MR][BB] of the
-// tile's gate and up rows; hbuf[pair][row] = SiLU(gate) * up.
+// tile's gate and up rows. Warps 0-3 own the gate rows, warps 4-7 the up
+// rows (thread = row = TMEM lane); hbuf[pair][row] = SiLU(gate) * up.
 template <int DT, int NS>
-__global__ void __launch_bounds__(MR, 1)
+__global__ void __launch_bounds__(NTH, 1)
     k_mgateup(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
               size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ hbuf, uint32_t *err) {
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -359,29 +368,31 @@ __global__ void __launch_bounds__(MR, 1)
     const int nb = D / 256;
     const MPlan P = mplan(2, (uint32_t)NS * 2 * MR * BB, nb);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
-    const int r = threadIdx.x;
-    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
-    if (r < 32) tmem_alloc(tmem_slot, 256);
+    const int tid = threadIdx.x, warp = tid >> 5, m = warp >> 2, r = (warp & 3) * 32 + (tid & 31);
+    if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    if (warp == 0) tmem_alloc(tmem_slot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     uint32_t phase = 0;
     bool ok = true;
     const int tiles = de / MR, na = grp[2 * E + 1];
     const size_t rb = (size_t)nb * BB;
     const int32_t *pairs = grp + 2 * E + 2;
+    float *xch = reinterpret_cast<float *>(sm + P.xch) + r * MT;
     bool first = true;
-    uint8_t *Arow0 = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16, *Arow1 = Arow0 + MR * 256;
+    uint8_t *Arow = sm + P.A + m * MR * 256 + (r >> 3) * 2048 + (r & 7) * 16;
     for (int item = blockIdx.x; item < na * tiles && ok; item += gridDim.x) {
         const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
         const uint8_t *wg = slots[e].m[0] + (size_t)tile * MR * rb, *wu = slots[e].m[1] + (size_t)tile * MR * rb;
         auto issue = [&](int b) {
             if (b < nb) {
                 uint8_t *st = sm + P.raw + (b % NS) * 2 * MR * BB;
-                for (int i = r; i < 2 * MR * CPB; i += MR) {
-                    const int m = i / (MR * CPB), rr = (i / CPB) % MR, c = i % CPB;
-                    cp16(st + (m * MR + rr) * BB + 16 * c, (m ? wu : wg) + rr * rb + (size_t)b * BB + 16 * c);
+                for (int i = tid; i < 2 * MR * CPB; i += NTH) {
+                    const int mm = i / (MR * CPB), rr = (i / CPB) % MR, c = i % CPB;
+                    cp16(st + (mm * MR + rr) * BB + 16 * c, (mm ? wu : wg) + rr * rb + (size_t)b * BB + 16 * c);
                 }
             }
             cp_commit();
@@ -392,28 +403,40 @@ __global__ void __launch_bounds__(MR, 1)
             first = false;
 #pragma unroll
             for (int b = 0; b < NS - 1; b++) issue(b);
-            float acc[2][MT];
+            float acc[MT];
 #pragma unroll
-            for (int t = 0; t < MT; t++) acc[0][t] = acc[1][t] = 0.0f;
+            for (int t = 0; t < MT; t++) acc[t] = 0.0f;
             for (int b = 0; b < nb; b++) {
                 cp_wait<NS - 2>();
-                __syncthreads();   // block b staged; the previous block's unpacked tiles are consumed
+                __syncthreads();   // block b staged; the previous block's tiles and accumulators are consumed
                 issue(b + NS - 1);
-                const uint8_t *st = sm + P.raw + (b % NS) * 2 * MR * BB;
-                RowBlk rbk[2];
-                rbk[0] = unpack_row<DT>(st + r * BB, Arow0);
-                rbk[1] = unpack_row<DT>(st + (MR + r) * BB, Arow1);
+                const RowBlk rk = unpack_row<DT>(sm + P.raw + (b % NS) * 2 * MR * BB + (m * MR + r) * BB, Arow);
                 fence_async_smem();
                 __syncthreads();
-                const bool got = mma_block<DT, 2>(sm, P, tmem, phase, b, rbk, acc, nt);
+                if (tid == 0) issue_block<DT, 2>(sm, P, tmem, b);
+                const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
+                phase ^= 1u;
+                tc_fence_after();
+                int is[MT];
+#pragma unroll
+                for (int t = 0; t < MT; t++) is[t] = 0;
+                add_scaled<DT>(lane_base, (uint32_t)(m * 8 * MT), 0, 2, rk, is);
+                chain_tokens<DT>(sm, P, b, rk, is, acc, nt);
+                tc_fence_before();
                 if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
                 if (!ok) break;
             }
             cp_wait<0>();
-            __syncthreads();
+            if (m == 1) {
 #pragma unroll
-            for (int t = 0; t < MT; t++)
-                if (t < nt) hbuf[(size_t)pairs[c0 + t] * de + tile * MR + r] = __fmul_rn(silu_f(acc[0][t]), acc[1][t]);
+                for (int t = 0; t < MT; t++) xch[t] = acc[t];
+            }
+            __syncthreads();
+            if (m == 0) {
+#pragma unroll
+                for (int t = 0; t < MT; t++)
+                    if (t < nt) hbuf[(size_t)pairs[c0 + t] * de + tile * MR + r] = __fmul_rn(silu_f(acc[t]), xch[t]);
+            }
         }
     }
     if (!ok) {   // an MMA may still be in flight: one more bounded wait before the TMEM goes
@@ -423,13 +446,15 @@ __global__ void __launch_bounds__(MR, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (r < 32) tmem_free(tmem, 256);
+    if (warp == 0) tmem_free(tmem, 256);
 }
 
 // down: K = de; the tile's MR rows x all blocks (contiguous in HBM) are
-// staged whole, double-buffered across items; eo[pair][row].
+// staged whole, double-buffered across items. The two threads of a row each
+// unpack and sum half of the block's sub-blocks; the second hands its
+// partial integer sums to the first, which runs the chain; eo[pair][row].
 template <int DT>
-__global__ void __launch_bounds__(MR, 1)
+__global__ void __launch_bounds__(NTH, 1)
     k_mdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ hq, int D,
             int de, int E, float *__restrict__ eo, uint32_t *err) {
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -440,26 +465,28 @@ __global__ void __launch_bounds__(MR, 1)
     const uint32_t tstride = align_up(tile_bytes, 128u);
     const MPlan P = mplan(1, 2 * tstride, nb);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
-    const int r = threadIdx.x;
-    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
-    if (r < 32) tmem_alloc(tmem_slot, NCOL);
+    const int tid = threadIdx.x, warp = tid >> 5, half = warp >> 2, r = (warp & 3) * 32 + (tid & 31);
+    if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    if (warp == 0) tmem_alloc(tmem_slot, NCOL);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     uint32_t phase = 0;
     bool ok = true;
     const int tiles = D / MR, na = grp[2 * E + 1], n_items = na * tiles;
     const size_t rbd = (size_t)nb * BB;
     const int32_t *pairs = grp + 2 * E + 2;
     const uint32_t qh = qvec_bytes(nb);
+    int *xch = reinterpret_cast<int *>(sm + P.xch) + r * MT;
     uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
     auto issue_tile = [&](int item, int buf) {
         if (item < n_items) {
             const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
             const uint8_t *src = slots[e].m[2] + (size_t)tile * MR * rbd;
             uint8_t *dst = sm + P.raw + buf * tstride;
-            for (uint32_t i = r; i < tile_bytes / 16; i += MR) cp16(dst + 16 * i, src + 16 * i);
+            for (uint32_t i = tid; i < tile_bytes / 16; i += NTH) cp16(dst + 16 * i, src + 16 * i);
         }
         cp_commit();
     };
@@ -479,21 +506,40 @@ __global__ void __launch_bounds__(MR, 1)
             // first pass of an item: prefetch the next item's tile into the
             // other buffer (its previous item ended at a barrier)
             if (c0 == grp[e]) issue_tile(item + gridDim.x, buf ^ 1);
-            float acc[1][MT];
+            float acc[MT];
 #pragma unroll
-            for (int t = 0; t < MT; t++) acc[0][t] = 0.0f;
+            for (int t = 0; t < MT; t++) acc[t] = 0.0f;
             for (int b = 0; b < nb; b++) {
-                RowBlk rbk[1];   // A is free: every thread waited for the previous block's MMAs
-                rbk[0] = unpack_row<DT>(wt + b * BB, Arow);
+                // A is free: every thread waited for the previous block's MMAs
+                const RowBlk rk = unpack_row<DT>(wt + b * BB, Arow, half);
                 fence_async_smem();
                 __syncthreads();
-                const bool got = mma_block<DT, 1>(sm, P, tmem, phase, b, rbk, acc, nt);
-                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
-                if (!ok) break;
-            }
+                if (tid == 0) issue_block<DT, 1>(sm, P, tmem, b);
+                const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
+                phase ^= 1u;
+                tc_fence_after();
+                int is[MT];
 #pragma unroll
-            for (int t = 0; t < MT; t++)
-                if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * MR + r] = acc[0][t];
+                for (int t = 0; t < MT; t++) is[t] = 0;
+                add_scaled<DT>(lane_base, 0u, half * (SUB / 2), SUB / 8, rk, is);
+                if (half == 1) {
+#pragma unroll
+                    for (int t = 0; t < MT; t++) xch[t] = is[t];
+                }
+                tc_fence_before();
+                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA; publishes xch
+                if (!ok) break;
+                if (half == 0) {
+#pragma unroll
+                    for (int t = 0; t < MT; t++) is[t] += xch[t];   // exact integer sum of both halves
+                    chain_tokens<DT>(sm, P, b, rk, is, acc, nt);
+                }
+            }
+            if (half == 0) {
+#pragma unroll
+                for (int t = 0; t < MT; t++)
+                    if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * MR + r] = acc[t];
+            }
             __syncthreads();   // staged tokens and, after the last pass, this buffer are rewritten next
         }
     }
@@ -505,7 +551,7 @@ __global__ void __launch_bounds__(MR, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (r < 32) tmem_free(tmem, NCOL);
+    if (warp == 0) tmem_free(tmem, NCOL);
 }
 
 }  // namespace
@@ -560,7 +606,7 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
                             : (three ? k_mgateup<DT_Q5_K, 3> : k_mgateup<DT_Q5_K, 2>);
     int rc = opt_in(fn, smem);
     if (rc) return rc;
-    fn<<<grid, MR, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, hbuf, err);
+    fn<<<grid, NTH, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, hbuf, err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core gate/up launch");
 }
@@ -573,7 +619,7 @@ int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t
     auto fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K> : dt == DT_Q5_K ? k_mdown<DT_Q5_K> : k_mdown<DT_Q6_K>;
     int rc = opt_in(fn, smem);
     if (rc) return rc;
-    fn<<<grid, MR, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
+    fn<<<grid, NTH, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core down launch");
 }
