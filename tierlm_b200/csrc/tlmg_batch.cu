@@ -51,6 +51,30 @@ __global__ void k_bquant(const float *__restrict__ in, int rows, int len, uint8_
     }
 }
 
+// k_bquant of h = SiLU(g) * u formed on the fly (the tensor-core gate/up
+// kernel leaves the gate and up dots in two arrays)
+__global__ void k_bquant_swiglu(const float *__restrict__ g, const float *__restrict__ u, int rows, int len,
+                                uint8_t *__restrict__ out) {
+    const int lane = threadIdx.x & 31, nb = len / 256;
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+    const uint32_t qb = qvb(nb);
+    for (int q = gw; q < rows * nb; q += nw) {
+        const int r = q / nb, b = q - r * nb;
+        const size_t off = (size_t)r * len + 256 * b + 8 * lane;
+        const float4 g0 = __ldg(reinterpret_cast<const float4 *>(g + off)),
+                     g1 = __ldg(reinterpret_cast<const float4 *>(g + off) + 1);
+        const float4 u0 = __ldg(reinterpret_cast<const float4 *>(u + off)),
+                     u1 = __ldg(reinterpret_cast<const float4 *>(u + off) + 1);
+        const float4 h0 = make_float4(__fmul_rn(silu_f(g0.x), u0.x), __fmul_rn(silu_f(g0.y), u0.y),
+                                      __fmul_rn(silu_f(g0.z), u0.z), __fmul_rn(silu_f(g0.w), u0.w));
+        const float4 h1 = make_float4(__fmul_rn(silu_f(g1.x), u1.x), __fmul_rn(silu_f(g1.y), u1.y),
+                                      __fmul_rn(silu_f(g1.z), u1.z), __fmul_rn(silu_f(g1.w), u1.w));
+        uint8_t *base = out + (size_t)r * qb;
+        warp_quant_swz(h0, h1, base, nb, b, reinterpret_cast<int16_t *>(base + 256 * nb) + 16 * b,
+                       reinterpret_cast<float *>(base + 288 * nb) + b, lane);
+    }
+}
+
 // one warp per token
 constexpr int RW = 2;   // warps per CTA
 __global__ void __launch_bounds__(32 * RW) k_broute(BatchArgs a, int32_t *__restrict__ ids, float *__restrict__ w) {
@@ -468,8 +492,8 @@ size_t ep_record_bytes(int D) { return 16 + qvb(D / 256); }
 
 void batch_release(BatchScratch &s) {
     const int kmode = s.kmode, kmode_dn = s.kmode_dn;
-    for (void *p : { (void *)s.xq, (void *)s.ids, (void *)s.w, (void *)s.grp, (void *)s.hbuf, (void *)s.hq,
-                     (void *)s.eo })
+    for (void *p : { (void *)s.xq, (void *)s.ids, (void *)s.w, (void *)s.grp, (void *)s.hbuf, (void *)s.ubuf,
+                     (void *)s.hq, (void *)s.eo })
         if (p) cudaFree(p);
     if (s.cnt) cudaFreeHost(s.cnt);
     s = BatchScratch{};
@@ -486,7 +510,8 @@ static int reserve(BatchScratch &s, int n_tok, int64_t n_pairs, int D, int de, i
     batch_release(s);
     if (cudaMalloc(&s.xq, (size_t)cap * qvb(D / 256)) != cudaSuccess || cudaMalloc(&s.ids, 4 * np) != cudaSuccess ||
         cudaMalloc(&s.w, 4 * np) != cudaSuccess || cudaMalloc(&s.grp, 4 * (2 * (size_t)ce + 2 + np)) != cudaSuccess ||
-        cudaMalloc(&s.hbuf, 4 * np * de) != cudaSuccess || cudaMalloc(&s.hq, np * qvb(de / 256)) != cudaSuccess ||
+        cudaMalloc(&s.hbuf, 4 * np * de) != cudaSuccess || cudaMalloc(&s.ubuf, 4 * np * de) != cudaSuccess ||
+        cudaMalloc(&s.hq, np * qvb(de / 256)) != cudaSuccess ||
         cudaMalloc(&s.eo, 4 * np * D) != cudaSuccess || cudaMallocHost(&s.cnt, 4 * (EP_MAX_RANKS + 2)) != cudaSuccess) {
         cudaGetLastError();
         batch_release(s);
@@ -565,8 +590,10 @@ static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn
     const size_t sgu = tgateup_smem(dt_gu, D), sdn = tdown_smem(dt_dn, de);
     uint32_t *err = reinterpret_cast<uint32_t *>(s.cnt + EP_MAX_RANKS + 1);
     TGateUpFn tgu = s.kmode >= 1 ? pick_tgateup(dt_gu) : nullptr;
-    if (s.kmode >= 2 && mma_gateup_supported(dt_gu, D, de)) {
-        int rc = launch_mma_gateup(dt_gu, slots, s.grp, x, xstride, xdiv, D, de, E, na_max * (de / 128), s.hbuf, err, st);
+    const bool mma_gu = s.kmode >= 2 && mma_gateup_supported(dt_gu, D, de);
+    if (mma_gu) {
+        int rc = launch_mma_gateup(dt_gu, slots, s.grp, x, xstride, xdiv, D, de, E, na_max * (de / 128), s.hbuf,
+                                   s.ubuf, err, st);
         if (rc) return rc;
     } else if (tgu && sgu <= SMEM_MAX && smem_opt_in(tgu, sgu)) {
         const int64_t items = na_max * (de / TR);
@@ -577,7 +604,10 @@ static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn
         pick_gateup(dt_gu, D)<<<warp_blocks(na_max * ((de + 3) / 4), nsm), 256, 0, st>>>(slots, s.grp, x, xstride,
                                                                                         xdiv, D, de, E, s.hbuf);
     }
-    k_bquant<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, (int)np, de, s.hq);
+    if (mma_gu)
+        k_bquant_swiglu<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, s.ubuf, (int)np, de, s.hq);
+    else
+        k_bquant<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, (int)np, de, s.hq);
     TDownFn tdn = s.kmode_dn >= 1 ? pick_tdown(dt_dn) : nullptr;
     if (s.kmode_dn >= 2 && mma_down_supported(dt_dn, D, de)) {
         int rc = launch_mma_down(dt_dn, slots, s.grp, s.hq, D, de, E, na_max * (D / 128), eo, err, st);

@@ -24,7 +24,8 @@ struct BatchScratch {
     int32_t *ids = nullptr;     // [cap][k]
     float *w = nullptr;         // [cap][k]
     int32_t *grp = nullptr;     // expert offsets [E + 1], active experts [E], count [1], pairs [cap * k]
-    float *hbuf = nullptr;      // [cap * k][de] SwiGLU rows per (token, rank) pair
+    float *hbuf = nullptr;      // [cap * k][de] SwiGLU rows per (token, rank) pair (tensor-core path: gate dots)
+    float *ubuf = nullptr;      // [cap * k][de] up dots of the tensor-core path
     uint8_t *hq = nullptr;      // [cap * k] quantised h per pair
     float *eo = nullptr;        // [cap * k][D] expert outputs per pair
     int32_t *cnt = nullptr;     // pinned host [EP_MAX_RANKS + 2]: dispatch record counts, the count of

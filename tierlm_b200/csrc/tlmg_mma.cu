@@ -1,14 +1,16 @@
 // tlmg_mma.cu - grouped expert GEMM on tcgen05 (sm_100a), exact.
 //
-// Work item = (active expert, tile of 128 weight rows); one CTA of 128
-// threads, thread r <-> weight row r <-> TMEM lane r. For each pass of up to
-// 16 tokens of the expert and each K-quant block b in ascending order:
+// Work item = (active expert, tile of 128 weight rows[, matrix]); one CTA of
+// threads (gate/up: one per weight row; down: two per row, each half of the
+// sub-blocks), thread r <-> weight row r <-> TMEM lane r. For each pass of
+// up to TN tokens of the expert (8 for gate/up, 16 for down) and each
+// K-quant block b in ascending order:
 //
 //   1. the tile's raw block column is staged with cp.async (16-byte pieces);
 //   2. thread r unpacks its row into int8 codes in the canonical K-major
 //      no-swizzle UMMA layout (core matrix = 8 rows x 16 bytes) - Q4_K / Q5_K
 //      codes 0..31, Q6_K codes minus 32 - and keeps the block's scales;
-//   3. one thread issues one tcgen05.mma kind::i8 (M = 128, N = 16, K = 32)
+//   3. one thread issues one tcgen05.mma kind::i8 (M = 128, N = TN, K = 32)
 //      per sub-block: A = the sub-block's codes, B = the tokens' Q8_K codes of
 //      the same elements, D = that sub-block's own int32 accumulator in TMEM
 //      (a Q4_K / Q5_K sub-block is 32 elements; a Q6_K group is 16 elements,
@@ -40,7 +42,6 @@ namespace tlmg {
 namespace {
 
 constexpr int MR = 128;   // rows per tile = TMEM lanes = MMA M = threads
-constexpr int MT = 16;    // tokens per pass = MMA N
 constexpr int MAXNB = 16; // K blocks per row (K <= 4096)
 
 template <int DT> struct KQ;
@@ -73,18 +74,13 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t start, uint32_t lbo, uint
     return (uint64_t)((start >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
 }
-// Instruction descriptor: D s32 (c_format 2), A and B signed 8-bit, both
-// K-major, N = 16, M = 128.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MT >> 3) << 17) |
-                           ((uint32_t)(MR >> 4) << 24);
-
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b) {
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc) {
     // D = A * B (enable-input-d false: every accumulator starts from zero)
     const uint32_t z = 0;
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(IDESC), "r"(z), "r"(z)
+        "l"(a), "l"(b), "r"(idesc), "r"(z), "r"(z)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t *mbar) {
@@ -221,27 +217,28 @@ __device__ __forceinline__ RowBlk unpack_row(const uint8_t *blk, uint8_t *A, int
 }
 
 // ---------------------------------------------------------------------------
-// Shared-memory plan of one CTA (same on host and device).
-constexpr int NTH = 2 * MR;   // threads: two per weight row (8 warps)
+// Shared-memory plan of one CTA (same on host and device); TN = tokens per
+// pass (MMA N, 8 or 16).
 struct MPlan {
     uint32_t raw, raw_bytes;   // raw weight stages
     uint32_t A;                // unpacked int8 tiles [nmat][16 groups][16 chunks][8 rows][16 B]
-    uint32_t X, xsbo;          // token codes [2 groups][KC + 1 chunks][8 tokens][16 B] (chunk KC zero)
-    uint32_t dx, bs;           // f32 [MT][MAXNB] block scales, int32 [MT][MAXNB][8] sub-block bsums
-    uint32_t xch;              // 32-bit [MR][MT]: the second thread of a row hands its results over
+    uint32_t X, xsbo;          // token codes [TN / 8 groups][KC + 1 chunks][8 tokens][16 B] (chunk KC zero)
+    uint32_t dx, bs;           // f32 [TN][nb] block scales, int32 [TN][nb][8] sub-block bsums
+    uint32_t xch;              // 32-bit [MR][TN]: the second thread of a row hands its results over (or none)
     uint32_t bar, total;       // mbarrier (8 B) + TMEM address (4 B)
 };
-__host__ __device__ inline MPlan mplan(int nmat, uint32_t raw_bytes, int nb) {
+template <int TN>
+__host__ __device__ inline MPlan mplan(int nmat, uint32_t raw_bytes, int nb, bool xch) {
     MPlan p{};
     p.raw = 0;
     p.raw_bytes = raw_bytes;
     p.A = align_up(raw_bytes, 1024u);
     p.X = p.A + (uint32_t)nmat * MR * 256u;
     p.xsbo = (uint32_t)(16 * nb + 1) * 128u;
-    p.dx = p.X + 2u * p.xsbo;
-    p.bs = p.dx + (uint32_t)MT * MAXNB * 4u;
-    p.xch = p.bs + (uint32_t)MT * MAXNB * 8u * 4u;
-    p.bar = p.xch + (uint32_t)MR * MT * 4u;
+    p.dx = p.X + (uint32_t)(TN / 8) * p.xsbo;
+    p.bs = p.dx + align_up((uint32_t)TN * nb * 4u, 16u);
+    p.xch = p.bs + (uint32_t)TN * nb * 8u * 4u;
+    p.bar = p.xch + (xch ? (uint32_t)MR * TN * 4u : 0u);
     p.total = p.bar + 16u;
     return p;
 }
@@ -249,13 +246,13 @@ __host__ __device__ inline MPlan mplan(int nmat, uint32_t raw_bytes, int nb) {
 // Stages the pass's tokens: codes into the canonical B layout (cp.async),
 // block scales and sub-block sums into dx / bs. Zeroes the chunk KC of each
 // token group once per CTA (first == true).
-template <int DT>
+template <int DT, int TN>
 __device__ __forceinline__ void stage_tokens(uint8_t *sm, const MPlan &P, const uint8_t *x, size_t xstride, int xdiv,
                                              const int32_t *pairs, int nt, int nb, bool first) {
     const int KC = 16 * nb;
     uint8_t *X = sm + P.X;
     if (first)
-        for (int i = threadIdx.x; i < 2 * 8; i += blockDim.x)
+        for (int i = threadIdx.x; i < TN; i += blockDim.x)
             *reinterpret_cast<uint4 *>(X + (i >> 3) * P.xsbo + KC * 128 + (i & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
     for (int i = threadIdx.x; i < nt * KC; i += blockDim.x) {
         const int t = i / KC, kc = i - t * KC;
@@ -268,18 +265,26 @@ __device__ __forceinline__ void stage_tokens(uint8_t *sm, const MPlan &P, const 
     for (int i = threadIdx.x; i < nt * nb; i += blockDim.x) {
         const int t = i / nb, b = i - t * nb;
         const uint8_t *v = x + (size_t)(pairs[t] / xdiv) * xstride;
-        dx[t * MAXNB + b] = reinterpret_cast<const float *>(v + 288 * nb)[b];
+        dx[i] = reinterpret_cast<const float *>(v + 288 * nb)[b];
         if constexpr (DT != DT_Q6_K) {
             const int16_t *s16 = reinterpret_cast<const int16_t *>(v + 256 * nb) + 16 * b;
 #pragma unroll
-            for (int s = 0; s < 8; s++) bs[(t * MAXNB + b) * 8 + s] = (int)s16[2 * s] + (int)s16[2 * s + 1];
+            for (int s = 0; s < 8; s++) bs[i * 8 + s] = (int)s16[2 * s] + (int)s16[2 * s + 1];
         }
     }
 }
 
-// Thread 0 issues the MMAs of block b for nmat matrices (every sub-block
-// into its own accumulator) and commits them to the barrier.
-template <int DT, int NMAT>
+// Instruction descriptor: D s32 (c_format 2), A and B signed 8-bit, both
+// K-major, N = TN, M = 128.
+template <int TN>
+constexpr uint32_t idesc() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(MR >> 4) << 24);
+}
+
+// Thread 0 issues the MMAs of block b for matrices m0 .. m0 + NMAT - 1 of
+// the A tiles (every sub-block into its own accumulator, columns
+// (m * SUB + s) * TN) and commits them to the barrier.
+template <int DT, int NMAT, int TN>
 __device__ __forceinline__ void issue_block(uint8_t *sm, const MPlan &P, uint32_t tmem, int b) {
     constexpr int SUB = KQ<DT>::SUB;
     const uint32_t Xs = saddr(sm + P.X), As = saddr(sm + P.A);
@@ -300,47 +305,49 @@ __device__ __forceinline__ void issue_block(uint8_t *sm, const MPlan &P, uint32_
                 ad = umma_desc(As + m * MR * 256u + 2 * s * 128u, 128u, 2048u);
                 bd = umma_desc(Xs + kc * 128u, 128u, P.xsbo);
             }
-            umma_i8(tmem + (uint32_t)((m * SUB + s) * MT), ad, bd);
+            umma_i8(tmem + (uint32_t)((m * SUB + s) * TN), ad, bd, idesc<TN>());
         }
     umma_commit(reinterpret_cast<uint64_t *>(sm + P.bar));
 }
 
-// is[t] += scale_s * dot_s[t] over sub-blocks s0 .. s0 + 4 * n4 - 1 of one
-// matrix whose sub-block s accumulator starts at column col0 + s * MT.
-template <int DT>
-__device__ __forceinline__ void add_scaled(uint32_t lane_base, uint32_t col0, int s0, int n4, const RowBlk &rb,
-                                           int (&is)[MT]) {
+// is[t] += scale_s * dot_s[t] over sub-blocks s0 .. s0 + ns - 1 (ns a
+// multiple of 64 / TN) of one matrix whose sub-block s accumulator starts at
+// column col0 + s * TN.
+template <int DT, int TN>
+__device__ __forceinline__ void add_scaled(uint32_t lane_base, uint32_t col0, int s0, int ns, const RowBlk &rb,
+                                           int (&is)[TN]) {
+    constexpr int SPL = 64 / TN;   // sub-blocks per 64-column load
 #pragma unroll 1
-    for (int g = 0; g < n4; g++) {
+    for (int g = 0; g < ns; g += SPL) {
         int v[64];
-        tmem_ld64(lane_base + col0 + (uint32_t)((s0 + 4 * g) * MT), v);
+        tmem_ld64(lane_base + col0 + (uint32_t)((s0 + g) * TN), v);
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int s = s0 + 4 * g + j;
+        for (int j = 0; j < SPL; j++) {
+            const int s = s0 + g + j;
             int sc;
             if constexpr (DT == DT_Q6_K) sc = (int)(int8_t)byte_of(rb.s[s >> 2], s & 3);
             else sc = (int)byte_of(rb.s[s >> 2], s & 3);
 #pragma unroll
-            for (int t = 0; t < MT; t++) is[t] += sc * v[16 * j + t];
+            for (int t = 0; t < TN; t++) is[t] += sc * v[TN * j + t];
         }
     }
 }
 
 // The block's chain step for every token of the pass: acc[t] =
 // fmaf(d_w d_a, is, acc) (and, Q4_K / Q5_K, fmaf(-dmin_w d_a, ms, acc)).
-template <int DT>
-__device__ __forceinline__ void chain_tokens(const uint8_t *sm, const MPlan &P, int b, const RowBlk &rb,
-                                             const int (&is)[MT], float (&acc)[MT], int nt) {
+template <int DT, int TN>
+__device__ __forceinline__ void chain_tokens(const uint8_t *sm, const MPlan &P, int b, int nb, const RowBlk &rb,
+                                             const int (&is)[TN], float (&acc)[TN], int nt) {
     const float *dx = reinterpret_cast<const float *>(sm + P.dx);
     const int *bs = reinterpret_cast<const int *>(sm + P.bs);
 #pragma unroll
-    for (int t = 0; t < MT; t++) {
+    for (int t = 0; t < TN; t++) {
         if (t < nt) {
-            const float d = dx[t * MAXNB + b];
+            const float d = dx[t * nb + b];
             int ms = 0;
             if constexpr (DT != DT_Q6_K) {
-                const int4 b0 = *reinterpret_cast<const int4 *>(bs + (t * MAXNB + b) * 8);
-                const int4 b1 = *reinterpret_cast<const int4 *>(bs + (t * MAXNB + b) * 8 + 4);
+                const int4 b0 = *reinterpret_cast<const int4 *>(bs + (t * nb + b) * 8);
+                const int4 b1 = *reinterpret_cast<const int4 *>(bs + (t * nb + b) * 8 + 4);
                 ms = (int)byte_of(rb.s[2], 0) * b0.x + (int)byte_of(rb.s[2], 1) * b0.y +
                      (int)byte_of(rb.s[2], 2) * b0.z + (int)byte_of(rb.s[2], 3) * b0.w +
                      (int)byte_of(rb.s[3], 0) * b1.x + (int)byte_of(rb.s[3], 1) * b1.y +
@@ -355,88 +362,88 @@ __device__ __forceinline__ void report(uint32_t *err, bool ok) {
     if (!ok && threadIdx.x == 0) atomicOr(err, 1u);
 }
 
-// gate/up: K = D, raw stages hold one block column [NS][2][MR][BB] of the
-// tile's gate and up rows. Warps 0-3 own the gate rows, warps 4-7 the up
-// rows (thread = row = TMEM lane); hbuf[pair][row] = SiLU(gate) * up.
+// gate or up: K = D. Work item = (active expert, 128-row tile, matrix);
+// thread = weight row = TMEM lane; raw stages hold one block column
+// [NS][MR][BB] of the tile. out[m][pair][row] = the row's dot (m = 0 gate,
+// 1 up). Small enough for two CTAs per SM, which overlap each other's
+// unpack, MMA wait and epilogue.
+constexpr int GU_THREADS = MR;
+constexpr int GU_TN = 8;
 template <int DT, int NS>
-__global__ void __launch_bounds__(NTH, 1)
-    k_mgateup(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
-              size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ hbuf, uint32_t *err) {
+__global__ void __launch_bounds__(GU_THREADS, 2)
+    k_mgu(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
+          size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ gout, float *__restrict__ uout,
+          uint32_t *err) {
+    constexpr int TN = GU_TN;
     extern __shared__ __align__(1024) uint8_t sm[];
     constexpr int BB = KQ<DT>::BB, CPB = BB / 16;
     static_assert(BB % 16 == 0, "gate/up blocks must be 16-byte multiples");
     const int nb = D / 256;
-    const MPlan P = mplan(2, (uint32_t)NS * 2 * MR * BB, nb);
+    const MPlan P = mplan<TN>(1, (uint32_t)NS * MR * BB, nb, false);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
-    const int tid = threadIdx.x, warp = tid >> 5, m = warp >> 2, r = (warp & 3) * 32 + (tid & 31);
-    if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
-    if (warp == 0) tmem_alloc(tmem_slot, 256);
+    const int r = threadIdx.x, warp = r >> 5;
+    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    if (warp == 0) tmem_alloc(tmem_slot, 64);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
     uint32_t phase = 0;
     bool ok = true;
     const int tiles = de / MR, na = grp[2 * E + 1];
     const size_t rb = (size_t)nb * BB;
     const int32_t *pairs = grp + 2 * E + 2;
-    float *xch = reinterpret_cast<float *>(sm + P.xch) + r * MT;
     bool first = true;
-    uint8_t *Arow = sm + P.A + m * MR * 256 + (r >> 3) * 2048 + (r & 7) * 16;
-    for (int item = blockIdx.x; item < na * tiles && ok; item += gridDim.x) {
-        const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
-        const uint8_t *wg = slots[e].m[0] + (size_t)tile * MR * rb, *wu = slots[e].m[1] + (size_t)tile * MR * rb;
+    uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
+    for (int item = blockIdx.x; item < na * tiles * 2 && ok; item += gridDim.x) {
+        const int m = item & 1, it = item >> 1, ae = it / tiles, tile = it - ae * tiles, e = grp[E + 1 + ae];
+        const uint8_t *w = slots[e].m[m] + (size_t)tile * MR * rb;
+        float *out = m ? uout : gout;
         auto issue = [&](int b) {
             if (b < nb) {
-                uint8_t *st = sm + P.raw + (b % NS) * 2 * MR * BB;
-                for (int i = tid; i < 2 * MR * CPB; i += NTH) {
-                    const int mm = i / (MR * CPB), rr = (i / CPB) % MR, c = i % CPB;
-                    cp16(st + (mm * MR + rr) * BB + 16 * c, (mm ? wu : wg) + rr * rb + (size_t)b * BB + 16 * c);
+                uint8_t *st = sm + P.raw + (b % NS) * MR * BB;
+                for (int i = r; i < MR * CPB; i += GU_THREADS) {
+                    const int rr = i / CPB, c = i - rr * CPB;
+                    cp16(st + rr * BB + 16 * c, w + rr * rb + (size_t)b * BB + 16 * c);
                 }
             }
             cp_commit();
         };
-        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += MT) {
-            const int nt = min(MT, grp[e + 1] - c0);
-            stage_tokens<DT>(sm, P, x, xstride, xdiv, pairs + c0, nt, nb, first);
+        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += TN) {
+            const int nt = min(TN, grp[e + 1] - c0);
+            stage_tokens<DT, TN>(sm, P, x, xstride, xdiv, pairs + c0, nt, nb, first);
             first = false;
 #pragma unroll
             for (int b = 0; b < NS - 1; b++) issue(b);
-            float acc[MT];
+            float acc[TN];
 #pragma unroll
-            for (int t = 0; t < MT; t++) acc[t] = 0.0f;
+            for (int t = 0; t < TN; t++) acc[t] = 0.0f;
             for (int b = 0; b < nb; b++) {
                 cp_wait<NS - 2>();
-                __syncthreads();   // block b staged; the previous block's tiles and accumulators are consumed
+                __syncthreads();   // block b staged; the previous block's tile and accumulators are consumed
                 issue(b + NS - 1);
-                const RowBlk rk = unpack_row<DT>(sm + P.raw + (b % NS) * 2 * MR * BB + (m * MR + r) * BB, Arow);
+                const RowBlk rk = unpack_row<DT>(sm + P.raw + (b % NS) * MR * BB + r * BB, Arow);
                 fence_async_smem();
                 __syncthreads();
-                if (tid == 0) issue_block<DT, 2>(sm, P, tmem, b);
+                if (r == 0) issue_block<DT, 1, TN>(sm, P, tmem, b);
                 const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
                 phase ^= 1u;
                 tc_fence_after();
-                int is[MT];
+                int is[TN];
 #pragma unroll
-                for (int t = 0; t < MT; t++) is[t] = 0;
-                add_scaled<DT>(lane_base, (uint32_t)(m * 8 * MT), 0, 2, rk, is);
-                chain_tokens<DT>(sm, P, b, rk, is, acc, nt);
+                for (int t = 0; t < TN; t++) is[t] = 0;
+                add_scaled<DT, TN>(lane_base, 0u, 0, 8, rk, is);
+                chain_tokens<DT, TN>(sm, P, b, nb, rk, is, acc, nt);
                 tc_fence_before();
                 if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
                 if (!ok) break;
             }
             cp_wait<0>();
-            if (m == 1) {
 #pragma unroll
-                for (int t = 0; t < MT; t++) xch[t] = acc[t];
-            }
-            __syncthreads();
-            if (m == 0) {
-#pragma unroll
-                for (int t = 0; t < MT; t++)
-                    if (t < nt) hbuf[(size_t)pairs[c0 + t] * de + tile * MR + r] = __fmul_rn(silu_f(acc[t]), xch[t]);
-            }
+            for (int t = 0; t < TN; t++)
+                if (t < nt) out[(size_t)pairs[c0 + t] * de + tile * MR + r] = acc[t];
+            __syncthreads();   // staged tokens are rewritten next
         }
     }
     if (!ok) {   // an MMA may still be in flight: one more bounded wait before the TMEM goes
@@ -446,24 +453,27 @@ __global__ void __launch_bounds__(NTH, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_free(tmem, 256);
+    if (warp == 0) tmem_free(tmem, 64);
 }
 
 // down: K = de; the tile's MR rows x all blocks (contiguous in HBM) are
 // staged whole, double-buffered across items. The two threads of a row each
 // unpack and sum half of the block's sub-blocks; the second hands its
 // partial integer sums to the first, which runs the chain; eo[pair][row].
+constexpr int DN_THREADS = 2 * MR;
+constexpr int DN_TN = 16;
 template <int DT>
-__global__ void __launch_bounds__(NTH, 1)
+__global__ void __launch_bounds__(DN_THREADS, 1)
     k_mdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ hq, int D,
             int de, int E, float *__restrict__ eo, uint32_t *err) {
+    constexpr int TN = DN_TN;
     extern __shared__ __align__(1024) uint8_t sm[];
     constexpr int BB = KQ<DT>::BB, SUB = KQ<DT>::SUB;
-    constexpr uint32_t NCOL = SUB * MT <= 128 ? 128 : 256;
+    constexpr uint32_t NCOL = SUB * TN <= 128 ? 128 : 256;
     const int nb = de / 256;
     const uint32_t tile_bytes = (uint32_t)MR * nb * BB;   // a multiple of 16
     const uint32_t tstride = align_up(tile_bytes, 128u);
-    const MPlan P = mplan(1, 2 * tstride, nb);
+    const MPlan P = mplan<TN>(1, 2 * tstride, nb, true);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
     const int tid = threadIdx.x, warp = tid >> 5, half = warp >> 2, r = (warp & 3) * 32 + (tid & 31);
     if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
@@ -479,14 +489,14 @@ __global__ void __launch_bounds__(NTH, 1)
     const size_t rbd = (size_t)nb * BB;
     const int32_t *pairs = grp + 2 * E + 2;
     const uint32_t qh = qvec_bytes(nb);
-    int *xch = reinterpret_cast<int *>(sm + P.xch) + r * MT;
+    int *xch = reinterpret_cast<int *>(sm + P.xch) + r * TN;
     uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
     auto issue_tile = [&](int item, int buf) {
         if (item < n_items) {
             const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
             const uint8_t *src = slots[e].m[2] + (size_t)tile * MR * rbd;
             uint8_t *dst = sm + P.raw + buf * tstride;
-            for (uint32_t i = tid; i < tile_bytes / 16; i += NTH) cp16(dst + 16 * i, src + 16 * i);
+            for (uint32_t i = tid; i < tile_bytes / 16; i += DN_THREADS) cp16(dst + 16 * i, src + 16 * i);
         }
         cp_commit();
     };
@@ -496,9 +506,9 @@ __global__ void __launch_bounds__(NTH, 1)
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, buf ^= 1) {
         const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
         const uint8_t *wt = sm + P.raw + buf * tstride + (size_t)r * rbd;
-        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += MT) {
-            const int nt = min(MT, grp[e + 1] - c0);
-            stage_tokens<DT>(sm, P, hq, qh, 1, pairs + c0, nt, nb, first);
+        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += TN) {
+            const int nt = min(TN, grp[e + 1] - c0);
+            stage_tokens<DT, TN>(sm, P, hq, qh, 1, pairs + c0, nt, nb, first);
             cp_commit();
             cp_wait<0>();          // this item's tile and the pass's tokens
             first = false;
@@ -506,38 +516,38 @@ __global__ void __launch_bounds__(NTH, 1)
             // first pass of an item: prefetch the next item's tile into the
             // other buffer (its previous item ended at a barrier)
             if (c0 == grp[e]) issue_tile(item + gridDim.x, buf ^ 1);
-            float acc[MT];
+            float acc[TN];
 #pragma unroll
-            for (int t = 0; t < MT; t++) acc[t] = 0.0f;
+            for (int t = 0; t < TN; t++) acc[t] = 0.0f;
             for (int b = 0; b < nb; b++) {
                 // A is free: every thread waited for the previous block's MMAs
                 const RowBlk rk = unpack_row<DT>(wt + b * BB, Arow, half);
                 fence_async_smem();
                 __syncthreads();
-                if (tid == 0) issue_block<DT, 1>(sm, P, tmem, b);
+                if (tid == 0) issue_block<DT, 1, TN>(sm, P, tmem, b);
                 const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
                 phase ^= 1u;
                 tc_fence_after();
-                int is[MT];
+                int is[TN];
 #pragma unroll
-                for (int t = 0; t < MT; t++) is[t] = 0;
-                add_scaled<DT>(lane_base, 0u, half * (SUB / 2), SUB / 8, rk, is);
+                for (int t = 0; t < TN; t++) is[t] = 0;
+                add_scaled<DT, TN>(lane_base, 0u, half * (SUB / 2), SUB / 2, rk, is);
                 if (half == 1) {
 #pragma unroll
-                    for (int t = 0; t < MT; t++) xch[t] = is[t];
+                    for (int t = 0; t < TN; t++) xch[t] = is[t];
                 }
                 tc_fence_before();
                 if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA; publishes xch
                 if (!ok) break;
                 if (half == 0) {
 #pragma unroll
-                    for (int t = 0; t < MT; t++) is[t] += xch[t];   // exact integer sum of both halves
-                    chain_tokens<DT>(sm, P, b, rk, is, acc, nt);
+                    for (int t = 0; t < TN; t++) is[t] += xch[t];   // exact integer sum of both halves
+                    chain_tokens<DT, TN>(sm, P, b, nb, rk, is, acc, nt);
                 }
             }
             if (half == 0) {
 #pragma unroll
-                for (int t = 0; t < MT; t++)
+                for (int t = 0; t < TN; t++)
                     if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * MR + r] = acc[t];
             }
             __syncthreads();   // staged tokens and, after the last pass, this buffer are rewritten next
@@ -561,11 +571,11 @@ static int gateup_stages(int D) { return D <= 2048 ? 3 : 2; }
 
 static uint32_t gateup_smem(int dt, int D) {
     const int BB = dt_block_bytes(dt);
-    return mplan(2, (uint32_t)gateup_stages(D) * 2 * MR * BB, D / 256).total;
+    return mplan<GU_TN>(1, (uint32_t)gateup_stages(D) * MR * BB, D / 256, false).total;
 }
 static uint32_t down_smem(int dt, int de) {
     const uint32_t tile = (uint32_t)MR * (de / 256) * dt_block_bytes(dt);
-    return mplan(1, 2 * align_up(tile, 128u), de / 256).total;
+    return mplan<DN_TN>(1, 2 * align_up(tile, 128u), de / 256, true).total;
 }
 constexpr uint32_t SMEM_LIMIT = 227 * 1024;
 
@@ -589,24 +599,25 @@ static int opt_in(F fn, uint32_t bytes) {
     return TLMG_OK;
 }
 
-static int grid_for(int64_t max_items) {
+static int grid_for(int64_t max_items, int per_sm) {
     int dev = 0, nsm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    return (int)std::max<int64_t>(1, std::min<int64_t>(max_items, nsm));
+    return (int)std::max<int64_t>(1, std::min<int64_t>(max_items, (int64_t)per_sm * nsm));
 }
 
 int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8_t *x, size_t xstride, int xdiv,
-                      int D, int de, int E, int64_t max_items, float *hbuf, uint32_t *err, cudaStream_t st) {
+                      int D, int de, int E, int64_t max_items, float *gout, float *uout, uint32_t *err,
+                      cudaStream_t st) {
     if (!mma_gateup_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core gate/up: dtype %d D %d", dt, D);
     const uint32_t smem = gateup_smem(dt, D);
-    const int grid = grid_for(max_items);
+    const int grid = grid_for(2 * max_items, smem <= 113 * 1024 ? 2 : 1);
     const bool three = gateup_stages(D) == 3;
-    auto fn = dt == DT_Q4_K ? (three ? k_mgateup<DT_Q4_K, 3> : k_mgateup<DT_Q4_K, 2>)
-                            : (three ? k_mgateup<DT_Q5_K, 3> : k_mgateup<DT_Q5_K, 2>);
+    auto fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3> : k_mgu<DT_Q4_K, 2>)
+                            : (three ? k_mgu<DT_Q5_K, 3> : k_mgu<DT_Q5_K, 2>);
     int rc = opt_in(fn, smem);
     if (rc) return rc;
-    fn<<<grid, NTH, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, hbuf, err);
+    fn<<<grid, GU_THREADS, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, gout, uout, err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core gate/up launch");
 }
@@ -615,11 +626,11 @@ int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t
                     int64_t max_items, float *eo, uint32_t *err, cudaStream_t st) {
     if (!mma_down_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core down: dtype %d de %d", dt, de);
     const uint32_t smem = down_smem(dt, de);
-    const int grid = grid_for(max_items);
+    const int grid = grid_for(max_items, 1);
     auto fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K> : dt == DT_Q5_K ? k_mdown<DT_Q5_K> : k_mdown<DT_Q6_K>;
     int rc = opt_in(fn, smem);
     if (rc) return rc;
-    fn<<<grid, NTH, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
+    fn<<<grid, DN_THREADS, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core down launch");
 }

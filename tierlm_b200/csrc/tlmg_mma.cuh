@@ -19,11 +19,13 @@ bool mma_down_supported(int dt, int D, int de);
 
 // grp: the expert grouping of the batched path (offsets [E + 1], active
 // experts [E], count, pairs). Pair q's quantised input (swizzled Q8_K
-// vector) at x + (q / xdiv) * xstride. hbuf[q][de] = SiLU(gate) * up.
+// vector) at x + (q / xdiv) * xstride. gout[q][de] / uout[q][de] receive
+// the gate / up row dots (the caller forms SiLU(gate) * up).
 // err: device word; bit 0 is set when a tensor-core wait expired. The
 // launchers queue one kernel each and leave launch counting to the caller.
 int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8_t *x, size_t xstride, int xdiv,
-                      int D, int de, int E, int64_t max_items, float *hbuf, uint32_t *err, cudaStream_t st);
+                      int D, int de, int E, int64_t max_items, float *gout, float *uout, uint32_t *err,
+                      cudaStream_t st);
 // hq: quantised h per pair (swizzled Q8_K vectors of de); eo[q][D].
 int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t *hq, int D, int de, int E,
                     int64_t max_items, float *eo, uint32_t *err, cudaStream_t st);
