@@ -61,6 +61,7 @@ __device__ __forceinline__ void cp16(void *dst, const void *src) {
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // generic-proxy shared writes -> visible to the tensor cores' async proxy
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -456,104 +457,115 @@ __global__ void __launch_bounds__(GU_THREADS, 2)
     if (warp == 0) tmem_free(tmem, 64);
 }
 
-// down: K = de; the tile's MR rows x all blocks (contiguous in HBM) are
-// staged whole, double-buffered across items. The two threads of a row each
-// unpack and sum half of the block's sub-blocks; the second hands its
-// partial integer sums to the first, which runs the chain; eo[pair][row].
-constexpr int DN_THREADS = 2 * MR;
-constexpr int DN_TN = 16;
+// down: K = de. Work item = (active expert, 128-row tile); thread = weight
+// row = TMEM lane. The tile's rows x all blocks (contiguous in HBM) are
+// staged whole; each block is unpacked and multiplied in two halves through
+// a half-block A tile (8 chunks), so that the CTA fits twice on an SM and
+// the two CTAs overlap each other's copies, unpacking and epilogues.
+constexpr int DN_THREADS = MR;
+constexpr int DN_TN = 8;
 template <int DT>
-__global__ void __launch_bounds__(DN_THREADS, 1)
+__global__ void __launch_bounds__(DN_THREADS, 2)
     k_mdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ hq, int D,
             int de, int E, float *__restrict__ eo, uint32_t *err) {
     constexpr int TN = DN_TN;
     extern __shared__ __align__(1024) uint8_t sm[];
     constexpr int BB = KQ<DT>::BB, SUB = KQ<DT>::SUB;
-    constexpr uint32_t NCOL = SUB * TN <= 128 ? 128 : 256;
+    constexpr uint32_t NCOL = SUB * TN <= 64 ? 64 : 128;
     const int nb = de / 256;
     const uint32_t tile_bytes = (uint32_t)MR * nb * BB;   // a multiple of 16
-    const uint32_t tstride = align_up(tile_bytes, 128u);
-    const MPlan P = mplan<TN>(1, 2 * tstride, nb, true);
+    const MPlan P = mplan<TN>(0, align_up(tile_bytes, 1024u) + MR * 128u, nb, false);   // raw tile + half A tile
+    const uint32_t Ahalf = align_up(tile_bytes, 1024u);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
-    const int tid = threadIdx.x, warp = tid >> 5, half = warp >> 2, r = (warp & 3) * 32 + (tid & 31);
-    if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    const int r = threadIdx.x, warp = r >> 5;
+    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
     if (warp == 0) tmem_alloc(tmem_slot, NCOL);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
     uint32_t phase = 0;
     bool ok = true;
     const int tiles = D / MR, na = grp[2 * E + 1], n_items = na * tiles;
     const size_t rbd = (size_t)nb * BB;
     const int32_t *pairs = grp + 2 * E + 2;
     const uint32_t qh = qvec_bytes(nb);
-    int *xch = reinterpret_cast<int *>(sm + P.xch) + r * TN;
-    uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
-    auto issue_tile = [&](int item, int buf) {
+    uint8_t *Arow = sm + Ahalf + (r >> 3) * 1024 + (r & 7) * 16;   // [16 groups][8 chunks][8 rows][16 B]
+    const uint32_t As = saddr(sm + Ahalf), Xs = saddr(sm + P.X);
+    const int KC = 16 * nb;
+    auto issue_tile = [&](int item) {
         if (item < n_items) {
             const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
             const uint8_t *src = slots[e].m[2] + (size_t)tile * MR * rbd;
-            uint8_t *dst = sm + P.raw + buf * tstride;
-            for (uint32_t i = tid; i < tile_bytes / 16; i += DN_THREADS) cp16(dst + 16 * i, src + 16 * i);
+            for (uint32_t i = r; i < tile_bytes / 16; i += DN_THREADS) cp16(sm + 16 * i, src + 16 * i);
         }
-        cp_commit();
     };
     bool first = true;
-    int buf = 0;
-    issue_tile(blockIdx.x, 0);
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, buf ^= 1) {
+    issue_tile(blockIdx.x);
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const int ae = item / tiles, tile = item - ae * tiles, e = grp[E + 1 + ae];
-        const uint8_t *wt = sm + P.raw + buf * tstride + (size_t)r * rbd;
+        const uint8_t *wt = sm + (size_t)r * rbd;
         for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += TN) {
             const int nt = min(TN, grp[e + 1] - c0);
+            const bool last_pass = c0 + TN >= grp[e + 1];
             stage_tokens<DT, TN>(sm, P, hq, qh, 1, pairs + c0, nt, nb, first);
             cp_commit();
             cp_wait<0>();          // this item's tile and the pass's tokens
             first = false;
             __syncthreads();
-            // first pass of an item: prefetch the next item's tile into the
-            // other buffer (its previous item ended at a barrier)
-            if (c0 == grp[e]) issue_tile(item + gridDim.x, buf ^ 1);
             float acc[TN];
 #pragma unroll
             for (int t = 0; t < TN; t++) acc[t] = 0.0f;
-            for (int b = 0; b < nb; b++) {
-                // A is free: every thread waited for the previous block's MMAs
-                const RowBlk rk = unpack_row<DT>(wt + b * BB, Arow, half);
-                fence_async_smem();
-                __syncthreads();
-                if (tid == 0) issue_block<DT, 1, TN>(sm, P, tmem, b);
-                const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
-                phase ^= 1u;
+            for (int b = 0; b < nb && ok; b++) {
+                RowBlk rk;
+#pragma unroll 1
+                for (int h = 0; h < 2; h++) {
+                    // the half tile is free: every thread waited for the previous MMAs
+                    rk = unpack_row<DT>(wt + b * BB, Arow - 8 * h * 128, h);
+                    fence_async_smem();
+                    __syncthreads();
+                    if (last_pass && b == nb - 1 && h == 1) issue_tile(item + gridDim.x);   // raw tile consumed
+                    if (r == 0) {
+                        tc_fence_after();
+                        if constexpr (DT == DT_Q6_K) {
+#pragma unroll
+                            for (int g = 0; g < 8; g++) {   // group 8h + g = chunk g of the half; B's second half: zero chunk
+                                const int kc = 16 * b + 8 * h + g;
+                                umma_i8(tmem + (uint32_t)((8 * h + g) * TN), umma_desc(As + g * 128u, 128u, 1024u),
+                                        umma_desc(Xs + kc * 128u, (uint32_t)(KC - kc) * 128u, P.xsbo), idesc<TN>());
+                            }
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; q++) {   // sub-block 4h + q = chunks 2q, 2q + 1 of the half
+                                const int kc = 16 * b + 8 * h + 2 * q;
+                                umma_i8(tmem + (uint32_t)((4 * h + q) * TN), umma_desc(As + 2 * q * 128u, 128u, 1024u),
+                                        umma_desc(Xs + kc * 128u, 128u, P.xsbo), idesc<TN>());
+                            }
+                        }
+                        umma_commit(reinterpret_cast<uint64_t *>(sm + P.bar));
+                    }
+                    const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
+                    phase ^= 1u;
+                    if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
+                    if (!ok) break;
+                }
+                if (!ok) break;
                 tc_fence_after();
                 int is[TN];
 #pragma unroll
                 for (int t = 0; t < TN; t++) is[t] = 0;
-                add_scaled<DT, TN>(lane_base, 0u, half * (SUB / 2), SUB / 2, rk, is);
-                if (half == 1) {
-#pragma unroll
-                    for (int t = 0; t < TN; t++) xch[t] = is[t];
-                }
+                add_scaled<DT, TN>(lane_base, 0u, 0, SUB, rk, is);
+                chain_tokens<DT, TN>(sm, P, b, nb, rk, is, acc, nt);
                 tc_fence_before();
-                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA; publishes xch
-                if (!ok) break;
-                if (half == 0) {
-#pragma unroll
-                    for (int t = 0; t < TN; t++) is[t] += xch[t];   // exact integer sum of both halves
-                    chain_tokens<DT, TN>(sm, P, b, nb, rk, is, acc, nt);
-                }
             }
-            if (half == 0) {
 #pragma unroll
-                for (int t = 0; t < TN; t++)
-                    if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * MR + r] = acc[t];
-            }
-            __syncthreads();   // staged tokens and, after the last pass, this buffer are rewritten next
+            for (int t = 0; t < TN; t++)
+                if (t < nt) eo[(size_t)pairs[c0 + t] * D + tile * MR + r] = acc[t];
+            __syncthreads();   // staged tokens are rewritten next
         }
     }
-    cp_wait<0>();
+    cp_wait_all();   // a prefetched tile may still be in flight
     if (!ok) {
         mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase ^ 1u, WAIT_LIMIT);   // the phase that expired
         report(err, false);
@@ -575,7 +587,7 @@ static uint32_t gateup_smem(int dt, int D) {
 }
 static uint32_t down_smem(int dt, int de) {
     const uint32_t tile = (uint32_t)MR * (de / 256) * dt_block_bytes(dt);
-    return mplan<DN_TN>(1, 2 * align_up(tile, 128u), de / 256, true).total;
+    return mplan<DN_TN>(0, align_up(tile, 1024u) + MR * 128u, de / 256, false).total;
 }
 constexpr uint32_t SMEM_LIMIT = 227 * 1024;
 
@@ -626,7 +638,7 @@ int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t
                     int64_t max_items, float *eo, uint32_t *err, cudaStream_t st) {
     if (!mma_down_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core down: dtype %d de %d", dt, de);
     const uint32_t smem = down_smem(dt, de);
-    const int grid = grid_for(max_items, 1);
+    const int grid = grid_for(max_items, smem <= 113 * 1024 ? 2 : 1);
     auto fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K> : dt == DT_Q5_K ? k_mdown<DT_Q5_K> : k_mdown<DT_Q6_K>;
     int rc = opt_in(fn, smem);
     if (rc) return rc;
