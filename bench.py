@@ -326,24 +326,41 @@ def main() -> None:
     h2d = L * (D + E) * 4
     d2h = L * D * 4
 
-    # ---- batched decode (bs = BATCH tokens through each layer, one call per layer)
+    # ---- batched decode (bs = BATCH tokens per GPU through each layer, one call per layer);
+    # at N > 1 expert-parallel: each GPU owns E / N experts of every layer and exchanges
+    # the (token, expert) records with NCCL all-to-all
     batch = None
     if args.batch > 1:
         B = args.batch
         bx = torch.randn((2, L, B, D), generator=g, device=dev)
         bl = torch.randn((2, L, B, E), generator=g, device=dev)
         bo = torch.empty((2, L, B, D), device=dev)
-        # distinct experts each layer call reads (softmax top-k = the k largest logits)
+        # distinct experts each layer call reads (softmax top-k = the k largest logits),
+        # over the tokens of every GPU
         sel = torch.topk(bl, K, dim=-1).indices                               # [2, L, B, K]
         hit = torch.zeros((2, L, E), dtype=torch.bool, device=dev)
         hit.scatter_(2, sel.reshape(2, L, B * K), True)
+        if world > 1:
+            hits = hit.to(torch.uint8)
+            dist.all_reduce(hits, op=dist.ReduceOp.MAX)
+            hit = hits.bool()
         uniq = hit.sum(-1).double()                                            # [2, L]
         bytes_expert = BYTES_LAYER_TOKEN // K
+        ep = None
+        if world > 1:
+            from tierlm_b200.ep import ExpertParallel
+            ep = ExpertParallel(ctx, D, E, K, device=dev)
+
+        def layer_call(layer, xi, li, oi):
+            if ep is None:
+                ctx.expert_ffn_batch(layer, xi, li, oi)
+            else:
+                ep.ffn_batch(layer, xi, li, oi)
 
         def bstep(s):
             i = s % 2
             for layer in range(L):
-                ctx.expert_ffn_batch(layer, bx[i, layer], bl[i, layer], bo[i, layer])
+                layer_call(layer, bx[i, layer], bl[i, layer], bo[i, layer])
 
         for s in range(args.warmup):
             bstep(s)
@@ -354,24 +371,34 @@ def main() -> None:
         ubytes = sum(float(uniq[s % 2].sum()) for s in range(args.steps)) * bytes_expert
         hbx, hbl = bx.cpu().pin_memory(), bl.cpu().pin_memory()
         hbo = torch.empty((2, L, B, D)).pin_memory()
+        dx_, dl_, do_ = torch.empty((B, D), device=dev), torch.empty((B, E), device=dev), torch.empty((B, D), device=dev)
 
         def bstep_host(s):
             i = s % 2
             for layer in range(L):
-                ctx.expert_ffn_batch(layer, hbx[i, layer], hbl[i, layer], hbo[i, layer])
+                if ep is None:
+                    ctx.expert_ffn_batch(layer, hbx[i, layer], hbl[i, layer], hbo[i, layer])
+                else:   # the exchange needs device buffers: the copies are part of the step
+                    dx_.copy_(hbx[i, layer], non_blocking=True)
+                    dl_.copy_(hbl[i, layer], non_blocking=True)
+                    ep.ffn_batch(layer, dx_, dl_, do_)
+                    hbo[i, layer].copy_(do_, non_blocking=True)
 
         for s in range(args.warmup):
             bstep_host(s)
         bms_e2e = timed(bstep_host, args.steps)
-        batch = {"batch": B, "metric": f"decode tok/s, bs={B}, expert FFN of {L} layers per token",
+        batch = {"batch": B, "metric": f"decode tok/s, bs={B} per GPU, expert FFN of {L} layers per token",
                  "tokens_per_s": round(world * args.steps * B / (bms * 1e-3), 1),
                  "ms_per_step": bms / args.steps,
-                 "unique_expert_GBps": round(world * ubytes / (bms * 1e-3) / 1e9, 1),
+                 "unique_expert_GBps": round(ubytes / (bms * 1e-3) / 1e9, 1),
                  "unique_experts_per_layer": round(float(uniq.mean()), 2),
                  "gpu_launches": blaunch,
+                 "kernels": "tcgen05.mma kind::i8 gate/up and down (one TMEM accumulator per sub-block)",
+                 "parallelism": "single GPU" if world == 1 else f"expert-parallel x{world} (NCCL all-to-all)",
                  "e2e": {"tokens_per_s": round(world * args.steps * B / (bms_e2e * 1e-3), 1),
                          "h2d_bytes_per_step": L * B * (D + E) * 4, "d2h_bytes_per_step": L * B * D * 4,
-                         "api": "tlmg_expert_ffn_batch (pinned host buffers)"},
+                         "api": "tlmg_expert_ffn_batch (pinned host buffers)" if world == 1 else
+                                "ExpertParallel.ffn_batch with pinned host copies in the step"},
                  "note": "one call per layer serves all B tokens; each selected expert is read once per call"}
 
     cpu = None
