@@ -233,6 +233,7 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="batched-decode section: tokens per layer call (<= 1: off)")
+    ap.add_argument("--prefill", type=int, default=2048, help="prefill section: prompt tokens per layer call (0: off)")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("TLMG_BENCH_ALLOW_SHORT"), \
         "use at least 3 warm-up steps"
@@ -401,6 +402,31 @@ def main() -> None:
                                 "ExpertParallel.ffn_batch with pinned host copies in the step"},
                  "note": "one call per layer serves all B tokens; each selected expert is read once per call"}
 
+    # ---- prefill: PREFILL tokens of one GPU's prompt through each layer's experts, one call per layer
+    prefill = None
+    if args.prefill > 0:
+        T = args.prefill
+        px = torch.randn((L, T, D), generator=g, device=dev)
+        pl = torch.randn((L, T, E), generator=g, device=dev)
+        po = torch.empty((L, T, D), device=dev)
+
+        def pstep(s):
+            for layer in range(L):
+                ctx.expert_ffn_batch(layer, px[layer], pl[layer], po[layer])
+
+        for s in range(args.warmup):
+            pstep(s)
+        psteps = max(1, min(args.steps, 5))
+        pms = timed(pstep, psteps)
+        pbytes = L * E * (BYTES_LAYER_TOKEN // K)           # every expert is selected at 2048 tokens
+        flops = 2.0 * T * K * (2 * DE * D + D * DE) * L      # int8 MACs x 2 per step
+        prefill = {"tokens": T, "metric": f"prefill tok/s, {T}-token prompt, expert FFN of {L} layers",
+                   "tokens_per_s": round(world * psteps * T / (pms * 1e-3), 1),
+                   "ms_per_step": pms / psteps, "steps": psteps,
+                   "int8_tops": round(world * psteps * flops / (pms * 1e-3) / 1e12, 2),
+                   "weight_GBps": round(world * psteps * pbytes / (pms * 1e-3) / 1e9, 1),
+                   "note": "tlmg_expert_ffn_batch with all prompt tokens of a layer in one call (tensor-core kernels)"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -432,7 +458,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
-            "batched_decode": batch,
+            "batched_decode": batch, "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     ctx.close()
