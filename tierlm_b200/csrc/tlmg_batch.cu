@@ -591,9 +591,10 @@ static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn
     uint32_t *err = reinterpret_cast<uint32_t *>(s.cnt + EP_MAX_RANKS + 1);
     TGateUpFn tgu = s.kmode >= 1 ? pick_tgateup(dt_gu) : nullptr;
     const bool mma_gu = s.kmode >= 2 && mma_gateup_supported(dt_gu, D, de);
+    const bool wide = np >= 24 * na_max;   // >= 24 tokens per expert on average
     if (mma_gu) {
-        int rc = launch_mma_gateup(dt_gu, slots, s.grp, x, xstride, xdiv, D, de, E, na_max * (de / 128), s.hbuf,
-                                   s.ubuf, err, st);
+        int rc = launch_mma_gateup(dt_gu, slots, s.grp, x, xstride, xdiv, D, de, E, na_max * (de / 128), wide,
+                                   s.hbuf, s.ubuf, err, st);
         if (rc) return rc;
     } else if (tgu && sgu <= SMEM_MAX && smem_opt_in(tgu, sgu)) {
         const int64_t items = na_max * (de / TR);
@@ -610,7 +611,7 @@ static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn
         k_bquant<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, (int)np, de, s.hq);
     TDownFn tdn = s.kmode_dn >= 1 ? pick_tdown(dt_dn) : nullptr;
     if (s.kmode_dn >= 2 && mma_down_supported(dt_dn, D, de)) {
-        int rc = launch_mma_down(dt_dn, slots, s.grp, s.hq, D, de, E, na_max * (D / 128), eo, err, st);
+        int rc = launch_mma_down(dt_dn, slots, s.grp, s.hq, D, de, E, na_max * (D / 128), wide, eo, err, st);
         if (rc) return rc;
     } else if (tdn && sdn <= SMEM_MAX && smem_opt_in(tdn, sdn)) {
         const int64_t items = na_max * (D / TR);

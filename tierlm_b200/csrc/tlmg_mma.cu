@@ -369,13 +369,11 @@ __device__ __forceinline__ void report(uint32_t *err, bool ok) {
 // 1 up). Small enough for two CTAs per SM, which overlap each other's
 // unpack, MMA wait and epilogue.
 constexpr int GU_THREADS = MR;
-constexpr int GU_TN = 8;
-template <int DT, int NS>
-__global__ void __launch_bounds__(GU_THREADS, 2)
+template <int DT, int NS, int TN>
+__global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? 2 : 1)
     k_mgu(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
           size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ gout, float *__restrict__ uout,
           uint32_t *err) {
-    constexpr int TN = GU_TN;
     extern __shared__ __align__(1024) uint8_t sm[];
     constexpr int BB = KQ<DT>::BB, CPB = BB / 16;
     static_assert(BB % 16 == 0, "gate/up blocks must be 16-byte multiples");
@@ -384,7 +382,7 @@ __global__ void __launch_bounds__(GU_THREADS, 2)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
     const int r = threadIdx.x, warp = r >> 5;
     if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
-    if (warp == 0) tmem_alloc(tmem_slot, 64);
+    if (warp == 0) tmem_alloc(tmem_slot, 8 * TN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -454,7 +452,7 @@ __global__ void __launch_bounds__(GU_THREADS, 2)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_free(tmem, 64);
+    if (warp == 0) tmem_free(tmem, 8 * TN);
 }
 
 // down: K = de. Work item = (active expert, 128-row tile); thread = weight
@@ -463,15 +461,13 @@ __global__ void __launch_bounds__(GU_THREADS, 2)
 // a half-block A tile (8 chunks), so that the CTA fits twice on an SM and
 // the two CTAs overlap each other's copies, unpacking and epilogues.
 constexpr int DN_THREADS = MR;
-constexpr int DN_TN = 8;
-template <int DT>
-__global__ void __launch_bounds__(DN_THREADS, 2)
+template <int DT, int TN>
+__global__ void __launch_bounds__(DN_THREADS, TN <= 8 ? 2 : 1)
     k_mdown(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ hq, int D,
             int de, int E, float *__restrict__ eo, uint32_t *err) {
-    constexpr int TN = DN_TN;
     extern __shared__ __align__(1024) uint8_t sm[];
     constexpr int BB = KQ<DT>::BB, SUB = KQ<DT>::SUB;
-    constexpr uint32_t NCOL = SUB * TN <= 64 ? 64 : 128;
+    constexpr uint32_t NCOL = SUB * TN <= 64 ? 64 : SUB * TN <= 128 ? 128 : SUB * TN <= 256 ? 256 : 512;
     const int nb = de / 256;
     const uint32_t tile_bytes = (uint32_t)MR * nb * BB;   // a multiple of 16
     const MPlan P = mplan<TN>(0, align_up(tile_bytes, 1024u) + MR * 128u, nb, false);   // raw tile + half A tile
@@ -579,25 +575,29 @@ __global__ void __launch_bounds__(DN_THREADS, 2)
 }  // namespace
 
 // ---------------------------------------------------------------------------
-static int gateup_stages(int D) { return D <= 2048 ? 3 : 2; }
+// Tokens per pass: 8 for decode-sized groups (small tiles, two CTAs per
+// SM), 32 when the experts average many tokens (prefill: the unpack and the
+// per-pass overheads are shared by 4x more tokens).
+static int pass_tokens(bool wide) { return wide ? 32 : 8; }
+static int gateup_stages(int D, int tn) { return D <= 2048 || tn <= 8 ? 3 : 2; }
 
-static uint32_t gateup_smem(int dt, int D) {
-    const int BB = dt_block_bytes(dt);
-    return mplan<GU_TN>(1, (uint32_t)gateup_stages(D) * MR * BB, D / 256, false).total;
+static uint32_t gateup_smem(int dt, int D, int tn) {
+    const uint32_t raw = (uint32_t)gateup_stages(D, tn) * MR * dt_block_bytes(dt);
+    return tn <= 8 ? mplan<8>(1, raw, D / 256, false).total : mplan<32>(1, raw, D / 256, false).total;
 }
-static uint32_t down_smem(int dt, int de) {
-    const uint32_t tile = (uint32_t)MR * (de / 256) * dt_block_bytes(dt);
-    return mplan<DN_TN>(0, align_up(tile, 1024u) + MR * 128u, de / 256, false).total;
+static uint32_t down_smem(int dt, int de, int tn) {
+    const uint32_t tile = align_up((uint32_t)MR * (de / 256) * dt_block_bytes(dt), 1024u) + MR * 128u;
+    return tn <= 8 ? mplan<8>(0, tile, de / 256, false).total : mplan<32>(0, tile, de / 256, false).total;
 }
 constexpr uint32_t SMEM_LIMIT = 227 * 1024;
 
 bool mma_gateup_supported(int dt, int D, int de) {
     return (dt == DT_Q4_K || dt == DT_Q5_K) && D % 256 == 0 && D / 256 <= MAXNB && de % MR == 0 &&
-           gateup_smem(dt, D) <= SMEM_LIMIT;
+           gateup_smem(dt, D, 8) <= SMEM_LIMIT;
 }
 bool mma_down_supported(int dt, int D, int de) {
     return (dt == DT_Q4_K || dt == DT_Q5_K || dt == DT_Q6_K) && de % 256 == 0 && de / 256 <= MAXNB && D % MR == 0 &&
-           down_smem(dt, de) <= SMEM_LIMIT;
+           down_smem(dt, de, 8) <= SMEM_LIMIT;
 }
 
 template <typename F>
@@ -619,14 +619,23 @@ static int grid_for(int64_t max_items, int per_sm) {
 }
 
 int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8_t *x, size_t xstride, int xdiv,
-                      int D, int de, int E, int64_t max_items, float *gout, float *uout, uint32_t *err,
+                      int D, int de, int E, int64_t max_items, bool wide, float *gout, float *uout, uint32_t *err,
                       cudaStream_t st) {
     if (!mma_gateup_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core gate/up: dtype %d D %d", dt, D);
-    const uint32_t smem = gateup_smem(dt, D);
+    int tn = pass_tokens(wide);
+    if (gateup_smem(dt, D, tn) > SMEM_LIMIT) tn = 8;
+    const uint32_t smem = gateup_smem(dt, D, tn);
     const int grid = grid_for(2 * max_items, smem <= 113 * 1024 ? 2 : 1);
-    const bool three = gateup_stages(D) == 3;
-    auto fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3> : k_mgu<DT_Q4_K, 2>)
-                            : (three ? k_mgu<DT_Q5_K, 3> : k_mgu<DT_Q5_K, 2>);
+    const bool three = gateup_stages(D, tn) == 3;
+    using Fn = void (*)(const Slot *, const int32_t *, const uint8_t *, size_t, int, int, int, int, float *, float *,
+                        uint32_t *);
+    Fn fn;
+    if (tn == 8)
+        fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3, 8> : k_mgu<DT_Q4_K, 2, 8>)
+                           : (three ? k_mgu<DT_Q5_K, 3, 8> : k_mgu<DT_Q5_K, 2, 8>);
+    else
+        fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3, 32> : k_mgu<DT_Q4_K, 2, 32>)
+                           : (three ? k_mgu<DT_Q5_K, 3, 32> : k_mgu<DT_Q5_K, 2, 32>);
     int rc = opt_in(fn, smem);
     if (rc) return rc;
     fn<<<grid, GU_THREADS, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, gout, uout, err);
@@ -635,11 +644,18 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
 }
 
 int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t *hq, int D, int de, int E,
-                    int64_t max_items, float *eo, uint32_t *err, cudaStream_t st) {
+                    int64_t max_items, bool wide, float *eo, uint32_t *err, cudaStream_t st) {
     if (!mma_down_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core down: dtype %d de %d", dt, de);
-    const uint32_t smem = down_smem(dt, de);
+    int tn = pass_tokens(wide);
+    if (down_smem(dt, de, tn) > SMEM_LIMIT) tn = 8;
+    const uint32_t smem = down_smem(dt, de, tn);
     const int grid = grid_for(max_items, smem <= 113 * 1024 ? 2 : 1);
-    auto fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K> : dt == DT_Q5_K ? k_mdown<DT_Q5_K> : k_mdown<DT_Q6_K>;
+    using Fn = void (*)(const Slot *, const int32_t *, const uint8_t *, int, int, int, float *, uint32_t *);
+    Fn fn;
+    if (tn == 8)
+        fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K, 8> : dt == DT_Q5_K ? k_mdown<DT_Q5_K, 8> : k_mdown<DT_Q6_K, 8>;
+    else
+        fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K, 32> : dt == DT_Q5_K ? k_mdown<DT_Q5_K, 32> : k_mdown<DT_Q6_K, 32>;
     int rc = opt_in(fn, smem);
     if (rc) return rc;
     fn<<<grid, DN_THREADS, smem, st>>>(slots, grp, hq, D, de, E, eo, err);

@@ -24,10 +24,12 @@ bool mma_down_supported(int dt, int D, int de);
 // err: device word; bit 0 is set when a tensor-core wait expired. The
 // launchers queue one kernel each and leave launch counting to the caller.
 int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8_t *x, size_t xstride, int xdiv,
-                      int D, int de, int E, int64_t max_items, float *gout, float *uout, uint32_t *err,
+                      int D, int de, int E, int64_t max_items, bool wide, float *gout, float *uout, uint32_t *err,
                       cudaStream_t st);
 // hq: quantised h per pair (swizzled Q8_K vectors of de); eo[q][D].
+// wide: the experts average many tokens (prefill) - 32 tokens per pass
+// instead of 8.
 int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t *hq, int D, int de, int E,
-                    int64_t max_items, float *eo, uint32_t *err, cudaStream_t st);
+                    int64_t max_items, bool wide, float *eo, uint32_t *err, cudaStream_t st);
 
 }  // namespace tlmg
