@@ -128,6 +128,16 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, int (&v)[64]) {
 
 constexpr uint32_t WAIT_LIMIT = 1u << 20;   // polls of a completion barrier before giving up
 
+// 32 consecutive columns (load and wait in one statement, as tmem_ld64)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Row unpack: one weight block of this thread's row -> 16 chunks of 16 int8
 // codes (chunk c = elements 16c .. 16c + 15) at A + c * 128 + (row % 8) * 16
@@ -311,12 +321,29 @@ __device__ __forceinline__ void issue_block(uint8_t *sm, const MPlan &P, uint32_
     umma_commit(reinterpret_cast<uint64_t *>(sm + P.bar));
 }
 
-// is[t] += scale_s * dot_s[t] over sub-blocks s0 .. s0 + ns - 1 (ns a
-// multiple of 64 / TN) of one matrix whose sub-block s accumulator starts at
-// column col0 + s * TN.
+// is[t] += scale_s * dot_s[t] over sub-blocks s0 .. s0 + ns - 1 of one
+// matrix whose sub-block s accumulator starts at column col0 + s * TN
+// (ns * TN a multiple of 32).
+template <int DT, int TN>
+__device__ __forceinline__ int scale_of(const RowBlk &rb, int s) {
+    if constexpr (DT == DT_Q6_K) return (int)(int8_t)byte_of(rb.s[s >> 2], s & 3);
+    else return (int)byte_of(rb.s[s >> 2], s & 3);
+}
 template <int DT, int TN>
 __device__ __forceinline__ void add_scaled(uint32_t lane_base, uint32_t col0, int s0, int ns, const RowBlk &rb,
                                            int (&is)[TN]) {
+    if (ns * TN == 32) {
+        constexpr int SPL = 32 / TN;
+        int v[32];
+        tmem_ld32(lane_base + col0 + (uint32_t)(s0 * TN), v);
+#pragma unroll
+        for (int j = 0; j < SPL; j++) {
+            const int sc = scale_of<DT, TN>(rb, s0 + j);
+#pragma unroll
+            for (int t = 0; t < TN; t++) is[t] += sc * v[TN * j + t];
+        }
+        return;
+    }
     constexpr int SPL = 64 / TN;   // sub-blocks per 64-column load
 #pragma unroll 1
     for (int g = 0; g < ns; g += SPL) {
@@ -324,25 +351,24 @@ __device__ __forceinline__ void add_scaled(uint32_t lane_base, uint32_t col0, in
         tmem_ld64(lane_base + col0 + (uint32_t)((s0 + g) * TN), v);
 #pragma unroll
         for (int j = 0; j < SPL; j++) {
-            const int s = s0 + g + j;
-            int sc;
-            if constexpr (DT == DT_Q6_K) sc = (int)(int8_t)byte_of(rb.s[s >> 2], s & 3);
-            else sc = (int)byte_of(rb.s[s >> 2], s & 3);
+            const int sc = scale_of<DT, TN>(rb, s0 + g + j);
 #pragma unroll
             for (int t = 0; t < TN; t++) is[t] += sc * v[TN * j + t];
         }
     }
 }
 
-// The block's chain step for every token of the pass: acc[t] =
-// fmaf(d_w d_a, is, acc) (and, Q4_K / Q5_K, fmaf(-dmin_w d_a, ms, acc)).
-template <int DT, int TN>
-__device__ __forceinline__ void chain_tokens(const uint8_t *sm, const MPlan &P, int b, int nb, const RowBlk &rb,
-                                             const int (&is)[TN], float (&acc)[TN], int nt) {
+// The chain step of block b for tokens t0 .. t0 + NTOK - 1 of the pass
+// (acc[i] belongs to token t0 + i): acc = fmaf(d_w d_a, is, acc) and, for
+// Q4_K / Q5_K, fmaf(-dmin_w d_a, ms, acc).
+template <int DT, int NTOK>
+__device__ __forceinline__ void chain_range(const uint8_t *sm, const MPlan &P, int b, int nb, const RowBlk &rb,
+                                            const int (&is)[NTOK], float (&acc)[NTOK], int t0, int nt) {
     const float *dx = reinterpret_cast<const float *>(sm + P.dx);
     const int *bs = reinterpret_cast<const int *>(sm + P.bs);
 #pragma unroll
-    for (int t = 0; t < TN; t++) {
+    for (int i = 0; i < NTOK; i++) {
+        const int t = t0 + i;
         if (t < nt) {
             const float d = dx[t * nb + b];
             int ms = 0;
@@ -354,9 +380,16 @@ __device__ __forceinline__ void chain_tokens(const uint8_t *sm, const MPlan &P, 
                      (int)byte_of(rb.s[3], 0) * b1.x + (int)byte_of(rb.s[3], 1) * b1.y +
                      (int)byte_of(rb.s[3], 2) * b1.z + (int)byte_of(rb.s[3], 3) * b1.w;
             }
-            acc[t] = chain<DT>(acc[t], __fmul_rn(rb.d, d), is[t], __fmul_rn(rb.dmin, d), ms);
+            acc[i] = chain<DT>(acc[i], __fmul_rn(rb.d, d), is[i], __fmul_rn(rb.dmin, d), ms);
         }
     }
+}
+
+// The block's chain step for every token of the pass.
+template <int DT, int TN>
+__device__ __forceinline__ void chain_tokens(const uint8_t *sm, const MPlan &P, int b, int nb, const RowBlk &rb,
+                                             const int (&is)[TN], float (&acc)[TN], int nt) {
+    chain_range<DT, TN>(sm, P, b, nb, rb, is, acc, 0, nt);
 }
 
 __device__ __forceinline__ void report(uint32_t *err, bool ok) {
@@ -364,35 +397,41 @@ __device__ __forceinline__ void report(uint32_t *err, bool ok) {
 }
 
 // gate or up: K = D. Work item = (active expert, 128-row tile, matrix);
-// thread = weight row = TMEM lane; raw stages hold one block column
-// [NS][MR][BB] of the tile. out[m][pair][row] = the row's dot (m = 0 gate,
-// 1 up). Small enough for two CTAs per SM, which overlap each other's
-// unpack, MMA wait and epilogue.
-constexpr int GU_THREADS = MR;
+// two threads per weight row (warps 0-3 and 4-7; TMEM lane = row): each
+// unpacks and sums half of the block's sub-blocks, they swap the partial
+// integer sums of each other's tokens and each runs the chains of half of
+// the pass's tokens. Raw stages hold one block column [NS][MR][BB] of the
+// tile. out[m][pair][row] = the row's dot (m = 0 gate, 1 up). Small enough
+// for two CTAs per SM at 8 tokens per pass.
+constexpr int GU_THREADS = 2 * MR;
 template <int DT, int NS, int TN>
 __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? 2 : 1)
     k_mgu(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
           size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ gout, float *__restrict__ uout,
           uint32_t *err) {
+    constexpr int TH = TN / 2;   // tokens per thread
     extern __shared__ __align__(1024) uint8_t sm[];
     constexpr int BB = KQ<DT>::BB, CPB = BB / 16;
     static_assert(BB % 16 == 0, "gate/up blocks must be 16-byte multiples");
     const int nb = D / 256;
-    const MPlan P = mplan<TN>(1, (uint32_t)NS * MR * BB, nb, false);
+    const MPlan P = mplan<TN>(1, (uint32_t)NS * MR * BB, nb, true);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
-    const int r = threadIdx.x, warp = r >> 5;
-    if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
+    const int tid = threadIdx.x, warp = tid >> 5, half = tid / MR, r = tid & (MR - 1);
+    if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
     if (warp == 0) tmem_alloc(tmem_slot, 8 * TN);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * warp) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
     uint32_t phase = 0;
     bool ok = true;
     const int tiles = de / MR, na = grp[2 * E + 1];
     const size_t rb = (size_t)nb * BB;
     const int32_t *pairs = grp + 2 * E + 2;
+    int *xmine = reinterpret_cast<int *>(sm + P.xch) + (half * MR + r) * TH;         // written by this thread
+    const int *xother = reinterpret_cast<const int *>(sm + P.xch) + ((1 - half) * MR + r) * TH;
+    const int t0 = half * TH;   // this thread's tokens t0 .. t0 + TH - 1
     bool first = true;
     uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
     for (int item = blockIdx.x; item < na * tiles * 2 && ok; item += gridDim.x) {
@@ -402,7 +441,7 @@ __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? 2 : 1)
         auto issue = [&](int b) {
             if (b < nb) {
                 uint8_t *st = sm + P.raw + (b % NS) * MR * BB;
-                for (int i = r; i < MR * CPB; i += GU_THREADS) {
+                for (int i = tid; i < MR * CPB; i += GU_THREADS) {
                     const int rr = i / CPB, c = i - rr * CPB;
                     cp16(st + rr * BB + 16 * c, w + rr * rb + (size_t)b * BB + 16 * c);
                 }
@@ -415,33 +454,38 @@ __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? 2 : 1)
             first = false;
 #pragma unroll
             for (int b = 0; b < NS - 1; b++) issue(b);
-            float acc[TN];
+            float acc[TH];
 #pragma unroll
-            for (int t = 0; t < TN; t++) acc[t] = 0.0f;
+            for (int i = 0; i < TH; i++) acc[i] = 0.0f;
             for (int b = 0; b < nb; b++) {
                 cp_wait<NS - 2>();
-                __syncthreads();   // block b staged; the previous block's tile and accumulators are consumed
+                __syncthreads();   // block b staged; the previous block's tile, accumulators and swaps are consumed
                 issue(b + NS - 1);
-                const RowBlk rk = unpack_row<DT>(sm + P.raw + (b % NS) * MR * BB + r * BB, Arow);
+                const RowBlk rk = unpack_row<DT>(sm + P.raw + (b % NS) * MR * BB + r * BB, Arow, half);
                 fence_async_smem();
                 __syncthreads();
-                if (r == 0) issue_block<DT, 1, TN>(sm, P, tmem, b);
+                if (tid == 0) issue_block<DT, 1, TN>(sm, P, tmem, b);
                 const bool got = mbar_wait(reinterpret_cast<uint64_t *>(sm + P.bar), phase, WAIT_LIMIT);
                 phase ^= 1u;
                 tc_fence_after();
                 int is[TN];
 #pragma unroll
                 for (int t = 0; t < TN; t++) is[t] = 0;
-                add_scaled<DT, TN>(lane_base, 0u, 0, 8, rk, is);
-                chain_tokens<DT, TN>(sm, P, b, nb, rk, is, acc, nt);
+                add_scaled<DT, TN>(lane_base, 0u, 4 * half, 4, rk, is);   // sub-blocks 4 half .. 4 half + 3
+#pragma unroll
+                for (int i = 0; i < TH; i++) xmine[i] = half ? is[i] : is[TH + i];   // the other thread's tokens
                 tc_fence_before();
-                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA
+                if (__syncthreads_or(!got)) ok = false;   // uniform across the CTA; publishes the swaps
                 if (!ok) break;
+                int own[TH];
+#pragma unroll
+                for (int i = 0; i < TH; i++) own[i] = (half ? is[TH + i] : is[i]) + xother[i];   // exact: both halves' sums
+                chain_range<DT, TH>(sm, P, b, nb, rk, own, acc, t0, nt);
             }
             cp_wait<0>();
 #pragma unroll
-            for (int t = 0; t < TN; t++)
-                if (t < nt) out[(size_t)pairs[c0 + t] * de + tile * MR + r] = acc[t];
+            for (int i = 0; i < TH; i++)
+                if (t0 + i < nt) out[(size_t)pairs[c0 + t0 + i] * de + tile * MR + r] = acc[i];
             __syncthreads();   // staged tokens are rewritten next
         }
     }
@@ -583,7 +627,7 @@ static int gateup_stages(int D, int tn) { return D <= 2048 || tn <= 8 ? 3 : 2; }
 
 static uint32_t gateup_smem(int dt, int D, int tn) {
     const uint32_t raw = (uint32_t)gateup_stages(D, tn) * MR * dt_block_bytes(dt);
-    return tn <= 8 ? mplan<8>(1, raw, D / 256, false).total : mplan<32>(1, raw, D / 256, false).total;
+    return tn <= 8 ? mplan<8>(1, raw, D / 256, true).total : mplan<32>(1, raw, D / 256, true).total;
 }
 static uint32_t down_smem(int dt, int de, int tn) {
     const uint32_t tile = align_up((uint32_t)MR * (de / 256) * dt_block_bytes(dt), 1024u) + MR * 128u;
