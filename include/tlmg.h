@@ -124,6 +124,32 @@ void tlmg_close(tlmg_ctx *ctx);
 int tlmg_set_expert(tlmg_ctx *ctx, int layer, int expert, const int32_t dt[3],
                     const void *payload, size_t payload_len, const uint64_t item_off[3]);
 
+/* ---- HBM expert-slot cache (reference expert store + lookahead,
+ * src/lib/tlm_store.c:586-719, src/lib/tlm_model.c:844-877). For models
+ * whose experts do not all fit in HBM: experts stay in (pinned) host
+ * memory and a pool of n_slots HBM slots of slot_bytes each holds the
+ * recently used ones. A layer whose experts are registered with
+ * tlmg_set_expert_host is served through the cache: each call routes on
+ * the GPU, brings the routed ids to the host (one stream synchronisation),
+ * copies the missing experts host -> HBM on a side stream and runs the
+ * expert kernels after exactly those copies; results are bit-identical to
+ * HBM-resident experts. Eviction: least recently acquired slot not needed
+ * by the same call (a hit is never evicted by a miss of the same call).
+ * Call tlmg_cache_enable once, before registering experts. */
+int tlmg_cache_enable(tlmg_ctx *ctx, int n_slots, size_t slot_bytes);
+/* Register one routed expert of `layer` in host memory (no copy now). The
+ * payload must stay valid (and, for asynchronous copies, pinned) while the
+ * context lives. Same arguments and checks as tlmg_set_expert. A layer is
+ * either fully HBM-resident (tlmg_set_expert) or cached. */
+int tlmg_set_expert_host(tlmg_ctx *ctx, int layer, int expert, const int32_t dt[3],
+                         const void *payload, size_t payload_len, const uint64_t item_off[3]);
+/* Start copies of the listed experts of `layer` (host ids) into free or
+ * least recently used slots without waiting (router lookahead). Call after
+ * the current step's launches are queued. No-op for resident layers. */
+int tlmg_cache_prefetch(tlmg_ctx *ctx, int layer, const int32_t *ids, int k);
+/* out[6] = hits, misses, prefetched, prefetch hits, evictions, bytes copied. */
+int tlmg_cache_stats(tlmg_ctx *ctx, int64_t out[6]);
+
 /* Resident per-layer tensors of the MoE block (DENSE packet,
  * src/lib/tlm_model.c:940-1055): ffn_norm f32[D]; router [E x D] of
  * router_dt (tlmc keeps it f32); router_bias f32[E] or NULL; mask u8[E]

@@ -76,6 +76,10 @@ _SIGS = {
     "tlmg_set_stream": (_I, [_P, _P]),
     "tlmg_set_fused": (_I, [_P, _I]),
     "tlmg_set_batch_kernels": (_I, [_P, _I]),
+    "tlmg_cache_enable": (_I, [_P, _I, _SZ]),
+    "tlmg_set_expert_host": (_I, [_P, _I, _I, _P, _P, _SZ, _P]),
+    "tlmg_cache_prefetch": (_I, [_P, _I, _P, _I]),
+    "tlmg_cache_stats": (_I, [_P, _P]),
     "tlmg_check": (_I, [_P]),
     "tlmg_trace": (_I, [_P, _I, _P, _I]),
     "tlmg_profile": (_I, [_P, _I]),

@@ -1,0 +1,211 @@
+// tlmg_cache.cu - HBM expert-slot cache with side-stream refill.
+//
+// Policy (reference tlm_store_acquire, src/lib/tlm_store.c:586-640): every
+// hit of an acquisition is referenced before any miss picks a victim, so a
+// miss never evicts an expert the same step needs; victims are free slots
+// first, then the least recently acquired slot not pinned by the current
+// acquisition; a repeated id is served by the slot loaded earlier in the
+// same pass. Prefetch (reference lookahead + tlm_store_prefetch,
+// src/lib/tlm_model.c:844-877) starts copies without pinning or waiting.
+//
+// Ordering on the GPU: a load into a slot waits (on the copy stream) for the
+// event recorded after the slot's last use on the compute stream; the
+// compute stream waits for the event recorded after the load. Copies from
+// pinned host memory run asynchronously to both streams.
+#include <algorithm>
+
+#include "tlmg_cache.cuh"
+#include "tlmg_internal.h"
+
+namespace tlmg {
+
+static size_t padded(size_t b) { return (b + 16 + 255) & ~size_t(255); }
+
+void cache_release(ExpertCache &c) {
+    if (c.copy_st) cudaStreamSynchronize(c.copy_st);
+    for (cudaEvent_t e : c.loaded)
+        if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : c.used)
+        if (e) cudaEventDestroy(e);
+    if (c.pool) cudaFree(c.pool);
+    if (c.copy_st) cudaStreamDestroy(c.copy_st);
+    c = ExpertCache{};
+}
+
+int cache_init(ExpertCache &c, int n_layers, int E, int n_slots, size_t slot_bytes) {
+    cache_release(c);
+    if (n_layers <= 0 || E <= 0 || n_slots <= 0 || slot_bytes == 0)
+        return set_error(TLMG_EINVAL, "cache: %d layers, %d experts, %d slots of %zu bytes", n_layers, E, n_slots,
+                         slot_bytes);
+    c.slot_bytes = (slot_bytes + 255) & ~size_t(255);
+    if (cudaMalloc(&c.pool, c.slot_bytes * (size_t)n_slots) != cudaSuccess) {
+        cudaGetLastError();
+        c = ExpertCache{};
+        return set_error(TLMG_ENOMEM, "cache: %d slots of %zu bytes", n_slots, c.slot_bytes);
+    }
+    if (cudaStreamCreateWithFlags(&c.copy_st, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        cache_release(c);
+        return set_error(TLMG_EIO, "cache: copy stream creation failed");
+    }
+    c.n_layers = n_layers;
+    c.E = E;
+    c.n_slots = n_slots;
+    c.src.assign((size_t)n_layers * E, CacheSrc{});
+    c.where.assign((size_t)n_layers * E, -1);
+    c.owner.assign(n_slots, -1);
+    c.stamp.assign(n_slots, 0);
+    c.pinned.assign(n_slots, 0);
+    c.fresh.assign(n_slots, 0);
+    c.used_valid.assign(n_slots, 0);
+    c.loaded.assign(n_slots, nullptr);
+    c.used.assign(n_slots, nullptr);
+    for (int s = 0; s < n_slots; s++)
+        if (cudaEventCreateWithFlags(&c.loaded[s], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c.used[s], cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            cache_release(c);
+            return set_error(TLMG_EIO, "cache: event creation failed");
+        }
+    c.on = true;
+    return TLMG_OK;
+}
+
+int cache_register(ExpertCache &c, int layer, int e, const int32_t dt[3], const void *host, const uint64_t off[3],
+                   const size_t bytes[3]) {
+    if (!c.on) return set_error(TLMG_EINVAL, "cache: not enabled (tlmg_cache_enable)");
+    const size_t need = padded(bytes[0]) + padded(bytes[1]) + padded(bytes[2]);
+    if (need > c.slot_bytes)
+        return set_error(TLMG_ERANGE, "cache: expert %d:%d needs %zu bytes, slots hold %zu", layer, e, need,
+                         c.slot_bytes);
+    const int key = layer * c.E + e;
+    if (c.where[key] >= 0) {   // re-registration: drop the resident copy
+        const int s = c.where[key];
+        c.owner[s] = -1;
+        c.where[key] = -1;
+    }
+    CacheSrc &d = c.src[key];
+    d.host = static_cast<const uint8_t *>(host);
+    for (int m = 0; m < 3; m++) {
+        d.off[m] = off[m];
+        d.bytes[m] = bytes[m];
+        d.dt[m] = dt[m];
+    }
+    d.ok = true;
+    return TLMG_OK;
+}
+
+bool cache_has(const ExpertCache &c, int layer) {
+    if (!c.on || layer < 0 || layer >= c.n_layers) return false;
+    for (int e = 0; e < c.E; e++)
+        if (c.src[(size_t)layer * c.E + e].ok) return true;
+    return false;
+}
+
+static int pick_victim(const ExpertCache &c, uint64_t now) {
+    int best = -1;
+    for (int s = 0; s < c.n_slots; s++) {
+        if (c.owner[s] < 0) return s;
+        if (c.pinned[s] == now) continue;
+        if (best < 0 || c.stamp[s] < c.stamp[best]) best = s;
+    }
+    return best;
+}
+
+static Slot slot_view(const ExpertCache &c, int s, const CacheSrc &d) {
+    Slot v{};
+    uint8_t *base = c.pool + (size_t)s * c.slot_bytes;
+    size_t o = 0;
+    for (int m = 0; m < 3; m++) {
+        v.m[m] = base + o;
+        v.dt[m] = d.dt[m];
+        o += padded(d.bytes[m]);
+    }
+    v.ok = 1;
+    return v;
+}
+
+int cache_acquire(ExpertCache &c, int layer, const int32_t *ids, int k, bool prefetch, cudaStream_t st, Slot *out) {
+    if (!c.on) return set_error(TLMG_EINVAL, "cache: not enabled");
+    if (layer < 0 || layer >= c.n_layers) return set_error(TLMG_ERANGE, "cache: layer %d", layer);
+    const uint64_t now = ++c.clock;
+    int rc = TLMG_OK;
+    // pass 1: hits
+    for (int i = 0; i < k; i++) {
+        if (ids[i] < 0 || ids[i] >= c.E || !c.src[(size_t)layer * c.E + ids[i]].ok) {
+            if (rc == TLMG_OK)
+                rc = set_error(TLMG_ENOTFOUND, "cache: layer %d expert %d is not registered", layer, ids[i]);
+            continue;
+        }
+        const int s = c.where[(size_t)layer * c.E + ids[i]];
+        if (s < 0) continue;
+        c.stamp[s] = now;
+        if (!prefetch) {
+            c.pinned[s] = now;
+            c.hits++;
+            if (c.fresh[s]) {
+                c.prefetch_hits++;
+                c.fresh[s] = 0;
+            }
+        }
+    }
+    if (rc) return rc;
+    // pass 2: misses
+    for (int i = 0; i < k; i++) {
+        const int key = layer * c.E + ids[i];
+        if (c.where[key] >= 0) {   // a repeated id loaded earlier in this pass
+            if (!prefetch) c.pinned[c.where[key]] = now;
+            continue;
+        }
+        const int v = pick_victim(c, now);
+        if (v < 0) {
+            if (prefetch) break;
+            return set_error(TLMG_EBUSY, "cache: all %d slots are held by this step; it needs at least top_k slots",
+                             c.n_slots);
+        }
+        if (c.owner[v] >= 0) {
+            c.where[c.owner[v]] = -1;
+            c.evictions++;
+        }
+        if (c.used_valid[v] && cudaStreamWaitEvent(c.copy_st, c.used[v], 0) != cudaSuccess)
+            return cuda_fail(cudaGetLastError(), "cache: copy stream wait");
+        const CacheSrc &d = c.src[key];
+        const Slot view = slot_view(c, v, d);
+        for (int m = 0; m < 3; m++) {
+            cudaError_t e = cudaMemcpyAsync(const_cast<uint8_t *>(view.m[m]), d.host + d.off[m], d.bytes[m],
+                                            cudaMemcpyHostToDevice, c.copy_st);
+            if (e != cudaSuccess) return cuda_fail(e, "cache: expert copy");
+            c.bytes_loaded += (int64_t)d.bytes[m];
+        }
+        if (cudaEventRecord(c.loaded[v], c.copy_st) != cudaSuccess)
+            return cuda_fail(cudaGetLastError(), "cache: event record");
+        c.owner[v] = key;
+        c.where[key] = v;
+        c.stamp[v] = now;
+        c.pinned[v] = prefetch ? 0 : now;
+        c.fresh[v] = prefetch ? 1 : 0;
+        if (prefetch) c.prefetched++;
+        else c.misses++;
+    }
+    if (prefetch) return TLMG_OK;
+    for (int i = 0; i < k; i++) {
+        const int key = layer * c.E + ids[i];
+        const int s = c.where[key];
+        if (cudaStreamWaitEvent(st, c.loaded[s], 0) != cudaSuccess)
+            return cuda_fail(cudaGetLastError(), "cache: compute stream wait");
+        if (out) out[i] = slot_view(c, s, c.src[key]);
+    }
+    return TLMG_OK;
+}
+
+int cache_mark_used(ExpertCache &c, int layer, const int32_t *ids, int k, cudaStream_t st) {
+    for (int i = 0; i < k; i++) {
+        const int s = c.where[(size_t)layer * c.E + ids[i]];
+        if (s < 0) continue;
+        if (cudaEventRecord(c.used[s], st) != cudaSuccess) return cuda_fail(cudaGetLastError(), "cache: event record");
+        c.used_valid[s] = 1;
+    }
+    return TLMG_OK;
+}
+
+}  // namespace tlmg

@@ -10,6 +10,7 @@
 
 #include "tlmg_dev.cuh"
 #include "tlmg_batch.cuh"
+#include "tlmg_cache.cuh"
 #include "tlmg_fused.cuh"
 #include "tlmg_internal.h"
 
@@ -61,6 +62,7 @@ struct Layer {
     const void *fused_plan = nullptr;   // the persistent kernel's plan when it can serve this layer
     int dt_gu = -1, dt_dn = -1;         // uniform gate/up and down dtypes of the layer (or -1)
     bool has_shared = false;
+    bool cached = false;                // experts registered in host memory, served by the HBM slot cache
     int sh_dt[3] = { 0, 0, 0 };
     void *sh_w[3] = { nullptr, nullptr, nullptr };
     float *sh_gate_inp = nullptr;
@@ -99,6 +101,9 @@ struct tlmg_ctx {
     int64_t launch0 = 0;
     FusedScratch fused;
     BatchScratch batch;            // batched-decode scratch (tlmg_expert_ffn_batch)
+    ExpertCache cache;             // HBM expert-slot cache (tlmg_cache_enable)
+    Slot *pin_slots = nullptr;     // pinned [n_layers][E] slot-table mirror of cached layers
+    int32_t *pin_ids = nullptr;    // pinned [64] routed ids of a cached layer
     bool fused_on = true;
     uint64_t *trace = nullptr;     // device [nsm][FUSED_TRACE_POINTS] when tracing
     Slot *slots_all = nullptr;     // device [n_layers][E]: every layer's slot table, contiguous
@@ -163,7 +168,7 @@ static int sync_slots(tlmg_ctx *c, Layer &Ly) {
     uniform = uniform && dgu >= 0;
     Ly.dt_gu = uniform ? dgu : -1;
     Ly.dt_dn = uniform ? ddn : -1;
-    Ly.fused_plan = uniform ? fused_plan(c->fused, c->g, dgu, ddn) : nullptr;
+    Ly.fused_plan = uniform && !Ly.cached ? fused_plan(c->fused, c->g, dgu, ddn) : nullptr;
     return TLMG_OK;
 }
 
@@ -339,7 +344,7 @@ static int launched(const char *what) {
 // The persistent kernel runs when enabled, when it has a plan for the
 // layer's dtypes and when x is 16-byte aligned (it reads x as float4).
 static bool use_fused_path(const tlmg_ctx *c, const Layer &Ly, const float *x) {
-    return c->fused_on && Ly.fused_plan && x && ((uintptr_t)x & 15u) == 0;
+    return c->fused_on && Ly.fused_plan && !Ly.cached && x && ((uintptr_t)x & 15u) == 0;
 }
 
 static cudaEvent_t prof_event(tlmg_ctx *c) {
@@ -414,6 +419,40 @@ static FusedArgs fused_args(tlmg_ctx *c, const Layer &Ly, int layer, int n_tok) 
     return a;
 }
 
+// Cached layer: the routed ids come to the host (one stream synchronisation),
+// the cache makes those experts resident (side-stream copies that the
+// compute stream waits for) and the layer's slot table is refreshed on the
+// compute stream from a pinned mirror.
+static int cache_route_acquire(tlmg_ctx *c, int layer) {
+    const int k = c->g.top_k, E = c->g.n_experts;
+    Layer &Ly = c->L[layer];
+    if (!c->pin_ids && cudaMallocHost(&c->pin_ids, 4 * 64) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(TLMG_ENOMEM, "cache: pinned id buffer");
+    }
+    if (!c->pin_slots) {
+        if (cudaMallocHost(&c->pin_slots, sizeof(Slot) * (size_t)c->g.n_layers * E) != cudaSuccess) {
+            cudaGetLastError();
+            c->pin_slots = nullptr;
+            return set_error(TLMG_ENOMEM, "cache: pinned slot table");
+        }
+        memset(c->pin_slots, 0, sizeof(Slot) * (size_t)c->g.n_layers * E);
+    }
+    cudaError_t e = cudaMemcpyAsync(c->pin_ids, c->ids, 4 * (size_t)k, cudaMemcpyDeviceToHost, c->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);   // also ends the previous table upload
+    if (e != cudaSuccess) return cuda_fail(e, "cache: routed ids");
+    Slot got[64];
+    int rc = cache_acquire(c->cache, layer, c->pin_ids, k, false, c->st, got);
+    if (rc) return rc;
+    Slot *tab = c->pin_slots + (size_t)layer * E;
+    for (int r = 0; r < k; r++) {
+        Ly.h_slots[c->pin_ids[r]] = got[r];
+        tab[c->pin_ids[r]] = got[r];
+    }
+    e = cudaMemcpyAsync(Ly.d_slots, tab, sizeof(Slot) * (size_t)E, cudaMemcpyHostToDevice, c->st);
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "cache: slot table upload");
+}
+
 // Routed experts for one token on the device: logits -> ids/w -> ffn (and
 // h += ffn when h != NULL). Inputs already quantised in xq8k / xq80.
 static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, float *h, const float *s_out,
@@ -441,6 +480,7 @@ static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, 
                           c->w, c->st);
     prof_mark(c, 2, false);
     if (rc) return rc;
+    if (Ly.cached && (rc = cache_route_acquire(c, layer))) return rc;
     (void)x;
     int k = g.top_k, D = g.d_model, de = g.d_expert;
     unsigned grid = (unsigned)std::min<int64_t>(((int64_t)k * de + FFN_WARPS - 1) / FFN_WARPS, 148 * 8);
@@ -456,10 +496,17 @@ static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, 
     k_ffn_down<<<(unsigned)std::min(148 * 8, (D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, c->st>>>(
         Ly.d_slots, c->ids, c->w, k, D, de, c->hq, c->hq_stride, s_out, sgate, ffn, h);
     prof_mark(c, 1, false);
-    return launched("ffn down");
+    if ((rc = launched("ffn down"))) return rc;
+    return Ly.cached ? cache_mark_used(c->cache, layer, c->pin_ids, k, c->st) : TLMG_OK;
 }
 
 static bool layer_ready(tlmg_ctx *c, Layer &Ly) {
+    if (Ly.cached) {   // every expert registered (resident or in host memory)
+        const int l = (int)(&Ly - c->L.data());
+        for (int e = 0; e < c->g.n_experts; e++)
+            if (!c->cache.src[(size_t)l * c->g.n_experts + e].ok) return false;
+        return true;
+    }
     for (const Slot &s : Ly.h_slots)
         if (!s.ok) return false;
     return !Ly.h_slots.empty();
@@ -592,6 +639,9 @@ void tlmg_close(tlmg_ctx *c) {
     if (c->own_st) cudaStreamSynchronize(c->own_st);
     fused_release(c->fused);
     batch_release(c->batch);
+    cache_release(c->cache);
+    if (c->pin_slots) cudaFreeHost(c->pin_slots);
+    if (c->pin_ids) cudaFreeHost(c->pin_ids);
     c->arena.release();
     for (void *p : c->owned) cudaFree(p);
     if (c->pin) cudaFreeHost(c->pin);
@@ -721,6 +771,7 @@ int tlmg_set_expert(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], con
                              expert, m, (unsigned long long)item_off[m], bytes[m], payload_len);
     }
     Layer &Ly = c->L[layer];
+    if (Ly.cached) return set_error(TLMG_EBUSY, "layer %d is served by the slot cache (tlmg_set_expert_host)", layer);
     Slot &s = Ly.h_slots[expert];
     size_t pad[3];
     for (int m = 0; m < 3; m++) pad[m] = (bytes[m] + 16 + 255) & ~size_t(255);
@@ -743,6 +794,72 @@ int tlmg_set_expert(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], con
     }
     s.ok = 1;
     Ly.slots_dirty = true;
+    return TLMG_OK;
+}
+
+int tlmg_cache_enable(tlmg_ctx *c, int n_slots, size_t slot_bytes) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    if (c->g.n_experts <= 0) return set_error(TLMG_EINVAL, "cache: geometry has no routed experts");
+    if (n_slots < c->g.top_k)
+        return set_error(TLMG_EINVAL, "cache: %d slots cannot hold one token's %d experts", n_slots, c->g.top_k);
+    cudaSetDevice(c->device);
+    if (c->st) cudaStreamSynchronize(c->st);
+    for (Layer &Ly : c->L)
+        if (Ly.cached) return set_error(TLMG_EBUSY, "cache: already holds registered experts");
+    return cache_init(c->cache, c->g.n_layers, c->g.n_experts, n_slots, slot_bytes);
+}
+
+int tlmg_set_expert_host(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], const void *payload,
+                         size_t payload_len, const uint64_t item_off[3]) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (expert < 0 || expert >= c->g.n_experts)
+        return set_error(TLMG_ERANGE, "expert %d out of range [0, %d)", expert, c->g.n_experts);
+    if (!dt || !payload || !item_off) return set_error(TLMG_EINVAL, "set_expert_host: NULL argument");
+    if (!c->cache.on) return set_error(TLMG_EINVAL, "set_expert_host: call tlmg_cache_enable first");
+    cudaSetDevice(c->device);
+    const int D = c->g.d_model, de = c->g.d_expert;
+    size_t bytes[3];
+    for (int m = 0; m < 3; m++) {
+        int q = dt_block(dt[m]);
+        if (q <= 1 || (m < 2 ? D : de) % q)
+            return set_error(TLMG_EUNSUP, "set_expert_host %d:%d: matrix %d dtype %d is not a block-quantised type",
+                             layer, expert, m, dt[m]);
+        bytes[m] = m < 2 ? (size_t)de * tlmg_row_bytes(dt[m], D) : (size_t)D * tlmg_row_bytes(dt[m], de);
+        if (item_off[m] > payload_len || bytes[m] > payload_len - item_off[m])
+            return set_error(TLMG_EFORMAT, "set_expert_host %d:%d: matrix %d [%llu, +%zu) exceeds payload %zu", layer,
+                             expert, m, (unsigned long long)item_off[m], bytes[m], payload_len);
+    }
+    Layer &Ly = c->L[layer];
+    if (!Ly.cached)
+        for (const Slot &sl : Ly.h_slots)
+            if (sl.ok) return set_error(TLMG_EBUSY, "layer %d already has HBM-resident experts", layer);
+    if (c->st) cudaStreamSynchronize(c->st);   // no launch may still read a slot this re-registration drops
+    if ((rc = cache_register(c->cache, layer, expert, dt, payload, item_off, bytes))) return rc;
+    Ly.cached = true;
+    Ly.h_slots[expert] = Slot{ { nullptr, nullptr, nullptr }, { dt[0], dt[1], dt[2] }, 0 };
+    Ly.slots_dirty = true;
+    return TLMG_OK;
+}
+
+int tlmg_cache_prefetch(tlmg_ctx *c, int layer, const int32_t *ids, int k) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!c->L[layer].cached) return TLMG_OK;   // resident layer: nothing to do
+    if (k < 0 || (k > 0 && !ids)) return set_error(TLMG_EINVAL, "cache_prefetch: bad argument");
+    cudaSetDevice(c->device);
+    return cache_acquire(c->cache, layer, ids, k, true, c->st, nullptr);
+}
+
+int tlmg_cache_stats(tlmg_ctx *c, int64_t out[6]) {
+    if (!c || !out) return set_error(TLMG_EINVAL, "cache_stats: NULL argument");
+    const ExpertCache &k = c->cache;
+    out[0] = k.hits;
+    out[1] = k.misses;
+    out[2] = k.prefetched;
+    out[3] = k.prefetch_hits;
+    out[4] = k.evictions;
+    out[5] = k.bytes_loaded;
     return TLMG_OK;
 }
 
@@ -970,7 +1087,7 @@ int tlmg_expert_ffn_batch(tlmg_ctx *c, int layer, int n_tok, const float *x, con
         di = ids ? c->bids : nullptr;
         dw = w ? c->bw : nullptr;
     }
-    if (c->fused_on && Ly.dt_gu >= 0 && Ly.dt_dn >= 0 && ((uintptr_t)dx & 15u) == 0 &&
+    if (c->fused_on && !Ly.cached && Ly.dt_gu >= 0 && Ly.dt_dn >= 0 && ((uintptr_t)dx & 15u) == 0 &&
         batch_supported(Ly.dt_gu, Ly.dt_dn, D, c->g.d_expert, E, k)) {
         BatchArgs a{};
         a.slots = Ly.d_slots;
@@ -1025,6 +1142,7 @@ static int ep_layer(tlmg_ctx *c, int layer, Layer **out) {
     cudaSetDevice(c->device);
     Layer &Ly = c->L[layer];
     if ((rc = sync_slots(c, Ly))) return rc;
+    if (Ly.cached) return set_error(TLMG_EUNSUP, "expert parallel: layer %d is served by the slot cache", layer);
     if (Ly.dt_gu < 0 || Ly.dt_dn < 0 ||
         !batch_supported(Ly.dt_gu, Ly.dt_dn, c->g.d_model, c->g.d_expert, c->g.n_experts, c->g.top_k))
         return set_error(TLMG_EUNSUP, "expert parallel: layer %d needs uniform K-quant gate/up and down dtypes", layer);

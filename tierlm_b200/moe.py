@@ -121,6 +121,27 @@ class MoeContext:
         payload = np.ascontiguousarray(payload, dtype=np.uint8)
         check(self._lib.tlmg_set_expert(self._h, layer, expert, dt, payload.ctypes.data, payload.nbytes, off))
 
+    # ---- HBM expert-slot cache (experts in host memory)
+    def cache_enable(self, n_slots: int, slot_bytes: int) -> None:
+        check(self._lib.tlmg_cache_enable(self._h, n_slots, slot_bytes))
+
+    def set_expert_host(self, layer: int, expert: int, dts, payload, item_off) -> None:
+        """Register an expert in host memory (a pinned torch tensor or a numpy
+        array that outlives the context); the cache copies it on demand."""
+        dt = (C.c_int32 * 3)(*dts)
+        off = (C.c_uint64 * 3)(*item_off)
+        n = payload.nbytes if hasattr(payload, "nbytes") else payload.numel() * payload.element_size()
+        check(self._lib.tlmg_set_expert_host(self._h, layer, expert, dt, _ptr(payload), n, off))
+
+    def cache_prefetch(self, layer: int, ids) -> None:
+        a = np.ascontiguousarray(ids, dtype=np.int32)
+        check(self._lib.tlmg_cache_prefetch(self._h, layer, a.ctypes.data, a.size))
+
+    def cache_stats(self) -> dict:
+        out = (C.c_int64 * 6)()
+        check(self._lib.tlmg_cache_stats(self._h, out))
+        return dict(zip(("hits", "misses", "prefetched", "prefetch_hits", "evictions", "bytes"), list(out)))
+
     def set_layer(self, layer: int, ffn_norm=None, router_dt: int = 0, router_w=None, router_row_bytes: int = 0,
                   router_bias=None, mask=None) -> None:
         check(self._lib.tlmg_set_layer(self._h, layer, _ptr(ffn_norm), router_dt, _ptr(router_w), router_row_bytes,
