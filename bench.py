@@ -234,6 +234,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="batched-decode section: tokens per layer call (<= 1: off)")
     ap.add_argument("--prefill", type=int, default=2048, help="prefill section: prompt tokens per layer call (0: off)")
+    ap.add_argument("--cache-layers", type=int, default=8, help="slot-cache section: layers (0: off)")
+    ap.add_argument("--cache-frac", type=float, default=0.5, help="slot-cache section: HBM slots / experts")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("TLMG_BENCH_ALLOW_SHORT"), \
         "use at least 3 warm-up steps"
@@ -427,6 +429,62 @@ def main() -> None:
                    "weight_GBps": round(world * psteps * pbytes / (pms * 1e-3) / 1e9, 1),
                    "note": "tlmg_expert_ffn_batch with all prompt tokens of a layer in one call (tensor-core kernels)"}
 
+    # ---- HBM slot cache (cold experts in pinned host memory): bs=1 decode through
+    # CL layers whose 128 experts share CACHE_FRAC x (CL x 128) HBM slots
+    cache = None
+    if args.cache_layers > 0:
+        from tierlm_b200 import synth
+        from tierlm_b200.moe import MoeContext
+        CL = args.cache_layers
+        cctx = MoeContext(CL, D, DE, E, K, router=0, device=dev.index)
+        cctx.set_stream(stream)
+        gen2 = torch.Generator(device=dev)
+        gen2.manual_seed(4242 + rank)
+        rb_g, rb_d = D // 256 * 144, DE // 256 * 210
+        per = 2 * DE * rb_g + D * rb_d
+        n_slots = max(K, int(args.cache_frac * CL * E))
+        cctx.cache_enable(n_slots, per + 3 * 512)
+        host = []
+        for layer in range(CL):
+            gu = synth.device_rows(DT_GATE, E * 2 * DE, D, gen2, dev).view(E, 2 * DE * rb_g)
+            dn = synth.device_rows(DT_DOWN, E * D, DE, gen2, dev).view(E, D * rb_d)
+            hb = torch.cat([gu, dn], dim=1).cpu().pin_memory()            # [E, per]: gate | up | down
+            host.append(hb)
+            for e in range(E):
+                cctx.set_expert_host(layer, e, (DT_GATE, DT_GATE, DT_DOWN), hb[e], (0, DE * rb_g, 2 * DE * rb_g))
+        NR = 64                                             # distinct token inputs, rotated: the working set
+        cx = torch.randn((NR, CL, D), generator=g, device=dev)   # (NR x CL x 8 experts) exceeds the slots
+        clg = torch.randn((NR, CL, E), generator=g, device=dev)
+        co = torch.empty((CL, D), device=dev)
+        nxt = torch.topk(clg, K, dim=-1).indices.to(torch.int32).cpu().numpy()   # each layer's routed ids
+
+        def cstep(s, lookahead):
+            i = s % NR
+            for layer in range(CL):
+                cctx.expert_ffn(layer, cx[i, layer], clg[i, layer], co[layer])
+                if lookahead:   # ids of the next layer, known one layer ahead (the reference's lookahead)
+                    j, l2 = (i, layer + 1) if layer + 1 < CL else ((s + 1) % NR, 0)
+                    cctx.cache_prefetch(l2, nxt[j, l2])
+
+        res = {}
+        for la in (False, True):
+            for s in range(args.warmup):
+                cstep(s, la)
+            st0 = cctx.cache_stats()
+            cms = timed(lambda s: cstep(s, la), args.steps)
+            st1 = cctx.cache_stats()
+            d = {k2: st1[k2] - st0[k2] for k2 in st1}
+            res["lookahead" if la else "demand"] = {
+                "tokens_per_s": round(world * args.steps / (cms * 1e-3), 1),
+                "layer_tokens_per_s": round(world * args.steps * CL / (cms * 1e-3), 1),
+                "hit_rate": round((d["hits"]) / max(1, d["hits"] + d["misses"]), 3),
+                "h2d_GBps": round(d["bytes"] / (cms * 1e-3) / 1e9, 1)}
+        cache = {"layers": CL, "slots": n_slots, "slot_fraction": args.cache_frac,
+                 "workload": "bs=1 decode, experts in pinned host memory, random routing (a worst case: "
+                             "no temporal locality)", **res}
+        cctx.close()
+        del host
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -458,7 +516,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
-            "batched_decode": batch, "prefill": prefill,
+            "batched_decode": batch, "prefill": prefill, "slot_cache": cache,
         }
         print(json.dumps(line), flush=True)
     ctx.close()
