@@ -48,7 +48,7 @@ constexpr int NAW = 8;                  // consumer warps [0, NAW) process gate/
 constexpr int NTHREADS = 32 * (NCW + 4);   // + stream, router and two duty warps
 constexpr int MAXCH = FUSED_MAXCH;
 constexpr int MAXK = 16;
-constexpr int SLOT_A = 50176;   // gate/up stage: the gate rows and the up rows of a chunk, half each
+constexpr int SLOT_A = 50720;   // gate/up stage: the gate rows and the up rows of a chunk, half each (22 Q4_K rows of D = 2048)
 constexpr int SLOT_B = 24576;   // down stage: the rows of one expert
 constexpr uint64_t WAIT_NS = 200000000ull;       // 0.2 s: an mbarrier wait gives up
 constexpr uint64_t BARRIER_NS = 500000000ull;    // 0.5 s: the grid barrier gives up
@@ -123,11 +123,13 @@ __device__ __forceinline__ void raise_error(uint32_t *err, uint32_t *bar, uint32
 
 
 // ---------------------------------------------------------------------------
-// Work split of one token over the CTAs. Phase A (gate/up): (rank, row)
-// pairs p = r * de + j, CTA c owns [P c / G, P (c+1) / G), P = k * de.
-// Phase B (down): (rank, output row) pairs q = r * D + i, CTA c owns
-// [Q c / G, Q (c+1) / G), Q = k * D. Either range is contiguous in the
-// weight matrices of at most two experts (for G >= 64), so a CTA streams it
+// Work split of one token over the CTAs, both phases per expert: expert
+// rank r gets the CTAs [G r / k, G (r+1) / k), which split its rows evenly
+// (qrange_lo). Phase A (gate/up): (rank, row) pairs p = r * de + j; phase B
+// (down): (rank, output row) pairs q = r * D + i. A CTA's rows are then
+// contiguous in one expert's matrices, so every CTA gets the same number
+// of chunks (a range across an expert boundary would add a chunk, and the
+// CTAs holding one set the pace of the token), and a CTA streams them
 // in a few large bulk copies (copies of ~24 KB reach the HBM peak; small
 // scattered ones do not).
 __host__ __device__ inline int range_lo(int64_t n, int c, int G) { return (int)(n * c / G); }
@@ -300,7 +302,6 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     int *misc = reinterpret_cast<int *>(smem + L.misc);    // [3] sticky error seen
     const uint32_t qvx = qv_bytes(nbx), qvd = qv_bytes(nbd);
     const int64_t P = (int64_t)k * de, Q = (int64_t)k * D;
-    const int p0 = range_lo(P, blockIdx.x, gridDim.x), p1 = range_lo(P, blockIdx.x + 1, gridDim.x);
     const int q0 = qrange_lo(blockIdx.x, gridDim.x, k, D), q1 = qrange_lo(blockIdx.x + 1, gridDim.x, k, D);
     const int rq0 = q0 / D;   // first expert rank of the CTA's down rows
 
@@ -796,7 +797,7 @@ void fused_release(FusedScratch &f) {
     f = FusedScratch{};
 }
 
-// Split of the layer-token's work over the CTAs (range_lo): phase A
+// Split of the layer-token's work over the CTAs (qrange_lo): phase A
 // (rank, row) pairs, phase B (rank, output row) pairs, each cut per expert
 // into balanced chunks of contiguous rows that fit one stage: a gate/up
 // chunk is one copy of gate rows and one of the same up rows, a down chunk
@@ -815,14 +816,12 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
     if (g.n_experts > RT_PER * 32 || k > MAXK) return nullptr;
     std::vector<int2> counts(G);
     std::vector<ChunkDesc> descs((size_t)G * MAXCH);
-    const int64_t P = (int64_t)k * de, Q = (int64_t)k * D;
     for (int c = 0; c < G; c++) {
         ChunkDesc *out = &descs[(size_t)c * MAXCH];
         int n = 0;
         for (int ph = 0; ph < 2; ph++) {
-            const int64_t N = ph == 0 ? P : Q, len = ph == 0 ? de : D;
-            const int64_t lo = ph == 0 ? range_lo(N, c, G) : qrange_lo(c, G, k, D);
-            const int64_t hi = ph == 0 ? range_lo(N, c + 1, G) : qrange_lo(c + 1, G, k, D);
+            const int64_t len = ph == 0 ? de : D;
+            const int64_t lo = qrange_lo(c, G, k, (int)len), hi = qrange_lo(c + 1, G, k, (int)len);
             const int cap = ph == 0 ? capA : capB, rbytes = ph == 0 ? rbg : rbd;
             for (int64_t p = lo; p < hi;) {
                 const int r = (int)(p / len), j0 = (int)(p % len);
