@@ -418,3 +418,41 @@ def test_expert_ffn_batch_matches_single(dev, orc, shape):
     finally:
         orc.set_expf_mode(0)
     ctx.close()
+
+
+@pytest.mark.parametrize("router", [1, 2])
+def test_expert_ffn_batch_mask_bias(dev, router):
+    """Batched decode with a pruning mask and (sigmoid router) a selection
+    bias: the routing of every token excludes the masked experts and equals
+    the single-token path, every mode of the batched kernels gives the same
+    bits, and an empty batch is a no-op."""
+    from tierlm_b200 import synth
+    D, de, E, k, T = 1024, 512, 32, 4, 21
+    rng = np.random.default_rng(60 + router)
+    experts = [synth.rand_expert(rng, D, de, (12, 12, 14)) for _ in range(E)]
+    ctx = build_ctx(experts, D, de, E, k, router)
+    mask = np.zeros(E, np.uint8)
+    mask[[0, 3, 7, 8, 30]] = 1
+    bias = (0.5 * rng.standard_normal(E)).astype(np.float32) if router == 2 else None
+    ctx.set_layer(0, mask=mask, router_bias=bias)
+    x = rng.standard_normal((T, D)).astype(np.float32)
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    lg[:, 3] = 10.0                                   # the largest logit belongs to a masked expert
+    outs = []
+    for mode in ("mma", "tiled", "warp"):
+        ctx.set_batch_kernels(mode)
+        out, ids, w = np.zeros((T, D), np.float32), np.zeros((T, k), np.int32), np.zeros((T, k), np.float32)
+        ctx.expert_ffn_batch(0, x, lg, out, ids, w)
+        assert not np.isin(ids, np.flatnonzero(mask)).any()
+        outs.append((out, ids, w))
+    for out, ids, w in outs[1:]:
+        assert same_bits(out, outs[0][0]).all() and np.array_equal(ids, outs[0][1]) and same_bits(w, outs[0][2]).all()
+    out, ids, w = outs[0]
+    for t in (0, T // 2, T - 1):
+        one, i1, w1 = np.zeros(D, np.float32), np.zeros(k, np.int32), np.zeros(k, np.float32)
+        ctx.expert_ffn(0, x[t], lg[t], one, i1, w1)
+        assert np.array_equal(i1, ids[t]) and same_bits(w1, w[t]).all() and same_bits(one, out[t]).all(), t
+    n0 = ctx.launches
+    ctx.expert_ffn_batch(0, x[:0], lg[:0], out[:0])   # empty batch
+    assert ctx.launches == n0
+    ctx.close()

@@ -53,6 +53,7 @@ struct Layer {
     Slot *d_slots = nullptr;       // [E] on the device
     std::vector<Slot> h_slots;     // host mirror
     bool slots_dirty = false;
+    bool ready = false;                 // every expert loaded (or registered with the cache); set by sync_slots
     float *ffn_norm = nullptr;
     int router_dt = -1;
     void *router_w = nullptr;
@@ -166,6 +167,15 @@ static int sync_slots(tlmg_ctx *c, Layer &Ly) {
         if (sl.dt[0] != dgu || sl.dt[1] != dgu || sl.dt[2] != ddn) uniform = false;
     }
     uniform = uniform && dgu >= 0;
+    if (Ly.cached) {
+        const int l = (int)(&Ly - c->L.data());
+        Ly.ready = true;
+        for (int e2 = 0; e2 < c->g.n_experts && Ly.ready; e2++)
+            Ly.ready = c->cache.src[(size_t)l * c->g.n_experts + e2].ok;
+    } else {
+        Ly.ready = !Ly.h_slots.empty();
+        for (const Slot &sl : Ly.h_slots) Ly.ready = Ly.ready && sl.ok;
+    }
     Ly.dt_gu = uniform ? dgu : -1;
     Ly.dt_dn = uniform ? ddn : -1;
     Ly.fused_plan = uniform && !Ly.cached ? fused_plan(c->fused, c->g, dgu, ddn) : nullptr;
@@ -500,17 +510,9 @@ static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, 
     return Ly.cached ? cache_mark_used(c->cache, layer, c->pin_ids, k, c->st) : TLMG_OK;
 }
 
-static bool layer_ready(tlmg_ctx *c, Layer &Ly) {
-    if (Ly.cached) {   // every expert registered (resident or in host memory)
-        const int l = (int)(&Ly - c->L.data());
-        for (int e = 0; e < c->g.n_experts; e++)
-            if (!c->cache.src[(size_t)l * c->g.n_experts + e].ok) return false;
-        return true;
-    }
-    for (const Slot &s : Ly.h_slots)
-        if (!s.ok) return false;
-    return !Ly.h_slots.empty();
-}
+// Every expert of the layer is loaded (or registered with the slot cache);
+// valid after sync_slots().
+static bool layer_ready(tlmg_ctx *, Layer &Ly) { return Ly.ready; }
 
 // Device-pointer core of tlmg_expert_ffn.
 static int expert_ffn_dev(tlmg_ctx *c, int layer, const float *x, const float *logits, float *ffn) {
