@@ -322,6 +322,42 @@ int tlmg_expert_ffn_noalloc(const tlmg_expert_slot *experts, int E, int D, int d
  * (counted on the host at each launch). */
 int64_t tlmg_launch_count(const tlmg_ctx *ctx);
 
+/* ---- decode attention over a paged KV cache ------------------------------
+ * Replaces attn_heads (src/lib/tlm_model.c:683-719) and the K/V write of
+ * attention() (src/lib/tlm_model.c:730-763). The reference holds one f32
+ * KV per sequence, [layer][kv_head][max_ctx][head_dim]; here one layer's
+ * K (and V) cache is a pool of pages [n_pages][KV][page_size][hd] of kv_dt
+ * (TLMG_DT_F32 or TLMG_DT_BF16), and position t of a sequence is row
+ * t % page_size of page page_table[t / page_size]. hd is 64, 128 or 256;
+ * H is a multiple of KV with at most 16 query heads per KV head.
+ *
+ * TLMG_ATTN_EXACT: the reference's order of operations (serial f32 dot,
+ *   times 1/sqrtf(hd), max, expf, serial double sum, serial f32 output
+ *   sums, ascending t): bit-identical to attn_heads for f32 KV given a
+ *   correctly rounded expf. Latency-bound (two serial chains of T per head).
+ * TLMG_ATTN_SPLIT: flash-decoding over spans of positions with a merge;
+ *   equal to the reference within float rounding. The long-context path. */
+enum { TLMG_ATTN_EXACT = 0, TLMG_ATTN_SPLIT = 1 };
+
+/* Device scratch (bytes) tlmg_decode_attention needs for this shape. */
+size_t tlmg_attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd);
+
+/* One decode position's attention over positions [0, T). DEVICE pointers:
+ * q f32 [H][hd]; k_pages / v_pages (16-byte aligned) n_pages pages each;
+ * page_table int32 [ceil(T / page_size)]; work (16-byte aligned,
+ * work_bytes >= tlmg_attention_work_bytes); out f32 [H][hd]. A page-table
+ * entry outside [0, n_pages) is not dereferenced: the heads that read it
+ * get NaN. Asynchronous on `stream`. */
+int tlmg_decode_attention(int mode, int kv_dt, const float *q, const void *k_pages, const void *v_pages,
+                          int n_pages, const int32_t *page_table, int page_size, int T, int H, int KV, int hd,
+                          void *work, size_t work_bytes, float *out, void *stream);
+
+/* Appends position `pos` (row pos % page_size of page page_id) of every KV
+ * head: k / v DEVICE f32 [KV][hd] -> the pages (bf16: round to nearest
+ * even). Asynchronous on `stream`. */
+int tlmg_kv_write(int kv_dt, const float *k, const float *v, void *k_pages, void *v_pages, int n_pages,
+                  int32_t page_id, int page_size, int pos, int KV, int hd, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,7 @@ _SIGS = {
     "tlmo_expert_ffn": (_I, [C.POINTER(Geom), C.POINTER(Expert), _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "tlmo_moe_layer": (_I, [C.POINTER(Geom), C.POINTER(Layer), _P, _P, _P]),
     "tlmo_rmsnorm": (None, [_P, _P, _P, _I64, _F]),
+    "tlmo_decode_attention": (None, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
 }
 
 _lib = None
@@ -101,6 +102,8 @@ def ref() -> C.CDLL | None:
         R.tlmref_physical_cores.restype = _I
         R.tlmref_expert_ffn.argtypes = [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P]
         R.tlmref_expert_ffn.restype = _I
+        R.tlmref_attn_heads.argtypes = [_P, _P, _P, _I, _I, _I, _I, _P]
+        R.tlmref_attn_heads.restype = _I
         _ref = R
     return _ref
 
@@ -157,6 +160,24 @@ def block_partials(dt: int, wrow: np.ndarray, act: np.ndarray, n: int, w_offset:
 
 def set_expf_mode(mode: int) -> None:
     lib().tlmo_set_expf_mode(mode)
+
+
+def decode_attention(q: np.ndarray, k_pages: np.ndarray, v_pages: np.ndarray, page_table: np.ndarray,
+                     page: int, T: int) -> np.ndarray:
+    """One decode position's attention over T cached positions (tlmo.c).
+    q [H][hd]; k_pages / v_pages [n_pages][KV][page][hd]; page_table[i] = the
+    page holding positions [i*page, (i+1)*page). Returns out [H][hd]."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k_pages = np.ascontiguousarray(k_pages, dtype=np.float32)
+    v_pages = np.ascontiguousarray(v_pages, dtype=np.float32)
+    table = np.ascontiguousarray(page_table, dtype=np.int32)
+    H, hd = q.shape
+    KV = k_pages.shape[1]
+    assert k_pages.shape[2] == page and k_pages.shape[3] == hd and v_pages.shape == k_pages.shape
+    assert table.size * page >= T and (T == 0 or table[: (T + page - 1) // page].max() < k_pages.shape[0])
+    out = np.zeros((H, hd), np.float32)
+    lib().tlmo_decode_attention(_p(q), _p(k_pages), _p(v_pages), _p(table), page, T, H, KV, hd, _p(out))
+    return out
 
 
 def route(router: int, logits: np.ndarray, k: int, routed_scale: float = 1.0, mask=None, bias=None):

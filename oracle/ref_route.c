@@ -34,3 +34,32 @@ int tlmref_route(int router, const float *logits, const uint8_t *mask, const flo
     free(zmask); free(p); free(lg);
     return 0;
 }
+
+/* The reference's decode attention of one token (attn_heads,
+ * src/lib/tlm_model.c:683-718) on a minimal model / KV object: q f32[H][hd]
+ * (after q-norm and RoPE), k / v f32[KV][T][hd] (one layer, max_ctx = T),
+ * out f32[H][hd]. Uses libm expf, as the reference does. */
+int tlmref_attn_heads(const float *q, const float *k, const float *v, int T, int H, int KV, int hd, float *out) {
+    if (T <= 0 || H <= 0 || KV <= 0 || H % KV || hd <= 0) return -1;
+    tlm_model M;
+    tlm_kv kv;
+    memset(&M, 0, sizeof M);
+    memset(&kv, 0, sizeof kv);
+    M.g.n_layers = 1;
+    M.g.n_heads = (uint32_t)H;
+    M.g.n_kv_heads = (uint32_t)KV;
+    M.g.head_dim = (uint32_t)hd;
+    M.q = (float *)q;
+    M.att = out;
+    kv.mdl = &M;
+    kv.max_ctx = T;
+    kv.len = T;
+    kv.k = (float *)k;
+    kv.v = (float *)v;
+    kv.scores = malloc(sizeof(float) * (size_t)H * (size_t)T);
+    if (!kv.scores) return -2;
+    attn_job aj = { &M, &kv, 0, T - 1 };
+    attn_heads(&aj, 0, H, 0);
+    free(kv.scores);
+    return 0;
+}

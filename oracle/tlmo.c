@@ -678,3 +678,45 @@ int tlmo_moe_layer(const tlmo_geom *g, const tlmo_layer *L, float *h, int *ids, 
     free(logits);
     return rc;
 }
+
+/* ---- decode attention over a paged KV cache ------------------------------
+ * Restates the reference's attn_heads (src/lib/tlm_model.c:683-718) for one
+ * token: for head h (kv head h / (H / KV)), scores d_t = (sum_i q_i k_ti in
+ * ascending i) * (1 / sqrtf(hd)); p_t = expf(d_t - max); sum in double in
+ * ascending t; inv = (float)(1 / sum); out_i = sum_t (p_t * inv) * v_ti in
+ * ascending t. Positions live in pages: position t of kv head j is row
+ * t % page of page page_table[t / page], pages laid out [KV][page][hd]. */
+void tlmo_decode_attention(const float *q, const float *kp, const float *vp, const int32_t *page_table, int page,
+                           int T, int H, int KV, int hd, float *out) {
+    const int grp = H / KV;
+    const float scale = 1.0f / sqrtf((float)hd);
+    float *s = (float *)malloc(sizeof(float) * (size_t)T);
+    for (int h = 0; h < H; h++) {
+        const int kvh = h / grp;
+        const float *qh = q + (size_t)h * hd;
+        float mx = -INFINITY;
+        for (int t = 0; t < T; t++) {
+            const size_t row = (((size_t)page_table[t / page] * KV + kvh) * page + (size_t)(t % page)) * hd;
+            float d = 0.0f;
+            for (int i = 0; i < hd; i++) d += qh[i] * kp[row + i];
+            d *= scale;
+            s[t] = d;
+            if (d > mx) mx = d;
+        }
+        double sum = 0.0;
+        for (int t = 0; t < T; t++) {
+            float p = tlmo_expf(s[t] - mx);
+            s[t] = p;
+            sum += (double)p;
+        }
+        const float inv = (float)(1.0 / sum);
+        float *o = out + (size_t)h * hd;
+        for (int i = 0; i < hd; i++) o[i] = 0.0f;
+        for (int t = 0; t < T; t++) {
+            const size_t row = (((size_t)page_table[t / page] * KV + kvh) * page + (size_t)(t % page)) * hd;
+            const float p = s[t] * inv;
+            for (int i = 0; i < hd; i++) o[i] += p * vp[row + i];
+        }
+    }
+    free(s);
+}

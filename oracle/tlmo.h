@@ -62,6 +62,11 @@ float tlmo_expf(float x);
 float tlmo_expf_cr(float x);
 
 /* Router (src/lib/tlm_model.c:776-839). mask/bias may be NULL. */
+/* Decode attention of one token over a paged f32 KV cache (attn_heads,
+ * src/lib/tlm_model.c:683-718): q [H][hd]; pages [n][KV][page][hd];
+ * page_table [ceil(T / page)]; out [H][hd]. expf per tlmo_set_expf_mode. */
+void tlmo_decode_attention(const float *q, const float *kp, const float *vp, const int32_t *page_table, int page,
+                           int T, int H, int KV, int hd, float *out);
 void tlmo_route(int router, const float *logits, const uint8_t *mask, const float *bias,
                 int E, int k, float routed_scale, int *ids, float *w);
 

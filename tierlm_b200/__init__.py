@@ -6,6 +6,7 @@ mirror of the reference interfaces for tests and benchmarks:
 
 - tierlm_b200.quant  - tlm_quantize_act / tlm_matvec_rows / tlm_vec_dot
 - tierlm_b200.moe    - HBM expert slots, expert FFN, the moe() block
+- tierlm_b200.attention - decode attention over a paged KV cache (attn_heads)
 """
 from ._lib import TlmError, load  # noqa: F401
 

@@ -58,6 +58,9 @@ _SIGS = {
     "tlmg_matvec_rows": (_I, [_I, _P, _SZ, _P, _P, _I64, _I64, _I64, _P]),
     "tlmg_block_partials": (_I, [_I, _P, _SZ, _P, _I64, _I64, _P, _P, _P]),
     "tlmg_route": (_I, [_I, _P, _P, _P, _I, _I, _F, _P, _P, _P]),
+    "tlmg_attention_work_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "tlmg_decode_attention": (_I, [_I, _I, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _SZ, _P, _P]),
+    "tlmg_kv_write": (_I, [_I, _P, _P, _P, _P, _I, C.c_int32, _I, _I, _I, _I, _P]),
     "tlmg_qmv_host": (None, [_I, _P, _SZ, _P, _P, _I64, _I64]),
     "tlmg_qdot_host": (_F, [_I, _P, _P, _I64]),
     "tlmg_open": (_I, [C.POINTER(Geom), _I, C.POINTER(_P)]),

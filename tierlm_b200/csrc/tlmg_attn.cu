@@ -1,0 +1,616 @@
+// tlmg_attn.cu - decode attention over a paged KV cache in HBM, and the
+// paged K/V append.
+//
+// Reference: attn_heads (src/lib/tlm_model.c:683-719) and the K/V write of
+// attention() (src/lib/tlm_model.c:730-763). The reference keeps one f32 KV
+// per sequence, [layer][kv_head][max_ctx][head_dim]. Here one layer's cache
+// is a pool of pages [n_pages][KV][page][hd] (f32 or bf16): position t of a
+// sequence lives in page table[t / page], row t % page, so sequences grow
+// page by page and share one pool.
+//
+// Two algorithms over the same layout:
+//  exact  the reference's arithmetic order. Per head: serial f32 dot q.k
+//         (each product rounded, then added), times 1/sqrtf(hd); max;
+//         p = expf(s - max); serial double sum in ascending t;
+//         inv = (float)(1/sum); out[i] = serial f32 sum over ascending t of
+//         (p*inv)*v[t][i]. Bit-identical to the reference given the same
+//         expf (correctly rounded here). Two kernels: scores (one thread per
+//         position, all heads of a KV group), then one CTA per head for the
+//         softmax and the output chains. Latency-bound: a serial double
+//         chain and a serial float chain of T adds per head.
+//  split  flash-decoding: positions are cut into spans; one CTA per
+//         (span, KV head) keeps a running max / sum / output over tiles of
+//         K and V staged in shared memory by cp.async (two stages), and a
+//         merge kernel combines the spans. Reassociated, so equal to the
+//         reference within float rounding, not bit for bit.
+//
+// A page-table entry outside [0, n_pages) is never dereferenced: its rows
+// read as NaN (exact) or poison the head's result with NaN (split).
+#include <algorithm>
+#include <cmath>
+#include <utility>
+#include <vector>
+#include <cuda_bf16.h>
+
+#include "tlmg_dev.cuh"
+#include "tlmg_internal.h"
+
+namespace tlmg {
+namespace {
+
+constexpr int XS_ROWS = 64;          // exact scores: positions per CTA
+constexpr int PSM_MAX = 16384;       // exact softmax: p kept in shared memory up to this T
+constexpr int SPLIT_THREADS = 128;
+constexpr int MAX_GRP = 16;          // query heads per KV head
+
+__device__ __forceinline__ bool bad_page(int32_t e, int n_pages) { return e < 0 || e >= n_pages; }
+
+// Four consecutive elements as floats.
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16 *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(bf16_to_f32(u.x & 0xFFFFu), bf16_to_f32(u.x >> 16), bf16_to_f32(u.y & 0xFFFFu),
+                       bf16_to_f32(u.y >> 16));
+}
+__device__ __forceinline__ float ld1(const float *p) { return *p; }
+__device__ __forceinline__ float ld1(const __nv_bfloat16 *p) {
+    return bf16_to_f32(*reinterpret_cast<const uint16_t *>(p));
+}
+__device__ __forceinline__ float2 ld2(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+__device__ __forceinline__ float2 ld2(const __nv_bfloat16 *p) {
+    const uint32_t u = *reinterpret_cast<const uint32_t *>(p);
+    return make_float2(bf16_to_f32(u & 0xFFFFu), bf16_to_f32(u >> 16));
+}
+
+__device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// 16-byte copy global -> shared; src_bytes 0 fills zeros and reads nothing.
+__device__ __forceinline__ void cp16(void *dst, const void *src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// ---- exact ---------------------------------------------------------------
+// Scores of one KV group's heads for XS_ROWS positions: s[h][t] =
+// (serial sum_i q[h][i] * k[t][i]) * scale. grid (ceil(T / XS_ROWS), KV).
+template <typename KT>
+__global__ void __launch_bounds__(XS_ROWS) k_attn_scores(const float *__restrict__ q, const KT *__restrict__ kpool,
+                                                         const int32_t *__restrict__ table, int n_pages, int page,
+                                                         int T, int H, int KV, int hd, float scale,
+                                                         float *__restrict__ s) {
+    extern __shared__ float4 sm4[];
+    float *sm = reinterpret_cast<float *>(sm4);
+    const int grp = H / KV, kvh = blockIdx.y, t0 = blockIdx.x * XS_ROWS, ld = hd + 4;
+    float *qs = sm;                        // [grp][hd]
+    float *ks = sm + grp * hd;             // [XS_ROWS][hd + 4]
+    for (int i = threadIdx.x; i < grp * hd; i += blockDim.x) qs[i] = q[(size_t)kvh * grp * hd + i];
+    const int c4 = hd / 4;
+    for (int idx = threadIdx.x; idx < XS_ROWS * c4; idx += blockDim.x) {
+        const int r = idx / c4, c = idx - r * c4, t = t0 + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < T) {
+            const int32_t e = table[t / page];
+            if (bad_page(e, n_pages)) v = make_float4(NAN, NAN, NAN, NAN);
+            else v = ld4(kpool + (((size_t)e * KV + kvh) * page + (size_t)(t % page)) * hd + 4 * c);
+        }
+        *reinterpret_cast<float4 *>(ks + r * ld + 4 * c) = v;
+    }
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    if (t >= T) return;
+    const float *kr = ks + threadIdx.x * ld;
+    for (int h0 = 0; h0 < grp; h0 += 4) {
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+        const float *q0 = qs + h0 * hd;
+        for (int i = 0; i < hd; i += 4) {
+            const float4 kv = *reinterpret_cast<const float4 *>(kr + i);
+#define TLMG_DOT4(D, J)                                                                                 \
+    if (h0 + J < grp) {                                                                                 \
+        const float4 qv = *reinterpret_cast<const float4 *>(q0 + J * hd + i);                           \
+        D = __fadd_rn(D, __fmul_rn(qv.x, kv.x));                                                        \
+        D = __fadd_rn(D, __fmul_rn(qv.y, kv.y));                                                        \
+        D = __fadd_rn(D, __fmul_rn(qv.z, kv.z));                                                        \
+        D = __fadd_rn(D, __fmul_rn(qv.w, kv.w));                                                        \
+    }
+            TLMG_DOT4(d0, 0)
+            TLMG_DOT4(d1, 1)
+            TLMG_DOT4(d2, 2)
+            TLMG_DOT4(d3, 3)
+#undef TLMG_DOT4
+        }
+        float *sr = s + (size_t)(kvh * grp + h0) * T + t;
+        sr[0] = __fmul_rn(d0, scale);
+        if (h0 + 1 < grp) sr[(size_t)T] = __fmul_rn(d1, scale);
+        if (h0 + 2 < grp) sr[2 * (size_t)T] = __fmul_rn(d2, scale);
+        if (h0 + 3 < grp) sr[3 * (size_t)T] = __fmul_rn(d3, scale);
+    }
+}
+
+// Row offsets (elements) of positions [tb, tb + rows) of KV head kvh into
+// ro[0..rows); -1 for a position at or past T_end or on a bad page.
+__device__ __forceinline__ void row_offsets(const int32_t *__restrict__ table, int n_pages, int page, int KV, int kvh,
+                                            int hd, int tb, int rows, int T_end, long long *ro, int *bad, int tid,
+                                            int nt) {
+    for (int r = tid; r < rows; r += nt) {
+        const int t = tb + r;
+        long long off = -1;
+        if (t < T_end) {
+            const int32_t e = table[t / page];
+            if (bad_page(e, n_pages)) *bad = 1;
+            else off = (long long)((((size_t)e * KV + kvh) * page + (size_t)(t % page)) * hd);
+        }
+        ro[r] = off;
+    }
+}
+
+// Stages `rows` rows (row_b bytes each, at byte stride ld_b in shared
+// memory) of pool; rows with offset -1 are zero-filled.
+template <typename KT>
+__device__ __forceinline__ void stage_rows(uint8_t *dst, int ld_b, const KT *__restrict__ pool, const long long *ro,
+                                           int rows, int row_b, int tid, int nt) {
+    const int c16 = row_b / 16;
+    for (int idx = tid; idx < rows * c16; idx += nt) {
+        const int r = idx / c16, c = idx - r * c16;
+        const long long off = ro[r];
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(pool + (off < 0 ? 0 : off)) + 16 * c;
+        cp16(dst + (size_t)r * ld_b + 16 * c, src, off < 0 ? 0 : 16);
+    }
+}
+
+constexpr int XO_ROWS = 64;   // exact output: V rows per staged tile
+
+// Softmax and output of one head (grid H, hd threads, thread i owns column
+// i): the reference's max, expf, serial double sum and serial output
+// chains. V is staged in 64-row tiles by cp.async (two buffers), so the
+// output chain reads shared memory only; the first tile's copies run under
+// the serial double sum.
+template <typename KT>
+__global__ void k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__restrict__ table, int n_pages,
+                                 int page, int T, int H, int KV, int hd, float *__restrict__ s,
+                                 float *__restrict__ out) {
+    extern __shared__ float4 sm4[];
+    __shared__ float red[33];
+    __shared__ long long ro[2][XO_ROWS];
+    __shared__ int bad_s;
+    const int h = blockIdx.x, kvh = h / (H / KV), tid = threadIdx.x, nt = blockDim.x;
+    const int row_b = hd * (int)sizeof(KT);
+    uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);                          // [2][XO_ROWS][row_b]
+    float *psm = reinterpret_cast<float *>(stage + 2 * (size_t)XO_ROWS * row_b);  // [T] when T <= PSM_MAX
+    float *srow = s + (size_t)h * T;
+    if (tid == 0) bad_s = 0;
+    // max: the first strictly greater value wins, NaN never does (as the
+    // serial scan; ties between +0 and -0 give the same p)
+    float mx = -INFINITY;
+    for (int t = tid; t < T; t += nt) {
+        const float d = srow[t];
+        if (d > mx) mx = d;
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, mx, o);
+        if (v > mx) mx = v;
+    }
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float m = -INFINITY;
+        for (int w = 0; w < nt / 32; w++)
+            if (red[w] > m) m = red[w];
+        red[32] = m;
+    }
+    row_offsets(table, n_pages, page, KV, kvh, hd, 0, XO_ROWS, T, ro[0], &bad_s, tid, nt);
+    __syncthreads();
+    mx = red[32];
+    stage_rows(stage, row_b, vpool, ro[0], XO_ROWS, row_b, tid, nt);
+    cp_commit();
+    float *pp = T <= PSM_MAX ? psm : srow;
+    for (int t = tid; t < T; t += nt) pp[t] = cr_expf(__fsub_rn(srow[t], mx));
+    __syncthreads();
+    if (tid == 0) {
+        double sum = 0.0;
+        int t = 0;
+        for (; t + 8 <= T; t += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = pp[t + j];
+#pragma unroll
+            for (int j = 0; j < 8; j++) sum = __dadd_rn(sum, (double)v[j]);
+        }
+        for (; t < T; t++) sum = __dadd_rn(sum, (double)pp[t]);
+        red[0] = __double2float_rn(__ddiv_rn(1.0, sum));
+    }
+    __syncthreads();
+    const float inv = red[0];
+    const int n_tiles = (T + XO_ROWS - 1) / XO_ROWS;
+    float o = 0.0f;
+    for (int tile = 0; tile < n_tiles; tile++) {
+        const int buf = tile & 1;
+        if (tile + 1 < n_tiles) {
+            row_offsets(table, n_pages, page, KV, kvh, hd, (tile + 1) * XO_ROWS, XO_ROWS, T, ro[buf ^ 1], &bad_s,
+                        tid, nt);
+            __syncthreads();
+            stage_rows(stage + (size_t)(buf ^ 1) * XO_ROWS * row_b, row_b, vpool, ro[buf ^ 1], XO_ROWS, row_b, tid,
+                       nt);
+            cp_commit();
+            cp_wait1();
+        } else {
+            cp_wait0();
+        }
+        __syncthreads();
+        const KT *vt = reinterpret_cast<const KT *>(stage + (size_t)buf * XO_ROWS * row_b) + tid;
+        const float *pt = pp + tile * XO_ROWS;
+        const int rows = min(XO_ROWS, T - tile * XO_ROWS);
+        int r = 0;
+        for (; r + 8 <= rows; r += 8) {
+            float pv[8], vv[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                pv[j] = __fmul_rn(pt[r + j], inv);
+                vv[j] = ld1(vt + (size_t)(r + j) * hd);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) o = __fadd_rn(o, __fmul_rn(pv[j], vv[j]));
+        }
+        for (; r < rows; r++) o = __fadd_rn(o, __fmul_rn(__fmul_rn(pt[r], inv), ld1(vt + (size_t)r * hd)));
+        __syncthreads();   // the next copies overwrite this buffer
+    }
+    out[(size_t)h * hd + tid] = bad_s ? NAN : o;
+}
+
+// ---- split ---------------------------------------------------------------
+struct SplitGeom {
+    int tr;       // rows per tile
+    int span;     // positions per CTA (a multiple of tr)
+    int n_span;
+};
+
+// One CTA per (span, KV head). Scores in log2 units (q pre-scaled by
+// scale * log2(e)); running max m, sum l and output o per head over the
+// span's tiles; partials pm/pl [H][n_span], po [H][n_span][hd].
+template <typename KT>
+__global__ void __launch_bounds__(SPLIT_THREADS) k_attn_split(const float *__restrict__ q,
+                                                              const KT *__restrict__ kpool,
+                                                              const KT *__restrict__ vpool,
+                                                              const int32_t *__restrict__ table, int n_pages, int page,
+                                                              int T, int H, int KV, int hd, int tr, int span,
+                                                              int n_span, float qscale, float *__restrict__ pm,
+                                                              float *__restrict__ pl, float *__restrict__ po) {
+    extern __shared__ float4 sm4[];
+    const int grp = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
+    const int row_b = hd * (int)sizeof(KT) + 16;              // padded row bytes in shared memory
+    const int sp_ld = grp + 1;
+    float *qs = reinterpret_cast<float *>(sm4);               // [grp][hd], pre-scaled
+    float *sp = qs + grp * hd;                                // [tr][grp + 1] scores -> p
+    float *m_s = sp + tr * sp_ld;                             // [grp] running max
+    float *l_s = m_s + MAX_GRP;                               // [grp] running sum
+    float *a_s = l_s + MAX_GRP;                               // [grp] rescale of this tile
+    int *bad_s = reinterpret_cast<int *>(a_s + MAX_GRP);
+    uint8_t *stage = reinterpret_cast<uint8_t *>(sm4) +
+                     ((size_t)(grp * hd + tr * sp_ld + 3 * MAX_GRP + 4) * 4 + 15) / 16 * 16;
+    const size_t mat_b = (size_t)tr * row_b;                  // one matrix tile
+    for (int i = tid; i < grp * hd; i += SPLIT_THREADS) qs[i] = q[(size_t)kvh * grp * hd + i] * qscale;
+    if (tid < MAX_GRP) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+    }
+    if (tid == 0) *bad_s = 0;
+    __syncthreads();
+    const int t_lo = sidx * span, t_hi = min(T, t_lo + span);
+    const int n_tiles = (t_hi - t_lo + tr - 1) / tr;
+    __shared__ long long ro_s[2][64];
+    auto issue = [&](int tile, int buf) {
+        uint8_t *kd = stage + (size_t)buf * 2 * mat_b, *vd = kd + mat_b;
+        row_offsets(table, n_pages, page, KV, kvh, hd, t_lo + tile * tr, tr, t_hi, ro_s[buf], bad_s, tid,
+                    SPLIT_THREADS);
+        __syncthreads();
+        stage_rows(kd, row_b, kpool, ro_s[buf], tr, hd * (int)sizeof(KT), tid, SPLIT_THREADS);
+        stage_rows(vd, row_b, vpool, ro_s[buf], tr, hd * (int)sizeof(KT), tid, SPLIT_THREADS);
+        cp_commit();
+    };
+    // output ownership: column pair cp, heads hs, hs + HS2, ...
+    const int np2 = hd / 2, HS2 = SPLIT_THREADS / np2, cpi = tid % np2, hs = tid / np2;
+    float acc[MAX_GRP][2];
+#pragma unroll
+    for (int j = 0; j < MAX_GRP; j++) acc[j][0] = acc[j][1] = 0.f;
+    // score ownership: row r, heads hq, hq + HSs, ...
+    const int HSs = SPLIT_THREADS / tr, r_own = tid % tr, hq = tid / tr;
+    const int warp = tid >> 5, lane = tid & 31;
+
+    if (n_tiles > 0) issue(0, 0);
+    for (int tile = 0; tile < n_tiles; tile++) {
+        const int buf = tile & 1;
+        if (tile + 1 < n_tiles) {
+            issue(tile + 1, buf ^ 1);
+            cp_wait1();
+        } else {
+            cp_wait0();
+        }
+        __syncthreads();
+        const uint8_t *kt = stage + (size_t)buf * 2 * mat_b, *vt = kt + mat_b;
+        const int tb = t_lo + tile * tr;
+        // scores
+        {
+            const KT *kr = reinterpret_cast<const KT *>(kt + (size_t)r_own * row_b);
+            float d[MAX_GRP / 2];
+#pragma unroll
+            for (int j = 0; j < MAX_GRP / 2; j++) d[j] = 0.f;
+            for (int i = 0; i < hd; i += 4) {
+                const float4 kv = ld4(kr + i);
+#pragma unroll
+                for (int j = 0; j < MAX_GRP / 2; j++) {
+                    const int h = hq + j * HSs;
+                    if (h < grp) {
+                        const float4 qv = *reinterpret_cast<const float4 *>(qs + h * hd + i);
+                        d[j] = __fmaf_rn(qv.x, kv.x, d[j]);
+                        d[j] = __fmaf_rn(qv.y, kv.y, d[j]);
+                        d[j] = __fmaf_rn(qv.z, kv.z, d[j]);
+                        d[j] = __fmaf_rn(qv.w, kv.w, d[j]);
+                    }
+                }
+            }
+            const bool valid = tb + r_own < t_hi;
+#pragma unroll
+            for (int j = 0; j < MAX_GRP / 2; j++) {
+                const int h = hq + j * HSs;
+                if (h < grp) sp[r_own * sp_ld + h] = valid ? d[j] : -INFINITY;
+            }
+        }
+        __syncthreads();
+        // per head: tile max, rescale, p, tile sum (one warp per head)
+        for (int h = warp; h < grp; h += SPLIT_THREADS / 32) {
+            float tmax = -INFINITY;
+            for (int r = lane; r < tr; r += 32) tmax = fmaxf(tmax, sp[r * sp_ld + h]);
+            for (int o = 16; o; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+            const float m_old = m_s[h], m_new = fmaxf(m_old, tmax);
+            const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_old - m_new);
+            float sum = 0.f;
+            for (int r = lane; r < tr; r += 32) {
+                const float p = m_new == -INFINITY ? 0.f : exp2f(sp[r * sp_ld + h] - m_new);
+                sp[r * sp_ld + h] = p;
+                sum += p;
+            }
+            for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                m_s[h] = m_new;
+                l_s[h] = l_s[h] * alpha + sum;
+                a_s[h] = alpha;
+            }
+        }
+        __syncthreads();
+        // output
+        {
+#pragma unroll
+            for (int j = 0; j < MAX_GRP; j++) {
+                const int h = hs + j * HS2;
+                if (h < grp) {
+                    acc[j][0] *= a_s[h];
+                    acc[j][1] *= a_s[h];
+                }
+            }
+            // rows past the span's end hold p = 0 and zero-filled V
+#pragma unroll 4
+            for (int r = 0; r < tr; r++) {
+                const float2 v = ld2(reinterpret_cast<const KT *>(vt + (size_t)r * row_b) + 2 * cpi);
+                const float *pr = sp + r * sp_ld;
+#pragma unroll
+                for (int j = 0; j < MAX_GRP; j++) {
+                    const int h = hs + j * HS2;
+                    if (h < grp) {
+                        const float p = pr[h];
+                        acc[j][0] = __fmaf_rn(p, v.x, acc[j][0]);
+                        acc[j][1] = __fmaf_rn(p, v.y, acc[j][1]);
+                    }
+                }
+            }
+        }
+        __syncthreads();   // the next tile's copies overwrite this buffer
+    }
+    const bool bad = *bad_s != 0;
+#pragma unroll
+    for (int j = 0; j < MAX_GRP; j++) {
+        const int h = hs + j * HS2;
+        if (h < grp) {
+            const size_t hh = (size_t)(kvh * grp + h) * n_span + sidx;
+            float *o = po + hh * hd + 2 * cpi;
+            o[0] = acc[j][0];
+            o[1] = acc[j][1];
+        }
+    }
+    if (tid < grp) {
+        const size_t hh = (size_t)(kvh * grp + tid) * n_span + sidx;
+        pm[hh] = bad ? NAN : m_s[tid];
+        pl[hh] = l_s[tid];
+    }
+}
+
+// out[h][i] = sum_s o_s[i] 2^(m_s - M) / sum_s l_s 2^(m_s - M). grid H, hd threads.
+__global__ void k_attn_merge(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
+                             int n_span, int hd, float *__restrict__ out) {
+    const int h = blockIdx.x;
+    const float *m = pm + (size_t)h * n_span, *l = pl + (size_t)h * n_span;
+    float M = -INFINITY;
+    bool bad = false;
+#pragma unroll 8
+    for (int s = 0; s < n_span; s++) {
+        bad |= m[s] != m[s];
+        M = fmaxf(M, m[s]);
+    }
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+        float L = 0.f, O = 0.f;
+#pragma unroll 8
+        for (int s = 0; s < n_span; s++) {
+            const float w = m[s] == -INFINITY ? 0.f : exp2f(m[s] - M);
+            L = __fmaf_rn(l[s], w, L);
+            O = __fmaf_rn(po[((size_t)h * n_span + s) * hd + i], w, O);
+        }
+        out[(size_t)h * hd + i] = bad ? NAN : __fdiv_rn(O, L);
+    }
+}
+
+// ---- K/V append ------------------------------------------------------------
+// Row `pos` of every KV head: k/v [KV][hd] f32 -> the pages (bf16: round to
+// nearest even, NaN kept).
+template <typename KT>
+__global__ void k_kv_write(const float *__restrict__ k, const float *__restrict__ v, KT *__restrict__ kpool,
+                           KT *__restrict__ vpool, int32_t e, int page, int pos, int KV, int hd) {
+    const int n = KV * hd;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += gridDim.x * blockDim.x) {
+        const int kvh = idx / hd, i = idx - kvh * hd;
+        const size_t off = (((size_t)e * KV + kvh) * page + (size_t)(pos % page)) * hd + i;
+        if constexpr (sizeof(KT) == 4) {
+            kpool[off] = k[idx];
+            vpool[off] = v[idx];
+        } else {
+            kpool[off] = __float2bfloat16_rn(k[idx]);
+            vpool[off] = __float2bfloat16_rn(v[idx]);
+        }
+    }
+}
+
+int sm_count_cached() {
+    static thread_local int dev = -1, n = 0;
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d != dev) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 148;
+        }
+        dev = d;
+    }
+    return n;
+}
+
+SplitGeom split_geom(int T, int KV, int hd, int kv_dt) {
+    const int es = kv_dt == TLMG_DT_F32 ? 4 : 2;
+    SplitGeom g{};
+    g.tr = std::min(64, std::max(16, 16384 / (hd * es)));
+    const int want = std::max(1, 2 * sm_count_cached() / KV);   // spans per KV head for two CTAs per SM
+    int span = (T + want - 1) / want;
+    span = std::max(g.tr, (span + g.tr - 1) / g.tr * g.tr);
+    g.span = span;
+    g.n_span = (T + span - 1) / span;
+    return g;
+}
+
+size_t split_smem(const SplitGeom &g, int grp, int hd, int es) {
+    const size_t head = ((size_t)(grp * hd + g.tr * (grp + 1) + 3 * MAX_GRP + 4) * 4 + 15) / 16 * 16;
+    return head + 2 * 2 * (size_t)g.tr * (hd * es + 16);
+}
+
+template <typename F>
+bool smem_opt_in(F fn, size_t bytes) {
+    static thread_local std::vector<std::pair<const void *, size_t>> done;
+    for (auto &d : done)
+        if (d.first == (const void *)fn && d.second >= bytes) return true;
+    if (cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    done.push_back({ (const void *)fn, bytes });
+    return true;
+}
+
+int check_geom(const char *who, int kv_dt, int T, int H, int KV, int hd, int page, int n_pages) {
+    if (kv_dt != TLMG_DT_F32 && kv_dt != TLMG_DT_BF16)
+        return set_error(TLMG_EINVAL, "%s: KV dtype %d (f32 or bf16)", who, kv_dt);
+    if (T <= 0 || H <= 0 || KV <= 0 || H % KV || H / KV > MAX_GRP)
+        return set_error(TLMG_EINVAL, "%s: T %d, %d heads over %d KV heads (at most %d per KV head)", who, T, H, KV,
+                         MAX_GRP);
+    if (hd != 64 && hd != 128 && hd != 256) return set_error(TLMG_EINVAL, "%s: head_dim %d (64, 128 or 256)", who, hd);
+    if (page <= 0 || n_pages <= 0) return set_error(TLMG_EINVAL, "%s: page %d, %d pages", who, page, n_pages);
+    return TLMG_OK;
+}
+
+}  // namespace
+
+size_t attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd) {
+    if (T <= 0 || H <= 0 || KV <= 0) return 0;
+    if (mode == TLMG_ATTN_EXACT) return (size_t)H * T * 4;
+    const SplitGeom g = split_geom(T, KV, hd, kv_dt);
+    return (size_t)H * g.n_span * (2 + (size_t)hd) * 4;
+}
+
+template <typename KT>
+static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp, const int32_t *table, int n_pages,
+                            int page, int T, int H, int KV, int hd, float *work, float *out, cudaStream_t st,
+                            int kv_dt) {
+    const int grp = H / KV;
+    if (mode == TLMG_ATTN_EXACT) {
+        const float scale = 1.0f / sqrtf((float)hd);
+        const size_t s1 = ((size_t)grp * hd + (size_t)XS_ROWS * (hd + 4)) * 4;
+        const size_t s2 = 2 * (size_t)XO_ROWS * hd * sizeof(KT) + (T <= PSM_MAX ? (size_t)T * 4 : 0);
+        if (!smem_opt_in(k_attn_scores<KT>, s1) || !smem_opt_in(k_attn_out_exact<KT>, std::max<size_t>(s2, 16)))
+            return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
+        dim3 g1((T + XS_ROWS - 1) / XS_ROWS, KV);
+        k_attn_scores<KT><<<g1, XS_ROWS, s1, st>>>(q, kp, table, n_pages, page, T, H, KV, hd, scale, work);
+        k_attn_out_exact<KT><<<H, hd, s2, st>>>(vp, table, n_pages, page, T, H, KV, hd, work, out);
+        count_launch(2);
+    } else {
+        const SplitGeom g = split_geom(T, KV, hd, kv_dt);
+        const size_t sm = split_smem(g, grp, hd, (int)sizeof(KT));
+        if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
+        float *pm = work, *pl = pm + (size_t)H * g.n_span, *po = pl + (size_t)H * g.n_span;
+        const float qscale = (float)(1.4426950408889634 / std::sqrt((double)hd));
+        dim3 g1(g.n_span, KV);
+        k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, hd, g.tr, g.span,
+                                                        g.n_span, qscale, pm, pl, po);
+        k_attn_merge<<<H, hd, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+        count_launch(2);
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "attention launch");
+}
+
+}  // namespace tlmg
+
+using namespace tlmg;
+
+extern "C" size_t tlmg_attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd) {
+    return attention_work_bytes(mode, kv_dt, T, H, KV, hd);
+}
+
+extern "C" int tlmg_decode_attention(int mode, int kv_dt, const float *q, const void *k_pages, const void *v_pages,
+                                     int n_pages, const int32_t *page_table, int page_size, int T, int H, int KV,
+                                     int hd, void *work, size_t work_bytes, float *out, void *stream) {
+    int rc = check_geom("decode_attention", kv_dt, T, H, KV, hd, page_size, n_pages);
+    if (rc) return rc;
+    if (mode != TLMG_ATTN_EXACT && mode != TLMG_ATTN_SPLIT)
+        return set_error(TLMG_EINVAL, "decode_attention: mode %d", mode);
+    if (!q || !k_pages || !v_pages || !page_table || !work || !out)
+        return set_error(TLMG_EINVAL, "decode_attention: null pointer");
+    if (((uintptr_t)k_pages | (uintptr_t)v_pages | (uintptr_t)q | (uintptr_t)work) & 15u)
+        return set_error(TLMG_EINVAL, "decode_attention: q, pages and work must be 16-byte aligned");
+    const size_t need = attention_work_bytes(mode, kv_dt, T, H, KV, hd);
+    if (work_bytes < need)
+        return set_error(TLMG_ERANGE, "decode_attention: work holds %zu bytes, needs %zu", work_bytes, need);
+    cudaStream_t st = pick_stream(stream);
+    float *w = static_cast<float *>(work);
+    if (kv_dt == TLMG_DT_F32)
+        return launch_attention<float>(mode, q, (const float *)k_pages, (const float *)v_pages, page_table, n_pages,
+                                       page_size, T, H, KV, hd, w, out, st, kv_dt);
+    return launch_attention<__nv_bfloat16>(mode, q, (const __nv_bfloat16 *)k_pages, (const __nv_bfloat16 *)v_pages,
+                                           page_table, n_pages, page_size, T, H, KV, hd, w, out, st, kv_dt);
+}
+
+extern "C" int tlmg_kv_write(int kv_dt, const float *k, const float *v, void *k_pages, void *v_pages, int n_pages,
+                             int32_t page_id, int page_size, int pos, int KV, int hd, void *stream) {
+    int rc = check_geom("kv_write", kv_dt, 1, KV, KV, hd, page_size, n_pages);
+    if (rc) return rc;
+    if (page_id < 0 || page_id >= n_pages || pos < 0)
+        return set_error(TLMG_ERANGE, "kv_write: page %d of %d, position %d", page_id, n_pages, pos);
+    if (!k || !v || !k_pages || !v_pages) return set_error(TLMG_EINVAL, "kv_write: null pointer");
+    cudaStream_t st = pick_stream(stream);
+    const int n = KV * hd, blocks = (n + 255) / 256;
+    if (kv_dt == TLMG_DT_F32)
+        k_kv_write<float><<<blocks, 256, 0, st>>>(k, v, (float *)k_pages, (float *)v_pages, page_id, page_size, pos,
+                                                  KV, hd);
+    else
+        k_kv_write<__nv_bfloat16><<<blocks, 256, 0, st>>>(k, v, (__nv_bfloat16 *)k_pages, (__nv_bfloat16 *)v_pages,
+                                                          page_id, page_size, pos, KV, hd);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "kv_write launch");
+}

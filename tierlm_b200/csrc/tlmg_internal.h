@@ -29,4 +29,7 @@ int launch_route(int router, const float *logits, const uint8_t *mask, const flo
 
 bool is_device_ptr(const void *p);
 
+// Device scratch of tlmg_decode_attention (tlmg_attn.cu).
+size_t attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd);
+
 }  // namespace tlmg
