@@ -236,6 +236,8 @@ def main() -> None:
     ap.add_argument("--prefill", type=int, default=2048, help="prefill section: prompt tokens per layer call (0: off)")
     ap.add_argument("--cache-layers", type=int, default=8, help="slot-cache section: layers (0: off)")
     ap.add_argument("--cache-frac", type=float, default=0.5, help="slot-cache section: HBM slots / experts")
+    ap.add_argument("--attn-ctx", default="768,4096,32768",
+                    help="decode-attention section: context lengths, comma-separated (empty: off)")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("TLMG_BENCH_ALLOW_SHORT"), \
         "use at least 3 warm-up steps"
@@ -485,6 +487,60 @@ def main() -> None:
         cctx.close()
         del host
 
+    # ---- decode attention over a paged KV cache (config-3 attention shape: 32 query heads,
+    # 4 KV heads, head_dim 128, 64-position pages), one layer per call, replicated per GPU
+    attn = None
+    ctxs = [int(v) for v in str(args.attn_ctx).split(",") if v.strip()]
+    if ctxs:
+        from tierlm_b200 import attention as A
+        AH, AKV, AHD, APG = 32, 4, 128, 64
+        astream = torch.cuda.Stream(dev)   # graphs are captured on a side stream
+        astream.wait_stream(stream)
+        attn = {"heads": AH, "kv_heads": AKV, "head_dim": AHD, "page": APG, "contexts": {},
+                "timing": "CUDA graph of R calls over R distinct KV pools (working set > L2), CUDA events",
+                "kv_bytes": "2 x T x kv_heads x head_dim x element size per call (K and V read once)"}
+        for T in ctxs:
+            row = {}
+            for name, dtype, mode in (("split_bf16", torch.bfloat16, A.SPLIT), ("split_f32", torch.float32, A.SPLIT),
+                                      ("exact_f32", torch.float32, A.EXACT)):
+                if mode == A.EXACT and T > 4096:
+                    continue
+                n_pages = -(-T // APG)
+                esz = torch.tensor([], dtype=dtype).element_size()
+                pool_b = 2 * n_pages * AKV * APG * AHD * esz
+                R = int(min(256, max(1, -(-400_000_000 // pool_b))))
+                pools = [(torch.randn((n_pages, AKV, APG, AHD), generator=g, device=dev).to(dtype),
+                          torch.randn((n_pages, AKV, APG, AHD), generator=g, device=dev).to(dtype)) for _ in range(R)]
+                table = torch.randperm(n_pages, device=dev).to(torch.int32)
+                aq = torch.randn((AH, AHD), generator=g, device=dev)
+                holder = A.PagedKV.__new__(A.PagedKV)
+                holder._work = torch.empty(A.work_bytes(mode, dtype, T, AH, AKV, AHD), dtype=torch.uint8, device=dev)
+                aout = torch.empty((AH, AHD), device=dev)
+                with torch.cuda.stream(astream):
+                    for kp_, vp_ in pools:
+                        A.decode_attention(aq, kp_, vp_, table, T, mode, out=aout, work=holder)
+                    astream.synchronize()
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, stream=astream):
+                        for kp_, vp_ in pools:
+                            A.decode_attention(aq, kp_, vp_, table, T, mode, out=aout, work=holder)
+                    for _ in range(3):
+                        graph.replay()
+                    reps = 5
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(astream)
+                    for _ in range(reps):
+                        graph.replay()
+                    e1.record(astream)
+                    astream.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (reps * R)
+                gbs = pool_b / (us * 1e-6) / 1e9
+                row[name] = {"us_per_layer": round(us, 2), "kv_GBps": round(gbs, 1),
+                             "hbm_frac": round(gbs / peak, 4), "pools": R}
+                del graph, pools
+            attn["contexts"][str(T)] = row
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -516,7 +572,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
-            "batched_decode": batch, "prefill": prefill, "slot_cache": cache,
+            "batched_decode": batch, "prefill": prefill, "slot_cache": cache, "decode_attention": attn,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

@@ -155,11 +155,15 @@ def rel_l2(a, b) -> float:
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype_name", ["float32", "bfloat16"])
-@pytest.mark.parametrize("case", GPU_CASES + [(41, 9000, 32, 4, 128, 64)])
+@pytest.mark.parametrize("case", GPU_CASES + [(41, 9000, 32, 4, 128, 64), (42, 5000, 16, 2, 64, 128),
+                                   (43, 3000, 8, 1, 256, 32)])
 def test_attention_split(orc, case, dtype_name):
     """SPLIT (flash-decoding) against the oracle on the same page contents
-    (bf16 pages widened exactly to f32): relative L2 error below 2e-6 and
-    every element within 1e-5 relative + 1e-6 absolute."""
+    (bf16 pages widened exactly to f32). f32 pages (CUDA cores, f32 FMA):
+    relative L2 error below 2e-6, every element within 1e-5 relative +
+    1e-6 absolute. bf16 pages (tensor cores; q and p carried as bf16
+    high + remainder, 16 significant bits): relative L2 below 2e-5, every
+    element within 1e-4 relative + 1e-5 absolute."""
     import torch
     from tierlm_b200 import attention as A
     dtype = getattr(torch, dtype_name)
@@ -167,8 +171,9 @@ def test_attention_split(orc, case, dtype_name):
     q, tq, tk, tv, tt, table = _gpu_inputs(seed, T, H, KV, hd, page, dtype)
     out = A.decode_attention(tq, tk, tv, tt, T, A.SPLIT).cpu().numpy()
     ref = orc.decode_attention(q, tk.float().cpu().numpy(), tv.float().cpu().numpy(), table, page, T)
-    assert rel_l2(out, ref) < 2e-6
-    np.testing.assert_allclose(out, ref, rtol=1e-5, atol=1e-6)
+    tol = (2e-6, 1e-5, 1e-6) if dtype == torch.float32 else (2e-5, 1e-4, 1e-5)
+    assert rel_l2(out, ref) < tol[0], rel_l2(out, ref)
+    np.testing.assert_allclose(out, ref, rtol=tol[1], atol=tol[2])
 
 
 @pytest.mark.gpu

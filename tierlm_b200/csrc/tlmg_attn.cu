@@ -424,27 +424,298 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_attn_split(const float *__res
     }
 }
 
-// out[h][i] = sum_s o_s[i] 2^(m_s - M) / sum_s l_s 2^(m_s - M). grid H, hd threads.
-__global__ void k_attn_merge(const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
-                             int n_span, int hd, float *__restrict__ out) {
-    const int h = blockIdx.x;
+// ---- split on the tensor cores (bf16 pages) ---------------------------------
+// mma.sync m16n8k16 (bf16 in, f32 accumulate) with the KV group's query heads
+// as the M dimension. A KV group has at most 8 query heads, below the
+// 64-row minimum of tcgen05.mma; the kernel is bound by HBM (two bytes of K
+// or V per 8 multiply-adds), which this MMA shape clears with a wide margin.
+// The 16 rows carry each head twice: rows 0..7 the bf16 high part of the
+// operand (q, then p) and rows 8..15 its bf16 remainder, so q and p keep
+// 16 significant bits and K / V are exact: the result stays within float
+// rounding of the f32 arithmetic. One CTA (4 warps) per (span, KV head);
+// K/V tiles of 64 positions are staged by cp.async in NST buffers; warp w
+// owns rows 16w..16w+15 of each tile with its own running max / sum /
+// output, and the four warps are merged through shared memory at the end.
+constexpr int TC_ROWS = 64;
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(saddr(p)));
+}
+// (hi, lo) bf16 pair words of two floats: hi = bf16(x), lo = bf16(x - hi).
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+template <int HD, int NST>
+__global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__ q,
+                                                       const __nv_bfloat16 *__restrict__ kpool,
+                                                       const __nv_bfloat16 *__restrict__ vpool,
+                                                       const int32_t *__restrict__ table, int n_pages, int page, int T,
+                                                       int H, int KV, int span, int n_span, float qscale,
+                                                       float *__restrict__ pm, float *__restrict__ pl,
+                                                       float *__restrict__ po) {
+    constexpr int ROW_B = HD * 2 + 16;           // padded row bytes in shared memory
+    constexpr int MAT_B = TC_ROWS * ROW_B;
+    constexpr int C16 = HD * 2 / 16;             // 16-byte pieces per row
+    constexpr int PIECES = TC_ROWS * C16 / 128;  // per thread per matrix
+    constexpr int NT = HD / 8;                   // output n-tiles
+    extern __shared__ float4 sm4[];
+    uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);
+    __shared__ int bad_s;
+    const int G = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    if (tid == 0) bad_s = 0;
+    __syncthreads();
+    const int t_lo = sidx * span, t_hi = min(T, t_lo + span);
+    const int n_tiles = (t_hi - t_lo + TC_ROWS - 1) / TC_ROWS;
+
+    // query fragments (rows g: high part, g + 8: remainder), scaled to log2 units
+    uint32_t qa[HD / 16][4];
+    {
+        const float *qh = q + ((size_t)kvh * G + g) * HD;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            float x0 = 0.f, x1 = 0.f, x2 = 0.f, x3 = 0.f;
+            if (g < G) {
+                const float2 u = *reinterpret_cast<const float2 *>(qh + 16 * kk + 2 * t4);
+                const float2 w = *reinterpret_cast<const float2 *>(qh + 16 * kk + 8 + 2 * t4);
+                x0 = u.x * qscale;
+                x1 = u.y * qscale;
+                x2 = w.x * qscale;
+                x3 = w.y * qscale;
+            }
+            split2(x0, x1, qa[kk][0], qa[kk][1]);
+            split2(x2, x3, qa[kk][2], qa[kk][3]);
+        }
+    }
+
+    auto issue = [&](int tile) {
+        if (tile < n_tiles) {
+            uint8_t *kd = stage + (size_t)(tile % NST) * 2 * MAT_B, *vd = kd + MAT_B;
+            const int tb = t_lo + tile * TC_ROWS;
+            long long off[PIECES];
+#pragma unroll
+            for (int k = 0; k < PIECES; k++) {
+                const int r = (tid + 128 * k) / C16, t = tb + r;
+                off[k] = -1;
+                if (t < t_hi) {
+                    const int32_t e = table[t / page];
+                    if (bad_page(e, n_pages)) bad_s = 1;
+                    else off[k] = (long long)((((size_t)e * KV + kvh) * page + (size_t)(t % page)) * HD);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < PIECES; k++) {
+                const int idx = tid + 128 * k, r = idx / C16, c = idx - r * C16;
+                const long long o = off[k] < 0 ? 0 : off[k];
+                const int nb = off[k] < 0 ? 0 : 16;
+                cp16(kd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(kpool + o) + 16 * c, nb);
+                cp16(vd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(vpool + o) + 16 * c, nb);
+            }
+        }
+        cp_commit();   // an empty group past the end keeps the group count uniform
+    };
+
+    float o_acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; j++) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < NST - 1; s++) issue(s);
+    for (int tile = 0; tile < n_tiles; tile++) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(NST - 2) : "memory");
+        __syncthreads();
+        issue(tile + NST - 1);
+        const uint8_t *kt = stage + (size_t)(tile % NST) * 2 * MAT_B, *vt = kt + MAT_B;
+        const int rb = 16 * warp;                               // this warp's rows in the tile
+        const int pos0 = t_lo + tile * TC_ROWS + rb;
+        // scores: two n-tiles of 8 positions
+        float sc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+            const uint8_t *kr = kt + (rb + 8 * nt + g) * ROW_B + 4 * t4;
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; kk++) {
+                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kr + 32 * kk);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kr + 32 * kk + 16);
+                mma16816(sc[nt], qa[kk], b0, b1);
+            }
+        }
+        // s[nt][j] for head g at position pos0 + 8 nt + 2 t4 + j
+        float sv[2][2];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float v = sc[nt][j] + sc[nt][2 + j];
+                sv[nt][j] = pos0 + 8 * nt + 2 * t4 + j < t_hi ? v : -INFINITY;
+                mx = fmaxf(mx, sv[nt][j]);
+            }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
+        float p[2][2];
+        float psum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                p[nt][j] = m_new == -INFINITY ? 0.f : exp2f(sv[nt][j] - m_new);
+                psum += p[nt][j];
+            }
+        l_run = l_run * alpha + psum;
+        m_run = m_new;
+        if (!__all_sync(0xffffffffu, alpha == 1.f)) {
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                o_acc[j][0] *= alpha;
+                o_acc[j][1] *= alpha;
+                o_acc[j][2] *= alpha;
+                o_acc[j][3] *= alpha;
+            }
+        }
+        uint32_t pa[4];
+        split2(p[0][0], p[0][1], pa[0], pa[1]);
+        split2(p[1][0], p[1][1], pa[2], pa[3]);
+        // P . V: V rows rb..rb+15 of the tile, two n-tiles per ldmatrix
+        const uint8_t *vr = vt + (rb + (lane & 15)) * ROW_B + 16 * (lane >> 4);
+#pragma unroll
+        for (int j = 0; j < NT; j += 2) {
+            uint32_t b[4];
+            ldsm_x4_t(b, vr + 16 * j);
+            mma16816(o_acc[j], pa, b[0], b[1]);
+            mma16816(o_acc[j + 1], pa, b[2], b[3]);
+        }
+    }
+    cp_wait0();
+    __syncthreads();
+    // merge the four warps: per head g, weights 2^(m_w - M)
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    float *wo = reinterpret_cast<float *>(stage);              // [4][8][HD]
+    float *wm = wo + 4 * 8 * HD, *wl = wm + 32;                // [4][8]
+    if (t4 == 0) {
+        wm[warp * 8 + g] = m_run;
+        wl[warp * 8 + g] = l_run;
+    }
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+        float *d = wo + (warp * 8 + g) * HD + 8 * j + 2 * t4;
+        d[0] = o_acc[j][0] + o_acc[j][2];
+        d[1] = o_acc[j][1] + o_acc[j][3];
+    }
+    __syncthreads();
+    const bool bad = bad_s != 0;
+    for (int idx = tid; idx < G * HD; idx += 128) {
+        const int h = idx / HD, d = idx - h * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; w++) M = fmaxf(M, wm[w * 8 + h]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            const float mw = wm[w * 8 + h];
+            const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+            L = __fmaf_rn(wl[w * 8 + h], f, L);
+            O = __fmaf_rn(wo[(w * 8 + h) * HD + d], f, O);
+        }
+        const size_t hh = (size_t)(kvh * G + h) * n_span + sidx;
+        po[hh * HD + d] = O;
+        if (d == 0) {
+            pm[hh] = bad ? NAN : M;
+            pl[hh] = L;
+        }
+    }
+}
+
+// out[h][i] = sum_s o_s[i] 2^(m_s - M) / sum_s l_s 2^(m_s - M).
+// grid H, 256 threads: hd/4 float4 columns x (1024/hd) span slices.
+__global__ void __launch_bounds__(256) k_attn_merge(const float *__restrict__ pm, const float *__restrict__ pl,
+                                                    const float *__restrict__ po, int n_span, int hd,
+                                                    float *__restrict__ out) {
+    __shared__ float red[256 * 5];
+    __shared__ float mM;
+    __shared__ int mbad;
+    const int h = blockIdx.x, tid = threadIdx.x;
     const float *m = pm + (size_t)h * n_span, *l = pl + (size_t)h * n_span;
     float M = -INFINITY;
-    bool bad = false;
-#pragma unroll 8
-    for (int s = 0; s < n_span; s++) {
+    int bad = 0;
+    for (int s = tid; s < n_span; s += 256) {
         bad |= m[s] != m[s];
         M = fmaxf(M, m[s]);
     }
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        float L = 0.f, O = 0.f;
-#pragma unroll 8
-        for (int s = 0; s < n_span; s++) {
-            const float w = m[s] == -INFINITY ? 0.f : exp2f(m[s] - M);
-            L = __fmaf_rn(l[s], w, L);
-            O = __fmaf_rn(po[((size_t)h * n_span + s) * hd + i], w, O);
+    for (int o = 16; o; o >>= 1) {
+        M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    if ((tid & 31) == 0) {
+        red[tid >> 5] = M;
+        red[8 + (tid >> 5)] = (float)bad;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float mm = -INFINITY;
+        int bb = 0;
+        for (int w = 0; w < 8; w++) {
+            mm = fmaxf(mm, red[w]);
+            bb |= red[8 + w] != 0.f;
         }
-        out[(size_t)h * hd + i] = bad ? NAN : __fdiv_rn(O, L);
+        mM = mm;
+        mbad = bb;
+    }
+    __syncthreads();
+    M = mM;
+    const int nd4 = hd / 4, nss = 256 / nd4, c = tid % nd4, ss = tid / nd4;
+    float L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = ss; s < n_span; s += nss) {
+        const float w = m[s] == -INFINITY ? 0.f : exp2f(m[s] - M);
+        const float4 v = *reinterpret_cast<const float4 *>(po + ((size_t)h * n_span + s) * hd + 4 * c);
+        L = __fmaf_rn(l[s], w, L);
+        O.x = __fmaf_rn(v.x, w, O.x);
+        O.y = __fmaf_rn(v.y, w, O.y);
+        O.z = __fmaf_rn(v.z, w, O.z);
+        O.w = __fmaf_rn(v.w, w, O.w);
+    }
+    __syncthreads();
+    red[tid * 5 + 0] = L;
+    red[tid * 5 + 1] = O.x;
+    red[tid * 5 + 2] = O.y;
+    red[tid * 5 + 3] = O.z;
+    red[tid * 5 + 4] = O.w;
+    __syncthreads();
+    if (ss == 0) {
+        for (int k = 1; k < nss; k++) {
+            const float *r = red + (k * nd4 + c) * 5;
+            L += r[0];
+            O.x += r[1];
+            O.y += r[2];
+            O.z += r[3];
+            O.w += r[4];
+        }
+        float *dst = out + (size_t)h * hd + 4 * c;
+        const bool b = mbad != 0;
+        dst[0] = b ? NAN : __fdiv_rn(O.x, L);
+        dst[1] = b ? NAN : __fdiv_rn(O.y, L);
+        dst[2] = b ? NAN : __fdiv_rn(O.z, L);
+        dst[3] = b ? NAN : __fdiv_rn(O.w, L);
     }
 }
 
@@ -482,10 +753,23 @@ int sm_count_cached() {
     return n;
 }
 
-SplitGeom split_geom(int T, int KV, int hd, int kv_dt) {
+// bf16 pages with at most 8 query heads per KV head run on the tensor cores.
+bool use_tc(int kv_dt, int grp) { return kv_dt == TLMG_DT_BF16 && grp <= 8; }
+
+template <int HD>
+constexpr int tc_stages() { return HD <= 128 ? 3 : 2; }
+
+size_t tc_smem(int hd) {
+    const int nst = hd <= 128 ? 3 : 2;
+    const size_t st = (size_t)nst * 2 * TC_ROWS * (hd * 2 + 16);
+    const size_t mg = (4 * 8 * (size_t)hd + 64) * 4;
+    return std::max(st, mg);
+}
+
+SplitGeom split_geom(int T, int H, int KV, int hd, int kv_dt) {
     const int es = kv_dt == TLMG_DT_F32 ? 4 : 2;
     SplitGeom g{};
-    g.tr = std::min(64, std::max(16, 16384 / (hd * es)));
+    g.tr = use_tc(kv_dt, H / KV) ? TC_ROWS : std::min(64, std::max(16, 16384 / (hd * es)));
     const int want = std::max(1, 2 * sm_count_cached() / KV);   // spans per KV head for two CTAs per SM
     int span = (T + want - 1) / want;
     span = std::max(g.tr, (span + g.tr - 1) / g.tr * g.tr);
@@ -529,7 +813,7 @@ int check_geom(const char *who, int kv_dt, int T, int H, int KV, int hd, int pag
 size_t attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd) {
     if (T <= 0 || H <= 0 || KV <= 0) return 0;
     if (mode == TLMG_ATTN_EXACT) return (size_t)H * T * 4;
-    const SplitGeom g = split_geom(T, KV, hd, kv_dt);
+    const SplitGeom g = split_geom(T, H, KV, hd, kv_dt);
     return (size_t)H * g.n_span * (2 + (size_t)hd) * 4;
 }
 
@@ -549,15 +833,37 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         k_attn_out_exact<KT><<<H, hd, s2, st>>>(vp, table, n_pages, page, T, H, KV, hd, work, out);
         count_launch(2);
     } else {
-        const SplitGeom g = split_geom(T, KV, hd, kv_dt);
-        const size_t sm = split_smem(g, grp, hd, (int)sizeof(KT));
-        if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
+        const SplitGeom g = split_geom(T, H, KV, hd, kv_dt);
         float *pm = work, *pl = pm + (size_t)H * g.n_span, *po = pl + (size_t)H * g.n_span;
         const float qscale = (float)(1.4426950408889634 / std::sqrt((double)hd));
         dim3 g1(g.n_span, KV);
+        if constexpr (sizeof(KT) == 2) {
+            if (use_tc(kv_dt, grp)) {
+                const size_t sm = tc_smem(hd);
+                bool ok = true;
+#define TLMG_TC(HDV)                                                                                            \
+    if (hd == HDV) {                                                                                            \
+        auto fn = k_attn_split_tc<HDV, tc_stages<HDV>()>;                                                       \
+        ok = smem_opt_in(fn, sm);                                                                               \
+        if (ok) fn<<<g1, 128, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, g.span, g.n_span, qscale, pm, \
+                                        pl, po);                                                                \
+    }
+                TLMG_TC(64)
+                TLMG_TC(128)
+                TLMG_TC(256)
+#undef TLMG_TC
+                if (!ok) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
+                k_attn_merge<<<H, 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+                count_launch(2);
+                cudaError_t e = cudaGetLastError();
+                return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "attention launch");
+            }
+        }
+        const size_t sm = split_smem(g, grp, hd, (int)sizeof(KT));
+        if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, hd, g.tr, g.span,
                                                         g.n_span, qscale, pm, pl, po);
-        k_attn_merge<<<H, hd, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+        k_attn_merge<<<H, 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
         count_launch(2);
     }
     cudaError_t e = cudaGetLastError();
