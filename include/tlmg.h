@@ -328,7 +328,8 @@ int64_t tlmg_launch_count(const tlmg_ctx *ctx);
  * KV per sequence, [layer][kv_head][max_ctx][head_dim]; here one layer's
  * K (and V) cache is a pool of pages [n_pages][KV][page_size][hd] of kv_dt
  * (TLMG_DT_F32 or TLMG_DT_BF16), and position t of a sequence is row
- * t % page_size of page page_table[t / page_size]. hd is 64, 128 or 256;
+ * t % page_size of page page_table[t / page_size]; page_size is a power of
+ * two (1 .. 65536). hd is 64, 128 or 256;
  * H is a multiple of KV with at most 16 query heads per KV head.
  *
  * TLMG_ATTN_EXACT: the reference's order of operations (serial f32 dot,

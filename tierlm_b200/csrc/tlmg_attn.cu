@@ -444,6 +444,11 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(saddr(p)));
+}
 __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -462,8 +467,8 @@ template <int HD, int NST>
 __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__ q,
                                                        const __nv_bfloat16 *__restrict__ kpool,
                                                        const __nv_bfloat16 *__restrict__ vpool,
-                                                       const int32_t *__restrict__ table, int n_pages, int page, int T,
-                                                       int H, int KV, int span, int n_span, float qscale,
+                                                       const int32_t *__restrict__ table, int n_pages, int page, int lp,
+                                                       int T, int H, int KV, int span, int n_span, float qscale,
                                                        float *__restrict__ pm, float *__restrict__ pl,
                                                        float *__restrict__ po) {
     constexpr int ROW_B = HD * 2 + 16;           // padded row bytes in shared memory
@@ -501,26 +506,34 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
         }
     }
 
+    // This thread copies rows (tid + 128 k) / C16 of every tile; their page-
+    // table entries are loaded one tile ahead of the copies (te), so the
+    // copy issue never waits on the table.
+    int32_t te[PIECES];
+    auto load_te = [&](int tile) {
+#pragma unroll
+        for (int k = 0; k < PIECES; k++) {
+            const int t = t_lo + tile * TC_ROWS + (tid + 128 * k) / C16;
+            te[k] = tile < n_tiles && t < t_hi ? __ldg(table + (t >> lp)) : -1;
+        }
+    };
     auto issue = [&](int tile) {
         if (tile < n_tiles) {
             uint8_t *kd = stage + (size_t)(tile % NST) * 2 * MAT_B, *vd = kd + MAT_B;
             const int tb = t_lo + tile * TC_ROWS;
-            long long off[PIECES];
 #pragma unroll
             for (int k = 0; k < PIECES; k++) {
-                const int r = (tid + 128 * k) / C16, t = tb + r;
-                off[k] = -1;
+                const int idx = tid + 128 * k, r = idx / C16, c = idx - r * C16, t = tb + r;
+                long long o = 0;
+                int nb = 0;
                 if (t < t_hi) {
-                    const int32_t e = table[t / page];
-                    if (bad_page(e, n_pages)) bad_s = 1;
-                    else off[k] = (long long)((((size_t)e * KV + kvh) * page + (size_t)(t % page)) * HD);
+                    if (bad_page(te[k], n_pages)) {
+                        bad_s = 1;
+                    } else {
+                        o = (long long)((((size_t)te[k] * KV + kvh) << lp) + (size_t)(t & (page - 1))) * HD;
+                        nb = 16;
+                    }
                 }
-            }
-#pragma unroll
-            for (int k = 0; k < PIECES; k++) {
-                const int idx = tid + 128 * k, r = idx / C16, c = idx - r * C16;
-                const long long o = off[k] < 0 ? 0 : off[k];
-                const int nb = off[k] < 0 ? 0 : 16;
                 cp16(kd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(kpool + o) + 16 * c, nb);
                 cp16(vd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(vpool + o) + 16 * c, nb);
             }
@@ -534,27 +547,42 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
     float m_run = -INFINITY, l_run = 0.f;
 
 #pragma unroll
-    for (int s = 0; s < NST - 1; s++) issue(s);
+    for (int s = 0; s < NST - 1; s++) {
+        load_te(s);
+        issue(s);
+    }
+    load_te(NST - 1);
     for (int tile = 0; tile < n_tiles; tile++) {
         asm volatile("cp.async.wait_group %0;" ::"n"(NST - 2) : "memory");
         __syncthreads();
         issue(tile + NST - 1);
+        load_te(tile + NST);
         const uint8_t *kt = stage + (size_t)(tile % NST) * 2 * MAT_B, *vt = kt + MAT_B;
         const int rb = 16 * warp;                               // this warp's rows in the tile
         const int pos0 = t_lo + tile * TC_ROWS + rb;
         // scores: two n-tiles of 8 positions
-        float sc[2][4];
+        // (even and odd k-steps in separate accumulators: four independent chains)
+        float sc[2][4], sc2[2][4];
 #pragma unroll
         for (int nt = 0; nt < 2; nt++) {
             sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
-            const uint8_t *kr = kt + (rb + 8 * nt + g) * ROW_B + 4 * t4;
-#pragma unroll
-            for (int kk = 0; kk < HD / 16; kk++) {
-                const uint32_t b0 = *reinterpret_cast<const uint32_t *>(kr + 32 * kk);
-                const uint32_t b1 = *reinterpret_cast<const uint32_t *>(kr + 32 * kk + 16);
-                mma16816(sc[nt], qa[kk], b0, b1);
-            }
+            sc2[nt][0] = sc2[nt][1] = sc2[nt][2] = sc2[nt][3] = 0.f;
         }
+        // B fragments of two k-steps per ldmatrix.x4: lane l addresses row
+        // (l & 7) of the n-tile, 16-byte column (l >> 3) of the 64-byte pair
+#pragma unroll
+        for (int kq = 0; kq < HD / 32; kq++)
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                uint32_t b[4];
+                ldsm_x4(b, kt + (rb + 8 * nt + (lane & 7)) * ROW_B + 64 * kq + 16 * (lane >> 3));
+                mma16816(sc[nt], qa[2 * kq], b[0], b[1]);
+                mma16816(sc2[nt], qa[2 * kq + 1], b[2], b[3]);
+            }
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[nt][j] += sc2[nt][j];
         // s[nt][j] for head g at position pos0 + 8 nt + 2 t4 + j
         float sv[2][2];
         float mx = -INFINITY;
@@ -645,14 +673,14 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
 }
 
 // out[h][i] = sum_s o_s[i] 2^(m_s - M) / sum_s l_s 2^(m_s - M).
-// grid H, 256 threads: hd/4 float4 columns x (1024/hd) span slices.
+// grid (H, hd / 32), 256 threads: 32 columns x 8 span slices.
 __global__ void __launch_bounds__(256) k_attn_merge(const float *__restrict__ pm, const float *__restrict__ pl,
                                                     const float *__restrict__ po, int n_span, int hd,
                                                     float *__restrict__ out) {
-    __shared__ float red[256 * 5];
+    __shared__ float red[2][8][33];
     __shared__ float mM;
     __shared__ int mbad;
-    const int h = blockIdx.x, tid = threadIdx.x;
+    const int h = blockIdx.x, tid = threadIdx.x, c = tid & 31, ss = tid >> 5, col = 32 * blockIdx.y + c;
     const float *m = pm + (size_t)h * n_span, *l = pl + (size_t)h * n_span;
     float M = -INFINITY;
     int bad = 0;
@@ -664,58 +692,40 @@ __global__ void __launch_bounds__(256) k_attn_merge(const float *__restrict__ pm
         M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
         bad |= __shfl_xor_sync(0xffffffffu, bad, o);
     }
-    if ((tid & 31) == 0) {
-        red[tid >> 5] = M;
-        red[8 + (tid >> 5)] = (float)bad;
+    if (c == 0) {
+        red[0][ss][0] = M;
+        red[1][ss][0] = (float)bad;
     }
     __syncthreads();
     if (tid == 0) {
         float mm = -INFINITY;
         int bb = 0;
         for (int w = 0; w < 8; w++) {
-            mm = fmaxf(mm, red[w]);
-            bb |= red[8 + w] != 0.f;
+            mm = fmaxf(mm, red[0][w][0]);
+            bb |= red[1][w][0] != 0.f;
         }
         mM = mm;
         mbad = bb;
     }
     __syncthreads();
     M = mM;
-    const int nd4 = hd / 4, nss = 256 / nd4, c = tid % nd4, ss = tid / nd4;
-    float L = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f, O = 0.f;
 #pragma unroll 4
-    for (int s = ss; s < n_span; s += nss) {
+    for (int s = ss; s < n_span; s += 8) {
         const float w = m[s] == -INFINITY ? 0.f : exp2f(m[s] - M);
-        const float4 v = *reinterpret_cast<const float4 *>(po + ((size_t)h * n_span + s) * hd + 4 * c);
         L = __fmaf_rn(l[s], w, L);
-        O.x = __fmaf_rn(v.x, w, O.x);
-        O.y = __fmaf_rn(v.y, w, O.y);
-        O.z = __fmaf_rn(v.z, w, O.z);
-        O.w = __fmaf_rn(v.w, w, O.w);
+        O = __fmaf_rn(po[((size_t)h * n_span + s) * hd + col], w, O);
     }
     __syncthreads();
-    red[tid * 5 + 0] = L;
-    red[tid * 5 + 1] = O.x;
-    red[tid * 5 + 2] = O.y;
-    red[tid * 5 + 3] = O.z;
-    red[tid * 5 + 4] = O.w;
+    red[0][ss][c] = L;
+    red[1][ss][c] = O;
     __syncthreads();
     if (ss == 0) {
-        for (int k = 1; k < nss; k++) {
-            const float *r = red + (k * nd4 + c) * 5;
-            L += r[0];
-            O.x += r[1];
-            O.y += r[2];
-            O.z += r[3];
-            O.w += r[4];
+        for (int k = 1; k < 8; k++) {
+            L += red[0][k][c];
+            O += red[1][k][c];
         }
-        float *dst = out + (size_t)h * hd + 4 * c;
-        const bool b = mbad != 0;
-        dst[0] = b ? NAN : __fdiv_rn(O.x, L);
-        dst[1] = b ? NAN : __fdiv_rn(O.y, L);
-        dst[2] = b ? NAN : __fdiv_rn(O.z, L);
-        dst[3] = b ? NAN : __fdiv_rn(O.w, L);
+        out[(size_t)h * hd + col] = mbad ? NAN : __fdiv_rn(O, L);
     }
 }
 
@@ -804,7 +814,8 @@ int check_geom(const char *who, int kv_dt, int T, int H, int KV, int hd, int pag
         return set_error(TLMG_EINVAL, "%s: T %d, %d heads over %d KV heads (at most %d per KV head)", who, T, H, KV,
                          MAX_GRP);
     if (hd != 64 && hd != 128 && hd != 256) return set_error(TLMG_EINVAL, "%s: head_dim %d (64, 128 or 256)", who, hd);
-    if (page <= 0 || n_pages <= 0) return set_error(TLMG_EINVAL, "%s: page %d, %d pages", who, page, n_pages);
+    if (page <= 0 || page > (1 << 16) || (page & (page - 1)) || n_pages <= 0)
+        return set_error(TLMG_EINVAL, "%s: page %d (a power of two up to 65536), %d pages", who, page, n_pages);
     return TLMG_OK;
 }
 
@@ -840,12 +851,14 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         if constexpr (sizeof(KT) == 2) {
             if (use_tc(kv_dt, grp)) {
                 const size_t sm = tc_smem(hd);
+                int lp = 0;
+                while ((1 << lp) < page) lp++;
                 bool ok = true;
 #define TLMG_TC(HDV)                                                                                            \
     if (hd == HDV) {                                                                                            \
         auto fn = k_attn_split_tc<HDV, tc_stages<HDV>()>;                                                       \
         ok = smem_opt_in(fn, sm);                                                                               \
-        if (ok) fn<<<g1, 128, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, g.span, g.n_span, qscale, pm, \
+        if (ok) fn<<<g1, 128, sm, st>>>(q, kp, vp, table, n_pages, page, lp, T, H, KV, g.span, g.n_span, qscale, pm, \
                                         pl, po);                                                                \
     }
                 TLMG_TC(64)
@@ -853,7 +866,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
                 TLMG_TC(256)
 #undef TLMG_TC
                 if (!ok) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
-                k_attn_merge<<<H, 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+                k_attn_merge<<<dim3(H, hd / 32), 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
                 count_launch(2);
                 cudaError_t e = cudaGetLastError();
                 return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "attention launch");
@@ -863,7 +876,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, hd, g.tr, g.span,
                                                         g.n_span, qscale, pm, pl, po);
-        k_attn_merge<<<H, 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+        k_attn_merge<<<dim3(H, hd / 32), 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
         count_launch(2);
     }
     cudaError_t e = cudaGetLastError();
