@@ -78,3 +78,45 @@ def decode_attention(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Tens
                                        wbuf.data_ptr(), wbuf.numel(), _dev(out, "out"),
                                        C.c_void_p(stream_handle())))
     return out
+
+
+def _main() -> None:
+    """`python -m tierlm_b200.attention --ctx T --kv bf16 --mode split`: one
+    layer's decode attention (32 query heads, 4 KV heads, head_dim 128,
+    64-position pages, shuffled page table) on random pages, `--calls`
+    times, each call timed with CUDA events."""
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ctx", type=int, default=32768)
+    ap.add_argument("--kv", choices=["bf16", "f32"], default="bf16")
+    ap.add_argument("--mode", choices=["exact", "split"], default="split")
+    ap.add_argument("--calls", type=int, default=3)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--kv-heads", type=int, default=4)
+    ap.add_argument("--head-dim", type=int, default=128)
+    ap.add_argument("--page", type=int, default=64)
+    a = ap.parse_args()
+    dev = torch.device("cuda:0")
+    dtype = torch.bfloat16 if a.kv == "bf16" else torch.float32
+    n_pages = -(-a.ctx // a.page)
+    g = torch.Generator(device=dev).manual_seed(0)
+    kv = PagedKV(n_pages, a.kv_heads, a.page, a.head_dim, dtype=dtype, device=dev)
+    kv.k.copy_(torch.randn(kv.k.shape, generator=g, device=dev))
+    kv.v.copy_(torch.randn(kv.v.shape, generator=g, device=dev))
+    table = torch.randperm(n_pages, device=dev, generator=g).to(torch.int32)
+    q = torch.randn((a.heads, a.head_dim), generator=g, device=dev)
+    mode = SPLIT if a.mode == "split" else EXACT
+    nbytes = 2 * a.ctx * a.kv_heads * a.head_dim * kv.k.element_size()
+    for i in range(a.calls):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = kv.attend(q, table, a.ctx, mode)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3
+        print(f"call {i}: {us:.1f} us (host launch included), {nbytes / us / 1e3:.1f} GB/s of K/V, "
+              f"|out| = {float(out.abs().sum()):.4f}")
+
+
+if __name__ == "__main__":
+    _main()

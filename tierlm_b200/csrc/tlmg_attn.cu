@@ -72,62 +72,6 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 __device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// ---- exact ---------------------------------------------------------------
-// Scores of one KV group's heads for XS_ROWS positions: s[h][t] =
-// (serial sum_i q[h][i] * k[t][i]) * scale. grid (ceil(T / XS_ROWS), KV).
-template <typename KT>
-__global__ void __launch_bounds__(XS_ROWS) k_attn_scores(const float *__restrict__ q, const KT *__restrict__ kpool,
-                                                         const int32_t *__restrict__ table, int n_pages, int page,
-                                                         int T, int H, int KV, int hd, float scale,
-                                                         float *__restrict__ s) {
-    extern __shared__ float4 sm4[];
-    float *sm = reinterpret_cast<float *>(sm4);
-    const int grp = H / KV, kvh = blockIdx.y, t0 = blockIdx.x * XS_ROWS, ld = hd + 4;
-    float *qs = sm;                        // [grp][hd]
-    float *ks = sm + grp * hd;             // [XS_ROWS][hd + 4]
-    for (int i = threadIdx.x; i < grp * hd; i += blockDim.x) qs[i] = q[(size_t)kvh * grp * hd + i];
-    const int c4 = hd / 4;
-    for (int idx = threadIdx.x; idx < XS_ROWS * c4; idx += blockDim.x) {
-        const int r = idx / c4, c = idx - r * c4, t = t0 + r;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < T) {
-            const int32_t e = table[t / page];
-            if (bad_page(e, n_pages)) v = make_float4(NAN, NAN, NAN, NAN);
-            else v = ld4(kpool + (((size_t)e * KV + kvh) * page + (size_t)(t % page)) * hd + 4 * c);
-        }
-        *reinterpret_cast<float4 *>(ks + r * ld + 4 * c) = v;
-    }
-    __syncthreads();
-    const int t = t0 + threadIdx.x;
-    if (t >= T) return;
-    const float *kr = ks + threadIdx.x * ld;
-    for (int h0 = 0; h0 < grp; h0 += 4) {
-        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
-        const float *q0 = qs + h0 * hd;
-        for (int i = 0; i < hd; i += 4) {
-            const float4 kv = *reinterpret_cast<const float4 *>(kr + i);
-#define TLMG_DOT4(D, J)                                                                                 \
-    if (h0 + J < grp) {                                                                                 \
-        const float4 qv = *reinterpret_cast<const float4 *>(q0 + J * hd + i);                           \
-        D = __fadd_rn(D, __fmul_rn(qv.x, kv.x));                                                        \
-        D = __fadd_rn(D, __fmul_rn(qv.y, kv.y));                                                        \
-        D = __fadd_rn(D, __fmul_rn(qv.z, kv.z));                                                        \
-        D = __fadd_rn(D, __fmul_rn(qv.w, kv.w));                                                        \
-    }
-            TLMG_DOT4(d0, 0)
-            TLMG_DOT4(d1, 1)
-            TLMG_DOT4(d2, 2)
-            TLMG_DOT4(d3, 3)
-#undef TLMG_DOT4
-        }
-        float *sr = s + (size_t)(kvh * grp + h0) * T + t;
-        sr[0] = __fmul_rn(d0, scale);
-        if (h0 + 1 < grp) sr[(size_t)T] = __fmul_rn(d1, scale);
-        if (h0 + 2 < grp) sr[2 * (size_t)T] = __fmul_rn(d2, scale);
-        if (h0 + 3 < grp) sr[3 * (size_t)T] = __fmul_rn(d3, scale);
-    }
-}
-
 // Row offsets (elements) of positions [tb, tb + rows) of KV head kvh into
 // ro[0..rows); -1 for a position at or past T_end or on a bad page.
 __device__ __forceinline__ void row_offsets(const int32_t *__restrict__ table, int n_pages, int page, int KV, int kvh,
@@ -159,31 +103,142 @@ __device__ __forceinline__ void stage_rows(uint8_t *dst, int ld_b, const KT *__r
     }
 }
 
+// ---- exact ---------------------------------------------------------------
+// Scores of one KV group's heads for XS_ROWS positions: s[h][t] =
+// (serial sum_i q[h][i] * k[t][i]) * scale. grid (ceil(T / XS_ROWS), KV).
+template <typename KT>
+__global__ void __launch_bounds__(XS_ROWS) k_attn_scores(const float *__restrict__ q, const KT *__restrict__ kpool,
+                                                         const int32_t *__restrict__ table, int n_pages, int page,
+                                                         int T, int H, int KV, int hd, float scale,
+                                                         float *__restrict__ s) {
+    extern __shared__ float4 sm4[];
+    __shared__ long long ro[XS_ROWS];
+    __shared__ int bad_s;
+    float *sm = reinterpret_cast<float *>(sm4);
+    const int grp = H / KV, kvh = blockIdx.y, t0 = blockIdx.x * XS_ROWS, tid = threadIdx.x;
+    const int row_b = hd * (int)sizeof(KT) + 16;    // padded: thread-per-row reads are conflict-free
+    float *qs = sm;                                  // [grp][hd]
+    uint8_t *ks = reinterpret_cast<uint8_t *>(sm + grp * hd);   // [XS_ROWS][row_b] raw K rows
+    row_offsets(table, n_pages, page, KV, kvh, hd, t0, XS_ROWS, T, ro, &bad_s, tid, XS_ROWS);
+    for (int i = tid; i < grp * hd; i += XS_ROWS) qs[i] = q[(size_t)kvh * grp * hd + i];
+    __syncthreads();
+    stage_rows(ks, row_b, kpool, ro, XS_ROWS, hd * (int)sizeof(KT), tid, XS_ROWS);
+    cp_commit();
+    cp_wait0();
+    __syncthreads();
+    const int t = t0 + tid;
+    if (t >= T) return;
+    if (ro[tid] < 0) {   // a bad page: the reference would read garbage; report NaN
+        for (int h = 0; h < grp; h++) s[(size_t)(kvh * grp + h) * T + t] = NAN;
+        return;
+    }
+    const KT *kr = reinterpret_cast<const KT *>(ks + (size_t)tid * row_b);
+    for (int h0 = 0; h0 < grp; h0 += 4) {
+        float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+        const float *q0 = qs + h0 * hd;
+        for (int i = 0; i < hd; i += 4) {
+            const float4 kv = ld4(kr + i);
+#define TLMG_DOT4(D, J)                                                                                 \
+    if (h0 + J < grp) {                                                                                 \
+        const float4 qv = *reinterpret_cast<const float4 *>(q0 + J * hd + i);                           \
+        D = __fadd_rn(D, __fmul_rn(qv.x, kv.x));                                                        \
+        D = __fadd_rn(D, __fmul_rn(qv.y, kv.y));                                                        \
+        D = __fadd_rn(D, __fmul_rn(qv.z, kv.z));                                                        \
+        D = __fadd_rn(D, __fmul_rn(qv.w, kv.w));                                                        \
+    }
+            TLMG_DOT4(d0, 0)
+            TLMG_DOT4(d1, 1)
+            TLMG_DOT4(d2, 2)
+            TLMG_DOT4(d3, 3)
+#undef TLMG_DOT4
+        }
+        float *sr = s + (size_t)(kvh * grp + h0) * T + t;
+        sr[0] = __fmul_rn(d0, scale);
+        if (h0 + 1 < grp) sr[(size_t)T] = __fmul_rn(d1, scale);
+        if (h0 + 2 < grp) sr[2 * (size_t)T] = __fmul_rn(d2, scale);
+        if (h0 + 3 < grp) sr[3 * (size_t)T] = __fmul_rn(d3, scale);
+    }
+}
+
 constexpr int XO_ROWS = 64;   // exact output: V rows per staged tile
 
-// Softmax and output of one head (grid H, hd threads, thread i owns column
+// V-tile buffers of the exact output kernel: as many as fit beside the p
+// array (up to PSM_MAX floats) in 227 KB, at most 4.
+template <typename KT, int HD>
+constexpr int xo_stages() {
+    return (227 * 1024 - PSM_MAX * 4) / (XO_ROWS * HD * (int)sizeof(KT)) >= 4 ? 4 : 2;
+}
+
+// Softmax and output of one head (grid H, HD threads, thread i owns column
 // i): the reference's max, expf, serial double sum and serial output
-// chains. V is staged in 64-row tiles by cp.async (two buffers), so the
-// output chain reads shared memory only; the first tile's copies run under
-// the serial double sum.
-template <typename KT>
-__global__ void k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__restrict__ table, int n_pages,
-                                 int page, int T, int H, int KV, int hd, float *__restrict__ s,
-                                 float *__restrict__ out) {
+// chains. V is staged in 64-row tiles by cp.async, NST tiles in flight, the
+// page-table entries of each tile loaded one tile earlier; the first tiles'
+// copies run under the expf pass and the serial double sum, and the output
+// chain reads shared memory only.
+template <typename KT, int HD, int NST>
+__global__ void __launch_bounds__(HD) k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__restrict__ table,
+                                                       int n_pages, int page, int T, int H, int KV,
+                                                       float *__restrict__ s, float *__restrict__ out) {
+    constexpr int ROW_B = HD * (int)sizeof(KT);
+    constexpr int C16 = ROW_B / 16;
     extern __shared__ float4 sm4[];
     __shared__ float red[33];
-    __shared__ long long ro[2][XO_ROWS];
     __shared__ int bad_s;
-    const int h = blockIdx.x, kvh = h / (H / KV), tid = threadIdx.x, nt = blockDim.x;
-    const int row_b = hd * (int)sizeof(KT);
-    uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);                          // [2][XO_ROWS][row_b]
-    float *psm = reinterpret_cast<float *>(stage + 2 * (size_t)XO_ROWS * row_b);  // [T] when T <= PSM_MAX
+    const int h = blockIdx.x, kvh = h / (H / KV), tid = threadIdx.x;
+    uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);                              // [NST][XO_ROWS][ROW_B]
+    float *psm = reinterpret_cast<float *>(stage + (size_t)NST * XO_ROWS * ROW_B);  // [T] when T <= PSM_MAX
     float *srow = s + (size_t)h * T;
+    const int n_tiles = (T + XO_ROWS - 1) / XO_ROWS;
     if (tid == 0) bad_s = 0;
+    __syncthreads();
+    // copies: piece idx = tid + HD k is row idx / C16, column idx % C16 (a
+    // warp's copies are contiguous); row offsets in ro[stage][row] are
+    // written one iteration ahead from the page-table entry loaded the
+    // iteration before (te, threads < XO_ROWS)
+    __shared__ long long ro[NST][XO_ROWS];
+    int32_t te = -1;
+    auto load_te = [&](int tile) {
+        const int t = tile * XO_ROWS + tid;
+        te = tid < XO_ROWS && tile < n_tiles && t < T ? __ldg(table + t / page) : -1;
+    };
+    auto put_ro = [&](int tile) {
+        if (tid < XO_ROWS) {
+            const int t = tile * XO_ROWS + tid;
+            long long o = -1;
+            if (tile < n_tiles && t < T) {
+                if (bad_page(te, n_pages)) bad_s = 1;
+                else o = (long long)((((size_t)te * KV + kvh) * page + (size_t)(t % page)) * HD);
+            }
+            ro[tile % NST][tid] = o;
+        }
+    };
+    auto issue = [&](int tile) {
+        if (tile < n_tiles) {
+            uint8_t *vd = stage + (size_t)(tile % NST) * XO_ROWS * ROW_B;
+            const long long *rr = ro[tile % NST];
+#pragma unroll
+            for (int k = 0; k < XO_ROWS * C16 / HD; k++) {
+                const int idx = tid + HD * k, r = idx / C16, c = idx - r * C16;
+                const long long o = rr[r];
+                const size_t oo = o < 0 ? 0 : (size_t)o;
+                cp16(vd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(vpool + oo) + 16 * c, o < 0 ? 0 : 16);
+            }
+        }
+        cp_commit();
+    };
+#pragma unroll
+    for (int k = 0; k < NST - 1; k++) {
+        load_te(k);
+        put_ro(k);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NST - 1; k++) issue(k);
+    load_te(NST - 1);
     // max: the first strictly greater value wins, NaN never does (as the
     // serial scan; ties between +0 and -0 give the same p)
     float mx = -INFINITY;
-    for (int t = tid; t < T; t += nt) {
+    for (int t = tid; t < T; t += HD) {
         const float d = srow[t];
         if (d > mx) mx = d;
     }
@@ -195,17 +250,14 @@ __global__ void k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__
     __syncthreads();
     if (tid == 0) {
         float m = -INFINITY;
-        for (int w = 0; w < nt / 32; w++)
+        for (int w = 0; w < HD / 32; w++)
             if (red[w] > m) m = red[w];
         red[32] = m;
     }
-    row_offsets(table, n_pages, page, KV, kvh, hd, 0, XO_ROWS, T, ro[0], &bad_s, tid, nt);
     __syncthreads();
     mx = red[32];
-    stage_rows(stage, row_b, vpool, ro[0], XO_ROWS, row_b, tid, nt);
-    cp_commit();
     float *pp = T <= PSM_MAX ? psm : srow;
-    for (int t = tid; t < T; t += nt) pp[t] = cr_expf(__fsub_rn(srow[t], mx));
+    for (int t = tid; t < T; t += HD) pp[t] = cr_expf(__fsub_rn(srow[t], mx));
     __syncthreads();
     if (tid == 0) {
         double sum = 0.0;
@@ -222,23 +274,14 @@ __global__ void k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__
     }
     __syncthreads();
     const float inv = red[0];
-    const int n_tiles = (T + XO_ROWS - 1) / XO_ROWS;
     float o = 0.0f;
     for (int tile = 0; tile < n_tiles; tile++) {
-        const int buf = tile & 1;
-        if (tile + 1 < n_tiles) {
-            row_offsets(table, n_pages, page, KV, kvh, hd, (tile + 1) * XO_ROWS, XO_ROWS, T, ro[buf ^ 1], &bad_s,
-                        tid, nt);
-            __syncthreads();
-            stage_rows(stage + (size_t)(buf ^ 1) * XO_ROWS * row_b, row_b, vpool, ro[buf ^ 1], XO_ROWS, row_b, tid,
-                       nt);
-            cp_commit();
-            cp_wait1();
-        } else {
-            cp_wait0();
-        }
+        put_ro(tile + NST - 1);
+        load_te(tile + NST);
+        asm volatile("cp.async.wait_group %0;" ::"n"(NST - 2) : "memory");
         __syncthreads();
-        const KT *vt = reinterpret_cast<const KT *>(stage + (size_t)buf * XO_ROWS * row_b) + tid;
+        issue(tile + NST - 1);
+        const KT *vt = reinterpret_cast<const KT *>(stage + (size_t)(tile % NST) * XO_ROWS * ROW_B) + tid;
         const float *pt = pp + tile * XO_ROWS;
         const int rows = min(XO_ROWS, T - tile * XO_ROWS);
         int r = 0;
@@ -247,15 +290,16 @@ __global__ void k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 pv[j] = __fmul_rn(pt[r + j], inv);
-                vv[j] = ld1(vt + (size_t)(r + j) * hd);
+                vv[j] = ld1(vt + (size_t)(r + j) * HD);
             }
 #pragma unroll
             for (int j = 0; j < 8; j++) o = __fadd_rn(o, __fmul_rn(pv[j], vv[j]));
         }
-        for (; r < rows; r++) o = __fadd_rn(o, __fmul_rn(__fmul_rn(pt[r], inv), ld1(vt + (size_t)r * hd)));
-        __syncthreads();   // the next copies overwrite this buffer
+        for (; r < rows; r++) o = __fadd_rn(o, __fmul_rn(__fmul_rn(pt[r], inv), ld1(vt + (size_t)r * HD)));
     }
-    out[(size_t)h * hd + tid] = bad_s ? NAN : o;
+    cp_wait0();
+    __syncthreads();
+    out[(size_t)h * HD + tid] = bad_s ? NAN : o;
 }
 
 // ---- split ---------------------------------------------------------------
@@ -278,6 +322,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_attn_split(const float *__res
                                                               float *__restrict__ pl, float *__restrict__ po) {
     extern __shared__ float4 sm4[];
     const int grp = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
+    asm volatile("griddepcontrol.launch_dependents;");   // the merge grid may start and wait
     const int row_b = hd * (int)sizeof(KT) + 16;              // padded row bytes in shared memory
     const int sp_ld = grp + 1;
     float *qs = reinterpret_cast<float *>(sm4);               // [grp][hd], pre-scaled
@@ -474,19 +519,73 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
     constexpr int ROW_B = HD * 2 + 16;           // padded row bytes in shared memory
     constexpr int MAT_B = TC_ROWS * ROW_B;
     constexpr int C16 = HD * 2 / 16;             // 16-byte pieces per row
-    constexpr int PIECES = TC_ROWS * C16 / 128;  // per thread per matrix
     constexpr int NT = HD / 8;                   // output n-tiles
     extern __shared__ float4 sm4[];
     uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);
     __shared__ int bad_s;
     const int G = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
+    asm volatile("griddepcontrol.launch_dependents;");   // the merge grid may start and wait
     if (tid == 0) bad_s = 0;
     __syncthreads();
     const int t_lo = sidx * span, t_hi = min(T, t_lo + span);
     const int n_tiles = (t_hi - t_lo + TC_ROWS - 1) / TC_ROWS;
 
-    // query fragments (rows g: high part, g + 8: remainder), scaled to log2 units
+    // Copies: piece idx = tid + 128 k is row idx / C16, 16-byte column
+    // idx % C16 of the tile, so a warp's copies are contiguous. Row offsets
+    // come from ro[stage][row], written one iteration ahead by thread `row`
+    // from the page-table entry it loaded the iteration before (te): neither
+    // the offsets nor the copies wait on the table.
+    __shared__ long long ro[NST][TC_ROWS];
+    int32_t te = -1;
+    auto load_te = [&](int tile) {
+        const int t = t_lo + tile * TC_ROWS + tid;
+        te = tid < TC_ROWS && tile < n_tiles && t < t_hi ? __ldg(table + (t >> lp)) : -1;
+    };
+    auto put_ro = [&](int tile) {
+        if (tid < TC_ROWS) {
+            const int t = t_lo + tile * TC_ROWS + tid;
+            long long o = -1;
+            if (tile < n_tiles && t < t_hi) {
+                if (bad_page(te, n_pages)) bad_s = 1;
+                else o = (long long)((((size_t)te * KV + kvh) << lp) + (size_t)(t & (page - 1))) * HD;
+            }
+            ro[tile % NST][tid] = o;
+        }
+    };
+    auto issue = [&](int tile) {   // after a barrier that follows put_ro(tile)
+        if (tile < n_tiles) {
+            uint8_t *kd = stage + (size_t)(tile % NST) * 2 * MAT_B, *vd = kd + MAT_B;
+            const long long *rr = ro[tile % NST];
+#pragma unroll
+            for (int k = 0; k < TC_ROWS * C16 / 128; k++) {
+                const int idx = tid + 128 * k, r = idx / C16, c = idx - r * C16;
+                const long long o = rr[r];
+                const size_t oo = o < 0 ? 0 : (size_t)o;
+                const int nb = o < 0 ? 0 : 16;
+                cp16(kd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(kpool + oo) + 16 * c, nb);
+                cp16(vd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(vpool + oo) + 16 * c, nb);
+            }
+        }
+        cp_commit();   // an empty group past the end keeps the group count uniform
+    };
+
+    float o_acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; j++) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < NST - 1; s++) {
+        load_te(s);
+        put_ro(s);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s < NST - 1; s++) issue(s);
+    load_te(NST - 1);
+    // query fragments (rows g: high part, g + 8: remainder) in log2 units,
+    // loaded while the first tiles are in flight
     uint32_t qa[HD / 16][4];
     {
         const float *qh = q + ((size_t)kvh * G + g) * HD;
@@ -506,57 +605,12 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
         }
     }
 
-    // This thread copies rows (tid + 128 k) / C16 of every tile; their page-
-    // table entries are loaded one tile ahead of the copies (te), so the
-    // copy issue never waits on the table.
-    int32_t te[PIECES];
-    auto load_te = [&](int tile) {
-#pragma unroll
-        for (int k = 0; k < PIECES; k++) {
-            const int t = t_lo + tile * TC_ROWS + (tid + 128 * k) / C16;
-            te[k] = tile < n_tiles && t < t_hi ? __ldg(table + (t >> lp)) : -1;
-        }
-    };
-    auto issue = [&](int tile) {
-        if (tile < n_tiles) {
-            uint8_t *kd = stage + (size_t)(tile % NST) * 2 * MAT_B, *vd = kd + MAT_B;
-            const int tb = t_lo + tile * TC_ROWS;
-#pragma unroll
-            for (int k = 0; k < PIECES; k++) {
-                const int idx = tid + 128 * k, r = idx / C16, c = idx - r * C16, t = tb + r;
-                long long o = 0;
-                int nb = 0;
-                if (t < t_hi) {
-                    if (bad_page(te[k], n_pages)) {
-                        bad_s = 1;
-                    } else {
-                        o = (long long)((((size_t)te[k] * KV + kvh) << lp) + (size_t)(t & (page - 1))) * HD;
-                        nb = 16;
-                    }
-                }
-                cp16(kd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(kpool + o) + 16 * c, nb);
-                cp16(vd + r * ROW_B + 16 * c, reinterpret_cast<const uint8_t *>(vpool + o) + 16 * c, nb);
-            }
-        }
-        cp_commit();   // an empty group past the end keeps the group count uniform
-    };
-
-    float o_acc[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; j++) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-
-#pragma unroll
-    for (int s = 0; s < NST - 1; s++) {
-        load_te(s);
-        issue(s);
-    }
-    load_te(NST - 1);
     for (int tile = 0; tile < n_tiles; tile++) {
+        put_ro(tile + NST - 1);
+        load_te(tile + NST);
         asm volatile("cp.async.wait_group %0;" ::"n"(NST - 2) : "memory");
         __syncthreads();
         issue(tile + NST - 1);
-        load_te(tile + NST);
         const uint8_t *kt = stage + (size_t)(tile % NST) * 2 * MAT_B, *vt = kt + MAT_B;
         const int rb = 16 * warp;                               // this warp's rows in the tile
         const int pos0 = t_lo + tile * TC_ROWS + rb;
@@ -680,6 +734,9 @@ __global__ void __launch_bounds__(256) k_attn_merge(const float *__restrict__ pm
     __shared__ float red[2][8][33];
     __shared__ float mM;
     __shared__ int mbad;
+    // launched early as a programmatic dependent of the split kernel: wait
+    // until that grid has completed and its partials are visible
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int h = blockIdx.x, tid = threadIdx.x, c = tid & 31, ss = tid >> 5, col = 32 * blockIdx.y + c;
     const float *m = pm + (size_t)h * n_span, *l = pl + (size_t)h * n_span;
     float M = -INFINITY;
@@ -807,6 +864,23 @@ bool smem_opt_in(F fn, size_t bytes) {
     return true;
 }
 
+// The merge kernel as a programmatic dependent launch: it is scheduled
+// while the split kernel runs and waits in griddepcontrol.wait.
+cudaError_t launch_merge(const float *pm, const float *pl, const float *po, int n_span, int H, int hd, float *out,
+                         cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(H, hd / 32);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k_attn_merge, pm, pl, po, n_span, hd, out);
+}
+
 int check_geom(const char *who, int kv_dt, int T, int H, int KV, int hd, int page, int n_pages) {
     if (kv_dt != TLMG_DT_F32 && kv_dt != TLMG_DT_BF16)
         return set_error(TLMG_EINVAL, "%s: KV dtype %d (f32 or bf16)", who, kv_dt);
@@ -835,13 +909,24 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
     const int grp = H / KV;
     if (mode == TLMG_ATTN_EXACT) {
         const float scale = 1.0f / sqrtf((float)hd);
-        const size_t s1 = ((size_t)grp * hd + (size_t)XS_ROWS * (hd + 4)) * 4;
-        const size_t s2 = 2 * (size_t)XO_ROWS * hd * sizeof(KT) + (T <= PSM_MAX ? (size_t)T * 4 : 0);
-        if (!smem_opt_in(k_attn_scores<KT>, s1) || !smem_opt_in(k_attn_out_exact<KT>, std::max<size_t>(s2, 16)))
-            return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
+        const size_t s1 = (size_t)grp * hd * 4 + (size_t)XS_ROWS * (hd * sizeof(KT) + 16);
+        if (!smem_opt_in(k_attn_scores<KT>, s1)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         dim3 g1((T + XS_ROWS - 1) / XS_ROWS, KV);
         k_attn_scores<KT><<<g1, XS_ROWS, s1, st>>>(q, kp, table, n_pages, page, T, H, KV, hd, scale, work);
-        k_attn_out_exact<KT><<<H, hd, s2, st>>>(vp, table, n_pages, page, T, H, KV, hd, work, out);
+        bool ok = true;
+#define TLMG_XO(HDV)                                                                                       \
+    if (hd == HDV) {                                                                                       \
+        constexpr int nst = xo_stages<KT, HDV>();                                                          \
+        const size_t s2 = (size_t)nst * XO_ROWS * HDV * sizeof(KT) + (T <= PSM_MAX ? (size_t)T * 4 : 0);   \
+        auto fn = k_attn_out_exact<KT, HDV, nst>;                                                          \
+        ok = smem_opt_in(fn, s2);                                                                          \
+        if (ok) fn<<<H, HDV, s2, st>>>(vp, table, n_pages, page, T, H, KV, work, out);                     \
+    }
+        TLMG_XO(64)
+        TLMG_XO(128)
+        TLMG_XO(256)
+#undef TLMG_XO
+        if (!ok) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         count_launch(2);
     } else {
         const SplitGeom g = split_geom(T, H, KV, hd, kv_dt);
@@ -866,9 +951,9 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
                 TLMG_TC(256)
 #undef TLMG_TC
                 if (!ok) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
-                k_attn_merge<<<dim3(H, hd / 32), 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+                cudaError_t e = launch_merge(pm, pl, po, g.n_span, H, hd, out, st);
                 count_launch(2);
-                cudaError_t e = cudaGetLastError();
+                if (e == cudaSuccess) e = cudaGetLastError();
                 return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "attention launch");
             }
         }
@@ -876,7 +961,8 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, hd, g.tr, g.span,
                                                         g.n_span, qscale, pm, pl, po);
-        k_attn_merge<<<dim3(H, hd / 32), 256, 0, st>>>(pm, pl, po, g.n_span, hd, out);
+        if (launch_merge(pm, pl, po, g.n_span, H, hd, out, st) != cudaSuccess)
+            return cuda_fail(cudaGetLastError(), "attention merge launch");
         count_launch(2);
     }
     cudaError_t e = cudaGetLastError();
