@@ -150,6 +150,41 @@ int tlmg_cache_prefetch(tlmg_ctx *ctx, int layer, const int32_t *ids, int k);
 /* out[6] = hits, misses, prefetched, prefetch hits, evictions, bytes copied. */
 int tlmg_cache_stats(tlmg_ctx *ctx, int64_t out[6]);
 
+/* ---- expert packets of the tlm store (src/lib/tlm_packet.h:39-54) ------
+ * A packet is the 64-byte header, the payload and zero padding to 4096
+ * bytes. Extension: the reference writer zeroes the header's reserved[16]
+ * (src/lib/tlm_packet.c:392); reserved[0] = 'D' (0x44) marks per-item
+ * dtypes in reserved[1..3] (gate, up, down), so one EXPERT packet can hold
+ * a Q4_K gate/up with a Q6_K down. reserved[0] = 0: every item has the
+ * header's dtype (every packet the reference writes). Any other value of
+ * reserved[0]: TLMG_EFORMAT. */
+enum { TLMG_PKT_VERIFY_CRC = 1, TLMG_PKT_HOST = 2 };
+typedef struct {
+    uint32_t type, version, layer, n_items, id, dtype, layout;
+    uint32_t crc32c;
+    uint64_t payload_len;
+    uint64_t total_len;      /* header + payload rounded up to 4096 */
+    uint64_t item_off[3];    /* from the start of the payload */
+    int32_t  item_dt[3];     /* per-item dtypes (extension) or dtype x 3 */
+    int32_t  mixed;          /* 1 when the header carries per-item dtypes */
+} tlmg_packet_info;
+/* CRC-32C of buf[0..len) continuing `crc` (0 to start); same value as
+ * tlm_crc32c (src/lib/tlm_platform.h:135). Host only. */
+uint32_t tlmg_crc32c(uint32_t crc, const void *buf, size_t len);
+/* Parse and check a packet in host memory (replaces the header half of
+ * tlm_packet_verify, src/lib/tlm_packet.c:788-815, same order and codes):
+ * len < 64 -> TLMG_EINVAL; bad magic/version or payload_len > len - 64 ->
+ * TLMG_EFORMAT; with TLMG_PKT_VERIFY_CRC a payload CRC mismatch ->
+ * TLMG_EFORMAT. Host only: needs no GPU. */
+int tlmg_packet_parse(const void *packet, size_t len, int flags, tlmg_packet_info *out);
+/* tlmg_packet_parse, then the header must name (EXPERT, layer, expert)
+ * (TLMG_EFORMAT "does not match" otherwise, as tlm_packet_verify), one
+ * item, layout 0; then tlmg_set_expert with the payload and the per-item
+ * dtypes, or tlmg_set_expert_host with TLMG_PKT_HOST (the packet buffer
+ * is then borrowed for the context's life, pinned for asynchronous
+ * copies). */
+int tlmg_set_expert_packet(tlmg_ctx *ctx, int layer, int expert, const void *packet, size_t len, int flags);
+
 /* Resident per-layer tensors of the MoE block (DENSE packet,
  * src/lib/tlm_model.c:940-1055): ffn_norm f32[D]; router [E x D] of
  * router_dt (tlmc keeps it f32); router_bias f32[E] or NULL; mask u8[E]

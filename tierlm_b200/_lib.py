@@ -35,6 +35,14 @@ class ExpertSlot(C.Structure):
     _fields_ = [("m", C.c_void_p * 3), ("dt", C.c_int32 * 3), ("pad", C.c_int32)]
 
 
+class PacketInfo(C.Structure):
+    """tlmg_packet_info: a parsed tlm packet header (include/tlmg.h)."""
+    _fields_ = [("type", C.c_uint32), ("version", C.c_uint32), ("layer", C.c_uint32), ("n_items", C.c_uint32),
+                ("id", C.c_uint32), ("dtype", C.c_uint32), ("layout", C.c_uint32), ("crc32c", C.c_uint32),
+                ("payload_len", C.c_uint64), ("total_len", C.c_uint64), ("item_off", C.c_uint64 * 3),
+                ("item_dt", C.c_int32 * 3), ("mixed", C.c_int32)]
+
+
 class Geom(C.Structure):
     _fields_ = [("n_layers", C.c_int32), ("d_model", C.c_int32), ("d_expert", C.c_int32),
                 ("d_shared", C.c_int32), ("n_experts", C.c_int32), ("top_k", C.c_int32),
@@ -82,6 +90,9 @@ _SIGS = {
     "tlmg_cache_enable": (_I, [_P, _I, _SZ]),
     "tlmg_set_expert_host": (_I, [_P, _I, _I, _P, _P, _SZ, _P]),
     "tlmg_cache_prefetch": (_I, [_P, _I, _P, _I]),
+    "tlmg_crc32c": (C.c_uint32, [C.c_uint32, _P, _SZ]),
+    "tlmg_packet_parse": (_I, [_P, _SZ, _I, _P]),
+    "tlmg_set_expert_packet": (_I, [_P, _I, _I, _P, _SZ, _I]),
     "tlmg_cache_stats": (_I, [_P, _P]),
     "tlmg_check": (_I, [_P]),
     "tlmg_trace": (_I, [_P, _I, _P, _I]),

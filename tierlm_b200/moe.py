@@ -121,6 +121,15 @@ class MoeContext:
         payload = np.ascontiguousarray(payload, dtype=np.uint8)
         check(self._lib.tlmg_set_expert(self._h, layer, expert, dt, payload.ctypes.data, payload.nbytes, off))
 
+    def set_expert_packet(self, layer: int, expert: int, packet, verify_crc: bool = True, host: bool = False) -> None:
+        """Load an EXPERT packet of the tlm store (header + payload, see
+        tierlm_b200/packet.py) into expert (layer, expert): HBM-resident, or
+        with host=True registered for the slot cache (the packet buffer is
+        then borrowed like set_expert_host's payload)."""
+        n = packet.nbytes if hasattr(packet, "nbytes") else packet.numel() * packet.element_size()
+        flags = (1 if verify_crc else 0) | (2 if host else 0)
+        check(self._lib.tlmg_set_expert_packet(self._h, layer, expert, _ptr(packet), n, flags))
+
     # ---- HBM expert-slot cache (experts in host memory)
     def cache_enable(self, n_slots: int, slot_bytes: int) -> None:
         check(self._lib.tlmg_cache_enable(self._h, n_slots, slot_bytes))
