@@ -400,10 +400,10 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     if (warp == NCW) {
         if (lane == 0 || lane == 1) {
             // ---- stream, in token order. Lane 0: each token's x and gate/up
-            // chunks once it is routed. Lane 1: once the token's grid barrier
-            // completes, the quantised h of the CTA's down experts and the
-            // down chunks (down chunks would otherwise hold stages while the
-            // barrier settles).
+            // chunks once it is routed. Lane 1: once the token is routed, the
+            // down chunks whose stages earlier tokens held; once the token's
+            // grid barrier completes, the raw h rows of the CTA's down
+            // experts, then the token's remaining down chunks.
             const bool isA = lane == 0;
             bool failed = isA && !grid_wait(xbar_word(bar), a.xbar_target);
             if (isA) fence_proxy_async();   // the quantised x was written by other CTAs' generic stores
@@ -428,7 +428,37 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                     *reinterpret_cast<volatile uint32_t *>(&xseq[xb]) = (uint32_t)tok;
                     if (tr && tok == trace_tok(a)) tr[21] = now_ns();
                     if (tr && tok == trace_tok(a) + 1) tr[28] = now_ns();
-                } else {
+                }
+                // chunk c of this token into its stage (after the stage's
+                // previous chunk, nsr chunks earlier, has been consumed)
+                auto issue = [&](int c) -> bool {
+                    const uint32_t cc = (uint32_t)(tok * nc + c), u = cc / (uint32_t)nsr;
+                    const int s = s0 + (int)(cc % (uint32_t)nsr);
+                    if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1u)) return false;
+                    const ChunkDesc &d = dd[c];
+                    uint8_t *stg = smem + (isA ? L.stageA + (size_t)s * SLOT_A : L.stageB + (size_t)(s - nsA) * SLOT_B);
+                    mbar_expect_tx(&full[s], d.tx);
+                    if (tr && tok == trace_tok(a) && (c == 0 || c == nc - 1))
+                        tr[(isA ? 22 : 24) + (c == 0 ? 0 : 1)] = now_ns();
+                    if (isA) {
+                        bulk_g2s(stg + d.dst[0], sl[d.rank].m[0] + d.lo[0], d.size[0], &full[s]);
+                        bulk_g2s(stg + d.dst[1], sl[d.rank].m[1] + d.lo[1], d.size[1], &full[s]);
+                    } else {
+                        bulk_g2s(stg, sl[d.rank].m[2] + d.lo[0], d.size[0], &full[s]);
+                    }
+                    *reinterpret_cast<volatile uint32_t *>(&seq[s]) = cc;
+                    return true;
+                };
+                // Down: the chunks whose stages were held by earlier tokens
+                // go out before the token's grid barrier (their weights
+                // stream while the token's gate/up still runs); a chunk whose
+                // stage's previous chunk belongs to this token needs this
+                // token's h, so it waits until h has been issued.
+                const int pre = isA ? nc : (nc < nsr ? nc : nsr);
+                int c = 0;
+                for (; c < pre && !failed; c++) failed = !issue(c);
+                if (failed) break;
+                if (!isA) {
                     const uint64_t gt = a.bar_base + (uint64_t)tok;
                     if ((tok >= 1 && !mbar_wait(&hfree[0], (uint32_t)(tok - 1) & 1u)) ||
                         !grid_wait(barrier_word(bar, gt), (gt / NBUF + 1u) * gridDim.x)) {
@@ -443,26 +473,7 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
                     if (tr && tok == trace_tok(a)) tr[10] = now_ns();
                     if (tr && tok == trace_tok(a) + 1) tr[30] = now_ns();
                 }
-                for (int c = 0; c < nc; c++) {
-                    const uint32_t cc = (uint32_t)(tok * nc + c), u = cc / (uint32_t)nsr;
-                    const int s = s0 + (int)(cc % (uint32_t)nsr);
-                    if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1u)) {
-                        failed = true;
-                        break;
-                    }
-                    const ChunkDesc &d = dd[c];
-                    uint8_t *stg = smem + (isA ? L.stageA + (size_t)s * SLOT_A : L.stageB + (size_t)(s - nsA) * SLOT_B);
-                    mbar_expect_tx(&full[s], d.tx);
-                    if (tr && tok == trace_tok(a) && (c == 0 || c == nc - 1))
-                        tr[(isA ? 22 : 24) + (c == 0 ? 0 : 1)] = now_ns();
-                    if (isA) {
-                        bulk_g2s(stg + d.dst[0], sl[d.rank].m[0] + d.lo[0], d.size[0], &full[s]);
-                        bulk_g2s(stg + d.dst[1], sl[d.rank].m[1] + d.lo[1], d.size[1], &full[s]);
-                    } else {
-                        bulk_g2s(stg, sl[d.rank].m[2] + d.lo[0], d.size[0], &full[s]);
-                    }
-                    *reinterpret_cast<volatile uint32_t *>(&seq[s]) = cc;
-                }
+                for (; c < nc && !failed; c++) failed = !issue(c);
             }
             if (failed) raise_error(err, bar, isA ? FUSED_ERR_COPY : FUSED_ERR_BARRIER);
         }
