@@ -577,8 +577,9 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
     // the down chunks, each group chunk by chunk in token order. All
     // threads of the group split the chunk's (row, block) units, one unit
     // each, and write the units' exact partials to shared memory; after a
-    // group barrier the stage is released and one thread per row runs the
-    // row's fmaf chain(s) over the blocks in ascending order (the next
+    // group barrier the stage is released and one thread per row (the
+    // group's highest threads) runs the row's fmaf chain(s) over the blocks
+    // in ascending order (the next
     // chunk's units go to the other partials buffer meanwhile). A stage is
     // thus held for one unit's work, not for a row's.
     const bool isA = warp < NAW;
@@ -677,8 +678,10 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
             }
 
             // the rows' chains
-            if (!(st & ST_ABORT) && gt < d.nrows) {
-                const int row = gt;
+            // the rows' chains run on the group's highest threads, which get
+            // the fewest units of the next chunk (units fill threads from 0)
+            if (!(st & ST_ABORT) && gth - 1 - gt < d.nrows) {
+                const int row = gth - 1 - gt;
                 if (isA) {
                     float ag = 0.0f, au = 0.0f;
                     for (int b = 0; b < nbx; b++) {
