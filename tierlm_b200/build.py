@@ -28,7 +28,7 @@ NVCC_FLAGS = [
 ]
 
 
-# The persistent kernel runs 17 warps per SM (96 registers a thread); its
+# The persistent kernel runs 20 warps per SM (96 registers a thread); its
 # per-step device functions are compiled separately under the same cap.
 FILE_FLAGS = {"tlmg_fused.cu": ["-maxrregcount=96"]}
 

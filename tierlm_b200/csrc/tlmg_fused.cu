@@ -43,9 +43,9 @@
 
 namespace tlmg {
 
-constexpr int NCW = 16;                 // consumer warps; warp NCW streams, NCW + 1 routes, NCW + 2 / NCW + 3 do duties
-constexpr int NAW = 8;                  // consumer warps [0, NAW) process gate/up chunks, the others down chunks
-constexpr int NTHREADS = 32 * (NCW + 4);   // + stream, router and two duty warps
+constexpr int NCW = 15;                 // consumer warps; warps NCW / NCW + 4 stream, NCW + 1 routes, NCW + 2 / NCW + 3 do duties
+constexpr int NAW = 7;                  // consumer warps [0, NAW) process gate/up chunks (<= 176 units + the chains), the others down chunks
+constexpr int NTHREADS = 32 * (NCW + 5);   // + gate/up stream, router, two duty warps, down stream (warp NCW + 4)
 constexpr int MAXCH = FUSED_MAXCH;
 constexpr int MAXK = 16;
 constexpr int SLOT_A = 50720;   // gate/up stage: the gate rows and the up rows of a chunk, half each (22 Q4_K rows of D = 2048)
@@ -250,9 +250,9 @@ __device__ __forceinline__ uint64_t *trace_row(const FusedArgs &a) {
 // ---------------------------------------------------------------------------
 // ---------------------------------------------------------------------------
 // The persistent kernel. One CTA per SM: warps 0..NCW-1 consume work items,
-// warp NCW streams (lane 0: the tokens' x and gate/up chunks; lane 1: each
-// token's quantised h and down chunks once its grid barrier completes),
-// warp NCW + 1 routes.
+// warp NCW streams the tokens' x and gate/up chunks, warp NCW + 4 each
+// token's down chunks and (once its grid barrier completes) its h rows,
+// warp NCW + 1 routes, warps NCW + 2 / NCW + 3 do the per-token duties.
 //
 //   launch start  every CTA quantises its share of the launch's inputs x
 //                 (n_tok x D / 256 blocks) into a.xq; one grid-wide count.
@@ -397,14 +397,16 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
         }
     }
 
-    if (warp == NCW) {
-        if (lane == 0 || lane == 1) {
-            // ---- stream, in token order. Lane 0: each token's x and gate/up
-            // chunks once it is routed. Lane 1: once the token is routed, the
-            // down chunks whose stages earlier tokens held; once the token's
-            // grid barrier completes, the raw h rows of the CTA's down
-            // experts, then the token's remaining down chunks.
-            const bool isA = lane == 0;
+    if (warp == NCW || warp == NCW + 4) {
+        if (lane == 0) {
+            // ---- streams, in token order, one warp each (a lane that sleeps
+            // in a wait would stall a divergent lane of the same warp).
+            // Warp NCW: each token's x and gate/up chunks once it is routed.
+            // Warp NCW + 4: once the token is routed, the down chunks whose
+            // stages earlier tokens held; once the token's grid barrier
+            // completes, the raw h rows of the CTA's down experts, then the
+            // token's remaining down chunks.
+            const bool isA = warp == NCW;
             bool failed = isA && !grid_wait(xbar_word(bar), a.xbar_target);
             if (isA) fence_proxy_async();   // the quantised x was written by other CTAs' generic stores
             const int nc = isA ? nA : nB, nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA;
