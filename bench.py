@@ -46,8 +46,8 @@ METRIC = "expert GEMV HBM GB/s, bs=1 MoE expert FFN (Qwen3-30B-A3B layer shape, 
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per layer-token of the persistent kernel, from one
 # ncu capture of a 4-layer-token launch (profiles/k_fused_ffn_config2.md):
-# 98,107,392 read + 5,727,488 written, over 4 layer-tokens.
-TRAFFIC_LAYER_TOKEN = (98_107_392 + 5_727_488) // 4
+# 98,106,880 read + 3,531,520 written, over 4 layer-tokens.
+TRAFFIC_LAYER_TOKEN = (98_106_880 + 3_531_520) // 4
 
 
 def peaks() -> tuple[float, str]:
