@@ -241,8 +241,13 @@ size_t tlmg_ep_record_bytes(const tlmg_ctx *ctx);
  * write one record per (token, rank) pair into send (room for n_tok * top_k
  * records), grouped by owner GPU, ascending pair order inside an owner.
  * perm i32[n_tok * top_k] receives each pair's record index, w f32[n_tok *
- * top_k] its routing weight, counts[n_ranks] the records per owner. Waits
- * for the stream (the counts size the exchange). */
+ * top_k] its routing weight, counts[n_ranks] the records per owner. With
+ * host counts the call waits for the stream (the counts size the
+ * exchange). counts may instead be a device pointer: they are then written
+ * on the stream and the call returns without waiting (one host read of
+ * the exchanged counts can then serve both directions); a foreign record
+ * of an earlier call is then reported by a later host-count call or by
+ * tlmg_check. */
 int tlmg_ep_dispatch(tlmg_ctx *ctx, int layer, int n_tok, const float *x, const float *logits,
                      int n_ranks, void *send, int32_t *perm, float *w, int64_t *counts);
 

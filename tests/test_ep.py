@@ -235,6 +235,42 @@ def test_ep_c_abi_emulated_ranks(n_ranks):
 
 
 @pytest.mark.gpu
+def test_ep_dispatch_device_counts():
+    """Counts written to device memory (no host wait) equal the host counts,
+    and the records, permutation and weights are the same bytes."""
+    from tierlm_b200 import synth
+    dev = torch.device("cuda:0")
+    D_, de, E_, k, n, nr = 1024, 512, 24, 4, 37, 3
+    rng = np.random.default_rng(41)
+    experts = [synth.rand_expert(rng, D_, de, (12, 12, 14)) for _ in range(E_)]
+    ctx = _gpu_ctx(experts, D_, de, E_, k)
+    RB = ctx.ep_record_bytes
+    x = torch.from_numpy(rng.standard_normal((n, D_)).astype(np.float32)).to(dev)
+    lg = torch.from_numpy(rng.standard_normal((n, E_)).astype(np.float32)).to(dev)
+    outs = []
+    for mode in ("host", "device"):
+        send = torch.zeros((n * k, RB), dtype=torch.uint8, device=dev)
+        perm = torch.zeros(n * k, dtype=torch.int32, device=dev)
+        w = torch.zeros(n * k, dtype=torch.float32, device=dev)
+        if mode == "host":
+            counts = ctx.ep_dispatch(0, x, lg, nr, send, perm, w)
+        else:
+            cd = torch.full((nr,), -1, dtype=torch.int64, device=dev)
+            ctx.ep_dispatch_async(0, x, lg, nr, send, perm, w, cd)
+            ctx.check()
+            counts = cd.tolist()
+        outs.append((counts, send.cpu(), perm.cpu(), w.cpu()))
+    assert outs[0][0] == outs[1][0] and sum(outs[0][0]) == n * k
+    for a, b in zip(outs[0][1:], outs[1][1:]):
+        assert torch.equal(a, b)
+    empty = torch.full((nr,), -1, dtype=torch.int64, device=dev)   # no tokens: zero counts
+    ctx.ep_dispatch_async(0, x[:0], lg[:0], nr, send, perm, w, empty)
+    ctx.check()
+    assert empty.tolist() == [0] * nr
+    ctx.close()
+
+
+@pytest.mark.gpu
 def test_ep_foreign_record_is_loud():
     """A record naming an expert outside the owner's range gets a NaN row and
     the context reports TLMG_EINVAL at the next check."""

@@ -256,6 +256,11 @@ __global__ void k_bcombine(const float *__restrict__ eo, const int32_t *__restri
 // expert ids[p], owner(e) = floor(e * nr / E); records are grouped by owner,
 // inside an owner in ascending pair order. perm[p] = the pair's record index,
 // cnt[d] = records for owner d.
+// counts (int32, the dispatch's pinned words) -> int64 device counts
+__global__ void k_epcount64(const int32_t *__restrict__ cnt, int nr, int64_t *__restrict__ out) {
+    for (int d = threadIdx.x; d < nr; d += blockDim.x) out[d] = cnt[d];
+}
+
 __global__ void __launch_bounds__(1024) k_epcount(const int32_t *__restrict__ ids, int np, int E, int nr,
                                                    int32_t *__restrict__ perm, int32_t *__restrict__ cnt) {
     __shared__ int tot[EP_MAX_RANKS], base[EP_MAX_RANKS], wsum[32];
@@ -655,8 +660,14 @@ int ep_dispatch(BatchScratch &s, const BatchArgs &a, int nr, uint8_t *send, int3
         return set_error(TLMG_EUNSUP, "expert-parallel dispatch: dtypes %d/%d or shape unsupported", a.dt_gu, a.dt_dn);
     if (nr < 1 || nr > EP_MAX_RANKS || nr > a.E)
         return set_error(TLMG_EINVAL, "expert-parallel dispatch: %d ranks (1..%d, at most E)", nr, EP_MAX_RANKS);
+    const bool dev_counts = is_device_ptr(counts);
     if (a.n <= 0) {
-        for (int d = 0; d < nr; d++) counts[d] = 0;
+        if (dev_counts) {
+            cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int64_t) * (size_t)nr, st);
+            if (e != cudaSuccess) return cuda_fail(e, "expert-parallel dispatch");
+        } else {
+            for (int d = 0; d < nr; d++) counts[d] = 0;
+        }
         return TLMG_OK;
     }
     int rc = batch_reserve(s, a.n, a.D, a.de, a.E, a.k);
@@ -670,6 +681,15 @@ int ep_dispatch(BatchScratch &s, const BatchArgs &a, int nr, uint8_t *send, int3
     k_epcount<<<1, 1024, 0, st>>>(s.ids, np, a.E, nr, perm, s.cnt);
     k_eppack<<<warp_blocks(np, nsm), 256, 0, st>>>(s.ids, perm, np, a.k, s.xq, qx, send, ep_record_bytes(a.D));
     count_launch(4);
+    if (dev_counts) {
+        // device counts: written on the stream, no wait (the caller's
+        // exchange of the counts is ordered after them on the same stream)
+        k_epcount64<<<1, 32, 0, st>>>(s.cnt, nr, counts);
+        count_launch(1);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e, "expert-parallel dispatch");
+        return TLMG_OK;
+    }
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);    // the record counts size the exchange
     if (e != cudaSuccess) return cuda_fail(e, "expert-parallel dispatch");

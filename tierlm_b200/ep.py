@@ -9,7 +9,8 @@ runs
 
     dispatch   home: route + quantise its tokens, one record per
                (token, rank) pair grouped by owner           (C ABI, CUDA)
-    exchange   record counts, then the records               (all-to-all)
+    exchange   record counts (kept on the device; one host read
+               of both directions), then the records         (all-to-all)
     experts    owner: the expert FFN of every received record (C ABI, CUDA)
     exchange   expert output rows back, in record order      (all-to-all)
     combine    home: ffn[t] = sum_r w[t, r] * eo[t, r], ascending r
@@ -92,14 +93,24 @@ class ExpertParallel:
         self._grow(n)
         npair = n * self.k
         send = self._send[:npair]
-        sent = self.b.ep_dispatch(layer, x, logits, self.n_ranks, send, self._perm, self._w)
+        # counts: sent[d] records go to owner d; received[s] arrive from home s
+        if self.device.type == "cuda" and hasattr(self.b, "ep_dispatch_async"):
+            # counts stay on the device through their exchange; one host read
+            # of both directions sizes the record exchange
+            sc = torch.empty(self.n_ranks, dtype=torch.int64, device=self.device)
+            self.b.ep_dispatch_async(layer, x, logits, self.n_ranks, send, self._perm, self._w, sc)
+            rc = torch.empty_like(sc)
+            self._a2a(rc, sc, None, None)
+            both = torch.cat([sc, rc]).tolist()
+            sent, received = both[:self.n_ranks], both[self.n_ranks:]
+        else:
+            sent = self.b.ep_dispatch(layer, x, logits, self.n_ranks, send, self._perm, self._w)
+            sc = torch.tensor(sent, dtype=torch.int64, device=self.device)
+            rc = torch.empty_like(sc)
+            self._a2a(rc, sc, None, None)
+            received = [int(v) for v in rc.tolist()]
         if sum(sent) != npair:
             raise RuntimeError(f"dispatch wrote {sum(sent)} records for {npair} pairs")
-        # counts: sent[d] records go to owner d; received[s] arrive from home s
-        sc = torch.tensor(sent, dtype=torch.int64, device=self.device)
-        rc = torch.empty_like(sc)
-        self._a2a(rc, sc, None, None)
-        received = [int(v) for v in rc.tolist()]
         n_rec = sum(received)
         self._grow_recv(n_rec)
         recv = self._recv[:n_rec]

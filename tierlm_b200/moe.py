@@ -190,6 +190,14 @@ class MoeContext:
                                          _ptr(perm), _ptr(w), counts))
         return list(counts)
 
+    def ep_dispatch_async(self, layer: int, x, logits, n_ranks: int, send, perm, w, counts) -> None:
+        """ep_dispatch with the per-owner record counts written to a device
+        int64 tensor on the stream; returns without waiting."""
+        if not (isinstance(counts, torch.Tensor) and counts.is_cuda and counts.dtype == torch.int64):
+            raise TypeError("counts must be a CUDA int64 tensor")
+        check(self._lib.tlmg_ep_dispatch(self._h, layer, x.shape[0], _ptr(x), _ptr(logits), n_ranks, _ptr(send),
+                                         _ptr(perm), _ptr(w), _ptr(counts)))
+
     def ep_experts(self, layer: int, e_lo: int, e_hi: int, n_rec: int, recv, eo) -> None:
         """Owner side of experts [e_lo, e_hi): n_rec received records -> eo [n_rec][D]."""
         check(self._lib.tlmg_ep_experts(self._h, layer, e_lo, e_hi, n_rec, _ptr(recv) if n_rec else None,
