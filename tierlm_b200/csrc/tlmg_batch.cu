@@ -118,15 +118,35 @@ __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids
         }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int s = 0, na = 0;
-        for (int e = 0; e < E; e++) {
+    if (threadIdx.x < 32) {
+        // warp 0: lane l owns experts [l * per, (l + 1) * per); exclusive
+        // scans of the pair counts and of the active-expert counts give the
+        // offsets and the ascending active list
+        const int lane = threadIdx.x, per = (E + 31) / 32, e0 = lane * per, e1 = min(E, e0 + per);
+        int sum = 0, act = 0;
+        for (int e = e0; e < e1; e++) {
+            sum += cnt[e];
+            act += cnt[e] != 0;
+        }
+        int xs = sum, xa = act;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int ys = __shfl_up_sync(0xffffffffu, xs, d), ya = __shfl_up_sync(0xffffffffu, xa, d);
+            if (lane >= d) {
+                xs += ys;
+                xa += ya;
+            }
+        }
+        int s = xs - sum, na = xa - act;
+        for (int e = e0; e < e1; e++) {
             off[e] = s;
             s += cnt[e];
             if (cnt[e]) grp[E + 1 + na++] = e;
         }
-        off[E] = s;
-        grp[2 * E + 1] = na;
+        if (lane == 31) {
+            off[E] = xs;
+            grp[2 * E + 1] = xa;
+        }
     }
     __syncthreads();
     for (int e = threadIdx.x; e <= E; e += blockDim.x) grp[e] = off[e];
