@@ -264,9 +264,22 @@ __global__ void k_bcombine(const float *__restrict__ eo, const int32_t *__restri
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n * D; idx += gridDim.x * blockDim.x) {
         const int t = idx / D, i = idx - t * D;
         float f = 0.0f;
-        for (int r = 0; r < k; r++) {
-            const int row = perm ? perm[t * k + r] : t * k + r;
-            f = __fadd_rn(f, __fmul_rn(w[(size_t)t * k + r], eo[(size_t)row * D + i]));
+        // ranks in groups of 8: the group's loads are issued together, then
+        // the products are added in ascending rank as before
+        for (int r0 = 0; r0 < k; r0 += 8) {
+            float wv[8], ev[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int r = r0 + j;
+                if (r < k) {
+                    const int row = perm ? perm[t * k + r] : t * k + r;
+                    wv[j] = w[(size_t)t * k + r];
+                    ev[j] = eo[(size_t)row * D + i];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (r0 + j < k) f = __fadd_rn(f, __fmul_rn(wv[j], ev[j]));
         }
         ffn[idx] = f;
     }
