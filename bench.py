@@ -45,7 +45,8 @@ BYTES_LAYER_TOKEN = K * (2 * DE * (D // 256 * 144) + D * (DE // 256 * 210))   # 
 METRIC = "expert GEMV HBM GB/s, bs=1 MoE expert FFN (Qwen3-30B-A3B layer shape, Q4_K gate/up + Q6_K down)"
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per layer-token of the persistent kernel, from one
-# ncu capture of a 4-layer-token launch (profiles/k_fused_ffn_config2.md):
+# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of a
+# 4-layer-token launch of the kernel as of commit 8075c4d:
 # 98,106,880 read + 3,531,520 written, over 4 layer-tokens.
 TRAFFIC_LAYER_TOKEN = (98_106_880 + 3_531_520) // 4
 
@@ -234,10 +235,11 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="batched-decode section: tokens per layer call (<= 1: off)")
     ap.add_argument("--prefill", type=int, default=2048, help="prefill section: prompt tokens per layer call (0: off)")
-    ap.add_argument("--cache-layers", type=int, default=8, help="slot-cache section: layers (0: off)")
+    ap.add_argument("--cache-layers", type=int, default=0, help="slot-cache section: layers (0: off)")
     ap.add_argument("--cache-frac", type=float, default=0.5, help="slot-cache section: HBM slots / experts")
-    ap.add_argument("--attn-ctx", default="768,4096,32768",
-                    help="decode-attention section: context lengths, comma-separated (empty: off)")
+    ap.add_argument("--attn-ctx", default="",
+                    help="decode-attention section: context lengths, comma-separated, e.g. 768,4096,32768 "
+                         "(empty: off)")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference" or os.environ.get("TLMG_BENCH_ALLOW_SHORT"), \
         "use at least 3 warm-up steps"
@@ -359,8 +361,8 @@ def main() -> None:
         def layer_call(layer, xi, li, oi):
             if ep is None:
                 ctx.expert_ffn_batch(layer, xi, li, oi)
-            else:
-                ep.ffn_batch(layer, xi, li, oi)
+            else:   # device errors of layer l surface in the call of l + 1, the step's last is checked
+                ep.ffn_batch(layer, xi, li, oi, check=layer == L - 1)
 
         def bstep(s):
             i = s % 2
@@ -386,7 +388,7 @@ def main() -> None:
                 else:   # the exchange needs device buffers: the copies are part of the step
                     dx_.copy_(hbx[i, layer], non_blocking=True)
                     dl_.copy_(hbl[i, layer], non_blocking=True)
-                    ep.ffn_batch(layer, dx_, dl_, do_)
+                    ep.ffn_batch(layer, dx_, dl_, do_, check=layer == L - 1)
                     hbo[i, layer].copy_(do_, non_blocking=True)
 
         for s in range(args.warmup):
@@ -408,7 +410,7 @@ def main() -> None:
 
     # ---- prefill: PREFILL tokens of one GPU's prompt through each layer's experts, one call per layer
     prefill = None
-    if args.prefill > 0:
+    if args.prefill > 0 and world == 1:
         T = args.prefill
         px = torch.randn((L, T, D), generator=g, device=dev)
         pl = torch.randn((L, T, E), generator=g, device=dev)
@@ -572,7 +574,9 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
-            "batched_decode": batch, "prefill": prefill, "slot_cache": cache, "decode_attention": attn,
+            "prefill": prefill, "slot_cache": cache, "decode_attention": attn,
+            # last key: the bs=64 (expert-parallel at N > 1) decode section
+            "batched_decode": batch,
         }
         print(json.dumps(line), flush=True)
     ctx.close()

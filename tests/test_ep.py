@@ -312,3 +312,36 @@ def test_ep_nccl_two_gpus():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert r.stdout.count("EP-OK") == 2, r.stdout[-2000:]
+
+
+@pytest.mark.gpu
+def test_ep_ffn_batch_raises_device_errors():
+    """ExpertParallel.ffn_batch on the CUDA path (device-side counts) raises
+    the error its own kernels flagged, without an explicit ctx.check(): the
+    owner range is narrowed by one expert, so records naming expert 0 are
+    foreign (NaN rows, TLMG_EINVAL). The next call with the true range
+    succeeds (the error is reported once)."""
+    from tierlm_b200 import _lib, synth
+    from tierlm_b200.ep import ExpertParallel
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(9)
+    D_, de, E_, k = 512, 256, 8, 2
+    experts = [synth.rand_expert(rng, D_, de, (12, 12, 14)) for _ in range(E_)]
+    ctx = _gpu_ctx(experts, D_, de, E_, k)
+    ep = ExpertParallel(ctx, D_, E_, k, device=dev)
+    x = torch.from_numpy(rng.standard_normal((5, D_)).astype(np.float32)).to(dev)
+    lg = torch.from_numpy(rng.standard_normal((5, E_)).astype(np.float32)).to(dev)
+    lg[:, 0] = 10.0                                          # every token routes to expert 0
+    ffn = torch.empty((5, D_), device=dev)
+    ep.lo = 1
+    with pytest.raises(_lib.TlmError) as ei:
+        ep.ffn_batch(0, x, lg, ffn)
+    assert ei.value.code == _lib.TLMG_EINVAL
+    assert torch.isnan(ffn).all(dim=1).all()
+    ep.lo = 0
+    ep.ffn_batch(0, x, lg, ffn)
+    ref = torch.empty_like(ffn)
+    ctx.expert_ffn_batch(0, x, lg, ref)
+    ctx.check()
+    assert torch.equal(ffn.view(torch.int32), ref.view(torch.int32))
+    ctx.close()

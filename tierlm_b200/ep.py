@@ -85,10 +85,19 @@ class ExpertParallel:
         else:
             dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
-    def ffn_batch(self, layer: int, x: torch.Tensor, logits: torch.Tensor, ffn: torch.Tensor) -> dict:
+    def ffn_batch(self, layer: int, x: torch.Tensor, logits: torch.Tensor, ffn: torch.Tensor,
+                  check: bool = True) -> dict:
         """x [n][D], logits [n][E] -> ffn [n][D] for this process's n tokens
         (n may be 0; every rank must call with the same layer). Returns the
-        record counts {"sent": [per owner], "received": [per home]}."""
+        record counts {"sent": [per owner], "received": [per home]}.
+
+        Errors the kernels raise on the device (a tensor-core wait that
+        expired, a received record naming an expert this GPU does not own)
+        are raised by this call: those of earlier calls once the counts are
+        back on the host, those of this call at the end when `check` is
+        true (one more stream synchronisation). A caller running many layers
+        back to back may pass check=False for all but the last layer of a
+        step: an error of layer l is then raised by the call for layer l+1."""
         n = int(x.shape[0])
         self._grow(n)
         npair = n * self.k
@@ -103,6 +112,8 @@ class ExpertParallel:
             self._a2a(rc, sc, None, None)
             both = torch.cat([sc, rc]).tolist()
             sent, received = both[:self.n_ranks], both[self.n_ranks:]
+            # the stream is idle now: report what earlier kernels flagged
+            self.b.check()
         else:
             sent = self.b.ep_dispatch(layer, x, logits, self.n_ranks, send, self._perm, self._w)
             sc = torch.tensor(sent, dtype=torch.int64, device=self.device)
@@ -120,4 +131,6 @@ class ExpertParallel:
         back = self._back[:npair]
         self._a2a(back, eo, sent, received)
         self.b.ep_combine(n, back, self._perm, self._w, ffn)
+        if check and hasattr(self.b, "check"):
+            self.b.check()
         return {"sent": sent, "received": received}
