@@ -198,6 +198,15 @@ int tlmg_set_layer(tlmg_ctx *ctx, int layer, const float *ffn_norm, int router_d
 int tlmg_set_shared(tlmg_ctx *ctx, int layer, const int32_t dt[3], const void *gate,
                     const void *up, const void *down, const float *gate_inp);
 
+/* Dense-FFN layer (the has_dense_ffn branch of moe(), src/lib/tlm_model.c:
+ * 947-964: first_k_dense_replace / mlp_only layers): gate/up [d_ffn x D]
+ * and down [D x d_ffn] with dtypes dt[3], HOST pointers, rows packed
+ * (tlmg_row_bytes). tlmg_moe_layer on such a layer runs RMSNorm, the SwiGLU
+ * FFN and h += ffn, with no router, experts or shared expert (and reports
+ * no ids / weights). The layer still needs its ffn_norm (tlmg_set_layer). */
+int tlmg_set_dense_ffn(tlmg_ctx *ctx, int layer, int d_ffn, const int32_t dt[3], const void *gate,
+                       const void *up, const void *down);
+
 /* Routed-expert FFN of one token (run_batch + rank-ordered combine,
  * src/lib/tlm_model.c:900-938, :1029-1036): x = normalised input f32[D],
  * logits f32[E]; ffn f32[D] receives sum_r w[r] * down_r(SiLU(gate_r x) *
@@ -268,6 +277,14 @@ int tlmg_ep_combine(tlmg_ctx *ctx, int n_tok, const float *back, const int32_t *
  * RMSNorm, router matvec, route, experts, shared expert, h += ffn.
  * h: f32[D] in/out; ids/w may be NULL. Host or device pointers. */
 int tlmg_moe_layer(tlmg_ctx *ctx, int layer, float *h, int32_t *ids, float *w);
+
+/* tlmg_moe_layer that also returns onorm f32[top_k] (may be NULL): per rank
+ * r, (float)sqrt(sum_i (double)c * c) over c = w[r] * eo_r[i], the output
+ * norms moe() hands to the route hook (src/lib/tlm_model.c:1029-1039,
+ * :1053; tlm_route_hook, src/lib/tlm_model.h:62-70). Asking for onorm runs
+ * this call on the multi-kernel expert path (the same bits). ids, w and
+ * onorm are left untouched on a dense-FFN layer. */
+int tlmg_moe_layer_ex(tlmg_ctx *ctx, int layer, float *h, int32_t *ids, float *w, float *onorm);
 
 /* Run the context's work on `stream` (a cudaStream_t passed as void *) from
  * now on; NULL returns to the context's own stream. Lets a caller order the

@@ -34,7 +34,8 @@ class Geom(C.Structure):
 class Layer(C.Structure):
     _fields_ = [("ffn_norm", _P), ("router_dt", C.c_int32), ("router_w", _P), ("router_rb", _SZ),
                 ("router_bias", _P), ("mask", _P), ("experts", C.POINTER(Expert)), ("has_shared", C.c_int32),
-                ("sh_dt", C.c_int32 * 3), ("sh_w", _P * 3), ("shared_gate_inp", _P)]
+                ("sh_dt", C.c_int32 * 3), ("sh_w", _P * 3), ("shared_gate_inp", _P),
+                ("has_dense", C.c_int32), ("d_ffn", C.c_int32), ("dn_dt", C.c_int32 * 3), ("dn_w", _P * 3)]
 
 
 _SIGS = {
@@ -55,6 +56,7 @@ _SIGS = {
     "tlmo_route": (None, [_I, _P, _P, _P, _I, _I, _F, _P, _P]),
     "tlmo_expert_ffn": (_I, [C.POINTER(Geom), C.POINTER(Expert), _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "tlmo_moe_layer": (_I, [C.POINTER(Geom), C.POINTER(Layer), _P, _P, _P]),
+    "tlmo_moe_layer_ex": (_I, [C.POINTER(Geom), C.POINTER(Layer), _P, _P, _P, _P]),
     "tlmo_rmsnorm": (None, [_P, _P, _P, _I64, _F]),
     "tlmo_decode_attention": (None, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
 }
@@ -213,8 +215,10 @@ def expert_ffn(geom: dict, experts: list[tuple[np.ndarray, tuple, tuple]], x: np
     return (ffn, ids, w, eo, hb) if want_intermediates else (ffn, ids, w)
 
 
-def moe_layer(geom: dict, layer: dict, experts, h: np.ndarray):
-    """The whole moe() block on a copy of h; returns (h_out, ids, w)."""
+def moe_layer(geom: dict, layer: dict, experts, h: np.ndarray, want_onorm: bool = False):
+    """The whole moe() block on a copy of h; returns (h_out, ids, w), plus
+    the route hook's output norms with want_onorm. layer["dense"] = (dts,
+    mats, d_ffn) makes it a dense-FFN layer."""
     g = Geom(geom["d_model"], geom["d_expert"], geom.get("d_shared", 0), geom["n_experts"], geom["top_k"],
              geom.get("router", 0), geom.get("routed_scale", 1.0), geom.get("norm_eps", 1e-6))
     arr = (Expert * max(len(experts), 1))()
@@ -240,10 +244,19 @@ def moe_layer(geom: dict, layer: dict, experts, h: np.ndarray):
         for m in range(3):
             keep.append(mats[m])
             L.sh_w[m] = mats[m].ctypes.data
+    if layer.get("dense") is not None:
+        dts, mats, d_ffn = layer["dense"]
+        L.has_dense = 1
+        L.d_ffn = d_ffn
+        L.dn_dt[:] = list(dts)
+        for m in range(3):
+            keep.append(mats[m])
+            L.dn_w[m] = mats[m].ctypes.data
     h = np.array(h, np.float32, copy=True)
     k = max(g.top_k, 1)
     ids = np.zeros(k, np.int32)
     w = np.zeros(k, np.float32)
-    rc = lib().tlmo_moe_layer(C.byref(g), C.byref(L), _p(h), _p(ids), _p(w))
+    onorm = np.zeros(k, np.float32)
+    rc = lib().tlmo_moe_layer_ex(C.byref(g), C.byref(L), _p(h), _p(ids), _p(w), _p(onorm) if want_onorm else None)
     assert rc == 0
-    return h, ids, w
+    return (h, ids, w, onorm) if want_onorm else (h, ids, w)

@@ -639,11 +639,24 @@ int tlmo_expert_ffn(const tlmo_geom *g, const tlmo_expert *experts, const uint8_
 }
 
 int tlmo_moe_layer(const tlmo_geom *g, const tlmo_layer *L, float *h, int *ids, float *w) {
-    int D = g->d_model, E = g->n_experts;
+    return tlmo_moe_layer_ex(g, L, h, ids, w, NULL);
+}
+
+int tlmo_moe_layer_ex(const tlmo_geom *g, const tlmo_layer *L, float *h, int *ids, float *w, float *onorm) {
+    int D = g->d_model, E = g->n_experts, k = g->top_k;
     float *xb = (float *)malloc(sizeof(float) * (size_t)D);
     float *ffn = (float *)malloc(sizeof(float) * (size_t)D);
     float *logits = (float *)malloc(sizeof(float) * (size_t)(E > 0 ? E : 1));
     tlmo_rmsnorm(xb, h, L->ffn_norm, D, g->norm_eps);
+    if (L->has_dense) {   /* tlm_model.c:947-964: SwiGLU block, h += ffn, no router */
+        float *hb = (float *)malloc(sizeof(float) * (size_t)L->d_ffn);
+        const uint8_t *mats[3] = { (const uint8_t *)L->dn_w[0], (const uint8_t *)L->dn_w[1],
+                                   (const uint8_t *)L->dn_w[2] };
+        swiglu_block(D, L->d_ffn, L->dn_dt, mats, xb, hb, ffn);
+        for (int i = 0; i < D; i++) h[i] += ffn[i];
+        free(hb); free(xb); free(ffn); free(logits);
+        return 0;
+    }
     for (int i = 0; i < D; i++) ffn[i] = 0.0f;
     int rc = 0;
     if (E > 0) {
@@ -652,7 +665,24 @@ int tlmo_moe_layer(const tlmo_geom *g, const tlmo_layer *L, float *h, int *ids, 
         tlmo_quantize_act(kr, xb, D, ar);
         tlmo_matvec_rows(L->router_dt, L->router_w, L->router_rb, ar, logits, D, 0, E);
         free(ar);
-        rc = tlmo_expert_ffn(g, L->experts, L->mask, L->router_bias, xb, logits, ffn, ids, w, NULL, NULL);
+        int rid[64];
+        float rw[64];
+        float *eo = onorm ? (float *)malloc(sizeof(float) * (size_t)k * D) : NULL;
+        rc = tlmo_expert_ffn(g, L->experts, L->mask, L->router_bias, xb, logits, ffn, rid, rw, eo, NULL);
+        if (rc == 0) {
+            if (ids) memcpy(ids, rid, sizeof(int) * (size_t)k);
+            if (w) memcpy(w, rw, sizeof(float) * (size_t)k);
+        }
+        if (rc == 0 && onorm)
+            for (int r = 0; r < k; r++) {
+                double nn = 0.0;
+                for (int i = 0; i < D; i++) {
+                    float c = rw[r] * eo[(size_t)r * D + i];
+                    nn += (double)c * (double)c;
+                }
+                onorm[r] = (float)sqrt(nn);
+            }
+        free(eo);
     }
     if (rc == 0 && L->has_shared && g->d_shared > 0) {
         int ds = g->d_shared;

@@ -96,6 +96,10 @@ typedef struct {
     int32_t            sh_dt[3];
     const void        *sh_w[3];           /* gate [ds x D], up [ds x D], down [D x ds] */
     const float       *shared_gate_inp;   /* [D] or NULL */
+    int32_t            has_dense;         /* dense-FFN layer: no router, experts or shared expert */
+    int32_t            d_ffn;
+    int32_t            dn_dt[3];
+    const void        *dn_w[3];           /* gate [d_ffn x D], up [d_ffn x D], down [D x d_ffn] */
 } tlmo_layer;
 
 /* Routed-expert FFN for one token (run_batch + the rank-ordered combine,
@@ -110,6 +114,11 @@ int tlmo_expert_ffn(const tlmo_geom *g, const tlmo_expert *experts, const uint8_
 /* The whole moe() block (src/lib/tlm_model.c:940-1055) without the store:
  * RMSNorm, router matvec, route, experts, shared expert, h += ffn. */
 int tlmo_moe_layer(const tlmo_geom *g, const tlmo_layer *L, float *h, int *ids, float *w);
+/* The same plus the route hook's per-rank output norms onorm [top_k]
+ * (src/lib/tlm_model.c:1029-1039): (float)sqrt of the double sum, in index
+ * order, of c*c over c = w[r]*eo_r[i]. onorm may be NULL. A dense-FFN layer
+ * (src/lib/tlm_model.c:947-964) leaves ids / w / onorm untouched. */
+int tlmo_moe_layer_ex(const tlmo_geom *g, const tlmo_layer *L, float *h, int *ids, float *w, float *onorm);
 
 /* RMSNorm (src/lib/tlm_model.c:164-169). */
 void tlmo_rmsnorm(float *out, const float *x, const float *w, int64_t n, float eps);

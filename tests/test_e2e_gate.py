@@ -1,0 +1,186 @@
+"""End-to-end gate of the quantised MoE decoder step.
+
+The reference's own decoder step runs on stores made by the reference's own
+`tlmc synth` + `tlmc compile --profile exact` (oracle/gate.py,
+oracle/ref_gate.c), once as is (tlm_model_step, src/lib/tlm_model.c:
+1058-1103) and once with every moe() (src/lib/tlm_model.c:940-1055) served by
+libtlmg's tlmg_moe_layer_ex on the GPU, through the C ABI. Embedding,
+attention and lm_head stay on the reference's CPU code in both.
+
+- north_star's gate, with the reference as built (libm expf): the 64-token
+  xorshift-42 prompt of `tierlm bench` (src/bin/tierlm.c:711-715) and 64
+  greedy tokens give the same tokens; teacher-forced, every position has
+  the same argmax and logits within LOGIT_RTOL relative L2.
+- With the reference's expf bound to a correctly rounded expf (the one the
+  CUDA tier computes): every logit of every position is bit-identical, and
+  so are the route hook's ids, weights and output norms.
+- tests/golden/moe_ref.npz holds the reference's moe() outputs on these
+  stores; the CPU oracle and the GPU reproduce them.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import gate as G
+
+LOGIT_RTOL = 1e-3      # north_star: logits within 1e-3 relative L2 (per position)
+FFN_RTOL = 1e-5        # one moe() block under libm expf vs the correctly rounded one
+ROUTE_RTOL = 3e-7      # routing weights under libm expf vs the correctly rounded one
+PROMPT, N_GEN = 64, 64
+
+pytestmark = pytest.mark.skipif(not G.available(), reason="oracle/_ref gate not built (make -C oracle gate)")
+
+GOLDEN = None
+
+
+def golden():
+    global GOLDEN
+    if GOLDEN is None:
+        from pathlib import Path
+        z = np.load(Path(__file__).resolve().parent / "golden" / "moe_ref.npz")
+        GOLDEN = [{k: z[f"{k}_{i}"] for k in ("store", "sha", "cr", "layer", "h", "h_out", "ids", "w", "onorm")}
+                  for i in range(int(z["count"]))]
+    return GOLDEN
+
+
+def bits(a):
+    return np.ascontiguousarray(a, np.float32).view(np.uint32)
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b) / max(np.linalg.norm(b.astype(np.float64)), 1e-30))
+
+
+# ---------------------------------------------------------------- CPU
+@pytest.mark.parametrize("name", list(G.STORES))
+def test_restated_step_is_the_reference(name):
+    """The step the GPU arm uses (tlm_model_step restated with the MoE block
+    swappable) gives the reference's logits bit for bit with moe() on the CPU."""
+    with G.Gate(name) as g:
+        seq = G.xorshift_prompt(16, g.vocab)
+        a = g.teacher(G.REF, seq)
+        b = g.teacher(G.CPU, seq)
+    assert np.array_equal(bits(a), bits(b))
+
+
+def test_golden_stores_are_the_pinned_ones():
+    """The stores tlmc rebuilds here hold the bytes the golden was made on."""
+    for name in {str(c["store"]) for c in golden()}:
+        sha = {str(c["sha"]) for c in golden() if str(c["store"]) == name}
+        assert sha == {G.store_sha256(name)}, name
+
+
+@pytest.mark.parametrize("name", list(G.STORES))
+def test_oracle_moe_matches_reference_golden(name):
+    """oracle.moe_layer (the C restatement) on the store's tensors reproduces
+    the reference's moe() bit for bit, ids / weights / output norms included,
+    under both expf builds (the oracle's expf mode follows)."""
+    import oracle
+    cases = [c for c in golden() if str(c["store"]) == name]
+    assert cases
+    with G.Gate(name) as g:
+        layers = {l_: g.oracle_layer(l_) for l_ in range(g.n_layers)}
+        geom = g.geom()
+    try:
+        for c in cases:
+            oracle.set_expf_mode(int(c["cr"]))
+            lay, ex = layers[int(c["layer"])]
+            h, ids, w, on = oracle.moe_layer(geom, lay, ex, c["h"], want_onorm=True)
+            assert np.array_equal(bits(h), bits(c["h_out"])), (name, int(c["layer"]), int(c["cr"]))
+            if "dense" in lay:
+                assert (c["ids"] == -1).all()            # moe() returns before the route hook
+                continue
+            assert np.array_equal(ids, c["ids"])
+            assert np.array_equal(bits(w), bits(c["w"]))
+            assert np.array_equal(bits(on), bits(c["onorm"]))
+    finally:
+        oracle.set_expf_mode(0)
+
+
+# ---------------------------------------------------------------- GPU
+def _gpu_gate(name, cr):
+    g = G.Gate(name, cr=cr)
+    g.attach_gpu(0)
+    return g
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(G.STORES))
+def test_gpu_moe_matches_reference_golden(name):
+    """tlmg_moe_layer_ex on the GPU against the reference's moe() golden:
+    bit-identical with the correctly rounded expf; with libm expf the same
+    ids, weights within ROUTE_RTOL and h within FFN_RTOL relative L2."""
+    for cr in (True, False):
+        cases = [c for c in golden() if str(c["store"]) == name and int(c["cr"]) == int(cr)]
+        with _gpu_gate(name, cr) as g:
+            for c in cases:
+                h, ids, w, on = g.moe(G.GPU, int(c["layer"]), c["h"])
+                dense = (c["ids"] == -1).all()
+                if cr:
+                    assert np.array_equal(bits(h), bits(c["h_out"])), (name, int(c["layer"]))
+                    if not dense:
+                        assert np.array_equal(ids, c["ids"])
+                        assert np.array_equal(bits(w), bits(c["w"]))
+                        assert np.array_equal(bits(on), bits(c["onorm"]))
+                else:
+                    assert rel_l2(h - c["h"], c["h_out"] - c["h"]) <= FFN_RTOL
+                    if not dense:
+                        assert np.array_equal(ids, c["ids"])
+                        np.testing.assert_allclose(w, c["w"], rtol=ROUTE_RTOL)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(G.STORES))
+def test_greedy_and_teacher_forced_gate(name):
+    """north_star's config-1 gate with the reference as built (libm expf):
+    64 prompt tokens (tierlm bench's xorshift-42 prompt) then 64 greedy
+    tokens give the same tokens with moe() on the GPU; teacher-forced over
+    that sequence every position has the same argmax and logits within
+    LOGIT_RTOL relative L2, and the top-10 ids (tierlm oracle's report,
+    src/bin/tierlm.c:670-700) agree wherever their scores are apart."""
+    with _gpu_gate(name, False) as g:
+        prompt = G.xorshift_prompt(PROMPT, g.vocab)
+        t_ref, l_ref = g.generate(G.REF, prompt, N_GEN)
+        t_gpu, l_gpu = g.generate(G.GPU, prompt, N_GEN)
+        assert np.array_equal(t_ref, t_gpu), (t_ref, t_gpu)
+        for i in range(l_ref.shape[0]):
+            assert rel_l2(l_gpu[i], l_ref[i]) <= LOGIT_RTOL, i
+        seq = np.concatenate([prompt, t_ref])
+        f_ref = g.teacher(G.REF, seq)
+        f_gpu = g.teacher(G.GPU, seq)
+    assert np.array_equal(f_ref.argmax(1), f_gpu.argmax(1))
+    worst = max(rel_l2(f_gpu[i], f_ref[i]) for i in range(len(seq)))
+    assert worst <= LOGIT_RTOL, worst
+    for i in range(len(seq)):
+        top = np.argsort(-f_ref[i], kind="stable")[:10]
+        gaps = np.abs(np.diff(f_ref[i][top]))
+        if (gaps > 1e-3 * np.abs(f_ref[i][top[0]])).all():
+            assert np.array_equal(top, np.argsort(-f_gpu[i], kind="stable")[:10]), i
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(G.STORES))
+def test_bit_identical_with_correctly_rounded_expf(name):
+    """With the reference's expf correctly rounded, the GPU-served decoder
+    gives the reference's logits bit for bit at every position of a greedy
+    run and of a teacher-forced run, and the route hook sees the same ids,
+    weights and output norms in every layer."""
+    with _gpu_gate(name, True) as g:
+        prompt = G.xorshift_prompt(PROMPT, g.vocab)
+        t_ref, l_ref = g.generate(G.REF, prompt, N_GEN)
+        t_gpu, l_gpu = g.generate(G.GPU, prompt, N_GEN)
+        assert np.array_equal(t_ref, t_gpu)
+        assert np.array_equal(bits(l_ref), bits(l_gpu))
+        seq = np.concatenate([prompt[:8], t_ref[:8]])
+        hooks = {}
+        for mode in (G.REF, G.GPU):
+            g.hook(True)
+            f = g.teacher(mode, seq)
+            hooks[mode] = (f, [g.hook_read(l_) for l_ in range(g.n_layers)])
+            g.hook(False)
+    assert np.array_equal(bits(hooks[G.REF][0]), bits(hooks[G.GPU][0]))
+    for (n_a, ia, wa, oa), (n_b, ib, wb, ob) in zip(hooks[G.REF][1], hooks[G.GPU][1]):
+        assert n_a == n_b
+        if n_a:
+            assert np.array_equal(ia, ib) and np.array_equal(bits(wa), bits(wb)) and np.array_equal(bits(oa), bits(ob))

@@ -84,6 +84,8 @@ _SIGS = {
     "tlmg_ep_experts": (_I, [_P, _I, _I, _I, _I64, _P, _P]),
     "tlmg_ep_combine": (_I, [_P, _I, _P, _P, _P, _P]),
     "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
+    "tlmg_moe_layer_ex": (_I, [_P, _I, _P, _P, _P, _P]),
+    "tlmg_set_dense_ffn": (_I, [_P, _I, _I, _P, _P, _P, _P]),
     "tlmg_set_stream": (_I, [_P, _P]),
     "tlmg_set_fused": (_I, [_P, _I]),
     "tlmg_set_batch_kernels": (_I, [_P, _I]),

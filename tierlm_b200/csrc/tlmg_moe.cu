@@ -67,6 +67,13 @@ struct Layer {
     int sh_dt[3] = { 0, 0, 0 };
     void *sh_w[3] = { nullptr, nullptr, nullptr };
     float *sh_gate_inp = nullptr;
+    // dense-FFN layer (no router, no experts): gate/up [d_ffn x D], down [D x d_ffn]
+    bool has_dense = false;
+    int d_ffn = 0;
+    int dn_dt[3] = { 0, 0, 0 };
+    void *dn_w[3] = { nullptr, nullptr, nullptr };
+    float *dn_gu = nullptr, *dn_h = nullptr, *dn_out = nullptr;   // [2 d_ffn], [d_ffn], [D]
+    uint8_t *dn_hq = nullptr;
 };
 
 }  // namespace tlmg
@@ -89,6 +96,8 @@ struct tlmg_ctx {
     size_t hq_stride = 0;
     float *sg = nullptr, *sh = nullptr, *s_out = nullptr, *sgate = nullptr;
     uint8_t *shq = nullptr;
+    float *cw = nullptr;           // [top_k][D] weighted expert outputs w[r] * eo_r (output norms)
+    float *onorm = nullptr;        // [64] per-rank output norms
     // many-token scratch
     float *mx = nullptr, *mlog = nullptr, *mffn = nullptr;
     int m_cap = 0;
@@ -276,7 +285,7 @@ __global__ void k_quant_h(const Slot *__restrict__ slots, const int32_t *__restr
 __global__ void __launch_bounds__(FFN_WARPS * 32)
 k_ffn_down(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, const float *__restrict__ w, int k,
            int D, int de, const uint8_t *__restrict__ hq, size_t hq_stride, const float *__restrict__ s_out,
-           const float *__restrict__ sgate, float *__restrict__ ffn, float *__restrict__ h) {
+           const float *__restrict__ sgate, float *__restrict__ ffn, float *__restrict__ h, float *__restrict__ cw = nullptr) {
     __shared__ BlockPart part[FFN_WARPS][FCHUNK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = blockIdx.x * FFN_WARPS + warp; i < D; i += gridDim.x * FFN_WARPS) {
@@ -286,7 +295,9 @@ k_ffn_down(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, cons
             int dt = s.dt[2];
             size_t rb = (size_t)(de / dt_block(dt)) * dt_block_bytes(dt);
             float eo = warp_row_dot(dt, s.m[2] + (size_t)i * rb, hq + hq_stride * r, de / dt_block(dt), part[warp], lane);
-            acc = __fadd_rn(acc, __fmul_rn(w[r], eo));
+            const float c = __fmul_rn(w[r], eo);
+            if (cw && lane == 0) cw[(size_t)r * D + i] = c;
+            acc = __fadd_rn(acc, c);
         }
         if (lane == 0) {
             if (s_out) acc = __fadd_rn(acc, __fmul_rn(*sgate, s_out[i]));
@@ -343,6 +354,38 @@ __global__ void k_shared_gate(const float *__restrict__ g, const float *__restri
     float d = 0.0f;
     for (int i = 0; i < n; i++) d = __fadd_rn(d, __fmul_rn(g[i], x[i]));
     *out = sigmoid_f(d);
+}
+
+// onorm[r] = (float)sqrt(sum_i (double)c[i] * c[i]) over c = cw[r][0..D) (the
+// per-rank output norm moe() hands to the route hook, reference
+// tlm_model.c:1029-1039), one warp per rank. The reference sums in index
+// order; every term is exact in double and nonnegative, so a tree sum is
+// within (2D + 8) * 2^-53 of it (relative), and when both ends of that
+// interval give the same float the result is the reference's; otherwise
+// lane 0 redoes the sequential sum.
+__global__ void k_onorm(const float *__restrict__ cw, int D, float *__restrict__ onorm) {
+    const int r = blockIdx.x, lane = threadIdx.x;
+    const float *c = cw + (size_t)r * D;
+    double s = 0.0;
+    for (int i = lane; i < D; i += 32) s = __dadd_rn(s, __dmul_rn((double)c[i], (double)c[i]));
+    for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
+    if (lane != 0) return;
+    const double bound = __dmul_rn(s, __dmul_rn(2.0 * (double)D + 8.0, 0x1p-53));
+    const float lo = __double2float_rn(__dsqrt_rn(fmax(__dsub_rn(s, bound), 0.0)));
+    const float hi = __double2float_rn(__dsqrt_rn(__dadd_rn(s, bound)));
+    if (lo == hi) {
+        onorm[r] = lo;
+        return;
+    }
+    double q = 0.0;
+    for (int i = 0; i < D; i++) q = __dadd_rn(q, __dmul_rn((double)c[i], (double)c[i]));
+    onorm[r] = __double2float_rn(__dsqrt_rn(q));
+}
+
+// h[i] += y[i] (the residual update of moe(), reference tlm_model.c:963, :1049).
+__global__ void k_add(float *__restrict__ h, const float *__restrict__ y, int n) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = __fadd_rn(h[i], y[i]);
 }
 
 static int launched(const char *what) {
@@ -466,11 +509,11 @@ static int cache_route_acquire(tlmg_ctx *c, int layer) {
 // Routed experts for one token on the device: logits -> ids/w -> ffn (and
 // h += ffn when h != NULL). Inputs already quantised in xq8k / xq80.
 static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, float *h, const float *s_out,
-                       const float *sgate, const float *x) {
+                       const float *sgate, const float *x, float *cw = nullptr) {
     const tlmg_geom &g = c->g;
     Layer &Ly = c->L[layer];
     prof_bytes(c, Ly);
-    if (use_fused_path(c, Ly, x)) {
+    if (!cw && use_fused_path(c, Ly, x)) {
         FusedArgs a = fused_args(c, Ly, layer, 1);
         a.x = x;
         a.logits = logits;
@@ -504,7 +547,7 @@ static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, 
     if ((rc = launched("ffn requant"))) return rc;
     prof_mark(c, 1, true);
     k_ffn_down<<<(unsigned)std::min(148 * 8, (D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, c->st>>>(
-        Ly.d_slots, c->ids, c->w, k, D, de, c->hq, c->hq_stride, s_out, sgate, ffn, h);
+        Ly.d_slots, c->ids, c->w, k, D, de, c->hq, c->hq_stride, s_out, sgate, ffn, h, cw);
     prof_mark(c, 1, false);
     if ((rc = launched("ffn down"))) return rc;
     return Ly.cached ? cache_mark_used(c->cache, layer, c->pin_ids, k, c->st) : TLMG_OK;
@@ -610,7 +653,8 @@ int tlmg_open(const tlmg_geom *g, int device, tlmg_ctx **out) {
               (c->ids = (int32_t *)dalloc(c, 4 * 64)) && (c->w = (float *)dalloc(c, 4 * 64)) &&
               (c->sg = (float *)dalloc(c, 8 * (size_t)ds)) && (c->sh = (float *)dalloc(c, 4 * (size_t)ds)) &&
               (c->s_out = (float *)dalloc(c, 4 * (size_t)D)) && (c->sgate = (float *)dalloc(c, 16)) &&
-              (c->shq = (uint8_t *)dalloc(c, std::max(tlmg_qact_bytes(DT_Q8_K, ds), tlmg_qact_bytes(DT_Q8_0, ds)) + 256));
+              (c->shq = (uint8_t *)dalloc(c, std::max(tlmg_qact_bytes(DT_Q8_K, ds), tlmg_qact_bytes(DT_Q8_0, ds)) + 256)) &&
+              (c->cw = (float *)dalloc(c, 4 * (size_t)k * D)) && (c->onorm = (float *)dalloc(c, 4 * 64));
     if (ok) ok = ensure_pin(c, 4 * (size_t)(2 * D + E + 2 * 64) + 1024) == TLMG_OK;
     if (ok) ok = fused_init(c->fused, *g) == TLMG_OK;
     if (!ok) {
@@ -943,6 +987,37 @@ int tlmg_set_shared(tlmg_ctx *c, int layer, const int32_t dt[3], const void *gat
     return TLMG_OK;
 }
 
+int tlmg_set_dense_ffn(tlmg_ctx *c, int layer, int d_ffn, const int32_t dt[3], const void *gate, const void *up_w,
+                       const void *down) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!dt || !gate || !up_w || !down || d_ffn <= 0) return set_error(TLMG_EINVAL, "set_dense_ffn: bad argument");
+    cudaSetDevice(c->device);
+    const int D = c->g.d_model;
+    Layer &Ly = c->L[layer];
+    if (Ly.has_dense) return set_error(TLMG_EBUSY, "set_dense_ffn: layer %d already has a dense FFN", layer);
+    const void *src[3] = { gate, up_w, down };
+    for (int m = 0; m < 3; m++) {
+        int q = dt_block(dt[m]);
+        if (!q || (m < 2 ? D : d_ffn) % q) return set_error(TLMG_EUNSUP, "set_dense_ffn: bad dtype %d", dt[m]);
+    }
+    for (int m = 0; m < 3; m++) {
+        size_t bytes = m < 2 ? (size_t)d_ffn * tlmg_row_bytes(dt[m], D) : (size_t)D * tlmg_row_bytes(dt[m], d_ffn);
+        void *p = dalloc(c, bytes + 256);
+        if (!p || cudaMemcpy(p, src[m], bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+            return set_error(TLMG_EIO, "set_dense_ffn: upload failed");
+        Ly.dn_w[m] = p;
+        Ly.dn_dt[m] = dt[m];
+    }
+    const size_t hq = std::max(tlmg_qact_bytes(DT_Q8_K, d_ffn), tlmg_qact_bytes(DT_Q8_0, d_ffn)) + 256;
+    if (!(Ly.dn_gu = (float *)dalloc(c, 8 * (size_t)d_ffn)) || !(Ly.dn_h = (float *)dalloc(c, 4 * (size_t)d_ffn)) ||
+        !(Ly.dn_out = (float *)dalloc(c, 4 * (size_t)D)) || !(Ly.dn_hq = (uint8_t *)dalloc(c, hq)))
+        return set_error(TLMG_ENOMEM, "set_dense_ffn: scratch");
+    Ly.d_ffn = d_ffn;
+    Ly.has_dense = true;
+    return TLMG_OK;
+}
+
 int tlmg_expert_ffn(tlmg_ctx *c, int layer, const float *x, const float *logits, float *ffn, int32_t *ids,
                     float *w) {
     int rc = check_layer(c, layer);
@@ -1205,14 +1280,42 @@ int tlmg_ep_combine(tlmg_ctx *c, int n_tok, const float *back, const int32_t *pe
     return ep_combine(n_tok, c->g.d_model, c->g.top_k, back, perm, w, ffn, c->st);
 }
 
-int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
+}  // extern "C"
+
+namespace tlmg {
+
+// The dense-FFN branch of moe() (reference tlm_model.c:947-964) on the
+// normalised input in c->x (already quantised): gate/up, SiLU(g) * u,
+// re-quantise, down, h += ffn.
+static int dense_ffn(tlmg_ctx *c, Layer &Ly, float *dh) {
+    const int D = c->g.d_model, F = Ly.d_ffn;
+    int rc;
+    for (int m = 0; m < 2; m++) {
+        int dt = Ly.dn_dt[m];
+        const void *act = act_kind_for(dt) == DT_Q8_0 ? (const void *)c->xq80
+                        : act_kind_for(dt) == DT_F32 ? (const void *)c->x : (const void *)c->xq8k;
+        if ((rc = launch_matvec(dt, Ly.dn_w[m], tlmg_row_bytes(dt, D), act, Ly.dn_gu + (size_t)m * F, D, 0, F, c->st)))
+            return rc;
+    }
+    k_swiglu<<<(F + 255) / 256, 256, 0, c->st>>>(Ly.dn_gu, F, Ly.dn_h);
+    if ((rc = launched("dense swiglu"))) return rc;
+    const int dd = Ly.dn_dt[2], kd = act_kind_for(dd);
+    if ((rc = launch_quant_act(kd, Ly.dn_h, F, Ly.dn_hq, c->st))) return rc;
+    if ((rc = launch_matvec(dd, Ly.dn_w[2], tlmg_row_bytes(dd, F), kd == DT_F32 ? (const void *)Ly.dn_h : Ly.dn_hq,
+                            Ly.dn_out, F, 0, D, c->st)))
+        return rc;
+    k_add<<<(D + 255) / 256, 256, 0, c->st>>>(dh, Ly.dn_out, D);
+    return launched("dense residual");
+}
+
+static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w, float *onorm) {
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (!h) return set_error(TLMG_EINVAL, "moe_layer: NULL h");
     cudaSetDevice(c->device);
     Layer &Ly = c->L[layer];
     const tlmg_geom &g = c->g;
-    const int D = g.d_model, E = g.n_experts, k = g.top_k;
+    const int D = g.d_model, E = Ly.has_dense ? 0 : g.n_experts, k = g.top_k;
     if (!Ly.ffn_norm) return set_error(TLMG_ENOTFOUND, "moe_layer: layer %d has no ffn_norm", layer);
     if (E > 0 && !Ly.router_w) return set_error(TLMG_ENOTFOUND, "moe_layer: layer %d has no router", layer);
     PtrKind kh = ptr_kind(h);
@@ -1225,6 +1328,15 @@ int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
     k_rmsnorm<<<1, 256, 0, c->st>>>(dh, Ly.ffn_norm, D, g.norm_eps, c->x);
     if ((rc = launched("rmsnorm"))) return rc;
     if ((rc = quant_inputs(c, c->x))) return rc;
+    if (Ly.has_dense) {
+        // no router, no experts, no shared expert, no route hook (moe() returns early)
+        if ((rc = dense_ffn(c, Ly, dh))) return rc;
+        if (kh != PK_DEVICE) {
+            if ((rc = d2h(c, h, dh, 4 * (size_t)D, kh, 0)) || (rc = stream_sync(c))) return rc;
+            finish_d2h(c, h, 4 * (size_t)D, kh, 0);
+        }
+        return TLMG_OK;
+    }
     const float *s_out = nullptr, *sgate = nullptr;
     if (Ly.has_shared && g.d_shared > 0) {
         const int ds = g.d_shared;
@@ -1258,11 +1370,15 @@ int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
         int kr = act_kind_for(Ly.router_dt);
         const void *ract = kr == DT_F32 ? (const void *)c->x : kr == DT_Q8_0 ? (const void *)c->xq80 : (const void *)c->xq8k;
         if ((rc = launch_matvec(Ly.router_dt, Ly.router_w, Ly.router_rb, ract, c->logits, D, 0, E, c->st))) return rc;
-        if ((rc = run_experts(c, layer, c->logits, c->ffn, dh, s_out, sgate, c->x))) return rc;
+        if ((rc = run_experts(c, layer, c->logits, c->ffn, dh, s_out, sgate, c->x, onorm ? c->cw : nullptr))) return rc;
+        if (onorm) {
+            k_onorm<<<k, 32, 0, c->st>>>(c->cw, D, c->onorm);
+            if ((rc = launched("output norms"))) return rc;
+        }
     } else if (s_out) {
         // no routed experts: ffn = sgate * s_out, h += ffn
         k_ffn_down<<<(unsigned)((D + FFN_WARPS - 1) / FFN_WARPS), FFN_WARPS * 32, 0, c->st>>>(
-            Ly.d_slots, c->ids, c->w, 0, D, g.d_expert, c->hq, c->hq_stride, s_out, sgate, c->ffn, dh);
+            Ly.d_slots, c->ids, c->w, 0, D, g.d_expert, c->hq, c->hq_stride, s_out, sgate, c->ffn, dh, nullptr);
         if ((rc = launched("shared combine"))) return rc;
     }
     if (kh != PK_DEVICE) {
@@ -1277,13 +1393,33 @@ int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
         if (is_device_ptr(w)) cudaMemcpyAsync(w, c->w, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st);
         else cudaMemcpyAsync(c->pin + o_w, c->w, 4 * (size_t)k, cudaMemcpyDeviceToHost, c->st);
     }
-    if (kh != PK_DEVICE || (ids && !is_device_ptr(ids)) || (w && !is_device_ptr(w))) {
+    const float *d_onorm = c->onorm;
+    const size_t o_on = o_w + 256;
+    if (onorm && E > 0) {
+        if (is_device_ptr(onorm)) cudaMemcpyAsync(onorm, d_onorm, 4 * (size_t)k, cudaMemcpyDeviceToDevice, c->st);
+        else cudaMemcpyAsync(c->pin + o_on, d_onorm, 4 * (size_t)k, cudaMemcpyDeviceToHost, c->st);
+    }
+    if (kh != PK_DEVICE || (ids && !is_device_ptr(ids)) || (w && !is_device_ptr(w)) ||
+        (onorm && !is_device_ptr(onorm))) {
         if ((rc = stream_sync(c))) return rc;
         if (kh != PK_DEVICE) finish_d2h(c, h, 4 * (size_t)D, kh, 0);
         if (ids && E > 0 && !is_device_ptr(ids)) memcpy(ids, c->pin + o_ids, 4 * (size_t)k);
         if (w && E > 0 && !is_device_ptr(w)) memcpy(w, c->pin + o_w, 4 * (size_t)k);
+        if (onorm && E > 0 && !is_device_ptr(onorm)) memcpy(onorm, c->pin + o_on, 4 * (size_t)k);
     }
     return TLMG_OK;
+}
+
+}  // namespace tlmg
+
+extern "C" {
+
+int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
+    return moe_layer_impl(c, layer, h, ids, w, nullptr);
+}
+
+int tlmg_moe_layer_ex(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w, float *onorm) {
+    return moe_layer_impl(c, layer, h, ids, w, onorm);
 }
 
 }  // extern "C"

@@ -207,5 +207,15 @@ class MoeContext:
         """Home side: ffn[t] = sum_r w[t, r] * back[perm[t, r]] in ascending r."""
         check(self._lib.tlmg_ep_combine(self._h, n_tok, _ptr(back), _ptr(perm), _ptr(w), _ptr(ffn)))
 
-    def moe_layer(self, layer: int, h, ids=None, w=None) -> None:
-        check(self._lib.tlmg_moe_layer(self._h, layer, _ptr(h), _ptr(ids), _ptr(w)))
+    def moe_layer(self, layer: int, h, ids=None, w=None, onorm=None) -> None:
+        """moe() of one token (h += ffn in place); onorm receives the route
+        hook's per-rank output norms."""
+        if onorm is None:
+            check(self._lib.tlmg_moe_layer(self._h, layer, _ptr(h), _ptr(ids), _ptr(w)))
+        else:
+            check(self._lib.tlmg_moe_layer_ex(self._h, layer, _ptr(h), _ptr(ids), _ptr(w), _ptr(onorm)))
+
+    def set_dense_ffn(self, layer: int, dts, gate, up, down, d_ffn: int) -> None:
+        """Make `layer` a dense-FFN layer (host weight rows, packed)."""
+        check(self._lib.tlmg_set_dense_ffn(self._h, layer, d_ffn, (C.c_int32 * 3)(*dts), _ptr(gate), _ptr(up),
+                                           _ptr(down)))
