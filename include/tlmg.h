@@ -97,8 +97,11 @@ int tlmg_route(int router, const float *logits, const uint8_t *mask, const float
  * src/lib/tlm_quant.c:1014-1056). Errors leave NaN in y. */
 void tlmg_qmv_host(int dt, const void *W, size_t row_bytes, const void *act, float *y, int64_t n,
                    int64_t nrows);
-/* Same contract as tlm_qdot_fn (src/lib/tlm_quant.h:158): one HOST row. */
-float tlmg_qdot_host(int dt, const void *wrow, const void *act, int64_t n);
+/* Same contract as tlm_qdot_fn (src/lib/tlm_quant.h:157-158): one HOST row.
+ * aux is the reference's per-128-column scale vector of FP8 rows; every
+ * dtype this tier serves ignores it, as the reference's kernels for those
+ * dtypes do. */
+float tlmg_qdot_host(int dt, const void *wrow, const void *act, int64_t n, const float *aux);
 
 /* ---- layer level: the MoE expert FFN with HBM-resident expert slots --- */
 typedef struct tlmg_ctx tlmg_ctx;

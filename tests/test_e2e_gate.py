@@ -130,29 +130,51 @@ def test_gpu_moe_matches_reference_golden(name):
                         np.testing.assert_allclose(w, c["w"], rtol=ROUTE_RTOL)
 
 
+def _sensitivity(name, prompt, seq):
+    """Per position, how far the reference's own logits move when its libm
+    expf is replaced by the correctly rounded one (both runs on the CPU):
+    (greedy run, teacher-forced run) relative L2."""
+    with G.Gate(name, cr=False) as a, G.Gate(name, cr=True) as b:
+        _, la = a.generate(G.REF, prompt, N_GEN)
+        _, lb = b.generate(G.REF, prompt, N_GEN)
+        fa, fb = a.teacher(G.REF, seq), b.teacher(G.REF, seq)
+    return ([rel_l2(lb[i], la[i]) for i in range(len(la))], [rel_l2(fb[i], fa[i]) for i in range(len(fa))])
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", list(G.STORES))
 def test_greedy_and_teacher_forced_gate(name):
     """north_star's config-1 gate with the reference as built (libm expf):
     64 prompt tokens (tierlm bench's xorshift-42 prompt) then 64 greedy
     tokens give the same tokens with moe() on the GPU; teacher-forced over
-    that sequence every position has the same argmax and logits within
-    LOGIT_RTOL relative L2, and the top-10 ids (tierlm oracle's report,
-    src/bin/tierlm.c:670-700) agree wherever their scores are apart."""
+    that sequence every position has the same argmax, logits within
+    LOGIT_RTOL relative L2, and the same top-10 ids (tierlm oracle's report,
+    src/bin/tierlm.c:670-700) wherever their scores are apart and the
+    reference itself is well conditioned.
+
+    The GPU's expf is correctly rounded and libm's is not, so the bound is
+    LOGIT_RTOL plus twice what the reference itself moves at that position
+    under the two expfs (a few 1e-7 on most positions; config1_q4k has a
+    routing near-tie from position 70 on where the reference alone moves
+    by ~1e-2). test_bit_identical_with_correctly_rounded_expf shows the GPU
+    then equals the reference bit for bit."""
     with _gpu_gate(name, False) as g:
         prompt = G.xorshift_prompt(PROMPT, g.vocab)
         t_ref, l_ref = g.generate(G.REF, prompt, N_GEN)
         t_gpu, l_gpu = g.generate(G.GPU, prompt, N_GEN)
         assert np.array_equal(t_ref, t_gpu), (t_ref, t_gpu)
-        for i in range(l_ref.shape[0]):
-            assert rel_l2(l_gpu[i], l_ref[i]) <= LOGIT_RTOL, i
         seq = np.concatenate([prompt, t_ref])
         f_ref = g.teacher(G.REF, seq)
         f_gpu = g.teacher(G.GPU, seq)
+    sens_g, sens_f = _sensitivity(name, prompt, seq)
+    for i in range(l_ref.shape[0]):
+        assert rel_l2(l_gpu[i], l_ref[i]) <= LOGIT_RTOL + 2 * sens_g[i], (i, sens_g[i])
     assert np.array_equal(f_ref.argmax(1), f_gpu.argmax(1))
-    worst = max(rel_l2(f_gpu[i], f_ref[i]) for i in range(len(seq)))
-    assert worst <= LOGIT_RTOL, worst
     for i in range(len(seq)):
+        assert rel_l2(f_gpu[i], f_ref[i]) <= LOGIT_RTOL + 2 * sens_f[i], (i, sens_f[i])
+    for i in range(len(seq)):
+        if sens_f[i] > LOGIT_RTOL / 10:      # the reference's own ranking moves with the expf there
+            continue
         top = np.argsort(-f_ref[i], kind="stable")[:10]
         gaps = np.abs(np.diff(f_ref[i][top]))
         if (gaps > 1e-3 * np.abs(f_ref[i][top[0]])).all():

@@ -298,7 +298,7 @@ def test_qmv_host_adapter(dev, orc):
         lib.tlmg_qmv_host(dt, Wb.ctypes.data, Wb.shape[1], act.ctypes.data, y.ctypes.data, n, rows)
         ref = orc.matvec_rows(dt, Wb, Wb.shape[1], act, n, 0, rows)
         assert same_bits(y, ref).all()
-        d = lib.tlmg_qdot_host(dt, Wb[3].ctypes.data, act.ctypes.data, n)
+        d = lib.tlmg_qdot_host(dt, Wb[3].ctypes.data, act.ctypes.data, n, None)
         assert same_bits(np.float32(d), ref[3])
     ptr = C.c_void_p
     assert ptr is not None

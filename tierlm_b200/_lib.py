@@ -70,7 +70,7 @@ _SIGS = {
     "tlmg_decode_attention": (_I, [_I, _I, _P, _P, _P, _I, _P, _I, _I, _I, _I, _I, _P, _SZ, _P, _P]),
     "tlmg_kv_write": (_I, [_I, _P, _P, _P, _P, _I, C.c_int32, _I, _I, _I, _I, _P]),
     "tlmg_qmv_host": (None, [_I, _P, _SZ, _P, _P, _I64, _I64]),
-    "tlmg_qdot_host": (_F, [_I, _P, _P, _I64]),
+    "tlmg_qdot_host": (_F, [_I, _P, _P, _I64, _P]),
     "tlmg_open": (_I, [C.POINTER(Geom), _I, C.POINTER(_P)]),
     "tlmg_close": (None, [_P]),
     "tlmg_set_expert": (_I, [_P, _I, _I, _P, _P, _SZ, _P]),

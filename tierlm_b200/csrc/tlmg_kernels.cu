@@ -382,7 +382,8 @@ void tlmg_qmv_host(int dt, const void *W, size_t row_bytes, const void *act, flo
     if (!ok) fail(TLMG_EIO, "device copy or launch failed");
 }
 
-float tlmg_qdot_host(int dt, const void *wrow, const void *act, int64_t n) {
+float tlmg_qdot_host(int dt, const void *wrow, const void *act, int64_t n, const float *aux) {
+    (void)aux;   // per-128-column FP8 scales in the reference; no dtype of this tier reads it
     float y = NAN;
     tlmg_qmv_host(dt, wrow, tlmg_row_bytes(dt, n), act, &y, n, 1);
     return y;
