@@ -153,6 +153,42 @@ int tlmg_cache_prefetch(tlmg_ctx *ctx, int layer, const int32_t *ids, int k);
 /* out[6] = hits, misses, prefetched, prefetch hits, evictions, bytes copied. */
 int tlmg_cache_stats(tlmg_ctx *ctx, int64_t out[6]);
 
+/* ---- the slot policy of the expert cache, on its own (host only) ---------
+ * The reference store's rules (src/lib/tlm_store.c): FREE -> LOADING ->
+ * READY slots; every selection adds 1 to the expert's frequency and
+ * tlmg_store_tick halves all frequencies every 16 ticks; victims are a FREE
+ * slot first, else the unreferenced READY slot with the lowest (frequency,
+ * last use); an acquisition references its hits before any miss picks a
+ * victim; hints take only FREE slots or READY slots of frequency-0 experts,
+ * are dropped while more than 4 demand loads are in flight and are bounded
+ * in flight by min(16, slots - max(1, top_k)). Keys are layer * E + expert.
+ * No memory is moved: the caller copies an expert into a slot the policy
+ * returned and then calls tlmg_store_load_done. The HBM expert cache above
+ * decides with this policy; a caller managing its own slot memory can use it
+ * directly. Replaces the policy half of tlm_store_acquire / _release /
+ * _prefetch / _tick (src/lib/tlm_store.h:41-69). */
+typedef struct tlmg_store tlmg_store;
+int  tlmg_store_open(int n_keys, int n_slots, int top_k, tlmg_store **out);
+void tlmg_store_close(tlmg_store *s);
+/* Demand acquisition of keys[0..k): slots[i] = the referenced slot holding
+ * or now loading keys[i]; loads[i] = 1 where the caller must copy the expert
+ * in. TLMG_EBUSY (slots[i] = -1) when every slot is referenced or loading. */
+int  tlmg_store_acquire(tlmg_store *s, const int32_t *keys, int k, int32_t *slots, int32_t *loads);
+/* Router-lookahead hints: returns how many loads it started (their slots and
+ * keys in slots[] / keys_out[]), or a negative code. */
+int  tlmg_store_prefetch(tlmg_store *s, const int32_t *keys, int k, int32_t *slots, int32_t *keys_out);
+/* The copy into `slot` has completed (LOADING -> READY). */
+int  tlmg_store_load_done(tlmg_store *s, int slot);
+/* Drops one reference of an acquired slot (tlm_store_release). */
+int  tlmg_store_release(tlmg_store *s, int slot);
+/* One model step has passed (tlm_store_tick). */
+int  tlmg_store_tick(tlmg_store *s);
+/* out = state (0 FREE, 1 LOADING, 2 READY), key (-1 none), references, hint
+ * not yet used. */
+int  tlmg_store_slot(const tlmg_store *s, int slot, int32_t out[4]);
+/* out = hits, misses, hints issued, hints used, hints dropped, evictions. */
+int  tlmg_store_stats(const tlmg_store *s, int64_t out[6]);
+
 /* ---- expert packets of the tlm store (src/lib/tlm_packet.h:39-54) ------
  * A packet is the 64-byte header, the payload and zero padding to 4096
  * bytes. Extension: the reference writer zeroes the header's reserved[16]

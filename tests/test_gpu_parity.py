@@ -334,18 +334,22 @@ def test_fused_matches_multikernel(dev, orc, shape):
     lg = rng.standard_normal((T, E)).astype(np.float32)
     lg[5] = 0.0                                   # all-tie routing row
     outs, launches = {}, {}
-    for fused in (True, False):
+    for fused in ("stream", "static", False):
         ctx.set_fused(fused)
         xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
         od = torch.zeros((T, D), device=dev)
         n0 = ctx.launches
-        ctx.expert_ffn_many(0, xd, ld, od)
+        for rep in range(2):                      # twice: queue heads, epochs and counts reset between launches
+            ctx.expert_ffn_many(0, xd, ld, od)
         ctx.check()
-        launches[fused] = ctx.launches - n0
+        launches[fused] = (ctx.launches - n0) // 2
         outs[fused] = od.cpu().numpy()
-    # the persistent kernel serves all T tokens in one launch
-    assert (launches[True] == 1) == fused_expected, launches
-    assert same_bits(outs[True], outs[False]).all()
+    # a persistent kernel serves all T tokens in one launch
+    assert (launches["stream"] == 1) == fused_expected, launches
+    assert (launches["static"] == 1) == fused_expected, launches
+    assert same_bits(outs["stream"], outs[False]).all()
+    assert same_bits(outs["static"], outs[False]).all()
+    outs[True] = outs["stream"]
     orc.set_expf_mode(1)
     try:
         geom = dict(d_model=D, d_expert=de, n_experts=E, top_k=k, router=0)

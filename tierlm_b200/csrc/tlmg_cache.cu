@@ -16,6 +16,7 @@
 
 #include "tlmg_cache.cuh"
 #include "tlmg_internal.h"
+#include "tlmg_store.h"
 
 namespace tlmg {
 
@@ -209,3 +210,84 @@ int cache_mark_used(ExpertCache &c, int layer, const int32_t *ids, int k, cudaSt
 }
 
 }  // namespace tlmg
+
+// ---------------------------------------------------------------------------
+// The slot policy on its own (C ABI): for callers that manage their own slot
+// memory, and for replaying a trace against the reference store.
+struct tlmg_store {
+    tlmg::StorePolicy p;
+};
+
+extern "C" {
+
+int tlmg_store_open(int n_keys, int n_slots, int top_k, tlmg_store **out) {
+    if (!out || n_keys <= 0 || n_slots <= 0) return tlmg::set_error(TLMG_EINVAL, "store_open: bad argument");
+    tlmg_store *s = new tlmg_store();
+    s->p.init(n_keys, n_slots, top_k);
+    *out = s;
+    return TLMG_OK;
+}
+
+void tlmg_store_close(tlmg_store *s) { delete s; }
+
+int tlmg_store_acquire(tlmg_store *s, const int32_t *keys, int k, int32_t *slots, int32_t *loads) {
+    if (!s || k < 0 || (k > 0 && (!keys || !slots || !loads)) || k > 1024)
+        return tlmg::set_error(TLMG_EINVAL, "store_acquire: bad argument");
+    for (int i = 0; i < k; i++)
+        if (keys[i] < 0 || keys[i] >= (int)s->p.n_keys())
+            return tlmg::set_error(TLMG_ENOTFOUND, "store_acquire: key %d out of range", keys[i]);
+    return s->p.acquire(keys, k, slots, loads) ? TLMG_OK
+                                                : tlmg::set_error(TLMG_EBUSY, "store: all %d slots are referenced, "
+                                                                              "pinned or loading", s->p.n_slots());
+}
+
+int tlmg_store_prefetch(tlmg_store *s, const int32_t *keys, int k, int32_t *slots, int32_t *keys_out) {
+    if (!s || k < 0 || (k > 0 && (!keys || !slots || !keys_out)) || k > 1024)
+        return tlmg::set_error(TLMG_EINVAL, "store_prefetch: bad argument");
+    for (int i = 0; i < k; i++)
+        if (keys[i] < 0 || keys[i] >= (int)s->p.n_keys())
+            return tlmg::set_error(TLMG_ENOTFOUND, "store_prefetch: key %d out of range", keys[i]);
+    return s->p.prefetch(keys, k, slots, keys_out);
+}
+
+int tlmg_store_load_done(tlmg_store *s, int slot) {
+    if (!s || slot < 0 || slot >= s->p.n_slots()) return tlmg::set_error(TLMG_EINVAL, "store_load_done: bad slot");
+    s->p.load_done(slot);
+    return TLMG_OK;
+}
+
+int tlmg_store_release(tlmg_store *s, int slot) {
+    if (!s || slot >= s->p.n_slots()) return tlmg::set_error(TLMG_EINVAL, "store_release: bad slot");
+    s->p.release(slot);
+    return TLMG_OK;
+}
+
+int tlmg_store_tick(tlmg_store *s) {
+    if (!s) return tlmg::set_error(TLMG_EINVAL, "store_tick: NULL store");
+    s->p.tick();
+    return TLMG_OK;
+}
+
+int tlmg_store_slot(const tlmg_store *s, int slot, int32_t out[4]) {
+    if (!s || !out || slot < 0 || slot >= s->p.n_slots()) return tlmg::set_error(TLMG_EINVAL, "store_slot: bad slot");
+    const tlmg::StorePolicy::SlotState &v = s->p.slot(slot);
+    out[0] = v.state;
+    out[1] = v.key;
+    out[2] = v.refcount;
+    out[3] = v.prefetched;
+    return TLMG_OK;
+}
+
+int tlmg_store_stats(const tlmg_store *s, int64_t out[6]) {
+    if (!s || !out) return tlmg::set_error(TLMG_EINVAL, "store_stats: bad argument");
+    const tlmg::StorePolicy::Stats &st = s->p.stats();
+    out[0] = st.hits;
+    out[1] = st.misses;
+    out[2] = st.prefetch_issued;
+    out[3] = st.prefetch_used;
+    out[4] = st.prefetch_dropped;
+    out[5] = st.evictions;
+    return TLMG_OK;
+}
+
+}  // extern "C"

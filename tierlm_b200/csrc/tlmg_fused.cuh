@@ -45,9 +45,22 @@ struct FusedPlanKey {
     bool operator<(const FusedPlanKey &o) const { return dt_gu != o.dt_gu ? dt_gu < o.dt_gu : dt_dn < o.dt_dn; }
 };
 
-// Per-context state of the persistent kernel.
+// Per-context state of the persistent kernels (k_fused_ffn: a static work
+// split with a grid barrier per token; k_stream_ffn: chunks handed out by
+// two global queues, per-expert h flags instead of the barrier).
+enum : int { FUSED_STATIC = 1, FUSED_STREAM = 2 };
+struct StreamPlanHost;
 struct FusedScratch {
     bool enabled = false;          // usable on this device / geometry
+    int mode = FUSED_STATIC;       // which persistent kernel serves a launch
+    uint32_t *sbar = nullptr;      // device: the stream kernel's grid words (64 bytes)
+    uint64_t sepoch = 0;           // stream-kernel launches since sbar was reset
+    uint8_t *hq = nullptr;         // [tok_cap][k] quantised h rows (stream kernel)
+    uint32_t *hcnt = nullptr;      // [tok_cap][k] h rows written (zero between launches)
+    uint32_t *hflag = nullptr;     // [tok_cap][k] launch epoch once hq is published
+    struct Slot *tslot = nullptr;  // [tok_cap][k] routed experts' slots
+    float *wg = nullptr;           // [tok_cap][k] routing weights
+    std::map<FusedPlanKey, StreamPlanHost *> splans;
     uint32_t *bar = nullptr;       // device: [2] sticky error, [4..11] four 64-bit barrier arrival words
     uint32_t *err_host = nullptr;  // mapped pinned word: error bits set by the kernel
     uint32_t *err_dev = nullptr;   // its device alias

@@ -57,9 +57,14 @@ class MoeContext:
         except Exception:
             pass
 
-    def set_fused(self, on: bool) -> None:
-        """Persistent single-launch kernel (True, default) or the multi-kernel path."""
-        check(self._lib.tlmg_set_fused(self._h, 1 if on else 0))
+    FUSED_MODES = {"stream": 3, "static": 2}
+
+    def set_fused(self, on) -> None:
+        """Persistent single-launch kernel (True, default: the stream kernel),
+        "stream" / "static" to pick one, or the multi-kernel path (False).
+        Identical bits."""
+        mode = self.FUSED_MODES[on] if isinstance(on, str) else (1 if on else 0)
+        check(self._lib.tlmg_set_fused(self._h, mode))
 
     BATCH_KERNELS = {"warp": 0, "tiled": 1, "mma": 2}
 
