@@ -136,9 +136,10 @@ int tlmg_set_expert(tlmg_ctx *ctx, int layer, int expert, const int32_t dt[3],
  * the GPU, brings the routed ids to the host (one stream synchronisation),
  * copies the missing experts host -> HBM on a side stream and runs the
  * expert kernels after exactly those copies; results are bit-identical to
- * HBM-resident experts. Eviction: least recently acquired slot not needed
- * by the same call (a hit is never evicted by a miss of the same call).
- * Call tlmg_cache_enable once, before registering experts. */
+ * HBM-resident experts. Slot decisions follow the reference store (the
+ * tlmg_store policy below: frequency with decay, then recency; hits before
+ * misses; hint rules). Call tlmg_cache_enable once, before registering
+ * experts. */
 int tlmg_cache_enable(tlmg_ctx *ctx, int n_slots, size_t slot_bytes);
 /* Register one routed expert of `layer` in host memory (no copy now). The
  * payload must stay valid (and, for asynchronous copies, pinned) while the
@@ -146,12 +147,23 @@ int tlmg_cache_enable(tlmg_ctx *ctx, int n_slots, size_t slot_bytes);
  * either fully HBM-resident (tlmg_set_expert) or cached. */
 int tlmg_set_expert_host(tlmg_ctx *ctx, int layer, int expert, const int32_t dt[3],
                          const void *payload, size_t payload_len, const uint64_t item_off[3]);
-/* Start copies of the listed experts of `layer` (host ids) into free or
- * least recently used slots without waiting (router lookahead). Call after
+/* Hints for the listed experts of `layer` (host ids): copies into the slots
+ * the hint rules allow, without waiting (tlm_store_prefetch). Call after
  * the current step's launches are queued. No-op for resident layers. */
 int tlmg_cache_prefetch(tlmg_ctx *ctx, int layer, const int32_t *ids, int k);
-/* out[6] = hits, misses, prefetched, prefetch hits, evictions, bytes copied. */
+/* out[6] = hits, misses, hints issued, hints used, evictions, bytes copied. */
 int tlmg_cache_stats(tlmg_ctx *ctx, int64_t out[6]);
+/* One model step has passed: every 16 ticks the experts' selection
+ * frequencies halve (tlm_store_tick, called by tlm_model_step,
+ * src/lib/tlm_model.c:1097). */
+int tlmg_cache_tick(tlmg_ctx *ctx);
+/* Router lookahead of tlmg_moe_layer on cached layers (reference
+ * lookahead(), src/lib/tlm_model.c:844-877; depth 1 = the next layer, 0 =
+ * off): with the current layer's routing, the GPU also runs the next
+ * layer's RMSNorm and router on the current residual and takes its top k
+ * (0 = top_k, capped at the routable experts); after the current layer's
+ * experts are acquired those ids go to the cache as hints. */
+int tlmg_cache_lookahead(tlmg_ctx *ctx, int depth, int k);
 
 /* ---- the slot policy of the expert cache, on its own (host only) ---------
  * The reference store's rules (src/lib/tlm_store.c): FREE -> LOADING ->

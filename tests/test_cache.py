@@ -1,9 +1,10 @@
 """HBM expert-slot cache (tlmg_cache_enable / tlmg_set_expert_host): experts
 in pinned host memory, a pool of HBM slots smaller than the expert count,
 side-stream copies on misses. Every result must equal the HBM-resident
-context bit for bit; the hit / miss / eviction counts must follow the
-reference store's policy (src/lib/tlm_store.c:586-640): a call's hits are
-never evicted by its own misses, victims are least recently used."""
+context bit for bit; the decisions are the reference store's policy
+(src/lib/tlm_store.c, tests/test_store_policy.py replays it against the
+reference): a call's hits are never evicted by its own misses, victims are
+the lowest (frequency, last use), hints obey the demand reserve."""
 from __future__ import annotations
 
 import numpy as np
@@ -84,25 +85,64 @@ def test_cache_matches_resident(dev):
 
 
 def test_cache_prefetch_and_policy(dev):
-    """Prefetching a token's experts before its call turns every miss into a
-    prefetch hit; a call's own hits survive its misses (slots = top_k)."""
+    """Hints follow the reference store's rules: with exactly top_k slots
+    every hint is dropped (the demand reserve); with 2 top_k slots a hint of
+    the next token's experts turns misses into hint hits once the
+    frequencies of earlier selections have decayed (one tick per token).
+    Results stay bit-identical to resident experts throughout."""
     experts = _experts(seed=9)
-    res, cac, pinned = _contexts(experts, n_slots=K)   # exactly one token's experts
-    rng = np.random.default_rng(4)
-    for t in range(12):
-        x = rng.standard_normal(D).astype(np.float32)
-        lg = rng.standard_normal(E).astype(np.float32)
-        ids = np.argsort(-lg, kind="stable")[:K].astype(np.int32)   # softmax top-k = largest logits
-        before = cac.cache_stats()
-        cac.cache_prefetch(0, ids)
-        a, b = np.zeros(D, np.float32), np.zeros(D, np.float32)
-        res.expert_ffn(0, x, lg, a)
-        cac.expert_ffn(0, x, lg, b)
-        assert same_bits(a, b).all(), t
-        after = cac.cache_stats()
-        assert after["misses"] == before["misses"], (t, before, after)       # all served by the prefetch
-        assert after["hits"] - before["hits"] == K
-    assert cac.cache_stats()["prefetch_hits"] > 0
+    for n_slots, expect_hints in ((K, False), (2 * K, True)):
+        res, cac, pinned = _contexts(experts, n_slots=n_slots)
+        rng = np.random.default_rng(4)
+        for t in range(48):
+            x = rng.standard_normal(D).astype(np.float32)
+            lg = rng.standard_normal(E).astype(np.float32)
+            ids = np.argsort(-lg, kind="stable")[:K].astype(np.int32)   # softmax top-k = largest logits
+            cac.cache_prefetch(0, ids)
+            a, b = np.zeros(D, np.float32), np.zeros(D, np.float32)
+            res.expert_ffn(0, x, lg, a)
+            cac.expert_ffn(0, x, lg, b)
+            cac.cache_tick()
+            assert same_bits(a, b).all(), (n_slots, t)
+        st = cac.cache_stats()
+        assert st["hits"] + st["misses"] == 48 * K, st
+        if expect_hints:
+            assert st["prefetched"] > 0 and st["prefetch_hits"] > 0, st
+        else:
+            assert st["prefetched"] == 0 and st["prefetch_hits"] == 0, st
+        res.close()
+        cac.close()
+
+
+def test_cache_lookahead_moe_layer(dev):
+    """moe_layer over 4 cached layers with the GPU router lookahead (the next
+    layer's RMSNorm + router on the current residual, top-k hints after the
+    current acquisition) gives the resident context's bits, and the hints
+    are taken and used."""
+    from tierlm_b200 import synth
+    from tierlm_b200.moe import MoeContext
+    NL = 4
+    rng = np.random.default_rng(12)
+    experts = [[synth.rand_expert(rng, D, DE, DTS) for _ in range(E)] for _ in range(NL)]
+    norms = [(1.0 + 0.1 * rng.standard_normal(D)).astype(np.float32) for _ in range(NL)]
+    routers = [(0.05 * rng.standard_normal((E, D))).astype(np.float32) for _ in range(NL)]
+    res, cac, pinned = _contexts(experts, n_slots=3 * K, n_layers=NL)
+    for ctx in (res, cac):
+        for l_ in range(NL):
+            ctx.set_layer(l_, norms[l_], 0, routers[l_], D * 4)
+    cac.cache_lookahead(1, 0)
+    for t in range(24):
+        h = rng.standard_normal(D).astype(np.float32)
+        ha, hb = h.copy(), h.copy()
+        for l_ in range(NL):
+            ia, ib = np.zeros(K, np.int32), np.zeros(K, np.int32)
+            res.moe_layer(l_, ha, ia)
+            cac.moe_layer(l_, hb, ib)
+            assert np.array_equal(ia, ib) and same_bits(ha, hb).all(), (t, l_)
+        cac.cache_tick()
+    st = cac.cache_stats()
+    assert st["hits"] + st["misses"] == 24 * NL * K, st
+    assert st["prefetched"] > 0 and st["prefetch_hits"] > 0, st
     res.close()
     cac.close()
 

@@ -96,6 +96,8 @@ _SIGS = {
     "tlmg_packet_parse": (_I, [_P, _SZ, _I, _P]),
     "tlmg_set_expert_packet": (_I, [_P, _I, _I, _P, _SZ, _I]),
     "tlmg_cache_stats": (_I, [_P, _P]),
+    "tlmg_cache_tick": (_I, [_P]),
+    "tlmg_cache_lookahead": (_I, [_P, _I, _I]),
     "tlmg_store_open": (_I, [_I, _I, _I, C.POINTER(_P)]),
     "tlmg_store_close": (None, [_P]),
     "tlmg_store_acquire": (_I, [_P, _P, _I, _P, _P]),

@@ -1,12 +1,10 @@
 // tlmg_cache.cu - HBM expert-slot cache with side-stream refill.
 //
-// Policy (reference tlm_store_acquire, src/lib/tlm_store.c:586-640): every
-// hit of an acquisition is referenced before any miss picks a victim, so a
-// miss never evicts an expert the same step needs; victims are free slots
-// first, then the least recently acquired slot not pinned by the current
-// acquisition; a repeated id is served by the slot loaded earlier in the
-// same pass. Prefetch (reference lookahead + tlm_store_prefetch,
-// src/lib/tlm_model.c:844-877) starts copies without pinning or waiting.
+// Decisions (which expert goes into which slot, which slot is evicted, which
+// router-lookahead hints are taken) are StorePolicy's, the reference store's
+// rules (tlmg_store.h); this file moves the bytes. A slot's load is LOADING
+// until its copy's event has completed (checked at every acquisition, as the
+// reference's slot turns READY when its read completes).
 //
 // Ordering on the GPU: a load into a slot waits (on the copy stream) for the
 // event recorded after the slot's last use on the compute stream; the
@@ -33,7 +31,7 @@ void cache_release(ExpertCache &c) {
     c = ExpertCache{};
 }
 
-int cache_init(ExpertCache &c, int n_layers, int E, int n_slots, size_t slot_bytes) {
+int cache_init(ExpertCache &c, int n_layers, int E, int top_k, int n_slots, size_t slot_bytes) {
     cache_release(c);
     if (n_layers <= 0 || E <= 0 || n_slots <= 0 || slot_bytes == 0)
         return set_error(TLMG_EINVAL, "cache: %d layers, %d experts, %d slots of %zu bytes", n_layers, E, n_slots,
@@ -53,11 +51,8 @@ int cache_init(ExpertCache &c, int n_layers, int E, int n_slots, size_t slot_byt
     c.E = E;
     c.n_slots = n_slots;
     c.src.assign((size_t)n_layers * E, CacheSrc{});
-    c.where.assign((size_t)n_layers * E, -1);
-    c.owner.assign(n_slots, -1);
-    c.stamp.assign(n_slots, 0);
-    c.pinned.assign(n_slots, 0);
-    c.fresh.assign(n_slots, 0);
+    c.policy.init(n_layers * E, n_slots, top_k);
+    c.held.clear();
     c.used_valid.assign(n_slots, 0);
     c.loaded.assign(n_slots, nullptr);
     c.used.assign(n_slots, nullptr);
@@ -80,11 +75,9 @@ int cache_register(ExpertCache &c, int layer, int e, const int32_t dt[3], const 
         return set_error(TLMG_ERANGE, "cache: expert %d:%d needs %zu bytes, slots hold %zu", layer, e, need,
                          c.slot_bytes);
     const int key = layer * c.E + e;
-    if (c.where[key] >= 0) {   // re-registration: drop the resident copy
-        const int s = c.where[key];
-        c.owner[s] = -1;
-        c.where[key] = -1;
-    }
+    if (c.policy.where(key) >= 0)
+        return set_error(TLMG_EBUSY, "cache: expert %d:%d is resident; register experts before their first use",
+                         layer, e);
     CacheSrc &d = c.src[key];
     d.host = static_cast<const uint8_t *>(host);
     for (int m = 0; m < 3; m++) {
@@ -103,16 +96,6 @@ bool cache_has(const ExpertCache &c, int layer) {
     return false;
 }
 
-static int pick_victim(const ExpertCache &c, uint64_t now) {
-    int best = -1;
-    for (int s = 0; s < c.n_slots; s++) {
-        if (c.owner[s] < 0) return s;
-        if (c.pinned[s] == now) continue;
-        if (best < 0 || c.stamp[s] < c.stamp[best]) best = s;
-    }
-    return best;
-}
-
 static Slot slot_view(const ExpertCache &c, int s, const CacheSrc &d) {
     Slot v{};
     uint8_t *base = c.pool + (size_t)s * c.slot_bytes;
@@ -126,87 +109,85 @@ static Slot slot_view(const ExpertCache &c, int s, const CacheSrc &d) {
     return v;
 }
 
+// LOADING -> READY for every slot whose copy has completed.
+static void reap(ExpertCache &c) {
+    for (int s = 0; s < c.n_slots; s++) {
+        if (c.policy.slot(s).state != StorePolicy::LOADING) continue;
+        cudaError_t e = cudaEventQuery(c.loaded[s]);
+        if (e == cudaSuccess) c.policy.load_done(s);
+        else if (e != cudaErrorNotReady) cudaGetLastError();
+    }
+}
+
+// Copy expert `key` into slot v on the copy stream, after the slot's last use.
+static int load_slot(ExpertCache &c, int v, int key) {
+    if (c.used_valid[v] && cudaStreamWaitEvent(c.copy_st, c.used[v], 0) != cudaSuccess)
+        return cuda_fail(cudaGetLastError(), "cache: copy stream wait");
+    const CacheSrc &d = c.src[key];
+    const Slot view = slot_view(c, v, d);
+    for (int m = 0; m < 3; m++) {
+        cudaError_t e = cudaMemcpyAsync(const_cast<uint8_t *>(view.m[m]), d.host + d.off[m], d.bytes[m],
+                                        cudaMemcpyHostToDevice, c.copy_st);
+        if (e != cudaSuccess) return cuda_fail(e, "cache: expert copy");
+        c.bytes_loaded += (int64_t)d.bytes[m];
+    }
+    if (cudaEventRecord(c.loaded[v], c.copy_st) != cudaSuccess)
+        return cuda_fail(cudaGetLastError(), "cache: event record");
+    return TLMG_OK;
+}
+
 int cache_acquire(ExpertCache &c, int layer, const int32_t *ids, int k, bool prefetch, cudaStream_t st, Slot *out) {
     if (!c.on) return set_error(TLMG_EINVAL, "cache: not enabled");
     if (layer < 0 || layer >= c.n_layers) return set_error(TLMG_ERANGE, "cache: layer %d", layer);
-    const uint64_t now = ++c.clock;
-    int rc = TLMG_OK;
-    // pass 1: hits
+    if (k < 0 || k > 64) return set_error(TLMG_EINVAL, "cache: %d experts", k);
+    int keys[64], slots[64], loads[64];
     for (int i = 0; i < k; i++) {
-        if (ids[i] < 0 || ids[i] >= c.E || !c.src[(size_t)layer * c.E + ids[i]].ok) {
-            if (rc == TLMG_OK)
-                rc = set_error(TLMG_ENOTFOUND, "cache: layer %d expert %d is not registered", layer, ids[i]);
-            continue;
-        }
-        const int s = c.where[(size_t)layer * c.E + ids[i]];
-        if (s < 0) continue;
-        c.stamp[s] = now;
-        if (!prefetch) {
-            c.pinned[s] = now;
-            c.hits++;
-            if (c.fresh[s]) {
-                c.prefetch_hits++;
-                c.fresh[s] = 0;
-            }
-        }
+        if (ids[i] < 0 || ids[i] >= c.E || !c.src[(size_t)layer * c.E + ids[i]].ok)
+            return set_error(TLMG_ENOTFOUND, "cache: layer %d expert %d is not registered", layer, ids[i]);
+        keys[i] = layer * c.E + ids[i];
     }
-    if (rc) return rc;
-    // pass 2: misses
-    for (int i = 0; i < k; i++) {
-        const int key = layer * c.E + ids[i];
-        if (c.where[key] >= 0) {   // a repeated id loaded earlier in this pass
-            if (!prefetch) c.pinned[c.where[key]] = now;
-            continue;
-        }
-        const int v = pick_victim(c, now);
-        if (v < 0) {
-            if (prefetch) break;
-            return set_error(TLMG_EBUSY, "cache: all %d slots are held by this step; it needs at least top_k slots",
-                             c.n_slots);
-        }
-        if (c.owner[v] >= 0) {
-            c.where[c.owner[v]] = -1;
-            c.evictions++;
-        }
-        if (c.used_valid[v] && cudaStreamWaitEvent(c.copy_st, c.used[v], 0) != cudaSuccess)
-            return cuda_fail(cudaGetLastError(), "cache: copy stream wait");
-        const CacheSrc &d = c.src[key];
-        const Slot view = slot_view(c, v, d);
-        for (int m = 0; m < 3; m++) {
-            cudaError_t e = cudaMemcpyAsync(const_cast<uint8_t *>(view.m[m]), d.host + d.off[m], d.bytes[m],
-                                            cudaMemcpyHostToDevice, c.copy_st);
-            if (e != cudaSuccess) return cuda_fail(e, "cache: expert copy");
-            c.bytes_loaded += (int64_t)d.bytes[m];
-        }
-        if (cudaEventRecord(c.loaded[v], c.copy_st) != cudaSuccess)
-            return cuda_fail(cudaGetLastError(), "cache: event record");
-        c.owner[v] = key;
-        c.where[key] = v;
-        c.stamp[v] = now;
-        c.pinned[v] = prefetch ? 0 : now;
-        c.fresh[v] = prefetch ? 1 : 0;
-        if (prefetch) c.prefetched++;
-        else c.misses++;
+    reap(c);
+    if (prefetch) {
+        int keys_out[64];
+        const int n = c.policy.prefetch(keys, k, slots, keys_out);
+        for (int i = 0; i < n; i++)
+            if (int rc = load_slot(c, slots[i], keys_out[i])) return rc;
+        return TLMG_OK;
     }
-    if (prefetch) return TLMG_OK;
+    const bool ok = c.policy.acquire(keys, k, slots, loads);
+    for (int i = 0; i < k; i++)
+        if (slots[i] >= 0) c.held.push_back(slots[i]);
+    if (!ok) {
+        for (int s : c.held) c.policy.release(s);
+        c.held.clear();
+        return set_error(TLMG_EBUSY, "cache: all %d slots are referenced or loading; it needs at least top_k slots",
+                         c.n_slots);
+    }
+    for (int i = 0; i < k; i++)
+        if (loads[i])
+            if (int rc = load_slot(c, slots[i], keys[i])) return rc;
     for (int i = 0; i < k; i++) {
-        const int key = layer * c.E + ids[i];
-        const int s = c.where[key];
-        if (cudaStreamWaitEvent(st, c.loaded[s], 0) != cudaSuccess)
+        if (cudaStreamWaitEvent(st, c.loaded[slots[i]], 0) != cudaSuccess)
             return cuda_fail(cudaGetLastError(), "cache: compute stream wait");
-        if (out) out[i] = slot_view(c, s, c.src[key]);
+        if (out) out[i] = slot_view(c, slots[i], c.src[keys[i]]);
     }
     return TLMG_OK;
 }
 
-int cache_mark_used(ExpertCache &c, int layer, const int32_t *ids, int k, cudaStream_t st) {
-    for (int i = 0; i < k; i++) {
-        const int s = c.where[(size_t)layer * c.E + ids[i]];
-        if (s < 0) continue;
-        if (cudaEventRecord(c.used[s], st) != cudaSuccess) return cuda_fail(cudaGetLastError(), "cache: event record");
+int cache_mark_used(ExpertCache &c, cudaStream_t st) {
+    int rc = TLMG_OK;
+    for (int s : c.held) {
+        if (rc == TLMG_OK && cudaEventRecord(c.used[s], st) != cudaSuccess)
+            rc = cuda_fail(cudaGetLastError(), "cache: event record");
         c.used_valid[s] = 1;
+        c.policy.release(s);
     }
-    return TLMG_OK;
+    c.held.clear();
+    return rc;
+}
+
+void cache_tick(ExpertCache &c) {
+    if (c.on) c.policy.tick();
 }
 
 }  // namespace tlmg

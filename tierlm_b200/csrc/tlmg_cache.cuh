@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include "tlmg_fused.cuh"   // Slot
+#include "tlmg_store.h"
 
 namespace tlmg {
 
@@ -30,19 +31,15 @@ struct ExpertCache {
     uint8_t *pool = nullptr;                // [n_slots][slot_bytes] in HBM
     cudaStream_t copy_st = nullptr;
     std::vector<CacheSrc> src;              // [layer * E + e]
-    std::vector<int> where;                 // [layer * E + e] -> slot, or -1
-    std::vector<int> owner;                 // [slot] -> key, or -1
-    std::vector<uint64_t> stamp;            // [slot] last acquisition (LRU)
-    std::vector<uint64_t> pinned;           // [slot] acquisition that may not evict it
-    std::vector<char> fresh;                // [slot] loaded by a prefetch and not used since
+    StorePolicy policy;                     // which expert in which slot (the reference store's rules)
+    std::vector<int> held;                  // slots referenced by the acquisition in progress
     std::vector<cudaEvent_t> loaded;        // [slot] recorded on copy_st after its last load
     std::vector<cudaEvent_t> used;          // [slot] recorded on the compute stream after its last use
     std::vector<char> used_valid;
-    uint64_t clock = 0;
-    int64_t hits = 0, misses = 0, prefetched = 0, prefetch_hits = 0, evictions = 0, bytes_loaded = 0;
+    int64_t bytes_loaded = 0;
 };
 
-int cache_init(ExpertCache &c, int n_layers, int E, int n_slots, size_t slot_bytes);
+int cache_init(ExpertCache &c, int n_layers, int E, int top_k, int n_slots, size_t slot_bytes);
 void cache_release(ExpertCache &c);
 // Records a host-resident expert (no copy).
 int cache_register(ExpertCache &c, int layer, int e, const int32_t dt[3], const void *host, const uint64_t off[3],
@@ -50,11 +47,15 @@ int cache_register(ExpertCache &c, int layer, int e, const int32_t dt[3], const 
 bool cache_has(const ExpertCache &c, int layer);
 // Makes experts ids[0..k) of `layer` resident and returns their slots'
 // matrix pointers in out[0..k). prefetch = false: an acquisition for
-// work queued next on `st` (st waits for the copies; the slots cannot be
-// evicted by this call); prefetch = true: starts the copies only (out may
-// be NULL). TLMG_EBUSY when every slot is pinned by this acquisition.
+// work queued next on `st` (st waits for the copies; the slots stay
+// referenced until cache_mark_used); prefetch = true: router-lookahead
+// hints, copies started only (out may be NULL), subject to the hint rules.
+// TLMG_EBUSY when no slot is free of references and loads.
 int cache_acquire(ExpertCache &c, int layer, const int32_t *ids, int k, bool prefetch, cudaStream_t st, Slot *out);
-// After the launches that read the acquired slots are queued on st.
-int cache_mark_used(ExpertCache &c, int layer, const int32_t *ids, int k, cudaStream_t st);
+// After the launches that read the acquired slots are queued on st: their
+// use is recorded and the references dropped.
+int cache_mark_used(ExpertCache &c, cudaStream_t st);
+// One model step has passed (the frequencies' decay clock).
+void cache_tick(ExpertCache &c);
 
 }  // namespace tlmg

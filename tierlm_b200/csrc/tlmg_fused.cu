@@ -783,13 +783,11 @@ struct StreamGeom {
     int rowsA, nceA, perA, rowsB, nceB, perB, nGU, nDN, nsA, nsB;
     uint32_t segA, segB;                // bytes of one matrix's rows in a gate/up stage, of the rows in a down stage
     uint32_t strideA, strideB;          // stage strides
-    uint32_t offA, offB, full, empty, sdesc, qA, qB, fqA, eqA, fqB, eqB, partA, partB, rscr, rt, total;
+    uint32_t offA, offB, full, empty, sdesc, qA, qB, fqA, eqA, fqB, eqB, partA, partB, hq, rscr, rt, total;
 };
 struct StreamArgs {
     StreamGeom g;
-    uint8_t *hq;                        // [n_tok][k] quantised h rows of each (token, expert)
-    uint32_t *hcnt;                     // [n_tok][k] h rows written (reset by the CTA completing them)
-    uint32_t *hflag;                    // [n_tok][k] = epoch once hq is published
+    uint32_t *hcnt;                     // [n_tok][k] h rows written (zeroed at launch start)
     Slot *tslot;                        // [n_tok][k] slots of the routed experts
     float *wg;                          // [n_tok][k] routing weights
     uint32_t epoch;                     // launch number (>= 1)
@@ -799,7 +797,7 @@ __host__ __device__ inline StreamGeom stream_layout(StreamGeom g, int D, int de)
     const uint32_t qvx = qv_bytes(D / 256), qvd = qv_bytes(de / 256);
     uint32_t o = 0;
     g.strideA = 2u * g.segA + qvx;
-    g.strideB = g.segB + qvd;
+    g.strideB = g.segB + 4u * (uint32_t)de;   // the rows and the expert's raw h (f32)
     g.offA = o; o += (uint32_t)g.nsA * g.strideA;
     g.offB = o; o += (uint32_t)g.nsB * g.strideB;
     const int ns = g.nsA + g.nsB;
@@ -815,6 +813,7 @@ __host__ __device__ inline StreamGeom stream_layout(StreamGeom g, int D, int de)
     // unit partials, double-buffered: gate/up [2][2 matrices][rowsA][nbx + 1], down [2][rowsB][2 nbd + 1]
     g.partA = o = up16(o); o += 16u * 2u * 2u * (uint32_t)g.rowsA * (uint32_t)(D / 256 + 1);
     g.partB = o = up16(o); o += 16u * 2u * (uint32_t)g.rowsB * (uint32_t)(2 * (de / 256) + 1);
+    g.hq = o = up16(o); o += qvd;            // the down group's quantised h (one chunk at a time)
     g.rscr = o = up16(o); o += 4u * (uint32_t)RT_SCRATCH;
     g.rt = o; o += 8u * MAXK;            // one token's ids and weights
     g.total = up16(o) + 64;
@@ -866,15 +865,18 @@ __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t *p) {
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+__device__ __forceinline__ void red_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ void fence_acq_rel() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 __device__ __forceinline__ void st_release(uint32_t *p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Wait until *p == v, for at most BARRIER_NS.
-__device__ __forceinline__ bool flag_wait(const uint32_t *p, uint32_t v) {
-    if (ld_acquire(p) == v) return true;
+// Wait until the counter *p reaches v (relaxed reads), for at most BARRIER_NS.
+__device__ __forceinline__ bool count_wait(const uint32_t *p, uint32_t v) {
+    if (ld_relaxed(p) >= v) return true;
     const uint64_t t0 = now_ns();
-    while (ld_acquire(p) != v) {
+    while (ld_relaxed(p) < v) {
         if (now_ns() - t0 > BARRIER_NS) return false;
         __nanosleep(64);
     }
@@ -939,6 +941,7 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
                 if (a.w_out) a.w_out[(size_t)tok * k + lane] = wr[lane];
                 sa.wg[(size_t)tok * k + lane] = wr[lane];
                 sa.tslot[(size_t)tok * k + lane] = a.slots_all[(size_t)layer * E + ids[lane]];
+                sa.hcnt[(size_t)tok * k + lane] = 0u;   // before the launch-start count: no row is counted yet
             }
             __syncwarp();
         }
@@ -976,7 +979,7 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
             int64_t g;
             int tok, r, row0, nrows;
             const uint8_t *m0, *m1;
-            uint32_t flag;   // down: the expert's h flag as read when the chunk was taken
+            uint32_t hc;     // down: the expert's h row count as read when the chunk was taken (relaxed)
         };
         auto fetch = [&](int64_t gi) -> Next {
             Next x{ gi, 0, 0, 0, 0, nullptr, nullptr, 0u };
@@ -993,13 +996,19 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
                 x.m1 = reinterpret_cast<const uint8_t *>(__ldcg(sl + 1));
             } else {
                 x.m0 = reinterpret_cast<const uint8_t *>(__ldcg(sl + 2));
-                x.flag = ld_relaxed(sa.hflag + (size_t)x.tok * k + x.r);   // in flight with the slot read
+                x.hc = ld_relaxed(sa.hcnt + (size_t)x.tok * k + x.r);   // in flight with the slot read
             }
             return x;
         };
         uint64_t gu_seen = 0;   // the gate/up queue head as last read
-        Next cur = fetch(failed ? total : (int64_t)atomicAdd(head, 1ull));
-        int64_t gn = failed ? total : (int64_t)atomicAdd(head, 1ull);   // chunk f + 1's index
+        uint32_t sticky = 0;    // the sticky error word, read (relaxed) at the end of the previous chunk
+        // down chunks are taken two at a time (consecutive chunks of one
+        // expert, so the consumers quantise that expert's h once for both)
+        const unsigned long long take = isA ? 1ull : 2ull;
+        int64_t g0 = failed ? total : (int64_t)atomicAdd(head, take);
+        int64_t pend = (!isA && g0 + 1 < total) ? g0 + 1 : -1;   // the pair's second chunk
+        Next cur = fetch(g0);
+        int64_t gn = failed ? total : (int64_t)atomicAdd(head, take);   // the next take's first index
         for (int f = 0;; f++) {
             const int s = s0 + f % nsr;
             const uint64_t te0 = tr ? now_ns() : 0;
@@ -1009,7 +1018,7 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
             }
             if (tr) t_empty += now_ns() - te0;
             SDesc *sd = &sdesc[s];
-            if (cur.g >= total || failed || ld_acquire(&bar[2])) {
+            if (cur.g >= total || failed || sticky) {
                 sd->tok = -1;
                 mbar_arrive(&full[s]);
                 break;
@@ -1027,6 +1036,12 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
                     if (tr) t_flag += now_ns() - tf0;
                 }
             }
+            if (tr && cur.tok == trace_tok(a)) {
+                const uint64_t tn = now_ns();
+                uint64_t &first = tr[isA ? 10 : 7], &last = tr[isA ? 11 : 12];
+                if (!first) first = tn;
+                last = tn;
+            }
             const uint64_t start = (uint64_t)cur.row0 * rb, lo = start & ~15ull;
             const uint32_t size = (uint32_t)(((start + (uint64_t)cur.nrows * rb + 15) & ~15ull) - lo);
             sd->tok = cur.tok;
@@ -1041,24 +1056,38 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
                 bulk_g2s(stg + SEG_A, cur.m1 + lo, size, &full[s]);
                 bulk_g2s(stg + 2 * SEG_A, a.xq + (size_t)cur.tok * qvx, qvx, &full[s]);
             } else {
-                mbar_expect_tx(&full[s], size + qvd);
+                mbar_expect_tx(&full[s], size + 4u * (uint32_t)de);
                 bulk_g2s(stg, cur.m0 + lo, size, &full[s]);
-                // the expert's h: published by the CTA that completed its rows
-                // (normally already when the chunk was taken)
-                const uint64_t tf0 = tr ? now_ns() : 0;
+                // the expert's h rows, once every gate/up chunk of (token, expert)
+                // has counted its rows (normally long before: the count was read
+                // when the chunk was taken)
+                const uint32_t *hc = sa.hcnt + (size_t)cur.tok * k + cur.r;
                 bool hok = true;
-                if (cur.flag == sa.epoch) fence_acq_rel();   // the relaxed read becomes an acquire
-                else hok = flag_wait(sa.hflag + (size_t)cur.tok * k + cur.r, sa.epoch);
-                if (tr) t_flag += now_ns() - tf0;
+                if (cur.hc != (uint32_t)de) {
+                    const uint64_t tf0 = tr ? now_ns() : 0;
+                    hok = count_wait(hc, (uint32_t)de);
+                    if (tr) {
+                        t_flag += now_ns() - tf0;
+                        if (cur.tok == trace_tok(a) && !tr[8]) tr[8] = now_ns();
+                    }
+                }
                 if (!hok) {
                     raise_error(err, bar, FUSED_ERR_BARRIER);
                     failed = true;   // the copy still goes out (so no copy is left pending); results are invalid
                 }
-                fence_proxy_async();
-                bulk_g2s(stg + SEG_B, sa.hq + ((size_t)cur.tok * k + cur.r) * qvd, qvd, &full[s]);
+                fence_acq_rel();     // the relaxed count read becomes an acquire of the rows
+                fence_proxy_async(); // ... for the bulk copy below
+                bulk_g2s(stg + SEG_B, a.hbuf + (size_t)cur.tok * P + (size_t)cur.r * de, 4u * (uint32_t)de, &full[s]);
             }
-            cur = fetch(gn);
-            gn = (int64_t)atomicAdd(head, 1ull);
+            if (pend >= 0) {
+                cur = fetch(pend);
+                pend = -1;
+            } else {
+                cur = fetch(gn);
+                pend = (!isA && gn + 1 < total) ? gn + 1 : -1;
+                gn = (int64_t)atomicAdd(head, take);
+            }
+            sticky = ld_relaxed(&bar[2]);
         }
         if (failed) raise_error(err, bar, FUSED_ERR_COPY);
         if (tr) {
@@ -1097,36 +1126,14 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
             if (endm) done = true;
             q += m;
             const bool mine = lane < mm;
+            if (tr && isA && __any_sync(0xFFFFFFFFu, mine && ent.tok == trace_tok(a)) && lane == 0 && !tr[14])
+                tr[14] = now_ns();
             if (isA) {
-                // h rows of (token, expert): the CTA completing them quantises h once
-                uint32_t complete = 0;
-                if (mine) {
-                    uint32_t *cnt = sa.hcnt + (size_t)ent.tok * k + ent.r;
-                    const uint32_t old = atom_add_acq_rel(cnt, (uint32_t)ent.nrows);
-                    complete = old + (uint32_t)ent.nrows == (uint32_t)de;
-                    if (complete) *cnt = 0u;   // ready for the next launch
-                }
-                uint32_t cm = __ballot_sync(0xFFFFFFFFu, complete != 0);
-                if (cm) {
-                    __syncwarp();   // the completing lane's acquire orders the whole warp's reads
-                    __threadfence();
-                }
-                while (cm) {
-                    const int src = __ffs(cm) - 1;
-                    cm &= cm - 1;
-                    const int tok = __shfl_sync(0xFFFFFFFFu, ent.tok, src), r = __shfl_sync(0xFFFFFFFFu, ent.r, src);
-                    const float *hr = a.hbuf + (size_t)tok * P + (size_t)r * de;
-                    const QVec hv = qvec(sa.hq + ((size_t)tok * k + r) * qvd, nbd);
-                    for (int b = 0; b < nbd; b++) {
-                        const float4 *h4 = reinterpret_cast<const float4 *>(hr + 256 * b) + 2 * lane;
-                        quant_block(__ldcg(h4), __ldcg(h4 + 1), hv, b, lane);
-                    }
-                    __syncwarp();
-                    if (lane == 0) {
-                        __threadfence();
-                        st_release(sa.hflag + (size_t)tok * k + r, sa.epoch);
-                    }
-                }
+                // count the chunk's h rows of (token, expert): one fence for the
+                // round (the rows were written before the entries were pushed),
+                // then fire-and-forget adds; the down producer reads the counts
+                __threadfence();
+                if (mine) red_add(sa.hcnt + (size_t)ent.tok * k + ent.r, (uint32_t)ent.nrows);
             } else {
                 // 64-row output groups: each entry's rows lie in at most two
                 // groups; the CTA completing a group combines its rows in
@@ -1209,7 +1216,7 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
             return true;
         };
         uint32_t tw = 0, tc = 0;
-        int pb = 0, nq_seen = 0;
+        int pb = 0, nq_seen = 0, qtok = -1, qr = -1;   // qtok / qr: whose h the group's quantised h holds
         bool dead = false;   // the pushing thread only: the duty ring stopped answering
         for (int f = 0;; f++) {
             const int s = s0 + f % nsr;
@@ -1227,6 +1234,19 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
             const SDesc d = sdesc[s];
             if (d.tok < 0) break;
             nq_seen++;
+            if (!isA && (d.tok != qtok || d.r != qr)) {
+                // the expert's raw h rows came with the chunk: quantise them once
+                // for the chunks of this (token, expert) that follow in a row
+                const float *hr = reinterpret_cast<const float *>(smem + G.offB + (size_t)(s - nsA) * G.strideB + SEG_B);
+                const QVec hq = qvec(smem + G.hq, nbd);
+                for (int b = gt >> 5; b < nbd; b += gth >> 5) {
+                    const float4 *h4 = reinterpret_cast<const float4 *>(hr + 256 * b) + 2 * lane;
+                    quant_block(h4[0], h4[1], hq, b, lane);
+                }
+                gsync();
+                qtok = d.tok;
+                qr = d.r;
+            }
             BlockSum *pp = part + pb * pbuf;
             const int units = d.nrows * nbu;
             if (isA) {
@@ -1243,7 +1263,7 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
                 }
             } else {
                 const uint8_t *stg = smem + G.offB + (size_t)(s - nsA) * G.strideB;
-                const QVec h = qvec(const_cast<uint8_t *>(stg) + SEG_B, nbd);
+                const QVec h = qvec(smem + G.hq, nbd);
                 for (int u = gt; u < units; u += gth) {
                     const int row = u / nbu, ub = u - row * nbu, b = ub >> 1;
                     BlockSum o1;
@@ -1275,6 +1295,7 @@ k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ Stream
             }
             if (gt >= gth - 32) {
                 __syncwarp();   // every chain of the chunk is written (they run in this warp)
+                if (tr && isA && gt == gth - 1 && d.tok == trace_tok(a) && !tr[13]) tr[13] = now_ns();
                 if (gt == gth - 1 && !push(QEnt{ d.tok, d.r, d.row0, d.nrows })) {
                     raise_error(err, bar, FUSED_ERR_BARRIER);
                     dead = true;   // voted at the next stage
@@ -1369,16 +1390,14 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
 }
 
 static void free_tokens(FusedScratch &f) {
-    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.eo, (void *)f.ocnt, (void *)f.hq, (void *)f.hcnt,
-                     (void *)f.hflag, (void *)f.tslot, (void *)f.wg })
+    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.eo, (void *)f.ocnt, (void *)f.hcnt, (void *)f.tslot,
+                     (void *)f.wg })
         if (p) cudaFree(p);
     f.xq = nullptr;
     f.hbuf = nullptr;
     f.eo = nullptr;
     f.ocnt = nullptr;
-    f.hq = nullptr;
     f.hcnt = nullptr;
-    f.hflag = nullptr;
     f.tslot = nullptr;
     f.wg = nullptr;
     f.tok_cap = 0;
@@ -1397,8 +1416,7 @@ static int reserve_tokens(FusedScratch &f, int n_tok) {
         cudaMalloc(&f.hbuf, (size_t)cap * P * 4) != cudaSuccess ||
         cudaMalloc(&f.eo, (size_t)cap * Q * 4) != cudaSuccess ||
         cudaMalloc(&f.ocnt, (size_t)cap * (f.D / 64) * 4) != cudaSuccess ||
-        cudaMalloc(&f.hq, ck * qv_bytes(f.de / 256)) != cudaSuccess || cudaMalloc(&f.hcnt, ck * 4) != cudaSuccess ||
-        cudaMalloc(&f.hflag, ck * 4) != cudaSuccess || cudaMalloc(&f.tslot, ck * sizeof(Slot)) != cudaSuccess ||
+        cudaMalloc(&f.hcnt, ck * 4) != cudaSuccess || cudaMalloc(&f.tslot, ck * sizeof(Slot)) != cudaSuccess ||
         cudaMalloc(&f.wg, ck * 4) != cudaSuccess) {
         cudaGetLastError();
         free_tokens(f);
@@ -1406,7 +1424,6 @@ static int reserve_tokens(FusedScratch &f, int n_tok) {
     }
     cudaMemset(f.ocnt, 0, (size_t)cap * (f.D / 64) * 4);
     cudaMemset(f.hcnt, 0, ck * 4);
-    cudaMemset(f.hflag, 0, ck * 4);
     // flags of a fresh buffer restart the epochs (the device is idle: cudaFree synchronised)
     cudaMemset(f.sbar, 0, 64);
     f.sepoch = 0;
@@ -1589,7 +1606,7 @@ static int launch_stream(FusedScratch &f, const StreamPlanHost &sp, const FusedA
     la.hbuf = f.hbuf;
     la.eo = f.eo;
     la.ocnt = f.ocnt;
-    StreamArgs sa{ sp.g, f.hq, f.hcnt, f.hflag, f.tslot, f.wg, (uint32_t)(f.sepoch + 1) };
+    StreamArgs sa{ sp.g, f.hcnt, f.tslot, f.wg, (uint32_t)(f.sepoch + 1) };
     cudaError_t e = cudaLaunchKernelEx(&cfg, sp.fn, la, sa, f.sbar, f.err_dev);
     count_launch();
     if (e != cudaSuccess) return cuda_fail(e, "stream expert FFN launch");
@@ -1645,7 +1662,6 @@ uint32_t fused_take_error(FusedScratch &f) {
         cudaMemset(f.sbar, 0, 64);
         if (f.ocnt) cudaMemset(f.ocnt, 0, (size_t)f.tok_cap * (f.D / 64) * 4);
         if (f.hcnt) cudaMemset(f.hcnt, 0, (size_t)f.tok_cap * f.k * 4);
-        if (f.hflag) cudaMemset(f.hflag, 0, (size_t)f.tok_cap * f.k * 4);
         f.rounds = 0;
         f.launches = 0;
         f.sepoch = 0;

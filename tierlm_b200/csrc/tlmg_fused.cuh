@@ -55,9 +55,7 @@ struct FusedScratch {
     int mode = FUSED_STATIC;       // which persistent kernel serves a launch
     uint32_t *sbar = nullptr;      // device: the stream kernel's grid words (64 bytes)
     uint64_t sepoch = 0;           // stream-kernel launches since sbar was reset
-    uint8_t *hq = nullptr;         // [tok_cap][k] quantised h rows (stream kernel)
-    uint32_t *hcnt = nullptr;      // [tok_cap][k] h rows written (zero between launches)
-    uint32_t *hflag = nullptr;     // [tok_cap][k] launch epoch once hq is published
+    uint32_t *hcnt = nullptr;      // [tok_cap][k] h rows counted (stream kernel; zeroed at launch start)
     struct Slot *tslot = nullptr;  // [tok_cap][k] routed experts' slots
     float *wg = nullptr;           // [tok_cap][k] routing weights
     std::map<FusedPlanKey, StreamPlanHost *> splans;

@@ -64,6 +64,7 @@ struct Layer {
     int dt_gu = -1, dt_dn = -1;         // uniform gate/up and down dtypes of the layer (or -1)
     bool has_shared = false;
     bool cached = false;                // experts registered in host memory, served by the HBM slot cache
+    int live = 1 << 30;                 // unmasked (routable) experts
     int sh_dt[3] = { 0, 0, 0 };
     void *sh_w[3] = { nullptr, nullptr, nullptr };
     float *sh_gate_inp = nullptr;
@@ -114,6 +115,12 @@ struct tlmg_ctx {
     ExpertCache cache;             // HBM expert-slot cache (tlmg_cache_enable)
     Slot *pin_slots = nullptr;     // pinned [n_layers][E] slot-table mirror of cached layers
     int32_t *pin_ids = nullptr;    // pinned [64] routed ids of a cached layer
+    // router lookahead of cached layers (tlmg_cache_lookahead)
+    int la_depth = 0, la_k = 0, la_k_now = 0;
+    int la_layer = -1;             // layer whose predicted ids are in pin_la, -1 = none
+    float *la_x = nullptr, *la_logits = nullptr, *la_w = nullptr;
+    uint8_t *la_q = nullptr;
+    int32_t *la_ids = nullptr, *pin_la = nullptr;
     bool fused_on = true;
     uint64_t *trace = nullptr;     // device [nsm][FUSED_TRACE_POINTS] when tracing
     Slot *slots_all = nullptr;     // device [n_layers][E]: every layer's slot table, contiguous
@@ -497,6 +504,14 @@ static int cache_route_acquire(tlmg_ctx *c, int layer) {
     Slot got[64];
     int rc = cache_acquire(c->cache, layer, c->pin_ids, k, false, c->st, got);
     if (rc) return rc;
+    // the lookahead hints for the next layer go out only now that this
+    // layer's experts are referenced, so a hint never takes their slots
+    // (reference moe(), src/lib/tlm_model.c:1014-1018)
+    if (c->la_layer >= 0) {
+        const int la = c->la_layer;
+        c->la_layer = -1;
+        if ((rc = cache_acquire(c->cache, la, c->pin_la, c->la_k_now, true, c->st, nullptr))) return rc;
+    }
     Slot *tab = c->pin_slots + (size_t)layer * E;
     for (int r = 0; r < k; r++) {
         Ly.h_slots[c->pin_ids[r]] = got[r];
@@ -550,7 +565,7 @@ static int run_experts(tlmg_ctx *c, int layer, const float *logits, float *ffn, 
         Ly.d_slots, c->ids, c->w, k, D, de, c->hq, c->hq_stride, s_out, sgate, ffn, h, cw);
     prof_mark(c, 1, false);
     if ((rc = launched("ffn down"))) return rc;
-    return Ly.cached ? cache_mark_used(c->cache, layer, c->pin_ids, k, c->st) : TLMG_OK;
+    return Ly.cached ? cache_mark_used(c->cache, c->st) : TLMG_OK;
 }
 
 // Every expert of the layer is loaded (or registered with the slot cache);
@@ -688,6 +703,7 @@ void tlmg_close(tlmg_ctx *c) {
     cache_release(c->cache);
     if (c->pin_slots) cudaFreeHost(c->pin_slots);
     if (c->pin_ids) cudaFreeHost(c->pin_ids);
+    if (c->pin_la) cudaFreeHost(c->pin_la);
     c->arena.release();
     for (void *p : c->owned) cudaFree(p);
     if (c->pin) cudaFreeHost(c->pin);
@@ -855,7 +871,7 @@ int tlmg_cache_enable(tlmg_ctx *c, int n_slots, size_t slot_bytes) {
     if (c->st) cudaStreamSynchronize(c->st);
     for (Layer &Ly : c->L)
         if (Ly.cached) return set_error(TLMG_EBUSY, "cache: already holds registered experts");
-    return cache_init(c->cache, c->g.n_layers, c->g.n_experts, n_slots, slot_bytes);
+    return cache_init(c->cache, c->g.n_layers, c->g.n_experts, c->g.top_k, n_slots, slot_bytes);
 }
 
 int tlmg_set_expert_host(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], const void *payload,
@@ -902,13 +918,42 @@ int tlmg_cache_prefetch(tlmg_ctx *c, int layer, const int32_t *ids, int k) {
 
 int tlmg_cache_stats(tlmg_ctx *c, int64_t out[6]) {
     if (!c || !out) return set_error(TLMG_EINVAL, "cache_stats: NULL argument");
-    const ExpertCache &k = c->cache;
+    const StorePolicy::Stats &k = c->cache.policy.stats();
     out[0] = k.hits;
     out[1] = k.misses;
-    out[2] = k.prefetched;
-    out[3] = k.prefetch_hits;
+    out[2] = k.prefetch_issued;
+    out[3] = k.prefetch_used;
     out[4] = k.evictions;
-    out[5] = k.bytes_loaded;
+    out[5] = c->cache.bytes_loaded;
+    return TLMG_OK;
+}
+
+int tlmg_cache_tick(tlmg_ctx *c) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    cache_tick(c->cache);
+    return TLMG_OK;
+}
+
+int tlmg_cache_lookahead(tlmg_ctx *c, int depth, int k) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    if (depth < 0 || depth > 1 || k < 0 || k > 64 || k > c->g.n_experts)
+        return set_error(TLMG_EINVAL, "cache_lookahead: depth %d (0 or 1), k %d (0 .. min(64, E))", depth, k);
+    cudaSetDevice(c->device);
+    if (depth && !c->la_x) {
+        const int D = c->g.d_model, E = c->g.n_experts;
+        const size_t xq = std::max(tlmg_qact_bytes(DT_Q8_K, D), tlmg_qact_bytes(DT_Q8_0, D)) + 256;
+        if (!(c->la_x = (float *)dalloc(c, 4 * (size_t)D)) || !(c->la_logits = (float *)dalloc(c, 4 * (size_t)E)) ||
+            !(c->la_q = (uint8_t *)dalloc(c, xq)) || !(c->la_ids = (int32_t *)dalloc(c, 4 * 64)) ||
+            !(c->la_w = (float *)dalloc(c, 4 * 64)))
+            return set_error(TLMG_ENOMEM, "cache_lookahead: scratch");
+        if (!c->pin_la && cudaMallocHost(&c->pin_la, 4 * 64) != cudaSuccess) {
+            cudaGetLastError();
+            c->pin_la = nullptr;
+            return set_error(TLMG_ENOMEM, "cache_lookahead: pinned ids");
+        }
+    }
+    c->la_depth = depth;
+    c->la_k = k ? k : c->g.top_k;
     return TLMG_OK;
 }
 
@@ -955,6 +1000,8 @@ int tlmg_set_layer(tlmg_ctx *c, int layer, const float *ffn_norm, int router_dt,
         }
         if (cudaMemcpy(Ly.mask, mask, (size_t)E, cudaMemcpyHostToDevice) != cudaSuccess)
             return set_error(TLMG_EIO, "set_layer: mask upload");
+        Ly.live = 0;
+        for (int e = 0; e < E; e++) Ly.live += !mask[e];
     }
     return TLMG_OK;
 }
@@ -1311,6 +1358,39 @@ static int dense_ffn(tlmg_ctx *c, Layer &Ly, float *dh) {
     return launched("dense residual");
 }
 
+// Router lookahead (reference lookahead(), src/lib/tlm_model.c:844-877): the
+// next layer's RMSNorm and router on the current residual h (before this
+// layer's h += ffn), top lookahead-k ids to pinned host memory; the copy
+// completes with the synchronisation that brings this layer's routed ids to
+// the host, and cache_route_acquire turns them into hints after this layer's
+// acquisition. Only for a cached next layer with a router (a dense-FFN layer
+// has none).
+static int launch_lookahead(tlmg_ctx *c, int layer, const float *dh) {
+    const int l2 = layer + 1;
+    if (!c->la_depth || l2 >= c->g.n_layers) return TLMG_OK;
+    Layer &N = c->L[l2];
+    if (!N.cached || N.has_dense || !N.router_w || !N.ffn_norm) return TLMG_OK;
+    const int D = c->g.d_model, E = c->g.n_experts;
+    int k = std::min(c->la_k, N.live);   // never more hints than routable experts
+    if (k <= 0) return TLMG_OK;
+    int rc;
+    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, N.ffn_norm, D, c->g.norm_eps, c->la_x);
+    if ((rc = launched("lookahead rmsnorm"))) return rc;
+    const int kr = act_kind_for(N.router_dt);
+    if (kr != DT_F32 && (rc = launch_quant_act(kr, c->la_x, D, c->la_q, c->st))) return rc;
+    if ((rc = launch_matvec(N.router_dt, N.router_w, N.router_rb, kr == DT_F32 ? (const void *)c->la_x : c->la_q,
+                            c->la_logits, D, 0, E, c->st)))
+        return rc;
+    if ((rc = launch_route(c->g.router, c->la_logits, N.mask, N.router_bias, E, k, c->g.routed_scale, c->la_ids,
+                           c->la_w, c->st)))
+        return rc;
+    cudaError_t e = cudaMemcpyAsync(c->pin_la, c->la_ids, 4 * (size_t)k, cudaMemcpyDeviceToHost, c->st);
+    if (e != cudaSuccess) return cuda_fail(e, "lookahead ids");
+    c->la_layer = l2;
+    c->la_k_now = k;
+    return TLMG_OK;
+}
+
 static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w, float *onorm) {
     int rc = check_layer(c, layer);
     if (rc) return rc;
@@ -1373,6 +1453,7 @@ static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float 
         int kr = act_kind_for(Ly.router_dt);
         const void *ract = kr == DT_F32 ? (const void *)c->x : kr == DT_Q8_0 ? (const void *)c->xq80 : (const void *)c->xq8k;
         if ((rc = launch_matvec(Ly.router_dt, Ly.router_w, Ly.router_rb, ract, c->logits, D, 0, E, c->st))) return rc;
+        if (Ly.cached && (rc = launch_lookahead(c, layer, dh))) return rc;
         if ((rc = run_experts(c, layer, c->logits, c->ffn, dh, s_out, sgate, c->x, onorm ? c->cw : nullptr))) return rc;
         if (onorm) {
             k_onorm<<<k, 32, 0, c->st>>>(c->cw, D, c->onorm);

@@ -156,6 +156,14 @@ class MoeContext:
         check(self._lib.tlmg_cache_stats(self._h, out))
         return dict(zip(("hits", "misses", "prefetched", "prefetch_hits", "evictions", "bytes"), list(out)))
 
+    def cache_tick(self) -> None:
+        """One model step has passed (the selection frequencies' decay clock)."""
+        check(self._lib.tlmg_cache_tick(self._h))
+
+    def cache_lookahead(self, depth: int = 1, k: int = 0) -> None:
+        """Router lookahead of moe_layer on cached layers (depth 1 or 0 = off)."""
+        check(self._lib.tlmg_cache_lookahead(self._h, depth, k))
+
     def set_layer(self, layer: int, ffn_norm=None, router_dt: int = 0, router_w=None, router_row_bytes: int = 0,
                   router_bias=None, mask=None) -> None:
         check(self._lib.tlmg_set_layer(self._h, layer, _ptr(ffn_norm), router_dt, _ptr(router_w), router_row_bytes,
