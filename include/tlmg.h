@@ -324,6 +324,38 @@ int tlmg_ep_experts(tlmg_ctx *ctx, int layer, int e_lo, int e_hi, int64_t n_rec,
 int tlmg_ep_combine(tlmg_ctx *ctx, int n_tok, const float *back, const int32_t *perm,
                     const float *w, float *ffn);
 
+/* ---- Expert parallelism over peer memory (one process per GPU, all GPUs
+ * of one node). The same split as above, with the exchange done by the
+ * library: each rank opens one buffer, publishes its CUDA IPC handle,
+ * maps every peer's, and then one tlmg_ep_layer call per layer does
+ * dispatch, the owner's experts, the return of the output rows and the
+ * combine, all queued on the context's stream with no host wait and no
+ * collective library; two bounded barriers over peer flags order the
+ * steps (a barrier that waits more than 1 s makes the next tlmg_check
+ * return TLMG_EIO). Results are bit-identical to tlmg_expert_ffn_batch.
+ * Every rank calls tlmg_ep_layer for the same layers in the same order,
+ * with n_tok = 0 where it has no tokens. */
+
+/* Allocates this rank's exchange buffer for up to max_tok tokens per call
+ * (rank in [0, n_ranks), n_ranks <= 8). */
+int tlmg_ep_open(tlmg_ctx *ctx, int rank, int n_ranks, int max_tok);
+/* Size of one rank's handle (a cudaIpcMemHandle_t). */
+size_t tlmg_ep_handle_bytes(void);
+/* This rank's handle -> handle (tlmg_ep_handle_bytes() bytes). */
+int tlmg_ep_handle(tlmg_ctx *ctx, void *handle);
+/* Maps every peer's buffer: handles = the n_ranks handles in rank order
+ * (this rank's own entry is ignored; NULL allowed when n_ranks == 1). */
+int tlmg_ep_connect(tlmg_ctx *ctx, const void *handles);
+/* One layer: x f32[n_tok][D], logits f32[n_tok][E] -> ffn f32[n_tok][D]
+ * (the routed experts' combine; ids / w [n_tok][top_k] may be NULL). DEVICE
+ * pointers, x 16-byte aligned. The rank's experts floor(e * n_ranks / E)
+ * == rank must be loaded. */
+int tlmg_ep_layer(tlmg_ctx *ctx, int layer, int n_tok, const float *x, const float *logits,
+                  float *ffn, int32_t *ids, float *w);
+/* Waits for the stream, then frees the buffer and unmaps the peers'
+ * (every rank closes after its last layer call). */
+int tlmg_ep_close(tlmg_ctx *ctx);
+
 /* The whole moe() block for one token (src/lib/tlm_model.c:940-1055):
  * RMSNorm, router matvec, route, experts, shared expert, h += ffn.
  * h: f32[D] in/out; ids/w may be NULL. Host or device pointers. */

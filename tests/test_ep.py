@@ -300,18 +300,58 @@ def test_ep_foreign_record_is_loud():
 
 
 @pytest.mark.gpu
-def test_ep_nccl_two_gpus():
-    """Two ranks over NCCL (skipped with fewer than two GPUs): each rank's
-    expert-parallel result equals its own single-GPU batched call bitwise."""
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_ep_two_gpus(exchange):
+    """Two ranks (skipped with fewer than two GPUs), the exchange over NCCL
+    or over peer memory: each rank's expert-parallel result (and, over peer
+    memory, its ids and weights) equals its own single-GPU batched call
+    bitwise; over peer memory a layer call that no peer joins fails with
+    TLMG_EIO after the bounded barrier wait."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
-           str(ROOT / "tests" / "ep_nccl_worker.py")]
+           str(ROOT / "tests" / "ep_nccl_worker.py"), exchange]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert r.stdout.count("EP-OK") == 2, r.stdout[-2000:]
+
+
+@pytest.mark.gpu
+def test_ep_peer_one_rank():
+    """PeerExpertParallel with one rank (no peers): back-to-back layer calls,
+    n = 0 included, equal tlmg_expert_ffn_batch bitwise; more tokens than
+    the exchange was opened for is an error."""
+    from tierlm_b200 import synth
+    from tierlm_b200.ep import PeerExpertParallel
+    dev = torch.device("cuda:0")
+    rng = np.random.default_rng(17)
+    D_, de, E_, k = 1024, 512, 24, 4
+    experts = [synth.rand_expert(rng, D_, de, (12, 12, 14)) for _ in range(E_)]
+    ctx = _gpu_ctx(experts, D_, de, E_, k)
+    ep = PeerExpertParallel(ctx, D_, E_, k, 40, device=dev)
+    runs = []
+    for n in (40, 0, 3, 1, 29):
+        x = torch.from_numpy(rng.standard_normal((n, D_)).astype(np.float32)).to(dev)
+        lg = torch.from_numpy(rng.standard_normal((n, E_)).astype(np.float32)).to(dev)
+        ffn = torch.empty((max(n, 1), D_), device=dev)
+        ep.ffn_batch(0, x, lg, ffn, check=False)
+        runs.append((x, lg, ffn))
+    ctx.check()
+    for x, lg, ffn in runs:
+        n = x.shape[0]
+        if not n:
+            continue
+        ref = torch.empty_like(ffn)
+        ctx.expert_ffn_batch(0, x, lg, ref)
+        ctx.check()
+        assert torch.equal(ffn[:n].view(torch.int32), ref[:n].view(torch.int32))
+    with pytest.raises(ValueError):
+        ep.ffn_batch(0, torch.zeros((41, D_), device=dev), torch.zeros((41, E_), device=dev),
+                     torch.zeros((41, D_), device=dev))
+    ep.close()
+    ctx.close()
 
 
 @pytest.mark.gpu

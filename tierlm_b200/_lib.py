@@ -83,6 +83,12 @@ _SIGS = {
     "tlmg_ep_dispatch": (_I, [_P, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "tlmg_ep_experts": (_I, [_P, _I, _I, _I, _I64, _P, _P]),
     "tlmg_ep_combine": (_I, [_P, _I, _P, _P, _P, _P]),
+    "tlmg_ep_open": (_I, [_P, _I, _I, _I]),
+    "tlmg_ep_handle_bytes": (_SZ, []),
+    "tlmg_ep_handle": (_I, [_P, _P]),
+    "tlmg_ep_connect": (_I, [_P, _P]),
+    "tlmg_ep_layer": (_I, [_P, _I, _I, _P, _P, _P, _P, _P]),
+    "tlmg_ep_close": (_I, [_P]),
     "tlmg_moe_layer": (_I, [_P, _I, _P, _P, _P]),
     "tlmg_moe_layer_ex": (_I, [_P, _I, _P, _P, _P, _P]),
     "tlmg_set_dense_ffn": (_I, [_P, _I, _I, _P, _P, _P, _P]),

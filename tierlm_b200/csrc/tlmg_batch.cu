@@ -98,8 +98,11 @@ __global__ void __launch_bounds__(32 * RW) k_broute(BatchArgs a, int32_t *__rest
 // in ascending id, [2E + 1] their count, [2E + 2, ..) the pairs t * k + r
 // grouped by expert (in no particular order inside an expert: every pair's
 // results are independent of the others)
+// With rcnt, the records sit in regions of cap slots and record p exists
+// only when p % cap < rcnt[p / cap]; the others are skipped.
 __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids, int istride, int np, int E,
-                                                  int lo, int hi, int32_t *grp, float *eo, int D, int32_t *bad) {
+                                                  int lo, int hi, int32_t *grp, float *eo, int D, int32_t *bad,
+                                                  const int32_t *__restrict__ rcnt, int cap) {
     __shared__ int cnt[RT_PER * 32], off[RT_PER * 32 + 1], fill[RT_PER * 32];
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         cnt[e] = 0;
@@ -107,6 +110,7 @@ __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids
     }
     __syncthreads();
     for (int p = threadIdx.x; p < np; p += blockDim.x) {
+        if (rcnt && p % cap >= rcnt[p / cap]) continue;
         const int e = ids[(size_t)p * istride];
         if (e >= lo && e < hi) {
             atomicAdd(&cnt[e], 1);
@@ -151,6 +155,7 @@ __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids
     __syncthreads();
     for (int e = threadIdx.x; e <= E; e += blockDim.x) grp[e] = off[e];
     for (int p = threadIdx.x; p < np; p += blockDim.x) {
+        if (rcnt && p % cap >= rcnt[p / cap]) continue;
         const int e = ids[(size_t)p * istride];
         if (e >= lo && e < hi) grp[2 * E + 2 + off[e] + atomicAdd(&fill[e], 1)] = p;
     }
@@ -620,9 +625,9 @@ static bool smem_opt_in(F fn, size_t bytes) {
 // x + (q / xdiv) * xstride -> eo[q] (f32 [D]).
 static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn, int D, int de, int E, int lo,
                          int hi, const int32_t *ids, int istride, int64_t np, const uint8_t *x, size_t xstride,
-                         int xdiv, float *eo, cudaStream_t st) {
+                         int xdiv, float *eo, cudaStream_t st, const int32_t *rcnt = nullptr, int cap = 0) {
     const int nsm = sm_count();
-    k_bgroup<<<1, 1024, 0, st>>>(ids, istride, (int)np, E, lo, hi, s.grp, eo, D, s.cnt + EP_MAX_RANKS);
+    k_bgroup<<<1, 1024, 0, st>>>(ids, istride, (int)np, E, lo, hi, s.grp, eo, D, s.cnt + EP_MAX_RANKS, rcnt, cap);
     // at most min(np, E) experts are active
     const int64_t na_max = std::min<int64_t>(np, E);
     const size_t sgu = tgateup_smem(dt_gu, D), sdn = tdown_smem(dt_dn, de);
@@ -767,6 +772,51 @@ int ep_combine(int n, int D, int k, const float *back, const int32_t *perm, cons
     count_launch(1);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "expert-parallel combine launch");
+}
+
+int epp_layer(BatchScratch &s, EpP2P &e, const BatchArgs &a, int lo, int hi, cudaStream_t st) {
+    if (!batch_supported(a.dt_gu, a.dt_dn, a.D, a.de, a.E, a.k))
+        return set_error(TLMG_EUNSUP, "expert-parallel layer: dtypes %d/%d or shape unsupported", a.dt_gu, a.dt_dn);
+    if (!e.base || e.nr > a.E) return set_error(TLMG_EINVAL, "expert-parallel layer: exchange not open");
+    for (int r = 0; r < e.nr; r++)
+        if (!e.peer[r]) return set_error(TLMG_EINVAL, "expert-parallel layer: rank %d not connected", r);
+    if (a.n < 0 || a.n > e.max_tok || (int64_t)a.n * a.k > e.cap || ep_record_bytes(a.D) != e.rb)
+        return set_error(TLMG_EINVAL, "expert-parallel layer: %d tokens (exchange sized for %d)", a.n, e.max_tok);
+    int rc = reserve(s, std::max(a.n, 1), (int64_t)e.nr * e.cap, a.D, a.de, a.E);
+    if (rc) return rc;
+    const int np = a.n * a.k, nsm = sm_count();
+    const uint32_t qx = qvb(a.D / 256);
+    e.epoch++;
+    if (a.n > 0) {
+        k_bquant<<<warp_blocks((int64_t)a.n * (a.D / 256), nsm), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
+        k_broute<<<(a.n + RW - 1) / RW, 32 * RW, 0, st>>>(a, s.ids, s.w);
+        count_launch(2);
+    }
+    k_epcount<<<1, 1024, 0, st>>>(s.ids, np, a.E, e.nr, e.perm, e.cnt);
+    epp_send(e, s.ids, np, a.k, a.E, s.xq, qx, st);
+    epp_barrier(e, 0, st);
+    count_launch(3);
+    const int32_t *rcnt = reinterpret_cast<const int32_t *>(e.base + e.off_rcnt);
+    if ((rc = expert_stage(s, a.slots, a.dt_gu, a.dt_dn, a.D, a.de, a.E, lo, hi, reinterpret_cast<const int32_t *>(e.base),
+                           (int)(e.rb / 4), (int64_t)e.nr * e.cap, e.base + 16, e.rb, 1, e.eo, st, rcnt, e.cap)))
+        return rc;
+    epp_return(e, a.D, st);
+    epp_barrier(e, 1, st);
+    count_launch(2);
+    if (a.n > 0) {
+        const float *back = reinterpret_cast<const float *>(e.base + e.off_back);
+        k_bcombine<<<combine_blocks(a.n, a.D), 256, 0, st>>>(back, e.slot_of, s.w, a.n, a.D, a.k, a.ffn);
+        count_launch(1);
+    }
+    cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? TLMG_OK : cuda_fail(err, "expert-parallel layer launch");
+}
+
+int epp_take_error(BatchScratch &s, EpP2P &e) {
+    if (e.err_host && *reinterpret_cast<volatile uint32_t *>(e.err_host))
+        return set_error(TLMG_EIO, "expert parallel: a peer barrier gave up after 1 s (a rank stopped or fell "
+                                   "behind); the exchange must be reopened");
+    return batch_take_error(s);
 }
 
 }  // namespace tlmg

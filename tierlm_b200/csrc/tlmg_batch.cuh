@@ -76,4 +76,37 @@ int batch_take_error(BatchScratch &s);
 int ep_combine(int n, int D, int k, const float *back, const int32_t *perm, const float *w, float *ffn,
                cudaStream_t st);
 
+// Expert parallelism over peer memory (tlmg_ep.cu): one allocation per rank,
+// mapped by every peer: record regions [nr][cap][rb], record counts
+// [EPP_SLOTS], output-row regions [nr][cap][D] f32, barrier flags
+// [2][EPP_SLOTS]; cap = (token, rank) pairs a home may send one owner.
+constexpr int EPP_SLOTS = 8;
+struct EpP2P {
+    int me = 0, nr = 1, cap = 0, max_tok = 0;
+    size_t rb = 0, off_rcnt = 0, off_back = 0, off_flags = 0, bytes = 0;
+    uint8_t *base = nullptr;             // this rank's allocation
+    uint8_t *peer[EPP_SLOTS] = {};       // every rank's allocation, mapped here (peer[me] = base)
+    bool opened[EPP_SLOTS] = {};         // peer[r] is an IPC mapping to close
+    int32_t *cnt = nullptr;              // [EPP_SLOTS] this call's records per owner
+    int32_t *perm = nullptr;             // [max_tok * k] pair -> record index in owner order
+    int32_t *slot_of = nullptr;          // [max_tok * k] pair -> its output row's index in the row regions
+    float *eo = nullptr;                 // [nr * cap][D] this GPU's expert output rows
+    uint32_t epoch = 0;                  // layer calls since the flags were zeroed
+    uint32_t *err_host = nullptr, *err_dev = nullptr;   // a barrier that gave up
+};
+int epp_alloc(EpP2P &e, int me, int nr, int max_tok, int D, int k);
+void epp_release(EpP2P &e);
+// Launchers of tlmg_ep.cu's kernels (stream-ordered, no host wait).
+void epp_send(const EpP2P &e, const int32_t *ids, int np, int k, int E, const uint8_t *xq, uint32_t qx,
+              cudaStream_t st);
+void epp_return(const EpP2P &e, int D, cudaStream_t st);
+void epp_barrier(const EpP2P &e, int which, cudaStream_t st);
+// One layer call: dispatch, barrier, expert stage, return, barrier, combine.
+// Every rank of the exchange makes the same calls in the same order, n = 0
+// included; a barrier that gave up shows at epp_take_error.
+int epp_layer(BatchScratch &s, EpP2P &e, const BatchArgs &a, int lo, int hi, cudaStream_t st);
+// TLMG_EIO once a barrier gave up (the exchange is then unusable), else the
+// batched kernels' own errors; read after the stream has been synchronised.
+int epp_take_error(BatchScratch &s, EpP2P &e);
+
 }  // namespace tlmg

@@ -1431,6 +1431,12 @@ static int reserve_tokens(FusedScratch &f, int n_tok) {
     return TLMG_OK;
 }
 
+using StreamFn = void (*)(const FusedArgs, const StreamArgs, uint32_t *, uint32_t *);
+struct StreamPlanHost {   // one (gate/up, down) dtype pair's geometry and kernel
+    StreamGeom g;
+    StreamFn fn;
+};
+
 void fused_release(FusedScratch &f) {
     free_tokens(f);
     if (f.bar) cudaFree(f.bar);
@@ -1521,11 +1527,6 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
 }
 
 // ---- the stream kernel's host side
-using StreamFn = void (*)(const FusedArgs, const StreamArgs, uint32_t *, uint32_t *);
-struct StreamPlanHost {
-    StreamGeom g;
-    StreamFn fn;
-};
 static StreamFn pick_stream(int dgu, int ddn) {
 #define TLMG_S(G, DN) \
     if (dgu == G && ddn == DN) return k_stream_ffn<G, DN>;

@@ -112,6 +112,7 @@ struct tlmg_ctx {
     int64_t launch0 = 0;
     FusedScratch fused;
     BatchScratch batch;            // batched-decode scratch (tlmg_expert_ffn_batch)
+    EpP2P epp;                     // peer-memory expert parallelism (tlmg_ep_open)
     ExpertCache cache;             // HBM expert-slot cache (tlmg_cache_enable)
     Slot *pin_slots = nullptr;     // pinned [n_layers][E] slot-table mirror of cached layers
     int32_t *pin_ids = nullptr;    // pinned [64] routed ids of a cached layer
@@ -620,7 +621,7 @@ static int finish_d2h(tlmg_ctx *c, void *dst, size_t bytes, PtrKind k, size_t st
 static int stream_sync(tlmg_ctx *c) {
     cudaError_t e = cudaStreamSynchronize(c->st);
     if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
-    if (int be = batch_take_error(c->batch)) return be;
+    if (int be = epp_take_error(c->batch, c->epp)) return be;
     uint32_t fe = fused_take_error(c->fused);
     if (fe)
         return set_error(TLMG_EIO, "expert FFN kernel gave up waiting (%s%s%s); results of this call are invalid",
@@ -700,6 +701,7 @@ void tlmg_close(tlmg_ctx *c) {
     if (c->own_st) cudaStreamSynchronize(c->own_st);
     fused_release(c->fused);
     batch_release(c->batch);
+    epp_release(c->epp);
     cache_release(c->cache);
     if (c->pin_slots) cudaFreeHost(c->pin_slots);
     if (c->pin_ids) cudaFreeHost(c->pin_ids);
@@ -1328,6 +1330,93 @@ int tlmg_ep_combine(tlmg_ctx *c, int n_tok, const float *back, const int32_t *pe
         return set_error(TLMG_EINVAL, "ep_combine: bad argument");
     cudaSetDevice(c->device);
     return ep_combine(n_tok, c->g.d_model, c->g.top_k, back, perm, w, ffn, c->st);
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism over peer memory
+
+int tlmg_ep_open(tlmg_ctx *c, int rank, int n_ranks, int max_tok) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    if (c->g.n_experts <= 0 || n_ranks > c->g.n_experts)
+        return set_error(TLMG_EINVAL, "ep_open: %d ranks for %d experts", n_ranks, c->g.n_experts);
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->st);
+    return epp_alloc(c->epp, rank, n_ranks, max_tok, c->g.d_model, c->g.top_k);
+}
+
+size_t tlmg_ep_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int tlmg_ep_handle(tlmg_ctx *c, void *handle) {
+    if (!c || !handle) return set_error(TLMG_EINVAL, "ep_handle: NULL argument");
+    if (!c->epp.base) return set_error(TLMG_EINVAL, "ep_handle: exchange not open");
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, c->epp.base);
+    if (e != cudaSuccess) return cuda_fail(e, "ep_handle");
+    memcpy(handle, &h, sizeof h);
+    return TLMG_OK;
+}
+
+int tlmg_ep_connect(tlmg_ctx *c, const void *handles) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    EpP2P &e = c->epp;
+    if (!e.base) return set_error(TLMG_EINVAL, "ep_connect: exchange not open");
+    if (e.nr > 1 && !handles) return set_error(TLMG_EINVAL, "ep_connect: NULL handles");
+    cudaSetDevice(c->device);
+    for (int r = 0; r < e.nr; r++) {
+        if (r == e.me || e.peer[r]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t *)handles + r * sizeof h, sizeof h);
+        void *p = nullptr;
+        cudaError_t err = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (err != cudaSuccess) return cuda_fail(err, "ep_connect: mapping a peer's exchange buffer");
+        e.peer[r] = (uint8_t *)p;
+        e.opened[r] = true;
+    }
+    return TLMG_OK;
+}
+
+int tlmg_ep_layer(tlmg_ctx *c, int layer, int n_tok, const float *x, const float *logits, float *ffn, int32_t *ids,
+                  float *w) {
+    Layer *Ly = nullptr;
+    int rc = ep_layer(c, layer, &Ly);
+    if (rc) return rc;
+    if (n_tok < 0 || (n_tok > 0 && (!x || !logits || !ffn)))
+        return set_error(TLMG_EINVAL, "ep_layer: bad argument");
+    if (n_tok > 0 && (ptr_kind(x) != PK_DEVICE || ptr_kind(logits) != PK_DEVICE || ptr_kind(ffn) != PK_DEVICE ||
+                      (ids && ptr_kind(ids) != PK_DEVICE) || (w && ptr_kind(w) != PK_DEVICE) || ((uintptr_t)x & 15u)))
+        return set_error(TLMG_EINVAL, "ep_layer: x, logits, ffn, ids and w must be device memory, x 16-byte aligned");
+    const int E = c->g.n_experts, nr = c->epp.nr, me = c->epp.me;
+    const int lo = (int)(((int64_t)me * E + nr - 1) / nr), hi = (int)(((int64_t)(me + 1) * E + nr - 1) / nr);
+    for (int e = lo; e < hi; e++)
+        if (!Ly->h_slots[e].ok) return set_error(TLMG_ENOTFOUND, "layer %d: owned expert %d is not loaded", layer, e);
+    BatchArgs a{};
+    a.slots = Ly->d_slots;
+    a.mask = Ly->mask;
+    a.bias = Ly->router_bias;
+    a.n = n_tok;
+    a.D = c->g.d_model;
+    a.de = c->g.d_expert;
+    a.E = E;
+    a.k = c->g.top_k;
+    a.router = c->g.router;
+    a.routed_scale = c->g.routed_scale;
+    a.dt_gu = Ly->dt_gu;
+    a.dt_dn = Ly->dt_dn;
+    a.x = x;
+    a.logits = logits;
+    a.ffn = ffn;
+    a.ids_out = ids;
+    a.w_out = w;
+    return epp_layer(c->batch, c->epp, a, lo, hi, c->st);
+}
+
+int tlmg_ep_close(tlmg_ctx *c) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    cudaSetDevice(c->device);
+    int rc = stream_sync(c);
+    epp_release(c->epp);
+    return rc;
 }
 
 }  // extern "C"

@@ -134,3 +134,55 @@ class ExpertParallel:
         if check and hasattr(self.b, "check"):
             self.b.check()
         return {"sent": sent, "received": received}
+
+
+class PeerExpertParallel:
+    """ExpertParallel with the exchange done by the library over peer memory
+    (tlmg_ep_open / tlmg_ep_layer, include/tlmg.h): each rank maps every
+    peer's exchange buffer through CUDA IPC, and one layer call queues
+    dispatch, the owner's experts, the return of the rows and the combine
+    on the stream, ordered by two bounded device barriers over peer flags:
+    no host synchronisation and no collective in the data path. Results are
+    bit-identical to ExpertParallel and to the one-GPU batched call.
+
+    torch.distributed is used once, to exchange the buffers' IPC handles.
+    All ranks must sit on GPUs of one node."""
+
+    def __init__(self, backend, d_model: int, n_experts: int, top_k: int, max_tok: int, group=None,
+                 device: torch.device | None = None):
+        self.b = backend
+        self.D, self.E, self.k = d_model, n_experts, top_k
+        self.group = group
+        self.n_ranks = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.max_tok = max_tok
+        if hasattr(backend, "set_stream"):
+            backend.set_stream(torch.cuda.current_stream(self.device))
+        self.lo, self.hi = owned_range(self.rank, self.n_ranks, n_experts)
+        mine = backend.ep_open(self.rank, self.n_ranks, max_tok)
+        handles = [mine]
+        if self.n_ranks > 1:
+            handles = [None] * self.n_ranks
+            dist.all_gather_object(handles, mine, group=self.group)
+        backend.ep_connect(handles)
+        torch.cuda.synchronize(self.device)
+        if self.n_ranks > 1:
+            dist.barrier(group=self.group)   # every peer mapped before the first device barrier
+
+    def ffn_batch(self, layer: int, x: torch.Tensor, logits: torch.Tensor, ffn: torch.Tensor,
+                  check: bool = True, ids: torch.Tensor | None = None, w: torch.Tensor | None = None) -> None:
+        """x [n][D], logits [n][E] -> ffn [n][D] for this process's n tokens
+        (n <= max_tok, may be 0; every rank calls with the same layers in
+        the same order). With `check` the call waits for the stream and
+        raises what the kernels flagged (a barrier that gave up, a
+        tensor-core wait that expired); otherwise that shows at a later
+        check."""
+        if x.shape[0] > self.max_tok:
+            raise ValueError(f"{x.shape[0]} tokens; the exchange was opened for {self.max_tok}")
+        self.b.ep_layer(layer, x, logits, ffn, ids, w)
+        if check:
+            self.b.check()
+
+    def close(self) -> None:
+        self.b.ep_close()

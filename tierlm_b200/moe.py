@@ -220,6 +220,28 @@ class MoeContext:
         """Home side: ffn[t] = sum_r w[t, r] * back[perm[t, r]] in ascending r."""
         check(self._lib.tlmg_ep_combine(self._h, n_tok, _ptr(back), _ptr(perm), _ptr(w), _ptr(ffn)))
 
+    def ep_open(self, rank: int, n_ranks: int, max_tok: int) -> bytes:
+        """Opens this rank's peer-memory exchange; returns its handle (bytes
+        to hand to every peer)."""
+        check(self._lib.tlmg_ep_open(self._h, rank, n_ranks, max_tok))
+        buf = C.create_string_buffer(self._lib.tlmg_ep_handle_bytes())
+        check(self._lib.tlmg_ep_handle(self._h, buf))
+        return buf.raw
+
+    def ep_connect(self, handles: list[bytes]) -> None:
+        """Maps every peer's exchange buffer (handles in rank order)."""
+        check(self._lib.tlmg_ep_connect(self._h, b"".join(handles)))
+
+    def ep_layer(self, layer: int, x, logits, ffn, ids=None, w=None) -> None:
+        """One expert-parallel layer over peer memory (device tensors):
+        ffn = the routed experts' combine of x; no host wait."""
+        n = x.shape[0]
+        check(self._lib.tlmg_ep_layer(self._h, layer, n, _ptr(x) if n else None, _ptr(logits) if n else None,
+                                      _ptr(ffn) if n else None, _ptr(ids), _ptr(w)))
+
+    def ep_close(self) -> None:
+        check(self._lib.tlmg_ep_close(self._h))
+
     def moe_layer(self, layer: int, h, ids=None, w=None, onorm=None) -> None:
         """moe() of one token (h += ffn in place); onorm receives the route
         hook's per-rank output norms."""
