@@ -224,6 +224,86 @@ def build_context(args, dev, seed: int):
     return ctx
 
 
+def decode_step_section(ctx, args, dev, g, peak: float) -> dict:
+    """BASELINE config 3 through tlmg_decode_step: Qwen3-30B-A3B shape
+    (48 layers, D 2048, 32 q / 4 KV heads x 128 with qk-norm, 128 experts
+    top-8, de 768, vocab 151,936), attention and down Q6_K, gate/up and
+    embedding Q4_K, router f32, lm_head Q6_K, random weights; bf16 KV pages
+    and split attention. A random prompt is stepped position by position
+    (no lm_head, as the reference's prefill), then greedy decode: each token
+    is the argmax of the previous step's logits, read by the host."""
+    import torch
+
+    from tierlm_b200 import synth
+    H, KVH, HD, V = 32, 4, 128, 151936
+    DT_ATT, DT_EMB, DT_HEAD, BF16, SPLIT = 14, 12, 14, 2, 1
+    L, P, NG = args.layers, args.step_prompt, args.step_gen
+    rng = np.random.default_rng(77)
+    inv = np.array([np.float32(1e6 ** (-2.0 * j / HD)) for j in range(HD // 2)], np.float32)
+    ctx.step_open(H, KVH, HD, V, inv, 1.0, max_ctx=P + NG, kv_dtype=BF16, attn_mode=SPLIT)
+    def norm(n):
+        return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    for layer in range(L):
+        ctx.set_layer(layer, norm(D), 0, (0.02 * rng.standard_normal((E, D))).astype(np.float32), 4 * D)
+        mats = [synth.device_rows(DT_ATT, r, c, g, dev) for r, c in ((H * HD, D), (KVH * HD, D), (KVH * HD, D),
+                                                                     (D, H * HD))]
+        ctx.set_attention(layer, norm(D), (DT_ATT,) * 4, *mats, q_norm=norm(HD), k_norm=norm(HD))
+        del mats
+    emb = synth.device_rows(DT_EMB, V, D, g, dev)
+    ctx.set_embedding(DT_EMB, emb)
+    del emb
+    head = synth.device_rows(DT_HEAD, V, D, g, dev)
+    ctx.set_output(norm(D), DT_HEAD, head)
+    del head
+    torch.cuda.synchronize(dev)
+    prompt = [int(t) for t in rng.integers(0, V, P)]
+    logits = torch.empty(V, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def run(n_warm=0):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(st)
+        for pos, tok in enumerate(prompt):
+            ctx.decode_step(tok, pos, logits if pos == P - 1 else None)
+        ev[1].record(st)
+        toks = []
+        tok = int(torch.argmax(logits))
+        h0 = time.perf_counter()
+        for i in range(NG):
+            ctx.decode_step(tok, P + i, logits)
+            tok = int(torch.argmax(logits))            # the host needs the token for the next step
+            toks.append(tok)
+        wall = time.perf_counter() - h0
+        ev[2].record(st)
+        torch.cuda.synchronize(dev)
+        return ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]), wall, toks
+
+    run()                                                   # warm-up pass (same positions)
+    n0 = ctx.launches
+    pre_ms, dec_ms, wall, toks = run()
+    launches = ctx.launches - n0
+    # algorithmic bytes per decode token: weights read once + the KV rows read
+    rb = lambda dt, n: n // 256 * {12: 144, 14: 210}[dt]   # noqa: E731
+    attn_w = (H * HD + 2 * KVH * HD) * rb(DT_ATT, D) + D * rb(DT_ATT, H * HD)
+    per_layer = attn_w + E * D * 4 + BYTES_LAYER_TOKEN + 4 * (2 * D + 2 * HD)
+    T_mean = P + (NG + 1) / 2
+    kv = 2 * KVH * HD * 2 * T_mean
+    bytes_tok = L * (per_layer + kv) + V * rb(DT_HEAD, D) + rb(DT_EMB, D) + 4 * D
+    tps = NG / (dec_ms * 1e-3)
+    return {"metric": "decode tok/s, bs=1, whole step (BASELINE config 3)",
+            "tokens_per_s": round(tps, 1), "ms_per_token": round(dec_ms / NG, 3),
+            "prefill_tokens_per_s": round(P / (pre_ms * 1e-3), 1),
+            "host_wall_tokens_per_s": round(NG / wall, 1),
+            "bytes_per_token": int(bytes_tok), "GBps": round(bytes_tok * tps / 1e9, 1),
+            "roofline_tokens_per_s": round(peak * 1e9 / bytes_tok, 1),
+            "frac": round(bytes_tok * tps / 1e9 / peak, 4),
+            "gpu_launches_per_token": round(launches / (P + NG), 1),
+            "prompt": P, "generated": NG, "kv": "bf16 pages, split attention", "distinct_tokens": len(set(toks)),
+            "api": "tlmg_decode_step per position; greedy token read by the host each step",
+            "weights": "random: attention/down/lm_head Q6_K, gate/up/embedding Q4_K, router f32"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -235,6 +315,11 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="batched-decode section: tokens per layer call (<= 1: off)")
     ap.add_argument("--prefill", type=int, default=2048, help="prefill section: prompt tokens per layer call (0: off)")
+    ap.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
+                    help="batched-decode section at N > 1: expert-parallel exchange over peer memory or NCCL")
+    ap.add_argument("--step-prompt", type=int, default=512,
+                    help="decode-step section (config 3): prompt positions before the timed decode (0: off)")
+    ap.add_argument("--step-gen", type=int, default=256, help="decode-step section: greedy tokens timed")
     ap.add_argument("--cache-layers", type=int, default=0, help="slot-cache section: layers (0: off)")
     ap.add_argument("--cache-frac", type=float, default=0.5, help="slot-cache section: HBM slots / experts")
     ap.add_argument("--attn-ctx", default="",
@@ -355,8 +440,9 @@ def main() -> None:
         bytes_expert = BYTES_LAYER_TOKEN // K
         ep = None
         if world > 1:
-            from tierlm_b200.ep import ExpertParallel
-            ep = ExpertParallel(ctx, D, E, K, device=dev)
+            from tierlm_b200.ep import ExpertParallel, PeerExpertParallel
+            ep = (PeerExpertParallel(ctx, D, E, K, B, device=dev) if args.ep_exchange == "peer"
+                  else ExpertParallel(ctx, D, E, K, device=dev))
 
         def layer_call(layer, xi, li, oi):
             if ep is None:
@@ -394,6 +480,12 @@ def main() -> None:
         for s in range(args.warmup):
             bstep_host(s)
         bms_e2e = timed(bstep_host, args.steps)
+        if hasattr(ep, "close"):
+            torch.cuda.synchronize(dev)
+            dist.barrier()   # every rank's layer calls are done before any exchange buffer is unmapped
+            ep.close()
+        exch = ("peer-memory exchange, device barriers" if args.ep_exchange == "peer"
+                else "NCCL all-to-all")
         batch = {"batch": B, "metric": f"decode tok/s, bs={B} per GPU, expert FFN of {L} layers per token",
                  "tokens_per_s": round(world * args.steps * B / (bms * 1e-3), 1),
                  "ms_per_step": bms / args.steps,
@@ -401,11 +493,11 @@ def main() -> None:
                  "unique_experts_per_layer": round(float(uniq.mean()), 2),
                  "gpu_launches": blaunch,
                  "kernels": "tcgen05.mma kind::i8 gate/up and down (one TMEM accumulator per sub-block)",
-                 "parallelism": "single GPU" if world == 1 else f"expert-parallel x{world} (NCCL all-to-all)",
+                 "parallelism": "single GPU" if world == 1 else f"expert-parallel x{world} ({exch})",
                  "e2e": {"tokens_per_s": round(world * args.steps * B / (bms_e2e * 1e-3), 1),
                          "h2d_bytes_per_step": L * B * (D + E) * 4, "d2h_bytes_per_step": L * B * D * 4,
                          "api": "tlmg_expert_ffn_batch (pinned host buffers)" if world == 1 else
-                                "ExpertParallel.ffn_batch with pinned host copies in the step"},
+                                f"{type(ep).__name__}.ffn_batch with pinned host copies in the step"},
                  "note": "one call per layer serves all B tokens; each selected expert is read once per call"}
 
     # ---- prefill: PREFILL tokens of one GPU's prompt through each layer's experts, one call per layer
@@ -543,6 +635,11 @@ def main() -> None:
                 del graph, pools
             attn["contexts"][str(T)] = row
 
+    # ---- the whole decoder step: embedding, 48 x (attention + MoE), lm_head
+    dstep = None
+    if args.step_prompt > 0 and world == 1:
+        dstep = decode_step_section(ctx, args, dev, g, peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -574,7 +671,7 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": kbytes,
                          "timing": "per-launch CUDA events on the launch stream, second pass of the same steps"},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": launches,
-            "prefill": prefill, "slot_cache": cache, "decode_attention": attn,
+            "prefill": prefill, "decode_step": dstep, "slot_cache": cache, "decode_attention": attn,
             # last key: the bs=64 (expert-parallel at N > 1) decode section
             "batched_decode": batch,
         }

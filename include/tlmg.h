@@ -74,6 +74,13 @@ int tlmg_quantize_act(int kind, const float *x, int64_t n, void *dst, void *stre
 int tlmg_matvec_rows(int dt, const void *W, size_t row_bytes, const void *act, float *y,
                      int64_t n, int64_t r0, int64_t r1, void *stream);
 
+/* Dequantisation of `rows` rows of n elements (row stride row_bytes),
+ * replaces tlm_dequantize_row (src/lib/tlm_quant.h, src/lib/tlm_quant.c:
+ * 629-675) for every dtype but MXFP4 / FP8: src device, y device f32
+ * [rows][n], bit-identical to the reference. */
+int tlmg_dequantize_rows(int dt, const void *src, size_t row_bytes, float *y, int64_t n, int64_t rows,
+                         void *stream);
+
 /* Per-block exact integer partials of rows [0, nrows) (integer formats):
  * isum/msum: device int32[nrows * n/block]. These are the int32 sums the
  * reference's scalar dots form before their fmaf chain
@@ -323,6 +330,39 @@ int tlmg_ep_experts(tlmg_ctx *ctx, int layer, int e_lo, int e_hi, int64_t n_rec,
  * ascending r (back = the expert output rows returned in record order). */
 int tlmg_ep_combine(tlmg_ctx *ctx, int n_tok, const float *back, const int32_t *perm,
                     const float *w, float *ffn);
+
+/* ---- The whole decoder step on the GPU (tlm_model_step,
+ * src/lib/tlm_model.c:1058-1103): embedding row, per layer attention()
+ * (:730-763: RMSNorm, q/k/v, qk-norm, NeoX RoPE, the K/V write, decode
+ * attention, o-proj, h += o) and moe() (the MoE block above), then the
+ * final RMSNorm and lm_head. Every value is formed in the reference's
+ * order of operations; with TLMG_ATTN_EXACT and F32 KV pages the logits
+ * are bit-identical to the reference's when its expf is correctly
+ * rounded (the GPU's is). The MoE layers are set as for tlmg_moe_layer. */
+
+/* Opens the step: heads, KV heads and head_dim of attention, the vocab,
+ * the RoPE inverse frequencies inv_freq[head_dim / 2] and attention scale
+ * exactly as the reference's model holds them (tlm_model_open, plain or
+ * YaRN-transformed), KV pages for max_ctx positions per layer (kv_dt F32
+ * or BF16) and the attention mode (TLMG_ATTN_EXACT or _SPLIT). */
+int tlmg_step_open(tlmg_ctx *ctx, int n_heads, int n_kv_heads, int head_dim, int vocab,
+                   const float *inv_freq, float attn_scale, int max_ctx, int kv_dt, int attn_mode);
+/* Attention weights of one layer (host or device memory, copied):
+ * attn_norm f32[D]; dt[4] / w[4] / rb[4] = q [H*hd][D], k and v
+ * [KV*hd][D], o [D][H*hd] (rb 0 = packed rows); q_norm / k_norm
+ * f32[head_dim] or NULL. */
+int tlmg_set_attention(tlmg_ctx *ctx, int layer, const float *attn_norm, const int32_t *dt,
+                       const void *const *w, const size_t *rb, const float *q_norm, const float *k_norm);
+/* Token embedding [vocab][D] of dtype dt (row_bytes 0 = packed). */
+int tlmg_set_embedding(tlmg_ctx *ctx, int dt, const void *tok_embd, size_t row_bytes);
+/* output_norm f32[D] and lm_head [vocab][D] of dtype dt. */
+int tlmg_set_output(tlmg_ctx *ctx, const float *out_norm, int dt, const void *lm_head, size_t row_bytes);
+/* One position: token at position pos (0 <= pos < max_ctx; positions
+ * 0..pos-1 must have been stepped before, pos = 0 starts a new sequence)
+ * -> logits f32[vocab] (host or device; NULL: no lm_head, as the
+ * reference's prefill steps). Device logits: asynchronous on the
+ * context's stream; host logits: the call waits. */
+int tlmg_decode_step(tlmg_ctx *ctx, int token, int pos, float *logits);
 
 /* ---- Expert parallelism over peer memory (one process per GPU, all GPUs
  * of one node). The same split as above, with the exchange done by the

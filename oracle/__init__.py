@@ -147,6 +147,15 @@ def dequantize_row(dt: int, src: np.ndarray, n: int) -> np.ndarray:
     return y
 
 
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """rmsnorm (src/lib/tlm_model.c:164-169): x * (1 / sqrtf(mean(x^2) + eps)) * w."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.zeros_like(x)
+    lib().tlmo_rmsnorm(_p(out), _p(x), _p(w), x.size, eps)
+    return out
+
+
 def vec_dot(dt: int, wrow: np.ndarray, act: np.ndarray, n: int) -> float:
     return float(lib().tlmo_vec_dot(dt, _p(wrow), _p(act), n))
 

@@ -11,7 +11,9 @@ It drives three things built by oracle/Makefile (`make -C oracle gate`):
   tlm_model.c with the store opened as `tierlm` opens it, stepping tokens
   through tlm_model_step (REF), a call-for-call restatement of it (CPU), or
   the restatement with every moe() served by libtlmg's tlmg_moe_layer_ex
-  (GPU). The `_cr` build binds tlm_model.c's expf to a correctly rounded
+  (GPU), or libtlmg's whole decoder step, tlmg_decode_step, with the
+  store's attention, embedding and lm_head weights and the KV pages on the
+  GPU too (STEP). The `_cr` build binds tlm_model.c's expf to a correctly rounded
   expf, the one the CUDA tier computes.
 """
 from __future__ import annotations
@@ -31,7 +33,7 @@ TLMC = HERE / "_ref" / "bin" / "tlmc"
 STORE_DIR = HERE / "_ref" / "stores"
 LIBS = {False: HERE / "_ref" / "libtlmgate.so", True: HERE / "_ref" / "libtlmgate_cr.so"}
 
-REF, CPU, GPU = 0, 1, 2
+REF, CPU, GPU, STEP = 0, 1, 2, 3
 
 _TINY = ["--layers", "4", "--experts", "32", "--top-k", "4", "--shared", "1", "--d-model", "512", "--heads", "8",
          "--kv-heads", "2", "--head-dim", "64", "--vocab", "4096", "--d-expert", "256", "--seed", "1"]

@@ -13,6 +13,8 @@
  *   GATE_CPU  gate_step_impl(): tlm_model_step restated call for call with
  *             the reference's own moe() (GATE_REF == GATE_CPU bit for bit is
  *             what shows the restatement is faithful);
+ *   GATE_STEP tlmg_decode_step: the whole step (embedding, attention, MoE,
+ *             lm_head) on the GPU, the KV pages in HBM;
  *   GATE_GPU  gate_step_impl() with every moe() (src/lib/tlm_model.c:
  *             940-1055) replaced by tlmg_moe_layer_ex on the GPU: RMSNorm,
  *             router, experts, shared expert or the dense FFN, h += ffn.
@@ -43,7 +45,7 @@ static float gate_cr_expf(float x) { return (float)expl((long double)x); }
 #include "tlm_store.h"
 #include "tlmg.h"
 
-enum { GATE_REF = 0, GATE_CPU = 1, GATE_GPU = 2 };
+enum { GATE_REF = 0, GATE_CPU = 1, GATE_GPU = 2, GATE_STEP = 3 };
 
 typedef struct {
     tlm_manifest m;
@@ -220,6 +222,26 @@ int gate_attach_gpu(void *p, int device) {
             if (rc) { snprintf(g_err, sizeof g_err, "layer %d expert %d: %s", l, e, tlmg_errmsg()); return rc; }
         }
     }
+    /* the rest of the step: attention weights, embedding, output (KV f32,
+     * exact attention: the reference's order of operations) */
+    rc = tlmg_step_open(G->gpu, (int)g->n_heads, (int)g->n_kv_heads, (int)g->head_dim, (int)g->vocab, M->inv_freq,
+                        M->rope_attn_scale, G->kv->max_ctx, TLMG_DT_F32, TLMG_ATTN_EXACT);
+    for (int l = 0; l < (int)g->n_layers && !rc; l++) {
+        layer_w *L = &M->L[l];
+        const wmat *q[4] = { &L->q, &L->k, &L->v, &L->o };
+        int32_t dt[4];
+        const void *w[4];
+        size_t rb[4];
+        for (int i = 0; i < 4; i++) {
+            dt[i] = (int32_t)q[i]->dt;
+            w[i] = q[i]->data;
+            rb[i] = q[i]->row_bytes;
+        }
+        rc = tlmg_set_attention(G->gpu, l, L->attn_norm, dt, w, rb, L->q_norm, L->k_norm);
+    }
+    if (!rc) rc = tlmg_set_embedding(G->gpu, (int)M->embd.dt, M->embd.data, M->embd.row_bytes);
+    if (!rc) rc = tlmg_set_output(G->gpu, M->out_norm, (int)M->lm_head.dt, M->lm_head.data, M->lm_head.row_bytes);
+    if (rc) { snprintf(g_err, sizeof g_err, "decoder step: %s", tlmg_errmsg()); return rc; }
     return 0;
 }
 
@@ -279,6 +301,14 @@ static int gate_step_impl(gate *G, tlm_kv *kv, int token, float *logits) {
 
 static int step_mode(gate *G, int mode, int token, float *logits) {
     if (mode == GATE_REF) return tlm_model_step(G->M, G->kv, token, logits);
+    if (mode == GATE_STEP) {
+        if (!G->gpu) return tlm_seterr(TLM_EINVAL, "gate: no GPU attached");
+        const int pos = G->kv->len;
+        if (pos >= G->kv->max_ctx) return tlm_seterr(TLM_ERANGE, "context full (%d tokens)", G->kv->max_ctx);
+        if (tlmg_decode_step(G->gpu, token, pos, logits)) return tlm_seterr(TLM_EIO, "tlmg_decode_step: %s", tlmg_errmsg());
+        G->kv->len = pos + 1;
+        return TLM_OK;
+    }
     if (mode == GATE_GPU && !G->gpu) return tlm_seterr(TLM_EINVAL, "gate: no GPU attached");
     G->use_gpu = mode == GATE_GPU;
     int rc = gate_step_impl(G, G->kv, token, logits);

@@ -16,6 +16,9 @@ attention and lm_head stay on the reference's CPU code in both.
   so are the route hook's ids, weights and output norms.
 - tests/golden/moe_ref.npz holds the reference's moe() outputs on these
   stores; the CPU oracle and the GPU reproduce them.
+- The whole step on the GPU (tlmg_decode_step: embedding, attention with
+  the KV pages in HBM, the MoE blocks, lm_head): the same gate, and bit
+  identity with the correctly rounded expf.
 """
 from __future__ import annotations
 
@@ -206,3 +209,36 @@ def test_bit_identical_with_correctly_rounded_expf(name):
         assert n_a == n_b
         if n_a:
             assert np.array_equal(ia, ib) and np.array_equal(bits(wa), bits(wb)) and np.array_equal(bits(oa), bits(ob))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", list(G.STORES))
+def test_whole_step_on_gpu(name):
+    """tlmg_decode_step runs every part of tlm_model_step on the GPU.
+    With the correctly rounded expf its logits equal the reference's bit for
+    bit at every position of the greedy run (64 prompt + 64 generated
+    tokens) and of a teacher-forced run over that sequence. With libm expf
+    it passes north_star's gate as test_greedy_and_teacher_forced_gate
+    states it: the same tokens, the same argmax everywhere, logits within
+    LOGIT_RTOL plus twice the reference's own expf sensitivity."""
+    with _gpu_gate(name, True) as g:
+        prompt = G.xorshift_prompt(PROMPT, g.vocab)
+        t_ref, l_ref = g.generate(G.REF, prompt, N_GEN)
+        t_gpu, l_gpu = g.generate(G.STEP, prompt, N_GEN)
+        assert np.array_equal(t_ref, t_gpu)
+        assert np.array_equal(bits(l_ref), bits(l_gpu))
+        seq = np.concatenate([prompt, t_ref])
+        assert np.array_equal(bits(g.teacher(G.REF, seq)), bits(g.teacher(G.STEP, seq)))
+    with _gpu_gate(name, False) as g:
+        t_ref, l_ref = g.generate(G.REF, prompt, N_GEN)
+        t_gpu, l_gpu = g.generate(G.STEP, prompt, N_GEN)
+        assert np.array_equal(t_ref, t_gpu), (t_ref, t_gpu)
+        seq = np.concatenate([prompt, t_ref])
+        f_ref = g.teacher(G.REF, seq)
+        f_gpu = g.teacher(G.STEP, seq)
+    sens_g, sens_f = _sensitivity(name, prompt, seq)
+    for i in range(l_ref.shape[0]):
+        assert rel_l2(l_gpu[i], l_ref[i]) <= LOGIT_RTOL + 2 * sens_g[i], (i, sens_g[i])
+    assert np.array_equal(f_ref.argmax(1), f_gpu.argmax(1))
+    for i in range(len(seq)):
+        assert rel_l2(f_gpu[i], f_ref[i]) <= LOGIT_RTOL + 2 * sens_f[i], (i, sens_f[i])

@@ -101,6 +101,28 @@ def test_matvec_random_vs_oracle(dev, orc, dt):
         assert bad.size == 0, (dt, n, bad[:5], got[bad[:5]], ref[bad[:5]])
 
 
+@pytest.mark.parametrize("dt", [0, 1, 2, 8, 12, 13, 14, 15])
+def test_dequantize_rows_vs_oracle(dev, orc, dt):
+    """tlmg_dequantize_rows (the decoder step's embedding gather) against
+    the oracle's tlm_dequantize_row restatement, bit for bit, on rows that
+    start at odd byte offsets (a padded row stride)."""
+    from tierlm_b200 import quant, synth
+    rng = np.random.default_rng(300 + dt)
+    rows, n = 37, 2048
+    if dt in (0, 1, 2):
+        wf = rng.standard_normal((rows, n)).astype(np.float32)
+        W = wf if dt == 0 else (wf.astype(np.float16) if dt == 1 else (wf.view(np.uint32) >> 16).astype(np.uint16))
+        Wb = np.ascontiguousarray(W).view(np.uint8).reshape(rows, -1)
+    else:
+        Wb = synth.rand_rows(dt, rows, n, rng)
+    rb = Wb.shape[1] + 3                                   # odd stride: every row at a different alignment
+    Wp = np.zeros((rows, rb), np.uint8)
+    Wp[:, : Wb.shape[1]] = Wb
+    ref = np.stack([orc.dequantize_row(dt, Wb[r], n) for r in range(rows)])
+    y = quant.dequantize_rows(dt, to_dev(Wp, dev), rb, n, rows)
+    assert same_bits(y.cpu().numpy(), ref).all(), dt
+
+
 @pytest.mark.parametrize("dt", [8, 12, 13, 14, 15, 39])
 def test_block_partials_vs_oracle(dev, orc, dt):
     """Integer block dot-product partial sums, bit-exact."""

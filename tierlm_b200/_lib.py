@@ -64,6 +64,7 @@ _SIGS = {
     "tlmg_act_kind_for": (_I, [_I]),
     "tlmg_quantize_act": (_I, [_I, _P, _I64, _P, _P]),
     "tlmg_matvec_rows": (_I, [_I, _P, _SZ, _P, _P, _I64, _I64, _I64, _P]),
+    "tlmg_dequantize_rows": (_I, [_I, _P, _SZ, _P, _I64, _I64, _P]),
     "tlmg_block_partials": (_I, [_I, _P, _SZ, _P, _I64, _I64, _P, _P, _P]),
     "tlmg_route": (_I, [_I, _P, _P, _P, _I, _I, _F, _P, _P, _P]),
     "tlmg_attention_work_bytes": (_SZ, [_I, _I, _I, _I, _I, _I]),
@@ -83,6 +84,11 @@ _SIGS = {
     "tlmg_ep_dispatch": (_I, [_P, _I, _I, _P, _P, _I, _P, _P, _P, _P]),
     "tlmg_ep_experts": (_I, [_P, _I, _I, _I, _I64, _P, _P]),
     "tlmg_ep_combine": (_I, [_P, _I, _P, _P, _P, _P]),
+    "tlmg_step_open": (_I, [_P, _I, _I, _I, _I, _P, C.c_float, _I, _I, _I]),
+    "tlmg_set_attention": (_I, [_P, _I, _P, _P, _P, _P, _P, _P]),
+    "tlmg_set_embedding": (_I, [_P, _I, _P, _SZ]),
+    "tlmg_set_output": (_I, [_P, _P, _I, _P, _SZ]),
+    "tlmg_decode_step": (_I, [_P, _I, _I, _P]),
     "tlmg_ep_open": (_I, [_P, _I, _I, _I]),
     "tlmg_ep_handle_bytes": (_SZ, []),
     "tlmg_ep_handle": (_I, [_P, _P]),

@@ -99,6 +99,37 @@ __device__ __forceinline__ float cr_expf(float xf) {
     return __double2float_rn(__dmul_rn(p, s));
 }
 // silu(x) = x / (1 + expf(-x)) (reference tlm_model.c:171)
+// 1 / sqrtf((float)(ss / n) + eps), ss = sum of x[i]^2 in double: the
+// reference's RMSNorm scale (rmsnorm, src/lib/tlm_model.c:164-169), whose
+// ss is a serial double sum. Every thread of the block calls this (blockDim
+// a multiple of 32, at most 1024): a tree sum of the exact squares gives
+// ss within an error bound; when both ends of the bound round to the same
+// float mean that is the reference's float, else thread 0 runs the serial
+// sum. red: shared [32], r_sh: shared.
+__device__ __forceinline__ float block_rms_inv(const float *x, int n, float eps, double *red, float *r_sh) {
+    double s = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __dadd_rn(s, __dmul_rn((double)x[i], (double)x[i]));
+    for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int q = 0; q < (int)(blockDim.x >> 5); q++) t = __dadd_rn(t, red[q]);
+        const double bound = __dmul_rn(t, __dmul_rn(2.0 * (double)n + 8.0, 0x1p-53));
+        const float flo = __double2float_rn(__ddiv_rn(__dsub_rn(t, bound), (double)n));
+        const float fhi = __double2float_rn(__ddiv_rn(__dadd_rn(t, bound), (double)n));
+        float f = flo;
+        if (flo != fhi) {
+            double q = 0.0;
+            for (int i = 0; i < n; i++) q = __dadd_rn(q, __dmul_rn((double)x[i], (double)x[i]));
+            f = __double2float_rn(__ddiv_rn(q, (double)n));
+        }
+        *r_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, eps)));
+    }
+    __syncthreads();
+    return *r_sh;
+}
+
 __device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, cr_expf(-x))); }
 __device__ __forceinline__ float sigmoid_f(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, cr_expf(-x))); }
 

@@ -22,8 +22,9 @@ int64_t launches_total();
 
 // Launchers of the kernel-level ops (also used by the layer code).
 int launch_quant_act(int kind, const float *x, int64_t n, void *dst, cudaStream_t st);
+// With res: y[r] = res[r] + dot (res may be y itself).
 int launch_matvec(int dt, const void *W, size_t rb, const void *act, float *y, int64_t n, int64_t r0,
-                  int64_t r1, cudaStream_t st);
+                  int64_t r1, cudaStream_t st, const float *res = nullptr);
 int launch_route(int router, const float *logits, const uint8_t *mask, const float *bias, int E, int k,
                  float routed_scale, int32_t *ids, float *w, cudaStream_t st);
 

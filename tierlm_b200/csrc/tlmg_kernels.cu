@@ -105,7 +105,7 @@ constexpr int MV_CHUNK = FCHUNK;
 template <int A>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_q(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act,
-           float *__restrict__ y, int64_t n, int64_t r0, int64_t r1) {
+           float *y, int64_t n, int64_t r0, int64_t r1, const float *res) {
     __shared__ BlockPart part[MV_WARPS][MV_CHUNK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
     const int qk = dt_block(dt), bb = dt_block_bytes(dt), abb = act_block_bytes(act_kind_for(dt));
@@ -138,7 +138,7 @@ k_matvec_q(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__re
                 }
             __syncwarp();
         }
-        if (lane == 0) y[row] = acc;
+        if (lane == 0) y[row] = res ? __fadd_rn(res[row], acc) : acc;
     }
 }
 
@@ -147,7 +147,7 @@ k_matvec_q(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__re
 template <int A>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_f(int dt, const uint8_t *__restrict__ W, size_t rb, const float *__restrict__ x,
-           float *__restrict__ y, int64_t n, int64_t r0, int64_t r1) {
+           float *y, int64_t n, int64_t r0, int64_t r1, const float *res) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int64_t row = r0 + (int64_t)blockIdx.x * MV_WARPS + warp; row < r1;
          row += (int64_t)gridDim.x * MV_WARPS) {
@@ -161,7 +161,7 @@ k_matvec_f(int dt, const uint8_t *__restrict__ W, size_t rb, const float *__rest
             acc = __fmaf_rn(w, __ldg(x + i), acc);
         }
         acc = tree32(acc);
-        if (lane == 0) y[row] = acc;
+        if (lane == 0) y[row] = res ? __fadd_rn(res[row], acc) : acc;
     }
 }
 
@@ -184,7 +184,7 @@ __global__ void k_fill_nan(float *y, int64_t r0, int64_t r1) {
 }
 
 int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, int64_t n, int64_t r0,
-                  int64_t r1, cudaStream_t st) {
+                  int64_t r1, cudaStream_t st, const float *res) {
     int qk = dt_block(dt);
     if (qk == 0 || n < 0 || n % qk) {
         if (r1 > r0) {
@@ -201,17 +201,17 @@ int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, 
     if (qk == 1) {
         const float *x = (const float *)act;
         switch (A) {
-        case 16: case 4: k_matvec_f<4><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1); break;
-        case 2: k_matvec_f<2><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1); break;
-        default: k_matvec_f<1><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1); break;
+        case 16: case 4: k_matvec_f<4><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
+        case 2: k_matvec_f<2><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
+        default: k_matvec_f<1><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
         }
     } else {
         const uint8_t *a = (const uint8_t *)act;
         switch (A) {
-        case 16: k_matvec_q<16><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
-        case 4: k_matvec_q<4><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
-        case 2: k_matvec_q<2><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
-        default: k_matvec_q<1><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1); break;
+        case 16: k_matvec_q<16><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
+        case 4: k_matvec_q<4><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
+        case 2: k_matvec_q<2><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
+        default: k_matvec_q<1><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
         }
     }
     count_launch();

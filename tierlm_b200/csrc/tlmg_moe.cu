@@ -13,6 +13,7 @@
 #include "tlmg_cache.cuh"
 #include "tlmg_fused.cuh"
 #include "tlmg_internal.h"
+#include "tlmg_step.cuh"
 
 namespace tlmg {
 
@@ -113,6 +114,7 @@ struct tlmg_ctx {
     FusedScratch fused;
     BatchScratch batch;            // batched-decode scratch (tlmg_expert_ffn_batch)
     EpP2P epp;                     // peer-memory expert parallelism (tlmg_ep_open)
+    StepModel *step = nullptr;     // the whole decoder step (tlmg_step_open)
     ExpertCache cache;             // HBM expert-slot cache (tlmg_cache_enable)
     Slot *pin_slots = nullptr;     // pinned [n_layers][E] slot-table mirror of cached layers
     int32_t *pin_ids = nullptr;    // pinned [64] routed ids of a cached layer
@@ -323,29 +325,7 @@ __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__
                           float *__restrict__ out) {
     __shared__ double red[32];
     __shared__ float r_sh;
-    double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __dadd_rn(s, __dmul_rn((double)x[i], (double)x[i]));
-    for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double t = 0.0;
-        for (int q = 0; q < (int)(blockDim.x >> 5); q++) t = __dadd_rn(t, red[q]);
-        double bound = __dmul_rn(t, __dmul_rn(2.0 * (double)n + 8.0, 0x1p-53));
-        float flo = __double2float_rn(__ddiv_rn(__dsub_rn(t, bound), (double)n));
-        float fhi = __double2float_rn(__ddiv_rn(__dadd_rn(t, bound), (double)n));
-        float f;
-        if (flo == fhi) {
-            f = flo;
-        } else {
-            double q = 0.0;
-            for (int i = 0; i < n; i++) q = __dadd_rn(q, __dmul_rn((double)x[i], (double)x[i]));
-            f = __double2float_rn(__ddiv_rn(q, (double)n));
-        }
-        r_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(f, eps)));
-    }
-    __syncthreads();
-    float r = r_sh;
+    const float r = block_rms_inv(x, n, eps, red, &r_sh);
     for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], r), wn[i]);
 }
 
@@ -702,6 +682,7 @@ void tlmg_close(tlmg_ctx *c) {
     fused_release(c->fused);
     batch_release(c->batch);
     epp_release(c->epp);
+    delete c->step;   // its device buffers are in c->owned
     cache_release(c->cache);
     if (c->pin_slots) cudaFreeHost(c->pin_slots);
     if (c->pin_ids) cudaFreeHost(c->pin_ids);
@@ -1594,6 +1575,259 @@ int tlmg_moe_layer(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w) {
 int tlmg_moe_layer_ex(tlmg_ctx *c, int layer, float *h, int32_t *ids, float *w, float *onorm) {
     return moe_layer_impl(c, layer, h, ids, w, onorm);
 }
+
+// ---------------------------------------------------------------------------
+// The whole decoder step
+
+int tlmg_step_open(tlmg_ctx *c, int n_heads, int n_kv_heads, int head_dim, int vocab, const float *inv_freq,
+                   float attn_scale, int max_ctx, int kv_dt, int attn_mode) {
+    if (!c || !inv_freq) return set_error(TLMG_EINVAL, "step_open: NULL argument");
+    if (c->step) return set_error(TLMG_EBUSY, "step_open: already open");
+    const int H = n_heads, KV = n_kv_heads, hd = head_dim, L = c->g.n_layers;
+    if (H <= 0 || KV <= 0 || H % KV || H / KV > 16 || (hd != 64 && hd != 128 && hd != 256) || vocab <= 0 ||
+        max_ctx <= 0 || max_ctx > 65536 || (kv_dt != DT_F32 && kv_dt != DT_BF16) ||
+        (attn_mode != TLMG_ATTN_EXACT && attn_mode != TLMG_ATTN_SPLIT))
+        return set_error(TLMG_EINVAL, "step_open: heads %d/%d x %d, vocab %d, max_ctx %d, kv dtype %d, mode %d", H, KV,
+                         hd, vocab, max_ctx, kv_dt, attn_mode);
+    cudaSetDevice(c->device);
+    StepModel *m = new StepModel();
+    m->H = H;
+    m->KV = KV;
+    m->hd = hd;
+    m->vocab = vocab;
+    m->max_ctx = max_ctx;
+    m->page = 1;
+    while (m->page < max_ctx) m->page <<= 1;
+    m->kv_dt = kv_dt;
+    m->attn_mode = attn_mode;
+    m->attn_scale = attn_scale;
+    m->inv_freq.assign(inv_freq, inv_freq + hd / 2);
+    m->A.resize(L);
+    const int D = c->g.d_model, nq = (H + 2 * KV) * hd;
+    const size_t es = kv_dt == DT_F32 ? 4 : 2, pool = (size_t)L * KV * m->page * hd * es;
+    size_t work = 0;
+    for (int T = 1; T <= max_ctx; T++) work = std::max(work, attention_work_bytes(attn_mode, kv_dt, T, H, KV, hd));
+    m->awork_bytes = work;
+    const size_t aq = std::max(tlmg_qact_bytes(DT_Q8_K, H * hd), tlmg_qact_bytes(DT_Q8_0, H * hd)) + 4 * (size_t)H * hd;
+    const size_t xq = tlmg_qact_bytes(DT_Q8_K, D) + tlmg_qact_bytes(DT_Q8_0, D) + 64;
+    if (!(m->kpool = dalloc(c, pool)) || !(m->vpool = dalloc(c, pool)) || !(m->table = (int32_t *)dalloc(c, 4 * L)) ||
+        !(m->awork = (float *)dalloc(c, work)) || !(m->qkv = (float *)dalloc(c, 4 * (size_t)nq)) ||
+        !(m->att = (float *)dalloc(c, 4 * (size_t)H * hd)) || !(m->aq = (uint8_t *)dalloc(c, aq)) ||
+        !(m->xb = (float *)dalloc(c, 4 * (size_t)D)) || !(m->xq = (uint8_t *)dalloc(c, xq)) ||
+        !(m->rope = (float *)dalloc(c, 4 * (size_t)max_ctx * hd)) || !(m->logits = (float *)dalloc(c, 4 * (size_t)vocab))) {
+        delete m;
+        return set_error(TLMG_ENOMEM, "step_open: KV pages and scratch (%zu bytes of pages)", 2 * pool);
+    }
+    // RoPE cos / sin of every position, as tlm_model_step forms them
+    // (src/lib/tlm_model.c:1066-1070): double angle, double cos / sin,
+    // rounded to float, times the attention scale; row pos = cs | sn
+    std::vector<float> rope((size_t)max_ctx * hd);
+    std::vector<int32_t> tab(L);
+    for (int pos = 0; pos < max_ctx; pos++)
+        for (int j = 0; j < hd / 2; j++) {
+            const double a = (double)pos * (double)m->inv_freq[j];
+            rope[(size_t)pos * hd + j] = (float)std::cos(a) * attn_scale;
+            rope[(size_t)pos * hd + hd / 2 + j] = (float)std::sin(a) * attn_scale;
+        }
+    for (int l = 0; l < L; l++) tab[l] = l;
+    if (cudaMemcpy(m->rope, rope.data(), 4 * rope.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->table, tab.data(), 4 * (size_t)L, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(m->kpool, 0, pool) != cudaSuccess || cudaMemset(m->vpool, 0, pool) != cudaSuccess) {
+        delete m;
+        return set_error(TLMG_EIO, "step_open: table upload");
+    }
+    c->step = m;
+    return TLMG_OK;
+}
+
+// Copies host or device memory into a new device buffer of the context.
+static int upload(tlmg_ctx *c, void **dst, const void *src, size_t bytes, const char *what) {
+    if (!(*dst = dalloc(c, bytes + 16))) return set_error(TLMG_ENOMEM, "%s: %zu bytes", what, bytes);
+    if (cudaMemcpy(*dst, src, bytes, cudaMemcpyDefault) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(TLMG_EIO, "%s: copy", what);
+    }
+    return TLMG_OK;
+}
+
+int tlmg_set_attention(tlmg_ctx *c, int layer, const float *attn_norm, const int32_t *dt, const void *const *w,
+                       const size_t *rb, const float *q_norm, const float *k_norm) {
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (!c->step) return set_error(TLMG_EINVAL, "set_attention: tlmg_step_open first");
+    if (!attn_norm || !dt || !w || !w[0] || !w[1] || !w[2] || !w[3])
+        return set_error(TLMG_EINVAL, "set_attention: NULL argument");
+    cudaSetDevice(c->device);
+    StepModel &m = *c->step;
+    StepLayer &A = m.A[layer];
+    const int D = c->g.d_model, hd = m.hd;
+    const int rows[4] = { m.H * hd, m.KV * hd, m.KV * hd, D }, cols[4] = { D, D, D, m.H * hd };
+    size_t r[4];
+    for (int i = 0; i < 4; i++) {
+        const int q = dt_block(dt[i]);
+        r[i] = rb && rb[i] ? rb[i] : tlmg_row_bytes(dt[i], cols[i]);
+        if (!q || cols[i] % q || dt[i] == DT_MXFP4 || r[i] < tlmg_row_bytes(dt[i], cols[i]) ||
+            (q > 1 && act_kind_for(dt[i]) == DT_Q8_K && cols[i] % 256))
+            return set_error(TLMG_EINVAL, "set_attention: matrix %d dtype %d / row bytes %zu", i, dt[i], r[i]);
+    }
+    A = StepLayer{};
+    if ((rc = upload(c, (void **)&A.attn_norm, attn_norm, 4 * (size_t)D, "attn_norm")) ||
+        (q_norm && (rc = upload(c, (void **)&A.q_norm, q_norm, 4 * (size_t)hd, "q_norm"))) ||
+        (k_norm && (rc = upload(c, (void **)&A.k_norm, k_norm, 4 * (size_t)hd, "k_norm"))))
+        return rc;
+    A.fused_qkv = dt[0] == dt[1] && dt[1] == dt[2] && r[0] == r[1] && r[1] == r[2];
+    if (A.fused_qkv) {   // q | k | v rows back to back: one matvec for all three
+        uint8_t *qkv = (uint8_t *)dalloc(c, r[0] * (size_t)(rows[0] + rows[1] + rows[2]) + 16);
+        if (!qkv) return set_error(TLMG_ENOMEM, "set_attention: q|k|v");
+        size_t off = 0;
+        for (int i = 0; i < 3; i++) {
+            if (cudaMemcpy(qkv + off, w[i], r[i] * (size_t)rows[i], cudaMemcpyDefault) != cudaSuccess)
+                return set_error(TLMG_EIO, "set_attention: copy");
+            A.w[i] = qkv + off;
+            off += r[i] * (size_t)rows[i];
+        }
+    } else {
+        for (int i = 0; i < 3; i++)
+            if ((rc = upload(c, (void **)&A.w[i], w[i], r[i] * (size_t)rows[i], "set_attention"))) return rc;
+    }
+    if ((rc = upload(c, (void **)&A.w[3], w[3], r[3] * (size_t)rows[3], "set_attention"))) return rc;
+    for (int i = 0; i < 4; i++) {
+        A.dt[i] = dt[i];
+        A.rb[i] = r[i];
+    }
+    A.set = true;
+    return TLMG_OK;
+}
+
+int tlmg_set_embedding(tlmg_ctx *c, int dt, const void *tok_embd, size_t row_bytes) {
+    if (!c || !tok_embd) return set_error(TLMG_EINVAL, "set_embedding: NULL argument");
+    if (!c->step) return set_error(TLMG_EINVAL, "set_embedding: tlmg_step_open first");
+    const int D = c->g.d_model, q = dt_block(dt);
+    const size_t rb = row_bytes ? row_bytes : tlmg_row_bytes(dt, D);
+    if (!q || D % q || dt == DT_MXFP4 || rb < tlmg_row_bytes(dt, D))
+        return set_error(TLMG_EINVAL, "set_embedding: dtype %d / row bytes %zu", dt, rb);
+    cudaSetDevice(c->device);
+    StepModel &m = *c->step;
+    int rc = upload(c, (void **)&m.embd, tok_embd, rb * (size_t)m.vocab, "set_embedding");
+    if (rc) return rc;
+    m.embd_dt = dt;
+    m.embd_rb = rb;
+    return TLMG_OK;
+}
+
+int tlmg_set_output(tlmg_ctx *c, const float *out_norm, int dt, const void *lm_head, size_t row_bytes) {
+    if (!c || !out_norm || !lm_head) return set_error(TLMG_EINVAL, "set_output: NULL argument");
+    if (!c->step) return set_error(TLMG_EINVAL, "set_output: tlmg_step_open first");
+    const int D = c->g.d_model, q = dt_block(dt);
+    const size_t rb = row_bytes ? row_bytes : tlmg_row_bytes(dt, D);
+    if (!q || D % q || dt == DT_MXFP4 || rb < tlmg_row_bytes(dt, D))
+        return set_error(TLMG_EINVAL, "set_output: dtype %d / row bytes %zu", dt, rb);
+    cudaSetDevice(c->device);
+    StepModel &m = *c->step;
+    int rc = upload(c, (void **)&m.out_norm, out_norm, 4 * (size_t)D, "set_output");
+    if (!rc) rc = upload(c, (void **)&m.head, lm_head, rb * (size_t)m.vocab, "set_output");
+    if (rc) return rc;
+    m.head_dt = dt;
+    m.head_rb = rb;
+    return TLMG_OK;
+}
+
+// Activations of x for weights of dtype dt: the reference's actc_get
+// (src/lib/tlm_model.c:150-161), quantised at most once per kind per x.
+struct ActCache {
+    const float *x;
+    int n;
+    uint8_t *q8k, *q80;
+    bool have8k = false, have80 = false;
+    int get(int dt, cudaStream_t st, const void **out) {
+        const int kind = act_kind_for(dt);
+        if (kind == DT_F32) {
+            *out = x;
+            return TLMG_OK;
+        }
+        bool &have = kind == DT_Q8_K ? have8k : have80;
+        uint8_t *buf = kind == DT_Q8_K ? q8k : q80;
+        if (!have) {
+            int rc = launch_quant_act(kind, x, n, buf, st);
+            if (rc) return rc;
+            have = true;
+        }
+        *out = buf;
+        return TLMG_OK;
+    }
+};
+
+static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    StepModel *mp = c->step;
+    if (!mp) return set_error(TLMG_EINVAL, "decode_step: tlmg_step_open first");
+    StepModel &m = *mp;
+    const tlmg_geom &g = c->g;
+    const int D = g.d_model, L = g.n_layers, H = m.H, KV = m.KV, hd = m.hd;
+    if (token < 0 || token >= m.vocab) return set_error(TLMG_EINVAL, "decode_step: token %d out of range", token);
+    if (pos < 0 || pos >= m.max_ctx) return set_error(TLMG_ERANGE, "decode_step: position %d (context %d)", pos, m.max_ctx);
+    if (!m.embd) return set_error(TLMG_ENOTFOUND, "decode_step: no embedding (tlmg_set_embedding)");
+    if (logits && !m.head) return set_error(TLMG_ENOTFOUND, "decode_step: no lm_head (tlmg_set_output)");
+    for (int l = 0; l < L; l++)
+        if (!m.A[l].set) return set_error(TLMG_ENOTFOUND, "decode_step: layer %d has no attention weights", l);
+    cudaSetDevice(c->device);
+    cudaStream_t st = c->st;
+    float *dh = c->h;
+    const size_t off80 = (tlmg_qact_bytes(DT_Q8_K, D) + 15) & ~size_t(15);
+    const size_t aoff80 = (tlmg_qact_bytes(DT_Q8_K, H * hd) + 15) & ~size_t(15);
+    int rc = step_embed(m.embd_dt, m.embd + (size_t)token * m.embd_rb, D, dh, st);
+    if (rc) return rc;
+    const int rows[3] = { H * hd, KV * hd, KV * hd };
+    for (int l = 0; l < L; l++) {
+        const StepLayer &A = m.A[l];
+        // attention() (src/lib/tlm_model.c:730-763)
+        k_rmsnorm<<<1, 256, 0, st>>>(dh, A.attn_norm, D, g.norm_eps, m.xb);
+        if ((rc = launched("attention rmsnorm"))) return rc;
+        ActCache ax{ m.xb, D, m.xq, m.xq + off80 };
+        const void *act;
+        if (A.fused_qkv) {
+            if ((rc = ax.get(A.dt[0], st, &act)) ||
+                (rc = launch_matvec(A.dt[0], A.w[0], A.rb[0], act, m.qkv, D, 0, rows[0] + rows[1] + rows[2], st)))
+                return rc;
+        } else {
+            int at = 0;
+            for (int i = 0; i < 3; i++) {
+                if ((rc = ax.get(A.dt[i], st, &act)) ||
+                    (rc = launch_matvec(A.dt[i], A.w[i], A.rb[i], act, m.qkv + at, D, 0, rows[i], st)))
+                    return rc;
+                at += rows[i];
+            }
+        }
+        if ((rc = step_heads(m, l, pos, g.norm_eps, st))) return rc;
+        if ((rc = tlmg_decode_attention(m.attn_mode, m.kv_dt, m.qkv, m.kpool, m.vpool, L, m.table + l, m.page, pos + 1,
+                                        H, KV, hd, m.awork, m.awork_bytes, m.att, st)))
+            return rc;
+        ActCache aa{ m.att, H * hd, m.aq, m.aq + aoff80 };
+        if ((rc = aa.get(A.dt[3], st, &act)) ||
+            (rc = launch_matvec(A.dt[3], A.w[3], A.rb[3], act, dh, H * hd, 0, D, st, dh)))   // h += o . att
+            return rc;
+        // moe() (src/lib/tlm_model.c:940-1055)
+        if ((rc = moe_layer_impl(c, l, dh, nullptr, nullptr, nullptr))) return rc;
+    }
+    if (!logits) return TLMG_OK;
+    k_rmsnorm<<<1, 256, 0, st>>>(dh, m.out_norm, D, g.norm_eps, m.xb);
+    if ((rc = launched("output rmsnorm"))) return rc;
+    ActCache af{ m.xb, D, m.xq, m.xq + off80 };
+    const void *act;
+    if ((rc = af.get(m.head_dt, st, &act)) ||
+        (rc = launch_matvec(m.head_dt, m.head, m.head_rb, act, m.logits, D, 0, m.vocab, st)))
+        return rc;
+    const size_t bytes = 4 * (size_t)m.vocab;
+    if (is_device_ptr(logits)) {
+        cudaError_t e = cudaMemcpyAsync(logits, m.logits, bytes, cudaMemcpyDeviceToDevice, st);
+        return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "decode_step: logits copy");
+    }
+    cudaError_t e = cudaMemcpyAsync(logits, m.logits, bytes, cudaMemcpyDefault, st);
+    if (e != cudaSuccess) return cuda_fail(e, "decode_step: logits copy");
+    return stream_sync(c);
+}
+
+int tlmg_decode_step(tlmg_ctx *c, int token, int pos, float *logits) { return decode_step(c, token, pos, logits); }
 
 }  // extern "C"
 

@@ -1,0 +1,59 @@
+// tlmg_step.cuh - the whole decoder step on the GPU: embedding row,
+// attention block, the MoE block of every layer, final norm and lm_head
+// (tlm_model_step, src/lib/tlm_model.c:1058-1103).
+#pragma once
+#include <cstdint>
+#include <vector>
+#include <cuda_runtime.h>
+
+namespace tlmg {
+
+// Attention weights of one layer, copied into device memory. When q, k and
+// v share a dtype their rows sit back to back in `qkv` ([H*hd | KV*hd |
+// KV*hd] rows of D columns) and one matvec computes all three.
+struct StepLayer {
+    bool set = false;
+    float *attn_norm = nullptr;        // [D]
+    float *q_norm = nullptr, *k_norm = nullptr;   // [hd] or null
+    int dt[4] = { -1, -1, -1, -1 };    // q, k, v, o
+    uint8_t *w[4] = {};
+    size_t rb[4] = {};
+    bool fused_qkv = false;            // w[0] points at the q|k|v block
+};
+
+struct StepModel {
+    int H = 0, KV = 0, hd = 0, vocab = 0, max_ctx = 0, page = 0;
+    int kv_dt = 0, attn_mode = 0;
+    float attn_scale = 1.0f;
+    std::vector<float> inv_freq;        // [hd / 2]
+    std::vector<StepLayer> A;
+    int embd_dt = -1;
+    uint8_t *embd = nullptr;            // [vocab][embd_rb]
+    size_t embd_rb = 0;
+    float *out_norm = nullptr;          // [D]
+    int head_dt = -1;
+    uint8_t *head = nullptr;            // [vocab][head_rb]
+    size_t head_rb = 0;
+    // KV pages: one page of `page` positions per layer, [L][KV][page][hd]
+    void *kpool = nullptr, *vpool = nullptr;
+    int32_t *table = nullptr;           // [L]: table[l] = l
+    float *awork = nullptr;
+    size_t awork_bytes = 0;
+    // per-step scratch
+    float *qkv = nullptr;               // [(H + 2 KV) * hd]
+    float *att = nullptr;               // [H * hd]
+    uint8_t *aq = nullptr;              // quantised att (Q8_K or Q8_0)
+    float *xb = nullptr;                // [D] normalised h
+    uint8_t *xq = nullptr;              // quantised xb
+    float *rope = nullptr;              // [max_ctx][hd]: cs | sn of every position
+    float *logits = nullptr;            // [vocab]
+};
+
+// Launchers (tlmg_step.cu); all asynchronous on `st`.
+int step_embed(int dt, const uint8_t *row, int D, float *h, cudaStream_t st);
+// qk-norm (when given), RoPE of the q and k heads in qkv, then k and v of
+// position pos into layer l's page (device buffers of m; the position's
+// RoPE row of m.rope).
+int step_heads(const StepModel &m, int l, int pos, float eps, cudaStream_t st);
+
+}  // namespace tlmg

@@ -220,6 +220,34 @@ class MoeContext:
         """Home side: ffn[t] = sum_r w[t, r] * back[perm[t, r]] in ascending r."""
         check(self._lib.tlmg_ep_combine(self._h, n_tok, _ptr(back), _ptr(perm), _ptr(w), _ptr(ffn)))
 
+    # ---- the whole decoder step (tlm_model_step on the GPU)
+    def step_open(self, n_heads: int, n_kv_heads: int, head_dim: int, vocab: int, inv_freq,
+                  attn_scale: float = 1.0, max_ctx: int = 1024, kv_dtype: int = 0, attn_mode: int = 0) -> None:
+        """KV pages for max_ctx positions (kv_dtype F32 = 0 or BF16 = 2),
+        attention mode 0 = exact, 1 = split; inv_freq f32[head_dim / 2]."""
+        inv = np.ascontiguousarray(inv_freq, np.float32)
+        check(self._lib.tlmg_step_open(self._h, n_heads, n_kv_heads, head_dim, vocab, _ptr(inv), float(attn_scale),
+                                       max_ctx, kv_dtype, attn_mode))
+
+    def set_attention(self, layer: int, attn_norm, dts, q, k, v, o, row_bytes=None, q_norm=None,
+                      k_norm=None) -> None:
+        """Attention weights of a layer: dts = (q, k, v, o) dtypes."""
+        dt = (C.c_int32 * 4)(*dts)
+        w = (C.c_void_p * 4)(*[_ptr(m) for m in (q, k, v, o)])
+        rb = (C.c_size_t * 4)(*(row_bytes or (0, 0, 0, 0)))
+        check(self._lib.tlmg_set_attention(self._h, layer, _ptr(attn_norm), dt, w, rb, _ptr(q_norm), _ptr(k_norm)))
+
+    def set_embedding(self, dt: int, table, row_bytes: int = 0) -> None:
+        check(self._lib.tlmg_set_embedding(self._h, dt, _ptr(table), row_bytes))
+
+    def set_output(self, out_norm, dt: int, lm_head, row_bytes: int = 0) -> None:
+        check(self._lib.tlmg_set_output(self._h, _ptr(out_norm), dt, _ptr(lm_head), row_bytes))
+
+    def decode_step(self, token: int, pos: int, logits=None) -> None:
+        """One position through every layer; logits f32[vocab] (host or
+        CUDA) or None (no lm_head)."""
+        check(self._lib.tlmg_decode_step(self._h, token, pos, _ptr(logits)))
+
     def ep_open(self, rank: int, n_ranks: int, max_tok: int) -> bytes:
         """Opens this rank's peer-memory exchange; returns its handle (bytes
         to hand to every peer)."""

@@ -85,6 +85,17 @@ def matvec_rows(dt: int, W: torch.Tensor, row_bytes_: int, act: torch.Tensor, y:
     check(rc)
 
 
+def dequantize_rows(dt: int, src: torch.Tensor, row_bytes_: int, n: int, rows: int,
+                    y: torch.Tensor | None = None) -> torch.Tensor:
+    """tlm_dequantize_row over `rows` rows of n elements (row stride
+    row_bytes_) -> f32 [rows][n]."""
+    if y is None:
+        y = torch.empty((rows, n), dtype=torch.float32, device=src.device)
+    check(load().tlmg_dequantize_rows(dt, _dev(src, "src"), row_bytes_, _dev(y, "y"), n, rows,
+                                      C.c_void_p(_stream_ptr())))
+    return y
+
+
 def vec_dot(dt: int, wrow: torch.Tensor, act: torch.Tensor, n: int) -> float:
     """tlm_vec_dot on one device row (synchronous)."""
     y = torch.empty(1, dtype=torch.float32, device=wrow.device)
