@@ -281,8 +281,10 @@ def decode_step_section(ctx, args, dev, g, peak: float) -> dict:
 
     run()                                                   # warm-up pass (same positions)
     n0 = ctx.launches
+    i0 = ctx.step_info()
     pre_ms, dec_ms, wall, toks = run()
     launches = ctx.launches - n0
+    i1 = ctx.step_info()
     # algorithmic bytes per decode token: weights read once + the KV rows read
     rb = lambda dt, n: n // 256 * {12: 144, 14: 210}[dt]   # noqa: E731
     attn_w = (H * HD + 2 * KVH * HD) * rb(DT_ATT, D) + D * rb(DT_ATT, H * HD)
@@ -299,6 +301,7 @@ def decode_step_section(ctx, args, dev, g, peak: float) -> dict:
             "roofline_tokens_per_s": round(peak * 1e9 / bytes_tok, 1),
             "frac": round(bytes_tok * tps / 1e9 / peak, 4),
             "gpu_launches_per_token": round(launches / (P + NG), 1),
+            "graph_replays": i1["replays"] - i0["replays"], "graphs_off": i1["graphs_off"],
             "prompt": P, "generated": NG, "kv": "bf16 pages, split attention", "distinct_tokens": len(set(toks)),
             "api": "tlmg_decode_step per position; greedy token read by the host each step",
             "weights": "random: attention/down/lm_head Q6_K, gate/up/embedding Q4_K, router f32"}

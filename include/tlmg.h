@@ -363,6 +363,16 @@ int tlmg_set_output(tlmg_ctx *ctx, const float *out_norm, int dt, const void *lm
  * reference's prefill steps). Device logits: asynchronous on the
  * context's stream; host logits: the call waits. */
 int tlmg_decode_step(tlmg_ctx *ctx, int token, int pos, float *logits);
+/* From a context's second step on, the step runs as a captured CUDA graph
+ * (one launch; the token and position are read from device memory) when
+ * every MoE layer is resident and the static persistent kernel serves the
+ * experts; on = 0 keeps every step eager. Results are the same either way
+ * (TLMG_ATTN_SPLIT may differ in float rounding, its spans being shaped for
+ * max_ctx in a graph). */
+int tlmg_step_graphs(tlmg_ctx *ctx, int on);
+/* out[4]: steps run, steps replayed from a graph, captures, 1 when a
+ * capture failed and graphs were turned off. */
+int tlmg_step_info(const tlmg_ctx *ctx, int64_t *out);
 
 /* ---- Expert parallelism over peer memory (one process per GPU, all GPUs
  * of one node). The same split as above, with the exchange done by the

@@ -4,7 +4,9 @@ step composed from the CPU oracle's restatements of the reference's parts
 (tlm_dequantize_row), per layer attention() (:730-763: rmsnorm, q/k/v
 matvecs, qk-norm, rope(), the K/V write, attn_heads, o-proj, h += o) and
 moe(), then the final rmsnorm and lm_head. Both sides use the correctly
-rounded expf, so every logit of every position must be bit-identical.
+rounded expf, so every logit of every position must be bit-identical, with
+the step replayed as a captured graph (from the second position on) and
+with every step eager.
 
 The model is tiny and mixes dtypes on purpose: layer 0 has q/k/v of one
 dtype (one fused matvec on the GPU) and qk-norm, layer 1 has three
@@ -123,7 +125,17 @@ def test_decode_step_matches_composed_oracle(orc):
     for pos, tok in enumerate(tokens):
         ctx.decode_step(tok, pos, dl if pos == len(tokens) - 1 else None)
     ctx.check()
+    info = ctx.step_info()
+    assert not info["graphs_off"] and info["replays"] == 2 * len(tokens) - 1 and info["captures"] == 2, info
     ctx.close()
+    # every step eager (no graph replay): the same bits
+    ctx = _gpu_ctx(m)
+    ctx.step_graphs(False)
+    eager = np.zeros_like(got)
+    for pos, tok in enumerate(tokens):
+        ctx.decode_step(tok, pos, eager[pos])
+    ctx.close()
+    assert same_bits(eager, got).all()
     assert np.isfinite(ref).all()
     for pos in range(len(tokens)):
         bad = np.flatnonzero(~same_bits(got[pos], ref[pos]))

@@ -109,8 +109,9 @@ __device__ __forceinline__ void stage_rows(uint8_t *dst, int ld_b, const KT *__r
 template <typename KT>
 __global__ void __launch_bounds__(XS_ROWS) k_attn_scores(const float *__restrict__ q, const KT *__restrict__ kpool,
                                                          const int32_t *__restrict__ table, int n_pages, int page,
-                                                         int T, int H, int KV, int hd, float scale,
-                                                         float *__restrict__ s) {
+                                                         int T, const int32_t *__restrict__ dT, int H, int KV,
+                                                         int hd, float scale, float *__restrict__ s) {
+    if (dT) T = *dT;   // graph replay: the position count lives in device memory
     extern __shared__ float4 sm4[];
     __shared__ long long ro[XS_ROWS];
     __shared__ int bad_s;
@@ -177,8 +178,10 @@ constexpr int xo_stages() {
 // chain reads shared memory only.
 template <typename KT, int HD, int NST>
 __global__ void __launch_bounds__(HD) k_attn_out_exact(const KT *__restrict__ vpool, const int32_t *__restrict__ table,
-                                                       int n_pages, int page, int T, int H, int KV,
-                                                       float *__restrict__ s, float *__restrict__ out) {
+                                                       int n_pages, int page, int T, const int32_t *__restrict__ dT,
+                                                       int psm_cap, int H, int KV, float *__restrict__ s,
+                                                       float *__restrict__ out) {
+    if (dT) T = *dT;
     constexpr int ROW_B = HD * (int)sizeof(KT);
     constexpr int C16 = ROW_B / 16;
     extern __shared__ float4 sm4[];
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(HD) k_attn_out_exact(const KT *__restrict__ vp
     __shared__ int bad_s;
     const int h = blockIdx.x, kvh = h / (H / KV), tid = threadIdx.x;
     uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);                              // [NST][XO_ROWS][ROW_B]
-    float *psm = reinterpret_cast<float *>(stage + (size_t)NST * XO_ROWS * ROW_B);  // [T] when T <= PSM_MAX
+    float *psm = reinterpret_cast<float *>(stage + (size_t)NST * XO_ROWS * ROW_B);  // [T] when T <= psm_cap
     float *srow = s + (size_t)h * T;
     const int n_tiles = (T + XO_ROWS - 1) / XO_ROWS;
     if (tid == 0) bad_s = 0;
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(HD) k_attn_out_exact(const KT *__restrict__ vp
     }
     __syncthreads();
     mx = red[32];
-    float *pp = T <= PSM_MAX ? psm : srow;
+    float *pp = T <= psm_cap ? psm : srow;
     for (int t = tid; t < T; t += HD) pp[t] = cr_expf(__fsub_rn(srow[t], mx));
     __syncthreads();
     if (tid == 0) {
@@ -317,10 +320,12 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_attn_split(const float *__res
                                                               const KT *__restrict__ kpool,
                                                               const KT *__restrict__ vpool,
                                                               const int32_t *__restrict__ table, int n_pages, int page,
-                                                              int T, int H, int KV, int hd, int tr, int span,
+                                                              int T, const int32_t *__restrict__ dT, int H, int KV,
+                                                              int hd, int tr, int span,
                                                               int n_span, float qscale, float *__restrict__ pm,
                                                               float *__restrict__ pl, float *__restrict__ po) {
     extern __shared__ float4 sm4[];
+    if (dT) T = *dT;
     const int grp = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
     asm volatile("griddepcontrol.launch_dependents;");   // the merge grid may start and wait
     const int row_b = hd * (int)sizeof(KT) + 16;              // padded row bytes in shared memory
@@ -513,7 +518,8 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
                                                        const __nv_bfloat16 *__restrict__ kpool,
                                                        const __nv_bfloat16 *__restrict__ vpool,
                                                        const int32_t *__restrict__ table, int n_pages, int page, int lp,
-                                                       int T, int H, int KV, int span, int n_span, float qscale,
+                                                       int T, const int32_t *__restrict__ dT, int H, int KV, int span,
+                                                       int n_span, float qscale,
                                                        float *__restrict__ pm, float *__restrict__ pl,
                                                        float *__restrict__ po) {
     constexpr int ROW_B = HD * 2 + 16;           // padded row bytes in shared memory
@@ -523,6 +529,7 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
     extern __shared__ float4 sm4[];
     uint8_t *stage = reinterpret_cast<uint8_t *>(sm4);
     __shared__ int bad_s;
+    if (dT) T = *dT;
     const int G = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, t4 = lane & 3;
     asm volatile("griddepcontrol.launch_dependents;");   // the merge grid may start and wait
@@ -902,17 +909,19 @@ size_t attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd) {
     return (size_t)H * g.n_span * (2 + (size_t)hd) * 4;
 }
 
+// T = the launch's geometry (grids, spans, shared memory); with dT the
+// kernels read the actual position count (<= T) from device memory.
 template <typename KT>
 static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp, const int32_t *table, int n_pages,
-                            int page, int T, int H, int KV, int hd, float *work, float *out, cudaStream_t st,
-                            int kv_dt) {
+                            int page, int T, const int32_t *dT, int H, int KV, int hd, float *work, float *out,
+                            cudaStream_t st, int kv_dt) {
     const int grp = H / KV;
     if (mode == TLMG_ATTN_EXACT) {
         const float scale = 1.0f / sqrtf((float)hd);
         const size_t s1 = (size_t)grp * hd * 4 + (size_t)XS_ROWS * (hd * sizeof(KT) + 16);
         if (!smem_opt_in(k_attn_scores<KT>, s1)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         dim3 g1((T + XS_ROWS - 1) / XS_ROWS, KV);
-        k_attn_scores<KT><<<g1, XS_ROWS, s1, st>>>(q, kp, table, n_pages, page, T, H, KV, hd, scale, work);
+        k_attn_scores<KT><<<g1, XS_ROWS, s1, st>>>(q, kp, table, n_pages, page, T, dT, H, KV, hd, scale, work);
         bool ok = true;
 #define TLMG_XO(HDV)                                                                                       \
     if (hd == HDV) {                                                                                       \
@@ -920,7 +929,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         const size_t s2 = (size_t)nst * XO_ROWS * HDV * sizeof(KT) + (T <= PSM_MAX ? (size_t)T * 4 : 0);   \
         auto fn = k_attn_out_exact<KT, HDV, nst>;                                                          \
         ok = smem_opt_in(fn, s2);                                                                          \
-        if (ok) fn<<<H, HDV, s2, st>>>(vp, table, n_pages, page, T, H, KV, work, out);                     \
+        if (ok) fn<<<H, HDV, s2, st>>>(vp, table, n_pages, page, T, dT, T <= PSM_MAX ? T : 0, H, KV, work, out); \
     }
         TLMG_XO(64)
         TLMG_XO(128)
@@ -943,7 +952,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
     if (hd == HDV) {                                                                                            \
         auto fn = k_attn_split_tc<HDV, tc_stages<HDV>()>;                                                       \
         ok = smem_opt_in(fn, sm);                                                                               \
-        if (ok) fn<<<g1, 128, sm, st>>>(q, kp, vp, table, n_pages, page, lp, T, H, KV, g.span, g.n_span, qscale, pm, \
+        if (ok) fn<<<g1, 128, sm, st>>>(q, kp, vp, table, n_pages, page, lp, T, dT, H, KV, g.span, g.n_span, qscale, pm, \
                                         pl, po);                                                                \
     }
                 TLMG_TC(64)
@@ -959,7 +968,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         }
         const size_t sm = split_smem(g, grp, hd, (int)sizeof(KT));
         if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
-        k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, H, KV, hd, g.tr, g.span,
+        k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, dT, H, KV, hd, g.tr, g.span,
                                                         g.n_span, qscale, pm, pl, po);
         if (launch_merge(pm, pl, po, g.n_span, H, hd, out, st) != cudaSuccess)
             return cuda_fail(cudaGetLastError(), "attention merge launch");
@@ -977,9 +986,11 @@ extern "C" size_t tlmg_attention_work_bytes(int mode, int kv_dt, int T, int H, i
     return attention_work_bytes(mode, kv_dt, T, H, KV, hd);
 }
 
-extern "C" int tlmg_decode_attention(int mode, int kv_dt, const float *q, const void *k_pages, const void *v_pages,
-                                     int n_pages, const int32_t *page_table, int page_size, int T, int H, int KV,
-                                     int hd, void *work, size_t work_bytes, float *out, void *stream) {
+namespace tlmg {
+
+int decode_attention_impl(int mode, int kv_dt, const float *q, const void *k_pages, const void *v_pages, int n_pages,
+                          const int32_t *page_table, int page_size, int T, const int32_t *dT, int H, int KV, int hd,
+                          void *work, size_t work_bytes, float *out, cudaStream_t st) {
     int rc = check_geom("decode_attention", kv_dt, T, H, KV, hd, page_size, n_pages);
     if (rc) return rc;
     if (mode != TLMG_ATTN_EXACT && mode != TLMG_ATTN_SPLIT)
@@ -991,13 +1002,21 @@ extern "C" int tlmg_decode_attention(int mode, int kv_dt, const float *q, const 
     const size_t need = attention_work_bytes(mode, kv_dt, T, H, KV, hd);
     if (work_bytes < need)
         return set_error(TLMG_ERANGE, "decode_attention: work holds %zu bytes, needs %zu", work_bytes, need);
-    cudaStream_t st = pick_stream(stream);
     float *w = static_cast<float *>(work);
     if (kv_dt == TLMG_DT_F32)
         return launch_attention<float>(mode, q, (const float *)k_pages, (const float *)v_pages, page_table, n_pages,
-                                       page_size, T, H, KV, hd, w, out, st, kv_dt);
+                                       page_size, T, dT, H, KV, hd, w, out, st, kv_dt);
     return launch_attention<__nv_bfloat16>(mode, q, (const __nv_bfloat16 *)k_pages, (const __nv_bfloat16 *)v_pages,
-                                           page_table, n_pages, page_size, T, H, KV, hd, w, out, st, kv_dt);
+                                           page_table, n_pages, page_size, T, dT, H, KV, hd, w, out, st, kv_dt);
+}
+
+}  // namespace tlmg
+
+extern "C" int tlmg_decode_attention(int mode, int kv_dt, const float *q, const void *k_pages, const void *v_pages,
+                                     int n_pages, const int32_t *page_table, int page_size, int T, int H, int KV,
+                                     int hd, void *work, size_t work_bytes, float *out, void *stream) {
+    return decode_attention_impl(mode, kv_dt, q, k_pages, v_pages, n_pages, page_table, page_size, T, nullptr, H, KV,
+                                 hd, work, work_bytes, out, pick_stream(stream));
 }
 
 extern "C" int tlmg_kv_write(int kv_dt, const float *k, const float *v, void *k_pages, void *v_pages, int n_pages,

@@ -17,7 +17,7 @@ enum : int {
     DT_Q6_K = 14, DT_Q8_K = 15, DT_MXFP4 = 39
 };
 
-__host__ __device__ inline int dt_block(int dt) {
+__host__ __device__ constexpr int dt_block(int dt) {
     switch (dt) {
     case DT_F32: case DT_F16: case DT_BF16: return 1;
     case DT_Q8_0: case DT_MXFP4: return 32;
@@ -26,7 +26,7 @@ __host__ __device__ inline int dt_block(int dt) {
     }
 }
 
-__host__ __device__ inline int dt_block_bytes(int dt) {
+__host__ __device__ constexpr int dt_block_bytes(int dt) {
     switch (dt) {
     case DT_F32: return 4;
     case DT_F16: case DT_BF16: return 2;
@@ -41,14 +41,14 @@ __host__ __device__ inline int dt_block_bytes(int dt) {
 }
 
 // Activation kind a weight dtype consumes (reference tlm_quant.c:691-697).
-__host__ __device__ inline int act_kind_for(int wdt) {
+__host__ __device__ constexpr int act_kind_for(int wdt) {
     switch (wdt) {
     case DT_Q4_K: case DT_Q5_K: case DT_Q6_K: case DT_Q8_K: return DT_Q8_K;
     case DT_Q8_0: case DT_MXFP4: return DT_Q8_0;
     default: return DT_F32;
     }
 }
-__host__ __device__ inline int act_block_bytes(int kind) { return kind == DT_Q8_K ? 292 : 36; }
+__host__ __device__ constexpr int act_block_bytes(int kind) { return kind == DT_Q8_K ? 292 : 36; }
 
 // ---------------------------------------------------------------------------
 // scalar conversions, built from integer fields so they are exact in every
@@ -102,13 +102,22 @@ __device__ __forceinline__ float cr_expf(float xf) {
 // 1 / sqrtf((float)(ss / n) + eps), ss = sum of x[i]^2 in double: the
 // reference's RMSNorm scale (rmsnorm, src/lib/tlm_model.c:164-169), whose
 // ss is a serial double sum. Every thread of the block calls this (blockDim
-// a multiple of 32, at most 1024): a tree sum of the exact squares gives
-// ss within an error bound; when both ends of the bound round to the same
+// a multiple of 32, at most 1024): a sum of the exact squares in any order
+// gives ss within an error bound; when both ends of the bound round to the same
 // float mean that is the reference's float, else thread 0 runs the serial
 // sum. red: shared [32], r_sh: shared.
 __device__ __forceinline__ float block_rms_inv(const float *x, int n, float eps, double *red, float *r_sh) {
     double s = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) s = __dadd_rn(s, __dmul_rn((double)x[i], (double)x[i]));
+    int i = threadIdx.x;
+    const int nt = blockDim.x;
+    for (; i + 7 * nt < n; i += 8 * nt) {   // eight loads in flight, then their squares
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = x[i + u * nt];
+#pragma unroll
+        for (int u = 0; u < 8; u++) s = __dadd_rn(s, __dmul_rn((double)v[u], (double)v[u]));
+    }
+    for (; i < n; i += nt) s = __dadd_rn(s, __dmul_rn((double)x[i], (double)x[i]));
     for (int o = 16; o > 0; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
     __syncthreads();

@@ -1637,6 +1637,14 @@ int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
     cfg.numAttrs = 1;
     int rc = reserve_tokens(f, a.n_tok);
     if (rc) return rc;
+    if (f.graph_mode || f.bar_stale) {
+        // the arrival words (not the sticky error words) back to zero
+        cudaError_t me = cudaMemsetAsync(reinterpret_cast<uint8_t *>(f.bar) + 16, 0, BAR_BYTES - 16, st);
+        if (me != cudaSuccess) return cuda_fail(me, "fused expert FFN barrier reset");
+        f.rounds = 0;
+        f.launches = 0;
+        f.bar_stale = f.graph_mode;
+    }
     FusedArgs la = a;
     la.xq = f.xq;
     la.hbuf = f.hbuf;

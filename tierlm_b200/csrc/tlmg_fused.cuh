@@ -66,6 +66,11 @@ struct FusedScratch {
     int nsA = 0, nsB = 0;          // gate/up and down stages in shared memory
     uint64_t rounds = 0;           // grid-barrier rounds (tokens) launched since the barrier words were reset
     uint64_t launches = 0;         // launches since the barrier words were reset
+    // Graph capture: every captured launch restarts the barrier words from
+    // zero (a replay cannot carry host counts), and the first launch after
+    // a capture or a replay restarts them too (bar_stale).
+    bool graph_mode = false;
+    bool bar_stale = false;
     // per-token global scratch of a launch, for up to tok_cap tokens
     int tok_cap = 0;
     uint8_t *xq = nullptr;         // [tok_cap][quantised x]

@@ -32,5 +32,10 @@ bool is_device_ptr(const void *p);
 
 // Device scratch of tlmg_decode_attention (tlmg_attn.cu).
 size_t attention_work_bytes(int mode, int kv_dt, int T, int H, int KV, int hd);
+// tlmg_decode_attention with launch geometry for T positions; with dT the
+// kernels read the actual count (1..T) from device memory (graph replay).
+int decode_attention_impl(int mode, int kv_dt, const float *q, const void *k_pages, const void *v_pages, int n_pages,
+                          const int32_t *page_table, int page_size, int T, const int32_t *dT, int H, int KV, int hd,
+                          void *work, size_t work_bytes, float *out, cudaStream_t st);
 
 }  // namespace tlmg

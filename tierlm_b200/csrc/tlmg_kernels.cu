@@ -2,6 +2,7 @@
 // quantisation, the generic row-matvec (drop-in for tlm_matvec_rows), exact
 // per-block partials, the router top-k, error handling and the host-buffer
 // adapters with the reference's tier-table signatures.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -142,24 +143,115 @@ k_matvec_q(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__re
     }
 }
 
+// The same per-row computation for 16-byte aligned rows of one integer
+// dtype (a template parameter, so the block code is specialised): each warp
+// owns rows r, r + stride, ... and double-buffers them in shared memory,
+// copying row r + stride (cp.async, 16-byte pieces) while it computes row
+// r from the other buffer. Block reads then come from shared memory at any
+// block alignment (Q6_K's 210-byte and Q8_0's 34-byte blocks), every row is
+// read from HBM once by full-width coalesced copies, and the grid is sized
+// to the resident warps so that each keeps two rows in flight.
+__device__ __forceinline__ void mv_cp16(void *dst, const void *src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+template <int DT>
+__global__ void __launch_bounds__(MV_WARPS * 32)
+k_matvec_qs(const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act, float *y, int nb, int64_t r0,
+            int64_t r1, const float *res) {
+    extern __shared__ uint4 mv_rows[];
+    __shared__ BlockPart part[MV_WARPS][MV_CHUNK];
+    constexpr int BB = dt_block_bytes(DT), ABB = act_block_bytes(act_kind_for(DT));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
+    const int nw = blockDim.x >> 5, n16 = nb * BB / 16;
+    uint4 *buf = mv_rows + (size_t)warp * 2 * n16;
+    const int64_t stride = (int64_t)gridDim.x * nw;
+    auto issue = [&](int64_t r, uint4 *dst) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(W + (size_t)r * rb);
+        for (int i = lane; i < n16; i += 32) mv_cp16(dst + i, src + i);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    int64_t row = r0 + (int64_t)blockIdx.x * nw + warp;
+    if (row < r1) issue(row, buf);
+    for (int it = 0; row < r1; row += stride, it++) {
+        const uint8_t *row_s = reinterpret_cast<const uint8_t *>(buf + (it & 1) * n16);
+        if (row + stride < r1) {
+            issue(row + stride, buf + ((it + 1) & 1) * n16);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncwarp();
+        float acc = 0.0f;
+        for (int c0 = 0; c0 < nb; c0 += MV_CHUNK) {
+            const int nc = min(MV_CHUNK, nb - c0);
+            for (int p0 = 0; p0 < nc; p0 += 4) {
+                const int p = p0 + g;
+                const bool valid = p < nc;
+                int is = 0, ms = 0;
+                const uint8_t *blk = row_s + (size_t)(c0 + p) * BB;
+                const uint8_t *ab = act + (size_t)(c0 + p) * ABB;
+                if (valid) block_part<SLoad>(DT, blk, ab, j, is, ms);
+                group8_sum(is, ms);
+                if (valid && j == 0) {
+                    float dA, dM;
+                    block_scales<SLoad>(DT, blk, ab, dA, dM);
+                    part[warp][p] = BlockPart{ is, ms, dA, dM };
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                for (int p = 0; p < nc; p++) {
+                    BlockPart q = part[warp][p];
+                    acc = chain_step(DT, acc, q.dA, q.dM, q.is, q.ms);
+                }
+            __syncwarp();
+        }
+        if (lane == 0) y[row] = res ? __fadd_rn(res[row], acc) : acc;
+    }
+}
+
+using MvFn = void (*)(const uint8_t *, size_t, const uint8_t *, float *, int, int64_t, int64_t, const float *);
+static MvFn pick_mv(int dt) {
+    switch (dt) {
+    case DT_Q4_K: return k_matvec_qs<DT_Q4_K>;
+    case DT_Q5_K: return k_matvec_qs<DT_Q5_K>;
+    case DT_Q6_K: return k_matvec_qs<DT_Q6_K>;
+    case DT_Q8_0: return k_matvec_qs<DT_Q8_0>;
+    case DT_Q8_K: return k_matvec_qs<DT_Q8_K>;
+    default: return nullptr;
+    }
+}
+
 // Float weights: element i into lane i mod 32 with fmaf, then the fixed
 // tree (reference tlm_quant.c:724-770).
 template <int A>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_f(int dt, const uint8_t *__restrict__ W, size_t rb, const float *__restrict__ x,
            float *y, int64_t n, int64_t r0, int64_t r1, const float *res) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int64_t row = r0 + (int64_t)blockIdx.x * MV_WARPS + warp; row < r1;
-         row += (int64_t)gridDim.x * MV_WARPS) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int64_t row = r0 + (int64_t)blockIdx.x * nw + warp; row < r1; row += (int64_t)gridDim.x * nw) {
         const uint8_t *wr = W + (size_t)row * rb;
         float acc = 0.0f;
-        for (int64_t i = lane; i < n; i += 32) {
-            float w;
-            if (dt == DT_F32) w = __uint_as_float(WLoad<A>::u32(wr + 4 * i));
-            else if (dt == DT_F16) w = f16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
-            else w = bf16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
-            acc = __fmaf_rn(w, __ldg(x + i), acc);
+        auto wload = [&](int64_t i) -> float {
+            if (dt == DT_F32) return __uint_as_float(WLoad<A>::u32(wr + 4 * i));
+            if (dt == DT_F16) return f16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
+            return bf16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
+        };
+        int64_t i = lane;
+        // eight elements' loads issued together, then their fmaf chain in order
+        for (; i + 7 * 32 < n; i += 8 * 32) {
+            float wv[8], xv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                wv[u] = wload(i + 32 * u);
+                xv[u] = __ldg(x + i + 32 * u);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) acc = __fmaf_rn(wv[u], xv[u], acc);
         }
+        for (; i < n; i += 32) acc = __fmaf_rn(wload(i), __ldg(x + i), acc);
         acc = tree32(acc);
         if (lane == 0) y[row] = res ? __fadd_rn(res[row], acc) : acc;
     }
@@ -198,12 +290,48 @@ int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, 
     int A = align_of((uintptr_t)W | (uintptr_t)rb | (uintptr_t)(qk > 1 ? dt_block_bytes(dt) : 16));
     unsigned grid = mv_grid(r1 - r0);
     const unsigned thr = MV_WARPS * 32;
+    // fewer warps per CTA when there are few rows, so that they spread over the SMs
+    const int64_t rows = r1 - r0;
+    const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(MV_WARPS, rows / 148));
+    const unsigned grid_nw = (unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + nw - 1) / nw, 148 * 32));
+    const size_t row_used = (size_t)(n / qk) * dt_block_bytes(dt);
+    MvFn mv = pick_mv(dt);
+    if (mv && ((uintptr_t)W & 15u) == 0 && rb % 16 == 0 && row_used % 16 == 0 && row_used <= 8192) {
+        // MV_WARPS warps a CTA, two row buffers a warp; as many CTAs as are resident
+        const size_t sm = 2 * row_used * MV_WARPS;
+        static thread_local size_t opted = 48 * 1024;
+        if (sm > opted) {
+            if (cudaFuncSetAttribute((const void *)mv, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
+                cudaSuccess)
+                opted = 160 * 1024;
+            else
+                cudaGetLastError();
+        }
+        if (sm <= opted) {
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void *)mv, MV_WARPS * 32, sm) !=
+                    cudaSuccess ||
+                per_sm < 1) {
+                cudaGetLastError();
+                per_sm = 1;
+            }
+            const int nsm = 148;
+            const int64_t need = (rows + MV_WARPS - 1) / MV_WARPS;
+            const unsigned gq = (unsigned)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)per_sm * nsm));
+            mv<<<gq, MV_WARPS * 32, sm, st>>>(W, rb, (const uint8_t *)act, y, (int)(n / qk), r0, r1, res);
+            count_launch();
+            cudaError_t e = cudaGetLastError();
+            return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "matvec_rows launch");
+        }
+    }
     if (qk == 1) {
         const float *x = (const float *)act;
+        grid = grid_nw;
+        const unsigned thr_f = 32 * nw;
         switch (A) {
-        case 16: case 4: k_matvec_f<4><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
-        case 2: k_matvec_f<2><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
-        default: k_matvec_f<1><<<grid, thr, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
+        case 16: case 4: k_matvec_f<4><<<grid, thr_f, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
+        case 2: k_matvec_f<2><<<grid, thr_f, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
+        default: k_matvec_f<1><<<grid, thr_f, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
         }
     } else {
         const uint8_t *a = (const uint8_t *)act;

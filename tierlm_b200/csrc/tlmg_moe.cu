@@ -115,6 +115,7 @@ struct tlmg_ctx {
     BatchScratch batch;            // batched-decode scratch (tlmg_expert_ffn_batch)
     EpP2P epp;                     // peer-memory expert parallelism (tlmg_ep_open)
     StepModel *step = nullptr;     // the whole decoder step (tlmg_step_open)
+    uint64_t wgen = 1;             // bumped by every call that changes weights, layers or launch set-up
     ExpertCache cache;             // HBM expert-slot cache (tlmg_cache_enable)
     Slot *pin_slots = nullptr;     // pinned [n_layers][E] slot-table mirror of cached layers
     int32_t *pin_ids = nullptr;    // pinned [64] routed ids of a cached layer
@@ -322,12 +323,31 @@ k_ffn_down(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, cons
 // unless the value lies within the two sums' combined error bound of a float
 // rounding boundary; then thread 0 redoes the sequential sum.
 __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ wn, int n, float eps,
-                          float *__restrict__ out) {
+                          float *__restrict__ out, uint8_t *__restrict__ q8k) {
     __shared__ double red[32];
     __shared__ float r_sh;
     const float r = block_rms_inv(x, n, eps, red, &r_sh);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], r), wn[i]);
+    const int nt = blockDim.x;
+    int i = threadIdx.x;
+    for (; i + 3 * nt < n; i += 4 * nt) {   // loads of four elements in flight together
+        float xv[4], wv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            xv[u] = x[i + u * nt];
+            wv[u] = wn[i + u * nt];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) out[i + u * nt] = __fmul_rn(__fmul_rn(xv[u], r), wv[u]);
+    }
+    for (; i < n; i += nt) out[i] = __fmul_rn(__fmul_rn(x[i], r), wn[i]);
+    if (!q8k) return;
+    // and out as Q8_K (tlm_quantize_act), one warp per 256-value block
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nb = (n + 255) / 256;
+    for (int b = warp; b < nb; b += nt >> 5) warp_quant_q8k(out + 256 * b, min(256, n - 256 * b), q8k + 292 * b, lane);
 }
+
+__global__ void k_set_f32(float *p, float v) { *p = v; }
 
 // silu(g)*u over a shared-expert row pair buffer [g | u].
 __global__ void k_swiglu(const float *__restrict__ gu, int n, float *__restrict__ h) {
@@ -682,6 +702,7 @@ void tlmg_close(tlmg_ctx *c) {
     fused_release(c->fused);
     batch_release(c->batch);
     epp_release(c->epp);
+    if (c->step) step_graphs_release(*c->step);
     delete c->step;   // its device buffers are in c->owned
     cache_release(c->cache);
     if (c->pin_slots) cudaFreeHost(c->pin_slots);
@@ -700,6 +721,7 @@ void tlmg_close(tlmg_ctx *c) {
 }
 
 int tlmg_profile(tlmg_ctx *c, int on) {
+    if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     cudaSetDevice(c->device);
     if (on) {
@@ -737,6 +759,7 @@ int tlmg_profile_read(tlmg_ctx *c, int cls, double *ms, int64_t *launches, int64
 }
 
 int tlmg_set_fused(tlmg_ctx *c, int on) {
+    if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     if (on < 0 || on > 3) return set_error(TLMG_EINVAL, "set_fused: mode %d", on);
     c->fused_on = on != 0;
@@ -746,6 +769,7 @@ int tlmg_set_fused(tlmg_ctx *c, int on) {
 }
 
 int tlmg_set_batch_kernels(tlmg_ctx *c, int mode) {
+    if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     // 0..2: both projections; 10 * g + d: gate/up mode g, down mode d
     const int g = mode >= 10 ? mode / 10 : mode, d = mode >= 10 ? mode % 10 : mode;
@@ -781,6 +805,7 @@ int tlmg_check(tlmg_ctx *c) {
 }
 
 int tlmg_set_stream(tlmg_ctx *c, void *stream) {
+    if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     cudaSetDevice(c->device);
     cudaStream_t next = stream ? (cudaStream_t)stream : c->own_st;
@@ -800,6 +825,7 @@ int64_t tlmg_launch_count(const tlmg_ctx *c) { return c ? launches_total() - c->
 
 int tlmg_set_expert(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], const void *payload,
                     size_t payload_len, const uint64_t item_off[3]) {
+    if (c) c->wgen++;
     int rc = check_layer(c, layer);
     if (rc) return rc;
     cudaSetDevice(c->device);
@@ -846,6 +872,7 @@ int tlmg_set_expert(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], con
 }
 
 int tlmg_cache_enable(tlmg_ctx *c, int n_slots, size_t slot_bytes) {
+    if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     if (c->g.n_experts <= 0) return set_error(TLMG_EINVAL, "cache: geometry has no routed experts");
     if (n_slots < c->g.top_k)
@@ -859,6 +886,7 @@ int tlmg_cache_enable(tlmg_ctx *c, int n_slots, size_t slot_bytes) {
 
 int tlmg_set_expert_host(tlmg_ctx *c, int layer, int expert, const int32_t dt[3], const void *payload,
                          size_t payload_len, const uint64_t item_off[3]) {
+    if (c) c->wgen++;
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (expert < 0 || expert >= c->g.n_experts)
@@ -918,6 +946,7 @@ int tlmg_cache_tick(tlmg_ctx *c) {
 }
 
 int tlmg_cache_lookahead(tlmg_ctx *c, int depth, int k) {
+    if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
     if (depth < 0 || depth > 1 || k < 0 || k > 64 || k > c->g.n_experts)
         return set_error(TLMG_EINVAL, "cache_lookahead: depth %d (0 or 1), k %d (0 .. min(64, E))", depth, k);
@@ -942,6 +971,7 @@ int tlmg_cache_lookahead(tlmg_ctx *c, int depth, int k) {
 
 int tlmg_set_layer(tlmg_ctx *c, int layer, const float *ffn_norm, int router_dt, const void *router_w,
                    size_t router_rb, const float *router_bias, const uint8_t *mask) {
+    if (c) c->wgen++;
     int rc = check_layer(c, layer);
     if (rc) return rc;
     cudaSetDevice(c->device);
@@ -991,6 +1021,7 @@ int tlmg_set_layer(tlmg_ctx *c, int layer, const float *ffn_norm, int router_dt,
 
 int tlmg_set_shared(tlmg_ctx *c, int layer, const int32_t dt[3], const void *gate, const void *up_w,
                     const void *down, const float *gate_inp) {
+    if (c) c->wgen++;
     int rc = check_layer(c, layer);
     if (rc) return rc;
     cudaSetDevice(c->device);
@@ -1022,6 +1053,7 @@ int tlmg_set_shared(tlmg_ctx *c, int layer, const int32_t dt[3], const void *gat
 
 int tlmg_set_dense_ffn(tlmg_ctx *c, int layer, int d_ffn, const int32_t dt[3], const void *gate, const void *up_w,
                        const void *down) {
+    if (c) c->wgen++;
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (!dt || !gate || !up_w || !down || d_ffn <= 0) return set_error(TLMG_EINVAL, "set_dense_ffn: bad argument");
@@ -1444,7 +1476,7 @@ static int launch_lookahead(tlmg_ctx *c, int layer, const float *dh) {
     int k = std::min(c->la_k, N.live);   // never more hints than routable experts
     if (k <= 0) return TLMG_OK;
     int rc;
-    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, N.ffn_norm, D, c->g.norm_eps, c->la_x);
+    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, N.ffn_norm, D, c->g.norm_eps, c->la_x, nullptr);
     if ((rc = launched("lookahead rmsnorm"))) return rc;
     const int kr = act_kind_for(N.router_dt);
     if (kr != DT_F32 && (rc = launch_quant_act(kr, c->la_x, D, c->la_q, c->st))) return rc;
@@ -1478,9 +1510,13 @@ static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float 
         dh = c->h;
     }
     // xb = rmsnorm(h); activations of xb
-    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, Ly.ffn_norm, D, g.norm_eps, c->x);
+    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, Ly.ffn_norm, D, g.norm_eps, c->x, nullptr);
     if ((rc = launched("rmsnorm"))) return rc;
-    if ((rc = quant_inputs(c, c->x))) return rc;
+    // the persistent kernel quantises its input itself: the activations of
+    // xb are only formed for the parts that read them
+    const bool fused_only = E > 0 && !Ly.has_dense && !(Ly.has_shared && g.d_shared > 0) && !onorm &&
+                            act_kind_for(Ly.router_dt) == DT_F32 && use_fused_path(c, Ly, c->x);
+    if (!fused_only && (rc = quant_inputs(c, c->x))) return rc;
     if (Ly.has_dense) {
         // no router, no experts, no shared expert, no route hook (moe() returns early)
         if ((rc = dense_ffn(c, Ly, dh))) return rc;
@@ -1506,16 +1542,11 @@ static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float 
         if ((rc = launch_matvec(Ly.sh_dt[2], Ly.sh_w[2], tlmg_row_bytes(Ly.sh_dt[2], ds), c->shq, c->s_out, ds, 0, D,
                                 c->st)))
             return rc;
-        float one = 1.0f;
-        if (Ly.sh_gate_inp) {
-            k_shared_gate<<<1, 32, 0, c->st>>>(Ly.sh_gate_inp, c->x, D, c->sgate);
-            if ((rc = launched("shared gate"))) return rc;
-        } else if (cudaMemcpyAsync(c->sgate, &one, 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) {
-            return set_error(TLMG_EIO, "shared gate copy");
-        }
+        if (Ly.sh_gate_inp) k_shared_gate<<<1, 32, 0, c->st>>>(Ly.sh_gate_inp, c->x, D, c->sgate);
+        else k_set_f32<<<1, 1, 0, c->st>>>(c->sgate, 1.0f);   // no gate: the shared expert's weight is 1
+        if ((rc = launched("shared gate"))) return rc;
         s_out = c->s_out;
         sgate = c->sgate;
-        if ((rc = stream_sync(c))) return rc;   // `one` lives on this stack frame
     }
     if (E > 0) {
         if ((rc = sync_slots(c, Ly))) return rc;
@@ -1614,7 +1645,8 @@ int tlmg_step_open(tlmg_ctx *c, int n_heads, int n_kv_heads, int head_dim, int v
         !(m->awork = (float *)dalloc(c, work)) || !(m->qkv = (float *)dalloc(c, 4 * (size_t)nq)) ||
         !(m->att = (float *)dalloc(c, 4 * (size_t)H * hd)) || !(m->aq = (uint8_t *)dalloc(c, aq)) ||
         !(m->xb = (float *)dalloc(c, 4 * (size_t)D)) || !(m->xq = (uint8_t *)dalloc(c, xq)) ||
-        !(m->rope = (float *)dalloc(c, 4 * (size_t)max_ctx * hd)) || !(m->logits = (float *)dalloc(c, 4 * (size_t)vocab))) {
+        !(m->rope = (float *)dalloc(c, 4 * (size_t)max_ctx * hd)) || !(m->logits = (float *)dalloc(c, 4 * (size_t)vocab)) ||
+        !(m->dargs = (int32_t *)dalloc(c, 16))) {
         delete m;
         return set_error(TLMG_ENOMEM, "step_open: KV pages and scratch (%zu bytes of pages)", 2 * pool);
     }
@@ -1652,6 +1684,7 @@ static int upload(tlmg_ctx *c, void **dst, const void *src, size_t bytes, const 
 
 int tlmg_set_attention(tlmg_ctx *c, int layer, const float *attn_norm, const int32_t *dt, const void *const *w,
                        const size_t *rb, const float *q_norm, const float *k_norm) {
+    if (c) c->wgen++;
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (!c->step) return set_error(TLMG_EINVAL, "set_attention: tlmg_step_open first");
@@ -1700,6 +1733,7 @@ int tlmg_set_attention(tlmg_ctx *c, int layer, const float *attn_norm, const int
 }
 
 int tlmg_set_embedding(tlmg_ctx *c, int dt, const void *tok_embd, size_t row_bytes) {
+    if (c) c->wgen++;
     if (!c || !tok_embd) return set_error(TLMG_EINVAL, "set_embedding: NULL argument");
     if (!c->step) return set_error(TLMG_EINVAL, "set_embedding: tlmg_step_open first");
     const int D = c->g.d_model, q = dt_block(dt);
@@ -1716,6 +1750,7 @@ int tlmg_set_embedding(tlmg_ctx *c, int dt, const void *tok_embd, size_t row_byt
 }
 
 int tlmg_set_output(tlmg_ctx *c, const float *out_norm, int dt, const void *lm_head, size_t row_bytes) {
+    if (c) c->wgen++;
     if (!c || !out_norm || !lm_head) return set_error(TLMG_EINVAL, "set_output: NULL argument");
     if (!c->step) return set_error(TLMG_EINVAL, "set_output: tlmg_step_open first");
     const int D = c->g.d_model, q = dt_block(dt);
@@ -1757,33 +1792,30 @@ struct ActCache {
     }
 };
 
-static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
-    if (!c) return set_error(TLMG_EINVAL, "NULL context");
-    StepModel *mp = c->step;
-    if (!mp) return set_error(TLMG_EINVAL, "decode_step: tlmg_step_open first");
-    StepModel &m = *mp;
+// The step's device work on the context's stream: embedding, every layer's
+// attention() and moe(), and (head) the final norm and lm_head into
+// m.logits. With dargs the token and position are read from device memory
+// (the body is then position-independent and can be captured); attention
+// launches are then shaped for max_ctx positions.
+static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *dargs) {
+    StepModel &m = *c->step;
     const tlmg_geom &g = c->g;
     const int D = g.d_model, L = g.n_layers, H = m.H, KV = m.KV, hd = m.hd;
-    if (token < 0 || token >= m.vocab) return set_error(TLMG_EINVAL, "decode_step: token %d out of range", token);
-    if (pos < 0 || pos >= m.max_ctx) return set_error(TLMG_ERANGE, "decode_step: position %d (context %d)", pos, m.max_ctx);
-    if (!m.embd) return set_error(TLMG_ENOTFOUND, "decode_step: no embedding (tlmg_set_embedding)");
-    if (logits && !m.head) return set_error(TLMG_ENOTFOUND, "decode_step: no lm_head (tlmg_set_output)");
-    for (int l = 0; l < L; l++)
-        if (!m.A[l].set) return set_error(TLMG_ENOTFOUND, "decode_step: layer %d has no attention weights", l);
-    cudaSetDevice(c->device);
     cudaStream_t st = c->st;
     float *dh = c->h;
     const size_t off80 = (tlmg_qact_bytes(DT_Q8_K, D) + 15) & ~size_t(15);
     const size_t aoff80 = (tlmg_qact_bytes(DT_Q8_K, H * hd) + 15) & ~size_t(15);
-    int rc = step_embed(m.embd_dt, m.embd + (size_t)token * m.embd_rb, D, dh, st);
+    int rc = step_embed(m.embd_dt, m.embd, m.embd_rb, token, dargs, D, dh, st);
     if (rc) return rc;
     const int rows[3] = { H * hd, KV * hd, KV * hd };
     for (int l = 0; l < L; l++) {
         const StepLayer &A = m.A[l];
         // attention() (src/lib/tlm_model.c:730-763)
-        k_rmsnorm<<<1, 256, 0, st>>>(dh, A.attn_norm, D, g.norm_eps, m.xb);
+        const bool xq_now = act_kind_for(A.dt[0]) == DT_Q8_K;   // xb as Q8_K from the norm kernel itself
+        k_rmsnorm<<<1, 256, 0, st>>>(dh, A.attn_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
         if ((rc = launched("attention rmsnorm"))) return rc;
         ActCache ax{ m.xb, D, m.xq, m.xq + off80 };
+        ax.have8k = xq_now;
         const void *act;
         if (A.fused_qkv) {
             if ((rc = ax.get(A.dt[0], st, &act)) ||
@@ -1798,9 +1830,10 @@ static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
                 at += rows[i];
             }
         }
-        if ((rc = step_heads(m, l, pos, g.norm_eps, st))) return rc;
-        if ((rc = tlmg_decode_attention(m.attn_mode, m.kv_dt, m.qkv, m.kpool, m.vpool, L, m.table + l, m.page, pos + 1,
-                                        H, KV, hd, m.awork, m.awork_bytes, m.att, st)))
+        if ((rc = step_heads(m, l, pos, dargs, g.norm_eps, st))) return rc;
+        if ((rc = decode_attention_impl(m.attn_mode, m.kv_dt, m.qkv, m.kpool, m.vpool, L, m.table + l, m.page,
+                                        dargs ? m.max_ctx : pos + 1, dargs ? dargs + 2 : nullptr, H, KV, hd, m.awork,
+                                        m.awork_bytes, m.att, st)))
             return rc;
         ActCache aa{ m.att, H * hd, m.aq, m.aq + aoff80 };
         if ((rc = aa.get(A.dt[3], st, &act)) ||
@@ -1809,14 +1842,104 @@ static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
         // moe() (src/lib/tlm_model.c:940-1055)
         if ((rc = moe_layer_impl(c, l, dh, nullptr, nullptr, nullptr))) return rc;
     }
-    if (!logits) return TLMG_OK;
-    k_rmsnorm<<<1, 256, 0, st>>>(dh, m.out_norm, D, g.norm_eps, m.xb);
+    if (!head) return TLMG_OK;
+    const bool xq_now = act_kind_for(m.head_dt) == DT_Q8_K;
+    k_rmsnorm<<<1, 256, 0, st>>>(dh, m.out_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
     if ((rc = launched("output rmsnorm"))) return rc;
     ActCache af{ m.xb, D, m.xq, m.xq + off80 };
+    af.have8k = xq_now;
     const void *act;
-    if ((rc = af.get(m.head_dt, st, &act)) ||
-        (rc = launch_matvec(m.head_dt, m.head, m.head_rb, act, m.logits, D, 0, m.vocab, st)))
-        return rc;
+    if ((rc = af.get(m.head_dt, st, &act))) return rc;
+    return launch_matvec(m.head_dt, m.head, m.head_rb, act, m.logits, D, 0, m.vocab, st);
+}
+
+// Graph replay is used from a context's second step on when nothing in the
+// step depends on host decisions made per call: every MoE layer resident
+// (no slot cache) and the static persistent kernel (its barrier words are
+// restarted per captured launch).
+static bool step_graph_allowed(const tlmg_ctx *c) {
+    const StepModel &m = *c->step;
+    if (m.graph_off || !m.use_graphs || m.calls == 0 || c->prof || c->fused.mode != FUSED_STATIC) return false;
+    for (const Layer &Ly : c->L)
+        if (Ly.cached) return false;
+    return true;
+}
+
+// Captures step_body(head) with device-side token / position. A capture
+// that fails turns graphs off for the context (the step stays eager).
+static int capture_step(tlmg_ctx *c, int head) {
+    StepModel &m = *c->step;
+    cudaStream_t st = c->st;
+    int rc;
+    for (Layer &Ly : c->L)
+        if ((rc = sync_slots(c, Ly))) return rc;   // uploads happen before the capture
+    if (m.graph[head]) {
+        cudaGraphExecDestroy(m.graph[head]);
+        m.graph[head] = nullptr;
+    }
+    cudaGraph_t gr = nullptr;
+    const int64_t n0 = launches_total();
+    if ((!m.cap_st && cudaStreamCreateWithFlags(&m.cap_st, cudaStreamNonBlocking) != cudaSuccess) ||
+        cudaStreamBeginCapture(m.cap_st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        m.graph_off = true;
+        return TLMG_OK;
+    }
+    c->st = m.cap_st;   // nothing runs while capturing: the graph is launched on the caller's stream
+    c->fused.graph_mode = true;
+    rc = step_body(c, 0, 0, head != 0, m.dargs);
+    c->fused.graph_mode = false;
+    c->fused.bar_stale = true;
+    c->st = st;
+    cudaError_t e = cudaStreamEndCapture(m.cap_st, &gr);
+    cudaGraphExec_t ex = nullptr;
+    if (!rc && e == cudaSuccess && gr) e = cudaGraphInstantiate(&ex, gr, 0);
+    if (gr) cudaGraphDestroy(gr);
+    if (rc || e != cudaSuccess || !ex) {
+        cudaGetLastError();
+        m.graph_off = true;   // run eagerly from now on
+        return TLMG_OK;
+    }
+    m.graph[head] = ex;
+    m.graph_gen[head] = c->wgen;
+    m.graph_launches[head] = launches_total() - n0;
+    m.captures++;
+    return TLMG_OK;
+}
+
+static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    StepModel *mp = c->step;
+    if (!mp) return set_error(TLMG_EINVAL, "decode_step: tlmg_step_open first");
+    StepModel &m = *mp;
+    const int L = c->g.n_layers;
+    if (token < 0 || token >= m.vocab) return set_error(TLMG_EINVAL, "decode_step: token %d out of range", token);
+    if (pos < 0 || pos >= m.max_ctx) return set_error(TLMG_ERANGE, "decode_step: position %d (context %d)", pos, m.max_ctx);
+    if (!m.embd) return set_error(TLMG_ENOTFOUND, "decode_step: no embedding (tlmg_set_embedding)");
+    if (logits && !m.head) return set_error(TLMG_ENOTFOUND, "decode_step: no lm_head (tlmg_set_output)");
+    for (int l = 0; l < L; l++)
+        if (!m.A[l].set) return set_error(TLMG_ENOTFOUND, "decode_step: layer %d has no attention weights", l);
+    cudaSetDevice(c->device);
+    cudaStream_t st = c->st;
+    const int head = logits != nullptr;
+    int rc;
+    bool replayed = false;
+    if (step_graph_allowed(c)) {
+        if (!m.graph[head] || m.graph_gen[head] != c->wgen)
+            if ((rc = capture_step(c, head))) return rc;
+        if (m.graph[head] && !m.graph_off) {
+            if ((rc = step_set_args(m.dargs, token, pos, st))) return rc;
+            cudaError_t e = cudaGraphLaunch(m.graph[head], st);
+            if (e != cudaSuccess) return cuda_fail(e, "decode_step: graph launch");
+            count_launch((int)m.graph_launches[head]);
+            c->fused.bar_stale = true;
+            replayed = true;
+            m.replays++;
+        }
+    }
+    if (!replayed && (rc = step_body(c, token, pos, head != 0, nullptr))) return rc;
+    m.calls++;
+    if (!logits) return TLMG_OK;
     const size_t bytes = 4 * (size_t)m.vocab;
     if (is_device_ptr(logits)) {
         cudaError_t e = cudaMemcpyAsync(logits, m.logits, bytes, cudaMemcpyDeviceToDevice, st);
@@ -1825,6 +1948,25 @@ static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
     cudaError_t e = cudaMemcpyAsync(logits, m.logits, bytes, cudaMemcpyDefault, st);
     if (e != cudaSuccess) return cuda_fail(e, "decode_step: logits copy");
     return stream_sync(c);
+}
+
+int tlmg_step_info(const tlmg_ctx *c, int64_t *out) {
+    if (!c || !out) return set_error(TLMG_EINVAL, "step_info: NULL argument");
+    if (!c->step) return set_error(TLMG_EINVAL, "step_info: tlmg_step_open first");
+    const StepModel &m = *c->step;
+    out[0] = m.calls;
+    out[1] = m.replays;
+    out[2] = m.captures;
+    out[3] = m.graph_off ? 1 : 0;
+    return TLMG_OK;
+}
+
+int tlmg_step_graphs(tlmg_ctx *c, int on) {
+    if (!c) return set_error(TLMG_EINVAL, "NULL context");
+    if (!c->step) return set_error(TLMG_EINVAL, "step_graphs: tlmg_step_open first");
+    c->step->use_graphs = on != 0;
+    if (on) c->step->graph_off = false;
+    return TLMG_OK;
 }
 
 int tlmg_decode_step(tlmg_ctx *c, int token, int pos, float *logits) { return decode_step(c, token, pos, logits); }

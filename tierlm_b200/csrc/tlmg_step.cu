@@ -64,15 +64,31 @@ __device__ float dequant_at(int dt, const uint8_t *row, int i) {
     }
 }
 
-__global__ void k_embed_row(int dt, const uint8_t *__restrict__ row, int n, float *__restrict__ out) {
+__global__ void k_embed_row(int dt, const uint8_t *__restrict__ base, size_t rb, int token,
+                            const int32_t *__restrict__ dargs, int n, float *__restrict__ out) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) out[i] = dequant_at(dt, row, i);
+    if (dargs) token = dargs[0];
+    if (i < n) out[i] = dequant_at(dt, base + (size_t)token * rb, i);
 }
 
-int step_embed(int dt, const uint8_t *row, int D, float *h, cudaStream_t st) {
+__global__ void k_step_args(int32_t *dargs, int token, int pos) {
+    dargs[0] = token;
+    dargs[1] = pos;
+    dargs[2] = pos + 1;
+}
+
+int step_set_args(int32_t *dargs, int token, int pos, cudaStream_t st) {
+    k_step_args<<<1, 1, 0, st>>>(dargs, token, pos);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "step arguments launch");
+}
+
+int step_embed(int dt, const uint8_t *base, size_t rb, int token, const int32_t *dargs, int D, float *h,
+               cudaStream_t st) {
     const int qk = dt_block(dt);
     if (qk == 0 || D % qk || dt == DT_MXFP4) return set_error(TLMG_EUNSUP, "embedding dtype %d", dt);
-    k_embed_row<<<(D + 255) / 256, 256, 0, st>>>(dt, row, D, h);
+    k_embed_row<<<(D + 255) / 256, 256, 0, st>>>(dt, base, rb, token, dargs, D, h);
     count_launch();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "embedding launch");
@@ -88,11 +104,14 @@ __device__ __forceinline__ void kv_store(__nv_bfloat16 *p, float v) { *p = __flo
 // k and v of position pos into the layer's page (pages [KV][page][hd]).
 template <typename KT>
 __global__ void k_heads(float *__restrict__ qkv, int H, int KV, int hd, const float *__restrict__ q_norm,
-                        const float *__restrict__ k_norm, float eps, const float *__restrict__ rope,
-                        KT *__restrict__ kpage, KT *__restrict__ vpage, int page, int pos) {
+                        const float *__restrict__ k_norm, float eps, const float *__restrict__ rope_all,
+                        KT *__restrict__ kpage, KT *__restrict__ vpage, int page, int pos,
+                        const int32_t *__restrict__ dargs) {
     __shared__ double red[32];
     __shared__ float r_sh;
     __shared__ float v[256];
+    if (dargs) pos = dargs[1];
+    const float *rope = rope_all + (size_t)pos * hd;
     const int b = blockIdx.x, i = threadIdx.x, half = hd / 2;
     const bool is_q = b < H;
     float *x = qkv + (size_t)b * hd;   // q heads [H][hd] then k heads [KV][hd]
@@ -117,19 +136,19 @@ __global__ void k_heads(float *__restrict__ qkv, int H, int KV, int hd, const fl
     }
 }
 
-int step_heads(const StepModel &m, int l, int pos, float eps, cudaStream_t st) {
+int step_heads(const StepModel &m, int l, int pos, const int32_t *dargs, float eps, cudaStream_t st) {
     const StepLayer &A = m.A[l];
-    const float *rope = m.rope + (size_t)pos * m.hd;
+    const float *rope = m.rope;
     const size_t per = (size_t)m.KV * m.page * m.hd;   // one layer's page
     if (m.kv_dt == DT_F32) {
         float *kp = static_cast<float *>(m.kpool) + (size_t)l * per, *vp = static_cast<float *>(m.vpool) + (size_t)l * per;
         k_heads<float><<<m.H + m.KV, m.hd, 0, st>>>(m.qkv, m.H, m.KV, m.hd, A.q_norm, A.k_norm, eps, rope, kp, vp,
-                                                    m.page, pos);
+                                                    m.page, pos, dargs);
     } else {
         __nv_bfloat16 *kp = static_cast<__nv_bfloat16 *>(m.kpool) + (size_t)l * per,
                       *vp = static_cast<__nv_bfloat16 *>(m.vpool) + (size_t)l * per;
         k_heads<__nv_bfloat16><<<m.H + m.KV, m.hd, 0, st>>>(m.qkv, m.H, m.KV, m.hd, A.q_norm, A.k_norm, eps, rope,
-                                                            kp, vp, m.page, pos);
+                                                            kp, vp, m.page, pos, dargs);
     }
     count_launch();
     cudaError_t e = cudaGetLastError();

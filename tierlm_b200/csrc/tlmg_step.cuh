@@ -47,13 +47,40 @@ struct StepModel {
     uint8_t *xq = nullptr;              // quantised xb
     float *rope = nullptr;              // [max_ctx][hd]: cs | sn of every position
     float *logits = nullptr;            // [vocab]
+    int32_t *dargs = nullptr;           // [3] token, position, position + 1 (graph replay)
+    // captured steps: [0] without lm_head, [1] with; valid while wgen matches
+    cudaGraphExec_t graph[2] = {};
+    uint64_t graph_gen[2] = {};
+    int64_t graph_launches[2] = {};     // kernels in each graph
+    bool use_graphs = true;             // tlmg_step_graphs
+    bool graph_off = false;             // capture failed once: eager from then on
+    int64_t calls = 0;                  // steps run (the first is always eager)
+    int64_t replays = 0, captures = 0;
+    cudaStream_t cap_st = nullptr;      // private stream graphs are captured on (the caller's may be the
+                                        // legacy default stream, which cannot be captured)
 };
 
-// Launchers (tlmg_step.cu); all asynchronous on `st`.
-int step_embed(int dt, const uint8_t *row, int D, float *h, cudaStream_t st);
+inline void step_graphs_release(StepModel &m) {
+    for (int h = 0; h < 2; h++)
+        if (m.graph[h]) {
+            cudaGraphExecDestroy(m.graph[h]);
+            m.graph[h] = nullptr;
+        }
+    if (m.cap_st) cudaStreamDestroy(m.cap_st);
+    m.cap_st = nullptr;
+}
+
+// Launchers (tlmg_step.cu); all asynchronous on `st`. With dargs (device
+// int32 [3]: token, position, position + 1, written by step_set_args) the
+// kernels read the token and position from device memory, so that one
+// captured graph serves every position; else they take token / pos.
+int step_set_args(int32_t *dargs, int token, int pos, cudaStream_t st);
+// h = row `token` of the embedding table (rows of rb bytes from base).
+int step_embed(int dt, const uint8_t *base, size_t rb, int token, const int32_t *dargs, int D, float *h,
+               cudaStream_t st);
 // qk-norm (when given), RoPE of the q and k heads in qkv, then k and v of
-// position pos into layer l's page (device buffers of m; the position's
+// the position into layer l's page (device buffers of m; the position's
 // RoPE row of m.rope).
-int step_heads(const StepModel &m, int l, int pos, float eps, cudaStream_t st);
+int step_heads(const StepModel &m, int l, int pos, const int32_t *dargs, float eps, cudaStream_t st);
 
 }  // namespace tlmg

@@ -248,6 +248,15 @@ class MoeContext:
         CUDA) or None (no lm_head)."""
         check(self._lib.tlmg_decode_step(self._h, token, pos, _ptr(logits)))
 
+    def step_graphs(self, on: bool) -> None:
+        """Graph replay of the step from the second call on (default on)."""
+        check(self._lib.tlmg_step_graphs(self._h, 1 if on else 0))
+
+    def step_info(self) -> dict:
+        out = (C.c_int64 * 4)()
+        check(self._lib.tlmg_step_info(self._h, out))
+        return {"steps": out[0], "replays": out[1], "captures": out[2], "graphs_off": bool(out[3])}
+
     def ep_open(self, rank: int, n_ranks: int, max_tok: int) -> bytes:
         """Opens this rank's peer-memory exchange; returns its handle (bytes
         to hand to every peer)."""
