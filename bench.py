@@ -224,6 +224,76 @@ def build_context(args, dev, seed: int):
     return ctx
 
 
+def slot_cache_section(args, dev, rank: int, world: int, stream, timed) -> dict:
+    """The reference's expert store on the GPU (BASELINE config 5 expert
+    size: D 4096, d_expert 1536, Q4_K gate/up/down, 10.6 MB per expert, 128
+    experts top-8): every expert of CL layers registered in pinned host
+    memory, cache_frac of them fit in HBM slots, and each step is one token
+    through the CL layers' whole moe() blocks (tlmg_moe_layer on a device h).
+    Arms: demand loads only, and the router lookahead (tlmg_cache_lookahead:
+    next layer's RMSNorm + router on the current residual, its top-k
+    prefetched while this layer computes). Random inputs: no temporal
+    locality beyond what the lookahead predicts."""
+    import torch
+
+    from tierlm_b200 import synth
+    from tierlm_b200.moe import MoeContext
+    D5, DE5, CL = 4096, 1536, args.cache_layers
+    rb_g, rb_d = D5 // 256 * 144, DE5 // 256 * 144
+    per = 2 * DE5 * rb_g + D5 * rb_d                        # 10,616,832 bytes per expert
+    cctx = MoeContext(CL, D5, DE5, E, K, router=0, device=dev.index)
+    cctx.set_stream(stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242 + rank)
+    n_slots = max(K + 1, int(args.cache_frac * CL * E))
+    cctx.cache_enable(n_slots, per + 3 * 512)
+    rng = np.random.default_rng(99 + rank)
+    host = []
+    for layer in range(CL):
+        gu = synth.device_rows(DT_GATE, E * 2 * DE5, D5, gen, dev).view(E, 2 * DE5 * rb_g)
+        dn = synth.device_rows(DT_GATE, E * D5, DE5, gen, dev).view(E, D5 * rb_d)
+        hb = torch.cat([gu, dn], dim=1).cpu().pin_memory()            # [E, per]: gate | up | down
+        del gu, dn
+        host.append(hb)
+        for e in range(E):
+            cctx.set_expert_host(layer, e, (DT_GATE, DT_GATE, DT_GATE), hb[e], (0, DE5 * rb_g, 2 * DE5 * rb_g))
+        cctx.set_layer(layer, (1.0 + 0.1 * rng.standard_normal(D5)).astype(np.float32), 0,
+                       (rng.standard_normal((E, D5)) / np.sqrt(D5)).astype(np.float32), 4 * D5)
+    NR = args.warmup + args.steps                           # every token of both arms distinct
+    hs = torch.randn((2 * NR, D5), generator=gen, device=dev)
+    h = torch.empty(D5, device=dev)
+    base = [0]
+
+    def cstep(s):
+        h.copy_(hs[base[0] + s % NR])
+        for layer in range(CL):
+            cctx.moe_layer(layer, h)
+        cctx.cache_tick()                                  # one model step (frequency decay clock)
+
+    res = {}
+    for arm, (name, depth) in enumerate((("demand", 0), ("lookahead", 1))):
+        base[0] = arm * NR
+        cctx.cache_lookahead(depth, K)
+        for s in range(args.warmup):
+            cstep(s)
+        st0 = cctx.cache_stats()
+        cms = timed(cstep, args.steps)
+        st1 = cctx.cache_stats()
+        d = {k2: st1[k2] - st0[k2] for k2 in st1}
+        res[name] = {"tokens_per_s": round(world * args.steps / (cms * 1e-3), 2),
+                     "ms_per_token": round(cms / args.steps, 3),
+                     "hit_rate": round(d["hits"] / max(1, d["hits"] + d["misses"]), 3),
+                     "prefetch_issued": d["prefetched"], "prefetch_used": d["prefetch_hits"],
+                     "h2d_GBps": round(d["bytes"] / (cms * 1e-3) / 1e9, 1)}
+    cctx.close()
+    del host
+    return {"config": "BASELINE config 5 expert size: D 4096, d_expert 1536, Q4_K gate/up/down "
+                      f"({per:,} bytes per expert), 128 experts top-8, {CL} layers",
+            "slots": n_slots, "cold_fraction": round(1 - n_slots / (CL * E), 3),
+            "policy": "the reference store's (LFU with decay, hint rules, demand reserve)",
+            "workload": "bs=1 decode, whole moe() per layer on a device residual, random inputs", **res}
+
+
 def decode_step_section(ctx, args, dev, g, peak: float) -> dict:
     """BASELINE config 3 through tlmg_decode_step: Qwen3-30B-A3B shape
     (48 layers, D 2048, 32 q / 4 KV heads x 128 with qk-norm, 128 experts
@@ -528,61 +598,11 @@ def main() -> None:
                    "weight_GBps": round(world * psteps * pbytes / (pms * 1e-3) / 1e9, 1),
                    "note": "tlmg_expert_ffn_batch with all prompt tokens of a layer in one call (tensor-core kernels)"}
 
-    # ---- HBM slot cache (cold experts in pinned host memory): bs=1 decode through
-    # CL layers whose 128 experts share CACHE_FRAC x (CL x 128) HBM slots
+    # ---- HBM slot cache (BASELINE config 5 expert size): cold experts in pinned host memory, bs=1
+    # decode through CL layers whose 128 experts share cache_frac x (CL x 128) HBM slots
     cache = None
     if args.cache_layers > 0:
-        from tierlm_b200 import synth
-        from tierlm_b200.moe import MoeContext
-        CL = args.cache_layers
-        cctx = MoeContext(CL, D, DE, E, K, router=0, device=dev.index)
-        cctx.set_stream(stream)
-        gen2 = torch.Generator(device=dev)
-        gen2.manual_seed(4242 + rank)
-        rb_g, rb_d = D // 256 * 144, DE // 256 * 210
-        per = 2 * DE * rb_g + D * rb_d
-        n_slots = max(K, int(args.cache_frac * CL * E))
-        cctx.cache_enable(n_slots, per + 3 * 512)
-        host = []
-        for layer in range(CL):
-            gu = synth.device_rows(DT_GATE, E * 2 * DE, D, gen2, dev).view(E, 2 * DE * rb_g)
-            dn = synth.device_rows(DT_DOWN, E * D, DE, gen2, dev).view(E, D * rb_d)
-            hb = torch.cat([gu, dn], dim=1).cpu().pin_memory()            # [E, per]: gate | up | down
-            host.append(hb)
-            for e in range(E):
-                cctx.set_expert_host(layer, e, (DT_GATE, DT_GATE, DT_DOWN), hb[e], (0, DE * rb_g, 2 * DE * rb_g))
-        NR = 64                                             # distinct token inputs, rotated: the working set
-        cx = torch.randn((NR, CL, D), generator=g, device=dev)   # (NR x CL x 8 experts) exceeds the slots
-        clg = torch.randn((NR, CL, E), generator=g, device=dev)
-        co = torch.empty((CL, D), device=dev)
-        nxt = torch.topk(clg, K, dim=-1).indices.to(torch.int32).cpu().numpy()   # each layer's routed ids
-
-        def cstep(s, lookahead):
-            i = s % NR
-            for layer in range(CL):
-                cctx.expert_ffn(layer, cx[i, layer], clg[i, layer], co[layer])
-                if lookahead:   # ids of the next layer, known one layer ahead (the reference's lookahead)
-                    j, l2 = (i, layer + 1) if layer + 1 < CL else ((s + 1) % NR, 0)
-                    cctx.cache_prefetch(l2, nxt[j, l2])
-
-        res = {}
-        for la in (False, True):
-            for s in range(args.warmup):
-                cstep(s, la)
-            st0 = cctx.cache_stats()
-            cms = timed(lambda s: cstep(s, la), args.steps)
-            st1 = cctx.cache_stats()
-            d = {k2: st1[k2] - st0[k2] for k2 in st1}
-            res["lookahead" if la else "demand"] = {
-                "tokens_per_s": round(world * args.steps / (cms * 1e-3), 1),
-                "layer_tokens_per_s": round(world * args.steps * CL / (cms * 1e-3), 1),
-                "hit_rate": round((d["hits"]) / max(1, d["hits"] + d["misses"]), 3),
-                "h2d_GBps": round(d["bytes"] / (cms * 1e-3) / 1e9, 1)}
-        cache = {"layers": CL, "slots": n_slots, "slot_fraction": args.cache_frac,
-                 "workload": "bs=1 decode, experts in pinned host memory, random routing (a worst case: "
-                             "no temporal locality)", **res}
-        cctx.close()
-        del host
+        cache = slot_cache_section(args, dev, rank, world, stream, timed)
 
     # ---- decode attention over a paged KV cache (config-3 attention shape: 32 query heads,
     # 4 KV heads, head_dim 128, 64-position pages), one layer per call, replicated per GPU

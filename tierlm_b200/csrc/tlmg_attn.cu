@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(XS_ROWS) k_attn_scores(const float *__restrict
                                                          const int32_t *__restrict__ table, int n_pages, int page,
                                                          int T, const int32_t *__restrict__ dT, int H, int KV,
                                                          int hd, float scale, float *__restrict__ s) {
+    pdl_enter();
     if (dT) T = *dT;   // graph replay: the position count lives in device memory
     extern __shared__ float4 sm4[];
     __shared__ long long ro[XS_ROWS];
@@ -181,6 +182,7 @@ __global__ void __launch_bounds__(HD) k_attn_out_exact(const KT *__restrict__ vp
                                                        int n_pages, int page, int T, const int32_t *__restrict__ dT,
                                                        int psm_cap, int H, int KV, float *__restrict__ s,
                                                        float *__restrict__ out) {
+    pdl_enter();
     if (dT) T = *dT;
     constexpr int ROW_B = HD * (int)sizeof(KT);
     constexpr int C16 = ROW_B / 16;
@@ -324,6 +326,7 @@ __global__ void __launch_bounds__(SPLIT_THREADS) k_attn_split(const float *__res
                                                               int hd, int tr, int span,
                                                               int n_span, float qscale, float *__restrict__ pm,
                                                               float *__restrict__ pl, float *__restrict__ po) {
+    pdl_enter();
     extern __shared__ float4 sm4[];
     if (dT) T = *dT;
     const int grp = H / KV, kvh = blockIdx.y, sidx = blockIdx.x, tid = threadIdx.x;
@@ -522,6 +525,7 @@ __global__ void __launch_bounds__(128) k_attn_split_tc(const float *__restrict__
                                                        int n_span, float qscale,
                                                        float *__restrict__ pm, float *__restrict__ pl,
                                                        float *__restrict__ po) {
+    pdl_enter();
     constexpr int ROW_B = HD * 2 + 16;           // padded row bytes in shared memory
     constexpr int MAT_B = TC_ROWS * ROW_B;
     constexpr int C16 = HD * 2 / 16;             // 16-byte pieces per row
@@ -921,7 +925,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         const size_t s1 = (size_t)grp * hd * 4 + (size_t)XS_ROWS * (hd * sizeof(KT) + 16);
         if (!smem_opt_in(k_attn_scores<KT>, s1)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
         dim3 g1((T + XS_ROWS - 1) / XS_ROWS, KV);
-        k_attn_scores<KT><<<g1, XS_ROWS, s1, st>>>(q, kp, table, n_pages, page, T, dT, H, KV, hd, scale, work);
+        launch_k(k_attn_scores<KT>, g1, XS_ROWS, s1, st, q, kp, table, n_pages, page, T, dT, H, KV, hd, scale, work);
         bool ok = true;
 #define TLMG_XO(HDV)                                                                                       \
     if (hd == HDV) {                                                                                       \
@@ -929,7 +933,8 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         const size_t s2 = (size_t)nst * XO_ROWS * HDV * sizeof(KT) + (T <= PSM_MAX ? (size_t)T * 4 : 0);   \
         auto fn = k_attn_out_exact<KT, HDV, nst>;                                                          \
         ok = smem_opt_in(fn, s2);                                                                          \
-        if (ok) fn<<<H, HDV, s2, st>>>(vp, table, n_pages, page, T, dT, T <= PSM_MAX ? T : 0, H, KV, work, out); \
+        if (ok) launch_k(fn, H, HDV, s2, st, vp, table, n_pages, page, T, dT, T <= PSM_MAX ? T : 0, H, KV, work,   \
+                         out);                                                                             \
     }
         TLMG_XO(64)
         TLMG_XO(128)
@@ -952,8 +957,8 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
     if (hd == HDV) {                                                                                            \
         auto fn = k_attn_split_tc<HDV, tc_stages<HDV>()>;                                                       \
         ok = smem_opt_in(fn, sm);                                                                               \
-        if (ok) fn<<<g1, 128, sm, st>>>(q, kp, vp, table, n_pages, page, lp, T, dT, H, KV, g.span, g.n_span, qscale, pm, \
-                                        pl, po);                                                                \
+        if (ok) launch_k(fn, g1, 128, sm, st, q, kp, vp, table, n_pages, page, lp, T, dT, H, KV, g.span, g.n_span,    \
+                         qscale, pm, pl, po);                                                                   \
     }
                 TLMG_TC(64)
                 TLMG_TC(128)
@@ -968,7 +973,7 @@ static int launch_attention(int mode, const float *q, const KT *kp, const KT *vp
         }
         const size_t sm = split_smem(g, grp, hd, (int)sizeof(KT));
         if (!smem_opt_in(k_attn_split<KT>, sm)) return set_error(TLMG_EIO, "attention: shared memory opt-in failed");
-        k_attn_split<KT><<<g1, SPLIT_THREADS, sm, st>>>(q, kp, vp, table, n_pages, page, T, dT, H, KV, hd, g.tr, g.span,
+        launch_k(k_attn_split<KT>, g1, SPLIT_THREADS, sm, st, q, kp, vp, table, n_pages, page, T, dT, H, KV, hd, g.tr, g.span,
                                                         g.n_span, qscale, pm, pl, po);
         if (launch_merge(pm, pl, po, g.n_span, H, hd, out, st) != cudaSuccess)
             return cuda_fail(cudaGetLastError(), "attention merge launch");

@@ -99,6 +99,15 @@ __device__ __forceinline__ float cr_expf(float xf) {
     return __double2float_rn(__dmul_rn(p, s));
 }
 // silu(x) = x / (1 + expf(-x)) (reference tlm_model.c:171)
+// Programmatic dependent launch: wait until the preceding grid of the
+// stream has completed and its writes are visible (returns at once when the
+// kernel was not launched as a dependent), then let the next one be
+// scheduled.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+}
+
 // 1 / sqrtf((float)(ss / n) + eps), ss = sum of x[i]^2 in double: the
 // reference's RMSNorm scale (rmsnorm, src/lib/tlm_model.c:164-169), whose
 // ss is a serial double sum. Every thread of the block calls this (blockDim

@@ -20,6 +20,30 @@ cudaStream_t pick_stream(void *user);
 void count_launch(int n = 1);
 int64_t launches_total();
 
+// Programmatic dependent launch of the decoder step's kernels: while a
+// thread has it on, the launchers below start their kernels with
+// programmatic stream serialisation (the kernel may be scheduled while its
+// predecessor finishes; every such kernel waits in griddepcontrol.wait
+// before it reads anything its predecessor wrote).
+void set_pdl(bool on);
+bool pdl_on();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_on() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, static_cast<KArgs>(args)...);
+}
+
 // Launchers of the kernel-level ops (also used by the layer code).
 int launch_quant_act(int kind, const float *x, int64_t n, void *dst, cudaStream_t st);
 // With res: y[r] = res[r] + dot (res may be y itself).

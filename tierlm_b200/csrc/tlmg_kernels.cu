@@ -34,6 +34,9 @@ int cuda_fail(cudaError_t e, const char *what) {
 
 static std::atomic<int64_t> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+static thread_local bool t_pdl = false;
+void set_pdl(bool on) { t_pdl = on; }
+bool pdl_on() { return t_pdl; }
 int64_t launches_total() { return g_launches.load(std::memory_order_relaxed); }
 
 static thread_local cudaStream_t t_stream = nullptr;
@@ -62,6 +65,7 @@ bool is_device_ptr(const void *p) {
 // ---------------------------------------------------------------------------
 // activation quantisation: one warp per block
 __global__ void k_quant_q8k(const float *__restrict__ x, int64_t n, uint8_t *__restrict__ dst) {
+    pdl_enter();
     int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (b * 256 >= n) return;
@@ -70,6 +74,7 @@ __global__ void k_quant_q8k(const float *__restrict__ x, int64_t n, uint8_t *__r
 }
 
 __global__ void k_quant_q80(const float *__restrict__ x, int64_t n, uint8_t *__restrict__ dst) {
+    pdl_enter();
     int64_t b = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     int lane = threadIdx.x & 31;
     if (b * 32 >= n) return;
@@ -88,8 +93,8 @@ int launch_quant_act(int kind, const float *x, int64_t n, void *dst, cudaStream_
     int64_t nb = kind == DT_Q8_K ? (n + 255) / 256 : (n + 31) / 32;
     const int wpb = 8;
     unsigned grid = (unsigned)((nb + wpb - 1) / wpb);
-    if (kind == DT_Q8_K) k_quant_q8k<<<grid, 32 * wpb, 0, st>>>(x, n, (uint8_t *)dst);
-    else k_quant_q80<<<grid, 32 * wpb, 0, st>>>(x, n, (uint8_t *)dst);
+    if (kind == DT_Q8_K) launch_k(k_quant_q8k, grid, 32 * wpb, 0, st, x, n, (uint8_t *)dst);
+    else launch_k(k_quant_q80, grid, 32 * wpb, 0, st, x, n, (uint8_t *)dst);
     count_launch();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "quantize_act launch");
@@ -107,6 +112,7 @@ template <int A>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_q(int dt, const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act,
            float *y, int64_t n, int64_t r0, int64_t r1, const float *res) {
+    pdl_enter();
     __shared__ BlockPart part[MV_WARPS][MV_CHUNK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
     const int qk = dt_block(dt), bb = dt_block_bytes(dt), abb = act_block_bytes(act_kind_for(dt));
@@ -160,6 +166,7 @@ template <int DT>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_qs(const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act, float *y, int nb, int64_t r0,
             int64_t r1, const float *res) {
+    pdl_enter();
     extern __shared__ uint4 mv_rows[];
     __shared__ BlockPart part[MV_WARPS][MV_CHUNK];
     constexpr int BB = dt_block_bytes(DT), ABB = act_block_bytes(act_kind_for(DT));
@@ -230,6 +237,7 @@ template <int A>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_f(int dt, const uint8_t *__restrict__ W, size_t rb, const float *__restrict__ x,
            float *y, int64_t n, int64_t r0, int64_t r1, const float *res) {
+    pdl_enter();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int64_t row = r0 + (int64_t)blockIdx.x * nw + warp; row < r1; row += (int64_t)gridDim.x * nw) {
         const uint8_t *wr = W + (size_t)row * rb;
@@ -318,9 +326,10 @@ int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, 
             const int nsm = 148;
             const int64_t need = (rows + MV_WARPS - 1) / MV_WARPS;
             const unsigned gq = (unsigned)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)per_sm * nsm));
-            mv<<<gq, MV_WARPS * 32, sm, st>>>(W, rb, (const uint8_t *)act, y, (int)(n / qk), r0, r1, res);
+            cudaError_t e = launch_k(mv, gq, MV_WARPS * 32, sm, st, W, rb, (const uint8_t *)act, y, (int)(n / qk), r0,
+                                     r1, res);
             count_launch();
-            cudaError_t e = cudaGetLastError();
+            if (e == cudaSuccess) e = cudaGetLastError();
             return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "matvec_rows launch");
         }
     }
@@ -329,17 +338,17 @@ int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, 
         grid = grid_nw;
         const unsigned thr_f = 32 * nw;
         switch (A) {
-        case 16: case 4: k_matvec_f<4><<<grid, thr_f, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
-        case 2: k_matvec_f<2><<<grid, thr_f, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
-        default: k_matvec_f<1><<<grid, thr_f, 0, st>>>(dt, W, rb, x, y, n, r0, r1, res); break;
+        case 16: case 4: launch_k(k_matvec_f<4>, grid, thr_f, 0, st, dt, W, rb, x, y, n, r0, r1, res); break;
+        case 2: launch_k(k_matvec_f<2>, grid, thr_f, 0, st, dt, W, rb, x, y, n, r0, r1, res); break;
+        default: launch_k(k_matvec_f<1>, grid, thr_f, 0, st, dt, W, rb, x, y, n, r0, r1, res); break;
         }
     } else {
         const uint8_t *a = (const uint8_t *)act;
         switch (A) {
-        case 16: k_matvec_q<16><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
-        case 4: k_matvec_q<4><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
-        case 2: k_matvec_q<2><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
-        default: k_matvec_q<1><<<grid, thr, 0, st>>>(dt, W, rb, a, y, n, r0, r1, res); break;
+        case 16: launch_k(k_matvec_q<16>, grid, thr, 0, st, dt, W, rb, a, y, n, r0, r1, res); break;
+        case 4: launch_k(k_matvec_q<4>, grid, thr, 0, st, dt, W, rb, a, y, n, r0, r1, res); break;
+        case 2: launch_k(k_matvec_q<2>, grid, thr, 0, st, dt, W, rb, a, y, n, r0, r1, res); break;
+        default: launch_k(k_matvec_q<1>, grid, thr, 0, st, dt, W, rb, a, y, n, r0, r1, res); break;
         }
     }
     count_launch();

@@ -324,6 +324,7 @@ k_ffn_down(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, cons
 // rounding boundary; then thread 0 redoes the sequential sum.
 __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ wn, int n, float eps,
                           float *__restrict__ out, uint8_t *__restrict__ q8k) {
+    pdl_enter();
     __shared__ double red[32];
     __shared__ float r_sh;
     const float r = block_rms_inv(x, n, eps, red, &r_sh);
@@ -1510,7 +1511,7 @@ static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float 
         dh = c->h;
     }
     // xb = rmsnorm(h); activations of xb
-    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, Ly.ffn_norm, D, g.norm_eps, c->x, nullptr);
+    launch_k(k_rmsnorm, 1, 256, 0, c->st, dh, Ly.ffn_norm, D, g.norm_eps, c->x, (uint8_t *)nullptr);
     if ((rc = launched("rmsnorm"))) return rc;
     // the persistent kernel quantises its input itself: the activations of
     // xb are only formed for the parts that read them
@@ -1812,7 +1813,7 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
         const StepLayer &A = m.A[l];
         // attention() (src/lib/tlm_model.c:730-763)
         const bool xq_now = act_kind_for(A.dt[0]) == DT_Q8_K;   // xb as Q8_K from the norm kernel itself
-        k_rmsnorm<<<1, 256, 0, st>>>(dh, A.attn_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
+        launch_k(k_rmsnorm, 1, 256, 0, st, dh, A.attn_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
         if ((rc = launched("attention rmsnorm"))) return rc;
         ActCache ax{ m.xb, D, m.xq, m.xq + off80 };
         ax.have8k = xq_now;
@@ -1844,7 +1845,7 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
     }
     if (!head) return TLMG_OK;
     const bool xq_now = act_kind_for(m.head_dt) == DT_Q8_K;
-    k_rmsnorm<<<1, 256, 0, st>>>(dh, m.out_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
+    launch_k(k_rmsnorm, 1, 256, 0, st, dh, m.out_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
     if ((rc = launched("output rmsnorm"))) return rc;
     ActCache af{ m.xb, D, m.xq, m.xq + off80 };
     af.have8k = xq_now;
@@ -1887,7 +1888,9 @@ static int capture_step(tlmg_ctx *c, int head) {
     }
     c->st = m.cap_st;   // nothing runs while capturing: the graph is launched on the caller's stream
     c->fused.graph_mode = true;
+    set_pdl(true);
     rc = step_body(c, 0, 0, head != 0, m.dargs);
+    set_pdl(false);
     c->fused.graph_mode = false;
     c->fused.bar_stale = true;
     c->st = st;
@@ -1937,7 +1940,12 @@ static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
             m.replays++;
         }
     }
-    if (!replayed && (rc = step_body(c, token, pos, head != 0, nullptr))) return rc;
+    if (!replayed) {
+        set_pdl(true);
+        rc = step_body(c, token, pos, head != 0, nullptr);
+        set_pdl(false);
+        if (rc) return rc;
+    }
     m.calls++;
     if (!logits) return TLMG_OK;
     const size_t bytes = 4 * (size_t)m.vocab;

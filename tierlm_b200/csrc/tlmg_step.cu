@@ -66,12 +66,14 @@ __device__ float dequant_at(int dt, const uint8_t *row, int i) {
 
 __global__ void k_embed_row(int dt, const uint8_t *__restrict__ base, size_t rb, int token,
                             const int32_t *__restrict__ dargs, int n, float *__restrict__ out) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (dargs) token = dargs[0];
     if (i < n) out[i] = dequant_at(dt, base + (size_t)token * rb, i);
 }
 
 __global__ void k_step_args(int32_t *dargs, int token, int pos) {
+    pdl_enter();
     dargs[0] = token;
     dargs[1] = pos;
     dargs[2] = pos + 1;
@@ -88,9 +90,9 @@ int step_embed(int dt, const uint8_t *base, size_t rb, int token, const int32_t 
                cudaStream_t st) {
     const int qk = dt_block(dt);
     if (qk == 0 || D % qk || dt == DT_MXFP4) return set_error(TLMG_EUNSUP, "embedding dtype %d", dt);
-    k_embed_row<<<(D + 255) / 256, 256, 0, st>>>(dt, base, rb, token, dargs, D, h);
+    cudaError_t e = launch_k(k_embed_row, (D + 255) / 256, 256, 0, st, dt, base, rb, token, dargs, D, h);
     count_launch();
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "embedding launch");
 }
 
@@ -107,6 +109,7 @@ __global__ void k_heads(float *__restrict__ qkv, int H, int KV, int hd, const fl
                         const float *__restrict__ k_norm, float eps, const float *__restrict__ rope_all,
                         KT *__restrict__ kpage, KT *__restrict__ vpage, int page, int pos,
                         const int32_t *__restrict__ dargs) {
+    pdl_enter();
     __shared__ double red[32];
     __shared__ float r_sh;
     __shared__ float v[256];
@@ -142,13 +145,13 @@ int step_heads(const StepModel &m, int l, int pos, const int32_t *dargs, float e
     const size_t per = (size_t)m.KV * m.page * m.hd;   // one layer's page
     if (m.kv_dt == DT_F32) {
         float *kp = static_cast<float *>(m.kpool) + (size_t)l * per, *vp = static_cast<float *>(m.vpool) + (size_t)l * per;
-        k_heads<float><<<m.H + m.KV, m.hd, 0, st>>>(m.qkv, m.H, m.KV, m.hd, A.q_norm, A.k_norm, eps, rope, kp, vp,
-                                                    m.page, pos, dargs);
+        launch_k(k_heads<float>, m.H + m.KV, m.hd, 0, st, m.qkv, m.H, m.KV, m.hd, A.q_norm, A.k_norm, eps, rope, kp,
+                 vp, m.page, pos, dargs);
     } else {
         __nv_bfloat16 *kp = static_cast<__nv_bfloat16 *>(m.kpool) + (size_t)l * per,
                       *vp = static_cast<__nv_bfloat16 *>(m.vpool) + (size_t)l * per;
-        k_heads<__nv_bfloat16><<<m.H + m.KV, m.hd, 0, st>>>(m.qkv, m.H, m.KV, m.hd, A.q_norm, A.k_norm, eps, rope,
-                                                            kp, vp, m.page, pos, dargs);
+        launch_k(k_heads<__nv_bfloat16>, m.H + m.KV, m.hd, 0, st, m.qkv, m.H, m.KV, m.hd, A.q_norm, A.k_norm, eps,
+                 rope, kp, vp, m.page, pos, dargs);
     }
     count_launch();
     cudaError_t e = cudaGetLastError();
