@@ -341,11 +341,12 @@ FUSED_SHAPES = [
 
 @pytest.mark.parametrize("shape", FUSED_SHAPES, ids=lambda s: f"D{s[0]}-de{s[1]}-E{s[2]}-k{s[3]}-{s[4]}")
 def test_fused_matches_multikernel(dev, orc, shape):
-    """The persistent kernel and the multi-kernel path give identical bits
+    """The persistent kernels and the multi-kernel path give identical bits
     over many consecutive tokens (the grid barrier, the stage ring and the
-    double-buffered routing are reused token after token), both equal the
-    oracle, and the persistent kernel really runs as one launch for the
-    whole token batch where it applies."""
+    double-buffered routing are reused token after token), the single-token
+    kernel too over one-token launches, all equal the oracle, and the
+    persistent kernel really runs as one launch for the whole token batch
+    where it applies."""
     from tierlm_b200 import synth
     D, de, E, k, dts, fused_expected = shape
     rng = np.random.default_rng(D + de + E + k + sum(dts))
@@ -371,6 +372,15 @@ def test_fused_matches_multikernel(dev, orc, shape):
     assert (launches["static"] == 1) == fused_expected, launches
     assert same_bits(outs["stream"], outs[False]).all()
     assert same_bits(outs["static"], outs[False]).all()
+    # one token per launch through the single-token kernel (where its
+    # shared memory suffices), twice over: the same bits
+    ctx.set_fused("single")
+    o1 = torch.zeros((T, D), device=dev)
+    for rep in range(2):
+        for t in range(T):
+            ctx.expert_ffn(0, xd[t], ld[t], o1[t])
+    ctx.check()
+    assert same_bits(o1.cpu().numpy(), outs[False]).all()
     outs[True] = outs["stream"]
     orc.set_expf_mode(1)
     try:
@@ -397,6 +407,38 @@ BATCH_SHAPES = [
     (1024, 512, 6, 3, (13, 13, 13), 0, 64, True),     # 32-token passes, Q5_K
     (1024, 768, 8, 2, (13, 13, 15), 0, 4, False),     # Q8_K down: per-token fallback
 ]
+
+
+def test_expert_ffn_batch_prefill_config2(dev):
+    """Prefill at the config-2 layer shape with every expert present: 2048
+    tokens through 128 experts (top-8, gate/up Q4_K, down Q6_K; ~128 tokens
+    per expert, the tensor-core kernels' 32-token passes) in one batched
+    call; sampled rows (ffn, ids, weights) equal the single-token path bit
+    for bit."""
+    from tierlm_b200 import synth
+    D, de, E, k, T = 2048, 768, 128, 8, 2048
+    rng = np.random.default_rng(2048128)
+    experts = [synth.rand_expert(rng, D, de, (12, 12, 14)) for _ in range(E)]
+    ctx = build_ctx(experts, D, de, E, k, 0)
+    ctx.set_batch_kernels("mma")
+    x = torch.from_numpy(rng.standard_normal((T, D)).astype(np.float32)).to(dev)
+    lg = torch.from_numpy(rng.standard_normal((T, E)).astype(np.float32)).to(dev)
+    out = torch.zeros((T, D), device=dev)
+    ids = torch.zeros((T, k), dtype=torch.int32, device=dev)
+    w = torch.zeros((T, k), device=dev)
+    ctx.expert_ffn_batch(0, x, lg, out, ids, w)
+    ctx.check()
+    hits = torch.zeros(E, dtype=torch.int64, device=dev).scatter_add_(0, ids.flatten().long(),
+                                                                     torch.ones(T * k, dtype=torch.int64, device=dev))
+    assert int(hits.min()) >= 24                     # every expert runs the wide (prefill) passes
+    out, ids, w = out.cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy()
+    for t in list(range(0, T, 97)) + [T - 1]:
+        one, i1, w1 = np.zeros(D, np.float32), np.zeros(k, np.int32), np.zeros(k, np.float32)
+        ctx.expert_ffn(0, x[t].cpu().numpy(), lg[t].cpu().numpy(), one, i1, w1)
+        assert np.array_equal(i1, ids[t]) and same_bits(w1, w[t]).all(), t
+        bad = np.flatnonzero(~same_bits(one, out[t]))
+        assert bad.size == 0, (t, bad[:4], out[t][bad[:4]], one[bad[:4]])
+    ctx.close()
 
 
 @pytest.mark.parametrize("shape", BATCH_SHAPES,

@@ -1378,6 +1378,8 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     cudaMemset(f.bar, 0, BAR_BYTES);
     if (cudaMalloc(&f.sbar, 64) != cudaSuccess) return set_error(TLMG_ENOMEM, "stream kernel grid words");
     cudaMemset(f.sbar, 0, 64);
+    if (cudaMalloc(&f.obar, 16) != cudaSuccess) return set_error(TLMG_ENOMEM, "single-token kernel grid words");
+    cudaMemset(f.obar, 0, 16);
     f.sepoch = 0;
     f.rounds = 0;
     f.launches = 0;
@@ -1441,6 +1443,7 @@ void fused_release(FusedScratch &f) {
     free_tokens(f);
     if (f.bar) cudaFree(f.bar);
     if (f.sbar) cudaFree(f.sbar);
+    if (f.obar) cudaFree(f.obar);
     for (auto &kv : f.splans) delete kv.second;
     if (f.err_host) cudaFreeHost(f.err_host);
     for (auto &kv : f.plans) cudaFree(kv.second);
@@ -1615,6 +1618,327 @@ static int launch_stream(FusedScratch &f, const StreamPlanHost &sp, const FusedA
     return TLMG_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Single-token kernel (k_ffn_one): one token, one launch, latency first.
+// Every CTA routes the token itself (the same warp_route as above), then
+// one thread issues bulk copies of ALL of the CTA's weights at once: its
+// share of the (rank, row) gate/up units (both matrices) and, for its
+// output rows [i0, i1), the down rows of all k experts (~170 KB at the
+// Qwen3-30B-A3B layer shape), while the warps quantise x into shared
+// memory. Gate/up units write SiLU(g) * u to hbuf; one grid barrier (a
+// self-resetting count + generation pair, so that a graph can replay the
+// launch); each CTA then quantises the k h rows itself and computes its
+// output rows for every expert, so the rank-ordered combine and h += ffn
+// stay inside the CTA. Same operations, in the same order, as the
+// multi-kernel path (k_ffn_gateup / k_quant_h / k_ffn_down): bit-identical.
+namespace one {
+constexpr int NT = 512;                 // 16 warps
+constexpr int NW = NT / 32;
+}
+
+// Dot of one row held in shared memory against a Q8_K vector (shared or
+// global), every lane returns it: the k_matvec_qs order.
+template <int DT>
+__device__ __forceinline__ float row_dot_s(const uint8_t *row, const uint8_t *act, int nb, BlockPart *part,
+                                           int lane) {
+    constexpr int BB = dt_block_bytes(DT), ABB = act_block_bytes(act_kind_for(DT));
+    const int g = lane >> 3, j = lane & 7;
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < nb; c0 += FCHUNK) {
+        const int nc = min(FCHUNK, nb - c0);
+        for (int p0 = 0; p0 < nc; p0 += 4) {
+            const int p = p0 + g;
+            const bool valid = p < nc;
+            int is = 0, ms = 0;
+            const uint8_t *blk = row + (size_t)(c0 + p) * BB;
+            const uint8_t *ab = act + (size_t)(c0 + p) * ABB;
+            if (valid) block_part<SLoad>(DT, blk, ab, j, is, ms);
+            group8_sum(is, ms);
+            if (valid && j == 0) {
+                float dA, dM;
+                block_scales<SLoad>(DT, blk, ab, dA, dM);
+                part[p] = BlockPart{ is, ms, dA, dM };
+            }
+        }
+        __syncwarp();
+        if (lane == 0)
+            for (int p = 0; p < nc; p++) acc = chain_step(DT, acc, part[p].dA, part[p].dM, part[p].is, part[p].ms);
+        __syncwarp();
+    }
+    return __shfl_sync(0xFFFFFFFFu, acc, 0);
+}
+
+// The CTA's shared-memory plan, the same on host and device.
+struct OneLayout {
+    uint32_t gu, dn, xq, hq, hraw, eo, part, ids, w, sl, rs, bars, total;
+};
+__host__ __device__ inline uint32_t al16(uint32_t v) { return (v + 15u) & ~15u; }
+// worst case over CTAs: U units of gate/up (at most U / de + 2 experts), R output rows
+__host__ __device__ inline OneLayout one_layout(int D, int de, int k, int G, int BG, int BD) {
+    OneLayout L{};
+    const int64_t P = (int64_t)k * de;
+    const uint32_t U = (uint32_t)((P + G - 1) / G), R = (uint32_t)((D + G - 1) / G);
+    const uint32_t rbg = (uint32_t)(D / 256 * BG), rbd = (uint32_t)(de / 256 * BD);
+    const uint32_t nr = U / (uint32_t)de + 2;
+    uint32_t o = 0;
+    L.gu = o; o += al16(2 * U * rbg + nr * 2 * 32);
+    L.dn = o; o += al16((uint32_t)k * (R * rbd + 32));
+    L.xq = o; o += al16((uint32_t)(D / 256) * 292);
+    L.hq = o; o += al16((uint32_t)k * (de / 256) * 292);
+    L.hraw = o; o += 256 * 4 * one::NW;
+    L.eo = o; o += al16(R * (uint32_t)k * 4);
+    L.part = o; o += al16((uint32_t)sizeof(BlockPart) * FCHUNK * one::NW);
+    L.ids = o; o += 4 * MAXK;
+    L.w = o; o += 4 * MAXK;
+    L.sl = o; o += al16((uint32_t)sizeof(Slot) * MAXK);
+    L.rs = o; o += 4 * RT_SCRATCH;
+    L.bars = o = (o + 7u) & ~7u; o += 16;
+    L.total = al16(o);
+    return L;
+}
+
+// Grid barrier of one launch: count + generation (gb[0], gb[1]); the last
+// CTA resets the count before it advances the generation. All CTAs are
+// resident (cooperative launch). false: gave up after BARRIER_NS.
+__device__ __forceinline__ bool one_grid_barrier(uint32_t *gb) {
+    const uint32_t g0 = ld_acquire(gb + 1);
+    __threadfence();
+    if (atomicAdd(gb, 1u) == gridDim.x - 1) {
+        atomicExch(gb, 0u);
+        __threadfence();
+        atomicAdd(gb + 1, 1u);
+        return true;
+    }
+    if (ld_acquire(gb + 1) != g0) return true;
+    const uint64_t t0 = now_ns();
+    while (ld_acquire(gb + 1) == g0) {
+        if (now_ns() - t0 > BARRIER_NS) return false;
+        __nanosleep(64);
+    }
+    return true;
+}
+
+template <int DGU, int DDN>
+__global__ void __launch_bounds__(one::NT, 1)
+    k_ffn_one(const FusedArgs a, uint32_t *bar, uint32_t *err, uint32_t *gb) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int BG = dt_block_bytes(DGU), BD = dt_block_bytes(DDN);
+    const int D = a.D, de = a.de, k = a.k, E = a.E, G = gridDim.x, c = blockIdx.x;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int nbx = D / 256, nbh = de / 256;
+    const uint32_t rbg = (uint32_t)nbx * BG, rbd = (uint32_t)nbh * BD;
+    const OneLayout L = one_layout(D, de, k, G, BG, BD);
+    const int64_t P = (int64_t)k * de;
+    const int u0 = range_lo(P, c, G), u1 = range_lo(P, c + 1, G);
+    const int i0 = range_lo(D, c, G), i1 = range_lo(D, c + 1, G);
+    uint8_t *gu_s = smem + L.gu, *dn_s = smem + L.dn, *xq_s = smem + L.xq, *hq_s = smem + L.hq;
+    float *hraw = reinterpret_cast<float *>(smem + L.hraw) + 256 * warp;
+    float *eo_s = reinterpret_cast<float *>(smem + L.eo);
+    BlockPart *part = reinterpret_cast<BlockPart *>(smem + L.part) + FCHUNK * warp;
+    int32_t *ids = reinterpret_cast<int32_t *>(smem + L.ids);
+    float *wr = reinterpret_cast<float *>(smem + L.w);
+    Slot *sl = reinterpret_cast<Slot *>(smem + L.sl);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bars);   // [0] gate/up in, [1] down in
+    __shared__ int fail_s;
+    const int layer = a.layer0 % a.n_layers;
+    uint64_t *tr = trace_row(a);   // [0] start [1] routed [2] copies issued [3] x quantised [4] gate/up in
+                                   // [5] gate/up done [6] barrier passed [7] h quantised [8] down in [9] done
+    if (tr && t == 0) {
+        for (int q = 1; q < FUSED_TRACE_POINTS; q++) tr[q] = 0;
+        tr[0] = now_ns();
+    }
+
+    if (t == 0) {
+        fail_s = ld_acquire(&bar[2]) != 0;   // an earlier launch failed: do nothing until reset
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        warp_route(a.router, a.logits, a.mask_all ? a.mask_all + (size_t)layer * E : nullptr,
+                   a.bias_all ? a.bias_all + (size_t)layer * E : nullptr, E, k, a.routed_scale,
+                   reinterpret_cast<uint32_t *>(smem + L.rs), ids, wr, lane);
+        __syncwarp();
+        if (lane < k) {
+            sl[lane] = a.slots_all[(size_t)layer * E + ids[lane]];
+            if (c == 0 && a.ids_out) a.ids_out[lane] = ids[lane];
+            if (c == 0 && a.w_out) a.w_out[lane] = wr[lane];
+        }
+        if (tr && lane == 0) tr[1] = now_ns();
+    }
+    __syncthreads();
+    if (fail_s) {
+        if (t == 0) raise_error(err, bar, FUSED_ERR_BARRIER);
+        return;   // every CTA reads the same sticky word before the grid barrier
+    }
+    // ---- every weight byte of the CTA in flight at once
+    if (t == 0) {
+        uint32_t off = 0, tx = 0;
+        for (int pass = 0; pass < 2; pass++) {   // pass 0 counts the bytes, pass 1 issues
+            if (pass == 1) mbar_expect_tx(&bars[0], tx);
+            off = 0;
+            for (int r = u0 / de; r * de < u1; r++) {
+                const int ja = max(u0, r * de) - r * de, jb = min(u1, (r + 1) * de) - r * de;
+                if (jb <= ja) continue;
+                for (int m = 0; m < 2; m++) {
+                    const uintptr_t src = reinterpret_cast<uintptr_t>(sl[r].m[m]) + (uintptr_t)ja * rbg;
+                    const uintptr_t lo = src & ~(uintptr_t)15, hi = (src + (uintptr_t)(jb - ja) * rbg + 15) & ~(uintptr_t)15;
+                    if (pass == 1) bulk_g2s(gu_s + off, reinterpret_cast<const void *>(lo), (uint32_t)(hi - lo), &bars[0]);
+                    else tx += (uint32_t)(hi - lo);
+                    off += (uint32_t)(hi - lo);
+                }
+            }
+        }
+        tx = 0;
+        for (int pass = 0; pass < 2; pass++) {
+            if (pass == 1) mbar_expect_tx(&bars[1], tx);
+            off = 0;
+            for (int r = 0; r < k && i1 > i0; r++) {
+                const uintptr_t src = reinterpret_cast<uintptr_t>(sl[r].m[2]) + (uintptr_t)i0 * rbd;
+                const uintptr_t lo = src & ~(uintptr_t)15, hi = (src + (uintptr_t)(i1 - i0) * rbd + 15) & ~(uintptr_t)15;
+                if (pass == 1) bulk_g2s(dn_s + off, reinterpret_cast<const void *>(lo), (uint32_t)(hi - lo), &bars[1]);
+                else tx += (uint32_t)(hi - lo);
+                off += (uint32_t)(hi - lo);
+            }
+        }
+        if (tr) tr[2] = now_ns();
+    }
+    // ---- x as Q8_K (k_quant_q8k's blocks)
+    for (int b = warp; b < nbx; b += one::NW) warp_quant_q8k(a.x + 256 * b, 256, xq_s + 292 * b, lane);
+    __syncthreads();
+    if (tr && t == 0) tr[3] = now_ns();
+    bool ok = mbar_wait(&bars[0], 0);
+    if (tr && t == 0) tr[4] = now_ns();
+    // ---- gate/up units: SiLU(gate . x) * (up . x) -> hbuf
+    if (ok) {
+        uint32_t base = 0;
+        for (int r = u0 / de; r * de < u1; r++) {
+            const int ja = max(u0, r * de) - r * de, jb = min(u1, (r + 1) * de) - r * de;
+            if (jb <= ja) continue;
+            uint32_t gofs[2];
+            for (int m = 0; m < 2; m++) {
+                const uintptr_t src = reinterpret_cast<uintptr_t>(sl[r].m[m]) + (uintptr_t)ja * rbg;
+                const uintptr_t lo = src & ~(uintptr_t)15, hi = (src + (uintptr_t)(jb - ja) * rbg + 15) & ~(uintptr_t)15;
+                gofs[m] = base + (uint32_t)(src - lo);
+                base += (uint32_t)(hi - lo);
+            }
+            for (int j = ja + warp; j < jb; j += one::NW) {
+                const float gv = row_dot_s<DGU>(gu_s + gofs[0] + (size_t)(j - ja) * rbg, xq_s, nbx, part, lane);
+                const float uv = row_dot_s<DGU>(gu_s + gofs[1] + (size_t)(j - ja) * rbg, xq_s, nbx, part, lane);
+                if (lane == 0) a.hbuf[(size_t)r * de + j] = __fmul_rn(silu_f(gv), uv);
+            }
+        }
+    }
+    __syncthreads();
+    if (t == 0) {
+        if (tr) tr[5] = now_ns();
+        if (!ok) raise_error(err, bar, FUSED_ERR_COPY);
+        if (!one_grid_barrier(gb)) {
+            raise_error(err, bar, FUSED_ERR_BARRIER);
+            ok = false;
+        }
+        fail_s = !ok;
+        if (tr) tr[6] = now_ns();
+    }
+    __syncthreads();
+    if (fail_s) {
+        if (t == 0) mbar_wait(&bars[1], 0);   // no copy may land after the CTA exits
+        return;
+    }
+    // ---- the k h rows as Q8_K (k_quant_h's blocks), read from L2
+    for (int q = warp; q < k * nbh; q += one::NW) {
+        const int r = q / nbh, b = q - r * nbh;
+        const float *src = a.hbuf + (size_t)r * de + 256 * b;
+        for (int e = lane; e < 256; e += 32) hraw[e] = __ldcg(src + e);
+        __syncwarp();
+        warp_quant_q8k(hraw, 256, hq_s + 292 * (size_t)q, lane);
+        __syncwarp();
+    }
+    __syncthreads();
+    if (tr && t == 0) tr[7] = now_ns();
+    ok = mbar_wait(&bars[1], 0);
+    if (tr && t == 0) tr[8] = now_ns();
+    if (!ok) {
+        if (t == 0) raise_error(err, bar, FUSED_ERR_COPY);
+        return;
+    }
+    // ---- down rows: c_r = w_r * (down_r[i] . h_r), then the combine
+    uint32_t dofs[MAXK];
+    {
+        uint32_t base = 0;
+        for (int r = 0; r < k; r++) {
+            const uintptr_t src = reinterpret_cast<uintptr_t>(sl[r].m[2]) + (uintptr_t)i0 * rbd;
+            const uintptr_t lo = src & ~(uintptr_t)15, hi = (src + (uintptr_t)(i1 - i0) * rbd + 15) & ~(uintptr_t)15;
+            dofs[r] = base + (uint32_t)(src - lo);
+            base += (uint32_t)(hi - lo);
+        }
+    }
+    const int nrow = i1 - i0;
+    for (int q = warp; q < nrow * k; q += one::NW) {
+        const int ii = q / k, r = q - ii * k;
+        const float e = row_dot_s<DDN>(dn_s + dofs[r] + (size_t)ii * rbd, hq_s + 292 * (size_t)r * nbh, nbh, part, lane);
+        if (lane == 0) eo_s[q] = __fmul_rn(wr[r], e);
+    }
+    __syncthreads();
+    for (int ii = t; ii < nrow; ii += one::NT) {
+        const int i = i0 + ii;
+        float acc = 0.0f;
+        for (int r = 0; r < k; r++) acc = __fadd_rn(acc, eo_s[ii * k + r]);
+        if (a.s_out) acc = __fadd_rn(acc, __fmul_rn(*a.sgate, a.s_out[i]));
+        a.ffn[i] = acc;
+        if (a.h) a.h[i] = __fadd_rn(a.h[i], acc);
+    }
+    if (tr && t == 0) tr[9] = now_ns();
+}
+
+using OneFn = void (*)(const FusedArgs, uint32_t *, uint32_t *, uint32_t *);
+static OneFn pick_one(int dgu, int ddn) {
+#define TLMG_O(G, DN) \
+    if (dgu == G && ddn == DN) return k_ffn_one<G, DN>;
+    TLMG_O(DT_Q4_K, DT_Q4_K) TLMG_O(DT_Q4_K, DT_Q5_K) TLMG_O(DT_Q4_K, DT_Q6_K)
+    TLMG_O(DT_Q5_K, DT_Q4_K) TLMG_O(DT_Q5_K, DT_Q5_K) TLMG_O(DT_Q5_K, DT_Q6_K)
+    TLMG_O(DT_Q6_K, DT_Q4_K) TLMG_O(DT_Q6_K, DT_Q5_K) TLMG_O(DT_Q6_K, DT_Q6_K)
+#undef TLMG_O
+    return nullptr;
+}
+
+// 1: launched; 0: this launch is not the single-token kernel's (the caller
+// uses another); < 0: error.
+static int launch_one(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
+    if (!f.single || a.n_tok != 1 || a.k > MAXK || !f.obar) return 0;
+    OneFn fn = pick_one(a.dt_gu, a.dt_dn);
+    if (!fn) return 0;
+    const OneLayout L = one_layout(a.D, a.de, a.k, f.nsm, dt_block_bytes(a.dt_gu), dt_block_bytes(a.dt_dn));
+    if ((size_t)L.total + 1024 > f.smem_limit) return 0;
+    static thread_local std::vector<const void *> opted;   // instances opted in to the large shared memory
+    if (std::find(opted.begin(), opted.end(), (const void *)fn) == opted.end()) {
+        if (cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)f.smem_limit - 1024) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        opted.push_back((const void *)fn);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)f.nsm);
+    cfg.blockDim = dim3(one::NT);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int rc = reserve_tokens(f, 1);
+    if (rc) return rc;
+    FusedArgs la = a;
+    la.hbuf = f.hbuf;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, la, f.bar, f.err_dev, f.obar);
+    count_launch();
+    if (e != cudaSuccess) return cuda_fail(e, "single-token expert FFN launch");
+    return 1;
+}
+
 int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
     if (f.mode == FUSED_STREAM) {
         if (const StreamPlanHost *sp = stream_plan(f, a.dt_gu, a.dt_dn)) {
@@ -1622,6 +1946,11 @@ int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
             if (rc) return rc;
             return launch_stream(f, *sp, a, st);
         }
+    }
+    {
+        const int r1 = launch_one(f, a, st);
+        if (r1 < 0) return r1;
+        if (r1 == 1) return TLMG_OK;
     }
     KernelFn kf = pick_kernel(a.dt_gu, a.dt_dn, a.D, a.de, a.k);
     if (!kf) return set_error(TLMG_EUNSUP, "fused kernel: no instance for dtypes %d/%d", a.dt_gu, a.dt_dn);
@@ -1669,6 +1998,7 @@ uint32_t fused_take_error(FusedScratch &f) {
         *(volatile uint32_t *)f.err_host = 0;
         cudaMemset(f.bar, 0, BAR_BYTES);
         cudaMemset(f.sbar, 0, 64);
+        if (f.obar) cudaMemset(f.obar, 0, 16);
         if (f.ocnt) cudaMemset(f.ocnt, 0, (size_t)f.tok_cap * (f.D / 64) * 4);
         if (f.hcnt) cudaMemset(f.hcnt, 0, (size_t)f.tok_cap * f.k * 4);
         f.rounds = 0;

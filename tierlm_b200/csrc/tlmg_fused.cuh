@@ -71,6 +71,10 @@ struct FusedScratch {
     // a capture or a replay restarts them too (bar_stale).
     bool graph_mode = false;
     bool bar_stale = false;
+    // one-token launches by the single-token kernel (k_ffn_one,
+    // tlmg_set_fused mode 4); grid words [2] count, generation
+    bool single = false;
+    uint32_t *obar = nullptr;
     // per-token global scratch of a launch, for up to tok_cap tokens
     int tok_cap = 0;
     uint8_t *xq = nullptr;         // [tok_cap][quantised x]

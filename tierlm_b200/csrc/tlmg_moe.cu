@@ -762,10 +762,10 @@ int tlmg_profile_read(tlmg_ctx *c, int cls, double *ms, int64_t *launches, int64
 int tlmg_set_fused(tlmg_ctx *c, int on) {
     if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
-    if (on < 0 || on > 3) return set_error(TLMG_EINVAL, "set_fused: mode %d", on);
+    if (on < 0 || on > 4) return set_error(TLMG_EINVAL, "set_fused: mode %d", on);
     c->fused_on = on != 0;
-    if (on == 2) c->fused.mode = FUSED_STATIC;
-    else if (on) c->fused.mode = FUSED_STREAM;
+    c->fused.mode = on == 3 ? FUSED_STREAM : FUSED_STATIC;
+    c->fused.single = on == 4;
     return c->fused.enabled ? TLMG_OK : (on ? set_error(TLMG_EUNSUP, "persistent kernel unavailable on this device") : TLMG_OK);
 }
 
