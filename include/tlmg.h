@@ -425,12 +425,12 @@ int tlmg_moe_layer_ex(tlmg_ctx *ctx, int layer, float *h, int32_t *ids, float *w
 int tlmg_set_stream(tlmg_ctx *ctx, void *stream);
 
 /* Choose the expert-FFN kernels: on = 1 (default) or 2 the static
- * persistent kernel wherever it can serve the layer, 3 its stream variant,
- * 4 the static kernel with one-token launches served by the single-token
- * kernel (every CTA fetches all of its weights at once), 0 the
- * multi-kernel path (router, gate/up, re-quantise, down launches). All
- * give identical bits. TLMG_EUNSUP when on != 0 and the device cannot run
- * the persistent kernels (the multi-kernel path stays in use). */
+ * persistent kernel wherever it can serve the layer, 4 the same with
+ * one-token launches served by the single-token kernel (every CTA fetches
+ * all of its weights at once), 0 the multi-kernel path (router, gate/up,
+ * re-quantise, down launches); 3 is not a mode (TLMG_EINVAL). All give
+ * identical bits. TLMG_EUNSUP when on != 0 and the device cannot run the
+ * persistent kernels (the multi-kernel path stays in use). */
 int tlmg_set_fused(tlmg_ctx *ctx, int on);
 /* Expert kernels of tlmg_expert_ffn_batch and the expert-parallel owner:
  * mode 2 (default) the tensor-core kernels (tcgen05.mma kind::i8, one int32

@@ -79,7 +79,7 @@ def test_matvec_random_vs_oracle(dev, orc, dt):
     """A 3000-row matrix of every dtype at a few widths, every row bit-exact."""
     from tierlm_b200 import quant, synth
     rng = np.random.default_rng(100 + dt)
-    for n in (256, 2048, 768 if dt != 39 else 736):
+    for n in (256, 2048, 768 if dt != 39 else 736, 4352 if dt != 39 else 4320):   # 4352: rows past 48 KB of staging
         rows = 3000
         if dt in (0, 1, 2):
             wf = rng.standard_normal((rows, n)).astype(np.float32)
@@ -357,20 +357,21 @@ def test_fused_matches_multikernel(dev, orc, shape):
     lg = rng.standard_normal((T, E)).astype(np.float32)
     lg[5] = 0.0                                   # all-tie routing row
     outs, launches = {}, {}
-    for fused in ("stream", "static", False):
+    for fused in ("static", False):
         ctx.set_fused(fused)
         xd, ld = torch.from_numpy(x).to(dev), torch.from_numpy(lg).to(dev)
         od = torch.zeros((T, D), device=dev)
         n0 = ctx.launches
         for rep in range(2):                      # twice: queue heads, epochs and counts reset between launches
             ctx.expert_ffn_many(0, xd, ld, od)
-        ctx.check()
+        try:
+            ctx.check()
+        except RuntimeError as ex:
+            raise AssertionError(f"kernel mode {fused!r}: {ex}") from ex
         launches[fused] = (ctx.launches - n0) // 2
         outs[fused] = od.cpu().numpy()
     # a persistent kernel serves all T tokens in one launch
-    assert (launches["stream"] == 1) == fused_expected, launches
     assert (launches["static"] == 1) == fused_expected, launches
-    assert same_bits(outs["stream"], outs[False]).all()
     assert same_bits(outs["static"], outs[False]).all()
     # one token per launch through the single-token kernel (where its
     # shared memory suffices), twice over: the same bits
@@ -379,9 +380,12 @@ def test_fused_matches_multikernel(dev, orc, shape):
     for rep in range(2):
         for t in range(T):
             ctx.expert_ffn(0, xd[t], ld[t], o1[t])
-    ctx.check()
+    try:
+        ctx.check()
+    except RuntimeError as ex:
+        raise AssertionError(f"kernel mode 'single': {ex}") from ex
     assert same_bits(o1.cpu().numpy(), outs[False]).all()
-    outs[True] = outs["stream"]
+    outs[True] = outs["static"]
     orc.set_expf_mode(1)
     try:
         geom = dict(d_model=D, d_expert=de, n_experts=E, top_k=k, router=0)

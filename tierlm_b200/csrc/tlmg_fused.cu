@@ -716,618 +716,6 @@ k_fused_ffn(const __grid_constant__ FusedArgs a, uint32_t *__restrict__ bar, uin
 
 
 // ---------------------------------------------------------------------------
-// The stream kernel: the same work as k_fused_ffn, handed out dynamically.
-//
-// Every layer-token's work is a fixed list of chunks, in expert-rank order:
-// nceA gate/up chunks per expert (perA rows of gate and the same rows of up,
-// one stage) and nceB down chunks per expert (perB output rows). Two global
-// queues enumerate (token, chunk) in token order, one for gate/up and one
-// for down; every CTA's two producer warps take the next index with one
-// atomicAdd each time a stage of theirs frees, so faster SMs simply take
-// more chunks and no CTA waits for the slowest one. There is no grid-wide
-// barrier per token: a down chunk of (token, expert r) needs only that
-// expert's h, and the CTA whose gate/up chunk completes h_r quantises it
-// once into global memory and publishes a per-(token, expert) flag; the
-// down producer copies the quantised h into the stage next to the weight
-// rows once the flag is up. The queues hand out gate/up chunks of token t+1
-// while the down chunks of token t run, so h_r is normally published long
-// before its down chunks are consumed.
-//
-//   warps [0, 7)     gate/up consumers      warp 15  gate/up producer
-//   warps [7, 15)    down consumers         warp 16  down producer
-//   warp 17          gate/up duty: row counts per (token, expert), h
-//                    quantisation, flag
-//   warp 18          down duty: 64-row output group counts, rank-ordered
-//                    combine of completed groups
-//   warp 19          routes the CTA's share of the launch's tokens at start
-//
-// Launch start: every CTA quantises its share of the inputs x and routes its
-// share of the tokens (ids, weights and slot addresses per (token, rank) into
-// global memory), then one grid-wide count; the producers wait for it.
-// Numerics are those of k_fused_ffn: the same unit partials, the same chains
-// in block order, the combine in ascending rank.
-namespace sk {
-#ifndef TLMG_SK_NAW
-#define TLMG_SK_NAW 7
-#endif
-constexpr int NAW = TLMG_SK_NAW, NCW = 15;
-constexpr int W_GP = NCW, W_DP = NCW + 1, W_GD = NCW + 2, W_DD = NCW + 3, W_RT = NCW + 4;
-constexpr int NTHREADS = 32 * (NCW + 5);
-constexpr int NQ = 16;                 // duty-ring entries per group
-// Rows per chunk at most (the chain threads of a chunk stay in the group's
-// last warp) and the stage bytes a chunk's copies may take: per matrix of a
-// gate/up stage ROWS_A rows of 1152 B (Q4_K, D = 2048) plus alignment
-// slack, the weights of a down stage ROWS_B rows of 630 B (Q6_K, de = 768).
-#ifndef TLMG_SK_ROWS_A
-#define TLMG_SK_ROWS_A 22
-#endif
-#ifndef TLMG_SK_NSA
-#define TLMG_SK_NSA 2
-#endif
-constexpr int ROWS_A = TLMG_SK_ROWS_A, ROWS_B = 32;
-constexpr uint32_t SEG_A = (uint32_t)(ROWS_A * 1152 + 32), SEG_B = 32 * 630 + 32;
-constexpr int NSA = TLMG_SK_NSA;
-constexpr int MAXS = 10;
-
-struct SDesc {                          // what a stage holds (producer -> consumers)
-    int32_t tok, r, row0, nrows;
-    uint32_t roff, pad0, pad1, pad2;
-};
-struct QEnt {                           // a consumed chunk (consumers -> duty warp)
-    int32_t tok, r, row0, nrows;
-};
-}  // namespace sk
-
-// Launch geometry of the stream kernel (host-built per dtype signature).
-struct StreamGeom {
-    int rowsA, nceA, perA, rowsB, nceB, perB, nGU, nDN, nsA, nsB;
-    uint32_t segA, segB;                // bytes of one matrix's rows in a gate/up stage, of the rows in a down stage
-    uint32_t strideA, strideB;          // stage strides
-    uint32_t offA, offB, full, empty, sdesc, qA, qB, fqA, eqA, fqB, eqB, partA, partB, hq, rscr, rt, total;
-};
-struct StreamArgs {
-    StreamGeom g;
-    uint32_t *hcnt;                     // [n_tok][k] h rows written (zeroed at launch start)
-    Slot *tslot;                        // [n_tok][k] slots of the routed experts
-    float *wg;                          // [n_tok][k] routing weights
-    uint32_t epoch;                     // launch number (>= 1)
-};
-
-__host__ __device__ inline StreamGeom stream_layout(StreamGeom g, int D, int de) {
-    const uint32_t qvx = qv_bytes(D / 256), qvd = qv_bytes(de / 256);
-    uint32_t o = 0;
-    g.strideA = 2u * g.segA + qvx;
-    g.strideB = g.segB + 4u * (uint32_t)de;   // the rows and the expert's raw h (f32)
-    g.offA = o; o += (uint32_t)g.nsA * g.strideA;
-    g.offB = o; o += (uint32_t)g.nsB * g.strideB;
-    const int ns = g.nsA + g.nsB;
-    g.full = o = up16(o); o += 8u * ns;
-    g.empty = o; o += 8u * ns;
-    g.fqA = o; o += 8u * sk::NQ;
-    g.eqA = o; o += 8u * sk::NQ;
-    g.fqB = o; o += 8u * sk::NQ;
-    g.eqB = o; o += 8u * sk::NQ;
-    g.sdesc = o = up16(o); o += (uint32_t)sizeof(sk::SDesc) * ns;
-    g.qA = o; o += (uint32_t)sizeof(sk::QEnt) * sk::NQ;
-    g.qB = o; o += (uint32_t)sizeof(sk::QEnt) * sk::NQ;
-    // unit partials, double-buffered: gate/up [2][2 matrices][rowsA][nbx + 1], down [2][rowsB][2 nbd + 1]
-    g.partA = o = up16(o); o += 16u * 2u * 2u * (uint32_t)g.rowsA * (uint32_t)(D / 256 + 1);
-    g.partB = o = up16(o); o += 16u * 2u * (uint32_t)g.rowsB * (uint32_t)(2 * (de / 256) + 1);
-    g.hq = o = up16(o); o += qvd;            // the down group's quantised h (one chunk at a time)
-    g.rscr = o = up16(o); o += 4u * (uint32_t)RT_SCRATCH;
-    g.rt = o; o += 8u * MAXK;            // one token's ids and weights
-    g.total = up16(o) + 64;
-    return g;
-}
-
-// Grid words of the stream kernel (a 64-byte device block): [2] sticky
-// error, 64-bit words at +4 the launch-start count, +6 the gate/up queue
-// head, +8 the down queue head, u32 at +10 the CTAs that have finished.
-__device__ __forceinline__ unsigned long long *sk_word(uint32_t *bar, int i) {
-    return reinterpret_cast<unsigned long long *>(bar + 4 + 2 * i);
-}
-// Non-blocking test of an mbarrier phase.
-__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Atomic add with release (the rows this CTA wrote before it, observed
-// through the CTA's own synchronisation) and acquire (the rows other CTAs
-// wrote before their adds) at gpu scope; returns the old value.
-__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t *p, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-// True in every thread of named barrier `id` (count threads) iff p is true in
-// all of them (a barrier: every thread of the group must call it).
-__device__ __forceinline__ bool group_all(bool p, int id, int count) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred pi, po;\n\t"
-        "setp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.and.pred po, %2, %3, pi;\n\t"
-        "selp.u32 %0, 1, 0, po;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)p), "r"(id), "r"(count)
-        : "memory");
-    return r != 0;
-}
-__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_add(uint32_t *p, uint32_t v) {
-    asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-__device__ __forceinline__ void st_release(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// Wait until the counter *p reaches v (relaxed reads), for at most BARRIER_NS.
-__device__ __forceinline__ bool count_wait(const uint32_t *p, uint32_t v) {
-    if (ld_relaxed(p) >= v) return true;
-    const uint64_t t0 = now_ns();
-    while (ld_relaxed(p) < v) {
-        if (now_ns() - t0 > BARRIER_NS) return false;
-        __nanosleep(64);
-    }
-    return true;
-}
-
-template <int DGU, int DDN>
-__global__ void __launch_bounds__(sk::NTHREADS, 1)
-k_stream_ffn(const __grid_constant__ FusedArgs a, const __grid_constant__ StreamArgs sa, uint32_t *__restrict__ bar,
-             uint32_t *__restrict__ err) {
-    constexpr int NAW = sk::NAW, NCW = sk::NCW, W_GP = sk::W_GP, W_DP = sk::W_DP, W_GD = sk::W_GD, W_DD = sk::W_DD,
-                  W_RT = sk::W_RT, NQ = sk::NQ;
-    const uint32_t SEG_A = sa.g.segA, SEG_B = sa.g.segB;
-    using sk::QEnt;
-    using sk::SDesc;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const StreamGeom &G = sa.g;
-    const int D = a.D, de = a.de, k = a.k, E = a.E, n = a.n_tok;
-    const int nbx = D / 256, nbd = de / 256;
-    const uint32_t qvx = qv_bytes(nbx), qvd = qv_bytes(nbd);
-    const int64_t P = (int64_t)k * de, Q = (int64_t)k * D;
-    const int nsA = G.nsA, nsB = G.nsB;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + G.full);
-    uint64_t *empty = reinterpret_cast<uint64_t *>(smem + G.empty);
-    SDesc *sdesc = reinterpret_cast<SDesc *>(smem + G.sdesc);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = threadIdx.x;
-    uint64_t *tr = trace_row(a);
-    if (tr && t == 0) {
-        for (int i = 1; i < FUSED_TRACE_POINTS; i++) tr[i] = 0;
-        tr[0] = now_ns();
-    }
-    if (t == 0) {
-        for (int i = 0; i < nsA + nsB; i++) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-        }
-        for (int i = 0; i < 4 * NQ; i++) mbar_init(reinterpret_cast<uint64_t *>(smem + G.fqA) + i, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    bool stop = ld_acquire(&bar[2]) != 0;   // an earlier launch failed: do nothing until the host resets
-    __syncthreads();
-
-    // ---- launch start: quantise this CTA's share of x (consumer warps) and
-    // route this CTA's share of the tokens (warp W_RT)
-    if (!stop && warp < NCW) {
-        for (int q = blockIdx.x * NCW + warp; q < n * nbx; q += gridDim.x * NCW) {
-            const int tok = q / nbx, b = q - tok * nbx;
-            const float4 *x4 = reinterpret_cast<const float4 *>(a.x + (size_t)tok * D + 256 * b) + 2 * lane;
-            quant_block(__ldg(x4), __ldg(x4 + 1), qvec(a.xq + (size_t)tok * qvx, nbx), b, lane);
-        }
-    } else if (!stop && warp == W_RT) {
-        uint32_t *rscr = reinterpret_cast<uint32_t *>(smem + G.rscr);
-        int32_t *ids = reinterpret_cast<int32_t *>(smem + G.rt);
-        float *wr = reinterpret_cast<float *>(smem + G.rt) + MAXK;
-        for (int tok = blockIdx.x; tok < n; tok += gridDim.x) {
-            const int layer = (a.layer0 + tok) % a.n_layers;
-            warp_route(a.router, a.logits + (size_t)tok * E, a.mask_all ? a.mask_all + (size_t)layer * E : nullptr,
-                       a.bias_all ? a.bias_all + (size_t)layer * E : nullptr, E, k, a.routed_scale, rscr, ids, wr,
-                       lane);
-            if (lane < k) {
-                if (a.ids_out) a.ids_out[(size_t)tok * k + lane] = ids[lane];
-                if (a.w_out) a.w_out[(size_t)tok * k + lane] = wr[lane];
-                sa.wg[(size_t)tok * k + lane] = wr[lane];
-                sa.tslot[(size_t)tok * k + lane] = a.slots_all[(size_t)layer * E + ids[lane]];
-                sa.hcnt[(size_t)tok * k + lane] = 0u;   // before the launch-start count: no row is counted yet
-            }
-            __syncwarp();
-        }
-    }
-    __syncthreads();
-    if (t == 0 && !stop) {
-        __threadfence();
-        atomicAdd(sk_word(bar, 0), 1ull);
-    }
-
-    const bool producer = (warp == W_GP || warp == W_DP) && lane == 0;
-    if (!stop && producer) {
-        // ---- producers: take (token, chunk) indices from the queue and copy
-        // the chunk (gate/up: the gate rows, the same up rows and the token's
-        // quantised x; down: the rows and, once published, the expert's
-        // quantised h) into the next free stage of the ring
-        const bool isA = warp == W_GP;
-        const int nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA, per_tok = isA ? G.nGU : G.nDN;
-        const int nce = isA ? G.nceA : G.nceB, per = isA ? G.perA : G.perB, len = isA ? de : D;
-        const uint32_t rb = isA ? (uint32_t)(nbx * dt_block_bytes(DGU)) : (uint32_t)(nbd * dt_block_bytes(DDN));
-        const int64_t total = (int64_t)n * per_tok;
-        unsigned long long *head = sk_word(bar, isA ? 1 : 2);
-        bool failed = !grid_wait(sk_word(bar, 0), (uint64_t)sa.epoch * gridDim.x);
-        fence_proxy_async();   // x, h and the routes were written by generic stores
-        if (tr && isA) tr[1] = now_ns();
-        uint64_t t_empty = 0, t_flag = 0;   // trace: ns waiting for a free stage / for h flags
-        const int64_t totalA = (int64_t)n * G.nGU;
-        const unsigned long long *gu_head = sk_word(bar, 1);
-        // A two-deep software pipeline: while chunk f is issued, the slot
-        // (and, for down, the h flag) of chunk f + 1 are already being read
-        // and the queue index of chunk f + 2 is being taken, so the atomic's
-        // and the reads' round trips overlap the stage waits instead of
-        // adding up per chunk.
-        struct Next {
-            int64_t g;
-            int tok, r, row0, nrows;
-            const uint8_t *m0, *m1;
-            uint32_t hc;     // down: the expert's h row count as read when the chunk was taken (relaxed)
-        };
-        auto fetch = [&](int64_t gi) -> Next {
-            Next x{ gi, 0, 0, 0, 0, nullptr, nullptr, 0u };
-            if (gi >= total) return x;
-            x.tok = (int)(gi / per_tok);
-            const int c = (int)(gi - (int64_t)x.tok * per_tok);
-            x.r = c / nce;
-            x.row0 = (c - x.r * nce) * per;
-            x.nrows = min(per, len - x.row0);
-            const unsigned long long *sl =
-                reinterpret_cast<const unsigned long long *>(sa.tslot + (size_t)x.tok * k + x.r);
-            if (isA) {
-                x.m0 = reinterpret_cast<const uint8_t *>(__ldcg(sl));
-                x.m1 = reinterpret_cast<const uint8_t *>(__ldcg(sl + 1));
-            } else {
-                x.m0 = reinterpret_cast<const uint8_t *>(__ldcg(sl + 2));
-                x.hc = ld_relaxed(sa.hcnt + (size_t)x.tok * k + x.r);   // in flight with the slot read
-            }
-            return x;
-        };
-        uint64_t gu_seen = 0;   // the gate/up queue head as last read
-        uint32_t sticky = 0;    // the sticky error word, read (relaxed) at the end of the previous chunk
-        // down chunks are taken two at a time (consecutive chunks of one
-        // expert, so the consumers quantise that expert's h once for both)
-        const unsigned long long take = isA ? 1ull : 2ull;
-        int64_t g0 = failed ? total : (int64_t)atomicAdd(head, take);
-        int64_t pend = (!isA && g0 + 1 < total) ? g0 + 1 : -1;   // the pair's second chunk
-        Next cur = fetch(g0);
-        int64_t gn = failed ? total : (int64_t)atomicAdd(head, take);   // the next take's first index
-        for (int f = 0;; f++) {
-            const int s = s0 + f % nsr;
-            const uint64_t te0 = tr ? now_ns() : 0;
-            if (f >= nsr && !mbar_wait(&empty[s], (uint32_t)(f / nsr - 1) & 1u)) {
-                failed = true;
-                break;   // the consumers time out on what is missing
-            }
-            if (tr) t_empty += now_ns() - te0;
-            SDesc *sd = &sdesc[s];
-            if (cur.g >= total || failed || sticky) {
-                sd->tok = -1;
-                mbar_arrive(&full[s]);
-                break;
-            }
-            if (!isA) {
-                // keep the down queue a token behind: a down chunk of token t
-                // goes out once every gate/up chunk of token t + 1 has been
-                // taken, so h of token t is normally published by then
-                const int64_t want = (int64_t)(cur.tok + 2) * G.nGU;
-                const uint64_t need = (uint64_t)(want < totalA ? want : totalA);
-                if (gu_seen < need) {
-                    const uint64_t tf0 = tr ? now_ns() : 0;
-                    if (!grid_wait(gu_head, need)) failed = true;
-                    gu_seen = ld_acquire64(gu_head);
-                    if (tr) t_flag += now_ns() - tf0;
-                }
-            }
-            if (tr && cur.tok == trace_tok(a)) {
-                const uint64_t tn = now_ns();
-                uint64_t &first = tr[isA ? 10 : 7], &last = tr[isA ? 11 : 12];
-                if (!first) first = tn;
-                last = tn;
-            }
-            const uint64_t start = (uint64_t)cur.row0 * rb, lo = start & ~15ull;
-            const uint32_t size = (uint32_t)(((start + (uint64_t)cur.nrows * rb + 15) & ~15ull) - lo);
-            sd->tok = cur.tok;
-            sd->r = cur.r;
-            sd->row0 = cur.row0;
-            sd->nrows = cur.nrows;
-            sd->roff = (uint32_t)(start - lo);
-            uint8_t *stg = smem + (isA ? G.offA + (size_t)s * G.strideA : G.offB + (size_t)(s - nsA) * G.strideB);
-            if (isA) {
-                mbar_expect_tx(&full[s], 2u * size + qvx);
-                bulk_g2s(stg, cur.m0 + lo, size, &full[s]);
-                bulk_g2s(stg + SEG_A, cur.m1 + lo, size, &full[s]);
-                bulk_g2s(stg + 2 * SEG_A, a.xq + (size_t)cur.tok * qvx, qvx, &full[s]);
-            } else {
-                mbar_expect_tx(&full[s], size + 4u * (uint32_t)de);
-                bulk_g2s(stg, cur.m0 + lo, size, &full[s]);
-                // the expert's h rows, once every gate/up chunk of (token, expert)
-                // has counted its rows (normally long before: the count was read
-                // when the chunk was taken)
-                const uint32_t *hc = sa.hcnt + (size_t)cur.tok * k + cur.r;
-                bool hok = true;
-                if (cur.hc != (uint32_t)de) {
-                    const uint64_t tf0 = tr ? now_ns() : 0;
-                    hok = count_wait(hc, (uint32_t)de);
-                    if (tr) {
-                        t_flag += now_ns() - tf0;
-                        if (cur.tok == trace_tok(a) && !tr[8]) tr[8] = now_ns();
-                    }
-                }
-                if (!hok) {
-                    raise_error(err, bar, FUSED_ERR_BARRIER);
-                    failed = true;   // the copy still goes out (so no copy is left pending); results are invalid
-                }
-                fence_acq_rel();     // the relaxed count read becomes an acquire of the rows
-                fence_proxy_async(); // ... for the bulk copy below
-                bulk_g2s(stg + SEG_B, a.hbuf + (size_t)cur.tok * P + (size_t)cur.r * de, 4u * (uint32_t)de, &full[s]);
-            }
-            if (pend >= 0) {
-                cur = fetch(pend);
-                pend = -1;
-            } else {
-                cur = fetch(gn);
-                pend = (!isA && gn + 1 < total) ? gn + 1 : -1;
-                gn = (int64_t)atomicAdd(head, take);
-            }
-            sticky = ld_relaxed(&bar[2]);
-        }
-        if (failed) raise_error(err, bar, FUSED_ERR_COPY);
-        if (tr) {
-            tr[isA ? 4 : 5] = t_empty;
-            if (!isA) tr[6] = t_flag;
-        }
-    } else if (!stop && (warp == W_GD || warp == W_DD)) {
-        // ---- duty warps: one entry per consumed chunk, in order. Lane 0
-        // waits for the next entry; every entry already pushed behind it is
-        // taken in the same round, one per lane, so the counts of a backlog
-        // go out together (one atomic round trip per round, not per entry)
-        const bool isA = warp == W_GD;
-        uint64_t *fq = reinterpret_cast<uint64_t *>(smem + (isA ? G.fqA : G.fqB));
-        uint64_t *eq = reinterpret_cast<uint64_t *>(smem + (isA ? G.eqA : G.eqB));
-        const QEnt *qe = reinterpret_cast<const QEnt *>(smem + (isA ? G.qA : G.qB));
-        bool done = false;
-        for (int q = 0; !done;) {
-            bool ok = lane == 0 ? mbar_wait(&fq[q % NQ], (uint32_t)(q / NQ) & 1u) : false;
-            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-            if (!ok) {
-                if (lane == 0) raise_error(err, bar, FUSED_ERR_BARRIER);
-                break;
-            }
-            // lanes 1 .. NQ-1 test the entries behind it; the round takes the
-            // ready prefix
-            const bool ready = lane == 0 || (lane < NQ && mbar_test(&fq[(q + lane) % NQ], (uint32_t)((q + lane) / NQ) & 1u));
-            const uint32_t rm = __ballot_sync(0xFFFFFFFFu, ready);
-            const int m = __ffs(~rm) - 1;   // lanes [0, m) hold ready entries
-            QEnt ent{ -1, 0, 0, 0 };
-            if (lane < m) ent = qe[(q + lane) % NQ];
-            __syncwarp();
-            if (lane < m) mbar_arrive(&eq[(q + lane) % NQ]);
-            // an END entry ends the ring: nothing after it is taken
-            const uint32_t endm = __ballot_sync(0xFFFFFFFFu, lane < m && ent.tok < 0);
-            const int mm = endm ? __ffs(endm) - 1 : m;
-            if (endm) done = true;
-            q += m;
-            const bool mine = lane < mm;
-            if (tr && isA && __any_sync(0xFFFFFFFFu, mine && ent.tok == trace_tok(a)) && lane == 0 && !tr[14])
-                tr[14] = now_ns();
-            if (isA) {
-                // count the chunk's h rows of (token, expert): one fence for the
-                // round (the rows were written before the entries were pushed),
-                // then fire-and-forget adds; the down producer reads the counts
-                __threadfence();
-                if (mine) red_add(sa.hcnt + (size_t)ent.tok * k + ent.r, (uint32_t)ent.nrows);
-            } else {
-                // 64-row output groups: each entry's rows lie in at most two
-                // groups; the CTA completing a group combines its rows in
-                // ascending rank
-                uint32_t cg[2] = { 0xFFFFFFFFu, 0xFFFFFFFFu };   // completed group per pass
-                for (int pass = 0; pass < 2; pass++) {
-                    if (!mine) continue;
-                    const int grp = (ent.row0 >> 6) + pass;
-                    if (64 * grp >= ent.row0 + ent.nrows) continue;
-                    const int ga = max(ent.row0, 64 * grp), gz = min(ent.row0 + ent.nrows, 64 * grp + 64);
-                    uint32_t *gc = a.ocnt + (size_t)ent.tok * (D / 64) + grp;
-                    if ((int)atom_add_acq_rel(gc, (uint32_t)(gz - ga)) + (gz - ga) == 64 * k) {
-                        *gc = 0u;
-                        cg[pass] = (uint32_t)grp;
-                    }
-                }
-                for (int pass = 0; pass < 2; pass++) {
-                    uint32_t cm = __ballot_sync(0xFFFFFFFFu, cg[pass] != 0xFFFFFFFFu);
-                    if (cm) {
-                        __syncwarp();
-                        __threadfence();
-                    }
-                    while (cm) {
-                        const int src = __ffs(cm) - 1;
-                        cm &= cm - 1;
-                        const int tok = __shfl_sync(0xFFFFFFFFu, ent.tok, src);
-                        const int grp = (int)__shfl_sync(0xFFFFFFFFu, cg[pass], src);
-                        float wk[MAXK];
-#pragma unroll
-                        for (int q2 = 0; q2 < MAXK; q2++) wk[q2] = q2 < k ? __ldcg(sa.wg + (size_t)tok * k + q2) : 0.0f;
-                        float e0[MAXK], e1[MAXK];
-                        const float *eb = a.eo + (size_t)tok * Q + 64 * grp + lane;
-#pragma unroll
-                        for (int q2 = 0; q2 < MAXK; q2++) {
-                            e0[q2] = q2 < k ? __ldcg(eb + (size_t)q2 * D) : 0.0f;
-                            e1[q2] = q2 < k ? __ldcg(eb + (size_t)q2 * D + 32) : 0.0f;
-                        }
-#pragma unroll
-                        for (int hh = 0; hh < 2; hh++) {
-                            const int i = 64 * grp + lane + 32 * hh;
-                            float fv = 0.0f;
-#pragma unroll
-                            for (int q2 = 0; q2 < MAXK; q2++)
-                                if (q2 < k) fv = __fadd_rn(fv, __fmul_rn(wk[q2], hh ? e1[q2] : e0[q2]));
-                            if (a.s_out) fv = __fadd_rn(fv, __fmul_rn(*a.sgate, a.s_out[i]));
-                            a.ffn[(size_t)tok * D + i] = fv;
-                            if (a.h) a.h[i] = __fadd_rn(a.h[i], fv);
-                        }
-                    }
-                }
-            }
-        }
-    } else if (!stop && warp < NCW) {
-        // ---- consumers: stages in fill order; one unit per thread into the
-        // shared partials, a group barrier that releases the stage, then the
-        // rows' chains on the group's last warp, which hands the chunk to the
-        // duty warp
-        const bool isA = warp < NAW;
-        const int gth = isA ? NAW * 32 : (NCW - NAW) * 32, gt = isA ? t : t - NAW * 32;
-        const int rbg = nbx * dt_block_bytes(DGU), rbd = nbd * dt_block_bytes(DDN);
-        const int nsr = isA ? nsA : nsB, s0 = isA ? 0 : nsA;
-        const int nbu = isA ? nbx : 2 * nbd, pstr = nbu + 1, pcap = isA ? G.rowsA : G.rowsB;
-        BlockSum *part = reinterpret_cast<BlockSum *>(smem + (isA ? G.partA : G.partB));
-        const int pbuf = (isA ? 2 : 1) * pcap * pstr;
-        uint64_t *fq = reinterpret_cast<uint64_t *>(smem + (isA ? G.fqA : G.fqB));
-        uint64_t *eq = reinterpret_cast<uint64_t *>(smem + (isA ? G.eqA : G.eqB));
-        QEnt *qe = reinterpret_cast<QEnt *>(smem + (isA ? G.qA : G.qB));
-        auto gsync = [&]() {
-            if (isA) asm volatile("bar.sync 2, %0;" ::"n"(NAW * 32) : "memory");
-            else asm volatile("bar.sync 3, %0;" ::"n"((NCW - NAW) * 32) : "memory");
-        };
-        // the duty ring: only the group's last thread pushes
-        int nq = 0;
-        auto push = [&](const QEnt &v) -> bool {
-            const int e = nq % NQ;
-            if (nq >= NQ && !mbar_wait(&eq[e], (uint32_t)(nq / NQ - 1) & 1u)) return false;
-            qe[e] = v;
-            mbar_arrive(&fq[e]);
-            nq++;
-            return true;
-        };
-        uint32_t tw = 0, tc = 0;
-        int pb = 0, nq_seen = 0, qtok = -1, qr = -1;   // qtok / qr: whose h the group's quantised h holds
-        bool dead = false;   // the pushing thread only: the duty ring stopped answering
-        for (int f = 0;; f++) {
-            const int s = s0 + f % nsr;
-            const uint32_t tw0 = tr ? (uint32_t)now_ns() : 0u;
-            // every thread of the group leaves together (a group barrier
-            // with a missing thread would never complete)
-            const bool ok = mbar_wait(&full[s], (uint32_t)(f / nsr) & 1u) && !dead;
-            if (!group_all(ok, isA ? 4 : 5, gth)) {
-                if (gt == 0) raise_error(err, bar, FUSED_ERR_COPY);
-                dead = true;
-                break;
-            }
-            const uint32_t tc0 = tr ? (uint32_t)now_ns() : 0u;
-            if (tr) tw += tc0 - tw0;
-            const SDesc d = sdesc[s];
-            if (d.tok < 0) break;
-            nq_seen++;
-            if (!isA && (d.tok != qtok || d.r != qr)) {
-                // the expert's raw h rows came with the chunk: quantise them once
-                // for the chunks of this (token, expert) that follow in a row
-                const float *hr = reinterpret_cast<const float *>(smem + G.offB + (size_t)(s - nsA) * G.strideB + SEG_B);
-                const QVec hq = qvec(smem + G.hq, nbd);
-                for (int b = gt >> 5; b < nbd; b += gth >> 5) {
-                    const float4 *h4 = reinterpret_cast<const float4 *>(hr + 256 * b) + 2 * lane;
-                    quant_block(h4[0], h4[1], hq, b, lane);
-                }
-                gsync();
-                qtok = d.tok;
-                qr = d.r;
-            }
-            BlockSum *pp = part + pb * pbuf;
-            const int units = d.nrows * nbu;
-            if (isA) {
-                const uint8_t *stg = smem + G.offA + (size_t)s * G.strideA;
-                const QVec x = qvec(const_cast<uint8_t *>(stg) + 2 * SEG_A, nbx);
-                for (int u = gt; u < units; u += gth) {
-                    const int row = u / nbx, b = u - row * nbx;
-                    const uint8_t *wb[2] = { stg + d.roff + (size_t)row * rbg + b * dt_block_bytes(DGU),
-                                             stg + SEG_A + d.roff + (size_t)row * rbg + b * dt_block_bytes(DGU) };
-                    BlockSum o2[2];
-                    kblock_dot<DGU, 2>(wb, XBlk{ x.codes, nbx, b, x.bs + 16 * b, x.d[b] }, o2);
-                    pp[row * pstr + b] = o2[0];
-                    pp[(pcap + row) * pstr + b] = o2[1];
-                }
-            } else {
-                const uint8_t *stg = smem + G.offB + (size_t)(s - nsA) * G.strideB;
-                const QVec h = qvec(smem + G.hq, nbd);
-                for (int u = gt; u < units; u += gth) {
-                    const int row = u / nbu, ub = u - row * nbu, b = ub >> 1;
-                    BlockSum o1;
-                    kblock_half<DDN>(stg + d.roff + (size_t)row * rbd + b * dt_block_bytes(DDN),
-                                     XBlk{ h.codes, nbd, b, h.bs + 16 * b, h.d[b] }, ub & 1, o1);
-                    pp[row * pstr + ub] = o1;
-                }
-            }
-            gsync();   // the chunk's partials are written; the stage is no longer read
-            if (gt == 0) mbar_arrive(&empty[s]);
-            if (gth - 1 - gt < d.nrows) {
-                const int row = gth - 1 - gt;
-                if (isA) {
-                    float ag = 0.0f, au = 0.0f;
-                    for (int b = 0; b < nbx; b++) {
-                        const BlockSum eg = pp[row * pstr + b], eu = pp[(pcap + row) * pstr + b];
-                        ag = chain<DGU>(ag, eg.dA, eg.is, eg.dM, eg.ms);
-                        au = chain<DGU>(au, eu.dA, eu.is, eu.dM, eu.ms);
-                    }
-                    a.hbuf[(size_t)d.tok * P + (size_t)d.r * de + d.row0 + row] = __fmul_rn(silu_f(ag), au);
-                } else {
-                    float eo = 0.0f;
-                    for (int b = 0; b < nbd; b++) {
-                        const BlockSum e0 = pp[row * pstr + 2 * b], e1 = pp[row * pstr + 2 * b + 1];
-                        eo = chain<DDN>(eo, e0.dA, e0.is + e1.is, e0.dM, e0.ms + e1.ms);
-                    }
-                    a.eo[(size_t)d.tok * Q + (size_t)d.r * D + d.row0 + row] = eo;
-                }
-            }
-            if (gt >= gth - 32) {
-                __syncwarp();   // every chain of the chunk is written (they run in this warp)
-                if (tr && isA && gt == gth - 1 && d.tok == trace_tok(a) && !tr[13]) tr[13] = now_ns();
-                if (gt == gth - 1 && !push(QEnt{ d.tok, d.r, d.row0, d.nrows })) {
-                    raise_error(err, bar, FUSED_ERR_BARRIER);
-                    dead = true;   // voted at the next stage
-                }
-            }
-            if (tr) tc += (uint32_t)now_ns() - tc0;
-            pb ^= 1;
-        }
-        if (gt == gth - 1 && !dead) push(QEnt{ -1, 0, 0, 0 });
-        if (tr && gt == 0) tr[isA ? 2 : 3] = (uint64_t)nq_seen;
-        if (tr && lane == 0) {
-            atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 16 : 18]), (unsigned long long)tw);
-            atomicAdd(reinterpret_cast<unsigned long long *>(&tr[isA ? 17 : 19]), (unsigned long long)tc);
-        }
-    }
-    __syncthreads();
-    if (t == 0) {
-        if (tr) tr[20] = now_ns();
-        if (!stop) {
-            // the last CTA out resets the queue heads for the next launch
-            __threadfence();
-            if (atomicAdd(bar + 10, 1u) == gridDim.x - 1) {
-                *sk_word(bar, 1) = 0ull;
-                *sk_word(bar, 2) = 0ull;
-                bar[10] = 0u;
-                __threadfence();
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
 // host side
 using KernelFn = void (*)(const FusedArgs, uint32_t *, uint32_t *, int, int);
 
@@ -1376,11 +764,8 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     f.k = g.top_k;
     if (cudaMalloc(&f.bar, BAR_BYTES) != cudaSuccess) return set_error(TLMG_ENOMEM, "fused barrier allocation");
     cudaMemset(f.bar, 0, BAR_BYTES);
-    if (cudaMalloc(&f.sbar, 64) != cudaSuccess) return set_error(TLMG_ENOMEM, "stream kernel grid words");
-    cudaMemset(f.sbar, 0, 64);
     if (cudaMalloc(&f.obar, 16) != cudaSuccess) return set_error(TLMG_ENOMEM, "single-token kernel grid words");
     cudaMemset(f.obar, 0, 16);
-    f.sepoch = 0;
     f.rounds = 0;
     f.launches = 0;
     if (cudaHostAlloc(&f.err_host, 64, cudaHostAllocMapped) != cudaSuccess)
@@ -1392,16 +777,12 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
 }
 
 static void free_tokens(FusedScratch &f) {
-    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.eo, (void *)f.ocnt, (void *)f.hcnt, (void *)f.tslot,
-                     (void *)f.wg })
+    for (void *p : { (void *)f.xq, (void *)f.hbuf, (void *)f.eo, (void *)f.ocnt })
         if (p) cudaFree(p);
     f.xq = nullptr;
     f.hbuf = nullptr;
     f.eo = nullptr;
     f.ocnt = nullptr;
-    f.hcnt = nullptr;
-    f.tslot = nullptr;
-    f.wg = nullptr;
     f.tok_cap = 0;
 }
 
@@ -1413,38 +794,23 @@ static int reserve_tokens(FusedScratch &f, int n_tok) {
     const int cap = n_tok < 64 ? 64 : n_tok;
     const int nbx = f.D / 256;
     const size_t P = (size_t)f.k * f.de, Q = (size_t)f.k * f.D;
-    const size_t ck = (size_t)cap * f.k;
     if (cudaMalloc(&f.xq, (size_t)cap * qv_bytes(nbx)) != cudaSuccess ||
         cudaMalloc(&f.hbuf, (size_t)cap * P * 4) != cudaSuccess ||
         cudaMalloc(&f.eo, (size_t)cap * Q * 4) != cudaSuccess ||
-        cudaMalloc(&f.ocnt, (size_t)cap * (f.D / 64) * 4) != cudaSuccess ||
-        cudaMalloc(&f.hcnt, ck * 4) != cudaSuccess || cudaMalloc(&f.tslot, ck * sizeof(Slot)) != cudaSuccess ||
-        cudaMalloc(&f.wg, ck * 4) != cudaSuccess) {
+        cudaMalloc(&f.ocnt, (size_t)cap * (f.D / 64) * 4) != cudaSuccess) {
         cudaGetLastError();
         free_tokens(f);
         return set_error(TLMG_ENOMEM, "fused per-token scratch for %d tokens", n_tok);
     }
     cudaMemset(f.ocnt, 0, (size_t)cap * (f.D / 64) * 4);
-    cudaMemset(f.hcnt, 0, ck * 4);
-    // flags of a fresh buffer restart the epochs (the device is idle: cudaFree synchronised)
-    cudaMemset(f.sbar, 0, 64);
-    f.sepoch = 0;
     f.tok_cap = cap;
     return TLMG_OK;
 }
 
-using StreamFn = void (*)(const FusedArgs, const StreamArgs, uint32_t *, uint32_t *);
-struct StreamPlanHost {   // one (gate/up, down) dtype pair's geometry and kernel
-    StreamGeom g;
-    StreamFn fn;
-};
-
 void fused_release(FusedScratch &f) {
     free_tokens(f);
     if (f.bar) cudaFree(f.bar);
-    if (f.sbar) cudaFree(f.sbar);
     if (f.obar) cudaFree(f.obar);
-    for (auto &kv : f.splans) delete kv.second;
     if (f.err_host) cudaFreeHost(f.err_host);
     for (auto &kv : f.plans) cudaFree(kv.second);
     f = FusedScratch{};
@@ -1527,95 +893,6 @@ const void *fused_plan(FusedScratch &f, const tlmg_geom &g, int dgu, int ddn) {
                cudaMemcpyHostToDevice);
     f.plans[key] = dp;
     return dp;
-}
-
-// ---- the stream kernel's host side
-static StreamFn pick_stream(int dgu, int ddn) {
-#define TLMG_S(G, DN) \
-    if (dgu == G && ddn == DN) return k_stream_ffn<G, DN>;
-    TLMG_S(DT_Q4_K, DT_Q4_K) TLMG_S(DT_Q4_K, DT_Q5_K) TLMG_S(DT_Q4_K, DT_Q6_K)
-    TLMG_S(DT_Q5_K, DT_Q4_K) TLMG_S(DT_Q5_K, DT_Q5_K) TLMG_S(DT_Q5_K, DT_Q6_K)
-    TLMG_S(DT_Q6_K, DT_Q4_K) TLMG_S(DT_Q6_K, DT_Q5_K) TLMG_S(DT_Q6_K, DT_Q6_K)
-#undef TLMG_S
-    return nullptr;
-}
-
-// Chunking per expert: nce chunks of per rows (the last one shorter), at
-// most rows_max rows in `seg` bytes of stage (copies start 16-aligned, so
-// up to 30 bytes of slack).
-static bool chunking(int len, int rb, int rows_max, uint32_t seg, int &rows, int &nce, int &per) {
-    rows = std::min<int>(rows_max, (int)((seg - 30) / (uint32_t)rb));
-    if (rows < 1) return false;
-    nce = (len + rows - 1) / rows;
-    per = (len + nce - 1) / nce;
-    return true;
-}
-
-static const StreamPlanHost *stream_plan(FusedScratch &f, int dgu, int ddn) {
-    const FusedPlanKey key{ dgu, ddn };
-    auto it = f.splans.find(key);
-    if (it != f.splans.end()) return it->second;
-    StreamFn fn = pick_stream(dgu, ddn);
-    const int D = f.D, de = f.de, k = f.k;
-    if (!fn || D / 256 > 16 || de / 256 > 16 || k > MAXK) return nullptr;
-    StreamGeom g{};
-    const int rbg = D / 256 * dt_block_bytes(dgu), rbd = de / 256 * dt_block_bytes(ddn);
-    g.segA = sk::SEG_A;
-    g.segB = sk::SEG_B;
-    if (!chunking(de, rbg, sk::ROWS_A, g.segA, g.rowsA, g.nceA, g.perA) ||
-        !chunking(D, rbd, sk::ROWS_B, g.segB, g.rowsB, g.nceB, g.perB))
-        return nullptr;
-    g.nGU = k * g.nceA;
-    g.nDN = k * g.nceB;
-    g.nsA = sk::NSA;
-    g.nsB = 0;
-    for (int nb = sk::MAXS - g.nsA; nb >= 2; nb--) {
-        StreamGeom t = g;
-        t.nsB = nb;
-        if (stream_layout(t, D, de).total <= f.smem_limit) {
-            g.nsB = nb;
-            break;
-        }
-    }
-    if (!g.nsB) return nullptr;
-    g = stream_layout(g, D, de);
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.total) != cudaSuccess) {
-        cudaGetLastError();
-        return nullptr;
-    }
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, sk::NTHREADS, g.total) != cudaSuccess ||
-        per_sm < 1) {
-        cudaGetLastError();
-        return nullptr;
-    }
-    StreamPlanHost *sp = new StreamPlanHost{ g, fn };
-    f.splans[key] = sp;
-    return sp;
-}
-
-static int launch_stream(FusedScratch &f, const StreamPlanHost &sp, const FusedArgs &a, cudaStream_t st) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)f.nsm);
-    cfg.blockDim = dim3(sk::NTHREADS);
-    cfg.dynamicSmemBytes = sp.g.total;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    FusedArgs la = a;
-    la.xq = f.xq;
-    la.hbuf = f.hbuf;
-    la.eo = f.eo;
-    la.ocnt = f.ocnt;
-    StreamArgs sa{ sp.g, f.hcnt, f.tslot, f.wg, (uint32_t)(f.sepoch + 1) };
-    cudaError_t e = cudaLaunchKernelEx(&cfg, sp.fn, la, sa, f.sbar, f.err_dev);
-    count_launch();
-    if (e != cudaSuccess) return cuda_fail(e, "stream expert FFN launch");
-    f.sepoch++;
-    return TLMG_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -1940,13 +1217,6 @@ static int launch_one(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
 }
 
 int launch_fused_ffn(FusedScratch &f, const FusedArgs &a, cudaStream_t st) {
-    if (f.mode == FUSED_STREAM) {
-        if (const StreamPlanHost *sp = stream_plan(f, a.dt_gu, a.dt_dn)) {
-            int rc = reserve_tokens(f, a.n_tok);
-            if (rc) return rc;
-            return launch_stream(f, *sp, a, st);
-        }
-    }
     {
         const int r1 = launch_one(f, a, st);
         if (r1 < 0) return r1;
@@ -1997,13 +1267,10 @@ uint32_t fused_take_error(FusedScratch &f) {
         // device word and the barrier state for the next launch
         *(volatile uint32_t *)f.err_host = 0;
         cudaMemset(f.bar, 0, BAR_BYTES);
-        cudaMemset(f.sbar, 0, 64);
         if (f.obar) cudaMemset(f.obar, 0, 16);
         if (f.ocnt) cudaMemset(f.ocnt, 0, (size_t)f.tok_cap * (f.D / 64) * 4);
-        if (f.hcnt) cudaMemset(f.hcnt, 0, (size_t)f.tok_cap * f.k * 4);
         f.rounds = 0;
         f.launches = 0;
-        f.sepoch = 0;
     }
     return e;
 }

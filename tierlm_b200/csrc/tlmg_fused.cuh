@@ -46,19 +46,9 @@ struct FusedPlanKey {
 };
 
 // Per-context state of the persistent kernels (k_fused_ffn: a static work
-// split with a grid barrier per token; k_stream_ffn: chunks handed out by
-// two global queues, per-expert h flags instead of the barrier).
-enum : int { FUSED_STATIC = 1, FUSED_STREAM = 2 };
-struct StreamPlanHost;
+// split with a grid barrier per token; k_ffn_one: one token per launch).
 struct FusedScratch {
     bool enabled = false;          // usable on this device / geometry
-    int mode = FUSED_STATIC;       // which persistent kernel serves a launch
-    uint32_t *sbar = nullptr;      // device: the stream kernel's grid words (64 bytes)
-    uint64_t sepoch = 0;           // stream-kernel launches since sbar was reset
-    uint32_t *hcnt = nullptr;      // [tok_cap][k] h rows counted (stream kernel; zeroed at launch start)
-    struct Slot *tslot = nullptr;  // [tok_cap][k] routed experts' slots
-    float *wg = nullptr;           // [tok_cap][k] routing weights
-    std::map<FusedPlanKey, StreamPlanHost *> splans;
     uint32_t *bar = nullptr;       // device: [2] sticky error, [4..11] four 64-bit barrier arrival words
     uint32_t *err_host = nullptr;  // mapped pinned word: error bits set by the kernel
     uint32_t *err_dev = nullptr;   // its device alias

@@ -305,17 +305,19 @@ int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, 
     const size_t row_used = (size_t)(n / qk) * dt_block_bytes(dt);
     MvFn mv = pick_mv(dt);
     if (mv && ((uintptr_t)W & 15u) == 0 && rb % 16 == 0 && row_used % 16 == 0 && row_used <= 8192) {
-        // MV_WARPS warps a CTA, two row buffers a warp; as many CTAs as are resident
+        // MV_WARPS warps a CTA, two row buffers a warp; as many CTAs as are resident.
+        // Each instance is opted in once to 160 KB of dynamic shared memory
+        // (its static `part` array comes on top of the dynamic bytes).
         const size_t sm = 2 * row_used * MV_WARPS;
-        static thread_local size_t opted = 48 * 1024;
-        if (sm > opted) {
-            if (cudaFuncSetAttribute((const void *)mv, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
-                cudaSuccess)
-                opted = 160 * 1024;
-            else
-                cudaGetLastError();
+        static thread_local std::vector<const void *> opted;
+        bool ok = std::find(opted.begin(), opted.end(), (const void *)mv) != opted.end();
+        if (!ok) {
+            ok = cudaFuncSetAttribute((const void *)mv, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024) ==
+                 cudaSuccess;
+            if (ok) opted.push_back((const void *)mv);
+            else cudaGetLastError();
         }
-        if (sm <= opted) {
+        if (ok && sm <= 160 * 1024) {
             int per_sm = 0;
             if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, (const void *)mv, MV_WARPS * 32, sm) !=
                     cudaSuccess ||

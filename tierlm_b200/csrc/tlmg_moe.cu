@@ -762,9 +762,8 @@ int tlmg_profile_read(tlmg_ctx *c, int cls, double *ms, int64_t *launches, int64
 int tlmg_set_fused(tlmg_ctx *c, int on) {
     if (c) c->wgen++;
     if (!c) return set_error(TLMG_EINVAL, "NULL context");
-    if (on < 0 || on > 4) return set_error(TLMG_EINVAL, "set_fused: mode %d", on);
+    if (on < 0 || on > 4 || on == 3) return set_error(TLMG_EINVAL, "set_fused: mode %d", on);
     c->fused_on = on != 0;
-    c->fused.mode = on == 3 ? FUSED_STREAM : FUSED_STATIC;
     c->fused.single = on == 4;
     return c->fused.enabled ? TLMG_OK : (on ? set_error(TLMG_EUNSUP, "persistent kernel unavailable on this device") : TLMG_OK);
 }
@@ -1856,11 +1855,11 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
 
 // Graph replay is used from a context's second step on when nothing in the
 // step depends on host decisions made per call: every MoE layer resident
-// (no slot cache) and the static persistent kernel (its barrier words are
-// restarted per captured launch).
+// (no slot cache; the persistent kernels' barrier words are restarted per
+// captured launch or reset themselves).
 static bool step_graph_allowed(const tlmg_ctx *c) {
     const StepModel &m = *c->step;
-    if (m.graph_off || !m.use_graphs || m.calls == 0 || c->prof || c->fused.mode != FUSED_STATIC) return false;
+    if (m.graph_off || !m.use_graphs || m.calls == 0 || c->prof) return false;
     for (const Layer &Ly : c->L)
         if (Ly.cached) return false;
     return true;

@@ -57,13 +57,12 @@ class MoeContext:
         except Exception:
             pass
 
-    FUSED_MODES = {"default": 1, "static": 2, "stream": 3, "single": 4}
+    FUSED_MODES = {"default": 1, "static": 2, "single": 4}
 
     def set_fused(self, on) -> None:
-        """Persistent kernels (True, default: the static kernel), "stream"
-        (its stream variant), "single" (one-token launches by the
-        single-token kernel), or the multi-kernel path (False). Identical
-        bits."""
+        """Persistent kernels (True, default: the static kernel), "single"
+        (one-token launches by the single-token kernel), or the multi-kernel
+        path (False). Identical bits."""
         mode = self.FUSED_MODES[on] if isinstance(on, str) else (1 if on else 0)
         check(self._lib.tlmg_set_fused(self._h, mode))
 
