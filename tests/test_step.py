@@ -23,21 +23,31 @@ from conftest import same_bits
 
 pytestmark = pytest.mark.gpu
 
-D, DE, E, K, H, KVH, HD, V, L = 512, 256, 8, 2, 4, 2, 64, 300, 2
 EPS, THETA = 1e-6, 10000.0
-LAYER_DTS = [(14, 14, 14, 8), (12, 8, 14, 13)]   # q, k, v, o
-EMB_DT, HEAD_DT = 14, 8
+
+# small: D 512, rows whose lengths are not 16-byte multiples (the kernels
+# with a separate norm / quantisation kernel); wide: D 2048 with Q6_K q|k|v,
+# Q4_K o and Q6_K lm_head rows of 16-byte multiples (the matvecs that form
+# their own activations) and an f32 router on the normalised residual
+SHAPES = {
+    "small": dict(D=512, DE=256, E=8, K=2, H=4, KVH=2, HD=64, V=300,
+                  LAYER_DTS=[(14, 14, 14, 8), (12, 8, 14, 13)], EMB_DT=14, HEAD_DT=8),
+    "wide": dict(D=2048, DE=768, E=8, K=2, H=8, KVH=2, HD=128, V=512,
+                 LAYER_DTS=[(14, 14, 14, 12), (12, 8, 14, 13)], EMB_DT=12, HEAD_DT=14),
+}
 
 
-def _model(seed):
+def _model(seed, shape="small"):
     from tierlm_b200 import synth
+    c = SHAPES[shape]
+    D, DE, E, H, KVH, HD = c["D"], c["DE"], c["E"], c["H"], c["KVH"], c["HD"]
     rng = np.random.default_rng(seed)
 
     def norm(n):
         return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
 
     layers = []
-    for l_, dts in enumerate(LAYER_DTS):
+    for l_, dts in enumerate(c["LAYER_DTS"]):
         mats = [synth.rand_rows(dts[0], H * HD, D, rng), synth.rand_rows(dts[1], KVH * HD, D, rng),
                 synth.rand_rows(dts[2], KVH * HD, D, rng), synth.rand_rows(dts[3], D, H * HD, rng)]
         layers.append(dict(dts=dts, mats=mats, attn_norm=norm(D), q_norm=norm(HD) if l_ == 0 else None,
@@ -45,8 +55,8 @@ def _model(seed):
                            router_w=(rng.standard_normal((E, D)) / np.sqrt(D)).astype(np.float32),
                            experts=[synth.rand_expert(rng, D, DE, (12, 12, 14)) for _ in range(E)]))
     inv = np.array([np.float32(THETA ** (-2.0 * j / HD)) for j in range(HD // 2)], np.float32)
-    return dict(layers=layers, emb=synth.rand_rows(EMB_DT, V, D, rng), head=synth.rand_rows(HEAD_DT, V, D, rng),
-                out_norm=norm(D), inv=inv)
+    return dict(cfg=c, layers=layers, emb=synth.rand_rows(c["EMB_DT"], c["V"], D, rng),
+                head=synth.rand_rows(c["HEAD_DT"], c["V"], D, rng), out_norm=norm(D), inv=inv)
 
 
 def _mv(orc, dt, W, x, rows):
@@ -57,13 +67,16 @@ def _mv(orc, dt, W, x, rows):
 
 def _ref_steps(orc, m, tokens):
     """Logits of every position, the reference's step composed on the oracle."""
+    c = m["cfg"]
+    D, DE, E, K, H, KVH, HD, V = (c[x] for x in ("D", "DE", "E", "K", "H", "KVH", "HD", "V"))
+    L = len(m["layers"])
     page = 16
     kp = np.zeros((L, KVH, page, HD), np.float32)
     vp = np.zeros((L, KVH, page, HD), np.float32)
     geom = dict(d_model=D, d_expert=DE, n_experts=E, top_k=K, router=0, norm_eps=EPS)
     out = []
     for pos, tok in enumerate(tokens):
-        h = orc.dequantize_row(EMB_DT, m["emb"][tok], D)
+        h = orc.dequantize_row(c["EMB_DT"], m["emb"][tok], D)
         cs = np.array([np.float32(math.cos(pos * float(f))) for f in m["inv"]], np.float32)
         sn = np.array([np.float32(math.sin(pos * float(f))) for f in m["inv"]], np.float32)
         for l_, A in enumerate(m["layers"]):
@@ -87,12 +100,15 @@ def _ref_steps(orc, m, tokens):
             layer = dict(ffn_norm=A["ffn_norm"], router_dt=0, router_w=A["router_w"], router_rb=4 * D)
             h = orc.moe_layer(geom, layer, A["experts"], h)[0]
         xb = orc.rmsnorm(h, m["out_norm"], EPS)
-        out.append(_mv(orc, HEAD_DT, m["head"], xb, V))
+        out.append(_mv(orc, c["HEAD_DT"], m["head"], xb, V))
     return np.stack(out)
 
 
 def _gpu_ctx(m):
     from tierlm_b200.moe import MoeContext
+    c = m["cfg"]
+    D, DE, E, K, H, KVH, HD, V = (c[x] for x in ("D", "DE", "E", "K", "H", "KVH", "HD", "V"))
+    L = len(m["layers"])
     ctx = MoeContext(L, D, DE, E, K, router=0)
     for l_, A in enumerate(m["layers"]):
         for e, (payload, off, dts) in enumerate(A["experts"]):
@@ -101,15 +117,17 @@ def _gpu_ctx(m):
     ctx.step_open(H, KVH, HD, V, m["inv"], 1.0, max_ctx=16, kv_dtype=0, attn_mode=0)
     for l_, A in enumerate(m["layers"]):
         ctx.set_attention(l_, A["attn_norm"], A["dts"], *A["mats"], q_norm=A["q_norm"], k_norm=A["k_norm"])
-    ctx.set_embedding(EMB_DT, m["emb"])
-    ctx.set_output(m["out_norm"], HEAD_DT, m["head"])
+    ctx.set_embedding(c["EMB_DT"], m["emb"])
+    ctx.set_output(m["out_norm"], c["HEAD_DT"], m["head"])
     return ctx
 
 
-def test_decode_step_matches_composed_oracle(orc):
+@pytest.mark.parametrize("shape", list(SHAPES))
+def test_decode_step_matches_composed_oracle(orc, shape):
     from tierlm_b200 import _lib
     _lib.check(_lib.load().tlmg_init(0))
-    m = _model(5)
+    m = _model(5, shape)
+    V = m["cfg"]["V"]
     tokens = [7, 299, 0, 123, 7, 42]
     orc.set_expf_mode(1)
     try:
@@ -149,6 +167,8 @@ def test_decode_step_errors(orc):
     from tierlm_b200.moe import MoeContext
     _lib.check(_lib.load().tlmg_init(0))
     m = _model(6)
+    c = m["cfg"]
+    V = c["V"]
     ctx = _gpu_ctx(m)
     lg = np.zeros(V, np.float32)
     for tok, pos, code in ((V, 0, _lib.TLMG_EINVAL), (-1, 0, _lib.TLMG_EINVAL), (0, 16, _lib.TLMG_ERANGE)):
@@ -156,10 +176,10 @@ def test_decode_step_errors(orc):
             ctx.decode_step(tok, pos, lg)
         assert ei.value.code == code
     ctx.close()
-    bare = MoeContext(L, D, DE, E, K, router=0)
+    bare = MoeContext(len(m["layers"]), c["D"], c["DE"], c["E"], c["K"], router=0)
     with pytest.raises(_lib.TlmError):
         bare.decode_step(0, 0, lg)
-    bare.step_open(H, KVH, HD, V, m["inv"], 1.0, max_ctx=16)
+    bare.step_open(c["H"], c["KVH"], c["HD"], V, m["inv"], 1.0, max_ctx=16)
     with pytest.raises(_lib.TlmError) as ei:
         bare.decode_step(0, 0, lg)
     assert ei.value.code == _lib.TLMG_ENOTFOUND
