@@ -48,8 +48,23 @@ constexpr int NAW = 7;                  // consumer warps [0, NAW) process gate/
 constexpr int NTHREADS = 32 * (NCW + 5);   // + gate/up stream, router, two duty warps, down stream (warp NCW + 4)
 constexpr int MAXCH = FUSED_MAXCH;
 constexpr int MAXK = 16;
-constexpr int SLOT_A = 50720;   // gate/up stage: the gate rows and the up rows of a chunk, half each (22 Q4_K rows of D = 2048)
-constexpr int SLOT_B = 24576;   // down stage: the rows of one expert
+// Stage sizes and counts (compile-time tuning; the defaults measured best):
+// a gate/up stage holds the gate rows and the up rows of a chunk, half
+// each (22 Q4_K rows of D = 2048); a down stage holds rows of one expert.
+#ifndef TLMG_SLOT_A
+#define TLMG_SLOT_A 50720
+#endif
+#ifndef TLMG_SLOT_B
+#define TLMG_SLOT_B 24576
+#endif
+#ifndef TLMG_NS_A
+#define TLMG_NS_A 2       // gate/up stages
+#endif
+#ifndef TLMG_NS_B_MAX
+#define TLMG_NS_B_MAX 3   // down stages, as many as fit up to this
+#endif
+constexpr int SLOT_A = TLMG_SLOT_A;
+constexpr int SLOT_B = TLMG_SLOT_B;
 constexpr uint64_t WAIT_NS = 200000000ull;       // 0.2 s: an mbarrier wait gives up
 constexpr uint64_t BARRIER_NS = 500000000ull;    // 0.5 s: the grid barrier gives up
 
@@ -747,17 +762,17 @@ int fused_init(FusedScratch &f, const tlmg_geom &g) {
     if (g.n_experts <= 0 || g.n_experts > RT_PER * 32 || g.top_k > MAXK) return TLMG_OK;
     if (g.d_model % 256 || g.d_expert % 256 || g.d_model > 4096) return TLMG_OK;
     f.smem_limit = prop.sharedMemPerBlockOptin;
-    // stage counts: two gate/up stages, as many down stages as fit (>= 2)
+    // stage counts: TLMG_NS_A gate/up stages, as many down stages as fit (>= 2)
     int nsB = 0;
-    for (int nb = 3; nb >= 2; nb--)
-        if (smem_layout(g.d_model, g.d_expert, g.top_k, 2, nb).total + 1024 <= f.smem_limit) {
+    for (int nb = TLMG_NS_B_MAX; nb >= 2; nb--)
+        if (smem_layout(g.d_model, g.d_expert, g.top_k, TLMG_NS_A, nb).total + 1024 <= f.smem_limit) {
             nsB = nb;
             break;
         }
     if (!nsB) return TLMG_OK;
-    f.nsA = 2;
+    f.nsA = TLMG_NS_A;
     f.nsB = nsB;
-    f.smem = smem_layout(g.d_model, g.d_expert, g.top_k, 2, nsB).total;
+    f.smem = smem_layout(g.d_model, g.d_expert, g.top_k, TLMG_NS_A, nsB).total;
     f.nsm = prop.multiProcessorCount;
     f.D = g.d_model;
     f.de = g.d_expert;
