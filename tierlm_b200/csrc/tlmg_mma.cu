@@ -404,8 +404,14 @@ __device__ __forceinline__ void report(uint32_t *err, bool ok) {
 // tile. out[m][pair][row] = the row's dot (m = 0 gate, 1 up). Small enough
 // for two CTAs per SM at 8 tokens per pass.
 constexpr int GU_THREADS = 2 * MR;
+#ifndef TLMG_MGU_MINB
+#define TLMG_MGU_MINB 2   // CTAs per SM the 8-token gate/up kernel is compiled for
+#endif
+#ifndef TLMG_MGU_NS8
+#define TLMG_MGU_NS8 3    // raw stages of the 8-token gate/up kernel (D <= 2048)
+#endif
 template <int DT, int NS, int TN>
-__global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? 2 : 1)
+__global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : 1)
     k_mgu(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
           size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ gout, float *__restrict__ uout,
           uint32_t *err) {
@@ -623,7 +629,7 @@ __global__ void __launch_bounds__(DN_THREADS, TN <= 8 ? 2 : 1)
 // SM), 32 when the experts average many tokens (prefill: the unpack and the
 // per-pass overheads are shared by 4x more tokens).
 static int pass_tokens(bool wide) { return wide ? 32 : 8; }
-static int gateup_stages(int D, int tn) { return D <= 2048 || tn <= 8 ? 3 : 2; }
+static int gateup_stages(int D, int tn) { return tn <= 8 ? TLMG_MGU_NS8 : D <= 2048 ? 3 : 2; }
 
 static uint32_t gateup_smem(int dt, int D, int tn) {
     const uint32_t raw = (uint32_t)gateup_stages(D, tn) * MR * dt_block_bytes(dt);
@@ -669,7 +675,9 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
     int tn = pass_tokens(wide);
     if (gateup_smem(dt, D, tn) > SMEM_LIMIT) tn = 8;
     const uint32_t smem = gateup_smem(dt, D, tn);
-    const int grid = grid_for(2 * max_items, smem <= 113 * 1024 ? 2 : 1);
+    // CTAs per SM: as many as the kernel is compiled for and 228 KB of shared memory per SM hold
+    const int per_sm = std::max(1, std::min<int>(tn <= 8 ? TLMG_MGU_MINB : 2, (int)(233472u / (smem + 1024u))));
+    const int grid = grid_for(2 * max_items, per_sm);
     const bool three = gateup_stages(D, tn) == 3;
     using Fn = void (*)(const Slot *, const int32_t *, const uint8_t *, size_t, int, int, int, int, float *, float *,
                         uint32_t *);
