@@ -373,6 +373,15 @@ int tlmg_step_graphs(tlmg_ctx *ctx, int on);
 /* out[4]: steps run, steps replayed from a graph, captures, 1 when a
  * capture failed and graphs were turned off. */
 int tlmg_step_info(const tlmg_ctx *ctx, int64_t *out);
+/* The step's counters in tlm_model_stats order (tlm_model_get_stats /
+ * tlm_model_reset_stats, src/lib/tlm_model.h:87-96): out[5] = tokens,
+ * attn_ns, moe_ns, expert_wait_ns, other_ns. tokens counts every
+ * tlmg_decode_step; the phase times are device time between CUDA events
+ * recorded at the phase boundaries of the steps run while tlmg_profile(ctx,
+ * 1) is on (those steps run eagerly and each waits for its end; other steps
+ * add no time). expert_wait_ns is always 0 here. reset != 0 zeroes them
+ * after reading. */
+int tlmg_step_stats(tlmg_ctx *ctx, uint64_t *out, int reset);
 
 /* ---- Expert parallelism over peer memory (one process per GPU, all GPUs
  * of one node). The same split as above, with the exchange done by the

@@ -184,3 +184,31 @@ def test_decode_step_errors(orc):
         bare.decode_step(0, 0, lg)
     assert ei.value.code == _lib.TLMG_ENOTFOUND
     bare.close()
+
+
+def test_decode_step_stats(orc):
+    """tlmg_step_stats counts every step; steps run while profiling add
+    their attention / MoE / other device time (each phase positive, their
+    sum the step's), give the same logits as graph replay, and reset zeroes
+    the counters."""
+    from tierlm_b200 import _lib
+    _lib.check(_lib.load().tlmg_init(0))
+    m = _model(8)
+    V = m["cfg"]["V"]
+    ctx = _gpu_ctx(m)
+    plain = np.zeros((3, V), np.float32)
+    for pos, tok in enumerate((3, 1, 4)):
+        ctx.decode_step(tok, pos, plain[pos])
+    s0 = ctx.step_stats()
+    assert s0["tokens"] == 3 and s0["attn_ns"] == 0 and s0["moe_ns"] == 0
+    ctx.profile(True)
+    prof = np.zeros((3, V), np.float32)
+    for pos, tok in enumerate((3, 1, 4)):
+        ctx.decode_step(tok, pos, prof[pos])
+    ctx.profile(False)
+    s1 = ctx.step_stats(reset=True)
+    assert s1["tokens"] == 6 and s1["attn_ns"] > 0 and s1["moe_ns"] > 0 and s1["other_ns"] > 0, s1
+    assert s1["expert_wait_ns"] == 0
+    assert ctx.step_stats() == dict(tokens=0, attn_ns=0, moe_ns=0, expert_wait_ns=0, other_ns=0)
+    assert same_bits(prof, plain).all()
+    ctx.close()

@@ -91,6 +91,7 @@ _SIGS = {
     "tlmg_decode_step": (_I, [_P, _I, _I, _P]),
     "tlmg_step_graphs": (_I, [_P, _I]),
     "tlmg_step_info": (_I, [_P, _P]),
+    "tlmg_step_stats": (_I, [_P, _P, _I]),
     "tlmg_ep_open": (_I, [_P, _I, _I, _I]),
     "tlmg_ep_handle_bytes": (_SZ, []),
     "tlmg_ep_handle": (_I, [_P, _P]),

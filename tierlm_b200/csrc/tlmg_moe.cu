@@ -1797,7 +1797,8 @@ struct ActCache {
 // m.logits. With dargs the token and position are read from device memory
 // (the body is then position-independent and can be captured); attention
 // launches are then shaped for max_ctx positions.
-static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *dargs) {
+static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *dargs,
+                     const cudaEvent_t *tev = nullptr) {
     StepModel &m = *c->step;
     const tlmg_geom &g = c->g;
     const int D = g.d_model, L = g.n_layers, H = m.H, KV = m.KV, hd = m.hd;
@@ -1805,11 +1806,13 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
     float *dh = c->h;
     const size_t off80 = (tlmg_qact_bytes(DT_Q8_K, D) + 15) & ~size_t(15);
     const size_t aoff80 = (tlmg_qact_bytes(DT_Q8_K, H * hd) + 15) & ~size_t(15);
+    if (tev) cudaEventRecord(tev[0], st);
     int rc = step_embed(m.embd_dt, m.embd, m.embd_rb, token, dargs, D, dh, st);
     if (rc) return rc;
     const int rows[3] = { H * hd, KV * hd, KV * hd };
     for (int l = 0; l < L; l++) {
         const StepLayer &A = m.A[l];
+        if (tev) cudaEventRecord(tev[1 + 2 * l], st);
         // attention() (src/lib/tlm_model.c:730-763)
         const bool xq_now = act_kind_for(A.dt[0]) == DT_Q8_K;   // xb as Q8_K from the norm kernel itself
         launch_k(k_rmsnorm, 1, 256, 0, st, dh, A.attn_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
@@ -1840,9 +1843,14 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
             (rc = launch_matvec(A.dt[3], A.w[3], A.rb[3], act, dh, H * hd, 0, D, st, dh)))   // h += o . att
             return rc;
         // moe() (src/lib/tlm_model.c:940-1055)
+        if (tev) cudaEventRecord(tev[2 + 2 * l], st);
         if ((rc = moe_layer_impl(c, l, dh, nullptr, nullptr, nullptr))) return rc;
     }
-    if (!head) return TLMG_OK;
+    if (tev) cudaEventRecord(tev[2 * L + 1], st);
+    if (!head) {
+        if (tev) cudaEventRecord(tev[2 * L + 2], st);
+        return TLMG_OK;
+    }
     const bool xq_now = act_kind_for(m.head_dt) == DT_Q8_K;
     launch_k(k_rmsnorm, 1, 256, 0, st, dh, m.out_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
     if ((rc = launched("output rmsnorm"))) return rc;
@@ -1850,7 +1858,9 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
     af.have8k = xq_now;
     const void *act;
     if ((rc = af.get(m.head_dt, st, &act))) return rc;
-    return launch_matvec(m.head_dt, m.head, m.head_rb, act, m.logits, D, 0, m.vocab, st);
+    rc = launch_matvec(m.head_dt, m.head, m.head_rb, act, m.logits, D, 0, m.vocab, st);
+    if (tev) cudaEventRecord(tev[2 * L + 2], st);
+    return rc;
 }
 
 // Graph replay is used from a context's second step on when nothing in the
@@ -1940,12 +1950,40 @@ static int decode_step(tlmg_ctx *c, int token, int pos, float *logits) {
         }
     }
     if (!replayed) {
+        // while profiling (graphs are then off) the phases are timed with events
+        const cudaEvent_t *tev = nullptr;
+        if (c->prof) {
+            if (m.tev.empty()) {
+                m.tev.resize(2 * (size_t)L + 3, nullptr);
+                for (cudaEvent_t &e : m.tev)
+                    if (cudaEventCreate(&e) != cudaSuccess) return cuda_fail(cudaGetLastError(), "step events");
+            }
+            tev = m.tev.data();
+        }
         set_pdl(true);
-        rc = step_body(c, token, pos, head != 0, nullptr);
+        rc = step_body(c, token, pos, head != 0, nullptr, tev);
         set_pdl(false);
         if (rc) return rc;
+        if (tev) {
+            cudaError_t e = cudaEventSynchronize(tev[2 * L + 2]);
+            if (e != cudaSuccess) return cuda_fail(e, "step events");
+            auto ms = [&](int a, int b) {
+                float t = 0.0f;
+                return cudaEventElapsedTime(&t, tev[a], tev[b]) == cudaSuccess ? (double)t : 0.0;
+            };
+            double attn = 0.0, moe = 0.0;
+            for (int l = 0; l < L; l++) {
+                attn += ms(1 + 2 * l, 2 + 2 * l);
+                moe += ms(2 + 2 * l, 3 + 2 * l);   // to the next layer's start, or after the last layer
+            }
+            const double total = ms(0, 2 * L + 2);
+            m.st_attn_ns += (uint64_t)(attn * 1e6);
+            m.st_moe_ns += (uint64_t)(moe * 1e6);
+            m.st_other_ns += (uint64_t)std::max(0.0, (total - attn - moe) * 1e6);
+        }
     }
     m.calls++;
+    m.st_tokens++;
     if (!logits) return TLMG_OK;
     const size_t bytes = 4 * (size_t)m.vocab;
     if (is_device_ptr(logits)) {
@@ -1965,6 +2003,19 @@ int tlmg_step_info(const tlmg_ctx *c, int64_t *out) {
     out[1] = m.replays;
     out[2] = m.captures;
     out[3] = m.graph_off ? 1 : 0;
+    return TLMG_OK;
+}
+
+int tlmg_step_stats(tlmg_ctx *c, uint64_t *out, int reset) {
+    if (!c || !out) return set_error(TLMG_EINVAL, "step_stats: NULL argument");
+    if (!c->step) return set_error(TLMG_EINVAL, "step_stats: tlmg_step_open first");
+    StepModel &m = *c->step;
+    out[0] = m.st_tokens;
+    out[1] = m.st_attn_ns;
+    out[2] = m.st_moe_ns;
+    out[3] = 0;   // expert_wait_ns: not measured (resident experts never wait)
+    out[4] = m.st_other_ns;
+    if (reset) m.st_tokens = m.st_attn_ns = m.st_moe_ns = m.st_other_ns = 0;
     return TLMG_OK;
 }
 

@@ -56,11 +56,19 @@ struct StepModel {
     bool graph_off = false;             // capture failed once: eager from then on
     int64_t calls = 0;                  // steps run (the first is always eager)
     int64_t replays = 0, captures = 0;
+    // tlm_model_stats counters (tlmg_step_stats): steps, and the device time
+    // of the phases of steps run while profiling (events at the boundaries:
+    // [0] start, [1 + 2 l] layer l's attention, [2 + 2 l] its MoE block,
+    // [2 L + 1] after the layers, [2 L + 2] end)
+    uint64_t st_tokens = 0, st_attn_ns = 0, st_moe_ns = 0, st_other_ns = 0;
+    std::vector<cudaEvent_t> tev;
     cudaStream_t cap_st = nullptr;      // private stream graphs are captured on (the caller's may be the
                                         // legacy default stream, which cannot be captured)
 };
 
 inline void step_graphs_release(StepModel &m) {
+    for (cudaEvent_t e : m.tev) cudaEventDestroy(e);
+    m.tev.clear();
     for (int h = 0; h < 2; h++)
         if (m.graph[h]) {
             cudaGraphExecDestroy(m.graph[h]);

@@ -257,6 +257,16 @@ class MoeContext:
         check(self._lib.tlmg_step_info(self._h, out))
         return {"steps": out[0], "replays": out[1], "captures": out[2], "graphs_off": bool(out[3])}
 
+    def step_stats(self, reset: bool = False) -> dict:
+        """tlm_model_stats of the step: tokens, attn_ns, moe_ns, expert_wait_ns,
+        other_ns (phase times from steps run while profiling)."""
+        out = (C.c_uint64 * 5)()
+        check(self._lib.tlmg_step_stats(self._h, out, 1 if reset else 0))
+        return dict(zip(("tokens", "attn_ns", "moe_ns", "expert_wait_ns", "other_ns"), list(out)))
+
+    def profile(self, on: bool) -> None:
+        check(self._lib.tlmg_profile(self._h, 1 if on else 0))
+
     def ep_open(self, rank: int, n_ranks: int, max_tok: int) -> bytes:
         """Opens this rank's peer-memory exchange; returns its handle (bytes
         to hand to every peer)."""
