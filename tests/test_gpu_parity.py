@@ -101,6 +101,22 @@ def test_matvec_random_vs_oracle(dev, orc, dt):
         assert bad.size == 0, (dt, n, bad[:5], got[bad[:5]], ref[bad[:5]])
 
 
+@pytest.mark.parametrize("dt", [12, 14])
+def test_matvec_tall_vs_oracle(dev, orc, dt):
+    """A tall matrix (70,000 rows of 2048: an lm_head's shape, each warp
+    walking many rows through its deeper row pipeline), every row bit-exact."""
+    from tierlm_b200 import quant, synth
+    rng = np.random.default_rng(700 + dt)
+    rows, n = 70000, 2048
+    Wb = synth.rand_rows(dt, rows, n, rng)
+    act = orc.quantize_act(orc.act_kind_for(dt), rng.standard_normal(n).astype(np.float32))
+    ref = orc.matvec_rows(dt, Wb, Wb.shape[1], act, n, 0, rows)
+    y = torch.empty(rows, device=dev)
+    quant.matvec_rows(dt, to_dev(Wb, dev), Wb.shape[1], to_dev(act, dev), y, n, 0, rows)
+    bad = np.flatnonzero(~same_bits(y.cpu().numpy(), ref))
+    assert bad.size == 0, (dt, bad[:5])
+
+
 @pytest.mark.parametrize("dt", [0, 1, 2, 8, 12, 13, 14, 15])
 def test_dequantize_rows_vs_oracle(dev, orc, dt):
     """tlmg_dequantize_rows (the decoder step's embedding gather) against

@@ -162,7 +162,10 @@ __device__ __forceinline__ void mv_cp16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
 }
 
-template <int DT>
+// NPF row buffers per warp: rows r + stride ... r + (NPF - 1) stride are
+// in flight while row r is computed (NPF = 2 by default; TLMG_MV_TALL_NPF
+// for tall matrices such as an lm_head, whose warps walk many rows).
+template <int DT, int NPF>
 __global__ void __launch_bounds__(MV_WARPS * 32)
 k_matvec_qs(const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act, float *y, int nb, int64_t r0,
             int64_t r1, const float *res) {
@@ -172,23 +175,24 @@ k_matvec_qs(const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict_
     constexpr int BB = dt_block_bytes(DT), ABB = act_block_bytes(act_kind_for(DT));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 3, j = lane & 7;
     const int nw = blockDim.x >> 5, n16 = nb * BB / 16;
-    uint4 *buf = mv_rows + (size_t)warp * 2 * n16;
+    uint4 *buf = mv_rows + (size_t)warp * NPF * n16;
     const int64_t stride = (int64_t)gridDim.x * nw;
+    // one cp.async group per row slot, an empty one past the last row, so
+    // that "all but the newest NPF - 1 groups complete" means "row ready"
     auto issue = [&](int64_t r, uint4 *dst) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(W + (size_t)r * rb);
-        for (int i = lane; i < n16; i += 32) mv_cp16(dst + i, src + i);
+        if (r < r1) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(W + (size_t)r * rb);
+            for (int i = lane; i < n16; i += 32) mv_cp16(dst + i, src + i);
+        }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     int64_t row = r0 + (int64_t)blockIdx.x * nw + warp;
-    if (row < r1) issue(row, buf);
+#pragma unroll
+    for (int q = 0; q < NPF - 1; q++) issue(row + (int64_t)q * stride, buf + q * n16);
     for (int it = 0; row < r1; row += stride, it++) {
-        const uint8_t *row_s = reinterpret_cast<const uint8_t *>(buf + (it & 1) * n16);
-        if (row + stride < r1) {
-            issue(row + stride, buf + ((it + 1) & 1) * n16);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-        }
+        const uint8_t *row_s = reinterpret_cast<const uint8_t *>(buf + (it % NPF) * n16);
+        issue(row + (int64_t)(NPF - 1) * stride, buf + ((it + NPF - 1) % NPF) * n16);
+        asm volatile("cp.async.wait_group %0;" ::"n"(NPF - 1) : "memory");
         __syncwarp();
         float acc = 0.0f;
         for (int c0 = 0; c0 < nb; c0 += MV_CHUNK) {
@@ -220,13 +224,14 @@ k_matvec_qs(const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict_
 }
 
 using MvFn = void (*)(const uint8_t *, size_t, const uint8_t *, float *, int, int64_t, int64_t, const float *);
+template <int NPF>
 static MvFn pick_mv(int dt) {
     switch (dt) {
-    case DT_Q4_K: return k_matvec_qs<DT_Q4_K>;
-    case DT_Q5_K: return k_matvec_qs<DT_Q5_K>;
-    case DT_Q6_K: return k_matvec_qs<DT_Q6_K>;
-    case DT_Q8_0: return k_matvec_qs<DT_Q8_0>;
-    case DT_Q8_K: return k_matvec_qs<DT_Q8_K>;
+    case DT_Q4_K: return k_matvec_qs<DT_Q4_K, NPF>;
+    case DT_Q5_K: return k_matvec_qs<DT_Q5_K, NPF>;
+    case DT_Q6_K: return k_matvec_qs<DT_Q6_K, NPF>;
+    case DT_Q8_0: return k_matvec_qs<DT_Q8_0, NPF>;
+    case DT_Q8_K: return k_matvec_qs<DT_Q8_K, NPF>;
     default: return nullptr;
     }
 }
@@ -303,12 +308,19 @@ int launch_matvec(int dt, const void *Wv, size_t rb, const void *act, float *y, 
     const int nw = (int)std::max<int64_t>(1, std::min<int64_t>(MV_WARPS, rows / 148));
     const unsigned grid_nw = (unsigned)std::max<int64_t>(1, std::min<int64_t>((rows + nw - 1) / nw, 148 * 32));
     const size_t row_used = (size_t)(n / qk) * dt_block_bytes(dt);
-    MvFn mv = pick_mv(dt);
+    // tall matrices: more row buffers a warp (each warp walks many rows); an
+    // lm_head of 151,936 Q6_K rows measured 129.6 us with 2, 123.1 with 3
+    // and 124.9 with 4 (graph-timed, B200): the kernel is issue-bound
+#ifndef TLMG_MV_TALL_NPF
+#define TLMG_MV_TALL_NPF 3
+#endif
+    const int npf = rows >= 65536 && row_used <= 4096 ? TLMG_MV_TALL_NPF : 2;
+    MvFn mv = npf == 4 ? pick_mv<4>(dt) : npf == 3 ? pick_mv<3>(dt) : pick_mv<2>(dt);
     if (mv && ((uintptr_t)W & 15u) == 0 && rb % 16 == 0 && row_used % 16 == 0 && row_used <= 8192) {
-        // MV_WARPS warps a CTA, two row buffers a warp; as many CTAs as are resident.
+        // MV_WARPS warps a CTA, npf row buffers a warp; as many CTAs as are resident.
         // Each instance is opted in once to 160 KB of dynamic shared memory
         // (its static `part` array comes on top of the dynamic bytes).
-        const size_t sm = 2 * row_used * MV_WARPS;
+        const size_t sm = (size_t)npf * row_used * MV_WARPS;
         static thread_local std::vector<const void *> opted;
         bool ok = std::find(opted.begin(), opted.end(), (const void *)mv) != opted.end();
         if (!ok) {
