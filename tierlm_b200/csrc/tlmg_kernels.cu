@@ -165,8 +165,11 @@ __device__ __forceinline__ void mv_cp16(void *dst, const void *src) {
 // NPF row buffers per warp: rows r + stride ... r + (NPF - 1) stride are
 // in flight while row r is computed (NPF = 2 by default; TLMG_MV_TALL_NPF
 // for tall matrices such as an lm_head, whose warps walk many rows).
+#ifndef TLMG_MV_MINB
+#define TLMG_MV_MINB 4   // CTAs per SM the staged matvec is compiled for (64 registers)
+#endif
 template <int DT, int NPF>
-__global__ void __launch_bounds__(MV_WARPS * 32)
+__global__ void __launch_bounds__(MV_WARPS * 32, TLMG_MV_MINB)
 k_matvec_qs(const uint8_t *__restrict__ W, size_t rb, const uint8_t *__restrict__ act, float *y, int nb, int64_t r0,
             int64_t r1, const float *res) {
     pdl_enter();
