@@ -322,6 +322,10 @@ k_ffn_down(const Slot *__restrict__ slots, const int32_t *__restrict__ ids, cons
 // sum in index order. A fixed tree gives the same float after the division
 // unless the value lies within the two sums' combined error bound of a float
 // rounding boundary; then thread 0 redoes the sequential sum.
+#ifndef TLMG_NORM_THREADS
+#define TLMG_NORM_THREADS 512
+#endif
+constexpr int NORM_THREADS = TLMG_NORM_THREADS;   // threads of the one-CTA RMSNorm kernel
 __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ wn, int n, float eps,
                           float *__restrict__ out, uint8_t *__restrict__ q8k) {
     pdl_enter();
@@ -1476,7 +1480,7 @@ static int launch_lookahead(tlmg_ctx *c, int layer, const float *dh) {
     int k = std::min(c->la_k, N.live);   // never more hints than routable experts
     if (k <= 0) return TLMG_OK;
     int rc;
-    k_rmsnorm<<<1, 256, 0, c->st>>>(dh, N.ffn_norm, D, c->g.norm_eps, c->la_x, nullptr);
+    k_rmsnorm<<<1, NORM_THREADS, 0, c->st>>>(dh, N.ffn_norm, D, c->g.norm_eps, c->la_x, nullptr);
     if ((rc = launched("lookahead rmsnorm"))) return rc;
     const int kr = act_kind_for(N.router_dt);
     if (kr != DT_F32 && (rc = launch_quant_act(kr, c->la_x, D, c->la_q, c->st))) return rc;
@@ -1510,7 +1514,7 @@ static int moe_layer_impl(tlmg_ctx *c, int layer, float *h, int32_t *ids, float 
         dh = c->h;
     }
     // xb = rmsnorm(h); activations of xb
-    launch_k(k_rmsnorm, 1, 256, 0, c->st, dh, Ly.ffn_norm, D, g.norm_eps, c->x, (uint8_t *)nullptr);
+    launch_k(k_rmsnorm, 1, NORM_THREADS, 0, c->st, dh, Ly.ffn_norm, D, g.norm_eps, c->x, (uint8_t *)nullptr);
     if ((rc = launched("rmsnorm"))) return rc;
     // the persistent kernel quantises its input itself: the activations of
     // xb are only formed for the parts that read them
@@ -1815,7 +1819,7 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
         if (tev) cudaEventRecord(tev[1 + 2 * l], st);
         // attention() (src/lib/tlm_model.c:730-763)
         const bool xq_now = act_kind_for(A.dt[0]) == DT_Q8_K;   // xb as Q8_K from the norm kernel itself
-        launch_k(k_rmsnorm, 1, 256, 0, st, dh, A.attn_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
+        launch_k(k_rmsnorm, 1, NORM_THREADS, 0, st, dh, A.attn_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
         if ((rc = launched("attention rmsnorm"))) return rc;
         ActCache ax{ m.xb, D, m.xq, m.xq + off80 };
         ax.have8k = xq_now;
@@ -1852,7 +1856,7 @@ static int step_body(tlmg_ctx *c, int token, int pos, bool head, const int32_t *
         return TLMG_OK;
     }
     const bool xq_now = act_kind_for(m.head_dt) == DT_Q8_K;
-    launch_k(k_rmsnorm, 1, 256, 0, st, dh, m.out_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
+    launch_k(k_rmsnorm, 1, NORM_THREADS, 0, st, dh, m.out_norm, D, g.norm_eps, m.xb, xq_now ? m.xq : nullptr);
     if ((rc = launched("output rmsnorm"))) return rc;
     ActCache af{ m.xb, D, m.xq, m.xq + off80 };
     af.have8k = xq_now;
