@@ -239,6 +239,11 @@ static MvFn pick_mv(int dt) {
     }
 }
 
+#ifndef TLMG_MVF_U
+#define TLMG_MVF_U 32
+#endif
+constexpr int MVF_U = TLMG_MVF_U;   // loads in flight per lane in the float matvec
+
 // Float weights: element i into lane i mod 32 with fmaf, then the fixed
 // tree (reference tlm_quant.c:724-770).
 template <int A>
@@ -256,16 +261,16 @@ k_matvec_f(int dt, const uint8_t *__restrict__ W, size_t rb, const float *__rest
             return bf16_to_f32(WLoad<(A < 2 ? A : 2)>::u16(wr + 2 * i));
         };
         int64_t i = lane;
-        // eight elements' loads issued together, then their fmaf chain in order
-        for (; i + 7 * 32 < n; i += 8 * 32) {
-            float wv[8], xv[8];
+        // MVF_U elements' loads issued together, then their fmaf chain in order
+        for (; i + (MVF_U - 1) * 32 < n; i += MVF_U * 32) {
+            float wv[MVF_U], xv[MVF_U];
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
+            for (int u = 0; u < MVF_U; u++) {
                 wv[u] = wload(i + 32 * u);
                 xv[u] = __ldg(x + i + 32 * u);
             }
 #pragma unroll
-            for (int u = 0; u < 8; u++) acc = __fmaf_rn(wv[u], xv[u], acc);
+            for (int u = 0; u < MVF_U; u++) acc = __fmaf_rn(wv[u], xv[u], acc);
         }
         for (; i < n; i += 32) acc = __fmaf_rn(wload(i), __ldg(x + i), acc);
         acc = tree32(acc);
