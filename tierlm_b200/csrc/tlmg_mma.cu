@@ -411,7 +411,7 @@ constexpr int GU_THREADS = 2 * MR;
 #define TLMG_MGU_NS8 3    // raw stages of the 8-token gate/up kernel (D <= 2048)
 #endif
 template <int DT, int NS, int TN>
-__global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : 1)
+__global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : TN <= 16 ? 2 : 1)
     k_mgu(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
           size_t xstride, int xdiv, int D, int de, int E, float *__restrict__ gout, float *__restrict__ uout,
           uint32_t *err) {
@@ -625,19 +625,43 @@ __global__ void __launch_bounds__(DN_THREADS, TN <= 8 ? 2 : 1)
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Tokens per pass: 8 for decode-sized groups (small tiles, two CTAs per
-// SM), 32 when the experts average many tokens (prefill: the unpack and the
-// per-pass overheads are shared by 4x more tokens).
-static int pass_tokens(bool wide) { return wide ? 32 : 8; }
-static int gateup_stages(int D, int tn) { return tn <= 8 ? TLMG_MGU_NS8 : D <= 2048 ? 3 : 2; }
+// Tokens per pass: NARROW_TN for decode-sized groups (small tiles, two CTAs
+// per SM); when the experts average many tokens (prefill) the wider passes
+// below, so that the unpack and the per-pass overheads are shared by more
+// tokens.
+constexpr int NARROW_TN = 8;
+// Tokens per gate/up pass when the experts average many tokens (16 or 32).
+// At 32 one CTA fits on an SM (177 registers, 180 KB of shared memory); at
+// 16 the kernel takes two raw stages and two CTAs share an SM (113
+// registers, 115 KB each). 2048-token prefill of 48 layers (B200, 16-token
+// down passes): 18.6k tok/s with 32, 21.6k with 16.
+#ifndef TLMG_GU_WIDE_TN
+#define TLMG_GU_WIDE_TN 16
+#endif
+static_assert(TLMG_GU_WIDE_TN == 16 || TLMG_GU_WIDE_TN == 32, "gate/up pass width: 16 or 32 tokens");
+static int gateup_stages(int D, int tn) { return tn <= 8 ? TLMG_MGU_NS8 : tn <= 16 ? 2 : D <= 2048 ? 3 : 2; }
 
 static uint32_t gateup_smem(int dt, int D, int tn) {
     const uint32_t raw = (uint32_t)gateup_stages(D, tn) * MR * dt_block_bytes(dt);
-    return tn <= 8 ? mplan<8>(1, raw, D / 256, true).total : mplan<32>(1, raw, D / 256, true).total;
+    return tn <= 8    ? mplan<8>(1, raw, D / 256, true).total
+           : tn <= 16 ? mplan<16>(1, raw, D / 256, true).total
+                      : mplan<32>(1, raw, D / 256, true).total;
 }
+// Tokens per down pass when the experts average many tokens. 32 keeps one
+// CTA per SM for Q6_K (16 groups x 32 TMEM columns, 127 KB of shared
+// memory); 16 halves the TMEM columns and the staged token codes, so that
+// two CTAs share an SM (110 KB each), at the price of twice the passes (each
+// unpacks the tile again). 2048-token prefill of 48 layers (B200): 17.7k
+// tok/s with 32, 18.7k with 16.
+#ifndef TLMG_DN_WIDE_TN
+#define TLMG_DN_WIDE_TN 16
+#endif
+static_assert(TLMG_DN_WIDE_TN == 16 || TLMG_DN_WIDE_TN == 32, "down pass width: 16 or 32 tokens");
 static uint32_t down_smem(int dt, int de, int tn) {
     const uint32_t tile = align_up((uint32_t)MR * (de / 256) * dt_block_bytes(dt), 1024u) + MR * 128u;
-    return tn <= 8 ? mplan<8>(0, tile, de / 256, false).total : mplan<32>(0, tile, de / 256, false).total;
+    return tn <= 8    ? mplan<8>(0, tile, de / 256, false).total
+           : tn <= 16 ? mplan<16>(0, tile, de / 256, false).total
+                      : mplan<32>(0, tile, de / 256, false).total;
 }
 constexpr uint32_t SMEM_LIMIT = 227 * 1024;
 
@@ -672,7 +696,7 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
                       int D, int de, int E, int64_t max_items, bool wide, float *gout, float *uout, uint32_t *err,
                       cudaStream_t st) {
     if (!mma_gateup_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core gate/up: dtype %d D %d", dt, D);
-    int tn = pass_tokens(wide);
+    int tn = wide ? TLMG_GU_WIDE_TN : NARROW_TN;
     if (gateup_smem(dt, D, tn) > SMEM_LIMIT) tn = 8;
     const uint32_t smem = gateup_smem(dt, D, tn);
     // CTAs per SM: as many as the kernel is compiled for and 228 KB of shared memory per SM hold
@@ -686,8 +710,8 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
         fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3, 8> : k_mgu<DT_Q4_K, 2, 8>)
                            : (three ? k_mgu<DT_Q5_K, 3, 8> : k_mgu<DT_Q5_K, 2, 8>);
     else
-        fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3, 32> : k_mgu<DT_Q4_K, 2, 32>)
-                           : (three ? k_mgu<DT_Q5_K, 3, 32> : k_mgu<DT_Q5_K, 2, 32>);
+        fn = dt == DT_Q4_K ? (three ? k_mgu<DT_Q4_K, 3, TLMG_GU_WIDE_TN> : k_mgu<DT_Q4_K, 2, TLMG_GU_WIDE_TN>)
+                           : (three ? k_mgu<DT_Q5_K, 3, TLMG_GU_WIDE_TN> : k_mgu<DT_Q5_K, 2, TLMG_GU_WIDE_TN>);
     int rc = opt_in(fn, smem);
     if (rc) return rc;
     fn<<<grid, GU_THREADS, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, gout, uout, err);
@@ -698,7 +722,7 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
 int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t *hq, int D, int de, int E,
                     int64_t max_items, bool wide, float *eo, uint32_t *err, cudaStream_t st) {
     if (!mma_down_supported(dt, D, de)) return set_error(TLMG_EUNSUP, "tensor-core down: dtype %d de %d", dt, de);
-    int tn = pass_tokens(wide);
+    int tn = wide ? TLMG_DN_WIDE_TN : NARROW_TN;
     if (down_smem(dt, de, tn) > SMEM_LIMIT) tn = 8;
     const uint32_t smem = down_smem(dt, de, tn);
     const int grid = grid_for(max_items, smem <= 113 * 1024 ? 2 : 1);
@@ -707,7 +731,9 @@ int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t
     if (tn == 8)
         fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K, 8> : dt == DT_Q5_K ? k_mdown<DT_Q5_K, 8> : k_mdown<DT_Q6_K, 8>;
     else
-        fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K, 32> : dt == DT_Q5_K ? k_mdown<DT_Q5_K, 32> : k_mdown<DT_Q6_K, 32>;
+        fn = dt == DT_Q4_K ? k_mdown<DT_Q4_K, TLMG_DN_WIDE_TN>
+             : dt == DT_Q5_K ? k_mdown<DT_Q5_K, TLMG_DN_WIDE_TN>
+                             : k_mdown<DT_Q6_K, TLMG_DN_WIDE_TN>;
     int rc = opt_in(fn, smem);
     if (rc) return rc;
     fn<<<grid, DN_THREADS, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
