@@ -44,11 +44,13 @@ DT_GATE, DT_DOWN = 12, 14                       # Q4_K gate/up, Q6_K down
 BYTES_LAYER_TOKEN = K * (2 * DE * (D // 256 * 144) + D * (DE // 256 * 210))   # 24,477,696
 METRIC = "expert GEMV HBM GB/s, bs=1 MoE expert FFN (Qwen3-30B-A3B layer shape, Q4_K gate/up + Q6_K down)"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) per layer-token of the persistent kernel, from one
-# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of a
-# 4-layer-token launch of the kernel as of commit 8075c4d:
-# 98,106,880 read + 3,531,520 written, over 4 layer-tokens.
-TRAFFIC_LAYER_TOKEN = (98_106_880 + 3_531_520) // 4
+# DRAM bytes (read + write) per layer-token of the persistent kernel, from
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum) over three consecutive
+# 4-layer-token launches of the kernel as last changed in commit b5603b9
+# (captured at a95d757): reads 98,118,912 / 98,110,976 / 98,109,184 B,
+# writes 3,106,560 / 484,864 / 455,424 B (the share of the written rows that
+# leaves L2 within the launch varies); the mean of the three, per layer-token.
+TRAFFIC_LAYER_TOKEN = ((98_118_912 + 98_110_976 + 98_109_184) + (3_106_560 + 484_864 + 455_424)) // (3 * 4)
 
 
 def peaks() -> tuple[float, str]:
