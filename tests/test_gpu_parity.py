@@ -423,8 +423,9 @@ BATCH_SHAPES = [
     (1024, 512, 160, 6, (12, 12, 13), 0, 33, True),   # E > 128
     (1024, 512, 40, 4, (12, 12, 14), 1, 17, True),    # sigmoid router
     (1024, 512, 4, 4, (12, 12, 14), 0, 40, True),     # every expert > 16 tokens: several passes per tile
-    (2048, 768, 8, 4, (12, 12, 14), 0, 100, True),    # prefill-like: 50 tokens per expert, 32-token passes
-    (1024, 512, 6, 3, (13, 13, 13), 0, 64, True),     # 32-token passes, Q5_K
+    (2048, 768, 8, 4, (12, 12, 14), 0, 100, True),    # prefill-like: 50 tokens per expert, wide passes
+    (1024, 512, 6, 3, (13, 13, 13), 0, 64, True),     # wide passes, Q5_K
+    (4096, 1536, 4, 2, (12, 12, 14), 0, 60, True),    # config-5 dims, 30 tokens per expert: wide passes, one CTA per SM
     (1024, 768, 8, 2, (13, 13, 15), 0, 4, False),     # Q8_K down: per-token fallback
 ]
 
