@@ -39,6 +39,7 @@ __host__ __device__ inline uint32_t qvb(int nb) { return 256u * nb + 32u * nb + 
 
 // rows x len floats -> rows quantised vectors of len / 256 blocks
 __global__ void k_bquant(const float *__restrict__ in, int rows, int len, uint8_t *__restrict__ out) {
+    pdl_enter();
     const int lane = threadIdx.x & 31, nb = len / 256;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
     const uint32_t qb = qvb(nb);
@@ -55,6 +56,7 @@ __global__ void k_bquant(const float *__restrict__ in, int rows, int len, uint8_
 // kernel leaves the gate and up dots in two arrays)
 __global__ void k_bquant_swiglu(const float *__restrict__ g, const float *__restrict__ u, int rows, int len,
                                 uint8_t *__restrict__ out) {
+    pdl_enter();
     const int lane = threadIdx.x & 31, nb = len / 256;
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
     const uint32_t qb = qvb(nb);
@@ -78,6 +80,7 @@ __global__ void k_bquant_swiglu(const float *__restrict__ g, const float *__rest
 // one warp per token
 constexpr int RW = 2;   // warps per CTA
 __global__ void __launch_bounds__(32 * RW) k_broute(BatchArgs a, int32_t *__restrict__ ids, float *__restrict__ w) {
+    pdl_enter();
     __shared__ uint32_t scr[RW][RT_SCRATCH];
     __shared__ int32_t sid[RW][64];
     __shared__ float sw[RW][64];
@@ -103,6 +106,7 @@ __global__ void __launch_bounds__(32 * RW) k_broute(BatchArgs a, int32_t *__rest
 __global__ void __launch_bounds__(1024) k_bgroup(const int32_t *__restrict__ ids, int istride, int np, int E,
                                                   int lo, int hi, int32_t *grp, float *eo, int D, int32_t *bad,
                                                   const int32_t *__restrict__ rcnt, int cap) {
+    pdl_enter();
     __shared__ int cnt[RT_PER * 32], off[RT_PER * 32 + 1], fill[RT_PER * 32];
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         cnt[e] = 0;
@@ -266,6 +270,7 @@ __global__ void __launch_bounds__(256) k_bdown(const Slot *__restrict__ slots, c
 // perm[t * k + r] when perm is given, else t * k + r
 __global__ void k_bcombine(const float *__restrict__ eo, const int32_t *__restrict__ perm, const float *__restrict__ w,
                            int n, int D, int k, float *__restrict__ ffn) {
+    pdl_enter();
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < n * D; idx += gridDim.x * blockDim.x) {
         const int t = idx / D, i = idx - t * D;
         float f = 0.0f;
@@ -627,7 +632,7 @@ static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn
                          int hi, const int32_t *ids, int istride, int64_t np, const uint8_t *x, size_t xstride,
                          int xdiv, float *eo, cudaStream_t st, const int32_t *rcnt = nullptr, int cap = 0) {
     const int nsm = sm_count();
-    k_bgroup<<<1, 1024, 0, st>>>(ids, istride, (int)np, E, lo, hi, s.grp, eo, D, s.cnt + EP_MAX_RANKS, rcnt, cap);
+    launch_k(k_bgroup, 1, 1024, 0, st, ids, istride, (int)np, E, lo, hi, s.grp, eo, D, s.cnt + EP_MAX_RANKS, rcnt, cap);
     // at most min(np, E) experts are active
     const int64_t na_max = std::min<int64_t>(np, E);
     const size_t sgu = tgateup_smem(dt_gu, D), sdn = tdown_smem(dt_dn, de);
@@ -649,9 +654,10 @@ static int expert_stage(BatchScratch &s, const Slot *slots, int dt_gu, int dt_dn
                                                                                         xdiv, D, de, E, s.hbuf);
     }
     if (mma_gu)
-        k_bquant_swiglu<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, s.ubuf, (int)np, de, s.hq);
+        launch_k(k_bquant_swiglu, warp_blocks(np * (de / 256), nsm), 256, 0, st, (const float *)s.hbuf,
+                 (const float *)s.ubuf, (int)np, de, s.hq);
     else
-        k_bquant<<<warp_blocks(np * (de / 256), nsm), 256, 0, st>>>(s.hbuf, (int)np, de, s.hq);
+        launch_k(k_bquant, warp_blocks(np * (de / 256), nsm), 256, 0, st, (const float *)s.hbuf, (int)np, de, s.hq);
     TDownFn tdn = s.kmode_dn >= 1 ? pick_tdown(dt_dn) : nullptr;
     if (s.kmode_dn >= 2 && mma_down_supported(dt_dn, D, de)) {
         int rc = launch_mma_down(dt_dn, slots, s.grp, s.hq, D, de, E, na_max * (D / 128), wide, eo, err, st);
@@ -680,13 +686,21 @@ int launch_batch(BatchScratch &s, const BatchArgs &a, cudaStream_t st) {
     int rc = batch_reserve(s, a.n, a.D, a.de, a.E, a.k);
     if (rc) return rc;
     const int np = a.n * a.k, nsm = sm_count();
-    k_bquant<<<warp_blocks((int64_t)a.n * (a.D / 256), nsm), 256, 0, st>>>(a.x, a.n, a.D, s.xq);
-    k_broute<<<(a.n + RW - 1) / RW, 32 * RW, 0, st>>>(a, s.ids, s.w);
+    // the seven kernels of the call as programmatic dependents of each other
+    // (each waits in griddepcontrol.wait before it reads its inputs)
+    struct PdlScope {
+        bool prev = pdl_on();
+        PdlScope() { set_pdl(true); }
+        ~PdlScope() { set_pdl(prev); }
+    } pdl_scope;
+    launch_k(k_bquant, warp_blocks((int64_t)a.n * (a.D / 256), nsm), 256, 0, st, a.x, a.n, a.D, s.xq);
+    launch_k(k_broute, (a.n + RW - 1) / RW, 32 * RW, 0, st, a, s.ids, s.w);
     count_launch(2);
     if ((rc = expert_stage(s, a.slots, a.dt_gu, a.dt_dn, a.D, a.de, a.E, 0, a.E, s.ids, 1, np, s.xq, qvb(a.D / 256),
                            a.k, s.eo, st)))
         return rc;
-    k_bcombine<<<combine_blocks(a.n, a.D), 256, 0, st>>>(s.eo, nullptr, s.w, a.n, a.D, a.k, a.ffn);
+    launch_k(k_bcombine, combine_blocks(a.n, a.D), 256, 0, st, (const float *)s.eo, (const int32_t *)nullptr,
+             (const float *)s.w, a.n, a.D, a.k, a.ffn);
     count_launch(1);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "batched expert FFN launch");

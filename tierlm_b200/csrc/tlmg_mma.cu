@@ -423,6 +423,7 @@ __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : TN <= 16
     const MPlan P = mplan<TN>(1, (uint32_t)NS * MR * BB, nb, true);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
     const int tid = threadIdx.x, warp = tid >> 5, half = tid / MR, r = tid & (MR - 1);
+    pdl_enter();
     if (tid == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
     if (warp == 0) tmem_alloc(tmem_slot, 8 * TN);
     tc_fence_before();
@@ -524,6 +525,7 @@ __global__ void __launch_bounds__(DN_THREADS, TN <= 8 ? 2 : 1)
     const uint32_t Ahalf = align_up(tile_bytes, 1024u);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + P.bar + 8);
     const int r = threadIdx.x, warp = r >> 5;
+    pdl_enter();
     if (r == 0) mbar_init(reinterpret_cast<uint64_t *>(sm + P.bar), 1);
     if (warp == 0) tmem_alloc(tmem_slot, NCOL);
     tc_fence_before();
@@ -714,8 +716,8 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
                            : (three ? k_mgu<DT_Q5_K, 3, TLMG_GU_WIDE_TN> : k_mgu<DT_Q5_K, 2, TLMG_GU_WIDE_TN>);
     int rc = opt_in(fn, smem);
     if (rc) return rc;
-    fn<<<grid, GU_THREADS, smem, st>>>(slots, grp, x, xstride, xdiv, D, de, E, gout, uout, err);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(fn, grid, GU_THREADS, smem, st, slots, grp, x, xstride, xdiv, D, de, E, gout, uout, err);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core gate/up launch");
 }
 
@@ -736,8 +738,8 @@ int launch_mma_down(int dt, const Slot *slots, const int32_t *grp, const uint8_t
                              : k_mdown<DT_Q6_K, TLMG_DN_WIDE_TN>;
     int rc = opt_in(fn, smem);
     if (rc) return rc;
-    fn<<<grid, DN_THREADS, smem, st>>>(slots, grp, hq, D, de, E, eo, err);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(fn, grid, DN_THREADS, smem, st, slots, grp, hq, D, de, E, eo, err);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? TLMG_OK : cuda_fail(e, "tensor-core down launch");
 }
 
