@@ -410,6 +410,13 @@ constexpr int GU_THREADS = 2 * MR;
 #ifndef TLMG_MGU_NS8
 #define TLMG_MGU_NS8 3    // raw stages of the 8-token gate/up kernel (D <= 2048)
 #endif
+// Work items per (expert, tile, matrix) with wide passes: 2 splits the
+// token passes in halves, so that 2048-token prefill's 1,536 gate/up items
+// (5.2 per CTA of 296) become 3,072 with a shorter last wave: 21.9k tok/s
+// against 21.6k with 1 (B200, 48 layers).
+#ifndef TLMG_GU_WIDE_PARTS
+#define TLMG_GU_WIDE_PARTS 2
+#endif
 template <int DT, int NS, int TN>
 __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : TN <= 16 ? 2 : 1)
     k_mgu(const Slot *__restrict__ slots, const int32_t *__restrict__ grp, const uint8_t *__restrict__ x,
@@ -441,8 +448,12 @@ __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : TN <= 16
     const int t0 = half * TH;   // this thread's tokens t0 .. t0 + TH - 1
     bool first = true;
     uint8_t *Arow = sm + P.A + (r >> 3) * 2048 + (r & 7) * 16;
-    for (int item = blockIdx.x; item < na * tiles * 2 && ok; item += gridDim.x) {
-        const int m = item & 1, it = item >> 1, ae = it / tiles, tile = it - ae * tiles, e = grp[E + 1 + ae];
+    // wide passes: each (expert, tile, matrix) is split into PARTS items by
+    // its token passes, so that the last wave of items is shorter
+    constexpr int PARTS = TN > 8 ? TLMG_GU_WIDE_PARTS : 1;
+    for (int item = blockIdx.x; item < na * tiles * 2 * PARTS && ok; item += gridDim.x) {
+        const int part = item % PARTS, mi = item / PARTS;
+        const int m = mi & 1, it = mi >> 1, ae = it / tiles, tile = it - ae * tiles, e = grp[E + 1 + ae];
         const uint8_t *w = slots[e].m[m] + (size_t)tile * MR * rb;
         float *out = m ? uout : gout;
         auto issue = [&](int b) {
@@ -455,8 +466,11 @@ __global__ void __launch_bounds__(GU_THREADS, TN <= 8 ? TLMG_MGU_MINB : TN <= 16
             }
             cp_commit();
         };
-        for (int c0 = grp[e]; c0 < grp[e + 1] && ok; c0 += TN) {
-            const int nt = min(TN, grp[e + 1] - c0);
+        const int passes = (grp[e + 1] - grp[e] + TN - 1) / TN;
+        const int c_lo = grp[e] + TN * (passes * part / PARTS);
+        const int c_hi = min(grp[e + 1], grp[e] + TN * (passes * (part + 1) / PARTS));
+        for (int c0 = c_lo; c0 < c_hi && ok; c0 += TN) {
+            const int nt = min(TN, c_hi - c0);
             stage_tokens<DT, TN>(sm, P, x, xstride, xdiv, pairs + c0, nt, nb, first);
             first = false;
 #pragma unroll
@@ -703,7 +717,7 @@ int launch_mma_gateup(int dt, const Slot *slots, const int32_t *grp, const uint8
     const uint32_t smem = gateup_smem(dt, D, tn);
     // CTAs per SM: as many as the kernel is compiled for and 228 KB of shared memory per SM hold
     const int per_sm = std::max(1, std::min<int>(tn <= 8 ? TLMG_MGU_MINB : 2, (int)(233472u / (smem + 1024u))));
-    const int grid = grid_for(2 * max_items, per_sm);
+    const int grid = grid_for(2 * max_items * (tn > NARROW_TN ? TLMG_GU_WIDE_PARTS : 1), per_sm);
     const bool three = gateup_stages(D, tn) == 3;
     using Fn = void (*)(const Slot *, const int32_t *, const uint8_t *, size_t, int, int, int, int, float *, float *,
                         uint32_t *);
