@@ -8,7 +8,8 @@
  * reference's own self-test and tier matrix on this table. Every entry
  * forwards to libtlmg's host adapters, which copy the operands to the GPU,
  * run the sm_100a kernel and copy the result back, so this tier is for
- * parity, not speed (the fast path is tlmg_moe_layer).
+ * parity, not speed (the fast path is the whole MoE block on the device,
+ * tlmg_moe_layer in include/tlmg.h, called in place of the reference's moe()).
  */
 #define TLM_QUANT_INTERNAL 1
 #include "tlm_quant.h"
